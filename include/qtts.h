@@ -1,0 +1,213 @@
+/*
+ * qtts.h -- C-ABI of libqtts.so, the B200 (sm_100a) implementation of the
+ * per-frame language-model path of mormot2-qwen-tts: the Qwen3-TTS talker
+ * (28 layers, code 0 of each 80 ms frame) and the 5-layer code predictor
+ * (codes 1..15), with their heads.
+ *
+ * The library sits UNDER the reference's Object Pascal stack API
+ * (src/tts/mormot.ai.tts.qwen.lm.pas, mormot.ai.tts.qwen.talker.pas).  Each
+ * entry point below names the reference call it replaces (file:line in the
+ * reference project).  Plain C types only: pointers, sizes, ints.
+ *
+ * Conventions
+ *  - Every entry returns an int: QTTS_OK (0) or a QTTS_E_* code.  Nothing
+ *    aborts the process.  qtts_last_error() gives the message of the last
+ *    failure of the calling thread (the Pascal side raises EQwenLm with it,
+ *    as lm.pas:167, 232-234 and 345 raise on bad shapes).
+ *  - Host pointers given to a create/add call are copied to the device
+ *    during the call; the caller may free them afterwards.  Weights are never
+ *    keyed by host address (the stale-weights issue of the reference's
+ *    README "Device weights are keyed by their host address" cannot occur).
+ *  - Ownership: qtts_lm_create takes ownership of its stack (as
+ *    TQwenLm.Create owns its TDecoderModel, lm.pas:118-123) but not of its
+ *    heads, which must outlive it.  Destroy order: talker, lm, heads, device.
+ *  - Threading: one lm or talker per thread, as TQwenTalker is "not to be
+ *    shared between threads" (talker.pas:77).  One device may serve several.
+ *  - Model dimensions: hidden 1024, 16 query heads, 8 KV heads, head_dim
+ *    128, intermediate 3072 (the two stacks of Qwen3-TTS-12Hz-0.6B); other
+ *    dimensions are rejected with QTTS_E_ARG.  Layers and head rows are free.
+ */
+#ifndef QTTS_H
+#define QTTS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QTTS_OK 0
+#define QTTS_E_ARG 1      /* bad argument, shape or handle */
+#define QTTS_E_OOM 2      /* device memory exhausted */
+#define QTTS_E_CUDA 3     /* a CUDA call failed */
+#define QTTS_E_CAPACITY 4 /* the KV cache is full (position >= max_pos) */
+#define QTTS_E_TIMEOUT 5  /* a bounded device-side wait gave up */
+#define QTTS_E_STATE 6    /* call out of order (e.g. next_frame before start) */
+
+/* weight formats (TInferDType idtF32 / idtQ8_0 / the BF16 of the file) */
+#define QTTS_DTYPE_F32 0
+#define QTTS_DTYPE_Q8_0 1 /* ggml block_q8_0: fp16 scale + 32 int8, 34 bytes */
+#define QTTS_DTYPE_BF16 2 /* source rows only: widened exactly to float32 */
+
+typedef struct qtts_device qtts_device;
+typedef struct qtts_stack qtts_stack;
+typedef struct qtts_heads qtts_heads;
+typedef struct qtts_lm qtts_lm;
+typedef struct qtts_talker qtts_talker;
+
+/* The decoder configuration of one stack (TDecoderConfig: talker_config or
+ * talker_config.code_predictor_config of config.json, talker.pas:252-273).
+ * dtype: the format the weights take on the device, F32 or Q8_0. */
+typedef struct qtts_stack_config {
+    int32_t layers;
+    int32_t hidden;
+    int32_t heads;
+    int32_t kv_heads;
+    int32_t head_dim;
+    int32_t intermediate;
+    float rms_eps;
+    float rope_theta;
+    int32_t dtype;
+} qtts_stack_config;
+
+/* The tensors of one layer, as host pointers.  Matrices are [out][in]
+ * (PyTorch nn.Linear layout) in `dtype` (F32 or BF16 rows, or Q8_0 ggml
+ * blocks along `in`); norm weights are float32. */
+typedef struct qtts_layer_src {
+    int32_t dtype;
+    const void *q_proj;    /* [heads*head_dim][hidden]     */
+    const void *k_proj;    /* [kv_heads*head_dim][hidden]  */
+    const void *v_proj;    /* [kv_heads*head_dim][hidden]  */
+    const void *o_proj;    /* [hidden][heads*head_dim]     */
+    const void *gate_proj; /* [intermediate][hidden]       */
+    const void *up_proj;   /* [intermediate][hidden]       */
+    const void *down_proj; /* [hidden][intermediate]       */
+    const float *input_norm; /* [hidden]   input_layernorm          */
+    const float *post_norm;  /* [hidden]   post_attention_layernorm */
+    const float *q_norm;     /* [head_dim] */
+    const float *k_norm;     /* [head_dim] */
+} qtts_layer_src;
+
+/* ------------------------------------------------------------------ device */
+
+/* Opens CUDA device `ordinal` (TQwenVulkan.Create, lm.pas:207-211). */
+int qtts_device_open(int ordinal, qtts_device **out);
+/* TQwenVulkan.DeviceName (lm.pas:219-222). */
+int qtts_device_name(qtts_device *dev, char *buf, int len);
+/* TQwenVulkan.DeviceBytes (lm.pas:59-61): bytes of the stack weights held. */
+int qtts_device_bytes(qtts_device *dev, int64_t *bytes);
+/* TQwenVulkan.Destroy (lm.pas:213-217). */
+int qtts_device_close(qtts_device *dev);
+
+/* ------------------------------------------------------------------ stack */
+
+/* One Qwen3 stack on the device: QwenLmStack -> TQwen3Model.CreateStack
+ * (lm.pas:174-179) plus the upload of TQwenLm.Create (lm.pas:347-356).
+ * layers: config->layers entries; final_norm: [hidden] float32.  F32 or
+ * BF16 sources with a Q8_0 config are quantised on the device with ggml's
+ * quantize_row_q8_0_ref rule. */
+int qtts_stack_create(qtts_device *dev, const qtts_stack_config *config, const qtts_layer_src *layers,
+                      const float *final_norm, qtts_stack **out);
+/* StackBytes (lm.pas:181-197): bytes of the matrices and norms. */
+int qtts_stack_bytes(const qtts_stack *stack, int64_t *bytes);
+int qtts_stack_destroy(qtts_stack *stack);
+
+/* ------------------------------------------------------------------ heads */
+
+/* TQwenLmHeads.Create (lm.pas:227-238): dtype F32 or Q8_0, hidden % 32 == 0. */
+int qtts_heads_create(qtts_device *dev, const char *name, int hidden, int dtype, qtts_heads **out);
+/* TQwenLmHeads.Add (lm.pas:277-308): a [rows][hidden] head from F32 or BF16
+ * host rows; *index receives its index.  Q8_0 conversion runs on the device
+ * and gives the bytes of ggml's quantize_row_q8_0_ref. */
+int qtts_heads_add(qtts_heads *heads, const void *src, int src_dtype, int rows, int *index);
+/* TQwenLmHeads.Digest (lm.pas:310-317): crc32c of the stored bytes (ggml
+ * blocks for Q8_0, float32 rows otherwise) in load order. */
+int qtts_heads_digest(qtts_heads *heads, uint32_t *crc);
+/* TQwenLmHeads.Count / Rows / Bytes (lm.pas:88-99). */
+int qtts_heads_count(qtts_heads *heads, int *count);
+int qtts_heads_rows(qtts_heads *heads, int index, int *rows);
+int qtts_heads_bytes(qtts_heads *heads, int64_t *bytes);
+int qtts_heads_destroy(qtts_heads *heads);
+
+/* ------------------------------------------------------------------ lm */
+
+/* TQwenLm.Create (lm.pas:337-360): takes ownership of `stack`; `heads` is not
+ * owned.  max_pos: KV cache capacity in positions (float32 cache, the
+ * reference's default, talker.pas:188-190). */
+int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out);
+/* TQwenLm.Reset (lm.pas:374-378): the next row is at position 0. */
+int qtts_lm_reset(qtts_lm *lm);
+/* TQwenLm.Forward (lm.pas:391-408): appends rows x[rows][hidden] at
+ * positions Length..Length+rows-1; for the last row, the normed state goes
+ * to hidden (may be NULL) and the logits of head `head` to logits (NULL:
+ * no head).  rows <= 0 does nothing. */
+int qtts_lm_forward(qtts_lm *lm, const float *x, int rows, int head, float *logits, float *hidden);
+/* TQwenLm.Length (lm.pas:136-138). */
+int qtts_lm_length(qtts_lm *lm, int *length);
+/* TQwenLm.Destroy (lm.pas:362-372): frees the cache, then the stack. */
+int qtts_lm_destroy(qtts_lm *lm);
+
+/* ------------------------------------------------------------------ talker */
+
+/* The choice of codes and the frame layout of TQwenTalker (talker.pas:
+ * 86-111, 193-201): vocab 3072 (talker), pred_vocab 2048, groups 16,
+ * codec_eos_token_id, repetition_penalty (1.05 in greedy mode). */
+typedef struct qtts_talker_config {
+    int32_t vocab;
+    int32_t pred_vocab;
+    int32_t groups;
+    int32_t codec_eos;
+    float repetition_penalty;
+} qtts_talker_config;
+
+/* The per-frame loop of TQwenTalker on the device (greedy): talker and
+ * predictor lms (not owned; their heads: 1 talker head [vocab][hidden], 15
+ * predictor heads [pred_vocab][hidden]), the code embeddings of the talker
+ * codec_emb [vocab][hidden] and of the predictor pred_emb
+ * [groups-1][pred_vocab][hidden], float32 (talker.pas:307-311). */
+int qtts_talker_create(qtts_lm *talker, qtts_lm *predictor, const qtts_talker_config *config,
+                       const float *codec_emb, const float *pred_emb, qtts_talker **out);
+/* The end of TQwenTalker.Start (talker.pas:561-592): the trailing text rows
+ * (trailing [trailing_rows][hidden]; tts_pad [hidden] after them), talker
+ * Reset + Forward of the prefill rows [rows][hidden], empty history.  The
+ * logits of the last row (head 0) and its normed state are returned when
+ * the pointers are not NULL. */
+int qtts_talker_start(qtts_talker *t, const float *prefill, int rows, const float *trailing, int trailing_rows,
+                      const float *tts_pad, float *logits, float *hidden);
+/* TQwenTalker.NextFrame (talker.pas:640-681), greedy: ChooseCode0, the
+ * predictor (2 rows then 14 steps, each with its head and argmax), the sum
+ * of the 16 embeddings plus the trailing row, the talker step.  codes[groups]
+ * receives the frame; *more = 0 at eos (codes untouched), 1 otherwise. */
+int qtts_talker_next_frame(qtts_talker *t, int32_t *codes, int *more);
+/* Up to `frames` NextFrame calls launched back to back with no host round
+ * trip between them (the producer loop of TQwenTtsProducer.Execute,
+ * mormot.ai.tts.qwen.pas:276-319, without its per-frame hand-over):
+ * codes[frames][groups] receives the frames, *produced their count (fewer
+ * than `frames` when eos was chosen). */
+int qtts_talker_run(qtts_talker *t, int frames, int32_t *codes, int *produced);
+/* The CUDA stream (cudaStream_t) the talker's kernels run on, for callers
+ * that time them with events. */
+int qtts_talker_stream(qtts_talker *t, void **stream);
+/* The talker probes of TQwenTalker.Emit (talker.pas:590, 678): the logits
+ * (head 0, [vocab]) and the normed state ([hidden]) of the last talker
+ * forward.  Either pointer may be NULL. */
+int qtts_talker_probe(qtts_talker *t, float *logits, float *hidden);
+/* TQwenTalker.Step (talker.pas:152-154): frames returned since start. */
+int qtts_talker_step(qtts_talker *t, int *step);
+int qtts_talker_destroy(qtts_talker *t);
+
+/* ------------------------------------------------------------------ utilities */
+
+/* InferQuantizeRowQ8_0Ref (mormot2-ai, used at lm.pas:267): n float32 (n %
+ * 32 == 0) to n/32 ggml blocks of 34 bytes, computed on the device. */
+int qtts_quantize_q8_0(qtts_device *dev, const float *src, int64_t n, uint8_t *dst);
+
+/* The message of the last failure on this thread ("" if none). */
+const char *qtts_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QTTS_H */

@@ -1,0 +1,1057 @@
+// qtts_api.cu -- the C-ABI of libqtts.so (declared in include/qtts.h).
+//
+// Host side of the B200 implementation of mormot2-qwen-tts's per-frame
+// language-model path.  Handles mirror the reference's objects:
+//   qtts_stack  ~ TDecoderModel from QwenLmStack (mormot.ai.tts.qwen.lm.pas:174-179)
+//   qtts_heads  ~ TQwenLmHeads (lm.pas:64-100, 225-332)
+//   qtts_lm     ~ TQwenLm (lm.pas:102-143, 335-408)
+//   qtts_talker ~ the per-frame part of TQwenTalker (mormot.ai.tts.qwen.talker.pas:595-681)
+// Compute runs in the persistent kernel of qtts_decode.cuh; this file uploads
+// and packs weights (bit-exact ggml Q8_0 quantisation on the device), owns the
+// device memory and launches.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/qtts.h"
+#include "qtts_decode.cuh"
+
+using namespace qtts;
+
+// ------------------------------------------------------------------ errors
+
+static thread_local std::string g_err;
+
+static int set_err(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) {                                                                     \
+            int c_ = (e_ == cudaErrorMemoryAllocation) ? QTTS_E_OOM : QTTS_E_CUDA;                   \
+            return set_err(c_, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+        }                                                                                            \
+    } while (0)
+
+extern "C" const char *qtts_last_error(void) { return g_err.c_str(); }
+
+// ------------------------------------------------------------------ handles
+
+struct qtts_device {
+    int ordinal;
+    int sms;
+    size_t smem;
+    cudaStream_t load;  // uploads
+    void *staging;      // device staging for uploads
+    size_t staging_bytes;
+    int64_t bytes;      // stack weights held (TQwenVulkan.DeviceBytes)
+    char name[256];
+};
+
+struct qtts_stack {
+    qtts_device *dev;
+    qtts_stack_config cfg;
+    std::vector<void *> allocs;
+    DLayer *d_layers;
+    float *d_final_norm;
+    int64_t bytes;
+    int keep_l2;
+};
+
+struct HeadMat {
+    uint8_t *d;
+    int rows;
+};
+
+struct qtts_heads {
+    qtts_device *dev;
+    std::string name;
+    int hidden, dtype;
+    std::vector<HeadMat> mats;
+    int64_t bytes;
+};
+
+struct Runner {  // scratch + stream of one lm (and of a talker built on it)
+    cudaStream_t stream;
+    Scratch s;
+    void *block;  // one allocation for all of the scratch
+    int grid;
+    int *h_err;   // pinned [2]
+};
+
+struct qtts_lm {
+    qtts_device *dev;
+    qtts_stack *stack;
+    qtts_heads *heads;
+    int max_pos;
+    int len;
+    float *k, *v;          // KV cache
+    float *rope_cos, *rope_sin;
+    Runner run;
+    float *d_x;            // [RMAX][H] input rows
+    float *h_x;            // pinned [RMAX][H]
+    float *h_out;          // pinned [max rows + H]
+    int max_head_rows;
+};
+
+struct qtts_talker {
+    qtts_lm *talker, *pred;
+    qtts_talker_config cfg;
+    float *codec_emb, *pred_emb, *trailing, *tts_pad;
+    int trailing_rows, trailing_cap;
+    int done;  // eos chosen for the next frame
+    unsigned char *seen;
+    FrameState *fs, *h_fs;
+    const uint8_t **d_pheads;
+    int *d_hist;  // codes of qtts_talker_run
+    size_t hist_cap;
+    int started;
+};
+
+// ------------------------------------------------------------------ kernels
+
+// f32 / bf16 rows or ggml Q8_0 blocks -> device layout (F32 rows or
+// row-packed Q8_0), one thread per 32-element block; out row = r*mul + off
+__global__ void pack_kernel(const void *src, int src_dtype, int rows, int k, uint8_t *dst, int dst_dtype,
+                            int mul, int off) {
+    const int nb = k / 32;
+    long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<long long>(rows) * nb) return;
+    const int r = static_cast<int>(t / nb), b = static_cast<int>(t % nb);
+    const int orow = r * mul + off;
+    float x[32];
+    bool have_q = false;
+    int8_t qv[32];
+    __half dh = __float2half_rn(0.f);
+    if (src_dtype == QTTS_DTYPE_F32) {
+        const float *s = static_cast<const float *>(src) + static_cast<size_t>(r) * k + b * 32;
+        for (int j = 0; j < 32; ++j) x[j] = s[j];
+    } else if (src_dtype == QTTS_DTYPE_BF16) {
+        const __nv_bfloat16 *s = static_cast<const __nv_bfloat16 *>(src) + static_cast<size_t>(r) * k + b * 32;
+        for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(s[j]);
+    } else {
+        const uint8_t *s = static_cast<const uint8_t *>(src) + (static_cast<size_t>(r) * nb + b) * 34;
+        uint16_t hb = static_cast<uint16_t>(s[0] | (s[1] << 8));
+        dh = __ushort_as_half(hb);
+        for (int j = 0; j < 32; ++j) qv[j] = static_cast<int8_t>(s[2 + j]);
+        have_q = true;
+        float d = __half2float(dh);
+        for (int j = 0; j < 32; ++j) x[j] = static_cast<float>(qv[j]) * d;
+    }
+    if (dst_dtype == QTTS_DTYPE_F32) {
+        float *o = reinterpret_cast<float *>(dst + static_cast<size_t>(orow) * k * 4) + b * 32;
+        for (int j = 0; j < 32; ++j) o[j] = x[j];
+        return;
+    }
+    if (!have_q) {
+        // ggml quantize_row_q8_0_ref: d = amax/127, id = 1/d, q = roundf(x*id)
+        float amax = 0.f;
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+        float d = __fdiv_rn(amax, 127.0f);
+        float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+        dh = __float2half_rn(d);
+        for (int j = 0; j < 32; ++j) qv[j] = static_cast<int8_t>(roundf(__fmul_rn(x[j], id)));
+    }
+    uint8_t *row = dst + static_cast<size_t>(orow) * (k + k / 16);
+    for (int j = 0; j < 32; ++j) row[b * 32 + j] = static_cast<uint8_t>(qv[j]);
+    reinterpret_cast<__half *>(row + k)[b] = dh;
+}
+
+// f32 -> ggml blocks (34 bytes), the same rule
+__global__ void quantize_ggml_kernel(const float *src, long long nb, uint8_t *dst) {
+    long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= nb) return;
+    const float *x = src + b * 32;
+    float amax = 0.f;
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+    float d = __fdiv_rn(amax, 127.0f);
+    float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    uint8_t *o = dst + b * 34;
+    // the fp16 scale as one 16-bit store (offset 34*b is even): storing its
+    // two bytes separately wrote 0 for the low byte with this toolchain
+    *reinterpret_cast<__half *>(o) = __float2half_rn(d);
+    for (int j = 0; j < 32; ++j) o[2 + j] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[j], id))));
+}
+
+// ChooseCode0 over the talker logits after the prefill (empty history:
+// eos forbidden, no penalty): one CTA
+__global__ void choose0_kernel(const float *logits, int vocab, int eos, FrameState *fs) {
+    __shared__ unsigned long long best[32];
+    unsigned long long b = 0ull;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        float w = logits[i];
+        if (i >= vocab - 1024 && i != eos) w = -INFINITY;
+        if (i == eos) w = -INFINITY;  // fewer than 2 frames
+        unsigned long long k = argkey(w, i);
+        b = k > b ? k : b;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+        b = t > b ? t : b;
+    }
+    if ((threadIdx.x & 31) == 0) best[threadIdx.x >> 5] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0ull;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) m = best[w] > m ? best[w] : m;
+        int c = key_index(m);
+        fs->next_code0 = c;
+        fs->done = c == eos ? 1 : 0;
+        fs->hist_len = 0;
+        fs->step = 0;
+    }
+}
+
+// ------------------------------------------------------------------ helpers
+
+static bool dims_ok(const qtts_stack_config *c) {
+    return c->hidden == H && c->heads == HQ && c->kv_heads == HKV && c->head_dim == HD &&
+           c->intermediate == INTER && c->layers > 0;
+}
+
+static size_t src_bytes(int dtype, int rows, int k) {
+    if (dtype == QTTS_DTYPE_F32) return static_cast<size_t>(rows) * k * 4;
+    if (dtype == QTTS_DTYPE_BF16) return static_cast<size_t>(rows) * k * 2;
+    return static_cast<size_t>(rows) * (k / 32) * 34;
+}
+
+static int ensure_staging(qtts_device *dev, size_t bytes) {
+    if (dev->staging_bytes >= bytes) return QTTS_OK;
+    if (dev->staging) CK(cudaFree(dev->staging));
+    dev->staging = nullptr;
+    dev->staging_bytes = 0;
+    CK(cudaMalloc(&dev->staging, bytes));
+    dev->staging_bytes = bytes;
+    return QTTS_OK;
+}
+
+// upload one [rows][k] source matrix into dst (device layout), rows at r*mul+off
+static int upload_matrix(qtts_device *dev, const void *src, int src_dtype, int rows, int k, uint8_t *dst,
+                         int dst_dtype, int mul, int off) {
+    if (!src) return set_err(QTTS_E_ARG, "missing weight matrix");
+    if (src_dtype == QTTS_DTYPE_Q8_0 && dst_dtype != QTTS_DTYPE_Q8_0)
+        return set_err(QTTS_E_ARG, "Q8_0 sources need Q8_0 weights");
+    size_t nb = src_bytes(src_dtype, rows, k);
+    int rc = ensure_staging(dev, nb);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(dev->staging, src, nb, cudaMemcpyHostToDevice, dev->load));
+    long long n = static_cast<long long>(rows) * (k / 32);
+    int threads = 256;
+    unsigned blocks = static_cast<unsigned>((n + threads - 1) / threads);
+    pack_kernel<<<blocks, threads, 0, dev->load>>>(dev->staging, src_dtype, rows, k, dst, dst_dtype, mul, off);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(dev->load));
+    return QTTS_OK;
+}
+
+static int upload_floats(qtts_device *dev, const float *src, size_t n, float **out, std::vector<void *> &allocs) {
+    if (!src) return set_err(QTTS_E_ARG, "missing norm weights");
+    CK(cudaMalloc(reinterpret_cast<void **>(out), n * 4));
+    allocs.push_back(*out);
+    CK(cudaMemcpy(*out, src, n * 4, cudaMemcpyHostToDevice));
+    return QTTS_OK;
+}
+
+// RoPE tables as transformers computes them in float32: inv_freq_i =
+// 1/theta^(2i/d), angle = pos * inv_freq_i (one float32 product), cos/sin of
+// that angle
+static void rope_tables(int max_pos, float theta, std::vector<float> &cs, std::vector<float> &sn) {
+    const int half = HD / 2;
+    cs.resize(static_cast<size_t>(max_pos) * half);
+    sn.resize(static_cast<size_t>(max_pos) * half);
+    for (int i = 0; i < half; ++i) {
+        float e = static_cast<float>(2 * i) / static_cast<float>(HD);
+        float inv = 1.0f / powf(theta, e);
+        for (int p = 0; p < max_pos; ++p) {
+            float a = static_cast<float>(p) * inv;
+            cs[static_cast<size_t>(p) * half + i] = cosf(a);
+            sn[static_cast<size_t>(p) * half + i] = sinf(a);
+        }
+    }
+}
+
+static uint32_t crc32c(uint32_t crc, const void *data, size_t n) {
+    static uint32_t table[256];
+    static bool init = false;
+    if (!init) {
+        for (uint32_t i = 0; i < 256; i++) {
+            uint32_t c = i;
+            for (int k = 0; k < 8; k++) c = c & 1 ? (c >> 1) ^ 0x82F63B78u : c >> 1;
+            table[i] = c;
+        }
+        init = true;
+    }
+    const uint8_t *p = static_cast<const uint8_t *>(data);
+    crc = ~crc;
+    for (size_t i = 0; i < n; i++) crc = table[(crc ^ p[i]) & 0xff] ^ (crc >> 8);
+    return ~crc;
+}
+
+// ------------------------------------------------------------------ device
+
+extern "C" int qtts_device_open(int ordinal, qtts_device **out) {
+    if (!out) return set_err(QTTS_E_ARG, "qtts_device_open: out is NULL");
+    *out = nullptr;
+    int n = 0;
+    CK(cudaGetDeviceCount(&n));
+    if (ordinal < 0 || ordinal >= n) return set_err(QTTS_E_ARG, "qtts_device_open: no CUDA device %d (%d)", ordinal, n);
+    CK(cudaSetDevice(ordinal));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, ordinal));
+    if (prop.major < 10) return set_err(QTTS_E_ARG, "qtts_device_open: %s is sm_%d%d, sm_100a needed", prop.name, prop.major, prop.minor);
+    if (!prop.cooperativeLaunch) return set_err(QTTS_E_ARG, "qtts_device_open: no cooperative launch");
+    size_t smem = sizeof(Smem) + 128;
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    int occ = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<WDT_Q8>, NTHREADS, smem));
+    if (occ < 1) return set_err(QTTS_E_CUDA, "qtts_device_open: the decode kernel does not fit on an SM");
+    qtts_device *d = new qtts_device();
+    d->ordinal = ordinal;
+    d->sms = prop.multiProcessorCount;
+    d->smem = smem;
+    d->staging = nullptr;
+    d->staging_bytes = 0;
+    d->bytes = 0;
+    snprintf(d->name, sizeof(d->name), "%s", prop.name);
+    cudaError_t e = cudaStreamCreateWithFlags(&d->load, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete d;
+        return set_err(QTTS_E_CUDA, "cudaStreamCreate: %s", cudaGetErrorString(e));
+    }
+    *out = d;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_device_name(qtts_device *dev, char *buf, int len) {
+    if (!dev || !buf || len <= 0) return set_err(QTTS_E_ARG, "qtts_device_name: bad argument");
+    snprintf(buf, len, "%s", dev->name);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_device_bytes(qtts_device *dev, int64_t *bytes) {
+    if (!dev || !bytes) return set_err(QTTS_E_ARG, "qtts_device_bytes: bad argument");
+    *bytes = dev->bytes;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_device_close(qtts_device *dev) {
+    if (!dev) return QTTS_OK;
+    cudaSetDevice(dev->ordinal);
+    if (dev->staging) cudaFree(dev->staging);
+    cudaStreamDestroy(dev->load);
+    delete dev;
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ stack
+
+static void stack_free(qtts_stack *s) {
+    for (void *p : s->allocs) cudaFree(p);
+    delete s;
+}
+
+extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, const qtts_layer_src *layers,
+                                 const float *final_norm, qtts_stack **out) {
+    if (!dev || !c || !layers || !final_norm || !out) return set_err(QTTS_E_ARG, "qtts_stack_create: NULL argument");
+    *out = nullptr;
+    if (!dims_ok(c))
+        return set_err(QTTS_E_ARG, "qtts_stack_create: unsupported dimensions (hidden %d, heads %d/%d, head_dim %d, intermediate %d, layers %d)",
+                       c->hidden, c->heads, c->kv_heads, c->head_dim, c->intermediate, c->layers);
+    if (c->dtype != QTTS_DTYPE_F32 && c->dtype != QTTS_DTYPE_Q8_0)
+        return set_err(QTTS_E_ARG, "qtts_stack_create: weights must be F32 or Q8_0");
+    CK(cudaSetDevice(dev->ordinal));
+    qtts_stack *s = new qtts_stack();
+    s->dev = dev;
+    s->cfg = *c;
+    s->d_layers = nullptr;
+    const int wdt = c->dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    std::vector<DLayer> hl(c->layers);
+    int rc = QTTS_OK;
+    auto alloc = [&](size_t bytes) -> uint8_t * {
+        void *p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+        s->allocs.push_back(p);
+        return static_cast<uint8_t *>(p);
+    };
+    int64_t mat_bytes = 0;
+    for (int l = 0; l < c->layers && rc == QTTS_OK; ++l) {
+        const qtts_layer_src &a = layers[l];
+        int sd = a.dtype;
+        if (sd != QTTS_DTYPE_F32 && sd != QTTS_DTYPE_BF16 && sd != QTTS_DTYPE_Q8_0) {
+            rc = set_err(QTTS_E_ARG, "qtts_stack_create: layer %d has dtype %d", l, sd);
+            break;
+        }
+        DLayer &d = hl[l];
+        size_t bqkv = static_cast<size_t>(QKV_ROWS) * row_bytes(wdt, H);
+        size_t bo = static_cast<size_t>(H) * row_bytes(wdt, QDIM);
+        size_t bgu = static_cast<size_t>(GU_ROWS) * row_bytes(wdt, H);
+        size_t bd = static_cast<size_t>(H) * row_bytes(wdt, INTER);
+        uint8_t *wqkv = alloc(bqkv), *wo = alloc(bo), *wgu = alloc(bgu), *wd = alloc(bd);
+        if (!wqkv || !wo || !wgu || !wd) {
+            rc = set_err(QTTS_E_OOM, "qtts_stack_create: out of device memory at layer %d", l);
+            break;
+        }
+        mat_bytes += bqkv + bo + bgu + bd;
+        int dt = c->dtype;
+        if ((rc = upload_matrix(dev, a.q_proj, sd, QDIM, H, wqkv, dt, 1, 0))) break;
+        if ((rc = upload_matrix(dev, a.k_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM))) break;
+        if ((rc = upload_matrix(dev, a.v_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM + KVDIM))) break;
+        if ((rc = upload_matrix(dev, a.o_proj, sd, H, QDIM, wo, dt, 1, 0))) break;
+        if ((rc = upload_matrix(dev, a.gate_proj, sd, INTER, H, wgu, dt, 2, 0))) break;
+        if ((rc = upload_matrix(dev, a.up_proj, sd, INTER, H, wgu, dt, 2, 1))) break;
+        if ((rc = upload_matrix(dev, a.down_proj, sd, H, INTER, wd, dt, 1, 0))) break;
+        d.wqkv = wqkv;
+        d.wo = wo;
+        d.wgu = wgu;
+        d.wd = wd;
+        float *p;
+        if ((rc = upload_floats(dev, a.input_norm, H, &p, s->allocs))) break;
+        d.in_norm = p;
+        if ((rc = upload_floats(dev, a.post_norm, H, &p, s->allocs))) break;
+        d.post_norm = p;
+        if ((rc = upload_floats(dev, a.q_norm, HD, &p, s->allocs))) break;
+        d.q_norm = p;
+        if ((rc = upload_floats(dev, a.k_norm, HD, &p, s->allocs))) break;
+        d.k_norm = p;
+    }
+    if (rc == QTTS_OK) rc = upload_floats(dev, final_norm, H, &s->d_final_norm, s->allocs);
+    if (rc == QTTS_OK) {
+        uint8_t *dl = alloc(sizeof(DLayer) * c->layers);
+        if (!dl)
+            rc = set_err(QTTS_E_OOM, "qtts_stack_create: out of device memory");
+        else if (cudaMemcpy(dl, hl.data(), sizeof(DLayer) * c->layers, cudaMemcpyHostToDevice) != cudaSuccess)
+            rc = set_err(QTTS_E_CUDA, "qtts_stack_create: layer table upload failed");
+        s->d_layers = reinterpret_cast<DLayer *>(dl);
+    }
+    if (rc != QTTS_OK) {
+        stack_free(s);
+        return rc;
+    }
+    // StackBytes (lm.pas:181-197): matrices + (2 hidden + 2 head_dim) norms
+    // per layer + the final norm
+    s->bytes = mat_bytes + (static_cast<int64_t>(2 * H + 2 * HD) * 4) * c->layers + H * 4;
+    // stacks that fit comfortably in L2 keep their lines (evict_last)
+    s->keep_l2 = mat_bytes <= (96ll << 20) ? 1 : 0;
+    dev->bytes += s->bytes;
+    *out = s;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_stack_bytes(const qtts_stack *s, int64_t *bytes) {
+    if (!s || !bytes) return set_err(QTTS_E_ARG, "qtts_stack_bytes: bad argument");
+    *bytes = s->bytes;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_stack_destroy(qtts_stack *s) {
+    if (!s) return QTTS_OK;
+    cudaSetDevice(s->dev->ordinal);
+    s->dev->bytes -= s->bytes;
+    stack_free(s);
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ heads
+
+extern "C" int qtts_heads_create(qtts_device *dev, const char *name, int hidden, int dtype, qtts_heads **out) {
+    if (!dev || !out) return set_err(QTTS_E_ARG, "qtts_heads_create: NULL argument");
+    *out = nullptr;
+    if (dtype != QTTS_DTYPE_F32 && dtype != QTTS_DTYPE_Q8_0)
+        return set_err(QTTS_E_ARG, "qtts_heads_create: %s weights not supported", dtype == QTTS_DTYPE_BF16 ? "BF16" : "unknown");
+    if (hidden <= 0 || (hidden & 31) != 0)
+        return set_err(QTTS_E_ARG, "qtts_heads_create: invalid width %d for %s", hidden, name ? name : "");
+    if (hidden != H) return set_err(QTTS_E_ARG, "qtts_heads_create: width %d, the stacks have %d", hidden, H);
+    qtts_heads *h = new qtts_heads();
+    h->dev = dev;
+    h->name = name ? name : "";
+    h->hidden = hidden;
+    h->dtype = dtype;
+    h->bytes = 0;
+    *out = h;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_add(qtts_heads *h, const void *src, int src_dtype, int rows, int *index) {
+    if (!h || !src) return set_err(QTTS_E_ARG, "qtts_heads_add: NULL argument");
+    if (rows <= 0) return set_err(QTTS_E_ARG, "qtts_heads_add: %d rows", rows);
+    if (src_dtype != QTTS_DTYPE_F32 && src_dtype != QTTS_DTYPE_BF16 && src_dtype != QTTS_DTYPE_Q8_0)
+        return set_err(QTTS_E_ARG, "qtts_heads_add: source dtype %d", src_dtype);
+    CK(cudaSetDevice(h->dev->ordinal));
+    const int wdt = h->dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    size_t bytes = static_cast<size_t>(rows) * row_bytes(wdt, h->hidden);
+    uint8_t *d = nullptr;
+    CK(cudaMalloc(&d, bytes));
+    int rc = upload_matrix(h->dev, src, src_dtype, rows, h->hidden, d, h->dtype, 1, 0);
+    if (rc) {
+        cudaFree(d);
+        return rc;
+    }
+    h->mats.push_back({d, rows});
+    // TQwenLmHeads.Bytes counts the stored bytes (ggml blocks: 34 per 32)
+    h->bytes += static_cast<int64_t>(rows) * (h->dtype == QTTS_DTYPE_F32 ? h->hidden * 4 : h->hidden / 32 * 34);
+    if (index) *index = static_cast<int>(h->mats.size()) - 1;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_digest(qtts_heads *h, uint32_t *crc) {
+    if (!h || !crc) return set_err(QTTS_E_ARG, "qtts_heads_digest: NULL argument");
+    CK(cudaSetDevice(h->dev->ordinal));
+    uint32_t c = 0;
+    const int k = h->hidden;
+    for (const HeadMat &m : h->mats) {
+        if (h->dtype == QTTS_DTYPE_F32) {
+            std::vector<uint8_t> buf(static_cast<size_t>(m.rows) * k * 4);
+            CK(cudaMemcpy(buf.data(), m.d, buf.size(), cudaMemcpyDeviceToHost));
+            c = crc32c(c, buf.data(), buf.size());
+        } else {
+            // row-packed -> ggml blocks, in order
+            size_t rb = static_cast<size_t>(k) + k / 16;
+            std::vector<uint8_t> buf(static_cast<size_t>(m.rows) * rb);
+            CK(cudaMemcpy(buf.data(), m.d, buf.size(), cudaMemcpyDeviceToHost));
+            std::vector<uint8_t> g(static_cast<size_t>(m.rows) * (k / 32) * 34);
+            for (int r = 0; r < m.rows; ++r)
+                for (int b = 0; b < k / 32; ++b) {
+                    const uint8_t *row = buf.data() + r * rb;
+                    uint8_t *o = g.data() + (static_cast<size_t>(r) * (k / 32) + b) * 34;
+                    o[0] = row[k + 2 * b];
+                    o[1] = row[k + 2 * b + 1];
+                    memcpy(o + 2, row + b * 32, 32);
+                }
+            c = crc32c(c, g.data(), g.size());
+        }
+    }
+    *crc = c;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_count(qtts_heads *h, int *count) {
+    if (!h || !count) return set_err(QTTS_E_ARG, "qtts_heads_count: NULL argument");
+    *count = static_cast<int>(h->mats.size());
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_rows(qtts_heads *h, int index, int *rows) {
+    if (!h || !rows) return set_err(QTTS_E_ARG, "qtts_heads_rows: NULL argument");
+    if (index < 0 || index >= static_cast<int>(h->mats.size()))
+        return set_err(QTTS_E_ARG, "qtts_heads_rows: no head %d", index);
+    *rows = h->mats[index].rows;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_bytes(qtts_heads *h, int64_t *bytes) {
+    if (!h || !bytes) return set_err(QTTS_E_ARG, "qtts_heads_bytes: NULL argument");
+    *bytes = h->bytes;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_heads_destroy(qtts_heads *h) {
+    if (!h) return QTTS_OK;
+    cudaSetDevice(h->dev->ordinal);
+    for (HeadMat &m : h->mats) cudaFree(m.d);
+    delete h;
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ runner
+
+static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
+    r.grid = dev->sms;
+    const int maxS = r.grid / HKV;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off += (bytes + 255) & ~static_cast<size_t>(255);
+        return o;
+    };
+    size_t ox = take(RMAX * H * 4), oqkv = take(RMAX * QKV_ROWS * 4), oattn = take(RMAX * QDIM * 4),
+           oact = take(RMAX * INTER * 4), opart = take(static_cast<size_t>(HKV) * maxS * RMAX * 2 * PSTRIDE * 4),
+           ocomb = take(HKV * 4), oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(16), oerr = take(16),
+           olog = take(static_cast<size_t>(max_head_rows) * 4), ohid = take(H * 4), oxt = take(H * 4);
+    CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
+    CK(cudaMalloc(&r.block, off));
+    CK(cudaMemset(r.block, 0, off));
+    uint8_t *b = static_cast<uint8_t *>(r.block);
+    r.s.x = reinterpret_cast<float *>(b + ox);
+    r.s.qkv = reinterpret_cast<float *>(b + oqkv);
+    r.s.attn = reinterpret_cast<float *>(b + oattn);
+    r.s.act = reinterpret_cast<float *>(b + oact);
+    r.s.part = reinterpret_cast<float *>(b + opart);
+    r.s.comb = reinterpret_cast<unsigned *>(b + ocomb);
+    r.s.arg = reinterpret_cast<unsigned long long *>(b + oarg);
+    r.s.bar = reinterpret_cast<unsigned *>(b + obar);
+    r.s.err = reinterpret_cast<int *>(b + oerr);
+    r.s.logits = reinterpret_cast<float *>(b + olog);
+    r.s.hidden = reinterpret_cast<float *>(b + ohid);
+    r.s.xt = reinterpret_cast<float *>(b + oxt);
+    CK(cudaMallocHost(reinterpret_cast<void **>(&r.h_err), 16));
+    return QTTS_OK;
+}
+
+static void runner_free(Runner &r) {
+    if (r.block) cudaFree(r.block);
+    if (r.h_err) cudaFreeHost(r.h_err);
+    if (r.stream) cudaStreamDestroy(r.stream);
+    r.block = nullptr;
+    r.h_err = nullptr;
+    r.stream = nullptr;
+}
+
+static int launch(qtts_device *dev, Runner &r, const Job &job, int wdt) {
+    void *args[] = {const_cast<Job *>(&job)};
+    const void *fn = wdt == WDT_F32 ? reinterpret_cast<const void *>(decode_kernel<WDT_F32>)
+                                    : reinterpret_cast<const void *>(decode_kernel<WDT_Q8>);
+    CK(cudaLaunchCooperativeKernel(fn, dim3(r.grid), dim3(NTHREADS), args, dev->smem, r.stream));
+    return QTTS_OK;
+}
+
+// after a launch: read the error word; on a device error, clear the
+// counters so that the next launch starts clean
+static int runner_check(Runner &r) {
+    CK(cudaMemcpyAsync(r.h_err, r.s.err, 8, cudaMemcpyDeviceToHost, r.stream));
+    CK(cudaStreamSynchronize(r.stream));
+    if (r.h_err[0] != 0) {
+        int code = r.h_err[0], where = r.h_err[1];
+        CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
+        CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+        CK(cudaMemsetAsync(r.s.comb, 0, HKV * 4, r.stream));
+        CK(cudaStreamSynchronize(r.stream));
+        return set_err(code == ERR_CAPACITY ? QTTS_E_CAPACITY : QTTS_E_TIMEOUT,
+                       "device wait gave up (code %d at %d): the kernel returned early", code, where);
+    }
+    return QTTS_OK;
+}
+
+static DStack dstack(const qtts_stack *s) {
+    DStack d;
+    d.layer = s->d_layers;
+    d.layers = s->cfg.layers;
+    d.eps = s->cfg.rms_eps;
+    d.final_norm = s->d_final_norm;
+    d.keep_l2 = s->keep_l2;
+    return d;
+}
+
+// ------------------------------------------------------------------ lm
+
+static void lm_free(qtts_lm *m) {
+    if (m->k) cudaFree(m->k);
+    if (m->v) cudaFree(m->v);
+    if (m->rope_cos) cudaFree(m->rope_cos);
+    if (m->rope_sin) cudaFree(m->rope_sin);
+    if (m->d_x) cudaFree(m->d_x);
+    if (m->h_x) cudaFreeHost(m->h_x);
+    if (m->h_out) cudaFreeHost(m->h_out);
+    runner_free(m->run);
+    delete m;
+}
+
+extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out) {
+    if (!stack || !heads || !out) return set_err(QTTS_E_ARG, "qtts_lm_create: NULL argument");
+    *out = nullptr;
+    if (heads->hidden != stack->cfg.hidden)
+        return set_err(QTTS_E_ARG, "qtts_lm_create: %s has a width of %d, its heads %d", heads->name.c_str(),
+                       stack->cfg.hidden, heads->hidden);
+    if (heads->dtype != stack->cfg.dtype)
+        return set_err(QTTS_E_ARG, "qtts_lm_create: heads and stack have different weight formats");
+    if (max_pos <= 0 || max_pos > (1 << 20)) return set_err(QTTS_E_ARG, "qtts_lm_create: max_pos %d", max_pos);
+    qtts_device *dev = stack->dev;
+    CK(cudaSetDevice(dev->ordinal));
+    qtts_lm *m = new qtts_lm();
+    m->dev = dev;
+    m->stack = nullptr;
+    m->heads = heads;
+    m->max_pos = max_pos;
+    m->len = 0;
+    m->max_head_rows = 4096;
+    for (const HeadMat &hm : heads->mats) m->max_head_rows = hm.rows > m->max_head_rows ? hm.rows : m->max_head_rows;
+    int rc = QTTS_OK;
+    size_t kvn = static_cast<size_t>(stack->cfg.layers) * HKV * max_pos * HD;
+    std::vector<float> cs, sn;
+    rope_tables(max_pos, stack->cfg.rope_theta, cs, sn);
+    if (cudaMalloc(&m->k, kvn * 4) != cudaSuccess || cudaMalloc(&m->v, kvn * 4) != cudaSuccess ||
+        cudaMalloc(&m->rope_cos, cs.size() * 4) != cudaSuccess || cudaMalloc(&m->rope_sin, sn.size() * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_x, RMAX * H * 4) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void **>(&m->h_x), RMAX * H * 4) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void **>(&m->h_out), (m->max_head_rows + H) * 4) != cudaSuccess) {
+        rc = set_err(QTTS_E_OOM, "qtts_lm_create: out of memory (KV cache of %d positions)", max_pos);
+    }
+    if (rc == QTTS_OK && (cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                          cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = set_err(QTTS_E_CUDA, "qtts_lm_create: RoPE upload failed");
+    if (rc == QTTS_OK) rc = runner_init(m->run, dev, m->max_head_rows);
+    if (rc != QTTS_OK) {
+        lm_free(m);
+        return rc;
+    }
+    m->stack = stack;  // owned from here on
+    *out = m;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_lm_reset(qtts_lm *m) {
+    if (!m) return set_err(QTTS_E_ARG, "qtts_lm_reset: NULL lm");
+    m->len = 0;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_lm_length(qtts_lm *m, int *length) {
+    if (!m || !length) return set_err(QTTS_E_ARG, "qtts_lm_length: NULL argument");
+    *length = m->len;
+    return QTTS_OK;
+}
+
+static Job base_job(qtts_lm *m) {
+    Job j;
+    memset(&j, 0, sizeof(j));
+    j.s = m->run.s;
+    j.rope_cos = m->rope_cos;
+    j.rope_sin = m->rope_sin;
+    j.rope_pos = m->max_pos;
+    return j;
+}
+
+extern "C" int qtts_lm_forward(qtts_lm *m, const float *x, int rows, int head, float *logits, float *hidden) {
+    if (!m) return set_err(QTTS_E_ARG, "qtts_lm_forward: NULL lm");
+    if (rows <= 0) return QTTS_OK;
+    if (!x) return set_err(QTTS_E_ARG, "qtts_lm_forward: x is NULL");
+    if (logits && (head < 0 || head >= static_cast<int>(m->heads->mats.size())))
+        return set_err(QTTS_E_ARG, "qtts_lm_forward: no head %d in %s", head, m->heads->name.c_str());
+    if (m->len + rows > m->max_pos)
+        return set_err(QTTS_E_CAPACITY, "qtts_lm_forward: %d + %d positions, the cache holds %d", m->len, rows,
+                       m->max_pos);
+    CK(cudaSetDevice(m->dev->ordinal));
+    const int wdt = m->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    Job j = base_job(m);
+    j.mode = 0;
+    j.st = dstack(m->stack);
+    j.ctx.k = m->k;
+    j.ctx.v = m->v;
+    j.ctx.max_pos = m->max_pos;
+    j.xin = m->d_x;
+    // RMAX rows per launch; the head and the normed state come from the last
+    for (int r0 = 0; r0 < rows; r0 += RMAX) {
+        int n = rows - r0 < RMAX ? rows - r0 : RMAX;
+        bool last = r0 + n == rows;
+        memcpy(m->h_x, x + static_cast<size_t>(r0) * H, static_cast<size_t>(n) * H * 4);
+        CK(cudaMemcpyAsync(m->d_x, m->h_x, static_cast<size_t>(n) * H * 4, cudaMemcpyHostToDevice, m->run.stream));
+        j.rows = n;
+        j.L0 = m->len;
+        j.head_w = (last && logits) ? m->heads->mats[head].d : nullptr;
+        j.head_rows = (last && logits) ? m->heads->mats[head].rows : 0;
+        int rc = launch(m->dev, m->run, j, wdt);
+        if (rc) return rc;
+        // positions are appended whatever happens next (the cache is written)
+        rc = runner_check(m->run);
+        if (rc) return rc;
+        m->len += n;
+    }
+    int hr = logits ? m->heads->mats[head].rows : 0;
+    if (logits) CK(cudaMemcpyAsync(m->h_out, m->run.s.logits, hr * 4, cudaMemcpyDeviceToHost, m->run.stream));
+    if (hidden) CK(cudaMemcpyAsync(m->h_out + m->max_head_rows, m->run.s.hidden, H * 4, cudaMemcpyDeviceToHost, m->run.stream));
+    CK(cudaStreamSynchronize(m->run.stream));
+    if (logits) memcpy(logits, m->h_out, hr * 4);
+    if (hidden) memcpy(hidden, m->h_out + m->max_head_rows, H * 4);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_lm_destroy(qtts_lm *m) {
+    if (!m) return QTTS_OK;
+    cudaSetDevice(m->dev->ordinal);
+    qtts_stack *s = m->stack;
+    lm_free(m);
+    qtts_stack_destroy(s);
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ talker
+
+static void talker_free(qtts_talker *t) {
+    if (t->codec_emb) cudaFree(t->codec_emb);
+    if (t->pred_emb) cudaFree(t->pred_emb);
+    if (t->trailing) cudaFree(t->trailing);
+    if (t->tts_pad) cudaFree(t->tts_pad);
+    if (t->seen) cudaFree(t->seen);
+    if (t->fs) cudaFree(t->fs);
+    if (t->h_fs) cudaFreeHost(t->h_fs);
+    if (t->d_pheads) cudaFree(t->d_pheads);
+    if (t->d_hist) cudaFree(t->d_hist);
+    delete t;
+}
+
+extern "C" int qtts_talker_create(qtts_lm *talker, qtts_lm *pred, const qtts_talker_config *c, const float *codec_emb,
+                                  const float *pred_emb, qtts_talker **out) {
+    if (!talker || !pred || !c || !codec_emb || !pred_emb || !out)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: NULL argument");
+    *out = nullptr;
+    if (talker->dev != pred->dev) return set_err(QTTS_E_ARG, "qtts_talker_create: the stacks are on two devices");
+    if (talker->stack->cfg.dtype != pred->stack->cfg.dtype)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: talker and predictor have different weight formats");
+    if (talker->stack->cfg.rope_theta != pred->stack->cfg.rope_theta)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: talker and predictor have different RoPE bases");
+    if (c->groups < 2 || c->groups > MAX_GROUPS) return set_err(QTTS_E_ARG, "qtts_talker_create: %d code groups", c->groups);
+    if (c->vocab <= 1024 || c->pred_vocab <= 0 || c->codec_eos < 0 || c->codec_eos >= c->vocab)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: unexpected vocabularies (%d, %d, eos %d)", c->vocab, c->pred_vocab,
+                       c->codec_eos);
+    if (talker->heads->mats.size() < 1 || talker->heads->mats[0].rows != c->vocab)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: the talker head must have %d rows", c->vocab);
+    if (static_cast<int>(pred->heads->mats.size()) < c->groups - 1)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: the predictor needs %d heads", c->groups - 1);
+    for (int g = 0; g < c->groups - 1; ++g)
+        if (pred->heads->mats[g].rows != c->pred_vocab)
+            return set_err(QTTS_E_ARG, "qtts_talker_create: predictor head %d has %d rows", g, pred->heads->mats[g].rows);
+    if (pred->max_pos < c->groups || talker->max_pos < c->groups)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: the caches must hold at least %d positions", c->groups);
+    CK(cudaSetDevice(talker->dev->ordinal));
+    qtts_talker *t = new qtts_talker();
+    t->talker = talker;
+    t->pred = pred;
+    t->cfg = *c;
+    size_t ne = static_cast<size_t>(c->vocab) * H, np = static_cast<size_t>(c->groups - 1) * c->pred_vocab * H;
+    int rc = QTTS_OK;
+    if (cudaMalloc(&t->codec_emb, ne * 4) != cudaSuccess || cudaMalloc(&t->pred_emb, np * 4) != cudaSuccess ||
+        cudaMalloc(&t->tts_pad, H * 4) != cudaSuccess || cudaMalloc(&t->seen, c->vocab) != cudaSuccess ||
+        cudaMalloc(&t->fs, sizeof(FrameState)) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void **>(&t->h_fs), sizeof(FrameState)) != cudaSuccess ||
+        cudaMalloc(&t->d_pheads, sizeof(uint8_t *) * (c->groups - 1)) != cudaSuccess)
+        rc = set_err(QTTS_E_OOM, "qtts_talker_create: out of device memory");
+    if (rc == QTTS_OK) {
+        std::vector<const uint8_t *> ph(c->groups - 1);
+        for (int g = 0; g < c->groups - 1; ++g) ph[g] = pred->heads->mats[g].d;
+        if (cudaMemcpy(t->codec_emb, codec_emb, ne * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(t->pred_emb, pred_emb, np * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(t->d_pheads, ph.data(), sizeof(uint8_t *) * ph.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(t->fs, 0, sizeof(FrameState)) != cudaSuccess || cudaMemset(t->seen, 0, c->vocab) != cudaSuccess)
+            rc = set_err(QTTS_E_CUDA, "qtts_talker_create: upload failed");
+    }
+    if (rc != QTTS_OK) {
+        talker_free(t);
+        return rc;
+    }
+    *out = t;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows, const float *trailing, int trailing_rows,
+                                 const float *tts_pad, float *logits, float *hidden) {
+    if (!t || !prefill || !tts_pad || rows <= 0 || trailing_rows < 0 || (trailing_rows > 0 && !trailing))
+        return set_err(QTTS_E_ARG, "qtts_talker_start: bad argument");
+    qtts_lm *tl = t->talker;
+    CK(cudaSetDevice(tl->dev->ordinal));
+    cudaStream_t st = tl->run.stream;
+    if (trailing_rows > t->trailing_cap) {
+        if (t->trailing) CK(cudaFree(t->trailing));
+        t->trailing = nullptr;
+        CK(cudaMalloc(&t->trailing, static_cast<size_t>(trailing_rows) * H * 4));
+        t->trailing_cap = trailing_rows;
+    }
+    if (trailing_rows > 0)
+        CK(cudaMemcpyAsync(t->trailing, trailing, static_cast<size_t>(trailing_rows) * H * 4, cudaMemcpyHostToDevice, st));
+    t->trailing_rows = trailing_rows;
+    CK(cudaMemcpyAsync(t->tts_pad, tts_pad, H * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(t->seen, 0, t->cfg.vocab, st));
+    t->started = 0;
+    // TQwenTalker.Start: fTalker.Reset; fTalker.Forward(prefill, rows, 0, ...)
+    qtts_lm_reset(tl);
+    // the head always runs: the first ChooseCode0 reads its logits
+    std::vector<float> tmp(logits ? 0 : t->cfg.vocab);
+    int rc = qtts_lm_forward(tl, prefill, rows, 0, logits ? logits : tmp.data(), hidden);
+    if (rc) return rc;
+    // the first ChooseCode0 (empty history), then the frame state
+    choose0_kernel<<<1, 1024, 0, st>>>(tl->run.s.logits, t->cfg.vocab, t->cfg.codec_eos, t->fs);
+    CK(cudaGetLastError());
+    FrameState h;
+    CK(cudaMemcpyAsync(&h, t->fs, sizeof(h), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    h.tlen = tl->len;
+    CK(cudaMemcpyAsync(t->fs, &h, sizeof(h), cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
+    t->done = h.done;
+    t->started = 1;
+    return QTTS_OK;
+}
+
+static Job frame_job(qtts_talker *t) {
+    qtts_lm *tl = t->talker, *pl = t->pred;
+    Job j = base_job(tl);
+    j.mode = 1;
+    j.tst = dstack(tl->stack);
+    j.pst = dstack(pl->stack);
+    j.tctx.k = tl->k;
+    j.tctx.v = tl->v;
+    j.tctx.max_pos = tl->max_pos;
+    j.pctx.k = pl->k;
+    j.pctx.v = pl->v;
+    j.pctx.max_pos = pl->max_pos;
+    j.theads = tl->heads->mats[0].d;
+    j.tvocab = t->cfg.vocab;
+    j.pheads = t->d_pheads;
+    j.pvocab = t->cfg.pred_vocab;
+    j.groups = t->cfg.groups;
+    j.codec_emb = t->codec_emb;
+    j.pred_emb = t->pred_emb;
+    j.trailing = t->trailing;
+    j.trailing_rows = t->trailing_rows;
+    j.tts_pad = t->tts_pad;
+    j.eos = t->cfg.codec_eos;
+    j.penalty = t->cfg.repetition_penalty;
+    j.seen = t->seen;
+    j.fs = t->fs;
+    j.codes_hist = nullptr;
+    j.codes_cap = 0;
+    return j;
+}
+
+extern "C" int qtts_talker_next_frame(qtts_talker *t, int32_t *codes, int *more) {
+    if (!t || !codes || !more) return set_err(QTTS_E_ARG, "qtts_talker_next_frame: NULL argument");
+    if (!t->started) return set_err(QTTS_E_STATE, "qtts_talker_next_frame: call qtts_talker_start first");
+    qtts_lm *tl = t->talker, *pl = t->pred;
+    if (t->done) {  // ChooseCode0 gave eos: NextFrame returns false
+        *more = 0;
+        return QTTS_OK;
+    }
+    if (tl->len + 1 > tl->max_pos)
+        return set_err(QTTS_E_CAPACITY, "qtts_talker_next_frame: the talker cache is full (%d positions)", tl->max_pos);
+    CK(cudaSetDevice(tl->dev->ordinal));
+    const int wdt = tl->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    Job j = frame_job(t);
+    int rc = launch(tl->dev, tl->run, j, wdt);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(t->h_fs, t->fs, sizeof(FrameState), cudaMemcpyDeviceToHost, tl->run.stream));
+    rc = runner_check(tl->run);
+    if (rc) return rc;
+    const FrameState &f = *t->h_fs;
+    if (f.tlen == tl->len) {  // eos was chosen before this frame: nothing ran
+        t->done = 1;
+        *more = 0;
+        return QTTS_OK;
+    }
+    for (int g = 0; g < t->cfg.groups; ++g) codes[g] = f.codes[g];
+    t->done = f.done;
+    tl->len = f.tlen;
+    pl->len = t->cfg.groups;
+    *more = 1;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_run(qtts_talker *t, int frames, int32_t *codes, int *produced) {
+    if (!t || !produced || frames < 0 || (frames > 0 && !codes)) return set_err(QTTS_E_ARG, "qtts_talker_run: bad argument");
+    if (!t->started) return set_err(QTTS_E_STATE, "qtts_talker_run: call qtts_talker_start first");
+    *produced = 0;
+    qtts_lm *tl = t->talker, *pl = t->pred;
+    if (t->done || frames == 0) return QTTS_OK;
+    if (tl->len + frames > tl->max_pos)
+        return set_err(QTTS_E_CAPACITY, "qtts_talker_run: %d + %d positions, the talker cache holds %d", tl->len, frames,
+                       tl->max_pos);
+    CK(cudaSetDevice(tl->dev->ordinal));
+    const int wdt = tl->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    size_t need = static_cast<size_t>(frames) * t->cfg.groups;
+    if (need > t->hist_cap) {
+        if (t->d_hist) CK(cudaFree(t->d_hist));
+        t->d_hist = nullptr;
+        t->hist_cap = 0;
+        CK(cudaMalloc(&t->d_hist, need * 4));
+        t->hist_cap = need;
+    }
+    CK(cudaMemcpyAsync(t->h_fs, t->fs, sizeof(FrameState), cudaMemcpyDeviceToHost, tl->run.stream));
+    CK(cudaStreamSynchronize(tl->run.stream));
+    const int step0 = t->h_fs->step;
+    Job j = frame_job(t);
+    // frame f is written at row (step0 + f) - step0: shift the base pointer
+    j.codes_hist = t->d_hist - static_cast<ptrdiff_t>(step0) * t->cfg.groups;
+    j.codes_cap = step0 + frames;
+    for (int f = 0; f < frames; ++f) {
+        int rc = launch(tl->dev, tl->run, j, wdt);
+        if (rc) return rc;
+    }
+    CK(cudaMemcpyAsync(t->h_fs, t->fs, sizeof(FrameState), cudaMemcpyDeviceToHost, tl->run.stream));
+    int rc = runner_check(tl->run);
+    if (rc) return rc;
+    const FrameState &f = *t->h_fs;
+    int n = f.step - step0;
+    if (n > 0) CK(cudaMemcpy(codes, t->d_hist, static_cast<size_t>(n) * t->cfg.groups * 4, cudaMemcpyDeviceToHost));
+    *produced = n;
+    t->done = f.done;
+    tl->len = f.tlen;
+    if (n > 0) pl->len = t->cfg.groups;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_stream(qtts_talker *t, void **stream) {
+    if (!t || !stream) return set_err(QTTS_E_ARG, "qtts_talker_stream: NULL argument");
+    *stream = static_cast<void *>(t->talker->run.stream);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_probe(qtts_talker *t, float *logits, float *hidden) {
+    if (!t) return set_err(QTTS_E_ARG, "qtts_talker_probe: NULL talker");
+    if (!t->started) return set_err(QTTS_E_STATE, "qtts_talker_probe: call qtts_talker_start first");
+    qtts_lm *tl = t->talker;
+    CK(cudaSetDevice(tl->dev->ordinal));
+    if (logits) CK(cudaMemcpy(logits, tl->run.s.logits, static_cast<size_t>(t->cfg.vocab) * 4, cudaMemcpyDeviceToHost));
+    if (hidden) CK(cudaMemcpy(hidden, tl->run.s.hidden, H * 4, cudaMemcpyDeviceToHost));
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_step(qtts_talker *t, int *step) {
+    if (!t || !step) return set_err(QTTS_E_ARG, "qtts_talker_step: NULL argument");
+    if (!t->started) {
+        *step = 0;
+        return QTTS_OK;
+    }
+    CK(cudaSetDevice(t->talker->dev->ordinal));
+    FrameState h;
+    CK(cudaMemcpy(&h, t->fs, sizeof(h), cudaMemcpyDeviceToHost));
+    *step = h.step;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_destroy(qtts_talker *t) {
+    if (!t) return QTTS_OK;
+    cudaSetDevice(t->talker->dev->ordinal);
+    talker_free(t);
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ utilities
+
+extern "C" int qtts_quantize_q8_0(qtts_device *dev, const float *src, int64_t n, uint8_t *dst) {
+    if (!dev || !src || !dst || n < 0 || (n & 31) != 0) return set_err(QTTS_E_ARG, "qtts_quantize_q8_0: bad argument");
+    if (n == 0) return QTTS_OK;
+    CK(cudaSetDevice(dev->ordinal));
+    float *d_src = nullptr;
+    uint8_t *d_dst = nullptr;
+    long long nb = n / 32;
+    CK(cudaMalloc(&d_src, n * 4));
+    cudaError_t e = cudaMalloc(&d_dst, nb * 34);
+    if (e != cudaSuccess) {
+        cudaFree(d_src);
+        return set_err(QTTS_E_OOM, "qtts_quantize_q8_0: %s", cudaGetErrorString(e));
+    }
+    int rc = QTTS_OK;
+    if (cudaMemcpy(d_src, src, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = set_err(QTTS_E_CUDA, "upload failed");
+    if (rc == QTTS_OK) {
+        quantize_ggml_kernel<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, dev->load>>>(d_src, nb, d_dst);
+        if (cudaStreamSynchronize(dev->load) != cudaSuccess ||
+            cudaMemcpy(dst, d_dst, nb * 34, cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = set_err(QTTS_E_CUDA, "qtts_quantize_q8_0: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    cudaFree(d_src);
+    cudaFree(d_dst);
+    return rc;
+}

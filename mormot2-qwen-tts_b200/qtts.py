@@ -1,0 +1,352 @@
+"""Host-side mirror of mormot2-qwen-tts's stack API over libqtts.so (ctypes).
+
+The reference is Object Pascal; its stack API lives in
+src/tts/mormot.ai.tts.qwen.lm.pas and its frame loop in
+src/tts/mormot.ai.tts.qwen.talker.pas.  This module keeps the same objects,
+names, argument meanings and error behaviour on top of the C-ABI of
+include/qtts.h, so that the tests read like the reference's own tests:
+
+    QwenVulkan-like device   -> QwenDevice            (lm.pas:43-62)
+    QwenLmStack(...)         -> qwen_lm_stack(...)     (lm.pas:149-150, 174-179)
+    TQwenLmHeads             -> QwenLmHeads            (lm.pas:64-100)
+    TQwenLm                  -> QwenLm                 (lm.pas:102-143)
+    TQwenTalker (per frame)  -> QwenTalker             (talker.pas:471-681)
+    EQwenLm                  -> EQwenLm
+
+Every failure of the library raises EQwenLm with qtts_last_error(), as the
+reference raises EQwenLm (lm.pas:167, 232-234, 345).  There is no CPU path:
+if libqtts.so is missing the import fails.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqtts.so")
+
+DTYPE_F32 = 0
+DTYPE_Q8_0 = 1
+DTYPE_BF16 = 2
+DTYPES = {"f32": DTYPE_F32, "q8_0": DTYPE_Q8_0, "bf16": DTYPE_BF16}
+
+E_ARG, E_OOM, E_CUDA, E_CAPACITY, E_TIMEOUT, E_STATE = 1, 2, 3, 4, 5, 6
+
+
+class EQwenLm(RuntimeError):
+    """A failure of the stack library (the reference's EQwenLm)."""
+
+    def __init__(self, code, message):
+        super().__init__(f"qtts error {code}: {message}")
+        self.code = code
+
+
+class StackConfig(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("dtype", ctypes.c_int32)]
+
+
+class LayerSrc(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32)] + [(n, ctypes.c_void_p) for n in (
+        "q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj",
+        "input_norm", "post_norm", "q_norm", "k_norm")]
+
+
+class TalkerConfig(ctypes.Structure):
+    _fields_ = [("vocab", ctypes.c_int32), ("pred_vocab", ctypes.c_int32), ("groups", ctypes.c_int32),
+                ("codec_eos", ctypes.c_int32), ("repetition_penalty", ctypes.c_float)]
+
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+PI = ctypes.POINTER(ctypes.c_int)
+
+# name -> argtypes; every entry returns int (0 = ok)
+EXPORTS = {
+    "qtts_device_open": [I, ctypes.POINTER(P)],
+    "qtts_device_name": [P, ctypes.c_char_p, I],
+    "qtts_device_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
+    "qtts_device_close": [P],
+    "qtts_stack_create": [P, ctypes.POINTER(StackConfig), ctypes.POINTER(LayerSrc), P, ctypes.POINTER(P)],
+    "qtts_stack_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
+    "qtts_stack_destroy": [P],
+    "qtts_heads_create": [P, ctypes.c_char_p, I, I, ctypes.POINTER(P)],
+    "qtts_heads_add": [P, P, I, I, PI],
+    "qtts_heads_digest": [P, ctypes.POINTER(ctypes.c_uint32)],
+    "qtts_heads_count": [P, PI],
+    "qtts_heads_rows": [P, I, PI],
+    "qtts_heads_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
+    "qtts_heads_destroy": [P],
+    "qtts_lm_create": [P, P, I, ctypes.POINTER(P)],
+    "qtts_lm_reset": [P],
+    "qtts_lm_forward": [P, P, I, I, P, P],
+    "qtts_lm_length": [P, PI],
+    "qtts_lm_destroy": [P],
+    "qtts_talker_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
+    "qtts_talker_start": [P, P, I, P, I, P, P, P],
+    "qtts_talker_next_frame": [P, P, PI],
+    "qtts_talker_run": [P, I, P, PI],
+    "qtts_talker_stream": [P, ctypes.POINTER(P)],
+    "qtts_talker_probe": [P, P, P],
+    "qtts_talker_step": [P, PI],
+    "qtts_talker_destroy": [P],
+    "qtts_quantize_q8_0": [P, P, ctypes.c_int64, P],
+}
+
+
+def load_library(path=LIB_PATH):
+    """Load libqtts.so and declare its entry points (fails loudly if absent)."""
+    if not os.path.exists(path):
+        raise EQwenLm(E_ARG, f"{path} is missing: build it (python __graft_entry__.py or make -C {HERE})")
+    lib = ctypes.CDLL(path)
+    for name, args in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    lib.qtts_last_error.argtypes = []
+    lib.qtts_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        _lib = load_library()
+    return _lib
+
+
+def check(rc):
+    if rc != 0:
+        raise EQwenLm(rc, lib().qtts_last_error().decode(errors="replace"))
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class QwenDevice:
+    """One CUDA device (the role of TQwenVulkan, lm.pas:43-62)."""
+
+    def __init__(self, ordinal=0):
+        h = P()
+        check(lib().qtts_device_open(ordinal, ctypes.byref(h)))
+        self.handle = h
+
+    @property
+    def name(self):
+        buf = ctypes.create_string_buffer(256)
+        check(lib().qtts_device_name(self.handle, buf, 256))
+        return buf.value.decode()
+
+    @property
+    def device_bytes(self):
+        v = ctypes.c_int64()
+        check(lib().qtts_device_bytes(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def quantize_q8_0(self, x):
+        """InferQuantizeRowQ8_0Ref on the device: float32 -> ggml blocks."""
+        x = _f32(x).reshape(-1)
+        out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+        check(lib().qtts_quantize_q8_0(self.handle, _ptr(x), x.size, _ptr(out)))
+        return out
+
+    def close(self):
+        if self.handle:
+            check(lib().qtts_device_close(self.handle))
+            self.handle = None
+
+
+class QwenStack:
+    """A stack on the device (TDecoderModel from QwenLmStack); owned by the
+    QwenLm it is given to."""
+
+    def __init__(self, handle, layers):
+        self.handle = handle
+        self.layers = layers
+
+    @property
+    def bytes(self):
+        v = ctypes.c_int64()
+        check(lib().qtts_stack_bytes(self.handle, ctypes.byref(v)))
+        return v.value
+
+
+def qwen_lm_stack(device, config, layers, final_norm, dtype="q8_0"):
+    """QwenLmStack (lm.pas:174-179): config = dict of the decoder config
+    (layers, hidden, heads, kv_heads, head_dim, intermediate, rms_eps,
+    rope_theta); layers = list of dicts with wq wk wv wo wg wu wd ([out][in]
+    float32) and in_norm post_norm q_norm k_norm; dtype = weights on the
+    device ('f32' or 'q8_0')."""
+    cfg = StackConfig(len(layers), config["hidden"], config["heads"], config["kv_heads"], config["head_dim"],
+                      config["intermediate"], config["rms_eps"], config["rope_theta"], DTYPES[dtype])
+    keep = []
+    srcs = (LayerSrc * len(layers))()
+    for i, L in enumerate(layers):
+        arrs = {k: _f32(L[k]) for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd",
+                                        "in_norm", "post_norm", "q_norm", "k_norm")}
+        keep.append(arrs)
+        s = srcs[i]
+        s.dtype = DTYPE_F32
+        s.q_proj, s.k_proj, s.v_proj, s.o_proj = (arrs[k].ctypes.data for k in ("wq", "wk", "wv", "wo"))
+        s.gate_proj, s.up_proj, s.down_proj = (arrs[k].ctypes.data for k in ("wg", "wu", "wd"))
+        s.input_norm, s.post_norm = arrs["in_norm"].ctypes.data, arrs["post_norm"].ctypes.data
+        s.q_norm, s.k_norm = arrs["q_norm"].ctypes.data, arrs["k_norm"].ctypes.data
+    fn = _f32(final_norm)
+    h = P()
+    check(lib().qtts_stack_create(device.handle, ctypes.byref(cfg), srcs, _ptr(fn), ctypes.byref(h)))
+    return QwenStack(h, len(layers))
+
+
+class QwenLmHeads:
+    """TQwenLmHeads (lm.pas:64-100): output heads [rows][hidden], f32 or Q8_0."""
+
+    def __init__(self, device, name, hidden, dtype="q8_0"):
+        self.name = name
+        self.hidden = hidden
+        self.dtype = dtype
+        h = P()
+        check(lib().qtts_heads_create(device.handle, name.encode(), hidden, DTYPES[dtype], ctypes.byref(h)))
+        self.handle = h
+
+    def add(self, tensor, rows=None):
+        """TQwenLmHeads.Add: a [rows][hidden] float32 head; returns its index."""
+        t = _f32(tensor)
+        rows = t.size // self.hidden if rows is None else rows
+        if t.size != rows * self.hidden:
+            raise EQwenLm(E_ARG, f"{self.name}: head of {t.size} values instead of [{rows},{self.hidden}]")
+        idx = ctypes.c_int()
+        check(lib().qtts_heads_add(self.handle, _ptr(t), DTYPE_F32, rows, ctypes.byref(idx)))
+        return idx.value
+
+    def digest(self):
+        v = ctypes.c_uint32()
+        check(lib().qtts_heads_digest(self.handle, ctypes.byref(v)))
+        return v.value
+
+    @property
+    def count(self):
+        v = ctypes.c_int()
+        check(lib().qtts_heads_count(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def rows(self, index):
+        v = ctypes.c_int()
+        check(lib().qtts_heads_rows(self.handle, index, ctypes.byref(v)))
+        return v.value
+
+    @property
+    def bytes(self):
+        v = ctypes.c_int64()
+        check(lib().qtts_heads_bytes(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_heads_destroy(self.handle))
+            self.handle = None
+
+
+class QwenLm:
+    """TQwenLm (lm.pas:102-143): a stack (owned), its heads (not owned) and
+    its KV cache."""
+
+    def __init__(self, stack, heads, max_pos=4096):
+        h = P()
+        check(lib().qtts_lm_create(stack.handle, heads.handle, max_pos, ctypes.byref(h)))
+        stack.handle = None  # owned by the lm from now on
+        self.handle = h
+        self.heads = heads
+        self.hidden = heads.hidden
+
+    def reset(self):
+        check(lib().qtts_lm_reset(self.handle))
+
+    def forward(self, x, rows=None, output=0, logits=None, hidden=None):
+        """TQwenLm.Forward(x, aRows, aOutput, aLogits, aHidden): logits and
+        hidden are float32 arrays to fill (None: not wanted)."""
+        x = _f32(x)
+        rows = x.size // self.hidden if rows is None else rows
+        check(lib().qtts_lm_forward(self.handle, _ptr(x), rows, output, _ptr(logits), _ptr(hidden)))
+
+    @property
+    def length(self):
+        v = ctypes.c_int()
+        check(lib().qtts_lm_length(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_lm_destroy(self.handle))
+            self.handle = None
+
+
+class QwenTalker:
+    """The per-frame device loop of TQwenTalker (talker.pas:471-681), greedy."""
+
+    def __init__(self, talker, predictor, codec_emb, pred_emb, eos, vocab=3072, pred_vocab=2048, groups=16,
+                 repetition_penalty=1.05):
+        cfg = TalkerConfig(vocab, pred_vocab, groups, eos, repetition_penalty)
+        ce, pe = _f32(codec_emb), _f32(pred_emb)
+        h = P()
+        check(lib().qtts_talker_create(talker.handle, predictor.handle, ctypes.byref(cfg), _ptr(ce), _ptr(pe),
+                                       ctypes.byref(h)))
+        self.handle = h
+        self.groups = groups
+        self.vocab = vocab
+        self.hidden = talker.hidden
+
+    def start(self, prefill, trailing, tts_pad, logits=None, hidden=None):
+        """The device part of TQwenTalker.Start: prefill rows, trailing text
+        rows, tts_pad."""
+        p = _f32(prefill)
+        t = _f32(trailing) if trailing is not None and len(trailing) else None
+        check(lib().qtts_talker_start(self.handle, _ptr(p), p.size // self.hidden, _ptr(t),
+                                      0 if t is None else t.size // self.hidden, _ptr(_f32(tts_pad)),
+                                      _ptr(logits), _ptr(hidden)))
+
+    def next_frame(self, codes):
+        """TQwenTalker.NextFrame: fills codes[groups] (int32); False at eos."""
+        more = ctypes.c_int()
+        check(lib().qtts_talker_next_frame(self.handle, _ptr(codes), ctypes.byref(more)))
+        return bool(more.value)
+
+    def run(self, frames):
+        """Up to `frames` frames back to back; returns codes [n][groups]."""
+        out = np.zeros((frames, self.groups), np.int32)
+        n = ctypes.c_int()
+        check(lib().qtts_talker_run(self.handle, frames, _ptr(out), ctypes.byref(n)))
+        return out[:n.value]
+
+    @property
+    def stream(self):
+        """The cudaStream_t of the talker's kernels (an integer handle)."""
+        v = P()
+        check(lib().qtts_talker_stream(self.handle, ctypes.byref(v)))
+        return v.value or 0
+
+    def probe(self):
+        """(logits, hidden) of the last talker forward (Emit 'talker.logits')."""
+        lg = np.empty(self.vocab, np.float32)
+        hd = np.empty(self.hidden, np.float32)
+        check(lib().qtts_talker_probe(self.handle, _ptr(lg), _ptr(hd)))
+        return lg, hd
+
+    @property
+    def step(self):
+        v = ctypes.c_int()
+        check(lib().qtts_talker_step(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_talker_destroy(self.handle))
+            self.handle = None

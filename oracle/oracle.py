@@ -1,0 +1,266 @@
+"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's
+per-frame language-model path (qtts_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+cpu_baseline / reference legs of bench.py, as the checker.  The product
+(libqtts.so and the package) never imports it.
+
+Objects follow the reference: OraStack (QwenLmStack, lm.pas:174-179),
+OraHeads (TQwenLmHeads, lm.pas:64-100), OraLm (TQwenLm, lm.pas:102-143),
+OraTalker (TQwenTalker.Start/NextFrame, talker.pas:471-681).
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+F32, Q8_0 = 0, 1
+ACT_F32, ACT_Q8_0 = 0, 1
+
+
+class OraConfig(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_int), ("hidden", ctypes.c_int), ("heads", ctypes.c_int),
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("inter", ctypes.c_int),
+                ("eps", ctypes.c_float), ("theta", ctypes.c_float), ("dtype", ctypes.c_int)]
+
+
+class OraLayerSrc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("in_norm", "post_norm", "q_norm", "k_norm",
+                                                "wq", "wk", "wv", "wo", "wg", "wu", "wd")]
+
+
+P = ctypes.c_void_p
+
+
+def build():
+    """Compile liboracle.so with the Makefile next to this file."""
+    subprocess.run(["make", "-C", HERE, "-s"], check=True)
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        build()
+    lib = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "ora_set_threads": (None, [ctypes.c_int]),
+        "ora_get_threads": (ctypes.c_int, []),
+        "ora_set_act_mode": (None, [ctypes.c_int]),
+        "ora_quantize_q8_0": (None, [P, ctypes.c_int64, P]),
+        "ora_dequantize_q8_0": (None, [P, ctypes.c_int64, P]),
+        "ora_crc32c": (ctypes.c_uint32, [ctypes.c_uint32, P, ctypes.c_size_t]),
+        "ora_stack_create": (P, [ctypes.POINTER(OraConfig), ctypes.POINTER(OraLayerSrc), P]),
+        "ora_stack_free": (None, [P]),
+        "ora_heads_create": (P, [ctypes.c_int, ctypes.c_int]),
+        "ora_heads_add": (ctypes.c_int, [P, P, ctypes.c_int]),
+        "ora_heads_digest": (ctypes.c_uint32, [P]),
+        "ora_heads_free": (None, [P]),
+        "ora_lm_create": (P, [P, ctypes.c_int]),
+        "ora_lm_free": (None, [P]),
+        "ora_lm_reset": (None, [P]),
+        "ora_lm_length": (ctypes.c_int, [P]),
+        "ora_lm_forward": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P, P, P, P]),
+        "ora_argmax": (ctypes.c_int, [P, ctypes.c_int]),
+        "ora_choose_code0": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, P]),
+        "ora_talker_create": (P, [P, P, P, P, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_float]),
+        "ora_talker_free": (None, [P]),
+        "ora_talker_start": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P]),
+        "ora_talker_next_frame": (ctypes.c_int, [P, P]),
+        "ora_talker_logits": (P, [P]),
+        "ora_talker_hidden": (P, [P]),
+        "ora_rope_table": (None, [ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def set_threads(n):
+    lib.ora_set_threads(int(n))
+
+
+def threads():
+    return lib.ora_get_threads()
+
+
+def set_act_mode(mode):
+    lib.ora_set_act_mode(mode)
+
+
+def quantize_q8_0(x):
+    """ggml quantize_row_q8_0_ref: float32 -> blocks of 34 bytes."""
+    x = _f32(x).reshape(-1)
+    out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+    lib.ora_quantize_q8_0(_p(x), x.size, _p(out))
+    return out
+
+
+def dequantize_q8_0(q, n):
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    out = np.empty(n, dtype=np.float32)
+    lib.ora_dequantize_q8_0(_p(q), n, _p(out))
+    return out
+
+
+def crc32c(data, crc=0):
+    a = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8) if isinstance(data, (bytes, bytearray))
+                             else data).view(np.uint8)
+    return lib.ora_crc32c(crc, _p(a), a.size)
+
+
+def argmax(x):
+    x = _f32(x)
+    return lib.ora_argmax(_p(x), x.size)
+
+
+def choose_code0(logits, eos, history, penalty=1.05):
+    lg = _f32(logits)
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    work = np.empty_like(lg)
+    return lib.ora_choose_code0(_p(lg), lg.size, eos, _p(h) if h.size else None, h.size, penalty, _p(work))
+
+
+def rope_table(max_pos, head_dim, theta):
+    c = np.empty((max_pos, head_dim // 2), dtype=np.float32)
+    s = np.empty_like(c)
+    lib.ora_rope_table(max_pos, head_dim, theta, _p(c), _p(s))
+    return c, s
+
+
+class OraStack:
+    """QwenLmStack on the CPU: layers = list of dicts (wq..wd [out][in],
+    in_norm, post_norm, q_norm, k_norm); dtype 'f32' or 'q8_0'."""
+
+    def __init__(self, config, layers, final_norm, dtype="f32"):
+        c = config
+        self.cfg = OraConfig(len(layers), c["hidden"], c["heads"], c["kv_heads"], c["head_dim"],
+                             c["intermediate"], c["rms_eps"], c["rope_theta"], F32 if dtype == "f32" else Q8_0)
+        keep = []
+        srcs = (OraLayerSrc * len(layers))()
+        for i, L in enumerate(layers):
+            arrs = {k: _f32(L[k]) for k in ("in_norm", "post_norm", "q_norm", "k_norm",
+                                            "wq", "wk", "wv", "wo", "wg", "wu", "wd")}
+            keep.append(arrs)
+            for k, a in arrs.items():
+                setattr(srcs[i], k, a.ctypes.data)
+        fn = _f32(final_norm)
+        self.handle = lib.ora_stack_create(ctypes.byref(self.cfg), srcs, _p(fn))
+        self.hidden = c["hidden"]
+        self.layers = len(layers)
+
+    def free(self):
+        if self.handle:
+            lib.ora_stack_free(self.handle)
+            self.handle = None
+
+
+class OraHeads:
+    def __init__(self, hidden, dtype="f32"):
+        self.hidden = hidden
+        self.handle = lib.ora_heads_create(hidden, F32 if dtype == "f32" else Q8_0)
+        self.rows_ = []
+
+    def add(self, tensor):
+        t = _f32(tensor)
+        self.rows_.append(t.size // self.hidden)
+        return lib.ora_heads_add(self.handle, _p(t), t.size // self.hidden)
+
+    def rows(self, i):
+        return self.rows_[i]
+
+    def digest(self):
+        return lib.ora_heads_digest(self.handle)
+
+    def free(self):
+        if self.handle:
+            lib.ora_heads_free(self.handle)
+            self.handle = None
+
+
+class OraLm:
+    """TQwenLm on the CPU (the stack is owned by the caller here)."""
+
+    def __init__(self, stack, heads, max_pos=4096):
+        self.stack = stack
+        self.heads = heads
+        self.hidden = stack.hidden
+        self.handle = lib.ora_lm_create(stack.handle, max_pos)
+
+    def reset(self):
+        lib.ora_lm_reset(self.handle)
+
+    @property
+    def length(self):
+        return lib.ora_lm_length(self.handle)
+
+    def forward(self, x, output=0, logits=None, hidden=None, states=None, normed=None):
+        x = _f32(x)
+        rows = x.size // self.hidden
+        rc = lib.ora_lm_forward(self.handle, _p(x), rows, self.heads.handle if self.heads else None, output,
+                                _p(logits), _p(hidden), _p(states), _p(normed))
+        if rc:
+            raise RuntimeError("oracle: KV cache full")
+
+    def free(self):
+        if self.handle:
+            lib.ora_lm_free(self.handle)
+            self.handle = None
+
+
+class OraTalker:
+    """TQwenTalker's frame loop (greedy) on the CPU."""
+
+    def __init__(self, talker, theads, pred, pheads, codec_emb, pred_emb, eos, penalty=1.05, groups=16):
+        self.ce = _f32(codec_emb)
+        self.pe = _f32(pred_emb)
+        vocab = self.ce.shape[0]
+        pvocab = self.pe.shape[1]
+        self.groups = groups
+        self.handle = lib.ora_talker_create(talker.handle, theads.handle, pred.handle, pheads.handle, _p(self.ce),
+                                            vocab, _p(self.pe), pvocab, groups, eos, penalty)
+        self.hidden = talker.hidden
+        self.vocab = vocab
+
+    def start(self, prefill, trailing, tts_pad):
+        p = _f32(prefill)
+        t = _f32(trailing) if trailing is not None and len(trailing) else None
+        rc = lib.ora_talker_start(self.handle, _p(p), p.size // self.hidden, _p(t),
+                                  0 if t is None else t.size // self.hidden, _p(_f32(tts_pad)))
+        if rc:
+            raise RuntimeError("oracle: KV cache full")
+
+    def next_frame(self, codes):
+        rc = lib.ora_talker_next_frame(self.handle, _p(codes))
+        if rc < 0:
+            raise RuntimeError("oracle: KV cache full")
+        return rc == 1
+
+    def logits(self):
+        ptr = lib.ora_talker_logits(self.handle)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)), (self.vocab,)).copy()
+
+    def hidden_state(self):
+        ptr = lib.ora_talker_hidden(self.handle)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)), (self.hidden,)).copy()
+
+    def free(self):
+        if self.handle:
+            lib.ora_talker_free(self.handle)
+            self.handle = None

@@ -1,0 +1,190 @@
+"""Parity of the CUDA path (libqtts.so, through the C-ABI) with the oracle on
+the same seeded weights and inputs.
+
+Tolerances (north_star of the build, following the reference's
+tests/test.tts.qwen.lm.pas:319-336 and test.tts.qwen.vulkan.pas:224-232):
+  f32 weights : logits within 1e-4 abs, identical greedy codes; the predictor
+                protocol within 1e-4 relative to the peak (ComparePredictor).
+  Q8_0 weights: logits within 2e-2 abs and cosine >= 0.9999 against the
+                oracle's Q8_0 path (f32 activations).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import golden_lib as G
+import oracle as O
+import qtts
+import synth
+from model_util import Pair, TalkerPair, cosine
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+F32_LOGITS_ATOL = 1e-4
+Q8_LOGITS_ATOL = 2e-2
+Q8_COSINE = 0.9999
+
+
+def test_device_quantize_matches_gguf(device):
+    f = np.load(os.path.join(GOLD, "q8_0_gguf.npz"))
+    assert np.array_equal(device.quantize_q8_0(f["x"]), f["q"])
+
+
+def test_device_quantize_matches_oracle_large(device):
+    x = synth.normal((4096, 1024), 0.02, 5, 5)
+    assert np.array_equal(device.quantize_q8_0(x), O.quantize_q8_0(x))
+
+
+@pytest.mark.parametrize("dtype", ["q8_0", "f32"])
+def test_heads_digest_matches_oracle(device, dtype):
+    # ParallelQ8MatchesSerial / TQwenLmHeads.Digest: the same bytes
+    heads = [synth.talker_head(3)] + synth.predictor_heads(3)[:2]
+    d = qtts.QwenLmHeads(device, "heads", synth.HIDDEN, dtype)
+    o = O.OraHeads(synth.HIDDEN, dtype)
+    for h in heads:
+        d.add(h)
+        o.add(h)
+    assert d.count == 3 and d.rows(0) == 3072 and d.rows(2) == 2048
+    assert d.digest() == o.digest()
+    per = 1024 * 4 if dtype == "f32" else 1024 // 32 * 34
+    assert d.bytes == (3072 + 2 * 2048) * per
+    d.free()
+    o.free()
+
+
+def test_forward_f32_prefill_and_steps(device):
+    pr = Pair(device, 11, "talker", 2, [synth.talker_head(11)], "f32", max_pos=64)
+    x = synth.prompt(11, 13)
+    ld, lo = np.zeros(3072, np.float32), np.zeros(3072, np.float32)
+    hd, ho = np.zeros(1024, np.float32), np.zeros(1024, np.float32)
+    # 10 prefill rows (launches of 4 + 4 + 2), then 3 single rows
+    pr.dev.forward(x[:10], output=0, logits=ld, hidden=hd)
+    pr.ora.forward(x[:10], 0, lo, ho)
+    assert np.abs(ld - lo).max() <= F32_LOGITS_ATOL
+    assert np.abs(hd - ho).max() <= 1e-4
+    assert int(np.argmax(ld)) == O.argmax(lo)
+    for r in range(10, 13):
+        pr.dev.forward(x[r:r + 1], output=0, logits=ld, hidden=hd)
+        pr.ora.forward(x[r:r + 1], 0, lo, ho)
+        assert np.abs(ld - lo).max() <= F32_LOGITS_ATOL
+        assert np.abs(hd - ho).max() <= 1e-4
+    assert pr.dev.length == 13 == pr.ora.length
+    pr.dev.reset()
+    assert pr.dev.length == 0
+    pr.free()
+
+
+def test_predictor_protocol_lcg_f32(device):
+    # ComparePredictor (tests/test.tts.qwen.vulkan.pas:150-222): the 5-layer
+    # predictor with its 15 heads, LCG inputs, 2 rows then one per group;
+    # relative error (max |diff| / peak) <= 1e-4 with a float32 cache
+    pr = Pair(device, 21, "predictor", 5, synth.predictor_heads(21), "f32", max_pos=32)
+    seed = 12345
+    worst = 0.0
+    ld, lo = np.zeros(2048, np.float32), np.zeros(2048, np.float32)
+    hd, ho = np.zeros(1024, np.float32), np.zeros(1024, np.float32)
+    for g in range(15):
+        rows = 2 if g == 0 else 1
+        x, seed = synth.lcg_rows(rows, seed)
+        pr.dev.forward(x, output=g, logits=ld, hidden=hd)
+        pr.ora.forward(x, g, lo, ho)
+        worst = max(worst, np.abs(ld - lo).max() / np.abs(lo).max(), np.abs(hd - ho).max() / np.abs(ho).max())
+        assert int(np.argmax(ld)) == O.argmax(lo)
+    assert worst <= 1e-4, worst
+    assert pr.dev.length == 16
+
+
+def test_forward_q8_matches_oracle(device):
+    pr = Pair(device, 31, "talker", 3, [synth.talker_head(31)], "q8_0", max_pos=64)
+    x = synth.prompt(31, 7)
+    ld, lo = np.zeros(3072, np.float32), np.zeros(3072, np.float32)
+    pr.dev.forward(x[:5], output=0, logits=ld)
+    pr.ora.forward(x[:5], 0, lo)
+    assert np.abs(ld - lo).max() <= Q8_LOGITS_ATOL and cosine(ld, lo) >= Q8_COSINE
+    for r in range(5, 7):
+        pr.dev.forward(x[r:r + 1], output=0, logits=ld)
+        pr.ora.forward(x[r:r + 1], 0, lo)
+        assert np.abs(ld - lo).max() <= Q8_LOGITS_ATOL and cosine(ld, lo) >= Q8_COSINE
+    pr.free()
+
+
+def test_capacity_is_an_error(device):
+    pr = Pair(device, 41, "talker", 1, [synth.talker_head(41)], "f32", max_pos=8)
+    x = synth.prompt(41, 10)
+    with pytest.raises(qtts.EQwenLm) as e:
+        pr.dev.forward(x)
+    assert e.value.code == qtts.E_CAPACITY
+    pr.dev.forward(x[:8])
+    assert pr.dev.length == 8
+    pr.free()
+
+
+def run_frames(tp, frames, atol, cos_min=None):
+    codes_d = np.zeros(16, np.int32)
+    codes_o = np.zeros(16, np.int32)
+    n = 0
+    for f in range(frames):
+        md = tp.dev.next_frame(codes_d)
+        mo = tp.ora.next_frame(codes_o)
+        assert md == mo, f"frame {f}: eos on one side only"
+        if not md:
+            break
+        assert np.array_equal(codes_d, codes_o), f"frame {f}: {codes_d} vs {codes_o}"
+        lg, hd = tp.dev.probe()
+        lo = tp.ora.logits()
+        assert np.abs(lg - lo).max() <= atol, (f, np.abs(lg - lo).max())
+        if cos_min:
+            assert cosine(lg, lo) >= cos_min
+        n += 1
+    return n
+
+
+@pytest.mark.parametrize("dtype", ["f32", "q8_0"])
+def test_talker_frames_match_oracle(device, dtype):
+    # NextFrame (talker.pas:640-681) on the device against the oracle: the
+    # same 16 codes frame by frame, the talker logits within tolerance
+    tp = TalkerPair(device, 51, 2, 2, dtype)
+    prefill = synth.prompt(51, 12)
+    trailing = synth.text_rows(51, 3)
+    pad = synth.text_rows(51, 1, key=1)[0]
+    lg, hd = tp.start(prefill, trailing, pad)
+    assert np.abs(lg - tp.ora.logits()).max() <= (F32_LOGITS_ATOL if dtype == "f32" else Q8_LOGITS_ATOL)
+    atol = F32_LOGITS_ATOL if dtype == "f32" else Q8_LOGITS_ATOL
+    n = run_frames(tp, 8, atol, None if dtype == "f32" else Q8_COSINE)
+    assert n == 8 and tp.dev.step == 8
+    assert tp.t.dev.length == 12 + 8 and tp.p.dev.length == 16
+    tp.free()
+
+
+def test_eos_ends_the_sentence(device):
+    # a talker head whose eos row dominates: eos is forbidden for the first
+    # 2 frames (talker.pas:610-611), then chosen; NextFrame returns false
+    th = synth.talker_head(61)
+    th[synth.CODEC_EOS] = th[synth.CODEC_EOS] * 40.0 + 0.05
+    tp = TalkerPair(device, 61, 1, 1, "f32", theads=[th])
+    tp.start(synth.prompt(61, 4), None, synth.text_rows(61, 1)[0])
+    codes = np.zeros(16, np.int32)
+    n = 0
+    while tp.dev.next_frame(codes):
+        n += 1
+        assert n < 10
+    codes_o = np.zeros(16, np.int32)
+    m = 0
+    while tp.ora.next_frame(codes_o):
+        m += 1
+    assert n == m == 2
+    assert not tp.dev.next_frame(codes)
+    tp.free()
+
+
+def test_config1_full_f32_frame(device):
+    # 28-layer talker + 5-layer predictor, f32, one frame
+    # after 128 prior positions of N(0, 1) rows
+    tp = TalkerPair(device, 1, 28, 5, "f32", max_pos=256)
+    prefill = synth.prompt(1, 128)
+    lg, _ = tp.start(prefill, None, synth.text_rows(1, 1)[0])
+    assert np.abs(lg - tp.ora.logits()).max() <= F32_LOGITS_ATOL
+    assert run_frames(tp, 2, F32_LOGITS_ATOL) == 2
+    tp.free()
