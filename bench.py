@@ -1,0 +1,376 @@
+"""Benchmark of the per-frame language-model path (talker + code predictor).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config q8_0|f32] [--impl reference]
+
+Workload: Qwen3-TTS talker (28 layers) + code
+predictor (5 layers, 15 heads), Q8_0 weights, batch 1, a 40-row N(0,1)
+prompt, then K frames of streaming generation (K=156: the cache grows from
+40 to ~196 positions).  Synthetic seeded weights of the real architecture
+(no checkpoint here).  One step = one 80 ms frame = 1 talker step + 15
+predictor steps + 16 heads with greedy choice.  --config f32 runs configs[0]
+(f32 weights, 128 prior positions).
+
+Arms
+- default: libqtts.so on the GPU.  `value` = frames/s with everything
+  resident in HBM: K frame kernels launched back to back
+  (qtts_talker_run), CUDA events on the talker's stream.  `e2e` = the public
+  API a caller uses (qtts_talker_start with the prompt from host memory, then
+  qtts_talker_next_frame per frame, codes read back to the host each frame).
+- --impl reference: the reference's CPU path, restated in C (oracle/; the
+  reference's own Pascal code cannot be built here), timed on all host cores.
+
+Multi-GPU (torchrun, one process per GPU): every GPU runs its own utterance
+on a full weight replica, no data exchange (weak scaling); `value` = all
+frames / the slowest rank's time.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mormot2-qwen-tts_b200")
+sys.path.insert(0, PKG)
+
+import synth  # noqa: E402
+
+PROMPT_ROWS = {"q8_0": 40, "f32": 128}
+SEED = 1
+# bytes per frame of the weights read (talker + 15 predictor steps, heads and
+# norms included), row-packed Q8_0 = 34 bytes per 32 weights
+LAYER_CELLS = 1024 * (2 * 2048 + 2 * 1024 + 3 * 3072)
+NORM_BYTES = (2 * 1024 + 2 * 128) * 4
+
+
+def weight_bytes_per_frame(dtype, tl=28, pl=5, groups=16):
+    per = (lambda cells: cells // 32 * 34) if dtype == "q8_0" else (lambda cells: cells * 4)
+    talker = tl * (per(LAYER_CELLS) + NORM_BYTES) + 1024 * 4 + per(3072 * 1024)
+    pred = pl * (per(LAYER_CELLS) + NORM_BYTES) + 1024 * 4 + per(2048 * 1024)
+    return talker + (groups - 1) * pred
+
+
+KV_POS_BYTES = 8 * 128 * 4 * 2  # K + V of one position in one layer (float32)
+
+
+def kv_bytes_frame(talker_len, tl=28, pl=5, groups=16):
+    """KV bytes read + written by one frame whose talker step is at position
+    talker_len (cache already holding talker_len positions)."""
+    t = tl * KV_POS_BYTES * (talker_len + 1)
+    p = 0
+    for g in range(groups - 1):
+        rows = 2 if g == 0 else 1
+        prior = 0 if g == 0 else g + 1
+        p += pl * KV_POS_BYTES * (prior + rows)
+    return t + p
+
+
+def measured_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return None
+
+
+def ncu_traffic(config):
+    """DRAM bytes per launch of the frame kernel from the committed ncu
+    summary (profiles/decode_kernel_<config>_frame.md), or None."""
+    path = os.path.join(ROOT, "profiles", f"decode_kernel_{config}_frame.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_host_model(dtype, seed=SEED):
+    t0 = time.time()
+    tl, tf = synth.stack(seed, "talker", 28)
+    pl, pf = synth.stack(seed, "predictor", 5)
+    m = dict(tl=tl, tf=tf, pl=pl, pf=pf, th=synth.talker_head(seed), ph=synth.predictor_heads(seed),
+             ce=synth.codec_embedding(seed), pe=synth.predictor_embeddings(seed),
+             pad=synth.text_rows(seed, 1, key=1)[0])
+    m["gen_s"] = time.time() - t0
+    return m
+
+
+def cpu_frames(m, dtype, prompt, frames, threads=None):
+    """The oracle on host cores: prefill (untimed), then `frames` frames;
+    returns (seconds, frames done, threads used)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if threads:
+        O.set_threads(threads)
+    ts = O.OraStack(synth.CONFIG, m["tl"], m["tf"], dtype)
+    ps = O.OraStack(synth.CONFIG, m["pl"], m["pf"], dtype)
+    th = O.OraHeads(synth.HIDDEN, dtype)
+    th.add(m["th"])
+    ph = O.OraHeads(synth.HIDDEN, dtype)
+    for h in m["ph"]:
+        ph.add(h)
+    tlm = O.OraLm(ts, th, prompt.shape[0] + frames + 8)
+    plm = O.OraLm(ps, ph, 32)
+    tk = O.OraTalker(tlm, th, plm, ph, m["ce"], m["pe"], synth.CODEC_EOS)
+    tk.start(prompt, None, m["pad"])
+    codes = np.zeros(16, np.int32)
+    done = 0
+    t0 = time.perf_counter()
+    for _ in range(frames):
+        if not tk.next_frame(codes):
+            tk.start(prompt, None, m["pad"])
+            continue
+        done += 1
+    dt = time.perf_counter() - t0
+    n = O.threads()
+    for o in (tk, tlm, plm, ts, ps, th, ph):
+        o.free()
+    return dt, done, n
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    dtype = args.config
+    m = build_host_model(dtype)
+    prompt = synth.prompt(SEED + 100, PROMPT_ROWS[dtype])
+    cores = os.cpu_count()
+    # warm-up frames, then K timed frames (each step = one frame on the CPU)
+    cpu_frames(m, dtype, prompt, max(1, args.warmup), cores) if args.warmup else None
+    dt, done, used = cpu_frames(m, dtype, prompt, args.steps, cores)
+    fps = done / dt
+    line = {
+        "impl": "reference",
+        "metric": metric_name(dtype), "value": fps, "unit": "frames/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(done, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(dtype),
+        "data": "synthetic (seeded N(0,0.02) weights of the Qwen3-TTS talker/predictor architecture)",
+        "config": config_dict(dtype, args),
+        "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": used, "kind": "port",
+                         "sample": f"{done} frames of the {PROMPT_ROWS[dtype]}-row-prompt utterance after its prefill "
+                                   "(C restatement of the reference CPU path, AVX2+FMA, OpenMP)"},
+        "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(dtype):
+    return f"talker+predictor frames/s @B=1 per GPU ({'Q8_0' if dtype == 'q8_0' else 'f32'}; ms/frame = ms_per_step)"
+
+
+def dtype_name(dtype):
+    return "q8_0 weights x f32 activations (f32 accumulate)" if dtype == "q8_0" else "f32"
+
+
+def config_dict(dtype, args):
+    return {"workload": ("configs[1]: Q8_0, batch 1 per GPU, 40-row N(0,1) prompt, then K streaming frames"
+                         if dtype == "q8_0" else "configs[0]: f32, batch 1 per GPU, 128 prior positions, then K frames"),
+            "model": "Qwen3-TTS-12Hz-0.6B talker (28 layers) + code predictor (5 layers, 15 heads), synthetic weights",
+            "global_batch": args.gpus, "frames": args.steps, "prompt_rows": PROMPT_ROWS[dtype],
+            "parallelism": f"replicas x{args.gpus} (independent utterances, no collective)",
+            "l2": "working set per frame (weights) larger than L2: no flush needed"}
+
+
+def gpu_arm(args, rank, world, local_rank):
+    import torch
+    import qtts
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local_rank))
+    dtype = args.config
+    m = build_host_model(dtype)
+    prompt = synth.prompt(SEED + 100 + rank, PROMPT_ROWS[dtype])
+    K, W = args.steps, args.warmup
+    dev = qtts.QwenDevice(local_rank)
+    th = qtts.QwenLmHeads(dev, "talker", synth.HIDDEN, dtype)
+    th.add(m["th"])
+    ph = qtts.QwenLmHeads(dev, "predictor", synth.HIDDEN, dtype)
+    for h in m["ph"]:
+        ph.add(h)
+    max_pos = PROMPT_ROWS[dtype] + max(K, W) + 16
+    tlm = qtts.QwenLm(qtts.qwen_lm_stack(dev, synth.CONFIG, m["tl"], m["tf"], dtype), th, max_pos)
+    plm = qtts.QwenLm(qtts.qwen_lm_stack(dev, synth.CONFIG, m["pl"], m["pf"], dtype), ph, 32)
+    tk = qtts.QwenTalker(tlm, plm, m["ce"], m["pe"], synth.CODEC_EOS)
+    stream = torch.cuda.ExternalStream(tk.stream, device=torch.device("cuda", local_rank))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def run_frames(n):
+        """n frames on the device loop, restarting the utterance at eos."""
+        done, restarts = 0, 0
+        while done < n:
+            got = tk.run(n - done).shape[0]
+            done += got
+            if done < n:
+                tk.start(prompt, None, m["pad"])
+                restarts += 1
+        return restarts
+
+    # warm-up
+    tk.start(prompt, None, m["pad"])
+    run_frames(W)
+    # value: frames with everything resident
+    tk.start(prompt, None, m["pad"])
+    barrier()
+    clocks = Clocks(local_rank) if rank == 0 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    restarts = run_frames(K)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop() if clocks else None
+    talker_len0 = PROMPT_ROWS[dtype]
+    # e2e: the public per-frame API, prompt from (pinned) host memory
+    pin_prompt = torch.from_numpy(prompt).pin_memory().numpy()
+    codes = np.zeros(16, np.int32)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    f0.record(stream)
+    tk.start(pin_prompt, None, m["pad"])
+    n_e2e = 0
+    while n_e2e < K:
+        if tk.next_frame(codes):
+            n_e2e += 1
+        else:
+            tk.start(pin_prompt, None, m["pad"])
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    wall_e2e = time.perf_counter() - w0
+    # max over ranks
+    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        # bounded CPU sample: ~15 s of the oracle on the host cores
+        t1, d1, _ = cpu_frames(m, dtype, prompt, 1)
+        nf = int(min(max(2, 15.0 / max(t1, 1e-3)), K))
+        dt, done, used = cpu_frames(m, dtype, prompt, nf)
+        cpu = {"value": done / dt, "unit": "frames/s", "cores": used, "kind": "port",
+               "sample": f"{done} frames of the same utterance after its prefill (C restatement of the reference "
+                         "CPU path, AVX2+FMA, OpenMP over output rows)"}
+    if rank == 0:
+        fps = world * K / (ms / 1000.0)
+        wb = weight_bytes_per_frame(dtype)
+        kv = sum(kv_bytes_frame(talker_len0 + f) for f in range(K)) / K
+        alg = wb + kv  # algorithmic bytes per launch (one frame)
+        per_launch_s = ms / 1000.0 / K
+        peaks = measured_peaks()
+        peak = peaks["hbm_gbs"] if peaks else 6650.0
+        achieved = alg / per_launch_s / 1e9
+        traffic = ncu_traffic(dtype)
+        prompt_bytes = prompt.size * 4 + 1024 * 4
+        line = {
+            "metric": metric_name(dtype), "value": fps, "unit": "frames/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": dtype_name(dtype),
+            "data": "synthetic (seeded N(0,0.02) weights of the Qwen3-TTS talker/predictor architecture, N(0,1) prompt)",
+            "config": config_dict(dtype, args),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
+                         "kernel": "qtts::decode_kernel (frame mode)",
+                         "algorithmic_bytes_per_launch": alg},
+            "e2e": {"value": world * K / (ms_e2e / 1000.0), "unit": "frames/s",
+                    "h2d_bytes_per_step": prompt_bytes / K,
+                    "d2h_bytes_per_step": 104 + (3072 * 4) / K,
+                    "wall_s_rank0": wall_e2e, "includes": "qtts_talker_start (prompt upload + prefill) + K x qtts_talker_next_frame"},
+            "gpu_launches": K + (2 * restarts),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            "restarts_at_eos": restarts,
+            "weights_generation_s": m["gen_s"],
+        }
+        print(json.dumps(line), flush=True)
+    tk.free()
+    tlm.free()
+    plm.free()
+    th.free()
+    ph.free()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=156)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--config", choices=["q8_0", "f32"], default="q8_0")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+    else:
+        gpu_arm(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()
