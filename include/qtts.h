@@ -186,6 +186,11 @@ int qtts_talker_next_frame(qtts_talker *t, int32_t *codes, int *more);
  * codes[frames][groups] receives the frames, *produced their count (fewer
  * than `frames` when eos was chosen). */
 int qtts_talker_run(qtts_talker *t, int frames, int32_t *codes, int *produced);
+/* NextFrame with a phase trace (profiling, the role of the reference's
+ * TPrecisionTimer stats, mormot.ai.tts.qwen.pas:86-96): stamps[cap] receives
+ * the timestamps of CTA 0 at each phase boundary, (tag << 48) | ns, and *n
+ * their count. */
+int qtts_talker_trace_frame(qtts_talker *t, int32_t *codes, int *more, uint64_t *stamps, int cap, int *n);
 /* The CUDA stream (cudaStream_t) the talker's kernels run on, for callers
  * that time them with events. */
 int qtts_talker_stream(qtts_talker *t, void **stream);

@@ -315,6 +315,8 @@ extern "C" int qtts_device_open(int ordinal, qtts_device **out) {
     CK(cudaGetDeviceProperties(&prop, ordinal));
     if (prop.major < 10) return set_err(QTTS_E_ARG, "qtts_device_open: %s is sm_%d%d, sm_100a needed", prop.name, prop.major, prop.minor);
     if (!prop.cooperativeLaunch) return set_err(QTTS_E_ARG, "qtts_device_open: no cooperative launch");
+    if (prop.multiProcessorCount * XS_MAX < H || prop.multiProcessorCount < 2 * HKV)
+        return set_err(QTTS_E_ARG, "qtts_device_open: %d SMs is too few", prop.multiProcessorCount);
     size_t smem = sizeof(Smem) + 128;
     CK(cudaFuncSetAttribute(decode_kernel<WDT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     CK(cudaFuncSetAttribute(decode_kernel<WDT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -579,9 +581,9 @@ static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
         off += (bytes + 255) & ~static_cast<size_t>(255);
         return o;
     };
-    size_t ox = take(RMAX * H * 4), oqkv = take(RMAX * QKV_ROWS * 4), oattn = take(RMAX * QDIM * 4),
-           oact = take(RMAX * INTER * 4), opart = take(static_cast<size_t>(HKV) * maxS * RMAX * 2 * PSTRIDE * 4),
-           ocomb = take(HKV * 4), oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(16), oerr = take(16),
+    size_t ox = take(RMAX * H * 4), oqkv = take(RMAX * QKV_ROWS * 4), oact = take(RMAX * INTER * 4),
+           opart = take(static_cast<size_t>(HKV) * maxS * RMAX * 2 * PSTRIDE * 4),
+           oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(16), oerr = take(16),
            olog = take(static_cast<size_t>(max_head_rows) * 4), ohid = take(H * 4), oxt = take(H * 4);
     CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&r.block, off));
@@ -589,10 +591,8 @@ static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
     uint8_t *b = static_cast<uint8_t *>(r.block);
     r.s.x = reinterpret_cast<float *>(b + ox);
     r.s.qkv = reinterpret_cast<float *>(b + oqkv);
-    r.s.attn = reinterpret_cast<float *>(b + oattn);
     r.s.act = reinterpret_cast<float *>(b + oact);
     r.s.part = reinterpret_cast<float *>(b + opart);
-    r.s.comb = reinterpret_cast<unsigned *>(b + ocomb);
     r.s.arg = reinterpret_cast<unsigned long long *>(b + oarg);
     r.s.bar = reinterpret_cast<unsigned *>(b + obar);
     r.s.err = reinterpret_cast<int *>(b + oerr);
@@ -629,7 +629,6 @@ static int runner_check(Runner &r) {
         int code = r.h_err[0], where = r.h_err[1];
         CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
         CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
-        CK(cudaMemsetAsync(r.s.comb, 0, HKV * 4, r.stream));
         CK(cudaStreamSynchronize(r.stream));
         return set_err(code == ERR_CAPACITY ? QTTS_E_CAPACITY : QTTS_E_TIMEOUT,
                        "device wait gave up (code %d at %d): the kernel returned early", code, where);
@@ -914,10 +913,25 @@ static Job frame_job(qtts_talker *t) {
     j.fs = t->fs;
     j.codes_hist = nullptr;
     j.codes_cap = 0;
+    j.trace = nullptr;
+    j.trace_cap = 0;
+    j.trace_n = nullptr;
     return j;
 }
 
+static int next_frame(qtts_talker *t, int32_t *codes, int *more, uint64_t *stamps, int cap, int *n);
+
 extern "C" int qtts_talker_next_frame(qtts_talker *t, int32_t *codes, int *more) {
+    return next_frame(t, codes, more, nullptr, 0, nullptr);
+}
+
+extern "C" int qtts_talker_trace_frame(qtts_talker *t, int32_t *codes, int *more, uint64_t *stamps, int cap, int *n) {
+    if (!stamps || cap <= 0 || !n) return set_err(QTTS_E_ARG, "qtts_talker_trace_frame: bad trace buffer");
+    *n = 0;
+    return next_frame(t, codes, more, stamps, cap, n);
+}
+
+static int next_frame(qtts_talker *t, int32_t *codes, int *more, uint64_t *stamps, int cap, int *n) {
     if (!t || !codes || !more) return set_err(QTTS_E_ARG, "qtts_talker_next_frame: NULL argument");
     if (!t->started) return set_err(QTTS_E_STATE, "qtts_talker_next_frame: call qtts_talker_start first");
     qtts_lm *tl = t->talker, *pl = t->pred;
@@ -930,10 +944,29 @@ extern "C" int qtts_talker_next_frame(qtts_talker *t, int32_t *codes, int *more)
     CK(cudaSetDevice(tl->dev->ordinal));
     const int wdt = tl->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
     Job j = frame_job(t);
+    unsigned long long *d_trace = nullptr;
+    if (stamps) {
+        CK(cudaMalloc(&d_trace, (static_cast<size_t>(cap) + 1) * 8));
+        j.trace = d_trace;
+        j.trace_cap = cap;
+        j.trace_n = reinterpret_cast<int *>(d_trace + cap);
+        CK(cudaMemset(j.trace_n, 0, 4));
+    }
     int rc = launch(tl->dev, tl->run, j, wdt);
-    if (rc) return rc;
+    if (rc) {
+        if (d_trace) cudaFree(d_trace);
+        return rc;
+    }
     CK(cudaMemcpyAsync(t->h_fs, t->fs, sizeof(FrameState), cudaMemcpyDeviceToHost, tl->run.stream));
     rc = runner_check(tl->run);
+    if (d_trace) {
+        int cnt = 0;
+        cudaMemcpy(&cnt, j.trace_n, 4, cudaMemcpyDeviceToHost);
+        cnt = cnt < cap ? cnt : cap;
+        cudaMemcpy(stamps, d_trace, static_cast<size_t>(cnt) * 8, cudaMemcpyDeviceToHost);
+        *n = cnt;
+        cudaFree(d_trace);
+    }
     if (rc) return rc;
     const FrameState &f = *t->h_fs;
     if (f.tlen == tl->len) {  // eos was chosen before this frame: nothing ran

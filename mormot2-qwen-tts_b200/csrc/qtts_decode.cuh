@@ -7,7 +7,7 @@
 // its head and ChooseCode0 for the next frame.
 //
 // Shape of the kernel
-//  - one CTA per SM (grid = SM count, ~200 KB shared memory each), 16 warps:
+//  - one CTA per SM (grid = SM count, ~206 KB shared memory each), 16 warps:
 //    warps 0..14 compute, warp 15 is the weight producer.
 //  - the producer walks the same program as the compute warps and streams
 //    this CTA's slice of every weight matrix, in program order, through a
@@ -16,11 +16,16 @@
 //    the stream runs ahead across grid barriers: the next matrix is already
 //    in shared memory when its activations become ready.
 //  - the compute warps run the phases of each layer, separated by grid
-//    barriers (monotonic counter, release/acquire, bounded spin):
-//      P1 rmsnorm + QKV GEMV -> qkv      | P2 q/k-norm + RoPE + KV append +
-//      split-K attention, last split combines -> attn | P3 O GEMV + residual
-//      | P4 rmsnorm + gate/up GEMV + SiLU*up -> act | P5 down GEMV + residual
-//    then the final rmsnorm + head GEMV + argmax.
+//    barriers (monotonic counter, red.release / ld.acquire, bounded spin):
+//      P1 rmsnorm + QKV GEMV -> qkv; then this CTA's cached K/V tile for P2
+//         is prefetched into shared memory (cp.async.bulk) before the barrier
+//      P2 q/k-norm + RoPE + KV append, attention over one split of the
+//         context (positions spread over the warps) -> partials (o, max, sum)
+//      P3 combine the partials of all heads + O GEMV + residual
+//      P4 rmsnorm + gate/up GEMV + SiLU*up -> act
+//      P5 down GEMV + residual
+//    then the final rmsnorm + head GEMV + argmax.  Each CTA keeps its slice
+//    of the residual stream in shared memory (its O/down rows).
 //  - every wait is bounded (%globaltimer); on timeout the kernel records
 //    QTTS_E_TIMEOUT in the error word, waits (bounded) for its own bulk copies
 //    in flight and returns.
@@ -57,10 +62,12 @@ constexpr int NCT = NCW * 32;    // compute threads
 constexpr int PRODUCER_WARP = NWARPS - 1;
 
 constexpr int STAGE_BYTES = 24576;
-constexpr int NSTAGES = 6;
+constexpr int NSTAGES = 5;
 constexpr int ACT_FLOATS = RMAX * INTER;  // staged activations [R][K]
-constexpr int MAX_ITEMS = 64;             // (row, 512-unit) items per stage
+constexpr int MAX_PARTS = 24;             // (row, 1024-segment) partial sums per stage
 constexpr int PSTRIDE = 132;              // attention partial: o[128], m, l
+constexpr int ATT_TILE = 32;              // context positions per attention tile
+constexpr int XS_MAX = 16;                // residual rows owned by a CTA (grid >= 64)
 
 constexpr int WDT_F32 = 0;
 constexpr int WDT_Q8 = 1;
@@ -68,9 +75,19 @@ constexpr int WDT_Q8 = 1;
 constexpr int ERR_TIMEOUT = 5;
 constexpr int ERR_CAPACITY = 4;
 
-constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
+// every wait gives up after this many SM cycles (about 2 s at B200 clocks);
+// clock64() is local to the SM and cheap, unlike %globaltimer
+constexpr long long WAIT_CYCLES = 4000000000ll;
 
 __host__ __device__ constexpr int row_bytes(int wdt, int k) { return wdt == WDT_F32 ? k * 4 : k + k / 16; }
+
+// attention splits of a context of T positions over a grid of g CTAs
+__host__ __device__ inline int att_splits(int T, int g) {
+    int s = (T + ATT_TILE - 1) / ATT_TILE;
+    int cap = g / HKV;
+    s = s < cap ? s : cap;
+    return s < 1 ? 1 : s;
+}
 
 // ------------------------------------------------------------------ descriptors
 
@@ -96,10 +113,8 @@ struct DCtx {      // KV cache [layers][HKV][max_pos][HD], float32
 struct Scratch {
     float *x;       // [RMAX][H] residual stream
     float *qkv;     // [RMAX][QKV_ROWS]
-    float *attn;    // [RMAX][QDIM]
     float *act;     // [RMAX][INTER]
     float *part;    // [HKV*maxS][RMAX][2][PSTRIDE] attention partials
-    unsigned *comb; // [HKV] split counters (last split combines)
     unsigned long long *arg;  // [grid] argmax keys
     unsigned *bar;  // [0] barrier counter, [1] exit counter
     int *err;       // [0] error code, [1] where
@@ -146,6 +161,10 @@ struct Job {
     FrameState *fs;
     int *codes_hist;         // [cap][groups] codes by frame index (may be NULL)
     int codes_cap;
+    // phase timestamps of CTA 0 (profiling; NULL = off): (tag << 48) | ns
+    unsigned long long *trace;
+    int trace_cap;
+    int *trace_n;
     // both
     Scratch s;
     const float *rope_cos, *rope_sin;  // [rope_pos][HD/2]
@@ -181,13 +200,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// non-blocking test of an mbarrier phase (no suspension)
+__device__ __forceinline__ bool mbar_test_now(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // bounded wait on an mbarrier phase; false on timeout
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, const volatile int *abort_flag) {
     if (mbar_test(b, parity)) return true;
-    unsigned long long t0 = gtimer();
+    const long long t0 = clock64();
     while (!mbar_test(b, parity)) {
         if (abort_flag && *abort_flag) return false;
-        if (gtimer() - t0 > WAIT_NS) return false;
+        if (clock64() - t0 > WAIT_CYCLES) return false;
     }
     return true;
 }
@@ -208,22 +237,36 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
-__device__ __forceinline__ void named_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
-
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
+// sums of a and b over the warp with 5 shuffles: lane 0 gets sum(a), lane 16 sum(b)
+__device__ __forceinline__ float warp_sum2(float a, float b, int lane) {
+    const bool hi = lane & 16;
+    float keep = hi ? b : a, send = hi ? a : b;
+    keep += __shfl_xor_sync(0xffffffffu, send, 16);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+    return keep;
+}
 
 // int8 x4 (one 32-bit word) -> 4 exact floats: byte b^0x80 placed in the
 // mantissa of 2^23, minus 2^23+128
-__device__ __forceinline__ void dq4(uint32_t w, float &a, float &b, float &c, float &d) {
-    uint32_t u = w ^ 0x80808080u;
-    a = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
-    b = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
-    c = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
-    d = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+__device__ __forceinline__ float4 dq4(uint32_t w) {
+    const uint32_t u = w ^ 0x80808080u;
+    return make_float4(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f,
+                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f,
+                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f,
+                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f);
 }
 
 // orderable key: larger value first, then smaller index (first maximum)
@@ -236,26 +279,38 @@ __device__ __forceinline__ int key_index(unsigned long long k) {
     return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
 }
 
+// loads through L2 (data written by other CTAs in this launch: this SM's L1
+// may hold an older copy)
+__device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+
 // ------------------------------------------------------------------ shared memory
 
 struct __align__(128) Smem {
     uint8_t ring[NSTAGES][STAGE_BYTES];
-    float act[ACT_FLOATS];
-    float part[MAX_ITEMS * RMAX];
-    float red[64];
+    float act[ACT_FLOATS];            // GEMV activations; attention scratch
+    float kv[2][ATT_TILE][HD];        // attention K / V tile
+    float xs[RMAX][XS_MAX];           // this CTA's rows of the residual stream
+    float part[2][MAX_PARTS * RMAX];  // GEMV partial sums, double-buffered by chunk
+    float red[NWARPS * RMAX];
     unsigned long long keys[NWARPS];
     uint64_t full[NSTAGES];
     uint64_t empty[NSTAGES];
+    uint64_t kvbar;
     int abort_flag;
-    int consumed;  // chunks released by the compute warps
+    int consumed;   // chunks released by the compute warps
     int bcast;
+    int kv_rows;    // cached rows of the prefetched tile (0: nothing in flight)
+    int barflag[3];     // OR reductions of the compute-warp barrier, rotating
 };
+
+// CTA-level barriers of the compute warps: Compute::cta_sync / cta_or
+#define named_sync() cta_sync()
+#define named_or(v) cta_or(v)
 
 // ------------------------------------------------------------------ program walk
 
-// Matrix phases in program order.  Both the producer and the compute warps
-// call walk(); the producer issues the copies of each matrix slice, the
-// compute warps do the work.  The order must not depend on data.
+// Matrix phases in program order.  The producer and the compute warps walk
+// the same order; it must not depend on data.
 enum Mat { M_QKV, M_O, M_GU, M_D, M_HEAD };
 
 __device__ __forceinline__ int mat_rows(Mat m, int head_rows) {
@@ -333,11 +388,40 @@ template <int WDT>
 struct Compute {
     Smem *sm;
     const Job *job;
-    int seq = 0;         // chunks consumed
-    unsigned target = 0; // grid barrier target
+    int seq = 0;          // chunks consumed
+    unsigned target = 0;  // grid barrier target
     bool ok = true;
-    int hist_now = 0;    // history length for ChooseCode0 (frame mode)
+    int hist_now = 0;     // history length for ChooseCode0 (frame mode)
+    uint32_t kv_phase = 0;
     int tid, warp, lane;
+    int c0, c1;           // this CTA's residual rows
+
+    int barc = 0;         // cta_or calls so far (the same count in every thread)
+
+    // Barrier of the compute warps (hardware barrier 1, 480 threads), each
+    // warp converged first.  With pred: also ORs pred over the compute
+    // threads through a rotating shared flag (no bar.red).
+    __device__ __forceinline__ void cta_sync() {
+        __syncwarp();
+        asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
+    }
+    __device__ __forceinline__ bool cta_or(bool pred) {
+        __syncwarp();
+        const bool wp = __any_sync(0xffffffffu, pred);
+        const int k = barc++;
+        if (lane == 0 && wp) sm->barflag[k % 3] = 1;
+        asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory");
+        const bool r = *reinterpret_cast<volatile int *>(&sm->barflag[k % 3]) != 0;
+        // the flag of call k+2 was last read at call k-1: free to clear
+        if (tid == 0) sm->barflag[(k + 2) % 3] = 0;
+        return r;
+    }
+
+    int ntrace = 0;
+    __device__ __forceinline__ void mark(int tag) {
+        if (job->trace && blockIdx.x == 0 && tid == 0 && ntrace < job->trace_cap)
+            job->trace[ntrace++] = (static_cast<unsigned long long>(tag) << 48) | (gtimer() & 0xFFFFFFFFFFFFull);
+    }
 
     __device__ void fail(int code, int where) {
         if (ok) {
@@ -348,161 +432,230 @@ struct Compute {
         }
     }
 
-    // grid-wide barrier among the compute warps of all CTAs
+    // grid-wide barrier among the compute warps of all CTAs: release-add on
+    // a monotonic counter, acquire-poll until every CTA has arrived.  It also
+    // makes `ok` uniform over the CTA (any thread's failure fails all).
     __device__ void grid_sync(int where) {
-        named_sync();
+        const bool bad = named_or(!ok);
+        mark(100 + where);  // arrival of CTA 0
         if (tid == 0) {
             target += gridDim.x;
-            if (ok) {
-                __threadfence();
-                atomicAdd(job->s.bar, 1u);
-                volatile unsigned *c = job->s.bar;
-                unsigned long long t0 = 0;
-                int spins = 0;
-                while (*c < target) {
+            int b = bad ? 1 : 0;
+            if (!bad) {
+                unsigned *bar = job->s.bar;
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+                const long long t0 = clock64();
+                while (true) {
+                    unsigned v;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+                    if (v >= target) break;
                     if (*reinterpret_cast<volatile int *>(job->s.err) != 0) {
                         fail(ERR_TIMEOUT, where);
+                        b = 1;
                         break;
                     }
-                    if (++spins == 64) t0 = gtimer();
-                    if (spins > 64 && gtimer() - t0 > WAIT_NS) {
+                    if (clock64() - t0 > WAIT_CYCLES) {
                         fail(ERR_TIMEOUT, where);
+                        b = 1;
                         break;
                     }
                 }
-                __threadfence();
             }
-            sm->bcast = ok ? 0 : 1;
+            sm->bcast = b;
         }
         named_sync();
-        if (sm->bcast) ok = false;
+        ok = sm->bcast == 0;
+        mark(200 + where);  // departure
     }
 
     // ---------------------------------------------------------------- staging
 
-    // act[r][0..H) = rmsnorm(row r) * w; rows given by up to 3 addends
-    // (((a + b) + c), the summation order of TQwenTalker.NextFrame)
+    // act[r][0..H) = rmsnorm(row r) * w, rows as the sum of up to 3 addends
+    // (((a + b) + c), the summation order of TQwenTalker.NextFrame); with
+    // init_resid, this CTA's residual rows [c0, c1) are taken from the sum
     __device__ void stage_norm(const float *const *a, const float *const *b, const float *const *c, int R,
-                               const float *w, float eps, float *copy_to, int c0, int c1) {
-        for (int r = 0; r < R; ++r) {
-            float ss = 0.f;
-            for (int i = tid; i < H; i += NCT) {
-                float v = a[r][i];
-                if (b && b[r]) v = v + b[r][i];
-                if (c && c[r]) v = v + c[r][i];
-                sm->act[r * H + i] = v;
-                ss += v * v;
-                if (copy_to && i >= c0 && i < c1) copy_to[r * H + i] = v;
+                               const float *w, float eps, bool init_resid) {
+        float ss[RMAX] = {0.f, 0.f, 0.f, 0.f};
+        for (int idx = tid; idx < R * (H / 4); idx += NCT) {
+            const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
+            float4 v = ldcg4(a[r] + i);
+            if (b && b[r]) {
+                const float4 t = ldcg4(b[r] + i);
+                v.x = v.x + t.x; v.y = v.y + t.y; v.z = v.z + t.z; v.w = v.w + t.w;
             }
-            ss = warp_sum(ss);
-            if (lane == 0) sm->red[warp] = ss;
-            named_sync();
-            if (warp == 0) {
-                float t = lane < NCW ? sm->red[lane] : 0.f;
-                t = warp_sum(t);
-                if (lane == 0) sm->red[32] = 1.0f / sqrtf(t / static_cast<float>(H) + eps);
+            if (c && c[r]) {
+                const float4 t = ldcg4(c[r] + i);
+                v.x = v.x + t.x; v.y = v.y + t.y; v.z = v.z + t.z; v.w = v.w + t.w;
             }
-            named_sync();
-            float inv = sm->red[32];
-            for (int i = tid; i < H; i += NCT) sm->act[r * H + i] = w[i] * (sm->act[r * H + i] * inv);
-            named_sync();
+            *reinterpret_cast<float4 *>(sm->act + r * H + i) = v;
+            float s = v.x * v.x;
+            s = fmaf(v.y, v.y, s);
+            s = fmaf(v.z, v.z, s);
+            s = fmaf(v.w, v.w, s);
+#pragma unroll
+            for (int rr = 0; rr < RMAX; ++rr)
+                if (rr == r) ss[rr] += s;
+            if (init_resid) {
+                const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (i + j >= c0 && i + j < c1) sm->xs[r][i + j - c0] = vv[j];
+            }
         }
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            if (r < R) {
+                const float t = warp_sum(ss[r]);
+                if (lane == 0) sm->red[warp * RMAX + r] = t;
+            }
+        }
+        named_sync();
+        for (int idx = tid; idx < R * (H / 4); idx += NCT) {
+            const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
+            float t = 0.f;
+            for (int w2 = 0; w2 < NCW; ++w2) t += sm->red[w2 * RMAX + r];
+            const float inv = 1.0f / sqrtf(t / static_cast<float>(H) + eps);
+            float4 v = *reinterpret_cast<float4 *>(sm->act + r * H + i);
+            const float4 g = *reinterpret_cast<const float4 *>(w + i);
+            v.x = g.x * (v.x * inv);
+            v.y = g.y * (v.y * inv);
+            v.z = g.z * (v.z * inv);
+            v.w = g.w * (v.w * inv);
+            *reinterpret_cast<float4 *>(sm->act + r * H + i) = v;
+        }
+        named_sync();
     }
+
     __device__ void stage_copy(const float *src, int R, int k) {
-        const float4 *s4 = reinterpret_cast<const float4 *>(src);
-        float4 *d4 = reinterpret_cast<float4 *>(sm->act);
-        for (int i = tid; i < R * k / 4; i += NCT) d4[i] = s4[i];
+        for (int i = tid; i < R * k / 4; i += NCT)
+            reinterpret_cast<float4 *>(sm->act)[i] = ldcg4(src + 4 * i);
+        named_sync();
+    }
+
+    // the attention output of all 16 query heads: combine the S partials of
+    // each (row, head): o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+    __device__ void stage_attn(int R, int S) {
+        const size_t split_stride = static_cast<size_t>(RMAX) * 2 * PSTRIDE;
+        for (int idx = tid; idx < R * HQ * (HD / 4); idx += NCT) {
+            const int r = idx / (HQ * (HD / 4));
+            const int rem = idx - r * HQ * (HD / 4);
+            const int qh = rem / (HD / 4), d4 = rem - qh * (HD / 4);
+            const int h = qh >> 1, q = qh & 1;
+            const float *base = job->s.part + ((static_cast<size_t>(h) * S * RMAX + r) * 2 + q) * PSTRIDE;
+            float M = -INFINITY;
+            for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * split_stride + HD));
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < S; ++s) {
+                const float *ps = base + s * split_stride;
+                const float ms = __ldcg(ps + HD);
+                const float e = ms == -INFINITY ? 0.f : expf(ms - M);
+                L = fmaf(__ldcg(ps + HD + 1), e, L);
+                const float4 o = ldcg4(ps + 4 * d4);
+                acc.x = fmaf(o.x, e, acc.x);
+                acc.y = fmaf(o.y, e, acc.y);
+                acc.z = fmaf(o.z, e, acc.z);
+                acc.w = fmaf(o.w, e, acc.w);
+            }
+            const float inv = 1.0f / L;
+            *reinterpret_cast<float4 *>(sm->act + r * QDIM + qh * HD + 4 * d4) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
         named_sync();
     }
 
     // ---------------------------------------------------------------- GEMV
 
-    // one (row, 512-unit) item: R dot products against the staged activations
-    template <int K>
-    __device__ __forceinline__ void item(const uint8_t *rowp, int u, int R, float *acc) {
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) acc[r] = 0.f;
-        if (WDT == WDT_Q8) {
-            const uint8_t *qp = rowp + u * 512;
-            const __half *sp = reinterpret_cast<const __half *>(rowp + K) + u * 16;
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                uint32_t w4 = *reinterpret_cast<const uint32_t *>(qp + 128 * g + 4 * lane);
-                float d = __half2float(sp[4 * g + (lane >> 3)]);
-                float q0, q1, q2, q3;
-                dq4(w4, q0, q1, q2, q3);
-#pragma unroll
-                for (int r = 0; r < RMAX; ++r) {
-                    if (r < R) {
-                        float4 xv = *reinterpret_cast<const float4 *>(sm->act + r * K + u * 512 + 128 * g + 4 * lane);
-                        float p = q0 * xv.x;
-                        p = fmaf(q1, xv.y, p);
-                        p = fmaf(q2, xv.z, p);
-                        p = fmaf(q3, xv.w, p);
-                        acc[r] = fmaf(d, p, acc[r]);
-                    }
-                }
-            }
-        } else {
-            const float *wp = reinterpret_cast<const float *>(rowp) + u * 512;
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                float4 w = *reinterpret_cast<const float4 *>(wp + 128 * g + 4 * lane);
-#pragma unroll
-                for (int r = 0; r < RMAX; ++r) {
-                    if (r < R) {
-                        float4 xv = *reinterpret_cast<const float4 *>(sm->act + r * K + u * 512 + 128 * g + 4 * lane);
-                        float p = acc[r];
-                        p = fmaf(w.x, xv.x, p);
-                        p = fmaf(w.y, xv.y, p);
-                        p = fmaf(w.z, xv.z, p);
-                        p = fmaf(w.w, xv.w, p);
-                        acc[r] = p;
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r)
-            if (r < R) acc[r] = warp_sum(acc[r]);
-    }
-
     // Epilogue kinds
-    enum Epi { E_STORE, E_ADD, E_SWIGLU, E_HEAD, E_HEAD0 };
+    enum Epi { E_STORE, E_RESID, E_SWIGLU, E_HEAD, E_HEAD0 };
 
-    // GEMV over this CTA's slice of matrix m; activations already staged in
-    // sm->act as [R][K].  Output per kind:
-    //  E_STORE: out[r*ld + row] = y      E_ADD: out[r*ld + row] += y
+    // GEMV over this CTA's slice of matrix m; activations staged in sm->act
+    // as [R][K].  Work items: (row pair, 1024-wide K segment) per warp, the
+    // activations loaded once for both rows; partial sums per (row, segment).
+    //  E_STORE: out[r*ld + row] = y
+    //  E_RESID: residual row: xs[r][row-c0] += y, out[r*H + row] = xs
     //  E_SWIGLU: out[r*ld + row/2] = silu(y_gate) * y_up
-    //  E_HEAD / E_HEAD0: out[row] = y (R == 1), argmax key of the CTA in
-    //  sm->keys[0]; E_HEAD0 applies ChooseCode0's processors to the key.
+    //  E_HEAD / E_HEAD0: out[row] = y (R == 1), the CTA's argmax key to
+    //  job->s.arg; E_HEAD0 applies ChooseCode0's processors first.
     template <int K>
     __device__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld) {
-        constexpr int UNITS = K / 512;
+        constexpr int SEG = K / 1024;
         const int rb = row_bytes(WDT, K);
-        int n = mat_rows(m, head_rows);
+        const int n = mat_rows(m, head_rows);
         int r0, r1;
         mat_slice(m, n, blockIdx.x, gridDim.x, r0, r1);
-        int sr = stage_rows(WDT, K, m);
+        const int sr = stage_rows(WDT, K, m);
         unsigned long long best = 0ull;
         for (int cr = r0; cr < r1; cr += sr) {
-            int nr = min(sr, r1 - cr);
-            int slot = seq % NSTAGES;
-            uint32_t par = (seq / NSTAGES) & 1;
+            const int nr = min(sr, r1 - cr);
+            const int slot = seq % NSTAGES;
+            // partials of this chunk; the buffer was last read in the epilogue
+            // of chunk seq-2, which every thread finished before the barrier
+            // of chunk seq-1
+            float *part = sm->part[seq & 1];
+            const uint32_t par = (seq / NSTAGES) & 1;
             // every thread waits (bounded); a timeout raises abort_flag, read
             // by all after the named barrier below, so the exit is uniform
-            bool got = ok && mbar_wait(&sm->full[slot], par, &sm->abort_flag);
+            const bool got = ok && mbar_wait(&sm->full[slot], par, &sm->abort_flag);
             if (!got) fail(ERR_TIMEOUT, 100 + m);
             const uint8_t *base = sm->ring[slot];
-            int items = got ? nr * UNITS : 0;
+            const int npairs = (nr + 1) >> 1;
+            const int items = got ? npairs * SEG : 0;
             for (int it = warp; it < items; it += NCW) {
-                int row = it / UNITS, u = it - row * UNITS;
-                float acc[RMAX];
-                item<K>(base + row * rb, u, R, acc);
-                if (lane == 0) {
+                const int pair = it / SEG, seg = it - pair * SEG;
+                const int ra = 2 * pair;
+                const bool two = ra + 1 < nr;
+                const uint8_t *rowa = base + ra * rb;
+                const uint8_t *rowb = two ? rowa + rb : rowa;
+                float aa[RMAX], ab[RMAX];
 #pragma unroll
-                    for (int r = 0; r < RMAX; ++r)
-                        if (r < R) sm->part[it * RMAX + r] = acc[r];
+                for (int r = 0; r < RMAX; ++r) aa[r] = ab[r] = 0.f;
+#pragma unroll
+                for (int uu = 0; uu < 2; ++uu) {
+                    const int u = seg * 2 + uu;
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int e = u * 512 + 128 * g + 4 * lane;  // first of this lane's 4 elements
+                        float4 wa, wb;
+                        float da = 1.f, db = 1.f;
+                        if (WDT == WDT_Q8) {
+                            wa = dq4(*reinterpret_cast<const uint32_t *>(rowa + e));
+                            wb = dq4(*reinterpret_cast<const uint32_t *>(rowb + e));
+                            da = __half2float(reinterpret_cast<const __half *>(rowa + K)[e >> 5]);
+                            db = __half2float(reinterpret_cast<const __half *>(rowb + K)[e >> 5]);
+                        } else {
+                            wa = *reinterpret_cast<const float4 *>(rowa + 4 * e);
+                            wb = *reinterpret_cast<const float4 *>(rowb + 4 * e);
+                        }
+#pragma unroll
+                        for (int r = 0; r < RMAX; ++r) {
+                            if (r < R) {
+                                const float4 xv = *reinterpret_cast<const float4 *>(sm->act + r * K + e);
+                                float pa = wa.x * xv.x, pb = wb.x * xv.x;
+                                pa = fmaf(wa.y, xv.y, pa);
+                                pb = fmaf(wb.y, xv.y, pb);
+                                pa = fmaf(wa.z, xv.z, pa);
+                                pb = fmaf(wb.z, xv.z, pb);
+                                pa = fmaf(wa.w, xv.w, pa);
+                                pb = fmaf(wb.w, xv.w, pb);
+                                if (WDT == WDT_Q8) {
+                                    aa[r] = fmaf(da, pa, aa[r]);
+                                    ab[r] = fmaf(db, pb, ab[r]);
+                                } else {
+                                    aa[r] += pa;
+                                    ab[r] += pb;
+                                }
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < RMAX; ++r) {
+                    if (r < R) {
+                        const float s = warp_sum2(aa[r], ab[r], lane);
+                        if (lane == 0) part[(ra * SEG + seg) * RMAX + r] = s;
+                        if (lane == 16 && two) part[((ra + 1) * SEG + seg) * RMAX + r] = s;
+                    }
                 }
             }
             named_sync();
@@ -516,52 +669,52 @@ struct Compute {
             }
             ++seq;
             if (kind == E_SWIGLU) {
-                int npairs = nr / 2;
-                for (int idx = tid; idx < npairs * R; idx += NCT) {
-                    int p = idx / R, r = idx - p * R;
+                const int np = nr / 2;
+                for (int idx = tid; idx < np * R; idx += NCT) {
+                    const int p = idx / R, r = idx - p * R;
                     float g = 0.f, v = 0.f;
 #pragma unroll
-                    for (int u = 0; u < UNITS; ++u) {
-                        g += sm->part[((2 * p) * UNITS + u) * RMAX + r];
-                        v += sm->part[((2 * p + 1) * UNITS + u) * RMAX + r];
+                    for (int sg = 0; sg < SEG; ++sg) {
+                        g += part[((2 * p) * SEG + sg) * RMAX + r];
+                        v += part[((2 * p + 1) * SEG + sg) * RMAX + r];
                     }
-                    float s = g / (1.0f + expf(-g));
+                    const float s = g / (1.0f + expf(-g));
                     out[r * ld + (cr + 2 * p) / 2] = s * v;
                 }
             } else {
                 for (int idx = tid; idx < nr * R; idx += NCT) {
-                    int row = idx / R, r = idx - row * R;
+                    const int row = idx / R, r = idx - row * R;
                     float y = 0.f;
 #pragma unroll
-                    for (int u = 0; u < UNITS; ++u) y += sm->part[(row * UNITS + u) * RMAX + r];
-                    int orow = cr + row;
+                    for (int sg = 0; sg < SEG; ++sg) y += part[(row * SEG + sg) * RMAX + r];
+                    const int orow = cr + row;
                     if (kind == E_STORE) {
                         out[r * ld + orow] = y;
-                    } else if (kind == E_ADD) {
-                        out[r * ld + orow] = out[r * ld + orow] + y;
+                    } else if (kind == E_RESID) {
+                        const float v = sm->xs[r][orow - c0] + y;
+                        sm->xs[r][orow - c0] = v;
+                        out[r * H + orow] = v;
                     } else {
                         out[orow] = y;
-                        float w = y;
-                        if (kind == E_HEAD0) w = choose0_value(orow, y);
-                        unsigned long long k = argkey(w, orow);
+                        const float w = kind == E_HEAD0 ? choose0_value(orow, y) : y;
+                        const unsigned long long k = argkey(w, orow);
                         best = k > best ? k : best;
                     }
                 }
             }
-            named_sync();
         }
         if (kind == E_HEAD || kind == E_HEAD0) {
             // CTA-wide max of the keys
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
-                unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
                 best = t > best ? t : best;
             }
             if (lane == 0) sm->keys[warp] = best;
             named_sync();
             if (tid == 0) {
                 unsigned long long b = 0ull;
-                for (int w = 0; w < NCW; ++w) b = sm->keys[w] > b ? sm->keys[w] : b;
+                for (int w2 = 0; w2 < NCW; ++w2) b = sm->keys[w2] > b ? sm->keys[w2] : b;
                 job->s.arg[blockIdx.x] = b;
             }
         }
@@ -571,7 +724,7 @@ struct Compute {
     // the last 1024 ids forbidden but eos, eos forbidden before 2 frames,
     // repetition penalty once per distinct code already returned
     __device__ __forceinline__ float choose0_value(int i, float s) {
-        int vocab = job->tvocab;
+        const int vocab = job->tvocab;
         if (i >= vocab - 1024 && i != job->eos) return -INFINITY;
         if (i == job->eos && hist_now < 2) return -INFINITY;
         if (job->penalty != 1.0f && job->seen[i]) return s > 0.f ? __fdiv_rn(s, job->penalty) : s * job->penalty;
@@ -582,12 +735,12 @@ struct Compute {
     __device__ int reduce_argmax() {
         unsigned long long b = 0ull;
         for (int i = lane; i < static_cast<int>(gridDim.x); i += 32) {
-            unsigned long long k = *reinterpret_cast<volatile unsigned long long *>(job->s.arg + i);
+            const unsigned long long k = __ldcg(job->s.arg + i);
             b = k > b ? k : b;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
             b = t > b ? t : b;
         }
         return key_index(b);
@@ -595,50 +748,85 @@ struct Compute {
 
     // ---------------------------------------------------------------- attention
 
-    // P2: per (kv head h, split s): q/k norm + RoPE, KV append (split 0),
-    // online-softmax attention over positions [p0, p1), partials to global;
-    // the last split of head h to finish combines them into attn.
+    // The attention item of this CTA for a context of T positions: kv head
+    // h, split s over positions [p0, p1); false when the CTA has none.
+    __device__ __forceinline__ bool att_item(int T, int &S, int &h, int &s, int &p0, int &p1) {
+        S = att_splits(T, gridDim.x);
+        const int C = (T + S - 1) / S;
+        const int item = blockIdx.x;
+        if (item >= HKV * S) return false;
+        h = item / S;
+        s = item - h * S;
+        p0 = s * C;
+        p1 = min(T, p0 + C);
+        return true;
+    }
+
+    // Issued at the end of P1, before the barrier: the cached K/V rows of the
+    // first tile of this CTA's split (positions < L0, written in earlier
+    // steps), bulk-copied into sm->kv.  Thread 0.
+    __device__ void prefetch_kv(const DCtx &kv, int layer, int R, int L0) {
+        if (tid == 0) {
+            sm->kv_rows = 0;
+            int S, h, s, p0, p1;
+            if (ok && att_item(L0 + R, S, h, s, p0, p1)) {
+                const int n = min(min(p1, L0), p0 + ATT_TILE) - p0;
+                if (n > 0) {
+                    const size_t off = ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + p0) * HD;
+                    // the rows were written through the generic proxy
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    mbar_arrive_tx(&sm->kvbar, static_cast<uint32_t>(2 * n * HD * 4));
+                    bulk_g2s(&sm->kv[0][0][0], kv.k + off, static_cast<uint32_t>(n * HD * 4), &sm->kvbar);
+                    bulk_g2s(&sm->kv[1][0][0], kv.v + off, static_cast<uint32_t>(n * HD * 4), &sm->kvbar);
+                    sm->kv_rows = n;
+                }
+            }
+        }
+    }
+
+    // P2 for this CTA's item: q (heads 2h, 2h+1) / k / v of the new rows
+    // normed and rotated, the new K/V appended to the cache (split 0), then
+    // online-softmax attention over [p0, p1) with positions spread over the
+    // warps; the partial (o, max, sum) of every (row, q head) to global.
     __device__ void attention(const DLayer &Ly, const DCtx &kv, int layer, int R, int L0, float eps) {
         const int T = L0 + R;
-        int S = min(static_cast<int>(gridDim.x) / HKV, (T + 15) / 16);
-        if (S < 1) S = 1;
-        const int C = (T + S - 1) / S;
-        const int item_id = blockIdx.x;
-        if (item_id >= HKV * S) return;
-        const int h = item_id / S, s = item_id - h * S;
-        const int p0 = s * C, p1 = min(T, p0 + C);
-        // shared layout inside sm->act: q[R][2][HD] | kn[R][HD] | vn[R][HD] | kt[32][HD] | vt[32][HD]
+        int S, h, s, p0, p1;
+        if (!att_item(T, S, h, s, p0, p1)) return;
+        const bool prefetched = sm->kv_rows > 0;
+        // shared layout inside sm->act: q[R][2][HD] | kn[R][HD] | vn[R][HD] | warp states
         float *qs = sm->act;
         float *kn = qs + RMAX * 2 * HD;
         float *vn = kn + RMAX * HD;
-        float *kt = vn + RMAX * HD;
-        float *vt = kt + 32 * HD;
+        float *wst = vn + RMAX * HD;  // [NCW][PSTRIDE]
         const int half = HD / 2;
-        // 1. q (heads 2h, 2h+1), k, v of the new rows: norm + RoPE
+        // 1. the new rows
         for (int vec = warp; vec < 4 * R; vec += NCW) {
-            int r = vec >> 2, t = vec & 3;  // t: 0,1 = q heads, 2 = k, 3 = v
+            const int r = vec >> 2, t = vec & 3;  // t: 0,1 = q heads, 2 = k, 3 = v
             const float *src = job->s.qkv + r * QKV_ROWS;
-            int off = t < 2 ? (2 * h + t) * HD : (t == 2 ? QDIM + h * HD : QDIM + KVDIM + h * HD);
-            float4 x = *reinterpret_cast<const float4 *>(src + off + 4 * lane);
+            const int off = t < 2 ? (2 * h + t) * HD : (t == 2 ? QDIM + h * HD : QDIM + KVDIM + h * HD);
+            const float4 x = ldcg4(src + off + 4 * lane);
             float y[4] = {x.x, x.y, x.z, x.w};
             if (t < 3) {
                 const float *nw = t < 2 ? Ly.q_norm : Ly.k_norm;
-                float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
-                float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) y[j] = nw[4 * lane + j] * (y[j] * inv);
+                const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+                const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
+                const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
+                y[0] = g.x * (y[0] * inv);
+                y[1] = g.y * (y[1] * inv);
+                y[2] = g.z * (y[2] * inv);
+                y[3] = g.w * (y[3] * inv);
                 const int pos = L0 + r;
-                const float *cs = job->rope_cos + static_cast<size_t>(pos) * half;
-                const float *sn = job->rope_sin + static_cast<size_t>(pos) * half;
+                const int e0 = (4 * lane) & (half - 1);
+                const float4 cs =
+                    *reinterpret_cast<const float4 *>(job->rope_cos + static_cast<size_t>(pos) * half + e0);
+                const float4 sn =
+                    *reinterpret_cast<const float4 *>(job->rope_sin + static_cast<size_t>(pos) * half + e0);
+                const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
                 float o[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float partner = __shfl_xor_sync(0xffffffffu, y[j], 16);
-                    int e = 4 * lane + j;
-                    if (e < half)
-                        o[j] = y[j] * cs[e] - partner * sn[e];
-                    else
-                        o[j] = y[j] * cs[e - half] + partner * sn[e - half];
+                    const float partner = __shfl_xor_sync(0xffffffffu, y[j], 16);
+                    o[j] = lane < 16 ? y[j] * cv[j] - partner * sv[j] : y[j] * cv[j] + partner * sv[j];
                 }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) y[j] = o[j];
@@ -651,47 +839,56 @@ struct Compute {
                 *reinterpret_cast<float4 *>(cache + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
             }
         }
+        if (prefetched) {
+            // every thread waits for the tile (bounded)
+            if (!mbar_wait(&sm->kvbar, kv_phase, &sm->abort_flag)) fail(ERR_TIMEOUT, 40);
+            kv_phase ^= 1u;
+        }
         named_sync();
-        // 2. online softmax over [p0, p1), 32-position tiles
+        if (tid == 0) sm->kv_rows = 0;
+        // 2. online softmax: warps grouped by (row, q head), positions strided
         const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-        float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-        const int combo = warp;  // (r, qh) = (combo >> 1, combo & 1)
+        const int nc = 2 * R, npw = NCW / nc;
+        const int combo = warp / npw, sub = warp - combo * npw;
+        const bool active = combo < nc;
         const int cr = combo >> 1, cq = combo & 1;
+        float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
         const float *kbase = kv.k + (static_cast<size_t>(layer) * HKV + h) * kv.max_pos * HD;
         const float *vbase = kv.v + (static_cast<size_t>(layer) * HKV + h) * kv.max_pos * HD;
-        for (int tp = p0; tp < p1; tp += 32) {
-            int nt = min(32, p1 - tp);
-            for (int i = tid; i < nt * (HD / 4); i += NCT) {
-                int pp = i / (HD / 4), d4 = i - pp * (HD / 4);
-                int p = tp + pp;
-                float4 kk, vv;
-                if (p < L0) {
-                    kk = reinterpret_cast<const float4 *>(kbase + static_cast<size_t>(p) * HD)[d4];
-                    vv = reinterpret_cast<const float4 *>(vbase + static_cast<size_t>(p) * HD)[d4];
-                } else {
-                    kk = reinterpret_cast<const float4 *>(kn + (p - L0) * HD)[d4];
-                    vv = reinterpret_cast<const float4 *>(vn + (p - L0) * HD)[d4];
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (active) q = *reinterpret_cast<const float4 *>(qs + (cr * 2 + cq) * HD + 4 * lane);
+        for (int tp = p0; tp < p1; tp += ATT_TILE) {
+            const int nt = min(ATT_TILE, p1 - tp);
+            const int cached = max(0, min(nt, L0 - tp));
+            if (tp != p0 || !prefetched) {
+                // a tile that was not prefetched: plain loads of its cached rows
+                if (tp != p0) named_sync();
+                for (int i = tid; i < cached * (HD / 4); i += NCT) {
+                    const int pp = i / (HD / 4), d4 = i - pp * (HD / 4);
+                    reinterpret_cast<float4 *>(&sm->kv[0][pp][0])[d4] =
+                        ldcg4(kbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
+                    reinterpret_cast<float4 *>(&sm->kv[1][pp][0])[d4] =
+                        ldcg4(vbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
                 }
-                reinterpret_cast<float4 *>(kt + pp * HD)[d4] = kk;
-                reinterpret_cast<float4 *>(vt + pp * HD)[d4] = vv;
+                named_sync();
             }
-            named_sync();
-            if (combo < 2 * R) {
-                float4 q = *reinterpret_cast<const float4 *>(qs + (cr * 2 + cq) * HD + 4 * lane);
-                for (int pp = 0; pp < nt; ++pp) {
-                    int p = tp + pp;
+            if (active && ok) {
+                for (int pp = sub; pp < nt; pp += npw) {
+                    const int p = tp + pp;
                     if (p > L0 + cr) break;  // causal
-                    float4 k = *reinterpret_cast<const float4 *>(kt + pp * HD + 4 * lane);
+                    const float *kp = p < L0 ? &sm->kv[0][pp][0] : kn + (p - L0) * HD;
+                    const float *vp = p < L0 ? &sm->kv[1][pp][0] : vn + (p - L0) * HD;
+                    const float4 k = *reinterpret_cast<const float4 *>(kp + 4 * lane);
                     float d = q.x * k.x;
                     d = fmaf(q.y, k.y, d);
                     d = fmaf(q.z, k.z, d);
                     d = fmaf(q.w, k.w, d);
                     d = warp_sum(d) * scale;
-                    float mn = fmaxf(m, d);
-                    float corr = expf(m - mn);
-                    float e = expf(d - mn);
+                    const float mn = fmaxf(m, d);
+                    const float corr = expf(m - mn);
+                    const float e = expf(d - mn);
                     l = l * corr + e;
-                    float4 v = *reinterpret_cast<const float4 *>(vt + pp * HD + 4 * lane);
+                    const float4 v = *reinterpret_cast<const float4 *>(vp + 4 * lane);
                     o[0] = fmaf(e, v.x, o[0] * corr);
                     o[1] = fmaf(e, v.y, o[1] * corr);
                     o[2] = fmaf(e, v.z, o[2] * corr);
@@ -699,43 +896,44 @@ struct Compute {
                     m = mn;
                 }
             }
-            named_sync();
         }
-        // 3. partials
-        if (combo < 2 * R) {
-            float *pp = job->s.part + ((static_cast<size_t>(item_id) * RMAX + cr) * 2 + cq) * PSTRIDE;
-            *reinterpret_cast<float4 *>(pp + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+        // 3. merge the warps of each (row, q head), partial to global
+        if (active) {
+            float *ws = wst + warp * PSTRIDE;
+            *reinterpret_cast<float4 *>(ws + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
             if (lane == 0) {
-                pp[HD] = m;
-                pp[HD + 1] = l;
+                ws[HD] = m;
+                ws[HD + 1] = l;
             }
         }
-        __threadfence();
         named_sync();
-        if (tid == 0) sm->bcast = (atomicAdd(job->s.comb + h, 1u) == static_cast<unsigned>(S - 1));
-        named_sync();
-        if (!sm->bcast) return;
-        // 4. last split of head h: combine
-        __threadfence();
-        for (int idx = tid; idx < R * 2 * HD; idx += NCT) {
-            int r = idx / (2 * HD), rem = idx - r * 2 * HD, q = rem / HD, d = rem - q * HD;
+        if (warp < nc) {
+            const int r = warp >> 1, qq = warp & 1;
+            const float *w0 = wst + (warp * npw) * PSTRIDE;
             float M = -INFINITY;
-            for (int j = 0; j < S; ++j) {
-                const volatile float *pj =
-                    job->s.part + ((static_cast<size_t>(h * S + j) * RMAX + r) * 2 + q) * PSTRIDE;
-                M = fmaxf(M, pj[HD]);
+            for (int j = 0; j < npw; ++j) M = fmaxf(M, w0[j * PSTRIDE + HD]);
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (M != -INFINITY) {
+                for (int j = 0; j < npw; ++j) {
+                    const float *wj = w0 + j * PSTRIDE;
+                    const float mj = wj[HD];
+                    const float e = mj == -INFINITY ? 0.f : expf(mj - M);
+                    L = fmaf(wj[HD + 1], e, L);
+                    const float4 v = *reinterpret_cast<const float4 *>(wj + 4 * lane);
+                    acc.x = fmaf(v.x, e, acc.x);
+                    acc.y = fmaf(v.y, e, acc.y);
+                    acc.z = fmaf(v.z, e, acc.z);
+                    acc.w = fmaf(v.w, e, acc.w);
+                }
             }
-            float L = 0.f, acc = 0.f;
-            for (int j = 0; j < S; ++j) {
-                const volatile float *pj =
-                    job->s.part + ((static_cast<size_t>(h * S + j) * RMAX + r) * 2 + q) * PSTRIDE;
-                float w = expf(pj[HD] - M);
-                L += pj[HD + 1] * w;
-                acc += pj[d] * w;
+            float *pp = job->s.part + ((static_cast<size_t>(h * S + s) * RMAX + r) * 2 + qq) * PSTRIDE;
+            *reinterpret_cast<float4 *>(pp + 4 * lane) = acc;
+            if (lane == 0) {
+                pp[HD] = M;
+                pp[HD + 1] = L;
             }
-            job->s.attn[r * QDIM + (2 * h + q) * HD + d] = acc / L;
         }
-        if (tid == 0) job->s.comb[h] = 0u;
     }
 
     // ---------------------------------------------------------------- stack
@@ -745,53 +943,64 @@ struct Compute {
     __device__ void stack(const DStack &st, const DCtx &kv, int R, int L0, const float *const *in0,
                           const float *const *in1, const float *const *in2) {
         const Scratch &S = job->s;
-        int c0, c1;
-        mat_slice(M_O, H, blockIdx.x, gridDim.x, c0, c1);
         const float *xr[RMAX];
         for (int r = 0; r < RMAX; ++r) xr[r] = S.x + r * H;
+        const int nsplit = att_splits(L0 + R, gridDim.x);
         for (int l = 0; l < st.layers && ok; ++l) {
             const DLayer Ly = st.layer[l];
             // P1
             if (l == 0)
-                stage_norm(in0, in1, in2, R, Ly.in_norm, st.eps, S.x, c0, c1);
+                stage_norm(in0, in1, in2, R, Ly.in_norm, st.eps, true);
             else
-                stage_norm(xr, nullptr, nullptr, R, Ly.in_norm, st.eps, nullptr, 0, 0);
+                stage_norm(xr, nullptr, nullptr, R, Ly.in_norm, st.eps, false);
+            mark(10);
             gemv<H>(M_QKV, 0, R, E_STORE, S.qkv, QKV_ROWS);
+            mark(11);
+            prefetch_kv(kv, l, R, L0);
             grid_sync(1);
             if (!ok) return;
             // P2
             attention(Ly, kv, l, R, L0, st.eps);
+            mark(21);
             grid_sync(2);
             if (!ok) return;
             // P3
-            stage_copy(S.attn, R, QDIM);
-            gemv<QDIM>(M_O, 0, R, E_ADD, S.x, H);
+            stage_attn(R, nsplit);
+            mark(30);
+            gemv<QDIM>(M_O, 0, R, E_RESID, S.x, H);
+            mark(31);
             grid_sync(3);
             if (!ok) return;
             // P4
-            stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, st.eps, nullptr, 0, 0);
+            stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, st.eps, false);
+            mark(40);
             gemv<H>(M_GU, 0, R, E_SWIGLU, S.act, INTER);
+            mark(41);
             grid_sync(4);
             if (!ok) return;
             // P5
             stage_copy(S.act, R, INTER);
-            gemv<INTER>(M_D, 0, R, E_ADD, S.x, H);
+            mark(50);
+            gemv<INTER>(M_D, 0, R, E_RESID, S.x, H);
+            mark(51);
             grid_sync(5);
         }
     }
 
-    // final norm of the last row, head GEMV; the normed state to `hidden`
+    // final norm of the last row, head GEMV; the normed state to hidden_out
     __device__ void head(const DStack &st, int R, int rows, int kind, float *hidden_out) {
         const Scratch &S = job->s;
         const float *last[1] = {S.x + (R - 1) * H};
-        stage_norm(last, nullptr, nullptr, 1, st.final_norm, st.eps, nullptr, 0, 0);
+        stage_norm(last, nullptr, nullptr, 1, st.final_norm, st.eps, false);
         if (hidden_out && blockIdx.x == 0)
             for (int i = tid; i < H; i += NCT) hidden_out[i] = sm->act[i];
+        mark(60);
         gemv<H>(M_HEAD, rows, 1, kind, S.logits, 0);
+        mark(61);
     }
 };
 
-// the program, walked by both roles
+// the program, walked by the producer
 template <int WDT, class V>
 __device__ void walk_stack(V &v, const DStack &st) {
     for (int l = 0; l < st.layers; ++l) {
@@ -829,16 +1038,19 @@ __device__ void compute(Smem *sm, const Job &job) {
     c.tid = threadIdx.x;
     c.warp = threadIdx.x >> 5;
     c.lane = threadIdx.x & 31;
+    mat_slice(M_O, H, blockIdx.x, gridDim.x, c.c0, c.c1);
     const Scratch &S = job.s;
+    c.mark(1);
     if (job.mode == 0) {
         const float *in[RMAX];
         for (int r = 0; r < RMAX; ++r) in[r] = job.xin + r * H;
         c.stack(job.st, job.ctx, job.rows, job.L0, in, nullptr, nullptr);
-        if (job.head_w && c.ok) c.head(job.st, job.rows, job.head_rows, Compute<WDT>::E_HEAD, S.hidden);
-        else if (c.ok) {
+        if (job.head_w && c.ok) {
+            c.head(job.st, job.rows, job.head_rows, Compute<WDT>::E_HEAD, S.hidden);
+        } else if (c.ok) {
             // no head: still return the normed last state
             const float *last[1] = {S.x + (job.rows - 1) * H};
-            c.stage_norm(last, nullptr, nullptr, 1, job.st.final_norm, job.st.eps, nullptr, 0, 0);
+            c.stage_norm(last, nullptr, nullptr, 1, job.st.final_norm, job.st.eps, false);
             if (blockIdx.x == 0)
                 for (int i = c.tid; i < H; i += NCT) S.hidden[i] = sm->act[i];
         }
@@ -846,16 +1058,15 @@ __device__ void compute(Smem *sm, const Job &job) {
         FrameState *fs = job.fs;
         const int code0 = fs->next_code0;
         const int tlen = fs->tlen;
+        const int step = fs->step;
         c.hist_now = fs->hist_len + 1;
-        int c0, c1;
-        mat_slice(M_O, H, blockIdx.x, gridDim.x, c0, c1);
         // the talker input starts as the code-0 embedding (talker.pas:669)
         const float *e0 = job.codec_emb + static_cast<size_t>(code0) * H;
-        for (int i = c0 + c.tid; i < c1; i += NCT) S.xt[i] = e0[i];
+        for (int i = c.c0 + c.tid; i < c.c1; i += NCT) S.xt[i] = e0[i];
         if (blockIdx.x == 0 && c.tid == 0) {
             job.seen[code0] = 1;
             fs->codes[0] = code0;
-            if (job.codes_hist && fs->step < job.codes_cap) job.codes_hist[fs->step * job.groups] = code0;
+            if (job.codes_hist && step < job.codes_cap) job.codes_hist[step * job.groups] = code0;
         }
         // predictor: [talker state, codec_emb[code0]] then one row per group
         int code = code0;
@@ -870,7 +1081,7 @@ __device__ void compute(Smem *sm, const Job &job) {
                 in[0] = job.pred_emb + (static_cast<size_t>(g - 1) * job.pvocab + code) * H;
                 R = 1;
             }
-            int L0 = g == 0 ? 0 : g + 1;
+            const int L0 = g == 0 ? 0 : g + 1;
             c.stack(job.pst, job.pctx, R, L0, in, nullptr, nullptr);
             if (!c.ok) break;
             c.head(job.pst, R, job.pvocab, Compute<WDT>::E_HEAD, nullptr);
@@ -879,12 +1090,12 @@ __device__ void compute(Smem *sm, const Job &job) {
             code = c.reduce_argmax();
             if (blockIdx.x == 0 && c.tid == 0) {
                 fs->codes[g + 1] = code;
-                if (job.codes_hist && fs->step < job.codes_cap) job.codes_hist[fs->step * job.groups + g + 1] = code;
+                if (job.codes_hist && step < job.codes_cap) job.codes_hist[step * job.groups + g + 1] = code;
             }
             if (g + 1 < job.groups - 1) {
                 // codes 1..14 enter the talker input now; code 15 at its staging
                 const float *e = job.pred_emb + (static_cast<size_t>(g) * job.pvocab + code) * H;
-                for (int i = c0 + c.tid; i < c1; i += NCT) S.xt[i] = S.xt[i] + e[i];
+                for (int i = c.c0 + c.tid; i < c.c1; i += NCT) S.xt[i] = S.xt[i] + e[i];
             }
         }
         if (c.ok) {
@@ -892,7 +1103,6 @@ __device__ void compute(Smem *sm, const Job &job) {
             const float *in0[RMAX] = {S.xt, nullptr, nullptr, nullptr};
             const float *in1[RMAX] = {job.pred_emb + (static_cast<size_t>(G - 2) * job.pvocab + code) * H, nullptr,
                                       nullptr, nullptr};
-            const int step = fs->step;
             const float *tr = step < job.trailing_rows ? job.trailing + static_cast<size_t>(step) * H : job.tts_pad;
             const float *in2[RMAX] = {tr, nullptr, nullptr, nullptr};
             c.stack(job.tst, job.tctx, 1, tlen, in0, in1, in2);
@@ -900,7 +1110,7 @@ __device__ void compute(Smem *sm, const Job &job) {
             if (c.ok) c.grid_sync(8);
             if (c.ok && blockIdx.x == 0 && c.warp == 0) {
                 // ChooseCode0 of the next frame; the history holds this frame's code 0
-                int next = c.reduce_argmax();
+                const int next = c.reduce_argmax();
                 if (c.lane == 0) {
                     fs->next_code0 = next;
                     fs->done = next == job.eos ? 1 : 0;
@@ -911,8 +1121,14 @@ __device__ void compute(Smem *sm, const Job &job) {
             }
         }
     }
+    if (job.trace && blockIdx.x == 0 && c.tid == 0) {
+        c.mark(999);
+        *job.trace_n = c.ntrace;
+    }
+    // a K/V prefetch still in flight (abort path) must land before exit
+    c.cta_sync();
+    if (c.tid == 0 && sm->kv_rows > 0) mbar_wait(&sm->kvbar, c.kv_phase, nullptr);
     // exit: the last CTA out resets the barrier counters for the next launch
-    named_sync();
     if (c.tid == 0 && c.ok) {
         __threadfence();
         if (atomicAdd(S.bar + 1, 1u) == gridDim.x - 1) {
@@ -924,7 +1140,7 @@ __device__ void compute(Smem *sm, const Job &job) {
 }
 
 template <int WDT>
-__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const Job job) {
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ Job job) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem *sm = reinterpret_cast<Smem *>(smem_raw);
     if (threadIdx.x == 0) {
@@ -932,8 +1148,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const Job job) {
             mbar_init(&sm->full[i], 1);
             mbar_init(&sm->empty[i], 1);
         }
+        mbar_init(&sm->kvbar, 1);
         sm->abort_flag = 0;
         sm->consumed = 0;
+        sm->kv_rows = 0;
+        sm->barflag[0] = sm->barflag[1] = sm->barflag[2] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();

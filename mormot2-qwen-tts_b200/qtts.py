@@ -87,6 +87,7 @@ EXPORTS = {
     "qtts_talker_start": [P, P, I, P, I, P, P, P],
     "qtts_talker_next_frame": [P, P, PI],
     "qtts_talker_run": [P, I, P, PI],
+    "qtts_talker_trace_frame": [P, P, PI, P, I, PI],
     "qtts_talker_stream": [P, ctypes.POINTER(P)],
     "qtts_talker_probe": [P, P, P],
     "qtts_talker_step": [P, PI],
@@ -318,6 +319,16 @@ class QwenTalker:
         more = ctypes.c_int()
         check(lib().qtts_talker_next_frame(self.handle, _ptr(codes), ctypes.byref(more)))
         return bool(more.value)
+
+    def trace_frame(self, codes, cap=8192):
+        """next_frame with CTA 0's phase timestamps: returns (more, [(tag, ns)])."""
+        more = ctypes.c_int()
+        st = np.zeros(cap, np.uint64)
+        n = ctypes.c_int()
+        check(lib().qtts_talker_trace_frame(self.handle, _ptr(codes), ctypes.byref(more), _ptr(st), cap,
+                                            ctypes.byref(n)))
+        st = st[:n.value]
+        return bool(more.value), [(int(v >> np.uint64(48)), int(v & np.uint64(0xFFFFFFFFFFFF))) for v in st]
 
     def run(self, frames):
         """Up to `frames` frames back to back; returns codes [n][groups]."""
