@@ -143,6 +143,25 @@ int qtts_lm_reset(qtts_lm *lm);
  * to hidden (may be NULL) and the logits of head `head` to logits (NULL:
  * no head).  rows <= 0 does nothing. */
 int qtts_lm_forward(qtts_lm *lm, const float *x, int rows, int head, float *logits, float *hidden);
+/* The forward of qtts_lm_forward for callers that must not allocate device
+ * memory while they run it: a real-time synthesis thread, for which
+ * cudaMalloc/cudaFree (they can synchronise the whole device and block for
+ * milliseconds) are off limits, or a host whose GPU memory is all handed out
+ * by its own pool allocator.  No counterpart in the reference.  x
+ * [rows][hidden], logits (head rows) and hidden [hidden] are DEVICE pointers
+ * owned by the caller (logits/hidden may be NULL); x is read in place.  The
+ * call allocates nothing: the kernel's scratch is one static device array of
+ * 833,280 bytes (every GPU that loads the library holds it until exit),
+ * sized for at most 160 SMs and heads of at most 4096 rows; larger requests
+ * fail with QTTS_E_CAPACITY.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current:
+ * make that first call before any stream capture.  All calls on one GPU
+ * share its copy of the array, which keeps the last call's contents (each
+ * call first clears the barrier and error words it needs at zero): calls
+ * that overlap on the same GPU, from two threads or two lms, race and must
+ * be serialised by the caller.  Runs on the lm's stream and returns once the
+ * results are in the caller's buffers. */
+int qtts_lm_forward_noalloc(qtts_lm *lm, const float *x, int rows, int head, float *logits, float *hidden);
 /* TQwenLm.Length (lm.pas:136-138). */
 int qtts_lm_length(qtts_lm *lm, int *length);
 /* TQwenLm.Destroy (lm.pas:362-372): frees the cache, then the stack. */

@@ -17,6 +17,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1087,4 +1088,129 @@ extern "C" int qtts_quantize_q8_0(qtts_device *dev, const float *src, int64_t n,
     cudaFree(d_src);
     cudaFree(d_dst);
     return rc;
+}
+
+// ------------------------------------------------------------------ forward without allocation
+//
+// qtts_lm_forward_noalloc: the same forward as qtts_lm_forward, for callers
+// that must not allocate device memory while they run it -- a real-time
+// synthesis thread, for which cudaMalloc/cudaFree (which can synchronise the
+// whole device and block for milliseconds) is off limits, or a host
+// application whose GPU memory is all handed out by its own pool allocator.
+// Inputs and outputs are the caller's device buffers; the kernel's scratch
+// (residual rows, q/k/v, SwiGLU activations, attention partials, argmax keys,
+// barrier and error words) lives in one static device array instead of
+// buffers of the lm.  Limits: a grid of at most NOALLOC_MAX_SMS CTAs (one per
+// SM) and heads of at most NOALLOC_MAX_HEAD_ROWS rows.
+
+constexpr int NOALLOC_MAX_SMS = 160;
+constexpr int NOALLOC_MAX_HEAD_ROWS = 4096;
+
+namespace {
+constexpr size_t al256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+constexpr size_t NA_X = 0;
+constexpr size_t NA_QKV = NA_X + al256(static_cast<size_t>(RMAX) * H * 4);
+constexpr size_t NA_ACT = NA_QKV + al256(static_cast<size_t>(RMAX) * QKV_ROWS * 4);
+constexpr size_t NA_PART = NA_ACT + al256(static_cast<size_t>(RMAX) * INTER * 4);
+constexpr size_t NA_ARG =
+    NA_PART + al256(static_cast<size_t>(HKV) * (NOALLOC_MAX_SMS / HKV) * RMAX * 2 * PSTRIDE * 4);
+constexpr size_t NA_BAR = NA_ARG + al256(static_cast<size_t>(NOALLOC_MAX_SMS) * 8);
+constexpr size_t NA_ERR = NA_BAR + al256(16);
+constexpr size_t NA_LOGITS = NA_ERR + al256(16);
+constexpr size_t NA_HIDDEN = NA_LOGITS + al256(static_cast<size_t>(NOALLOC_MAX_HEAD_ROWS) * 4);
+constexpr size_t NA_XT = NA_HIDDEN + al256(H * 4);
+constexpr size_t NA_BYTES = NA_XT + al256(H * 4);  // 833,280 bytes
+}  // namespace
+
+// Every GPU that loads the library holds this array until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+// its device address, per device (taken once, with that device current)
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_ptr[256];
+
+static int noalloc_scratch(int ordinal, unsigned char **out) {
+    if (ordinal < 0 || ordinal >= 256) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: device %d", ordinal);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[ordinal]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_err(QTTS_E_CUDA, "qtts_lm_forward_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[ordinal] = p;
+    }
+    *out = static_cast<unsigned char *>(g_noalloc_ptr[ordinal]);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int head, float *logits,
+                                       float *hidden) {
+    if (!m) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: NULL lm");
+    if (rows <= 0) return QTTS_OK;
+    if (!x) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: x is NULL");
+    if (logits && (head < 0 || head >= static_cast<int>(m->heads->mats.size())))
+        return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: no head %d in %s", head, m->heads->name.c_str());
+    if (logits && m->heads->mats[head].rows > NOALLOC_MAX_HEAD_ROWS)
+        return set_err(QTTS_E_CAPACITY, "qtts_lm_forward_noalloc: head of %d rows, the static scratch holds %d",
+                       m->heads->mats[head].rows, NOALLOC_MAX_HEAD_ROWS);
+    if (m->dev->sms > NOALLOC_MAX_SMS)
+        return set_err(QTTS_E_CAPACITY, "qtts_lm_forward_noalloc: a grid of %d CTAs, the static scratch holds %d",
+                       m->dev->sms, NOALLOC_MAX_SMS);
+    if (m->len + rows > m->max_pos)
+        return set_err(QTTS_E_CAPACITY, "qtts_lm_forward_noalloc: %d + %d positions, the cache holds %d", m->len,
+                       rows, m->max_pos);
+    CK(cudaSetDevice(m->dev->ordinal));
+    unsigned char *sc = nullptr;
+    int rc = noalloc_scratch(m->dev->ordinal, &sc);
+    if (rc) return rc;
+    Runner r;
+    r.stream = m->run.stream;
+    r.grid = m->dev->sms;
+    r.block = nullptr;
+    r.h_err = nullptr;
+    r.s.x = reinterpret_cast<float *>(sc + NA_X);
+    r.s.qkv = reinterpret_cast<float *>(sc + NA_QKV);
+    r.s.act = reinterpret_cast<float *>(sc + NA_ACT);
+    r.s.part = reinterpret_cast<float *>(sc + NA_PART);
+    r.s.arg = reinterpret_cast<unsigned long long *>(sc + NA_ARG);
+    r.s.bar = reinterpret_cast<unsigned *>(sc + NA_BAR);
+    r.s.err = reinterpret_cast<int *>(sc + NA_ERR);
+    r.s.logits = logits ? logits : reinterpret_cast<float *>(sc + NA_LOGITS);
+    r.s.hidden = hidden ? hidden : reinterpret_cast<float *>(sc + NA_HIDDEN);
+    r.s.xt = reinterpret_cast<float *>(sc + NA_XT);
+    // the array keeps the last call's contents: the barrier counters and the
+    // error word must start at zero
+    CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+    CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
+    const int wdt = m->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    Job j = base_job(m);
+    j.s = r.s;
+    j.mode = 0;
+    j.st = dstack(m->stack);
+    j.ctx.k = m->k;
+    j.ctx.v = m->v;
+    j.ctx.max_pos = m->max_pos;
+    for (int r0 = 0; r0 < rows; r0 += RMAX) {
+        const int n = rows - r0 < RMAX ? rows - r0 : RMAX;
+        const bool last = r0 + n == rows;
+        j.xin = x + static_cast<size_t>(r0) * H;  // the caller's rows, read in place
+        j.rows = n;
+        j.L0 = m->len;
+        j.head_w = (last && logits) ? m->heads->mats[head].d : nullptr;
+        j.head_rows = (last && logits) ? m->heads->mats[head].rows : 0;
+        rc = launch(m->dev, r, j, wdt);
+        if (rc) return rc;
+        int err[2] = {0, 0};
+        CK(cudaMemcpyAsync(err, r.s.err, 8, cudaMemcpyDeviceToHost, r.stream));
+        CK(cudaStreamSynchronize(r.stream));
+        if (err[0] != 0) {
+            CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+            CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
+            CK(cudaStreamSynchronize(r.stream));
+            return set_err(err[0] == ERR_CAPACITY ? QTTS_E_CAPACITY : QTTS_E_TIMEOUT,
+                           "qtts_lm_forward_noalloc: device wait gave up (code %d at %d)", err[0], err[1]);
+        }
+        m->len += n;
+    }
+    return QTTS_OK;
 }

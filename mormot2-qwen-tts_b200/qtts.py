@@ -81,6 +81,7 @@ EXPORTS = {
     "qtts_lm_create": [P, P, I, ctypes.POINTER(P)],
     "qtts_lm_reset": [P],
     "qtts_lm_forward": [P, P, I, I, P, P],
+    "qtts_lm_forward_noalloc": [P, P, I, I, P, P],
     "qtts_lm_length": [P, PI],
     "qtts_lm_destroy": [P],
     "qtts_talker_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
@@ -277,6 +278,12 @@ class QwenLm:
         x = _f32(x)
         rows = x.size // self.hidden if rows is None else rows
         check(lib().qtts_lm_forward(self.handle, _ptr(x), rows, output, _ptr(logits), _ptr(hidden)))
+
+    def forward_noalloc(self, x_dev, rows, output=0, logits_dev=None, hidden_dev=None):
+        """qtts_lm_forward_noalloc: the same forward on device buffers the
+        caller owns (integer device addresses), with no allocation at all:
+        for callers that may not allocate device memory while they run."""
+        check(lib().qtts_lm_forward_noalloc(self.handle, x_dev, rows, output, logits_dev, hidden_dev))
 
     @property
     def length(self):
