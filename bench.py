@@ -133,10 +133,10 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def build_host_model(dtype, seed=SEED):
+def build_host_model(dtype, seed=SEED, tlayers=28, players=5):
     t0 = time.time()
-    tl, tf = synth.stack(seed, "talker", 28)
-    pl, pf = synth.stack(seed, "predictor", 5)
+    tl, tf = synth.stack(seed, "talker", tlayers)
+    pl, pf = synth.stack(seed, "predictor", players)
     m = dict(tl=tl, tf=tf, pl=pl, pf=pf, th=synth.talker_head(seed), ph=synth.predictor_heads(seed),
              ce=synth.codec_embedding(seed), pe=synth.predictor_embeddings(seed),
              pad=synth.text_rows(seed, 1, key=1)[0])
@@ -212,7 +212,9 @@ def dtype_name(dtype):
 
 
 def config_dict(dtype, args):
-    return {"workload": ("configs[1]: Q8_0, batch 1 per GPU, 40-row N(0,1) prompt, then K streaming frames"
+    extra = {} if (args.talker_layers, args.pred_layers) == (28, 5) else {
+        "layers_override": f"talker {args.talker_layers}, predictor {args.pred_layers} (profiling case, not a bench line)"}
+    return {**extra, "workload": ("configs[1]: Q8_0, batch 1 per GPU, 40-row N(0,1) prompt, then K streaming frames"
                          if dtype == "q8_0" else "configs[0]: f32, batch 1 per GPU, 128 prior positions, then K frames"),
             "model": "Qwen3-TTS-12Hz-0.6B talker (28 layers) + code predictor (5 layers, 15 heads), synthetic weights",
             "global_batch": args.gpus, "frames": args.steps, "prompt_rows": PROMPT_ROWS[dtype],
@@ -231,7 +233,7 @@ def gpu_arm(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local_rank))
     dtype = args.config
-    m = build_host_model(dtype)
+    m = build_host_model(dtype, tlayers=args.talker_layers, players=args.pred_layers)
     prompt = synth.prompt(SEED + 100 + rank, PROMPT_ROWS[dtype])
     K, W = args.steps, args.warmup
     dev = qtts.QwenDevice(local_rank)
@@ -312,8 +314,8 @@ def gpu_arm(args, rank, world, local_rank):
                          "CPU path, AVX2+FMA, OpenMP over output rows)"}
     if rank == 0:
         fps = world * K / (ms / 1000.0)
-        wb = weight_bytes_per_frame(dtype)
-        kv = sum(kv_bytes_frame(talker_len0 + f) for f in range(K)) / K
+        wb = weight_bytes_per_frame(dtype, args.talker_layers, args.pred_layers)
+        kv = sum(kv_bytes_frame(talker_len0 + f, args.talker_layers, args.pred_layers) for f in range(K)) / K
         alg = wb + kv  # algorithmic bytes per launch (one frame)
         per_launch_s = ms / 1000.0 / K
         peaks = measured_peaks()
@@ -362,6 +364,9 @@ def main():
     ap.add_argument("--config", choices=["q8_0", "f32"], default="q8_0")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller stacks for profiler captures only (the benchmark is 28 + 5)
+    ap.add_argument("--talker-layers", type=int, default=28)
+    ap.add_argument("--pred-layers", type=int, default=5)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
