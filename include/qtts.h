@@ -128,6 +128,11 @@ int qtts_heads_digest(qtts_heads *heads, uint32_t *crc);
 int qtts_heads_count(qtts_heads *heads, int *count);
 int qtts_heads_rows(qtts_heads *heads, int index, int *rows);
 int qtts_heads_bytes(qtts_heads *heads, int64_t *bytes);
+/* TInferBackend.Linear on a head (lm.pas:404-406: the reference applies the
+ * heads with fCpu.Linear), for many rows at once: y[rows][head rows] =
+ * x[rows][hidden] . head^T, host buffers.  Runs the tcgen05 GEMM (fp16
+ * operands, f32 accumulation). */
+int qtts_heads_linear(qtts_heads *heads, int index, const float *x, int rows, float *y);
 int qtts_heads_destroy(qtts_heads *heads);
 
 /* ------------------------------------------------------------------ lm */

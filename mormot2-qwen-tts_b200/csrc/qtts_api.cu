@@ -23,6 +23,9 @@
 
 #include "../../include/qtts.h"
 #include "qtts_decode.cuh"
+#include "qtts_gemm.cuh"
+
+#include <cudaTypedefs.h>
 
 using namespace qtts;
 
@@ -85,6 +88,11 @@ struct qtts_heads {
     int hidden, dtype;
     std::vector<HeadMat> mats;
     int64_t bytes;
+    // buffers of qtts_heads_linear (grown on demand)
+    float *lx = nullptr, *ly = nullptr;
+    __half *lh = nullptr;
+    int *lerr = nullptr;
+    size_t lrows = 0, lycap = 0;
 };
 
 struct Runner {  // scratch + stream of one lm (and of a talker built on it)
@@ -301,6 +309,79 @@ static uint32_t crc32c(uint32_t crc, const void *data, size_t n) {
     crc = ~crc;
     for (size_t i = 0; i < n; i++) crc = table[(crc ^ p[i]) & 0xff] ^ (crc >> 8);
     return ~crc;
+}
+
+// ------------------------------------------------------------------ tcgen05 GEMM (host)
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_cap, int box_rows) {
+    if (!g_encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (!fn || q != cudaDriverEntryPointSuccess) return set_err(QTTS_E_CUDA, "cuTensorMapEncodeTiled not found");
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows_cap)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(G_BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_err(QTTS_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return QTTS_OK;
+}
+
+template <int WDT, int BN>
+static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 grid, cudaStream_t st) {
+    static bool attr[2] = {false, false};
+    const size_t smem = sizeof(GemmSmem<BN>) + 1024;
+    if (!attr[WDT]) {
+        CK(cudaFuncSetAttribute(gemm_kernel<WDT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        attr[WDT] = true;
+    }
+    CUtensorMap map;
+    int rc = tensor_map_f16(&map, x, a.K, rows_cap, BN);
+    if (rc) return rc;
+    gemm_kernel<WDT, BN><<<grid, G_THREADS, smem, st>>>(a, map);
+    CK(cudaGetLastError());
+    return QTTS_OK;
+}
+
+// y[t][n] (+)= x[t][:] . w[n][:] for t < T (x: fp16 [rows_cap][K] on the
+// device, rows_cap >= T).  With `add`, the products are added to y (residual);
+// otherwise y is overwritten (zeroed first when the K split needs atomics).
+static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
+                bool add, int *err, cudaStream_t st) {
+    if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
+    const int bn = T <= 64 ? 64 : (T <= 128 ? 128 : 256);
+    const int tiles = ((n_rows + G_BM - 1) / G_BM) * ((T + bn - 1) / bn);
+    const int kb = k / G_BK;
+    int split = 1;
+    while (split * 2 <= kb && kb % (split * 2) == 0 && tiles * split * 2 <= 160) split *= 2;
+    GemmArgs a;
+    a.w = w;
+    a.n_rows = n_rows;
+    a.K = k;
+    a.T = T;
+    a.out = y;
+    a.ld = ld;
+    a.atomic = (add || split > 1) ? 1 : 0;
+    a.ksplit = split;
+    a.err = err;
+    if (!add && split > 1)
+        for (int t = 0; t < T; ++t) CK(cudaMemsetAsync(y + static_cast<size_t>(t) * ld, 0, n_rows * 4, st));
+    dim3 grid((n_rows + G_BM - 1) / G_BM, (T + bn - 1) / bn, split);
+    if (wdt == WDT_Q8) {
+        if (bn == 64) return gemm_launch_t<WDT_Q8, 64>(a, x, rows_cap, grid, st);
+        if (bn == 128) return gemm_launch_t<WDT_Q8, 128>(a, x, rows_cap, grid, st);
+        return gemm_launch_t<WDT_Q8, 256>(a, x, rows_cap, grid, st);
+    }
+    if (bn == 64) return gemm_launch_t<WDT_F32, 64>(a, x, rows_cap, grid, st);
+    if (bn == 128) return gemm_launch_t<WDT_F32, 128>(a, x, rows_cap, grid, st);
+    return gemm_launch_t<WDT_F32, 256>(a, x, rows_cap, grid, st);
 }
 
 // ------------------------------------------------------------------ device
@@ -563,10 +644,58 @@ extern "C" int qtts_heads_bytes(qtts_heads *h, int64_t *bytes) {
     return QTTS_OK;
 }
 
+extern "C" int qtts_heads_linear(qtts_heads *h, int index, const float *x, int rows, float *y) {
+    if (!h || !x || !y) return set_err(QTTS_E_ARG, "qtts_heads_linear: NULL argument");
+    if (index < 0 || index >= static_cast<int>(h->mats.size()))
+        return set_err(QTTS_E_ARG, "qtts_heads_linear: no head %d in %s", index, h->name.c_str());
+    if (rows <= 0) return QTTS_OK;
+    CK(cudaSetDevice(h->dev->ordinal));
+    const HeadMat &m = h->mats[index];
+    const int k = h->hidden;
+    cudaStream_t st = h->dev->load;
+    if (static_cast<size_t>(rows) > h->lrows) {
+        if (h->lx) CK(cudaFree(h->lx));
+        if (h->lh) CK(cudaFree(h->lh));
+        h->lx = nullptr;
+        h->lh = nullptr;
+        h->lrows = 0;
+        CK(cudaMalloc(&h->lx, static_cast<size_t>(rows) * k * 4));
+        CK(cudaMalloc(&h->lh, static_cast<size_t>(rows) * k * 2));
+        h->lrows = rows;
+    }
+    const size_t ny = static_cast<size_t>(rows) * m.rows;
+    if (ny > h->lycap) {
+        if (h->ly) CK(cudaFree(h->ly));
+        h->ly = nullptr;
+        h->lycap = 0;
+        CK(cudaMalloc(&h->ly, ny * 4));
+        h->lycap = ny;
+    }
+    if (!h->lerr) CK(cudaMalloc(&h->lerr, 16));
+    CK(cudaMemsetAsync(h->lerr, 0, 16, st));
+    const long long n = static_cast<long long>(rows) * k;
+    CK(cudaMemcpyAsync(h->lx, x, n * 4, cudaMemcpyHostToDevice, st));
+    to_half_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(h->lx, h->lh, n);
+    CK(cudaGetLastError());
+    const int wdt = h->dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    int rc = gemm(m.d, wdt, m.rows, k, h->lh, rows, static_cast<int>(h->lrows), h->ly, m.rows, false, h->lerr, st);
+    if (rc) return rc;
+    int err = 0;
+    CK(cudaMemcpyAsync(&err, h->lerr, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(y, h->ly, ny * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (err) return set_err(QTTS_E_TIMEOUT, "qtts_heads_linear: a device wait gave up");
+    return QTTS_OK;
+}
+
 extern "C" int qtts_heads_destroy(qtts_heads *h) {
     if (!h) return QTTS_OK;
     cudaSetDevice(h->dev->ordinal);
     for (HeadMat &m : h->mats) cudaFree(m.d);
+    if (h->lx) cudaFree(h->lx);
+    if (h->ly) cudaFree(h->ly);
+    if (h->lh) cudaFree(h->lh);
+    if (h->lerr) cudaFree(h->lerr);
     delete h;
     return QTTS_OK;
 }

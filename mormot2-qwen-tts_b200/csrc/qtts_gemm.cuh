@@ -1,0 +1,268 @@
+// qtts_gemm.cuh -- weight-stationary tcgen05 GEMM of libqtts (sm_100a).
+//
+// Y[t][n] (+)= sum_k X[t][k] * W[n][k] for the batched paths (many
+// utterances per decode step, or a long prefill): the projections become a
+// dense contraction, so they run on the 5th-generation tensor cores.
+//
+//  - CTA tile: 128 weight rows (MMA M) x BN tokens (MMA N = 64, 128 or 256),
+//    K in blocks of 64 (one 128-byte swizzle row of fp16), an optional K
+//    split over blockIdx.z whose partial sums are added with f32 atomics
+//    (which also gives the residual add for free).
+//  - A operand (weights): warps 0-3, one weight row per thread, read the
+//    row-packed Q8_0 (or f32) block from global memory, dequantise it to
+//    fp16 (w = q * d, rounded once) and store it in the UMMA K-major
+//    128B-swizzle layout; fence.proxy.async, then an mbarrier arrival.
+//  - B operand (activations, fp16 [T][K]): one TMA tiled load per stage
+//    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast).
+//  - MMA: one thread issues tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 ->
+//    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage) and tcgen05.commit frees the
+//    stage; the accumulator (BN TMEM columns) is read back by warps 4-7 with
+//    tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31 = its weight rows).
+//  - every mbarrier wait is bounded; a timeout sets the error word.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "qtts_decode.cuh"
+
+namespace qtts {
+
+constexpr int G_BM = 128;           // weight rows per CTA tile
+constexpr int G_BK = 64;            // K per stage (128 bytes of fp16)
+constexpr int G_STAGES = 4;
+constexpr int G_THREADS = 256;
+constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
+
+struct GemmArgs {
+    const uint8_t *w;  // [n_rows] rows, row-packed Q8_0 or f32 (row_bytes(wdt, K))
+    int n_rows, K;
+    int T;             // tokens
+    float *out;        // out[t * ld + n]
+    int ld;
+    int atomic;        // add into out (split-K and/or residual) instead of storing
+    int ksplit;        // K blocks per split = (K / G_BK) / ksplit
+    int *err;          // error word (QTTS_E_TIMEOUT on a wait that gave up)
+};
+
+template <int BN>
+struct __align__(1024) GemmSmem {
+    uint8_t a[G_STAGES][G_A_BYTES];   // 1024-aligned: swizzle atoms
+    uint8_t b[G_STAGES][BN * 128];
+    uint64_t full_a[G_STAGES];        // 128 producer arrivals
+    uint64_t full_b[G_STAGES];        // TMA tx bytes
+    uint64_t empty[G_STAGES];         // tcgen05.commit
+    uint64_t accum;                   // last MMA done
+    uint32_t tmem_base;
+};
+
+// ------------------------------------------------------------------ tcgen05 helpers
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void *smem) {
+    // K-major, 128B swizzle: LBO 16 B (encoded 1), SBO 1024 B (8 rows x 128 B),
+    // version 1 (sm100), layout type 2 (SWIZZLE_128B), base offset 0
+    const uint64_t addr = (smem_u32(smem) >> 4) & 0x3FFFull;
+    return addr | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+    // c f32 (bit 4), a/b f16 (0), K-major both, N>>3 at bit 17, M>>4 at bit 24
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void gemm_fail(int *err) {
+    if (err) atomicCAS(err, 0, ERR_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ kernel
+
+template <int WDT, int BN>
+__global__ void __launch_bounds__(G_THREADS, 1)
+    gemm_kernel(const GemmArgs args, const __grid_constant__ CUtensorMap xmap) {
+    extern __shared__ __align__(1024) uint8_t gsmem_raw[];
+    // the dynamic window is aligned up to 1024 bytes (the swizzle atom)
+    GemmSmem<BN> *sm = reinterpret_cast<GemmSmem<BN> *>(
+        (reinterpret_cast<uintptr_t>(gsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row0 = blockIdx.x * G_BM, tok0 = blockIdx.y * BN;
+    const int kb_total = args.K / G_BK, kb_n = kb_total / args.ksplit, kb0 = blockIdx.z * kb_n;
+    if (tid == 0) {
+        for (int s = 0; s < G_STAGES; ++s) {
+            mbar_init(&sm->full_a[s], 128);
+            mbar_init(&sm->full_b[s], 1);
+            mbar_init(&sm->empty[s], 1);
+        }
+        mbar_init(&sm->accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {  // TMEM: BN f32 columns for the 128 x BN accumulator
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
+                     "n"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = sm->tmem_base;
+    bool ok = true;
+
+    if (warp < 4) {
+        // ---- A producers: thread = weight row
+        const int r = tid;
+        const int n = row0 + r;
+        const int rb = row_bytes(WDT, args.K);
+        const uint8_t *row = args.w + static_cast<size_t>(n < args.n_rows ? n : 0) * rb;
+        for (int i = 0; i < kb_n; ++i) {
+            const int s = i % G_STAGES;
+            if (i >= G_STAGES && !mbar_wait(&sm->empty[s], ((i / G_STAGES) - 1) & 1, nullptr)) {
+                ok = false;
+                gemm_fail(args.err);
+                break;
+            }
+            const int k0 = (kb0 + i) * G_BK;
+            uint8_t *dst = sm->a[s] + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 k
+                __half2 h[4];
+                if (n < args.n_rows) {
+                    if (WDT == WDT_Q8) {
+                        const uint2 q = *reinterpret_cast<const uint2 *>(row + k0 + 8 * c);
+                        const float d = __half2float(reinterpret_cast<const __half *>(row + args.K)[(k0 + 8 * c) >> 5]);
+                        const float4 lo = dq4(q.x), hi = dq4(q.y);
+                        h[0] = __floats2half2_rn(lo.x * d, lo.y * d);
+                        h[1] = __floats2half2_rn(lo.z * d, lo.w * d);
+                        h[2] = __floats2half2_rn(hi.x * d, hi.y * d);
+                        h[3] = __floats2half2_rn(hi.z * d, hi.w * d);
+                    } else {
+                        const float4 lo = *reinterpret_cast<const float4 *>(row + 4 * (k0 + 8 * c));
+                        const float4 hi = *reinterpret_cast<const float4 *>(row + 4 * (k0 + 8 * c + 4));
+                        h[0] = __floats2half2_rn(lo.x, lo.y);
+                        h[1] = __floats2half2_rn(lo.z, lo.w);
+                        h[2] = __floats2half2_rn(hi.x, hi.y);
+                        h[3] = __floats2half2_rn(hi.z, hi.w);
+                    }
+                } else {
+                    h[0] = h[1] = h[2] = h[3] = __floats2half2_rn(0.f, 0.f);
+                }
+                *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(h);
+            }
+            // the tensor core reads shared memory through the async proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&sm->full_a[s]);
+        }
+    } else if (warp == 4) {
+        // ---- B producer (TMA)
+        if (lane == 0) {
+            for (int i = 0; i < kb_n; ++i) {
+                const int s = i % G_STAGES;
+                if (i >= G_STAGES && !mbar_wait(&sm->empty[s], ((i / G_STAGES) - 1) & 1, nullptr)) {
+                    ok = false;
+                    gemm_fail(args.err);
+                    break;
+                }
+                mbar_arrive_tx(&sm->full_b[s], BN * 128);
+                tma_load_2d(sm->b[s], &xmap, (kb0 + i) * G_BK, tok0, &sm->full_b[s]);
+            }
+        }
+    } else if (warp == 5) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(G_BM, BN);
+            for (int i = 0; i < kb_n; ++i) {
+                const int s = i % G_STAGES;
+                const uint32_t par = (i / G_STAGES) & 1;
+                if (!mbar_wait(&sm->full_a[s], par, nullptr) || !mbar_wait(&sm->full_b[s], par, nullptr)) {
+                    ok = false;
+                    gemm_fail(args.err);
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t da = umma_desc_sw128(sm->a[s]), db = umma_desc_sw128(sm->b[s]);
+#pragma unroll
+                for (int k = 0; k < G_BK / 16; ++k)  // +32 bytes (2 in 16-byte units) per K=16
+                    umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+                umma_commit(&sm->empty[s]);
+            }
+            umma_commit(&sm->accum);
+        }
+    }
+    // ---- epilogue: warps 4-7, TMEM lane quarter = warp % 4
+    if (warp >= 4) {
+        const bool good = mbar_wait(&sm->accum, 0, nullptr);
+        if (!good) gemm_fail(args.err);
+        __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of warps 4/5 had other work
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int q = warp & 3;
+        const int n = row0 + 32 * q + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
+            if (good && n < args.n_rows) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = tok0 + c + j;
+                    if (t < args.T) {
+                        float *o = args.out + static_cast<size_t>(t) * args.ld + n;
+                        if (args.atomic)
+                            atomicAdd(o, v[j]);
+                        else
+                            *o = v[j];
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 5) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(BN) : "memory");
+    }
+    (void)ok;
+}
+
+// f32 rows -> fp16 rows (the activations of the tensor-core path)
+__global__ void to_half_kernel(const float *x, __half *y, long long n) {
+    long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 3 < n) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + i);
+        *reinterpret_cast<__half2 *>(y + i) = __floats2half2_rn(v.x, v.y);
+        *reinterpret_cast<__half2 *>(y + i + 2) = __floats2half2_rn(v.z, v.w);
+    } else {
+        for (; i < n; ++i) y[i] = __float2half_rn(x[i]);
+    }
+}
+
+}  // namespace qtts

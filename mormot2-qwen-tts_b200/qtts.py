@@ -77,6 +77,7 @@ EXPORTS = {
     "qtts_heads_count": [P, PI],
     "qtts_heads_rows": [P, I, PI],
     "qtts_heads_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
+    "qtts_heads_linear": [P, I, P, I, P],
     "qtts_heads_destroy": [P],
     "qtts_lm_create": [P, P, I, ctypes.POINTER(P)],
     "qtts_lm_reset": [P],
@@ -233,6 +234,13 @@ class QwenLmHeads:
         v = ctypes.c_uint32()
         check(lib().qtts_heads_digest(self.handle, ctypes.byref(v)))
         return v.value
+
+    def linear(self, index, x):
+        """TInferBackend.Linear with head `index`: x [rows][hidden] -> [rows][head rows]."""
+        x = _f32(x).reshape(-1, self.hidden)
+        y = np.empty((x.shape[0], self.rows(index)), np.float32)
+        check(lib().qtts_heads_linear(self.handle, index, _ptr(x), x.shape[0], _ptr(y)))
+        return y
 
     @property
     def count(self):
