@@ -172,6 +172,32 @@ int qtts_lm_length(qtts_lm *lm, int *length);
 /* TQwenLm.Destroy (lm.pas:362-372): frees the cache, then the stack. */
 int qtts_lm_destroy(qtts_lm *lm);
 
+/* ------------------------------------------------------------------ batch */
+
+typedef struct qtts_batch qtts_batch;
+
+/* Many sequences (utterances) through one stack per call: the TQwenLm.Forward
+ * protocol (lm.pas:391-408) for a batch, as the batched decode and the
+ * batched prefill of the TTS engine need it; no counterpart object in the
+ * reference, which runs one TQwenLm per stack.  The stack and the heads are
+ * not owned (destroy the batch first).  Up to max_seqs sequences (ids
+ * 0..max_seqs-1) of up to max_pos positions, up to max_tokens rows per call;
+ * the KV cache is paged (16 positions per page), kv_dtype F32 or BF16.  The
+ * projections run on the tcgen05 GEMM (fp16 operands, f32 accumulation). */
+int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_seqs, int max_tokens, int max_pos, int kv_dtype,
+                      qtts_batch **out);
+/* TQwenLm.Reset of one sequence: its pages return to the pool. */
+int qtts_batch_reset(qtts_batch *batch, int seq);
+/* TQwenLm.Length of one sequence. */
+int qtts_batch_length(qtts_batch *batch, int seq, int *length);
+/* One call: sequence seqs[i] (distinct) receives rows[i] rows, the rows of
+ * all sequences concatenated in x [sum rows][hidden]; for each sequence the
+ * normed state of its last row goes to hidden [nseq][hidden] and the logits
+ * of head `head` to logits [nseq][head rows] (either may be NULL). */
+int qtts_batch_forward(qtts_batch *batch, int nseq, const int32_t *seqs, const int32_t *rows, const float *x, int head,
+                       float *logits, float *hidden);
+int qtts_batch_destroy(qtts_batch *batch);
+
 /* ------------------------------------------------------------------ talker */
 
 /* The choice of codes and the frame layout of TQwenTalker (talker.pas:

@@ -24,6 +24,7 @@
 #include "../../include/qtts.h"
 #include "qtts_decode.cuh"
 #include "qtts_gemm.cuh"
+#include "qtts_batch.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -71,6 +72,7 @@ struct qtts_stack {
     qtts_device *dev;
     qtts_stack_config cfg;
     std::vector<void *> allocs;
+    std::vector<DLayer> hlayers;  // the same table, host side (batched path)
     DLayer *d_layers;
     float *d_final_norm;
     int64_t bytes;
@@ -371,8 +373,12 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.atomic = (add || split > 1) ? 1 : 0;
     a.ksplit = split;
     a.err = err;
-    if (!add && split > 1)
-        for (int t = 0; t < T; ++t) CK(cudaMemsetAsync(y + static_cast<size_t>(t) * ld, 0, n_rows * 4, st));
+    if (!add && split > 1) {
+        if (ld == n_rows)
+            CK(cudaMemsetAsync(y, 0, static_cast<size_t>(T) * ld * 4, st));
+        else
+            for (int t = 0; t < T; ++t) CK(cudaMemsetAsync(y + static_cast<size_t>(t) * ld, 0, n_rows * 4, st));
+    }
     dim3 grid((n_rows + G_BM - 1) / G_BM, (T + bn - 1) / bn, split);
     if (wdt == WDT_Q8) {
         if (bn == 64) return gemm_launch_t<WDT_Q8, 64>(a, x, rows_cap, grid, st);
@@ -522,6 +528,7 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
         else if (cudaMemcpy(dl, hl.data(), sizeof(DLayer) * c->layers, cudaMemcpyHostToDevice) != cudaSuccess)
             rc = set_err(QTTS_E_CUDA, "qtts_stack_create: layer table upload failed");
         s->d_layers = reinterpret_cast<DLayer *>(dl);
+        s->hlayers = hl;
     }
     if (rc != QTTS_OK) {
         stack_free(s);
@@ -1341,5 +1348,286 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
         }
         m->len += n;
     }
+    return QTTS_OK;
+}
+
+
+// ------------------------------------------------------------------ batched forward
+//
+// qtts_batch: one stack (not owned) run for many sequences at once -- the
+// TQwenLm.Forward protocol (lm.pas:391-408) for a batch of utterances, with a
+// paged KV cache and the projections on the tcgen05 GEMM.
+
+struct qtts_batch {
+    qtts_device *dev;
+    qtts_stack *stack;
+    qtts_heads *heads;
+    int max_seqs, max_tokens, max_pos, kv_dtype, mpps, npages, head_rows;
+    void *pool;
+    int *d_pages;
+    std::vector<int> h_pages;  // [max_seqs][mpps], -1 = none
+    std::vector<int> free_pages;
+    std::vector<int> len;
+    float *rope_cos, *rope_sin;
+    cudaStream_t stream;
+    // per-call buffers
+    float *x, *qkv, *q32, *gu, *part, *hidden, *logits;
+    __half *h16, *attn16, *act16, *hlast16;
+    int *meta;  // token metadata and attention items
+    size_t meta_bytes;
+    int *err;
+    std::vector<void *> allocs;
+};
+
+static void batch_free(qtts_batch *b) {
+    for (void *p : b->allocs) cudaFree(p);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    delete b;
+}
+
+extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_seqs, int max_tokens, int max_pos,
+                                 int kv_dtype, qtts_batch **out) {
+    if (!stack || !heads || !out) return set_err(QTTS_E_ARG, "qtts_batch_create: NULL argument");
+    *out = nullptr;
+    if (max_seqs <= 0 || max_tokens <= 0 || max_pos <= 0 || max_tokens < max_seqs)
+        return set_err(QTTS_E_ARG, "qtts_batch_create: bad sizes (%d seqs, %d tokens, %d positions)", max_seqs,
+                       max_tokens, max_pos);
+    if (kv_dtype != QTTS_DTYPE_F32 && kv_dtype != QTTS_DTYPE_BF16)
+        return set_err(QTTS_E_ARG, "qtts_batch_create: KV cache in F32 or BF16");
+    if (heads->hidden != stack->cfg.hidden || heads->dtype != stack->cfg.dtype)
+        return set_err(QTTS_E_ARG, "qtts_batch_create: heads and stack do not match");
+    qtts_device *dev = stack->dev;
+    CK(cudaSetDevice(dev->ordinal));
+    qtts_batch *b = new qtts_batch();
+    b->dev = dev;
+    b->stack = stack;
+    b->heads = heads;
+    b->max_seqs = max_seqs;
+    b->max_tokens = max_tokens;
+    b->max_pos = max_pos;
+    b->kv_dtype = kv_dtype;
+    b->mpps = (max_pos + PAGE - 1) / PAGE;
+    b->npages = max_seqs * b->mpps;
+    b->head_rows = 0;
+    for (const HeadMat &m : heads->mats) b->head_rows = m.rows > b->head_rows ? m.rows : b->head_rows;
+    b->h_pages.assign(static_cast<size_t>(max_seqs) * b->mpps, -1);
+    for (int p = b->npages - 1; p >= 0; --p) b->free_pages.push_back(p);
+    b->len.assign(max_seqs, 0);
+    const int L = stack->cfg.layers;
+    const size_t kvb = kv_dtype == QTTS_DTYPE_F32 ? 4 : 2;
+    const size_t T = max_tokens;
+    const int max_items = max_tokens * HKV + max_seqs * HKV * 64;
+    b->meta_bytes = (T * 2 + static_cast<size_t>(max_items) * (sizeof(AttnItem) / 4) + max_seqs * (HKV * 2 + 2)) * 4;
+    struct A {
+        void **p;
+        size_t bytes;
+    } want[] = {
+        {&b->pool, static_cast<size_t>(b->npages) * L * 2 * HKV * PAGE * HD * kvb},
+        {reinterpret_cast<void **>(&b->d_pages), b->h_pages.size() * 4},
+        {reinterpret_cast<void **>(&b->rope_cos), static_cast<size_t>(max_pos) * (HD / 2) * 4},
+        {reinterpret_cast<void **>(&b->rope_sin), static_cast<size_t>(max_pos) * (HD / 2) * 4},
+        {reinterpret_cast<void **>(&b->x), T * H * 4},
+        {reinterpret_cast<void **>(&b->qkv), T * QKV_ROWS * 4},
+        {reinterpret_cast<void **>(&b->q32), T * QDIM * 4},
+        {reinterpret_cast<void **>(&b->gu), T * GU_ROWS * 4},
+        {reinterpret_cast<void **>(&b->part), static_cast<size_t>(max_seqs) * HKV * 64 * AQB * 2 * PSTRIDE * 4},
+        {reinterpret_cast<void **>(&b->hidden), static_cast<size_t>(max_seqs) * H * 4},
+        {reinterpret_cast<void **>(&b->logits), static_cast<size_t>(max_seqs) * (b->head_rows > 0 ? b->head_rows : 1) * 4},
+        {reinterpret_cast<void **>(&b->h16), T * H * 2},
+        {reinterpret_cast<void **>(&b->attn16), T * QDIM * 2},
+        {reinterpret_cast<void **>(&b->act16), T * INTER * 2},
+        {reinterpret_cast<void **>(&b->hlast16), static_cast<size_t>(max_seqs) * H * 2},
+        {reinterpret_cast<void **>(&b->meta), b->meta_bytes},
+        {reinterpret_cast<void **>(&b->err), 16},
+    };
+    for (const A &a : want) {
+        if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
+            batch_free(b);
+            return set_err(QTTS_E_OOM, "qtts_batch_create: out of device memory (%zu bytes)", a.bytes);
+        }
+        b->allocs.push_back(*a.p);
+    }
+    std::vector<float> cs, sn;
+    rope_tables(max_pos, stack->cfg.rope_theta, cs, sn);
+    if (cudaMemcpy(b->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(b->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(b->err, 0, 16) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        batch_free(b);
+        return set_err(QTTS_E_CUDA, "qtts_batch_create: set-up failed");
+    }
+    *out = b;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_batch_reset(qtts_batch *b, int seq) {
+    if (!b || seq < 0 || seq >= b->max_seqs) return set_err(QTTS_E_ARG, "qtts_batch_reset: bad sequence %d", seq);
+    for (int i = 0; i < b->mpps; ++i) {
+        int &pg = b->h_pages[static_cast<size_t>(seq) * b->mpps + i];
+        if (pg >= 0) b->free_pages.push_back(pg);
+        pg = -1;
+    }
+    b->len[seq] = 0;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_batch_length(qtts_batch *b, int seq, int *length) {
+    if (!b || !length || seq < 0 || seq >= b->max_seqs) return set_err(QTTS_E_ARG, "qtts_batch_length: bad argument");
+    *length = b->len[seq];
+    return QTTS_OK;
+}
+
+template <class KVT>
+static void batch_layers(qtts_batch *b, int T, int nitems, const int *tok_seq, const int *tok_pos,
+                         const AttnItem *items, int ncomb, const int *cfirst, const int *ccount, const int *ctok,
+                         int wdt, cudaStream_t st, int &rc) {
+    const qtts_stack *s = b->stack;
+    KVPool<KVT> pool;
+    pool.base = static_cast<KVT *>(b->pool);
+    pool.pages = b->d_pages;
+    pool.mpps = b->mpps;
+    pool.layers = s->cfg.layers;
+    const float eps = s->cfg.rms_eps;
+    const int cap = b->max_tokens;
+    for (int l = 0; l < s->cfg.layers && rc == QTTS_OK; ++l) {
+        const DLayer &Ly = s->hlayers[l];
+        rmsnorm_f16_kernel<<<(T + 7) / 8, 256, 0, st>>>(b->x, nullptr, T, Ly.in_norm, eps, b->h16, nullptr);
+        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st))) return;
+        qkv_post_kernel<KVT><<<dim3(T, 4), 256, 0, st>>>(b->qkv, tok_seq, tok_pos, Ly.q_norm, Ly.k_norm, eps,
+                                                         b->rope_cos, b->rope_sin, b->q32, pool, l);
+        attn_kernel<KVT><<<nitems, ATHREADS, 0, st>>>(items, b->q32, pool, l, b->attn16, b->part);
+        if (ncomb > 0)
+            attn_combine_kernel<<<(ncomb * HQ + 7) / 8, 256, 0, st>>>(cfirst, ccount, ctok, ncomb, b->part, b->attn16);
+        if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
+        rmsnorm_f16_kernel<<<(T + 7) / 8, 256, 0, st>>>(b->x, nullptr, T, Ly.post_norm, eps, b->h16, nullptr);
+        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, b->gu, GU_ROWS, false, b->err, st))) return;
+        const long long np = static_cast<long long>(T) * INTER;
+        swiglu_f16_kernel<<<static_cast<unsigned>((np + 255) / 256), 256, 0, st>>>(b->gu, np, b->act16);
+        if ((rc = gemm(Ly.wd, wdt, H, INTER, b->act16, T, cap, b->x, H, true, b->err, st))) return;
+        if (cudaGetLastError() != cudaSuccess) rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: kernel launch failed");
+    }
+}
+
+extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x,
+                                  int head, float *logits, float *hidden) {
+    if (!b || nseq <= 0 || !seqs || !rows || !x) return set_err(QTTS_E_ARG, "qtts_batch_forward: bad argument");
+    if (nseq > b->max_seqs) return set_err(QTTS_E_ARG, "qtts_batch_forward: %d sequences, at most %d", nseq, b->max_seqs);
+    if (logits && (head < 0 || head >= static_cast<int>(b->heads->mats.size())))
+        return set_err(QTTS_E_ARG, "qtts_batch_forward: no head %d", head);
+    // validate, count tokens, allocate pages
+    int T = 0;
+    std::vector<char> seen(b->max_seqs, 0);
+    for (int i = 0; i < nseq; ++i) {
+        const int sq = seqs[i], n = rows[i];
+        if (sq < 0 || sq >= b->max_seqs || seen[sq] || n <= 0)
+            return set_err(QTTS_E_ARG, "qtts_batch_forward: entry %d (sequence %d, %d rows)", i, sq, n);
+        seen[sq] = 1;
+        if (b->len[sq] + n > b->max_pos)
+            return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: sequence %d: %d + %d positions, at most %d", sq,
+                           b->len[sq], n, b->max_pos);
+        T += n;
+    }
+    if (T > b->max_tokens) return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: %d rows, at most %d", T, b->max_tokens);
+    for (int i = 0; i < nseq; ++i) {
+        const int sq = seqs[i];
+        const int need = (b->len[sq] + rows[i] + PAGE - 1) / PAGE;
+        for (int pg = 0; pg < need; ++pg) {
+            int &slot = b->h_pages[static_cast<size_t>(sq) * b->mpps + pg];
+            if (slot < 0) {
+                if (b->free_pages.empty()) return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: out of KV pages");
+                slot = b->free_pages.back();
+                b->free_pages.pop_back();
+            }
+        }
+    }
+    // metadata: tokens, attention items, combine lists
+    std::vector<int> tok_seq(T), tok_pos(T), last(nseq);
+    std::vector<AttnItem> items;
+    std::vector<int> cfirst, ccount, ctok;
+    int t = 0, nparts = 0;
+    for (int i = 0; i < nseq; ++i) {
+        const int sq = seqs[i], n = rows[i], L0 = b->len[sq];
+        for (int r = 0; r < n; ++r) {
+            tok_seq[t + r] = sq;
+            tok_pos[t + r] = L0 + r;
+        }
+        last[i] = t + n - 1;
+        if (n == 1) {
+            // one query: the context in splits of 64 keys, combined afterwards
+            const int ctx = L0 + 1;
+            const int S = (ctx + 63) / 64 < 64 ? (ctx + 63) / 64 : 64;
+            const int C = (ctx + S - 1) / S;
+            for (int h = 0; h < HKV; ++h) {
+                cfirst.push_back(nparts);
+                ccount.push_back(S);
+                for (int sp = 0; sp < S; ++sp)
+                    items.push_back({t, L0, 0, 1, h, sp * C, (sp + 1) * C < ctx ? (sp + 1) * C : ctx, sq, nparts++});
+            }
+            ctok.push_back(t);
+        } else {
+            for (int qa = 0; qa < n; qa += AQB)
+                for (int h = 0; h < HKV; ++h)
+                    items.push_back({t, L0, qa, qa + AQB < n ? qa + AQB : n, h, 0, L0 + n, sq, -1});
+        }
+        t += n;
+    }
+    const int ncomb = static_cast<int>(ctok.size());
+    // one upload: tok_seq | tok_pos | items | cfirst | ccount | ctok | last
+    std::vector<int> meta;
+    meta.insert(meta.end(), tok_seq.begin(), tok_seq.end());
+    meta.insert(meta.end(), tok_pos.begin(), tok_pos.end());
+    const size_t o_items = meta.size();
+    const int* ip = reinterpret_cast<const int *>(items.data());
+    meta.insert(meta.end(), ip, ip + items.size() * (sizeof(AttnItem) / 4));
+    const size_t o_cf = meta.size();
+    meta.insert(meta.end(), cfirst.begin(), cfirst.end());
+    const size_t o_cc = meta.size();
+    meta.insert(meta.end(), ccount.begin(), ccount.end());
+    const size_t o_ct = meta.size();
+    meta.insert(meta.end(), ctok.begin(), ctok.end());
+    const size_t o_last = meta.size();
+    meta.insert(meta.end(), last.begin(), last.end());
+    if (meta.size() * 4 > b->meta_bytes) return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: too many attention items");
+    CK(cudaSetDevice(b->dev->ordinal));
+    cudaStream_t st = b->stream;
+    CK(cudaMemcpyAsync(b->meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->d_pages, b->h_pages.data(), b->h_pages.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->x, x, static_cast<size_t>(T) * H * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(b->err, 0, 16, st));
+    const int wdt = b->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    int rc = QTTS_OK;
+    const int *m = b->meta;
+    const AttnItem *d_items = reinterpret_cast<const AttnItem *>(m + o_items);
+    if (b->kv_dtype == QTTS_DTYPE_F32)
+        batch_layers<float>(b, T, static_cast<int>(items.size()), m, m + T, d_items, ncomb, m + o_cf, m + o_cc, m + o_ct,
+                            wdt, st, rc);
+    else
+        batch_layers<__nv_bfloat16>(b, T, static_cast<int>(items.size()), m, m + T, d_items, ncomb, m + o_cf, m + o_cc,
+                                    m + o_ct, wdt, st, rc);
+    if (rc) return rc;
+    // the last row of every sequence: final norm, head
+    rmsnorm_f16_kernel<<<(nseq + 7) / 8, 256, 0, st>>>(b->x, m + o_last, nseq, b->stack->d_final_norm,
+                                                       b->stack->cfg.rms_eps, b->hlast16, b->hidden);
+    CK(cudaGetLastError());
+    int hr = 0;
+    if (logits) {
+        const HeadMat &hm = b->heads->mats[head];
+        hr = hm.rows;
+        if ((rc = gemm(hm.d, wdt, hr, H, b->hlast16, nseq, b->max_seqs, b->logits, hr, false, b->err, st))) return rc;
+    }
+    int err = 0;
+    CK(cudaMemcpyAsync(&err, b->err, 4, cudaMemcpyDeviceToHost, st));
+    if (logits) CK(cudaMemcpyAsync(logits, b->logits, static_cast<size_t>(nseq) * hr * 4, cudaMemcpyDeviceToHost, st));
+    if (hidden) CK(cudaMemcpyAsync(hidden, b->hidden, static_cast<size_t>(nseq) * H * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (err) return set_err(QTTS_E_TIMEOUT, "qtts_batch_forward: a device wait gave up");
+    for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
+    return QTTS_OK;
+}
+
+extern "C" int qtts_batch_destroy(qtts_batch *b) {
+    if (!b) return QTTS_OK;
+    cudaSetDevice(b->dev->ordinal);
+    batch_free(b);
     return QTTS_OK;
 }

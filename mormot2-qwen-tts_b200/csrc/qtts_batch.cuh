@@ -1,0 +1,287 @@
+// qtts_batch.cuh -- the batched forward of libqtts (sm_100a): many sequences
+// (utterances) through one stack per call, the projections on the tcgen05
+// GEMM (qtts_gemm.cuh), the rest here: RMSNorm to fp16, q/k-norm + RoPE +
+// append into a paged KV cache, causal GQA attention over the pages, SwiGLU.
+//
+// Paged KV cache: pages of 16 positions; a page holds, for every layer, K and
+// V of the 8 KV heads: [page][layer][k|v][head][16][128], in float32 or bf16.
+// Each sequence has a page table (page of position p = table[p / 16]).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "qtts_decode.cuh"
+
+namespace qtts {
+
+constexpr int PAGE = 16;   // positions per page
+constexpr int AQB = 16;    // query rows per attention item (prefill)
+constexpr int AKT = 16;    // keys per attention tile
+constexpr int ATHREADS = 256;
+
+template <class KVT>
+struct KVPool {
+    KVT *base;
+    const int *pages;  // [max_seqs][mpps]
+    int mpps;          // max pages per sequence
+    int layers;
+};
+
+template <class KVT>
+__device__ __forceinline__ KVT *kv_at(const KVPool<KVT> &p, int layer, int seq, int pos, int which, int head) {
+    const int page = p.pages[seq * p.mpps + pos / PAGE];
+    return p.base + ((((static_cast<size_t>(page) * p.layers + layer) * 2 + which) * HKV + head) * PAGE + pos % PAGE) * HD;
+}
+__device__ __forceinline__ void store4(float *d, float4 v) { *reinterpret_cast<float4 *>(d) = v; }
+__device__ __forceinline__ void store4(__nv_bfloat16 *d, float4 v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(d) = u;
+}
+__device__ __forceinline__ float4 load4(const float *s) { return *reinterpret_cast<const float4 *>(s); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16 *s) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(s);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// One warp per row: out16[o] = fp16(rmsnorm(x[idx[o]]) * w); optionally the
+// float32 normed row too (the normed state returned as `hidden`).
+__global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, const float *w, float eps, __half *out16,
+                                   float *out32) {
+    const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (o >= rows) return;
+    const float *r = x + static_cast<size_t>(idx ? idx[o] : o) * H;
+    float4 v[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = load4(r + 4 * (lane + 32 * i));
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(H) + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = 4 * (lane + 32 * i);
+        const float4 g = load4(w + e);
+        const float4 y = make_float4(g.x * (v[i].x * inv), g.y * (v[i].y * inv), g.z * (v[i].z * inv), g.w * (v[i].w * inv));
+        *reinterpret_cast<__half2 *>(out16 + static_cast<size_t>(o) * H + e) = __floats2half2_rn(y.x, y.y);
+        *reinterpret_cast<__half2 *>(out16 + static_cast<size_t>(o) * H + e + 2) = __floats2half2_rn(y.z, y.w);
+        if (out32) store4(out32 + static_cast<size_t>(o) * H + e, y);
+    }
+}
+
+// q/k-norm + RoPE of every token's 16 q and 8 k heads, raw v; q to q32
+// [T][16][128], k and v appended to the pages at the token's position.
+// grid (T, 4), 8 warps: warp v of 32 = q head v (< 16), k head v-16, v head v-24.
+template <class KVT>
+__global__ void qkv_post_kernel(const float *qkv, const int *tok_seq, const int *tok_pos, const float *q_norm,
+                                const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
+                                float *q32, KVPool<KVT> pool, int layer) {
+    const int t = blockIdx.x, v = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int seq = tok_seq[t], pos = tok_pos[t];
+    const int off = v < 16 ? v * HD : (v < 24 ? QDIM + (v - 16) * HD : QDIM + KVDIM + (v - 24) * HD);
+    const float4 x = load4(qkv + static_cast<size_t>(t) * QKV_ROWS + off + 4 * lane);
+    float y[4] = {x.x, x.y, x.z, x.w};
+    if (v < 24) {
+        const float *nw = v < 16 ? q_norm : k_norm;
+        const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
+        const float4 g = load4(nw + 4 * lane);
+        y[0] = g.x * (y[0] * inv);
+        y[1] = g.y * (y[1] * inv);
+        y[2] = g.z * (y[2] * inv);
+        y[3] = g.w * (y[3] * inv);
+        const int half = HD / 2, e0 = (4 * lane) & (half - 1);
+        const float4 cs = load4(rope_cos + static_cast<size_t>(pos) * half + e0);
+        const float4 sn = load4(rope_sin + static_cast<size_t>(pos) * half + e0);
+        const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float partner = __shfl_xor_sync(0xffffffffu, y[j], 16);
+            o[j] = lane < 16 ? y[j] * cv[j] - partner * sv[j] : y[j] * cv[j] + partner * sv[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) y[j] = o[j];
+    }
+    const float4 r = make_float4(y[0], y[1], y[2], y[3]);
+    if (v < 16)
+        store4(q32 + static_cast<size_t>(t) * QDIM + v * HD + 4 * lane, r);
+    else
+        store4(kv_at(pool, layer, seq, pos, v < 24 ? 0 : 1, v < 24 ? v - 16 : v - 24) + 4 * lane, r);
+}
+
+// One attention work item: the new rows [qa, qb) of one sequence (token t0
+// is its first new row, at position L0) against keys [ka, kb) of kv head h.
+struct AttnItem {
+    int t0, L0, qa, qb, h, ka, kb, seq, part;  // part < 0: write the normalised output
+};
+
+// Causal GQA attention of one item; query heads 2h and 2h+1 share kv head h.
+// Warps are spread over the (row, q head) combos and, when there are fewer
+// combos than warps, over the keys of each tile; their online-softmax
+// states are merged in shared memory.
+template <class KVT>
+__global__ void __launch_bounds__(ATHREADS) attn_kernel(const AttnItem *items, const float *q32, KVPool<KVT> pool,
+                                                        int layer, __half *attn16, float *part) {
+    __shared__ __align__(16) float qs[AQB][2][HD];
+    __shared__ __align__(16) float ks[AKT][HD];
+    __shared__ __align__(16) float vs[AKT][HD];
+    __shared__ __align__(16) float ws[8][HD + 4];
+    const AttnItem it = items[blockIdx.x];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int R = it.qb - it.qa, nc = 2 * R;
+    for (int i = tid; i < R * 2 * (HD / 4); i += ATHREADS) {
+        const int j = i / (2 * (HD / 4)), rem = i - j * 2 * (HD / 4), q = rem / (HD / 4), d4 = rem - q * (HD / 4);
+        store4(&qs[j][q][4 * d4],
+               load4(q32 + static_cast<size_t>(it.t0 + it.qa + j) * QDIM + (2 * it.h + q) * HD + 4 * d4));
+    }
+    // warp layout: npw warps per combo (nc <= 8), or combos w, w+8, .. per warp
+    const int npw = nc <= 8 ? 8 / nc : 1;
+    const int ncw = nc <= 8 ? 1 : (nc + 7) / 8;  // combos per warp
+    const int kend = min(it.kb, it.L0 + it.qb);  // keys beyond the last row are masked anyway
+    float m[4], l[4], o[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        m[c] = -INFINITY;
+        l[c] = 0.f;
+        o[c][0] = o[c][1] = o[c][2] = o[c][3] = 0.f;
+    }
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+    for (int kt = it.ka; kt < kend; kt += AKT) {
+        const int nt = min(AKT, kend - kt);
+        __syncthreads();
+        for (int i = tid; i < nt * (HD / 4); i += ATHREADS) {
+            const int p = i / (HD / 4), d4 = i - p * (HD / 4);
+            store4(&ks[p][4 * d4], load4(kv_at(pool, layer, it.seq, kt + p, 0, it.h) + 4 * d4));
+            store4(&vs[p][4 * d4], load4(kv_at(pool, layer, it.seq, kt + p, 1, it.h) + 4 * d4));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (c >= ncw) break;
+            const int combo = nc <= 8 ? warp / npw : warp + 8 * c;
+            const int sub = nc <= 8 ? warp - combo * npw : 0;
+            if (combo >= nc) break;
+            const int j = combo >> 1, q = combo & 1;
+            const int qpos = it.L0 + it.qa + j;
+            const float4 qv = load4(&qs[j][q][4 * lane]);
+            for (int p = sub; p < nt; p += npw) {
+                if (kt + p > qpos) break;  // causal
+                const float4 kv4 = load4(&ks[p][4 * lane]);
+                float d = qv.x * kv4.x;
+                d = fmaf(qv.y, kv4.y, d);
+                d = fmaf(qv.z, kv4.z, d);
+                d = fmaf(qv.w, kv4.w, d);
+                d = warp_sum(d) * scale;
+                const float mn = fmaxf(m[c], d);
+                const float corr = expf(m[c] - mn), e = expf(d - mn);
+                l[c] = l[c] * corr + e;
+                const float4 vv = load4(&vs[p][4 * lane]);
+                o[c][0] = fmaf(e, vv.x, o[c][0] * corr);
+                o[c][1] = fmaf(e, vv.y, o[c][1] * corr);
+                o[c][2] = fmaf(e, vv.z, o[c][2] * corr);
+                o[c][3] = fmaf(e, vv.w, o[c][3] * corr);
+                m[c] = mn;
+            }
+        }
+    }
+    // results: merge the npw warps of a combo (nc <= 8), then write
+    for (int c = 0; c < ncw; ++c) {
+        int combo = nc <= 8 ? warp / npw : warp + 8 * c;
+        float M = m[c], L = l[c];
+        float4 acc = make_float4(o[c][0], o[c][1], o[c][2], o[c][3]);
+        bool writer = combo < nc;
+        if (nc <= 8) {
+            __syncthreads();
+            if (combo < nc) {
+                store4(&ws[warp][4 * lane], acc);
+                if (lane == 0) {
+                    ws[warp][HD] = M;
+                    ws[warp][HD + 1] = L;
+                }
+            }
+            __syncthreads();
+            writer = combo < nc && warp == combo * npw;
+            if (writer) {
+                M = -INFINITY;
+                for (int s = 0; s < npw; ++s) M = fmaxf(M, ws[combo * npw + s][HD]);
+                L = 0.f;
+                acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (M != -INFINITY) {
+                    for (int s = 0; s < npw; ++s) {
+                        const float ms = ws[combo * npw + s][HD];
+                        const float e = ms == -INFINITY ? 0.f : expf(ms - M);
+                        L = fmaf(ws[combo * npw + s][HD + 1], e, L);
+                        const float4 v = load4(&ws[combo * npw + s][4 * lane]);
+                        acc.x = fmaf(v.x, e, acc.x);
+                        acc.y = fmaf(v.y, e, acc.y);
+                        acc.z = fmaf(v.z, e, acc.z);
+                        acc.w = fmaf(v.w, e, acc.w);
+                    }
+                }
+            }
+        }
+        if (!writer) continue;
+        const int j = combo >> 1, q = combo & 1;
+        if (it.part < 0) {
+            const float inv = 1.0f / L;
+            __half *dst = attn16 + static_cast<size_t>(it.t0 + it.qa + j) * QDIM + (2 * it.h + q) * HD + 4 * lane;
+            *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
+            *reinterpret_cast<__half2 *>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
+        } else {
+            float *pp = part + (static_cast<size_t>(it.part) * AQB * 2 + j * 2 + q) * PSTRIDE;
+            store4(pp + 4 * lane, acc);
+            if (lane == 0) {
+                pp[HD] = M;
+                pp[HD + 1] = L;
+            }
+        }
+    }
+}
+
+// The splits of one-row sequences: warp per (call, q head); items
+// first[call*8 + h] .. +count of kv head h hold its partials.
+__global__ void attn_combine_kernel(const int *first, const int *count, const int *tok, int ncalls, const float *part,
+                                    __half *attn16) {
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (w >= ncalls * HQ) return;
+    const int call = w / HQ, qh = w - call * HQ, h = qh >> 1, q = qh & 1;
+    const int f = first[call * HKV + h], n = count[call * HKV + h];
+    if (n <= 0) return;
+    float M = -INFINITY;
+    for (int s = 0; s < n; ++s) M = fmaxf(M, part[(static_cast<size_t>(f + s) * AQB * 2 + q) * PSTRIDE + HD]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < n; ++s) {
+        const float *pp = part + (static_cast<size_t>(f + s) * AQB * 2 + q) * PSTRIDE;
+        const float e = pp[HD] == -INFINITY ? 0.f : expf(pp[HD] - M);
+        L = fmaf(pp[HD + 1], e, L);
+        const float4 v = load4(pp + 4 * lane);
+        acc.x = fmaf(v.x, e, acc.x);
+        acc.y = fmaf(v.y, e, acc.y);
+        acc.z = fmaf(v.z, e, acc.z);
+        acc.w = fmaf(v.w, e, acc.w);
+    }
+    const float inv = 1.0f / L;
+    __half *dst = attn16 + static_cast<size_t>(tok[call]) * QDIM + qh * HD + 4 * lane;
+    *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
+    *reinterpret_cast<__half2 *>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
+}
+
+// act16[t][j] = fp16(silu(gate) * up); gate j and up j are columns 2j, 2j+1
+__global__ void swiglu_f16_kernel(const float *gu, long long n_pairs, __half *act16) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n_pairs) return;
+    const float2 gv = *reinterpret_cast<const float2 *>(gu + 2 * i);
+    const float s = gv.x / (1.0f + expf(-gv.x));
+    act16[i] = __float2half_rn(s * gv.y);
+}
+
+}  // namespace qtts

@@ -85,6 +85,11 @@ EXPORTS = {
     "qtts_lm_forward_noalloc": [P, P, I, I, P, P],
     "qtts_lm_length": [P, PI],
     "qtts_lm_destroy": [P],
+    "qtts_batch_create": [P, P, I, I, I, I, ctypes.POINTER(P)],
+    "qtts_batch_reset": [P, I],
+    "qtts_batch_length": [P, I, PI],
+    "qtts_batch_forward": [P, I, P, P, P, I, P, P],
+    "qtts_batch_destroy": [P],
     "qtts_talker_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
     "qtts_talker_start": [P, P, I, P, I, P, P, P],
     "qtts_talker_next_frame": [P, P, PI],
@@ -303,6 +308,51 @@ class QwenLm:
         if self.handle:
             check(lib().qtts_lm_destroy(self.handle))
             self.handle = None
+
+
+class QwenBatch:
+    """Many sequences through one stack per call (batched decode / prefill),
+    paged KV cache; the stack and heads are not owned."""
+
+    def __init__(self, stack, heads, max_seqs, max_tokens, max_pos, kv_dtype="f32"):
+        h = P()
+        check(lib().qtts_batch_create(stack.handle, heads.handle, max_seqs, max_tokens, max_pos, DTYPES[kv_dtype],
+                                      ctypes.byref(h)))
+        self.handle = h
+        self.heads = heads
+        self.hidden = heads.hidden
+
+    def reset(self, seq):
+        check(lib().qtts_batch_reset(self.handle, seq))
+
+    def length(self, seq):
+        v = ctypes.c_int()
+        check(lib().qtts_batch_length(self.handle, seq, ctypes.byref(v)))
+        return v.value
+
+    def forward(self, seqs, rows, x, head=0, logits=True, hidden=True):
+        """Append rows[i] rows to sequence seqs[i]; returns (logits [n][rows
+        of head] or None, hidden [n][hidden] or None)."""
+        sq = np.ascontiguousarray(seqs, dtype=np.int32)
+        rw = np.ascontiguousarray(rows, dtype=np.int32)
+        x = _f32(x)
+        n = sq.size
+        lg = np.empty((n, self.heads.rows(head)), np.float32) if logits else None
+        hd = np.empty((n, self.hidden), np.float32) if hidden else None
+        check(lib().qtts_batch_forward(self.handle, n, _ptr(sq), _ptr(rw), _ptr(x), head, _ptr(lg), _ptr(hd)))
+        return lg, hd
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_batch_destroy(self.handle))
+            self.handle = None
+
+
+def stack_destroy(stack):
+    """Free a stack that no lm owns (the batch borrows its stack)."""
+    if stack.handle:
+        check(lib().qtts_stack_destroy(stack.handle))
+        stack.handle = None
 
 
 class QwenTalker:
