@@ -306,9 +306,9 @@ def gpu_arm(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         # bounded CPU sample: ~15 s of the oracle on the host cores
-        t1, d1, _ = cpu_frames(m, dtype, prompt, 1)
+        t1, d1, _ = cpu_frames(m, dtype, prompt, 1, os.cpu_count())
         nf = int(min(max(2, 15.0 / max(t1, 1e-3)), K))
-        dt, done, used = cpu_frames(m, dtype, prompt, nf)
+        dt, done, used = cpu_frames(m, dtype, prompt, nf, os.cpu_count())
         cpu = {"value": done / dt, "unit": "frames/s", "cores": used, "kind": "port",
                "sample": f"{done} frames of the same utterance after its prefill (C restatement of the reference "
                          "CPU path, AVX2+FMA, OpenMP over output rows)"}

@@ -403,7 +403,7 @@ extern "C" int qtts_device_open(int ordinal, qtts_device **out) {
     CK(cudaGetDeviceProperties(&prop, ordinal));
     if (prop.major < 10) return set_err(QTTS_E_ARG, "qtts_device_open: %s is sm_%d%d, sm_100a needed", prop.name, prop.major, prop.minor);
     if (!prop.cooperativeLaunch) return set_err(QTTS_E_ARG, "qtts_device_open: no cooperative launch");
-    if (prop.multiProcessorCount * XS_MAX < H || prop.multiProcessorCount < 2 * HKV)
+    if (prop.multiProcessorCount * XS_MAX < H || prop.multiProcessorCount < 128)
         return set_err(QTTS_E_ARG, "qtts_device_open: %d SMs is too few", prop.multiProcessorCount);
     size_t smem = sizeof(Smem) + 128;
     CK(cudaFuncSetAttribute(decode_kernel<WDT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));

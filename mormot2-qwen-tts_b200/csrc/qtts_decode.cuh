@@ -64,7 +64,7 @@ constexpr int PRODUCER_WARP = NWARPS - 1;
 constexpr int STAGE_BYTES = 24576;
 constexpr int NSTAGES = 5;
 constexpr int ACT_FLOATS = RMAX * INTER;  // staged activations [R][K]
-constexpr int MAX_PARTS = 24;             // (row, 1024-segment) partial sums per stage
+constexpr int MAX_PARTS = 48;             // (row, 1024-segment) partial sums of a CTA slice (grid >= 128)
 constexpr int PSTRIDE = 132;              // attention partial: o[128], m, l
 constexpr int ATT_TILE = 32;              // context positions per attention tile
 constexpr int XS_MAX = 16;                // residual rows owned by a CTA (grid >= 64)
@@ -290,14 +290,14 @@ struct __align__(128) Smem {
     float act[ACT_FLOATS];            // GEMV activations; attention scratch
     float kv[2][ATT_TILE][HD];        // attention K / V tile
     float xs[RMAX][XS_MAX];           // this CTA's rows of the residual stream
-    float part[2][MAX_PARTS * RMAX];  // GEMV partial sums, double-buffered by chunk
+    float part[MAX_PARTS * RMAX];     // GEMV partial sums of the slice
     float red[NWARPS * RMAX];
     unsigned long long keys[NWARPS];
     uint64_t full[NSTAGES];
     uint64_t empty[NSTAGES];
     uint64_t kvbar;
     int abort_flag;
-    int consumed;   // chunks released by the compute warps
+    int issued;     // chunks the producer has issued
     int bcast;
     int kv_rows;    // cached rows of the prefetched tile (0: nothing in flight)
     int barflag[3];     // OR reductions of the compute-warp barrier, rotating
@@ -373,13 +373,10 @@ struct Producer {
             mbar_arrive_tx(&sm->full[slot], bytes);
             bulk_g2s(sm->ring[slot], w + static_cast<size_t>(r) * rb, bytes, &sm->full[slot], pol);
             ++seq;
+            sm->issued = seq;
         }
     }
-    // the copies issued but not consumed must land before the CTA exits
-    __device__ void drain() {
-        int c = *reinterpret_cast<volatile int *>(&sm->consumed);
-        for (int n = c; n < seq; ++n) mbar_wait(&sm->full[n % NSTAGES], (n / NSTAGES) & 1, nullptr);
-    }
+
 };
 
 // ------------------------------------------------------------------ compute
@@ -470,11 +467,13 @@ struct Compute {
 
     // ---------------------------------------------------------------- staging
 
-    // act[r][0..H) = rmsnorm(row r) * w, rows as the sum of up to 3 addends
-    // (((a + b) + c), the summation order of TQwenTalker.NextFrame); with
-    // init_resid, this CTA's residual rows [c0, c1) are taken from the sum
+    // act[r][0..H) = x_r * w for the rows x_r = ((a + b) + c) (up to 3
+    // addends: the summation order of TQwenTalker.NextFrame), and the sums
+    // of squares of x_r per warp in red[]: the RMSNorm scale 1/rms(x_r) is
+    // applied by the GEMV epilogue (norm_inv), so staging needs one barrier.
+    // With init_resid, this CTA's residual rows [c0, c1) come from the sum.
     __device__ void stage_norm(const float *const *a, const float *const *b, const float *const *c, int R,
-                               const float *w, float eps, bool init_resid) {
+                               const float *w, bool init_resid) {
         float ss[RMAX] = {0.f, 0.f, 0.f, 0.f};
         for (int idx = tid; idx < R * (H / 4); idx += NCT) {
             const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
@@ -487,7 +486,8 @@ struct Compute {
                 const float4 t = ldcg4(c[r] + i);
                 v.x = v.x + t.x; v.y = v.y + t.y; v.z = v.z + t.z; v.w = v.w + t.w;
             }
-            *reinterpret_cast<float4 *>(sm->act + r * H + i) = v;
+            const float4 g = *reinterpret_cast<const float4 *>(w + i);
+            *reinterpret_cast<float4 *>(sm->act + r * H + i) = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
             float s = v.x * v.x;
             s = fmaf(v.y, v.y, s);
             s = fmaf(v.z, v.z, s);
@@ -510,20 +510,12 @@ struct Compute {
             }
         }
         named_sync();
-        for (int idx = tid; idx < R * (H / 4); idx += NCT) {
-            const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
-            float t = 0.f;
-            for (int w2 = 0; w2 < NCW; ++w2) t += sm->red[w2 * RMAX + r];
-            const float inv = 1.0f / sqrtf(t / static_cast<float>(H) + eps);
-            float4 v = *reinterpret_cast<float4 *>(sm->act + r * H + i);
-            const float4 g = *reinterpret_cast<const float4 *>(w + i);
-            v.x = g.x * (v.x * inv);
-            v.y = g.y * (v.y * inv);
-            v.z = g.z * (v.z * inv);
-            v.w = g.w * (v.w * inv);
-            *reinterpret_cast<float4 *>(sm->act + r * H + i) = v;
-        }
-        named_sync();
+    }
+    // 1/rms of staged row r (after stage_norm's barrier)
+    __device__ __forceinline__ float norm_inv(int r, float eps) const {
+        float t = 0.f;
+        for (int w2 = 0; w2 < NCW; ++w2) t += sm->red[w2 * RMAX + r];
+        return 1.0f / sqrtf(t / static_cast<float>(H) + eps);
     }
 
     __device__ void stage_copy(const float *src, int R, int k) {
@@ -570,39 +562,49 @@ struct Compute {
     enum Epi { E_STORE, E_RESID, E_SWIGLU, E_HEAD, E_HEAD0 };
 
     // GEMV over this CTA's slice of matrix m; activations staged in sm->act
-    // as [R][K].  Work items: (row pair, 1024-wide K segment) per warp, the
-    // activations loaded once for both rows; partial sums per (row, segment).
+    // as [R][K].  Work items are (row pair, 1024-wide K segment), the
+    // activations loaded once for both rows, numbered over the whole slice
+    // chunk by chunk; warp w takes items w, w+15, ...  Each warp waits for
+    // the stages it reads and releases every stage of the phase itself (the
+    // empty barriers count the 15 compute warps), so the phase has a single
+    // CTA barrier, before the epilogue.  eps >= 0: the rows were staged by
+    // stage_norm and y is scaled by their 1/rms.
     //  E_STORE: out[r*ld + row] = y
     //  E_RESID: residual row: xs[r][row-c0] += y, out[r*H + row] = xs
     //  E_SWIGLU: out[r*ld + row/2] = silu(y_gate) * y_up
     //  E_HEAD / E_HEAD0: out[row] = y (R == 1), the CTA's argmax key to
     //  job->s.arg; E_HEAD0 applies ChooseCode0's processors first.
     template <int K>
-    __device__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld) {
+    __device__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld, float eps) {
         constexpr int SEG = K / 1024;
         const int rb = row_bytes(WDT, K);
         const int n = mat_rows(m, head_rows);
         int r0, r1;
         mat_slice(m, n, blockIdx.x, gridDim.x, r0, r1);
+        const int nrows = r1 - r0;
         const int sr = stage_rows(WDT, K, m);
-        unsigned long long best = 0ull;
-        for (int cr = r0; cr < r1; cr += sr) {
-            const int nr = min(sr, r1 - cr);
-            const int slot = seq % NSTAGES;
-            // partials of this chunk; the buffer was last read in the epilogue
-            // of chunk seq-2, which every thread finished before the barrier
-            // of chunk seq-1
-            float *part = sm->part[seq & 1];
-            const uint32_t par = (seq / NSTAGES) & 1;
-            // every thread waits (bounded); a timeout raises abort_flag, read
-            // by all after the named barrier below, so the exit is uniform
-            const bool got = ok && mbar_wait(&sm->full[slot], par, &sm->abort_flag);
-            if (!got) fail(ERR_TIMEOUT, 100 + m);
+        const int nchunks = (nrows + sr - 1) / sr;
+        const int pairs_full = (sr + 1) >> 1;  // pairs of a full chunk
+        int it = warp;                         // next item of this warp
+        bool good = ok;
+        for (int ch = 0; ch < nchunks; ++ch) {
+            const int slot = (seq + ch) % NSTAGES;
+            const uint32_t par = ((seq + ch) / NSTAGES) & 1;
+            const int nr = min(sr, nrows - ch * sr);
+            const int item_end = (ch * pairs_full + ((nr + 1) >> 1)) * SEG;  // items of chunks <= ch
+            // every warp observes every stage (so that no parity is skipped)
+            // before it releases it; warp-uniform verdict for the shuffles
+            if (good) {
+                const bool got = __all_sync(0xffffffffu, mbar_wait(&sm->full[slot], par, &sm->abort_flag));
+                if (!got) {
+                    good = false;
+                    fail(ERR_TIMEOUT, 100 + m);
+                }
+            }
             const uint8_t *base = sm->ring[slot];
-            const int npairs = (nr + 1) >> 1;
-            const int items = got ? npairs * SEG : 0;
-            for (int it = warp; it < items; it += NCW) {
-                const int pair = it / SEG, seg = it - pair * SEG;
+            for (; it < item_end; it += NCW) {
+                if (!good) continue;
+                const int pair = it / SEG - ch * pairs_full, seg = it % SEG;
                 const int ra = 2 * pair;
                 const bool two = ra + 1 < nr;
                 const uint8_t *rowa = base + ra * rb;
@@ -649,57 +651,65 @@ struct Compute {
                         }
                     }
                 }
+                const int row = ch * sr + ra;  // row within the slice
 #pragma unroll
                 for (int r = 0; r < RMAX; ++r) {
                     if (r < R) {
                         const float s = warp_sum2(aa[r], ab[r], lane);
-                        if (lane == 0) part[(ra * SEG + seg) * RMAX + r] = s;
-                        if (lane == 16 && two) part[((ra + 1) * SEG + seg) * RMAX + r] = s;
+                        if (lane == 0) sm->part[(row * SEG + seg) * RMAX + r] = s;
+                        if (lane == 16 && two) sm->part[((row + 1) * SEG + seg) * RMAX + r] = s;
                     }
                 }
             }
-            named_sync();
-            if (*reinterpret_cast<volatile int *>(&sm->abort_flag)) {
-                ok = false;
-                return;
-            }
-            if (tid == 0) {
-                mbar_arrive(&sm->empty[slot]);
-                sm->consumed = seq + 1;
-            }
-            ++seq;
-            if (kind == E_SWIGLU) {
-                const int np = nr / 2;
-                for (int idx = tid; idx < np * R; idx += NCT) {
-                    const int p = idx / R, r = idx - p * R;
-                    float g = 0.f, v = 0.f;
+            // this warp is done with the stage
+            __syncwarp();
+            if (lane == 0 && good) mbar_arrive(&sm->empty[slot]);
+        }
+        seq += nchunks;
+        named_sync();
+        if (*reinterpret_cast<volatile int *>(&sm->abort_flag)) {
+            ok = false;
+            return;
+        }
+        // epilogue over the slice
+        unsigned long long best = 0ull;
+        if (kind == E_SWIGLU) {
+            const int np = nrows / 2;
+            for (int idx = tid; idx < np * R; idx += NCT) {
+                const int p = idx / R, r = idx - p * R;
+                float g = 0.f, v = 0.f;
 #pragma unroll
-                    for (int sg = 0; sg < SEG; ++sg) {
-                        g += part[((2 * p) * SEG + sg) * RMAX + r];
-                        v += part[((2 * p + 1) * SEG + sg) * RMAX + r];
-                    }
-                    const float s = g / (1.0f + expf(-g));
-                    out[r * ld + (cr + 2 * p) / 2] = s * v;
+                for (int sg = 0; sg < SEG; ++sg) {
+                    g += sm->part[((2 * p) * SEG + sg) * RMAX + r];
+                    v += sm->part[((2 * p + 1) * SEG + sg) * RMAX + r];
                 }
-            } else {
-                for (int idx = tid; idx < nr * R; idx += NCT) {
-                    const int row = idx / R, r = idx - row * R;
-                    float y = 0.f;
+                if (eps >= 0.f) {
+                    const float inv = norm_inv(r, eps);
+                    g *= inv;
+                    v *= inv;
+                }
+                const float s = g / (1.0f + expf(-g));
+                out[r * ld + (r0 + 2 * p) / 2] = s * v;
+            }
+        } else {
+            for (int idx = tid; idx < nrows * R; idx += NCT) {
+                const int row = idx / R, r = idx - row * R;
+                float y = 0.f;
 #pragma unroll
-                    for (int sg = 0; sg < SEG; ++sg) y += part[(row * SEG + sg) * RMAX + r];
-                    const int orow = cr + row;
-                    if (kind == E_STORE) {
-                        out[r * ld + orow] = y;
-                    } else if (kind == E_RESID) {
-                        const float v = sm->xs[r][orow - c0] + y;
-                        sm->xs[r][orow - c0] = v;
-                        out[r * H + orow] = v;
-                    } else {
-                        out[orow] = y;
-                        const float w = kind == E_HEAD0 ? choose0_value(orow, y) : y;
-                        const unsigned long long k = argkey(w, orow);
-                        best = k > best ? k : best;
-                    }
+                for (int sg = 0; sg < SEG; ++sg) y += sm->part[(row * SEG + sg) * RMAX + r];
+                if (eps >= 0.f) y *= norm_inv(r, eps);
+                const int orow = r0 + row;
+                if (kind == E_STORE) {
+                    out[r * ld + orow] = y;
+                } else if (kind == E_RESID) {
+                    const float v = sm->xs[r][orow - c0] + y;
+                    sm->xs[r][orow - c0] = v;
+                    out[r * H + orow] = v;
+                } else {
+                    out[orow] = y;
+                    const float w = kind == E_HEAD0 ? choose0_value(orow, y) : y;
+                    const unsigned long long k = argkey(w, orow);
+                    best = k > best ? k : best;
                 }
             }
         }
@@ -950,11 +960,11 @@ struct Compute {
             const DLayer Ly = st.layer[l];
             // P1
             if (l == 0)
-                stage_norm(in0, in1, in2, R, Ly.in_norm, st.eps, true);
+                stage_norm(in0, in1, in2, R, Ly.in_norm, true);
             else
-                stage_norm(xr, nullptr, nullptr, R, Ly.in_norm, st.eps, false);
+                stage_norm(xr, nullptr, nullptr, R, Ly.in_norm, false);
             mark(10);
-            gemv<H>(M_QKV, 0, R, E_STORE, S.qkv, QKV_ROWS);
+            gemv<H>(M_QKV, 0, R, E_STORE, S.qkv, QKV_ROWS, st.eps);
             mark(11);
             prefetch_kv(kv, l, R, L0);
             grid_sync(1);
@@ -967,21 +977,21 @@ struct Compute {
             // P3
             stage_attn(R, nsplit);
             mark(30);
-            gemv<QDIM>(M_O, 0, R, E_RESID, S.x, H);
+            gemv<QDIM>(M_O, 0, R, E_RESID, S.x, H, -1.f);
             mark(31);
             grid_sync(3);
             if (!ok) return;
             // P4
-            stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, st.eps, false);
+            stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, false);
             mark(40);
-            gemv<H>(M_GU, 0, R, E_SWIGLU, S.act, INTER);
+            gemv<H>(M_GU, 0, R, E_SWIGLU, S.act, INTER, st.eps);
             mark(41);
             grid_sync(4);
             if (!ok) return;
             // P5
             stage_copy(S.act, R, INTER);
             mark(50);
-            gemv<INTER>(M_D, 0, R, E_RESID, S.x, H);
+            gemv<INTER>(M_D, 0, R, E_RESID, S.x, H, -1.f);
             mark(51);
             grid_sync(5);
         }
@@ -991,11 +1001,13 @@ struct Compute {
     __device__ void head(const DStack &st, int R, int rows, int kind, float *hidden_out) {
         const Scratch &S = job->s;
         const float *last[1] = {S.x + (R - 1) * H};
-        stage_norm(last, nullptr, nullptr, 1, st.final_norm, st.eps, false);
-        if (hidden_out && blockIdx.x == 0)
-            for (int i = tid; i < H; i += NCT) hidden_out[i] = sm->act[i];
+        stage_norm(last, nullptr, nullptr, 1, st.final_norm, false);
+        if (hidden_out && blockIdx.x == 0) {
+            const float inv = norm_inv(0, st.eps);
+            for (int i = tid; i < H; i += NCT) hidden_out[i] = sm->act[i] * inv;
+        }
         mark(60);
-        gemv<H>(M_HEAD, rows, 1, kind, S.logits, 0);
+        gemv<H>(M_HEAD, rows, 1, kind, S.logits, 0, st.eps);
         mark(61);
     }
 };
@@ -1027,7 +1039,6 @@ __device__ void produce(Smem *sm, const Job &job) {
         walk_stack<WDT>(p, job.tst);
         p.matrix(job.theads, M_HEAD, job.tvocab, false);
     }
-    p.drain();
 }
 
 template <int WDT>
@@ -1050,9 +1061,11 @@ __device__ void compute(Smem *sm, const Job &job) {
         } else if (c.ok) {
             // no head: still return the normed last state
             const float *last[1] = {S.x + (job.rows - 1) * H};
-            c.stage_norm(last, nullptr, nullptr, 1, job.st.final_norm, job.st.eps, false);
-            if (blockIdx.x == 0)
-                for (int i = c.tid; i < H; i += NCT) S.hidden[i] = sm->act[i];
+            c.stage_norm(last, nullptr, nullptr, 1, job.st.final_norm, false);
+            if (blockIdx.x == 0) {
+                const float inv = c.norm_inv(0, job.st.eps);
+                for (int i = c.tid; i < H; i += NCT) S.hidden[i] = sm->act[i] * inv;
+            }
         }
     } else {
         FrameState *fs = job.fs;
@@ -1146,11 +1159,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGES; ++i) {
             mbar_init(&sm->full[i], 1);
-            mbar_init(&sm->empty[i], 1);
+            mbar_init(&sm->empty[i], NCW);
         }
         mbar_init(&sm->kvbar, 1);
         sm->abort_flag = 0;
-        sm->consumed = 0;
+        sm->issued = 0;
         sm->kv_rows = 0;
         sm->barflag[0] = sm->barflag[1] = sm->barflag[2] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1161,6 +1174,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
         if (threadIdx.x % 32 == 0) produce<WDT>(sm, job);
     } else {
         compute<WDT>(sm, job);
+    }
+    // no bulk copy may be in flight when the CTA exits: after everyone is
+    // done, wait for the last chunk issued into each slot (earlier chunks of
+    // a slot completed before it was reused; normally all have landed)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int issued = sm->issued;
+        for (int s = 0; s < NSTAGES && s < issued; ++s) {
+            const int last = s + NSTAGES * ((issued - 1 - s) / NSTAGES);
+            mbar_wait(&sm->full[s], (last / NSTAGES) & 1, nullptr);
+        }
     }
 }
 
