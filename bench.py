@@ -222,6 +222,80 @@ def config_dict(dtype, args):
             "l2": "working set per frame (weights) larger than L2: no flush needed"}
 
 
+BATCH_CTX = (50, 1000)  # configs[2]: per-utterance context drawn uniformly
+KV_POS_BF16 = 8 * 128 * 2 * 2  # K + V of one position in one layer (bf16)
+
+
+def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist):
+    """B utterances (default 64) decoded together,
+    Q8_0 weights, contexts drawn uniformly in [50, 1000] (prefilled through
+    the batched path), paged bf16 KV cache; one step = one frame of every
+    utterance (15 batched predictor steps + 1 batched talker step) through
+    qtts_talkers_next_frame, codes read back to the host each frame."""
+    B, K, W = args.batch, args.batch_steps, 3
+    rng = np.random.default_rng(SEED + 7 + rank)
+    ctx = rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, B)
+    chunk = 16384
+    tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=chunk, max_pos=BATCH_CTX[1] + K + W + 8, kv_dtype="bf16")
+    pb = qtts.QwenBatch(pstack, ph, max_seqs=B, max_tokens=2 * B, max_pos=16, kv_dtype="bf16")
+    ts = qtts.QwenTalkers(tb, pb, m["ce"], m["pe"], synth.CODEC_EOS)
+    stream = torch.cuda.ExternalStream(ts.stream, device=torch.device("cuda", local_rank))
+    t0 = time.perf_counter()
+    i = 0
+    while i < B:
+        j, rows = i, 0
+        while j < B and rows + ctx[j] <= chunk:
+            rows += int(ctx[j])
+            j += 1
+        ts.start(list(range(i, j)), [synth.prompt(SEED + 1000 + s, int(ctx[s])) for s in range(i, j)],
+                 [None] * (j - i), m["pad"])
+        i = j
+    prefill_s = time.perf_counter() - t0
+    seqs = list(range(B))
+    for _ in range(W):
+        ts.next_frame(seqs)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    frames = 0
+    for _ in range(K):
+        _, more = ts.next_frame(seqs)
+        frames += int(more.sum())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    world = dist.get_world_size() if dist else 1
+    ts.free()
+    tb.free()
+    pb.free()
+    # algorithmic bytes of one batched frame: the weights once, the talker KV
+    # of every utterance (bf16), the predictor KV
+    wb = weight_bytes_per_frame("q8_0")
+    mean_ctx = float(ctx.mean()) + W + K / 2.0
+    kv = 28 * KV_POS_BF16 * B * (mean_ctx + 1)
+    kv += sum(5 * KV_POS_BF16 * B * ((0 if g == 0 else g + 1) + (2 if g == 0 else 1)) for g in range(15))
+    peaks = measured_peaks()
+    peak = peaks["hbm_gbs"] if peaks else 6650.0
+    achieved = (wb + kv) / (ms / 1000.0 / K) / 1e9
+    return {"workload": f"configs[2]: {B} utterances per GPU, contexts U({BATCH_CTX[0]},{BATCH_CTX[1]}), Q8_0 weights, "
+                        "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs",
+            "metric": "frames/s per GPU @B=%d" % B if world == 1 else "box frames/s @B=%d per GPU" % B,
+            "value": world * frames / (ms / 1000.0), "unit": "frames/s", "steps": K, "warmup": W,
+            "ms_per_batched_frame": ms / K, "frames": frames, "prefill_s_rank0": prefill_s,
+            "mean_ctx": float(ctx.mean()),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "algorithmic_bytes_per_batched_frame": wb + kv, "traffic": None,
+                         "what": "whole batched frame (weights once + talker/predictor KV), CUDA events on the stream"},
+            "e2e_note": "timed through qtts_talkers_next_frame (the public call), codes of every frame read back to "
+                        "the host inside the timed region; the prefill is outside it"}
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import qtts
@@ -243,8 +317,15 @@ def gpu_arm(args, rank, world, local_rank):
     for h in m["ph"]:
         ph.add(h)
     max_pos = PROMPT_ROWS[dtype] + max(K, W) + 16
-    tlm = qtts.QwenLm(qtts.qwen_lm_stack(dev, synth.CONFIG, m["tl"], m["tf"], dtype), th, max_pos)
-    plm = qtts.QwenLm(qtts.qwen_lm_stack(dev, synth.CONFIG, m["pl"], m["pf"], dtype), ph, 32)
+    tstack = qtts.qwen_lm_stack(dev, synth.CONFIG, m["tl"], m["tf"], dtype)
+    pstack = qtts.qwen_lm_stack(dev, synth.CONFIG, m["pl"], m["pf"], dtype)
+    # the batched frames share the stacks; they run first and
+    # are freed before the lms take ownership of the stacks
+    batched = None
+    if args.batch > 0 and dtype == "q8_0":
+        batched = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist)
+    tlm = qtts.QwenLm(tstack, th, max_pos)
+    plm = qtts.QwenLm(pstack, ph, 32)
     tk = qtts.QwenTalker(tlm, plm, m["ce"], m["pe"], synth.CODEC_EOS)
     stream = torch.cuda.ExternalStream(tk.stream, device=torch.device("cuda", local_rank))
 
@@ -342,6 +423,7 @@ def gpu_arm(args, rank, world, local_rank):
             "clocks": clk,
             "cpu_baseline": cpu,
             "restarts_at_eos": restarts,
+            "batched": batched,
             "weights_generation_s": m["gen_s"],
         }
         print(json.dumps(line), flush=True)
@@ -364,6 +446,9 @@ def main():
     ap.add_argument("--config", choices=["q8_0", "f32"], default="q8_0")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # configs[2] beside the bench line: B utterances decoded together (0: off)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch-steps", type=int, default=20)
     # smaller stacks for profiler captures only (the benchmark is 28 + 5)
     ap.add_argument("--talker-layers", type=int, default=28)
     ap.add_argument("--pred-layers", type=int, default=5)

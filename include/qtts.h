@@ -252,6 +252,39 @@ int qtts_talker_probe(qtts_talker *t, float *logits, float *hidden);
 int qtts_talker_step(qtts_talker *t, int *step);
 int qtts_talker_destroy(qtts_talker *t);
 
+/* ------------------------------------------------------------------ talkers (batched frames) */
+
+typedef struct qtts_talkers qtts_talkers;
+
+/* TQwenTalker (talker.pas:78-158), greedy, for many utterances at once: the
+ * per-frame loop of NextFrame (talker.pas:640-681) over a talker batch and a
+ * predictor batch (not owned; heads as for qtts_talker_create).  No
+ * counterpart object in the reference, which runs one TQwenTalker per
+ * utterance; each utterance follows that protocol exactly.  Utterance ids
+ * are the talker batch's sequence ids; the predictor batch needs as many
+ * sequences, `groups` positions and 2 rows per sequence per call.  A frame
+ * of n utterances is 15 batched predictor calls and one batched talker call
+ * (tcgen05 projections, paged KV), with the choices on the device. */
+int qtts_talkers_create(qtts_batch *talker, qtts_batch *predictor, const qtts_talker_config *config,
+                        const float *codec_emb, const float *pred_emb, qtts_talkers **out);
+/* The end of TQwenTalker.Start (talker.pas:561-592) for nseq utterances
+ * seqs[i] (distinct), in one batched prefill: talker Reset + Forward of
+ * rows[i] rows (all concatenated in prefill [sum rows][hidden]), the
+ * utterance's trailing text rows (trailing_rows[i] rows, concatenated in
+ * trailing; trailing_rows may be NULL for none), tts_pad [hidden] after
+ * them, empty history, ChooseCode0 of frame 0. */
+int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows, const float *prefill,
+                       const int32_t *trailing_rows, const float *trailing, const float *tts_pad);
+/* TQwenTalker.NextFrame (talker.pas:640-681) for nseq started utterances
+ * seqs[i] (distinct): codes [nseq][groups] receives row i's frame and
+ * more[i] = 1, or more[i] = 0 when the utterance has chosen eos (its codes
+ * row untouched). */
+int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t *seqs, int32_t *codes, int32_t *more);
+/* The CUDA stream (cudaStream_t) the frames run on, for callers that time
+ * them with events. */
+int qtts_talkers_stream(qtts_talkers *t, void **stream);
+int qtts_talkers_destroy(qtts_talkers *t);
+
 /* ------------------------------------------------------------------ utilities */
 
 /* InferQuantizeRowQ8_0Ref (mormot2-ai, used at lm.pas:267): n float32 (n %

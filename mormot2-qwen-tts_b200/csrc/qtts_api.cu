@@ -1377,9 +1377,20 @@ struct qtts_batch {
     size_t meta_bytes;
     int *err;
     std::vector<void *> allocs;
+    // pinned staging of the per-call metadata and page table: a ring, so
+    // that the host builds call k+1 while call k's copy is still queued
+    static constexpr int NSLOT = 4;
+    int *hmeta[NSLOT] = {};
+    cudaEvent_t mev[NSLOT] = {};
+    bool mev_live[NSLOT] = {};
+    int mslot = 0;
 };
 
 static void batch_free(qtts_batch *b) {
+    for (int k = 0; k < qtts_batch::NSLOT; ++k) {
+        if (b->mev[k]) cudaEventDestroy(b->mev[k]);
+        if (b->hmeta[k]) cudaFreeHost(b->hmeta[k]);
+    }
     for (void *p : b->allocs) cudaFree(p);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
@@ -1456,6 +1467,14 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         batch_free(b);
         return set_err(QTTS_E_CUDA, "qtts_batch_create: set-up failed");
     }
+    for (int k = 0; k < qtts_batch::NSLOT; ++k) {
+        if (cudaHostAlloc(reinterpret_cast<void **>(&b->hmeta[k]), b->meta_bytes + b->h_pages.size() * 4,
+                          cudaHostAllocDefault) != cudaSuccess ||
+            cudaEventCreateWithFlags(&b->mev[k], cudaEventDisableTiming) != cudaSuccess) {
+            batch_free(b);
+            return set_err(QTTS_E_OOM, "qtts_batch_create: out of pinned host memory");
+        }
+    }
     *out = b;
     return QTTS_OK;
 }
@@ -1508,11 +1527,15 @@ static void batch_layers(qtts_batch *b, int T, int nitems, const int *tok_seq, c
     }
 }
 
-extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x,
-                                  int head, float *logits, float *hidden) {
+// One batched forward, queued on stream st without waiting: x is a host
+// (x_dev false) or device pointer; the logits of head `head` (< 0: none)
+// and the normed last rows stay in b->logits / b->hidden, in call order.
+// Device waits that give up set b->err (read by the caller).
+static int batch_run(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x, bool x_dev,
+                     int head, cudaStream_t st) {
     if (!b || nseq <= 0 || !seqs || !rows || !x) return set_err(QTTS_E_ARG, "qtts_batch_forward: bad argument");
     if (nseq > b->max_seqs) return set_err(QTTS_E_ARG, "qtts_batch_forward: %d sequences, at most %d", nseq, b->max_seqs);
-    if (logits && (head < 0 || head >= static_cast<int>(b->heads->mats.size())))
+    if (head >= static_cast<int>(b->heads->mats.size()))
         return set_err(QTTS_E_ARG, "qtts_batch_forward: no head %d", head);
     // validate, count tokens, allocate pages
     int T = 0;
@@ -1589,11 +1612,21 @@ extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, 
     meta.insert(meta.end(), last.begin(), last.end());
     if (meta.size() * 4 > b->meta_bytes) return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: too many attention items");
     CK(cudaSetDevice(b->dev->ordinal));
-    cudaStream_t st = b->stream;
-    CK(cudaMemcpyAsync(b->meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(b->d_pages, b->h_pages.data(), b->h_pages.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(b->x, x, static_cast<size_t>(T) * H * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemsetAsync(b->err, 0, 16, st));
+    // stage metadata + page table in the next pinned slot (wait for the
+    // copy that last used it), then two copies to the device
+    const int k = b->mslot;
+    b->mslot = (k + 1) % qtts_batch::NSLOT;
+    if (b->mev_live[k]) CK(cudaEventSynchronize(b->mev[k]));
+    int *hm = b->hmeta[k];
+    std::memcpy(hm, meta.data(), meta.size() * 4);
+    const size_t pg_off = b->meta_bytes / 4;
+    std::memcpy(hm + pg_off, b->h_pages.data(), b->h_pages.size() * 4);
+    CK(cudaMemcpyAsync(b->meta, hm, meta.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->d_pages, hm + pg_off, b->h_pages.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaEventRecord(b->mev[k], st));
+    b->mev_live[k] = true;
+    CK(cudaMemcpyAsync(b->x, x, static_cast<size_t>(T) * H * 4, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                       st));
     const int wdt = b->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
     int rc = QTTS_OK;
     const int *m = b->meta;
@@ -1609,19 +1642,36 @@ extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, 
     rmsnorm_f16_kernel<<<(nseq + 7) / 8, 256, 0, st>>>(b->x, m + o_last, nseq, b->stack->d_final_norm,
                                                        b->stack->cfg.rms_eps, b->hlast16, b->hidden);
     CK(cudaGetLastError());
-    int hr = 0;
-    if (logits) {
+    if (head >= 0) {
         const HeadMat &hm = b->heads->mats[head];
-        hr = hm.rows;
-        if ((rc = gemm(hm.d, wdt, hr, H, b->hlast16, nseq, b->max_seqs, b->logits, hr, false, b->err, st))) return rc;
+        if ((rc = gemm(hm.d, wdt, hm.rows, H, b->hlast16, nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st)))
+            return rc;
     }
+    for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
+    return QTTS_OK;
+}
+
+extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x,
+                                  int head, float *logits, float *hidden) {
+    if (!b) return set_err(QTTS_E_ARG, "qtts_batch_forward: NULL batch");
+    if (logits && (head < 0 || head >= static_cast<int>(b->heads->mats.size())))
+        return set_err(QTTS_E_ARG, "qtts_batch_forward: no head %d", head);
+    CK(cudaSetDevice(b->dev->ordinal));
+    cudaStream_t st = b->stream;
+    CK(cudaMemsetAsync(b->err, 0, 16, st));
+    std::vector<int> saved(b->len);
+    int rc = batch_run(b, nseq, seqs, rows, x, false, logits ? head : -1, st);
+    if (rc) return rc;
     int err = 0;
+    const int hr = logits ? b->heads->mats[head].rows : 0;
     CK(cudaMemcpyAsync(&err, b->err, 4, cudaMemcpyDeviceToHost, st));
     if (logits) CK(cudaMemcpyAsync(logits, b->logits, static_cast<size_t>(nseq) * hr * 4, cudaMemcpyDeviceToHost, st));
     if (hidden) CK(cudaMemcpyAsync(hidden, b->hidden, static_cast<size_t>(nseq) * H * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
-    if (err) return set_err(QTTS_E_TIMEOUT, "qtts_batch_forward: a device wait gave up");
-    for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
+    if (err) {
+        b->len = saved;
+        return set_err(QTTS_E_TIMEOUT, "qtts_batch_forward: a device wait gave up");
+    }
     return QTTS_OK;
 }
 
@@ -1629,5 +1679,266 @@ extern "C" int qtts_batch_destroy(qtts_batch *b) {
     if (!b) return QTTS_OK;
     cudaSetDevice(b->dev->ordinal);
     batch_free(b);
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ batched frames
+//
+// qtts_talkers: TQwenTalker (greedy) for many utterances at once over a
+// talker batch and a predictor batch.  The state of every utterance lives on
+// the device; a frame is 15 predictor calls and one talker call over all
+// active utterances, queued back to back with the choices between them,
+// and one read of the codes at its end.
+
+struct qtts_talkers {
+    qtts_batch *tb, *pb;
+    qtts_talker_config cfg;
+    cudaStream_t stream;
+    float *codec_emb, *pred_emb, *tts_pad, *hid, *px, *xt;
+    const float **d_trail;
+    std::vector<float *> trail;  // per utterance, device (NULL: none)
+    SeqState *ss;
+    unsigned char *seen;
+    int *d_seqs, *d_aux, *d_codes, *d_done;
+    int *h_io;  // pinned: seqs | aux | codes | done | errs
+    std::vector<char> started, done;
+    std::vector<void *> allocs;
+};
+
+static void talkers_free(qtts_talkers *t) {
+    for (float *p : t->trail)
+        if (p) cudaFree(p);
+    for (void *p : t->allocs) cudaFree(p);
+    if (t->h_io) cudaFreeHost(t->h_io);
+    delete t;
+}
+
+extern "C" int qtts_talkers_create(qtts_batch *talker, qtts_batch *pred, const qtts_talker_config *c,
+                                   const float *codec_emb, const float *pred_emb, qtts_talkers **out) {
+    if (!talker || !pred || !c || !codec_emb || !pred_emb || !out)
+        return set_err(QTTS_E_ARG, "qtts_talkers_create: NULL argument");
+    *out = nullptr;
+    if (talker->dev != pred->dev) return set_err(QTTS_E_ARG, "qtts_talkers_create: batches on different devices");
+    if (c->groups < 2 || c->groups > MAX_GROUPS || c->vocab <= 1024 || c->pred_vocab <= 0 || c->codec_eos < 0 ||
+        c->codec_eos >= c->vocab || !(c->repetition_penalty > 0.f))
+        return set_err(QTTS_E_ARG, "qtts_talkers_create: bad talker configuration");
+    if (talker->heads->mats.size() != 1 || talker->heads->mats[0].rows != c->vocab)
+        return set_err(QTTS_E_ARG, "qtts_talkers_create: the talker needs one head of %d rows", c->vocab);
+    if (static_cast<int>(pred->heads->mats.size()) != c->groups - 1)
+        return set_err(QTTS_E_ARG, "qtts_talkers_create: the predictor needs %d heads", c->groups - 1);
+    for (const HeadMat &m : pred->heads->mats)
+        if (m.rows != c->pred_vocab) return set_err(QTTS_E_ARG, "qtts_talkers_create: predictor head rows");
+    const int S = talker->max_seqs;
+    if (pred->max_seqs < S || pred->max_pos < c->groups || pred->max_tokens < 2 * S)
+        return set_err(QTTS_E_ARG,
+                       "qtts_talkers_create: the predictor batch needs >= %d sequences, %d positions, %d rows", S,
+                       c->groups, 2 * S);
+    CK(cudaSetDevice(talker->dev->ordinal));
+    qtts_talkers *t = new qtts_talkers();
+    t->tb = talker;
+    t->pb = pred;
+    t->cfg = *c;
+    t->stream = talker->stream;
+    t->trail.assign(S, nullptr);
+    t->started.assign(S, 0);
+    t->done.assign(S, 0);
+    const size_t G = c->groups;
+    struct A {
+        void **p;
+        size_t bytes;
+    } want[] = {
+        {reinterpret_cast<void **>(&t->codec_emb), static_cast<size_t>(c->vocab) * H * 4},
+        {reinterpret_cast<void **>(&t->pred_emb), (G - 1) * c->pred_vocab * H * 4},
+        {reinterpret_cast<void **>(&t->tts_pad), static_cast<size_t>(S) * H * 4},
+        {reinterpret_cast<void **>(&t->hid), static_cast<size_t>(S) * H * 4},
+        {reinterpret_cast<void **>(&t->px), static_cast<size_t>(2 * S) * H * 4},
+        {reinterpret_cast<void **>(&t->xt), static_cast<size_t>(S) * H * 4},
+        {reinterpret_cast<void **>(&t->d_trail), static_cast<size_t>(S) * sizeof(float *)},
+        {reinterpret_cast<void **>(&t->ss), static_cast<size_t>(S) * sizeof(SeqState)},
+        {reinterpret_cast<void **>(&t->seen), static_cast<size_t>(S) * c->vocab},
+        {reinterpret_cast<void **>(&t->d_seqs), static_cast<size_t>(S) * 4},
+        {reinterpret_cast<void **>(&t->d_aux), static_cast<size_t>(S) * 4},
+        {reinterpret_cast<void **>(&t->d_codes), static_cast<size_t>(S) * G * 4},
+        {reinterpret_cast<void **>(&t->d_done), static_cast<size_t>(S) * 4},
+    };
+    for (const A &a : want) {
+        if (cudaMalloc(a.p, a.bytes) != cudaSuccess) {
+            talkers_free(t);
+            return set_err(QTTS_E_OOM, "qtts_talkers_create: out of device memory (%zu bytes)", a.bytes);
+        }
+        t->allocs.push_back(*a.p);
+    }
+    if (cudaHostAlloc(reinterpret_cast<void **>(&t->h_io), (static_cast<size_t>(S) * (G + 3) + 8) * 4,
+                      cudaHostAllocDefault) != cudaSuccess) {
+        talkers_free(t);
+        return set_err(QTTS_E_OOM, "qtts_talkers_create: out of pinned host memory");
+    }
+    if (cudaMemcpy(t->codec_emb, codec_emb, static_cast<size_t>(c->vocab) * H * 4, cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemcpy(t->pred_emb, pred_emb, (G - 1) * c->pred_vocab * H * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(t->d_trail, 0, static_cast<size_t>(S) * sizeof(float *)) != cudaSuccess) {
+        talkers_free(t);
+        return set_err(QTTS_E_CUDA, "qtts_talkers_create: upload failed");
+    }
+    *out = t;
+    return QTTS_OK;
+}
+
+// the pinned I/O area: [S] seqs | [S] aux | [S*G] codes | [S] done | [8] errs
+static int *io_seqs(qtts_talkers *t) { return t->h_io; }
+static int *io_aux(qtts_talkers *t) { return t->h_io + t->tb->max_seqs; }
+static int *io_codes(qtts_talkers *t) { return t->h_io + 2 * t->tb->max_seqs; }
+static int *io_done(qtts_talkers *t) { return t->h_io + (2 + t->cfg.groups) * t->tb->max_seqs; }
+static int *io_errs(qtts_talkers *t) { return t->h_io + (3 + t->cfg.groups) * t->tb->max_seqs; }
+
+static int distinct_seqs(const qtts_talkers *t, int nseq, const int32_t *seqs, const char *who) {
+    if (nseq <= 0 || nseq > t->tb->max_seqs || !seqs) return set_err(QTTS_E_ARG, "%s: bad sequence list", who);
+    std::vector<char> seen(t->tb->max_seqs, 0);
+    for (int i = 0; i < nseq; ++i) {
+        if (seqs[i] < 0 || seqs[i] >= t->tb->max_seqs || seen[seqs[i]])
+            return set_err(QTTS_E_ARG, "%s: entry %d: sequence %d", who, i, seqs[i]);
+        seen[seqs[i]] = 1;
+    }
+    return QTTS_OK;
+}
+
+// both batches' error words, read after the stream has drained
+static int talkers_finish(qtts_talkers *t, const char *who) {
+    cudaStream_t st = t->stream;
+    int *e = io_errs(t);
+    CK(cudaMemcpyAsync(e, t->tb->err, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(e + 1, t->pb->err, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (e[0] || e[1]) return set_err(QTTS_E_TIMEOUT, "%s: a device wait gave up", who);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows,
+                                  const float *prefill, const int32_t *trailing_rows, const float *trailing,
+                                  const float *tts_pad) {
+    if (!t || !rows || !prefill || !tts_pad) return set_err(QTTS_E_ARG, "qtts_talkers_start: NULL argument");
+    int rc = distinct_seqs(t, nseq, seqs, "qtts_talkers_start");
+    if (rc) return rc;
+    size_t ntrail = 0;
+    for (int i = 0; i < nseq; ++i) {
+        const int tr = trailing_rows ? trailing_rows[i] : 0;
+        if (rows[i] <= 0 || tr < 0) return set_err(QTTS_E_ARG, "qtts_talkers_start: entry %d: bad row counts", i);
+        if (rows[i] > t->tb->max_pos)
+            return set_err(QTTS_E_CAPACITY, "qtts_talkers_start: %d prefill rows, at most %d", rows[i], t->tb->max_pos);
+        ntrail += tr;
+    }
+    if (ntrail > 0 && !trailing) return set_err(QTTS_E_ARG, "qtts_talkers_start: NULL trailing rows");
+    CK(cudaSetDevice(t->tb->dev->ordinal));
+    cudaStream_t st = t->stream;
+    CK(cudaStreamSynchronize(st));
+    // the utterances' trailing text rows and tts_pad
+    const float *src = trailing;
+    for (int i = 0; i < nseq; ++i) {
+        const int s = seqs[i], tr = trailing_rows ? trailing_rows[i] : 0;
+        t->started[s] = 0;
+        if (t->trail[s]) cudaFree(t->trail[s]);
+        t->trail[s] = nullptr;
+        if (tr > 0) {
+            if (cudaMalloc(&t->trail[s], static_cast<size_t>(tr) * H * 4) != cudaSuccess)
+                return set_err(QTTS_E_OOM, "qtts_talkers_start: out of device memory");
+            CK(cudaMemcpy(t->trail[s], src, static_cast<size_t>(tr) * H * 4, cudaMemcpyHostToDevice));
+            src += static_cast<size_t>(tr) * H;
+        }
+        CK(cudaMemcpy(t->d_trail + s, &t->trail[s], sizeof(float *), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(t->tts_pad + static_cast<size_t>(s) * H, tts_pad, H * 4, cudaMemcpyHostToDevice));
+        qtts_batch_reset(t->tb, s);
+        io_seqs(t)[i] = s;
+        io_aux(t)[i] = tr;
+    }
+    CK(cudaMemcpyAsync(t->d_seqs, io_seqs(t), nseq * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(t->d_aux, io_aux(t), nseq * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(t->tb->err, 0, 16, st));
+    CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
+    frames_start_kernel<<<nseq, 256, 0, st>>>(t->d_seqs, t->d_aux, t->ss, t->seen, t->cfg.vocab);
+    CK(cudaGetLastError());
+    if ((rc = batch_run(t->tb, nseq, seqs, rows, prefill, false, 0, st))) return rc;
+    frames_choose0_kernel<<<nseq, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
+                                                t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
+                                                t->d_done, 1);
+    CK(cudaGetLastError());
+    if ((rc = talkers_finish(t, "qtts_talkers_start"))) return rc;
+    for (int i = 0; i < nseq; ++i) {
+        t->started[seqs[i]] = 1;
+        t->done[seqs[i]] = 0;  // eos is forbidden before 2 frames
+    }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t *seqs, int32_t *codes,
+                                       int32_t *more) {
+    if (!t || !codes || !more) return set_err(QTTS_E_ARG, "qtts_talkers_next_frame: NULL argument");
+    int rc = distinct_seqs(t, nseq, seqs, "qtts_talkers_next_frame");
+    if (rc) return rc;
+    const int G = t->cfg.groups;
+    std::vector<int> act, slot;
+    for (int i = 0; i < nseq; ++i) {
+        const int s = seqs[i];
+        if (!t->started[s]) return set_err(QTTS_E_STATE, "qtts_talkers_next_frame: sequence %d not started", s);
+        more[i] = 0;
+        if (t->done[s]) continue;
+        if (t->tb->len[s] + 1 > t->tb->max_pos)
+            return set_err(QTTS_E_CAPACITY, "qtts_talkers_next_frame: sequence %d: talker cache full (%d positions)",
+                           s, t->tb->max_pos);
+        act.push_back(s);
+        slot.push_back(i);
+    }
+    const int n = static_cast<int>(act.size());
+    if (n == 0) return QTTS_OK;
+    CK(cudaSetDevice(t->tb->dev->ordinal));
+    cudaStream_t st = t->stream;
+    std::memcpy(io_seqs(t), act.data(), n * 4);
+    CK(cudaMemcpyAsync(t->d_seqs, io_seqs(t), n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(t->tb->err, 0, 16, st));
+    CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
+    frames_begin_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->seen, t->cfg.vocab, t->hid, t->codec_emb, t->px,
+                                           t->d_codes, G);
+    CK(cudaGetLastError());
+    // predictor: Reset, [state, codec_emb[code 0]] with head 0, then one row
+    // per group with head g (talker.pas:656-675)
+    for (int s : act) qtts_batch_reset(t->pb, s);
+    std::vector<int> rows(n, 2);
+    const int pv = t->cfg.pred_vocab;
+    for (int g = 0; g < G - 1; ++g) {
+        if ((rc = batch_run(t->pb, n, act.data(), rows.data(), t->px, true, g, st))) return rc;
+        frames_pred_argmax_kernel<<<n, 256, 0, st>>>(t->pb->logits, pv, g, G, t->pred_emb, t->px, t->d_codes);
+        CK(cudaGetLastError());
+        if (g == 0) rows.assign(n, 1);
+    }
+    // talker step, then ChooseCode0 of the next frame
+    frames_talker_in_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->d_codes, G, t->codec_emb, t->pred_emb, pv,
+                                               t->d_trail, t->tts_pad, t->xt);
+    CK(cudaGetLastError());
+    if ((rc = batch_run(t->tb, n, act.data(), rows.data(), t->xt, true, 0, st))) return rc;
+    frames_choose0_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
+                                             t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
+                                             t->d_done, 0);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(io_codes(t), t->d_codes, static_cast<size_t>(n) * G * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(io_done(t), t->d_done, n * 4, cudaMemcpyDeviceToHost, st));
+    if ((rc = talkers_finish(t, "qtts_talkers_next_frame"))) return rc;
+    for (int j = 0; j < n; ++j) {
+        std::memcpy(codes + static_cast<size_t>(slot[j]) * G, io_codes(t) + static_cast<size_t>(j) * G, G * 4);
+        more[slot[j]] = 1;
+        t->done[act[j]] = io_done(t)[j] ? 1 : 0;
+    }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_stream(qtts_talkers *t, void **stream) {
+    if (!t || !stream) return set_err(QTTS_E_ARG, "qtts_talkers_stream: NULL argument");
+    *stream = t->stream;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_destroy(qtts_talkers *t) {
+    if (!t) return QTTS_OK;
+    cudaSetDevice(t->tb->dev->ordinal);
+    cudaStreamSynchronize(t->stream);
+    talkers_free(t);
     return QTTS_OK;
 }

@@ -284,4 +284,153 @@ __global__ void swiglu_f16_kernel(const float *gu, long long n_pairs, __half *ac
     act16[i] = __float2half_rn(s * gv.y);
 }
 
+// ------------------------------------------------------------------ batched frames
+//
+// TQwenTalker.NextFrame (talker.pas:640-681) for many utterances: the
+// per-utterance state lives on the device, the steps of a frame are batched
+// forwards over all utterances (one predictor call per group, one talker
+// call), and these kernels do the choices and the embedding sums between them.
+
+// per-utterance frame state (TQwenTalker fields fHistory, fStep, ...)
+struct SeqState {
+    int next_code0;     // chosen at the end of the previous talker forward
+    int done;           // next_code0 == eos
+    int hist_len;       // frames returned (history length)
+    int step;           // fStep
+    int trailing_rows;  // rows of this utterance's trailing text
+    int pad[3];
+};
+
+// Start: reset the state of seqs[i], clear its history marks.
+__global__ void frames_start_kernel(const int *seqs, const int *trailing_rows, SeqState *ss, unsigned char *seen,
+                                    int vocab) {
+    const int s = seqs[blockIdx.x];
+    unsigned char *m = seen + static_cast<size_t>(s) * vocab;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) m[i] = 0;
+    if (threadIdx.x == 0) {
+        SeqState st = {};
+        st.trailing_rows = trailing_rows[blockIdx.x];
+        ss[s] = st;
+    }
+}
+
+// Frame begin (talker.pas:656-667): code 0 joins the history; predictor
+// input rows 2i, 2i+1 = [talker state, codec_emb[code 0]].
+__global__ void frames_begin_kernel(const int *seqs, SeqState *ss, unsigned char *seen, int vocab,
+                                    const float *hid, const float *codec_emb, float *px, int *codes, int groups) {
+    const int i = blockIdx.x, s = seqs[i];
+    const int c0 = ss[s].next_code0;
+    const float *h = hid + static_cast<size_t>(s) * H;
+    const float *e = codec_emb + static_cast<size_t>(c0) * H;
+    float *x0 = px + static_cast<size_t>(2 * i) * H;
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        store4(x0 + 4 * c, load4(h + 4 * c));
+        store4(x0 + H + 4 * c, load4(e + 4 * c));
+    }
+    if (threadIdx.x == 0) {
+        seen[static_cast<size_t>(s) * vocab + c0] = 1;
+        ss[s].hist_len += 1;
+        codes[i * groups] = c0;
+    }
+}
+
+// block-wide argmax key of n values
+__device__ __forceinline__ unsigned long long block_argmax(unsigned long long b, unsigned long long *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+        b = t > b ? t : b;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = b;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+            b = t > b ? t : b;
+        }
+        if (threadIdx.x == 0) red[0] = b;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+// ChooseCode (talker.pas:632-638), greedy, after predictor step g: code g+1
+// of row i = the first maximum of its logits; the next predictor input row
+// is pred_emb[g][code] (talker.pas:670-675).
+__global__ void frames_pred_argmax_kernel(const float *logits, int vocab, int g, int groups, const float *pred_emb,
+                                          float *px, int *codes) {
+    __shared__ unsigned long long red[32];
+    const int i = blockIdx.x;
+    const float *lg = logits + static_cast<size_t>(i) * vocab;
+    unsigned long long b = 0ull;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+        const unsigned long long k = argkey(lg[j], j);
+        b = k > b ? k : b;
+    }
+    const int code = key_index(block_argmax(b, red));
+    if (threadIdx.x == 0) codes[i * groups + g + 1] = code;
+    if (g + 1 < groups - 1) {
+        const float *e = pred_emb + (static_cast<size_t>(g) * vocab + code) * H;
+        float *x = px + static_cast<size_t>(i) * H;
+        for (int c = threadIdx.x; c < H / 4; c += blockDim.x) store4(x + 4 * c, load4(e + 4 * c));
+    }
+}
+
+// The next talker input (talker.pas:669-677): codec_emb[code 0] + the 15
+// predictor embeddings in group order + trailing[step] (tts_pad after the
+// trailing rows), summed left to right in float32.
+__global__ void frames_talker_in_kernel(const int *seqs, const SeqState *ss, const int *codes, int groups,
+                                        const float *codec_emb, const float *pred_emb, int pvocab,
+                                        const float *const *trailing, const float *tts_pad, float *xt) {
+    const int i = blockIdx.x, s = seqs[i];
+    const int *cd = codes + i * groups;
+    const int step = ss[s].step;
+    const float *tr = step < ss[s].trailing_rows ? trailing[s] + static_cast<size_t>(step) * H
+                                                 : tts_pad + static_cast<size_t>(s) * H;
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        float4 a = load4(codec_emb + static_cast<size_t>(cd[0]) * H + 4 * c);
+        for (int g = 1; g < groups; ++g) {
+            const float4 e = load4(pred_emb + (static_cast<size_t>(g - 1) * pvocab + cd[g]) * H + 4 * c);
+            a = make_float4(a.x + e.x, a.y + e.y, a.z + e.z, a.w + e.w);
+        }
+        const float4 e = load4(tr + 4 * c);
+        store4(xt + static_cast<size_t>(i) * H + 4 * c, make_float4(a.x + e.x, a.y + e.y, a.z + e.z, a.w + e.w));
+    }
+}
+
+// ChooseCode0 (talker.pas:595-630), greedy, after a talker forward: the
+// last 1024 ids forbidden but eos, eos forbidden before 2 frames, the
+// repetition penalty once per distinct code of the history; the normed
+// state of the row becomes the utterance's talker state.  done[i] = eos
+// chosen (read by the host).  start != 0: after the prefill (empty history).
+__global__ void frames_choose0_kernel(const int *seqs, const float *logits, const float *hidden, int vocab, int eos,
+                                      float penalty, const unsigned char *seen, SeqState *ss, float *hid, int *done,
+                                      int start) {
+    __shared__ unsigned long long red[32];
+    const int i = blockIdx.x, s = seqs[i];
+    const float *lg = logits + static_cast<size_t>(i) * vocab;
+    const unsigned char *m = seen + static_cast<size_t>(s) * vocab;
+    const int hist = ss[s].hist_len;
+    unsigned long long b = 0ull;
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+        float w = lg[j];
+        if (j >= vocab - 1024 && j != eos) w = -INFINITY;
+        else if (j == eos && hist < 2) w = -INFINITY;
+        else if (penalty != 1.0f && m[j]) w = w > 0.f ? __fdiv_rn(w, penalty) : w * penalty;
+        const unsigned long long k = argkey(w, j);
+        b = k > b ? k : b;
+    }
+    const int code = key_index(block_argmax(b, red));
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x)
+        store4(hid + static_cast<size_t>(s) * H + 4 * c, load4(hidden + static_cast<size_t>(i) * H + 4 * c));
+    if (threadIdx.x == 0) {
+        ss[s].next_code0 = code;
+        ss[s].done = code == eos ? 1 : 0;
+        if (!start) ss[s].step += 1;
+        done[i] = code == eos ? 1 : 0;
+    }
+}
+
 }  // namespace qtts

@@ -99,6 +99,11 @@ EXPORTS = {
     "qtts_talker_probe": [P, P, P],
     "qtts_talker_step": [P, PI],
     "qtts_talker_destroy": [P],
+    "qtts_talkers_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
+    "qtts_talkers_start": [P, I, P, P, P, P, P, P],
+    "qtts_talkers_next_frame": [P, I, P, P, P],
+    "qtts_talkers_stream": [P, ctypes.POINTER(P)],
+    "qtts_talkers_destroy": [P],
     "qtts_quantize_q8_0": [P, P, ctypes.c_int64, P],
 }
 
@@ -425,4 +430,52 @@ class QwenTalker:
     def free(self):
         if self.handle:
             check(lib().qtts_talker_destroy(self.handle))
+            self.handle = None
+
+
+class QwenTalkers:
+    """TQwenTalker (greedy) for many utterances at once over a talker batch
+    and a predictor batch (not owned); utterance ids are sequence ids."""
+
+    def __init__(self, talker, predictor, codec_emb, pred_emb, eos, vocab=3072, pred_vocab=2048, groups=16,
+                 repetition_penalty=1.05):
+        cfg = TalkerConfig(vocab, pred_vocab, groups, eos, repetition_penalty)
+        ce, pe = _f32(codec_emb), _f32(pred_emb)
+        h = P()
+        check(lib().qtts_talkers_create(talker.handle, predictor.handle, ctypes.byref(cfg), _ptr(ce), _ptr(pe),
+                                        ctypes.byref(h)))
+        self.handle = h
+        self.groups = groups
+        self.hidden = talker.hidden
+
+    def start(self, seqs, prefills, trailings, tts_pad):
+        """TQwenTalker.Start for utterances seqs[i]: prefills[i] [rows][hidden],
+        trailings[i] [rows][hidden] or None, one tts_pad [hidden]."""
+        sq = np.ascontiguousarray(seqs, dtype=np.int32)
+        rows = np.array([len(p) for p in prefills], np.int32)
+        trs = np.array([0 if t is None else len(t) for t in trailings], np.int32)
+        pf = _f32(np.concatenate([np.asarray(p, np.float32) for p in prefills]))
+        tl = [np.asarray(t, np.float32) for t in trailings if t is not None and len(t)]
+        tr = _f32(np.concatenate(tl)) if tl else None
+        check(lib().qtts_talkers_start(self.handle, sq.size, _ptr(sq), _ptr(rows), _ptr(pf), _ptr(trs), _ptr(tr),
+                                       _ptr(_f32(tts_pad))))
+
+    def next_frame(self, seqs):
+        """TQwenTalker.NextFrame for utterances seqs: returns (codes [n][groups],
+        more [n] bool)."""
+        sq = np.ascontiguousarray(seqs, dtype=np.int32)
+        codes = np.zeros((sq.size, self.groups), np.int32)
+        more = np.zeros(sq.size, np.int32)
+        check(lib().qtts_talkers_next_frame(self.handle, sq.size, _ptr(sq), _ptr(codes), _ptr(more)))
+        return codes, more.astype(bool)
+
+    @property
+    def stream(self):
+        v = P()
+        check(lib().qtts_talkers_stream(self.handle, ctypes.byref(v)))
+        return v.value or 0
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_talkers_destroy(self.handle))
             self.handle = None

@@ -70,6 +70,7 @@ def _load():
         "ora_talker_free": (None, [P]),
         "ora_talker_start": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P]),
         "ora_talker_next_frame": (ctypes.c_int, [P, P]),
+        "ora_talker_check_frame": (ctypes.c_int, [P, P, P]),
         "ora_talker_logits": (P, [P]),
         "ora_talker_hidden": (P, [P]),
         "ora_rope_table": (None, [ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P]),
@@ -251,6 +252,17 @@ class OraTalker:
         if rc < 0:
             raise RuntimeError("oracle: KV cache full")
         return rc == 1
+
+    def check_frame(self, codes):
+        """The frame whose codes were chosen elsewhere: returns (more, gaps),
+        gaps[g] = how far codes[g] falls below the best value of choice g
+        (0 when it is a first maximum or a tie)."""
+        c = np.ascontiguousarray(codes, dtype=np.int32)
+        gap = np.zeros(self.groups, np.float32)
+        rc = lib.ora_talker_check_frame(self.handle, _p(c), _p(gap))
+        if rc < 0:
+            raise RuntimeError("oracle: KV cache full")
+        return rc == 1, gap
 
     def logits(self):
         ptr = lib.ora_talker_logits(self.handle)

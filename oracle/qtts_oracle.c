@@ -660,11 +660,21 @@ static void add_row(float *y, const float *row, int H) {
     for (int c = 0; c < H; c++) y[c] = y[c] + row[c];
 }
 
-/* TQwenTalker.NextFrame (talker.pas:640-681), greedy: returns 1 and fills
- * codes[groups], 0 at eos, -1 when a cache is full */
-int ora_talker_next_frame(ora_talker *t, int *codes) {
+/* TQwenTalker.NextFrame (talker.pas:640-681), greedy.  force == NULL: the
+ * oracle's own choices go to codes[groups].  force != NULL: the frame is
+ * driven by the codes force[groups] (another implementation's choices) and
+ * gap[g] receives how far force[g] falls below the best value of choice g
+ * under the same rule (0 for a first maximum or a tie; +inf for a forbidden
+ * id).  Returns 1 after a frame, 0 when code 0 is eos, -1 when a cache is
+ * full. */
+static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap) {
     int H = t->H;
     int code = ora_choose_code0(t->logits, t->vocab, t->eos, t->history, t->nhist, t->penalty, t->work);
+    if (force) {
+        gap[0] = t->work[code] - t->work[force[0]];
+        if (t->work[force[0]] == -INFINITY) gap[0] = INFINITY;
+        code = force[0];
+    }
     if (code == t->eos) return 0;
     codes[0] = code;
     if (t->nhist == t->cap) {
@@ -681,7 +691,12 @@ int ora_talker_next_frame(ora_talker *t, int *codes) {
             memcpy(t->x, t->pred_emb + ((size_t)(g - 1) * t->pvocab + codes[g]) * H, H * sizeof(float));
             if (ora_lm_forward(t->pred, t->x, 1, t->ph, g, t->plogits, NULL, NULL, NULL)) return -1;
         }
-        codes[g + 1] = ora_argmax(t->plogits, t->pvocab);
+        int best = ora_argmax(t->plogits, t->pvocab);
+        if (force) {
+            gap[g + 1] = t->plogits[best] - t->plogits[force[g + 1]];
+            best = force[g + 1];
+        }
+        codes[g + 1] = best;
     }
     memcpy(t->x, t->codec_emb + (size_t)code * H, H * sizeof(float));
     for (int g = 1; g < t->groups; g++)
@@ -693,6 +708,16 @@ int ora_talker_next_frame(ora_talker *t, int *codes) {
     if (ora_lm_forward(t->talker, t->x, 1, t->th, 0, t->logits, t->past_hidden, NULL, NULL)) return -1;
     t->step++;
     return 1;
+}
+
+/* returns 1 and fills codes[groups], 0 at eos, -1 when a cache is full */
+int ora_talker_next_frame(ora_talker *t, int *codes) { return talker_frame(t, NULL, codes, NULL); }
+
+/* the frame chosen elsewhere (codes[groups]), with the gaps of its choices */
+int ora_talker_check_frame(ora_talker *t, const int *codes, float *gap) {
+    int own[64];
+    if (t->groups > 64) return -1;
+    return talker_frame(t, codes, own, gap);
 }
 
 const float *ora_talker_logits(const ora_talker *t) { return t->logits; }

@@ -1,0 +1,166 @@
+"""The batched frame loop (qtts_talkers_*: TQwenTalker.NextFrame for many
+utterances at once, talker.pas:640-681) against the oracle, utterance by
+utterance.
+
+The batched path computes its projections with fp16 activations (tcgen05
+GEMM, f32 accumulation), so a greedy choice may differ from the oracle's on a
+near-tie.  Each frame is therefore replayed in the oracle driven by the
+device's codes (ora_talker_check_frame), and every choice must be a maximum
+of the oracle's values to within twice the logit tolerance of the batched
+forward (2e-2 abs with Q8_0 weights and f32 KV, 5e-2 with bf16 KV, 2e-3 with
+f32 weights and f32 KV).  Shapes follow BASELINE.json configs[2] at reduced
+size: ragged prompts, utterances started at different times, subsets of
+utterances per frame.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import qtts
+import synth
+
+pytestmark = pytest.mark.gpu
+
+GAP = {("q8_0", "f32"): 4e-2, ("q8_0", "bf16"): 1e-1, ("f32", "f32"): 4e-3}
+
+
+class Rig:
+    """Talker + predictor batches and the batched talkers on the device; one
+    oracle TQwenTalker per utterance on shared oracle stacks."""
+
+    def __init__(self, device, seed, tlayers, players, dtype, kv, nseq, max_pos=256, theads=None,
+                 max_tokens=1024):
+        th = [synth.talker_head(seed)] if theads is None else theads
+        ph = synth.predictor_heads(seed)
+        tls, tfinal = synth.stack(seed, "talker", tlayers)
+        pls, pfinal = synth.stack(seed, "predictor", players)
+        self.tst = qtts.qwen_lm_stack(device, synth.CONFIG, tls, tfinal, dtype)
+        self.pst = qtts.qwen_lm_stack(device, synth.CONFIG, pls, pfinal, dtype)
+        self.th = qtts.QwenLmHeads(device, "talker", synth.HIDDEN, dtype)
+        self.ph = qtts.QwenLmHeads(device, "predictor", synth.HIDDEN, dtype)
+        self.oth = O.OraHeads(synth.HIDDEN, dtype)
+        self.oph = O.OraHeads(synth.HIDDEN, dtype)
+        for h in th:
+            self.th.add(h)
+            self.oth.add(h)
+        for h in ph:
+            self.ph.add(h)
+            self.oph.add(h)
+        self.tb = qtts.QwenBatch(self.tst, self.th, max_seqs=nseq, max_tokens=max_tokens, max_pos=max_pos,
+                                 kv_dtype=kv)
+        self.pb = qtts.QwenBatch(self.pst, self.ph, max_seqs=nseq, max_tokens=2 * nseq, max_pos=16, kv_dtype=kv)
+        ce = synth.codec_embedding(seed)
+        pe = synth.predictor_embeddings(seed)
+        self.dev = qtts.QwenTalkers(self.tb, self.pb, ce, pe, synth.CODEC_EOS)
+        self.ots = O.OraStack(synth.CONFIG, tls, tfinal, dtype)
+        self.ops = O.OraStack(synth.CONFIG, pls, pfinal, dtype)
+        self.olms = []
+        self.ora = []
+        for _ in range(nseq):
+            tl = O.OraLm(self.ots, self.oth, max_pos)
+            pl = O.OraLm(self.ops, self.oph, 32)
+            self.olms += [tl, pl]
+            self.ora.append(O.OraTalker(tl, self.oth, pl, self.oph, ce, pe, synth.CODEC_EOS))
+
+    def free(self):
+        self.dev.free()
+        self.tb.free()
+        self.pb.free()
+        qtts.stack_destroy(self.tst)
+        qtts.stack_destroy(self.pst)
+        self.th.free()
+        self.ph.free()
+        for o in self.ora:
+            o.free()
+        for o in self.olms:
+            o.free()
+        self.ots.free()
+        self.ops.free()
+        self.oth.free()
+        self.oph.free()
+
+
+def start(rig, seqs, seed):
+    pad = synth.text_rows(seed, 1, key=1)[0]
+    rng = np.random.default_rng(seed)
+    prefills = [synth.prompt(seed * 100 + s, int(rng.integers(5, 60))) for s in seqs]
+    trailings = [synth.text_rows(seed * 100 + s, int(rng.integers(0, 5))) for s in seqs]
+    trailings = [t if len(t) else None for t in trailings]
+    rig.dev.start(seqs, prefills, trailings, pad)
+    for s, p, t in zip(seqs, prefills, trailings):
+        rig.ora[s].start(p, t, pad)
+    return prefills
+
+
+def frame(rig, seqs, max_gap, stats):
+    codes, more = rig.dev.next_frame(seqs)
+    for i, s in enumerate(seqs):
+        if not more[i]:
+            # eos: the oracle's ChooseCode0 must allow eos as a maximum
+            m, gap = rig.ora[s].check_frame(np.full(16, synth.CODEC_EOS, np.int32))
+            assert not m and gap[0] <= max_gap, (s, gap[0])
+            continue
+        m, gap = rig.ora[s].check_frame(codes[i])
+        assert m, f"utterance {s}: eos in the oracle only"
+        assert np.all(gap <= max_gap), (s, codes[i], gap)
+        stats[0] += int(np.sum(gap == 0))
+        stats[1] += gap.size
+    return codes, more
+
+
+@pytest.mark.parametrize("dtype,kv", [("q8_0", "bf16"), ("q8_0", "f32"), ("f32", "f32")])
+def test_batched_frames_match_oracle(device, dtype, kv):
+    rig = Rig(device, 71, 2, 2, dtype, kv, nseq=6)
+    gap = GAP[(dtype, kv)]
+    stats = [0, 0]
+    lens = {}
+    for s, p in zip([0, 1, 2, 3], start(rig, [0, 1, 2, 3], 71)):
+        lens[s] = len(p)
+    for _ in range(2):
+        frame(rig, [0, 1, 2, 3], gap, stats)
+    # two more utterances join; then frames over subsets in any order
+    for s, p in zip([5, 4], start(rig, [5, 4], 72)):
+        lens[s] = len(p)
+    frame(rig, [4, 5, 0, 1, 2, 3], gap, stats)
+    frame(rig, [3, 5, 1], gap, stats)
+    frame(rig, [0, 1, 2, 3, 4, 5], gap, stats)
+    frames = {0: 4, 1: 5, 2: 4, 3: 5, 4: 2, 5: 3}
+    for s in range(6):
+        assert rig.tb.length(s) == lens[s] + frames[s]
+    # nearly all choices are the oracle's own first maximum
+    assert stats[0] >= 0.9 * stats[1], stats
+    rig.free()
+
+
+def test_batched_eos_and_errors(device):
+    # an eos-dominant talker head: eos is forbidden for 2 frames
+    # (talker.pas:610-611), then chosen by every utterance
+    th = synth.talker_head(61)
+    th[synth.CODEC_EOS] = th[synth.CODEC_EOS] * 40.0 + 0.05
+    rig = Rig(device, 61, 1, 1, "f32", "f32", nseq=3, max_pos=8, theads=[th], max_tokens=64)
+    with pytest.raises(qtts.EQwenLm) as e:
+        rig.dev.next_frame([0])                       # not started
+    assert e.value.code == qtts.E_STATE
+    pad = synth.text_rows(61, 1)[0]
+    rig.dev.start([0, 1, 2], [synth.prompt(61, 4), synth.prompt(62, 5), synth.prompt(63, 4)], [None] * 3, pad)
+    for s, n in zip(range(3), (4, 5, 4)):
+        rig.ora[s].start(synth.prompt(61 + s, n), None, pad)
+    with pytest.raises(qtts.EQwenLm) as e:
+        rig.dev.next_frame([1, 1])                    # the same utterance twice
+    assert e.value.code == qtts.E_ARG
+    stats = [0, 0]
+    for f in range(2):
+        codes, more = frame(rig, [0, 1, 2], GAP[("f32", "f32")], stats)
+        assert more.all()
+    codes, more = frame(rig, [0, 1, 2], GAP[("f32", "f32")], stats)
+    assert not more.any()
+    codes, more = rig.dev.next_frame([2, 0])          # stays at eos
+    assert not more.any()
+    # capacity: 4 prefill rows + 2 frames in 8 positions, then restart with 7
+    rig.dev.start([0], [synth.prompt(64, 7)], [None], pad)
+    codes, more = rig.dev.next_frame([0])
+    assert more.all()
+    with pytest.raises(qtts.EQwenLm) as e:
+        rig.dev.next_frame([0])
+    assert e.value.code == qtts.E_CAPACITY
+    rig.free()

@@ -164,3 +164,44 @@ def test_reference_dataset_is_consistent():
     for g in range(15):
         assert O.argmax(t["predictor.logits"][g]) == codes[g + 1]
     assert np.array_equal(t["predictor.embed"][0], t["talker.norm"][-1])
+
+
+def test_check_frame_replays_next_frame():
+    # ora_talker_check_frame, the checker of the batched frame loop: driven
+    # by the oracle's own codes it reproduces NextFrame with zero gaps; a
+    # planted non-maximal choice shows a positive gap at that choice only
+    import synth
+    ls, final = synth.stack(81, "talker", 1)
+    pls, pfinal = synth.stack(81, "predictor", 1)
+    ts, ps = O.OraStack(synth.CONFIG, ls, final, "q8_0"), O.OraStack(synth.CONFIG, pls, pfinal, "q8_0")
+    th, ph = O.OraHeads(synth.HIDDEN, "q8_0"), O.OraHeads(synth.HIDDEN, "q8_0")
+    th.add(synth.talker_head(81))
+    for h in synth.predictor_heads(81):
+        ph.add(h)
+    ce, pe = synth.codec_embedding(81), synth.predictor_embeddings(81)
+    lms = [O.OraLm(ts, th, 64), O.OraLm(ps, ph, 32), O.OraLm(ts, th, 64), O.OraLm(ps, ph, 32)]
+    a = O.OraTalker(lms[0], th, lms[1], ph, ce, pe, synth.CODEC_EOS)
+    b = O.OraTalker(lms[2], th, lms[3], ph, ce, pe, synth.CODEC_EOS)
+    pad = synth.text_rows(81, 1, key=1)[0]
+    for t in (a, b):
+        t.start(synth.prompt(81, 6), synth.text_rows(81, 2), pad)
+    codes = np.zeros(16, np.int32)
+    for f in range(3):
+        assert a.next_frame(codes)
+        more, gap = b.check_frame(codes)
+        assert more and np.all(gap == 0), gap
+        assert np.array_equal(a.logits(), b.logits())
+    # a planted mistake: the second-best code at choice 3 of the next frame
+    c = a.next_frame(codes)
+    plant = codes.copy()
+    assert c
+    # any other id than the first maximum of choice 3 has a positive gap
+    plant[3] = (codes[3] + 1) % synth.PRED_VOCAB
+    more, gap = b.check_frame(plant)
+    assert more and gap[3] > 0 and np.all(gap[:3] == 0)
+    for t in (a, b):
+        t.free()
+    for o in lms:
+        o.free()
+    for o in (ts, ps, th, ph):
+        o.free()
