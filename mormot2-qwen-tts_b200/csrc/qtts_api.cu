@@ -6,13 +6,16 @@
 //   qtts_heads  ~ TQwenLmHeads (lm.pas:64-100, 225-332)
 //   qtts_lm     ~ TQwenLm (lm.pas:102-143, 335-408)
 //   qtts_talker ~ the per-frame part of TQwenTalker (mormot.ai.tts.qwen.talker.pas:595-681)
-// Compute runs in the persistent kernel of qtts_decode.cuh; this file uploads
-// and packs weights (bit-exact ggml Q8_0 quantisation on the device), owns the
-// device memory and launches.
+//   qtts_batch / qtts_talkers ~ the same protocols for many utterances at once
+// Batch 1 runs in the persistent kernel of qtts_decode.cuh, batches on the
+// tcgen05 GEMM (qtts_gemm.cuh) and the kernels of qtts_batch.cuh; this file
+// uploads and packs weights (bit-exact ggml Q8_0 quantisation on the
+// device), owns the device memory, launches and captures the frame graphs.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -72,7 +75,8 @@ struct qtts_stack {
     qtts_device *dev;
     qtts_stack_config cfg;
     std::vector<void *> allocs;
-    std::vector<DLayer> hlayers;  // the same table, host side (batched path)
+    std::vector<DLayer> hlayers;  // the same table, host side
+    std::vector<DLayer> tlayers;  // the matrices tile-packed for the GEMM (built on first batched use)
     DLayer *d_layers;
     float *d_final_norm;
     int64_t bytes;
@@ -82,6 +86,7 @@ struct qtts_stack {
 struct HeadMat {
     uint8_t *d;
     int rows;
+    uint8_t *t;  // tile-packed for the GEMM (built on first use), or NULL
 };
 
 struct qtts_heads {
@@ -317,7 +322,7 @@ static uint32_t crc32c(uint32_t crc, const void *data, size_t n) {
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_cap, int box_rows) {
+static int encode_init() {
     if (!g_encode) {
         void *fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -325,6 +330,12 @@ static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_
         if (!fn || q != cudaDriverEntryPointSuccess) return set_err(QTTS_E_CUDA, "cuTensorMapEncodeTiled not found");
         g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
+    return QTTS_OK;
+}
+
+static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_cap, int box_rows) {
+    int rc0 = encode_init();
+    if (rc0) return rc0;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows_cap)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(G_BK), static_cast<cuuint32_t>(box_rows)};
@@ -337,13 +348,35 @@ static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_
 }
 
 template <int WDT, int BN>
+static int gemm_attr() {
+    CK(cudaFuncSetAttribute(gemm_kernel<WDT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(sizeof(GemmSmem<WDT, BN>) + 1024)));
+    return QTTS_OK;
+}
+
+// kernel attributes and the tensor-map encoder, once per device (before
+// any stream capture, where they could not be set)
+static int gemm_init(qtts_device *dev) {
+    static std::mutex mu;
+    static bool done[256] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev->ordinal >= 0 && dev->ordinal < 256 && done[dev->ordinal]) return QTTS_OK;
+    int rc;
+    if ((rc = gemm_attr<WDT_Q8, 64>()) || (rc = gemm_attr<WDT_Q8, 128>()) || (rc = gemm_attr<WDT_Q8, 256>()) ||
+        (rc = gemm_attr<WDT_F32, 64>()) || (rc = gemm_attr<WDT_F32, 128>()) || (rc = gemm_attr<WDT_F32, 256>()))
+        return rc;
+    CK(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(sizeof(DecodeSmem<float>))));
+    CK(cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(sizeof(DecodeSmem<__nv_bfloat16>))));
+    if ((rc = encode_init())) return rc;
+    if (dev->ordinal >= 0 && dev->ordinal < 256) done[dev->ordinal] = true;
+    return QTTS_OK;
+}
+
+template <int WDT, int BN>
 static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 grid, cudaStream_t st) {
-    static bool attr[2] = {false, false};
-    const size_t smem = sizeof(GemmSmem<BN>) + 1024;
-    if (!attr[WDT]) {
-        CK(cudaFuncSetAttribute(gemm_kernel<WDT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        attr[WDT] = true;
-    }
+    const size_t smem = sizeof(GemmSmem<WDT, BN>) + 1024;
     CUtensorMap map;
     int rc = tensor_map_f16(&map, x, a.K, rows_cap, BN);
     if (rc) return rc;
@@ -352,7 +385,7 @@ static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 
     return QTTS_OK;
 }
 
-// y[t][n] (+)= x[t][:] . w[n][:] for t < T (x: fp16 [rows_cap][K] on the
+// y[t][n] (+)= x[t][:] . w[n][:] for t < T (w tile-packed; x: fp16 [rows_cap][K] on the
 // device, rows_cap >= T).  With `add`, the products are added to y (residual);
 // otherwise y is overwritten (zeroed first when the K split needs atomics).
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
@@ -388,6 +421,21 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     if (bn == 64) return gemm_launch_t<WDT_F32, 64>(a, x, rows_cap, grid, st);
     if (bn == 128) return gemm_launch_t<WDT_F32, 128>(a, x, rows_cap, grid, st);
     return gemm_launch_t<WDT_F32, 256>(a, x, rows_cap, grid, st);
+}
+
+// the tile-packed copy of a row-packed matrix (freed by the caller)
+static int tile_pack(const uint8_t *src, int wdt, int n_rows, int k, uint8_t **out) {
+    *out = nullptr;
+    const size_t bytes = static_cast<size_t>((n_rows + G_BM - 1) / G_BM) * (k / G_BK) * g_chunk_bytes(wdt);
+    if (cudaMalloc(out, bytes) != cudaSuccess) return set_err(QTTS_E_OOM, "gemm tiles: out of device memory");
+    const long long n = static_cast<long long>((n_rows + G_BM - 1) / G_BM * G_BM) * (k / G_BK) * 8;
+    gemm_tile_pack_kernel<<<static_cast<unsigned>((n + 255) / 256), 256>>>(src, wdt, n_rows, k, *out);
+    if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(*out);
+        *out = nullptr;
+        return set_err(QTTS_E_CUDA, "gemm tiles: packing failed");
+    }
+    return QTTS_OK;
 }
 
 // ------------------------------------------------------------------ device
@@ -593,7 +641,7 @@ extern "C" int qtts_heads_add(qtts_heads *h, const void *src, int src_dtype, int
         cudaFree(d);
         return rc;
     }
-    h->mats.push_back({d, rows});
+    h->mats.push_back({d, rows, nullptr});
     // TQwenLmHeads.Bytes counts the stored bytes (ggml blocks: 34 per 32)
     h->bytes += static_cast<int64_t>(rows) * (h->dtype == QTTS_DTYPE_F32 ? h->hidden * 4 : h->hidden / 32 * 34);
     if (index) *index = static_cast<int>(h->mats.size()) - 1;
@@ -651,12 +699,46 @@ extern "C" int qtts_heads_bytes(qtts_heads *h, int64_t *bytes) {
     return QTTS_OK;
 }
 
+static int heads_tiles(qtts_heads *h) {
+    const int wdt = h->dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    for (HeadMat &m : h->mats) {
+        if (m.t) continue;
+        int rc = tile_pack(m.d, wdt, m.rows, h->hidden, &m.t);
+        if (rc) return rc;
+    }
+    return QTTS_OK;
+}
+
+static int stack_tiles(qtts_stack *s) {
+    if (!s->tlayers.empty()) return QTTS_OK;
+    const int wdt = s->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    std::vector<DLayer> tl(s->hlayers);
+    for (DLayer &d : tl) {
+        struct M {
+            const uint8_t **p;
+            int rows, k;
+        } ms[] = {{&d.wqkv, QKV_ROWS, H}, {&d.wo, H, QDIM}, {&d.wgu, GU_ROWS, H}, {&d.wd, H, INTER}};
+        for (const M &m : ms) {
+            uint8_t *t = nullptr;
+            int rc = tile_pack(*m.p, wdt, m.rows, m.k, &t);
+            if (rc) return rc;
+            s->allocs.push_back(t);
+            *m.p = t;
+        }
+    }
+    s->tlayers = tl;
+    return QTTS_OK;
+}
+
 extern "C" int qtts_heads_linear(qtts_heads *h, int index, const float *x, int rows, float *y) {
     if (!h || !x || !y) return set_err(QTTS_E_ARG, "qtts_heads_linear: NULL argument");
     if (index < 0 || index >= static_cast<int>(h->mats.size()))
         return set_err(QTTS_E_ARG, "qtts_heads_linear: no head %d in %s", index, h->name.c_str());
     if (rows <= 0) return QTTS_OK;
     CK(cudaSetDevice(h->dev->ordinal));
+    int rc = gemm_init(h->dev);
+    if (rc == QTTS_OK) rc = heads_tiles(h);
+    if (rc) return rc;
     const HeadMat &m = h->mats[index];
     const int k = h->hidden;
     cudaStream_t st = h->dev->load;
@@ -685,7 +767,7 @@ extern "C" int qtts_heads_linear(qtts_heads *h, int index, const float *x, int r
     to_half_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(h->lx, h->lh, n);
     CK(cudaGetLastError());
     const int wdt = h->dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
-    int rc = gemm(m.d, wdt, m.rows, k, h->lh, rows, static_cast<int>(h->lrows), h->ly, m.rows, false, h->lerr, st);
+    rc = gemm(m.t, wdt, m.rows, k, h->lh, rows, static_cast<int>(h->lrows), h->ly, m.rows, false, h->lerr, st);
     if (rc) return rc;
     int err = 0;
     CK(cudaMemcpyAsync(&err, h->lerr, 4, cudaMemcpyDeviceToHost, st));
@@ -698,7 +780,10 @@ extern "C" int qtts_heads_linear(qtts_heads *h, int index, const float *x, int r
 extern "C" int qtts_heads_destroy(qtts_heads *h) {
     if (!h) return QTTS_OK;
     cudaSetDevice(h->dev->ordinal);
-    for (HeadMat &m : h->mats) cudaFree(m.d);
+    for (HeadMat &m : h->mats) {
+        cudaFree(m.d);
+        if (m.t) cudaFree(m.t);
+    }
     if (h->lx) cudaFree(h->lx);
     if (h->ly) cudaFree(h->ly);
     if (h->lh) cudaFree(h->lh);
@@ -1384,6 +1469,10 @@ struct qtts_batch {
     cudaEvent_t mev[NSLOT] = {};
     bool mev_live[NSLOT] = {};
     int mslot = 0;
+    // fixed pinned slots, one per call of a frame graph (read by its copies)
+    static constexpr int NFIXED = 16;
+    int *hfixed[NFIXED] = {};
+    size_t max_parts = 0;  // attention partials the part buffer holds
 };
 
 static void batch_free(qtts_batch *b) {
@@ -1391,6 +1480,8 @@ static void batch_free(qtts_batch *b) {
         if (b->mev[k]) cudaEventDestroy(b->mev[k]);
         if (b->hmeta[k]) cudaFreeHost(b->hmeta[k]);
     }
+    for (int k = 0; k < qtts_batch::NFIXED; ++k)
+        if (b->hfixed[k]) cudaFreeHost(b->hfixed[k]);
     for (void *p : b->allocs) cudaFree(p);
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
@@ -1409,6 +1500,10 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         return set_err(QTTS_E_ARG, "qtts_batch_create: heads and stack do not match");
     qtts_device *dev = stack->dev;
     CK(cudaSetDevice(dev->ordinal));
+    int rc0 = gemm_init(dev);
+    if (rc0 == QTTS_OK) rc0 = stack_tiles(stack);
+    if (rc0 == QTTS_OK) rc0 = heads_tiles(heads);
+    if (rc0) return rc0;
     qtts_batch *b = new qtts_batch();
     b->dev = dev;
     b->stack = stack;
@@ -1427,7 +1522,9 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
     const int L = stack->cfg.layers;
     const size_t kvb = kv_dtype == QTTS_DTYPE_F32 ? 4 : 2;
     const size_t T = max_tokens;
-    const int max_items = max_tokens * HKV + max_seqs * HKV * 64;
+    const int max_splits = std::max((max_pos + DSPLIT - 1) / DSPLIT, DMAX_SPLITS);
+    const int max_items = max_tokens * HKV + max_seqs * HKV * max_splits;
+    b->max_parts = static_cast<size_t>(max_seqs) * HKV * max_splits;
     b->meta_bytes = (T * 2 + static_cast<size_t>(max_items) * (sizeof(AttnItem) / 4) + max_seqs * (HKV * 2 + 2)) * 4;
     struct A {
         void **p;
@@ -1441,7 +1538,7 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         {reinterpret_cast<void **>(&b->qkv), T * QKV_ROWS * 4},
         {reinterpret_cast<void **>(&b->q32), T * QDIM * 4},
         {reinterpret_cast<void **>(&b->gu), T * GU_ROWS * 4},
-        {reinterpret_cast<void **>(&b->part), static_cast<size_t>(max_seqs) * HKV * 64 * AQB * 2 * PSTRIDE * 4},
+        {reinterpret_cast<void **>(&b->part), static_cast<size_t>(max_seqs) * HKV * max_splits * 2 * PSTRIDE * 4},
         {reinterpret_cast<void **>(&b->hidden), static_cast<size_t>(max_seqs) * H * 4},
         {reinterpret_cast<void **>(&b->logits), static_cast<size_t>(max_seqs) * (b->head_rows > 0 ? b->head_rows : 1) * 4},
         {reinterpret_cast<void **>(&b->h16), T * H * 2},
@@ -1497,9 +1594,9 @@ extern "C" int qtts_batch_length(qtts_batch *b, int seq, int *length) {
 }
 
 template <class KVT>
-static void batch_layers(qtts_batch *b, int T, int nitems, const int *tok_seq, const int *tok_pos,
-                         const AttnItem *items, int ncomb, const int *cfirst, const int *ccount, const int *ctok,
-                         int wdt, cudaStream_t st, int &rc) {
+static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pitems, int nditems,
+                         const AttnItem *ditems, const int *tok_seq, const int *tok_pos, int ncomb, const int *cfirst,
+                         const int *ccount, const int *ctok, int wdt, cudaStream_t st, int &rc) {
     const qtts_stack *s = b->stack;
     KVPool<KVT> pool;
     pool.base = static_cast<KVT *>(b->pool);
@@ -1509,12 +1606,15 @@ static void batch_layers(qtts_batch *b, int T, int nitems, const int *tok_seq, c
     const float eps = s->cfg.rms_eps;
     const int cap = b->max_tokens;
     for (int l = 0; l < s->cfg.layers && rc == QTTS_OK; ++l) {
-        const DLayer &Ly = s->hlayers[l];
+        const DLayer &Ly = s->tlayers[l];
         rmsnorm_f16_kernel<<<(T + 7) / 8, 256, 0, st>>>(b->x, nullptr, T, Ly.in_norm, eps, b->h16, nullptr);
         if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st))) return;
         qkv_post_kernel<KVT><<<dim3(T, 4), 256, 0, st>>>(b->qkv, tok_seq, tok_pos, Ly.q_norm, Ly.k_norm, eps,
                                                          b->rope_cos, b->rope_sin, b->q32, pool, l);
-        attn_kernel<KVT><<<nitems, ATHREADS, 0, st>>>(items, b->q32, pool, l, b->attn16, b->part);
+        if (npitems > 0) attn_kernel<KVT><<<npitems, ATHREADS, 0, st>>>(pitems, b->q32, pool, l, b->attn16);
+        if (nditems > 0)
+            attn_decode_kernel<KVT><<<nditems, DTHREADS, sizeof(DecodeSmem<KVT>), st>>>(ditems, b->q32, pool, l,
+                                                                                        b->attn16, b->part, b->err);
         if (ncomb > 0)
             attn_combine_kernel<<<(ncomb * HQ + 7) / 8, 256, 0, st>>>(cfirst, ccount, ctok, ncomb, b->part, b->attn16);
         if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
@@ -1527,16 +1627,26 @@ static void batch_layers(qtts_batch *b, int T, int nitems, const int *tok_seq, c
     }
 }
 
-// One batched forward, queued on stream st without waiting: x is a host
-// (x_dev false) or device pointer; the logits of head `head` (< 0: none)
-// and the normed last rows stay in b->logits / b->hidden, in call order.
-// Device waits that give up set b->err (read by the caller).
-static int batch_run(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x, bool x_dev,
-                     int head, cudaStream_t st) {
-    if (!b || nseq <= 0 || !seqs || !rows || !x) return set_err(QTTS_E_ARG, "qtts_batch_forward: bad argument");
+// The host half of one batched forward: validation, KV pages, the token
+// metadata and attention items, staged in pinned memory (a slot of the ring,
+// or the fixed slot `fixed` of the frame graphs); b->len advances.  Decode
+// rows (one new row of a sequence) get `dsplits` page-aligned context splits
+// each (0: one split per DSPLIT keys).
+struct BatchPlan {
+    int nseq, T, np, nd, ncomb, ring;  // ring: slot of the ring, -1 = fixed slot
+    size_t meta_ints, o_ditems, o_cf, o_cc, o_ct, o_last;
+    const int *hm;                     // pinned: meta | page table
+    bool same_shape(const BatchPlan &o) const {
+        return nseq == o.nseq && T == o.T && np == o.np && nd == o.nd && ncomb == o.ncomb &&
+               meta_ints == o.meta_ints && hm == o.hm;
+    }
+};
+
+static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, int dsplits, int fixed,
+                      BatchPlan *P) {
+    if (!b || nseq <= 0 || !seqs || !rows) return set_err(QTTS_E_ARG, "qtts_batch_forward: bad argument");
     if (nseq > b->max_seqs) return set_err(QTTS_E_ARG, "qtts_batch_forward: %d sequences, at most %d", nseq, b->max_seqs);
-    if (head >= static_cast<int>(b->heads->mats.size()))
-        return set_err(QTTS_E_ARG, "qtts_batch_forward: no head %d", head);
+    if (dsplits < 0 || dsplits > DMAX_SPLITS) return set_err(QTTS_E_ARG, "qtts_batch_forward: %d splits", dsplits);
     // validate, count tokens, allocate pages
     int T = 0;
     std::vector<char> seen(b->max_seqs, 0);
@@ -1565,7 +1675,7 @@ static int batch_run(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t
     }
     // metadata: tokens, attention items, combine lists
     std::vector<int> tok_seq(T), tok_pos(T), last(nseq);
-    std::vector<AttnItem> items;
+    std::vector<AttnItem> pitems, ditems;
     std::vector<int> cfirst, ccount, ctok;
     int t = 0, nparts = 0;
     for (int i = 0; i < nseq; ++i) {
@@ -1576,79 +1686,134 @@ static int batch_run(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t
         }
         last[i] = t + n - 1;
         if (n == 1) {
-            // one query: the context in splits of 64 keys, combined afterwards
+            // one query: page-aligned splits of the context, combined
+            // afterwards when there are several (a split may be empty)
             const int ctx = L0 + 1;
-            const int S = (ctx + 63) / 64 < 64 ? (ctx + 63) / 64 : 64;
-            const int C = (ctx + S - 1) / S;
+            const int S = dsplits > 0 ? dsplits : (ctx + DSPLIT - 1) / DSPLIT;
             for (int h = 0; h < HKV; ++h) {
-                cfirst.push_back(nparts);
-                ccount.push_back(S);
-                for (int sp = 0; sp < S; ++sp)
-                    items.push_back({t, L0, 0, 1, h, sp * C, (sp + 1) * C < ctx ? (sp + 1) * C : ctx, sq, nparts++});
+                if (S > 1) {
+                    cfirst.push_back(nparts);
+                    ccount.push_back(S);
+                }
+                for (int sp = 0; sp < S; ++sp) {
+                    int ka, kb;
+                    if (dsplits > 0) {
+                        ka = static_cast<int>(static_cast<long long>(ctx) * sp / S) / PAGE * PAGE;
+                        kb = sp == S - 1 ? ctx : static_cast<int>(static_cast<long long>(ctx) * (sp + 1) / S) / PAGE * PAGE;
+                    } else {
+                        ka = sp * DSPLIT;
+                        kb = (sp + 1) * DSPLIT < ctx ? (sp + 1) * DSPLIT : ctx;
+                    }
+                    ditems.push_back({t, L0, 0, 1, h, ka, kb, sq, S > 1 ? nparts++ : -1});
+                }
             }
-            ctok.push_back(t);
+            if (S > 1) ctok.push_back(t);
         } else {
             for (int qa = 0; qa < n; qa += AQB)
                 for (int h = 0; h < HKV; ++h)
-                    items.push_back({t, L0, qa, qa + AQB < n ? qa + AQB : n, h, 0, L0 + n, sq, -1});
+                    pitems.push_back({t, L0, qa, qa + AQB < n ? qa + AQB : n, h, 0, L0 + n, sq, -1});
         }
         t += n;
     }
-    const int ncomb = static_cast<int>(ctok.size());
-    // one upload: tok_seq | tok_pos | items | cfirst | ccount | ctok | last
+    if (static_cast<size_t>(nparts) > b->max_parts)
+        return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: too many attention splits");
+    // tok_seq | tok_pos | prefill items | decode items | cfirst | ccount | ctok | last
     std::vector<int> meta;
     meta.insert(meta.end(), tok_seq.begin(), tok_seq.end());
     meta.insert(meta.end(), tok_pos.begin(), tok_pos.end());
-    const size_t o_items = meta.size();
-    const int* ip = reinterpret_cast<const int *>(items.data());
-    meta.insert(meta.end(), ip, ip + items.size() * (sizeof(AttnItem) / 4));
-    const size_t o_cf = meta.size();
+    const int *ip = reinterpret_cast<const int *>(pitems.data());
+    meta.insert(meta.end(), ip, ip + pitems.size() * (sizeof(AttnItem) / 4));
+    P->o_ditems = meta.size();
+    ip = reinterpret_cast<const int *>(ditems.data());
+    meta.insert(meta.end(), ip, ip + ditems.size() * (sizeof(AttnItem) / 4));
+    P->o_cf = meta.size();
     meta.insert(meta.end(), cfirst.begin(), cfirst.end());
-    const size_t o_cc = meta.size();
+    P->o_cc = meta.size();
     meta.insert(meta.end(), ccount.begin(), ccount.end());
-    const size_t o_ct = meta.size();
+    P->o_ct = meta.size();
     meta.insert(meta.end(), ctok.begin(), ctok.end());
-    const size_t o_last = meta.size();
+    P->o_last = meta.size();
     meta.insert(meta.end(), last.begin(), last.end());
     if (meta.size() * 4 > b->meta_bytes) return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: too many attention items");
-    CK(cudaSetDevice(b->dev->ordinal));
-    // stage metadata + page table in the next pinned slot (wait for the
-    // copy that last used it), then two copies to the device
-    const int k = b->mslot;
-    b->mslot = (k + 1) % qtts_batch::NSLOT;
-    if (b->mev_live[k]) CK(cudaEventSynchronize(b->mev[k]));
-    int *hm = b->hmeta[k];
+    int *hm;
+    if (fixed >= 0) {
+        if (fixed >= qtts_batch::NFIXED) return set_err(QTTS_E_ARG, "qtts_batch_forward: fixed slot %d", fixed);
+        if (!b->hfixed[fixed] && cudaHostAlloc(reinterpret_cast<void **>(&b->hfixed[fixed]),
+                                               b->meta_bytes + b->h_pages.size() * 4, cudaHostAllocDefault) != cudaSuccess) {
+            b->hfixed[fixed] = nullptr;
+            return set_err(QTTS_E_OOM, "qtts_batch_forward: out of pinned host memory");
+        }
+        hm = b->hfixed[fixed];
+        P->ring = -1;
+    } else {
+        // the next ring slot, once the copy that last used it has run
+        const int k = b->mslot;
+        b->mslot = (k + 1) % qtts_batch::NSLOT;
+        if (b->mev_live[k]) CK(cudaEventSynchronize(b->mev[k]));
+        hm = b->hmeta[k];
+        P->ring = k;
+    }
     std::memcpy(hm, meta.data(), meta.size() * 4);
-    const size_t pg_off = b->meta_bytes / 4;
-    std::memcpy(hm + pg_off, b->h_pages.data(), b->h_pages.size() * 4);
-    CK(cudaMemcpyAsync(b->meta, hm, meta.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(b->d_pages, hm + pg_off, b->h_pages.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaEventRecord(b->mev[k], st));
-    b->mev_live[k] = true;
-    CK(cudaMemcpyAsync(b->x, x, static_cast<size_t>(T) * H * 4, x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                       st));
+    std::memcpy(hm + b->meta_bytes / 4, b->h_pages.data(), b->h_pages.size() * 4);
+    P->hm = hm;
+    P->nseq = nseq;
+    P->T = T;
+    P->np = static_cast<int>(pitems.size());
+    P->nd = static_cast<int>(ditems.size());
+    P->ncomb = static_cast<int>(ctok.size());
+    P->meta_ints = meta.size();
+    for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
+    return QTTS_OK;
+}
+
+// The device half: the metadata and page table to the device, the input
+// rows (host or device pointer), the layers, the final norm of the last row
+// of each sequence and the head `head` (< 0: none); logits and normed rows
+// stay in b->logits / b->hidden in call order.  Nothing waits: device waits
+// that give up set b->err (read by the caller).
+static int batch_enqueue(qtts_batch *b, const BatchPlan &P, const float *x, bool x_dev, int head, cudaStream_t st) {
+    if (!x) return set_err(QTTS_E_ARG, "qtts_batch_forward: NULL rows");
+    if (head >= static_cast<int>(b->heads->mats.size()))
+        return set_err(QTTS_E_ARG, "qtts_batch_forward: no head %d", head);
+    CK(cudaSetDevice(b->dev->ordinal));
+    CK(cudaMemcpyAsync(b->meta, P.hm, P.meta_ints * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->d_pages, P.hm + b->meta_bytes / 4, b->h_pages.size() * 4, cudaMemcpyHostToDevice, st));
+    if (P.ring >= 0) {
+        CK(cudaEventRecord(b->mev[P.ring], st));
+        b->mev_live[P.ring] = true;
+    }
+    CK(cudaMemcpyAsync(b->x, x, static_cast<size_t>(P.T) * H * 4,
+                       x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
     const int wdt = b->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
     int rc = QTTS_OK;
     const int *m = b->meta;
-    const AttnItem *d_items = reinterpret_cast<const AttnItem *>(m + o_items);
+    const AttnItem *d_pitems = reinterpret_cast<const AttnItem *>(m + 2 * P.T);
+    const AttnItem *d_ditems = reinterpret_cast<const AttnItem *>(m + P.o_ditems);
     if (b->kv_dtype == QTTS_DTYPE_F32)
-        batch_layers<float>(b, T, static_cast<int>(items.size()), m, m + T, d_items, ncomb, m + o_cf, m + o_cc, m + o_ct,
-                            wdt, st, rc);
+        batch_layers<float>(b, P.T, P.np, d_pitems, P.nd, d_ditems, m, m + P.T, P.ncomb, m + P.o_cf, m + P.o_cc,
+                            m + P.o_ct, wdt, st, rc);
     else
-        batch_layers<__nv_bfloat16>(b, T, static_cast<int>(items.size()), m, m + T, d_items, ncomb, m + o_cf, m + o_cc,
-                                    m + o_ct, wdt, st, rc);
+        batch_layers<__nv_bfloat16>(b, P.T, P.np, d_pitems, P.nd, d_ditems, m, m + P.T, P.ncomb, m + P.o_cf,
+                                    m + P.o_cc, m + P.o_ct, wdt, st, rc);
     if (rc) return rc;
-    // the last row of every sequence: final norm, head
-    rmsnorm_f16_kernel<<<(nseq + 7) / 8, 256, 0, st>>>(b->x, m + o_last, nseq, b->stack->d_final_norm,
-                                                       b->stack->cfg.rms_eps, b->hlast16, b->hidden);
+    rmsnorm_f16_kernel<<<(P.nseq + 7) / 8, 256, 0, st>>>(b->x, m + P.o_last, P.nseq, b->stack->d_final_norm,
+                                                         b->stack->cfg.rms_eps, b->hlast16, b->hidden);
     CK(cudaGetLastError());
     if (head >= 0) {
         const HeadMat &hm = b->heads->mats[head];
-        if ((rc = gemm(hm.d, wdt, hm.rows, H, b->hlast16, nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st)))
+        if ((rc = gemm(hm.t, wdt, hm.rows, H, b->hlast16, P.nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st)))
             return rc;
     }
-    for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
     return QTTS_OK;
+}
+
+// plan + enqueue (the ring of pinned slots, splits by DSPLIT)
+static int batch_run(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x, bool x_dev,
+                     int head, cudaStream_t st) {
+    BatchPlan P;
+    int rc = batch_plan(b, nseq, seqs, rows, 0, -1, &P);
+    if (rc) return rc;
+    return batch_enqueue(b, P, x, x_dev, head, st);
 }
 
 extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, const int32_t *rows, const float *x,
@@ -1661,7 +1826,10 @@ extern "C" int qtts_batch_forward(qtts_batch *b, int nseq, const int32_t *seqs, 
     CK(cudaMemsetAsync(b->err, 0, 16, st));
     std::vector<int> saved(b->len);
     int rc = batch_run(b, nseq, seqs, rows, x, false, logits ? head : -1, st);
-    if (rc) return rc;
+    if (rc) {
+        b->len = saved;
+        return rc;
+    }
     int err = 0;
     const int hr = logits ? b->heads->mats[head].rows : 0;
     CK(cudaMemcpyAsync(&err, b->err, 4, cudaMemcpyDeviceToHost, st));
@@ -1703,9 +1871,16 @@ struct qtts_talkers {
     int *h_io;  // pinned: seqs | aux | codes | done | errs
     std::vector<char> started, done;
     std::vector<void *> allocs;
+    // the frame as one CUDA graph, for one list of active utterances; its
+    // calls read their metadata from fixed pinned slots rewritten each frame
+    cudaGraphExec_t graph = nullptr;
+    std::vector<int> graph_seqs;
+    BatchPlan graph_plans[MAX_GROUPS];
+    int frames_eager = 0, frames_graph = 0, captures = 0;
 };
 
 static void talkers_free(qtts_talkers *t) {
+    if (t->graph) cudaGraphExecDestroy(t->graph);
     for (float *p : t->trail)
         if (p) cudaFree(p);
     for (void *p : t->allocs) cudaFree(p);
@@ -1869,6 +2044,44 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
     return QTTS_OK;
 }
 
+// context splits per sequence of the batched talker step: about 4 CTAs per
+// SM over all (utterance, kv head) pairs, 2 to DMAX_SPLITS
+static int talker_splits(const qtts_talkers *t, int n) {
+    const int want = (4 * t->tb->dev->sms + n * HKV - 1) / (n * HKV);
+    return want < 2 ? 2 : (want > DMAX_SPLITS ? DMAX_SPLITS : want);
+}
+
+// the device work of one frame of n utterances (plans[0..G-2]: predictor
+// steps, plans[G-1]: talker step), queued on st (or captured)
+static int frame_enqueue(qtts_talkers *t, int n, const BatchPlan *plans, cudaStream_t st) {
+    const int G = t->cfg.groups, pv = t->cfg.pred_vocab;
+    int rc;
+    CK(cudaMemcpyAsync(t->d_seqs, io_seqs(t), n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(t->tb->err, 0, 16, st));
+    CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
+    frames_begin_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->seen, t->cfg.vocab, t->hid, t->codec_emb, t->px,
+                                           t->d_codes, G);
+    CK(cudaGetLastError());
+    for (int g = 0; g < G - 1; ++g) {
+        if ((rc = batch_enqueue(t->pb, plans[g], t->px, true, g, st))) return rc;
+        frames_pred_argmax_kernel<<<n, 256, 0, st>>>(t->pb->logits, pv, g, G, t->pred_emb, t->px, t->d_codes);
+        CK(cudaGetLastError());
+    }
+    frames_talker_in_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->d_codes, G, t->codec_emb, t->pred_emb, pv,
+                                               t->d_trail, t->tts_pad, t->xt);
+    CK(cudaGetLastError());
+    if ((rc = batch_enqueue(t->tb, plans[G - 1], t->xt, true, 0, st))) return rc;
+    frames_choose0_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
+                                             t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
+                                             t->d_done, 0);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(io_codes(t), t->d_codes, static_cast<size_t>(n) * G * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(io_done(t), t->d_done, n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(io_errs(t), t->tb->err, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(io_errs(t) + 1, t->pb->err, 4, cudaMemcpyDeviceToHost, st));
+    return QTTS_OK;
+}
+
 extern "C" int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t *seqs, int32_t *codes,
                                        int32_t *more) {
     if (!t || !codes || !more) return set_err(QTTS_E_ARG, "qtts_talkers_next_frame: NULL argument");
@@ -1891,36 +2104,50 @@ extern "C" int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t 
     if (n == 0) return QTTS_OK;
     CK(cudaSetDevice(t->tb->dev->ordinal));
     cudaStream_t st = t->stream;
-    std::memcpy(io_seqs(t), act.data(), n * 4);
-    CK(cudaMemcpyAsync(t->d_seqs, io_seqs(t), n * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemsetAsync(t->tb->err, 0, 16, st));
-    CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
-    frames_begin_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->seen, t->cfg.vocab, t->hid, t->codec_emb, t->px,
-                                           t->d_codes, G);
-    CK(cudaGetLastError());
-    // predictor: Reset, [state, codec_emb[code 0]] with head 0, then one row
-    // per group with head g (talker.pas:656-675)
+    // host half of every call of the frame: predictor Reset, [state,
+    // codec_emb[code 0]] with head 0, then one row per group with head g
+    // (talker.pas:656-675); the talker step
+    const std::vector<int> tlen(t->tb->len);
+    BatchPlan plans[MAX_GROUPS];
     for (int s : act) qtts_batch_reset(t->pb, s);
     std::vector<int> rows(n, 2);
-    const int pv = t->cfg.pred_vocab;
-    for (int g = 0; g < G - 1; ++g) {
-        if ((rc = batch_run(t->pb, n, act.data(), rows.data(), t->px, true, g, st))) return rc;
-        frames_pred_argmax_kernel<<<n, 256, 0, st>>>(t->pb->logits, pv, g, G, t->pred_emb, t->px, t->d_codes);
-        CK(cudaGetLastError());
+    for (int g = 0; g < G - 1 && rc == QTTS_OK; ++g) {
+        rc = batch_plan(t->pb, n, act.data(), rows.data(), 1, g, &plans[g]);
         if (g == 0) rows.assign(n, 1);
     }
-    // talker step, then ChooseCode0 of the next frame
-    frames_talker_in_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->d_codes, G, t->codec_emb, t->pred_emb, pv,
-                                               t->d_trail, t->tts_pad, t->xt);
-    CK(cudaGetLastError());
-    if ((rc = batch_run(t->tb, n, act.data(), rows.data(), t->xt, true, 0, st))) return rc;
-    frames_choose0_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
-                                             t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
-                                             t->d_done, 0);
-    CK(cudaGetLastError());
-    CK(cudaMemcpyAsync(io_codes(t), t->d_codes, static_cast<size_t>(n) * G * 4, cudaMemcpyDeviceToHost, st));
-    CK(cudaMemcpyAsync(io_done(t), t->d_done, n * 4, cudaMemcpyDeviceToHost, st));
-    if ((rc = talkers_finish(t, "qtts_talkers_next_frame"))) return rc;
+    if (rc == QTTS_OK) rc = batch_plan(t->tb, n, act.data(), rows.data(), talker_splits(t, n), 0, &plans[G - 1]);
+    if (rc) {
+        t->tb->len = tlen;
+        return rc;
+    }
+    std::memcpy(io_seqs(t), act.data(), n * 4);
+    bool reuse = t->graph && t->graph_seqs == act;
+    for (int g = 0; g < G && reuse; ++g) reuse = plans[g].same_shape(t->graph_plans[g]);
+    if (!reuse) {
+        if (t->graph) CK(cudaGraphExecDestroy(t->graph));
+        t->graph = nullptr;
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = frame_enqueue(t, n, plans, st);
+        const cudaError_t ce = cudaStreamEndCapture(st, &g);
+        if (rc == QTTS_OK && ce != cudaSuccess) rc = set_err(QTTS_E_CUDA, "frame graph capture: %s", cudaGetErrorString(ce));
+        if (rc == QTTS_OK && cudaGraphInstantiate(&t->graph, g, 0) != cudaSuccess) {
+            t->graph = nullptr;
+            rc = set_err(QTTS_E_CUDA, "frame graph: instantiation failed");
+        }
+        if (g) cudaGraphDestroy(g);
+        if (rc) {
+            t->tb->len = tlen;
+            return rc;
+        }
+        t->graph_seqs = act;
+        for (int k = 0; k < G; ++k) t->graph_plans[k] = plans[k];
+        ++t->captures;
+    }
+    CK(cudaGraphLaunch(t->graph, st));
+    CK(cudaStreamSynchronize(st));
+    ++t->frames_graph;
+    if (io_errs(t)[0] || io_errs(t)[1]) return set_err(QTTS_E_TIMEOUT, "qtts_talkers_next_frame: a device wait gave up");
     for (int j = 0; j < n; ++j) {
         std::memcpy(codes + static_cast<size_t>(slot[j]) * G, io_codes(t) + static_cast<size_t>(j) * G, G * 4);
         more[slot[j]] = 1;

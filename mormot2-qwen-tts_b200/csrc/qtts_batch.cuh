@@ -123,13 +123,14 @@ struct AttnItem {
     int t0, L0, qa, qb, h, ka, kb, seq, part;  // part < 0: write the normalised output
 };
 
-// Causal GQA attention of one item; query heads 2h and 2h+1 share kv head h.
+// Causal GQA attention of one prefill item (several new rows of a
+// sequence, all of its keys); query heads 2h and 2h+1 share kv head h.
 // Warps are spread over the (row, q head) combos and, when there are fewer
 // combos than warps, over the keys of each tile; their online-softmax
 // states are merged in shared memory.
 template <class KVT>
 __global__ void __launch_bounds__(ATHREADS) attn_kernel(const AttnItem *items, const float *q32, KVPool<KVT> pool,
-                                                        int layer, __half *attn16, float *part) {
+                                                        int layer, __half *attn16) {
     __shared__ __align__(16) float qs[AQB][2][HD];
     __shared__ __align__(16) float ks[AKT][HD];
     __shared__ __align__(16) float vs[AKT][HD];
@@ -230,18 +231,151 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(const AttnItem *items, c
         }
         if (!writer) continue;
         const int j = combo >> 1, q = combo & 1;
-        if (it.part < 0) {
-            const float inv = 1.0f / L;
-            __half *dst = attn16 + static_cast<size_t>(it.t0 + it.qa + j) * QDIM + (2 * it.h + q) * HD + 4 * lane;
-            *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
-            *reinterpret_cast<__half2 *>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
-        } else {
-            float *pp = part + (static_cast<size_t>(it.part) * AQB * 2 + j * 2 + q) * PSTRIDE;
-            store4(pp + 4 * lane, acc);
-            if (lane == 0) {
-                pp[HD] = M;
-                pp[HD + 1] = L;
+        const float inv = 1.0f / L;
+        __half *dst = attn16 + static_cast<size_t>(it.t0 + it.qa + j) * QDIM + (2 * it.h + q) * HD + 4 * lane;
+        *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
+        *reinterpret_cast<__half2 *>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
+    }
+}
+
+// ------------------------------------------------------------------ decode attention
+//
+// One new row per sequence (the decode steps of the talker and the
+// predictor): split-K over the context.  One CTA per (sequence, kv head,
+// split); the split's keys [ka, kb) (ka page-aligned) are visited in tiles of
+// DSPLIT keys (4 pages), double-buffered: the K and V pages of a tile come in
+// by bulk copies (16 positions x 128 of one head are contiguous in a page)
+// while the previous tile is used.  Per tile, 128 threads score the 2 query
+// heads x 64 keys, a shuffle softmax per head updates the running (m, l), and
+// thread (head, dim pair) accumulates the output.  A single split writes the
+// normalised row, several write (m, l, o) partials for attn_combine_kernel.
+constexpr int DSPLIT = 64;
+constexpr int DTHREADS = 128;
+constexpr int DMAX_SPLITS = 16;  // fixed split count per sequence at most
+
+template <class KVT>
+struct DecodeSmem {
+    KVT ks[2][DSPLIT][HD];
+    KVT vs[2][DSPLIT][HD];
+    float qs[2][HD];
+    float p[2][DSPLIT];
+    float red[4][2];
+    uint64_t bar[2];
+    int ok;
+};
+
+__device__ __forceinline__ float2 load2(const float *s) { return *reinterpret_cast<const float2 *>(s); }
+__device__ __forceinline__ float2 load2(const __nv_bfloat16 *s) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(s));
+}
+
+template <class KVT>
+__device__ __forceinline__ void decode_issue(DecodeSmem<KVT> *sm, const KVPool<KVT> &pool, int layer, int seq,
+                                             int head, int k0, int nk, int buf) {
+    constexpr uint32_t PAGE_BYTES = PAGE * HD * sizeof(KVT);
+    const int npg = (nk + PAGE - 1) / PAGE;
+    mbar_arrive_tx(&sm->bar[buf], 2 * npg * PAGE_BYTES);
+    for (int i = 0; i < npg; ++i) {
+        const int pos = k0 + i * PAGE;
+        bulk_g2s(&sm->ks[buf][i * PAGE][0], kv_at(pool, layer, seq, pos, 0, head), PAGE_BYTES, &sm->bar[buf]);
+        bulk_g2s(&sm->vs[buf][i * PAGE][0], kv_at(pool, layer, seq, pos, 1, head), PAGE_BYTES, &sm->bar[buf]);
+    }
+}
+
+template <class KVT>
+__global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *items, const float *q32,
+                                                              KVPool<KVT> pool, int layer, __half *attn16,
+                                                              float *part, int *err) {
+    extern __shared__ __align__(128) uint8_t dsm_raw[];
+    DecodeSmem<KVT> *sm = reinterpret_cast<DecodeSmem<KVT> *>(dsm_raw);
+    const AttnItem it = items[blockIdx.x];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = tid >> 6, j = tid & 63;  // scores: (head, key); output: (head, dim pair j)
+    const int nkeys = it.kb > it.ka ? it.kb - it.ka : 0;
+    const int ntiles = (nkeys + DSPLIT - 1) / DSPLIT;
+    if (tid == 0) {
+        mbar_init(&sm->bar[0], 1);
+        mbar_init(&sm->bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (ntiles > 0) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys), 0);
+    }
+    for (int i = tid; i < 2 * HD / 4; i += DTHREADS) {
+        const int hq = i / (HD / 4), d4 = i - hq * (HD / 4);
+        store4(&sm->qs[hq][4 * d4], load4(q32 + static_cast<size_t>(it.t0) * QDIM + (2 * it.h + hq) * HD + 4 * d4));
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+    float m_run = -INFINITY, l_run = 0.f, ox = 0.f, oy = 0.f;
+    int waited = 0;  // tiles whose copies are known to have landed (thread 0)
+    for (int t = 0; t < ntiles; ++t) {
+        const int buf = t & 1;
+        const int k0 = it.ka + t * DSPLIT, nk = min(DSPLIT, it.kb - k0);
+        if (tid == 0) {
+            if (t + 1 < ntiles)
+                decode_issue(sm, pool, layer, it.seq, it.h, k0 + DSPLIT, min(DSPLIT, it.kb - k0 - DSPLIT), buf ^ 1);
+            const bool got = mbar_wait(&sm->bar[buf], (t >> 1) & 1, nullptr);
+            waited = got ? t + 1 : waited;
+            sm->ok = got ? 1 : 0;
+        }
+        __syncthreads();  // (A) tile t landed (or not: uniform decision)
+        if (!sm->ok) break;
+        float sc = -INFINITY;
+        if (j < nk) {
+            // the dims from pair j on: the 32 keys of a warp hit 32 banks
+            float a = 0.f;
+#pragma unroll 8
+            for (int e = 0; e < HD / 2; ++e) {
+                const int pr = (e + j) & (HD / 2 - 1);
+                const float2 kv2 = load2(&sm->ks[buf][j][2 * pr]);
+                const float2 qv2 = *reinterpret_cast<const float2 *>(&sm->qs[q][2 * pr]);
+                a = fmaf(qv2.x, kv2.x, a);
+                a = fmaf(qv2.y, kv2.y, a);
             }
+            sc = a * scale;
+        }
+        float mt = sc;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+        if (lane == 0) sm->red[warp][0] = mt;
+        __syncthreads();  // (B)
+        const float m_new = fmaxf(m_run, fmaxf(sm->red[2 * q][0], sm->red[2 * q + 1][0]));
+        const float e = j < nk ? expf(sc - m_new) : 0.f;
+        float lt = e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
+        if (lane == 0) sm->red[warp][1] = lt;
+        sm->p[q][j] = e;
+        __syncthreads();  // (C)
+        const float corr = expf(m_run - m_new);  // 0 on the first tile
+        l_run = fmaf(l_run, corr, sm->red[2 * q][1] + sm->red[2 * q + 1][1]);
+        ox *= corr;
+        oy *= corr;
+        for (int k = 0; k < nk; ++k) {
+            const float pk = sm->p[q][k];
+            const float2 v2 = load2(&sm->vs[buf][k][2 * j]);
+            ox = fmaf(pk, v2.x, ox);
+            oy = fmaf(pk, v2.y, oy);
+        }
+        m_run = m_new;
+        __syncthreads();  // (D) buffer, p and red free for the next tiles
+    }
+    if (tid == 0 && waited < ntiles) {
+        // a wait gave up: report it, then wait (bounded) for every copy
+        // issued so that none lands after the CTA has exited
+        atomicCAS(err, 0, ERR_TIMEOUT);
+        const int issued = min(ntiles, waited + 2);
+        for (int t = waited; t < issued; ++t) mbar_wait(&sm->bar[t & 1], (t >> 1) & 1, nullptr);
+    }
+    if (it.part < 0) {
+        const float inv = 1.0f / l_run;
+        *reinterpret_cast<__half2 *>(attn16 + static_cast<size_t>(it.t0) * QDIM + (2 * it.h + q) * HD + 2 * j) =
+            __floats2half2_rn(ox * inv, oy * inv);
+    } else {
+        float *pp = part + (static_cast<size_t>(it.part) * 2 + q) * PSTRIDE;
+        *reinterpret_cast<float2 *>(pp + 2 * j) = make_float2(ox, oy);
+        if (j == 0) {
+            pp[HD] = m_run;
+            pp[HD + 1] = l_run;
         }
     }
 }
@@ -256,11 +390,11 @@ __global__ void attn_combine_kernel(const int *first, const int *count, const in
     const int f = first[call * HKV + h], n = count[call * HKV + h];
     if (n <= 0) return;
     float M = -INFINITY;
-    for (int s = 0; s < n; ++s) M = fmaxf(M, part[(static_cast<size_t>(f + s) * AQB * 2 + q) * PSTRIDE + HD]);
+    for (int s = 0; s < n; ++s) M = fmaxf(M, part[(static_cast<size_t>(f + s) * 2 + q) * PSTRIDE + HD]);
     float L = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < n; ++s) {
-        const float *pp = part + (static_cast<size_t>(f + s) * AQB * 2 + q) * PSTRIDE;
+        const float *pp = part + (static_cast<size_t>(f + s) * 2 + q) * PSTRIDE;
         const float e = pp[HD] == -INFINITY ? 0.f : expf(pp[HD] - M);
         L = fmaf(pp[HD + 1], e, L);
         const float4 v = load4(pp + 4 * lane);

@@ -8,10 +8,13 @@
 //    K in blocks of 64 (one 128-byte swizzle row of fp16), an optional K
 //    split over blockIdx.z whose partial sums are added with f32 atomics
 //    (which also gives the residual add for free).
-//  - A operand (weights): warps 0-3, one weight row per thread, read the
-//    row-packed Q8_0 (or f32) block from global memory, dequantise it to
-//    fp16 (w = q * d, rounded once) and store it in the UMMA K-major
-//    128B-swizzle layout; fence.proxy.async, then an mbarrier arrival.
+//  - A operand (weights): the matrix is kept a second time in a tile-packed
+//    layout (gemm_tile_pack_kernel): the 128 rows x 64 k of one stage are one
+//    contiguous chunk (Q8_0: 8192 int8 + 256 fp16 scales = 8704 bytes), so
+//    one bulk copy (cp.async.bulk) brings a stage's weights into shared
+//    memory; warps 0-3 (one weight row per thread) dequantise it there to
+//    fp16 (w = q * d, rounded once) in the UMMA K-major 128B-swizzle layout,
+//    fence.proxy.async, then an mbarrier arrival.
 //  - B operand (activations, fp16 [T][K]): one TMA tiled load per stage
 //    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast).
 //  - MMA: one thread issues tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 ->
@@ -30,12 +33,25 @@ namespace qtts {
 
 constexpr int G_BM = 128;           // weight rows per CTA tile
 constexpr int G_BK = 64;            // K per stage (128 bytes of fp16)
-constexpr int G_STAGES = 4;
 constexpr int G_THREADS = 256;
 constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
 
+// one tile-packed chunk: 128 rows x 64 k.  The values are grouped by 8 k:
+// [8 groups][128 rows][8 values] (so that thread r reads group c of its row
+// at a conflict-free address), then for Q8_0 the scales [128 rows][2 fp16]
+// of the two 32-blocks.
+__host__ __device__ constexpr int g_chunk_bytes(int wdt) {
+    return wdt == WDT_Q8 ? G_BM * G_BK + G_BM * 4 : G_BM * G_BK * 4;
+}
+// pipeline depth from the shared-memory budget (at most 6 stages)
+__host__ __device__ constexpr int g_stages(int wdt, int bn) {
+    return (220 * 1024) / (g_chunk_bytes(wdt) + G_A_BYTES + bn * 128) < 6
+               ? (220 * 1024) / (g_chunk_bytes(wdt) + G_A_BYTES + bn * 128)
+               : 6;
+}
+
 struct GemmArgs {
-    const uint8_t *w;  // [n_rows] rows, row-packed Q8_0 or f32 (row_bytes(wdt, K))
+    const uint8_t *w;  // tile-packed: chunk (row tile rt, k block kb) at (rt * K/64 + kb) * g_chunk_bytes
     int n_rows, K;
     int T;             // tokens
     float *out;        // out[t * ld + n]
@@ -45,16 +61,57 @@ struct GemmArgs {
     int *err;          // error word (QTTS_E_TIMEOUT on a wait that gave up)
 };
 
-template <int BN>
+template <int WDT, int BN>
 struct __align__(1024) GemmSmem {
-    uint8_t a[G_STAGES][G_A_BYTES];   // 1024-aligned: swizzle atoms
-    uint8_t b[G_STAGES][BN * 128];
-    uint64_t full_a[G_STAGES];        // 128 producer arrivals
-    uint64_t full_b[G_STAGES];        // TMA tx bytes
-    uint64_t empty[G_STAGES];         // tcgen05.commit
+    static constexpr int S = g_stages(WDT, BN);
+    uint8_t a[S][G_A_BYTES];          // 1024-aligned: swizzle atoms
+    uint8_t b[S][BN * 128];
+    uint8_t raw[S][g_chunk_bytes(WDT)];  // the packed weights of a stage
+    uint64_t full_raw[S];             // bulk copy tx bytes
+    uint64_t full_a[S];               // 128 dequantiser arrivals
+    uint64_t full_b[S];               // TMA tx bytes
+    uint64_t empty[S];                // tcgen05.commit
     uint64_t accum;                   // last MMA done
     uint32_t tmem_base;
 };
+
+// row-packed matrix (Q8_0: [K int8][K/32 fp16] per row; f32 rows) -> the
+// tile-packed chunks; rows beyond n_rows are zero.  One thread per (row of
+// the padded tile grid, k block, group of 8).
+__global__ void gemm_tile_pack_kernel(const uint8_t *src, int wdt, int n_rows, int K, uint8_t *dst) {
+    const int KB = K / G_BK;
+    const int rows_p = (n_rows + G_BM - 1) / G_BM * G_BM;
+    const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<long long>(rows_p) * KB * 8) return;
+    const int c = static_cast<int>(t & 7);
+    const long long rk = t >> 3;
+    const int kb = static_cast<int>(rk % KB);
+    const int n = static_cast<int>(rk / KB);
+    const int rt = n / G_BM, r = n % G_BM;
+    uint8_t *chunk = dst + (static_cast<size_t>(rt) * KB + kb) * g_chunk_bytes(wdt);
+    const int k = kb * G_BK + 8 * c;
+    if (wdt == WDT_Q8) {
+        const int rb = K + K / 16;
+        uint2 q = make_uint2(0u, 0u);
+        if (n < n_rows) q = *reinterpret_cast<const uint2 *>(src + static_cast<size_t>(n) * rb + k);
+        *reinterpret_cast<uint2 *>(chunk + (c * G_BM + r) * 8) = q;
+        if (c < 2) {
+            uint16_t d = 0;
+            if (n < n_rows) d = reinterpret_cast<const uint16_t *>(src + static_cast<size_t>(n) * rb + K)[kb * 2 + c];
+            reinterpret_cast<uint16_t *>(chunk + G_BM * G_BK)[r * 2 + c] = d;
+        }
+    } else {
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        if (n < n_rows) {
+            const float *row = reinterpret_cast<const float *>(src + static_cast<size_t>(n) * K * 4);
+            lo = *reinterpret_cast<const float4 *>(row + k);
+            hi = *reinterpret_cast<const float4 *>(row + k + 4);
+        }
+        float4 *o = reinterpret_cast<float4 *>(chunk + (c * G_BM + r) * 32);
+        o[0] = lo;
+        o[1] = hi;
+    }
+}
 
 // ------------------------------------------------------------------ tcgen05 helpers
 
@@ -109,15 +166,18 @@ __device__ __forceinline__ void gemm_fail(int *err) {
 template <int WDT, int BN>
 __global__ void __launch_bounds__(G_THREADS, 1)
     gemm_kernel(const GemmArgs args, const __grid_constant__ CUtensorMap xmap) {
+    using Smem = GemmSmem<WDT, BN>;
+    constexpr int S = Smem::S;
+    constexpr uint32_t CHUNK = g_chunk_bytes(WDT);
     extern __shared__ __align__(1024) uint8_t gsmem_raw[];
     // the dynamic window is aligned up to 1024 bytes (the swizzle atom)
-    GemmSmem<BN> *sm = reinterpret_cast<GemmSmem<BN> *>(
-        (reinterpret_cast<uintptr_t>(gsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    Smem *sm = reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(gsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * G_BM, tok0 = blockIdx.y * BN;
     const int kb_total = args.K / G_BK, kb_n = kb_total / args.ksplit, kb0 = blockIdx.z * kb_n;
     if (tid == 0) {
-        for (int s = 0; s < G_STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&sm->full_raw[s], 1);
             mbar_init(&sm->full_a[s], 128);
             mbar_init(&sm->full_b[s], 1);
             mbar_init(&sm->empty[s], 1);
@@ -135,45 +195,45 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm->tmem_base;
-    bool ok = true;
+    // every copy issued is waited for before the CTA exits (also on a
+    // timeout), so no bulk copy lands in shared memory of a later CTA
+    int issued = 0;
 
     if (warp < 4) {
-        // ---- A producers: thread = weight row
+        // ---- dequantisers: thread = weight row of the tile
         const int r = tid;
-        const int n = row0 + r;
-        const int rb = row_bytes(WDT, args.K);
-        const uint8_t *row = args.w + static_cast<size_t>(n < args.n_rows ? n : 0) * rb;
         for (int i = 0; i < kb_n; ++i) {
-            const int s = i % G_STAGES;
-            if (i >= G_STAGES && !mbar_wait(&sm->empty[s], ((i / G_STAGES) - 1) & 1, nullptr)) {
-                ok = false;
+            const int s = i % S;
+            if (!mbar_wait(&sm->full_raw[s], (i / S) & 1, nullptr)) {
                 gemm_fail(args.err);
                 break;
             }
-            const int k0 = (kb0 + i) * G_BK;
+            const uint8_t *raw = sm->raw[s];
             uint8_t *dst = sm->a[s] + (r >> 3) * 1024 + (r & 7) * 128;
+            float dsc[2] = {0.f, 0.f};
+            if (WDT == WDT_Q8) {
+                const __half2 d2 = *reinterpret_cast<const __half2 *>(raw + G_BM * G_BK + r * 4);
+                dsc[0] = __low2float(d2);
+                dsc[1] = __high2float(d2);
+            }
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 k
+            for (int c = 0; c < 8; ++c) {  // 8 groups of 8 k
                 __half2 h[4];
-                if (n < args.n_rows) {
-                    if (WDT == WDT_Q8) {
-                        const uint2 q = *reinterpret_cast<const uint2 *>(row + k0 + 8 * c);
-                        const float d = __half2float(reinterpret_cast<const __half *>(row + args.K)[(k0 + 8 * c) >> 5]);
-                        const float4 lo = dq4(q.x), hi = dq4(q.y);
-                        h[0] = __floats2half2_rn(lo.x * d, lo.y * d);
-                        h[1] = __floats2half2_rn(lo.z * d, lo.w * d);
-                        h[2] = __floats2half2_rn(hi.x * d, hi.y * d);
-                        h[3] = __floats2half2_rn(hi.z * d, hi.w * d);
-                    } else {
-                        const float4 lo = *reinterpret_cast<const float4 *>(row + 4 * (k0 + 8 * c));
-                        const float4 hi = *reinterpret_cast<const float4 *>(row + 4 * (k0 + 8 * c + 4));
-                        h[0] = __floats2half2_rn(lo.x, lo.y);
-                        h[1] = __floats2half2_rn(lo.z, lo.w);
-                        h[2] = __floats2half2_rn(hi.x, hi.y);
-                        h[3] = __floats2half2_rn(hi.z, hi.w);
-                    }
+                if (WDT == WDT_Q8) {
+                    const uint2 q = *reinterpret_cast<const uint2 *>(raw + (c * G_BM + r) * 8);
+                    const float d = dsc[c >> 2];
+                    const float4 lo = dq4(q.x), hi = dq4(q.y);
+                    h[0] = __floats2half2_rn(lo.x * d, lo.y * d);
+                    h[1] = __floats2half2_rn(lo.z * d, lo.w * d);
+                    h[2] = __floats2half2_rn(hi.x * d, hi.y * d);
+                    h[3] = __floats2half2_rn(hi.z * d, hi.w * d);
                 } else {
-                    h[0] = h[1] = h[2] = h[3] = __floats2half2_rn(0.f, 0.f);
+                    const float4 *v = reinterpret_cast<const float4 *>(raw + (c * G_BM + r) * 32);
+                    const float4 lo = v[0], hi = v[1];
+                    h[0] = __floats2half2_rn(lo.x, lo.y);
+                    h[1] = __floats2half2_rn(lo.z, lo.w);
+                    h[2] = __floats2half2_rn(hi.x, hi.y);
+                    h[3] = __floats2half2_rn(hi.z, hi.w);
                 }
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(h);
             }
@@ -182,17 +242,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             mbar_arrive(&sm->full_a[s]);
         }
     } else if (warp == 4) {
-        // ---- B producer (TMA)
+        // ---- producer: the weight chunk (bulk copy) and the activations (TMA)
         if (lane == 0) {
+            const uint8_t *wt = args.w + (static_cast<size_t>(blockIdx.x) * kb_total + kb0) * CHUNK;
             for (int i = 0; i < kb_n; ++i) {
-                const int s = i % G_STAGES;
-                if (i >= G_STAGES && !mbar_wait(&sm->empty[s], ((i / G_STAGES) - 1) & 1, nullptr)) {
-                    ok = false;
+                const int s = i % S;
+                if (i >= S && !mbar_wait(&sm->empty[s], ((i / S) - 1) & 1, nullptr)) {
                     gemm_fail(args.err);
                     break;
                 }
+                mbar_arrive_tx(&sm->full_raw[s], CHUNK);
+                bulk_g2s(sm->raw[s], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[s]);
                 mbar_arrive_tx(&sm->full_b[s], BN * 128);
                 tma_load_2d(sm->b[s], &xmap, (kb0 + i) * G_BK, tok0, &sm->full_b[s]);
+                issued = i + 1;
             }
         }
     } else if (warp == 5) {
@@ -200,10 +263,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(G_BM, BN);
             for (int i = 0; i < kb_n; ++i) {
-                const int s = i % G_STAGES;
-                const uint32_t par = (i / G_STAGES) & 1;
+                const int s = i % S;
+                const uint32_t par = (i / S) & 1;
                 if (!mbar_wait(&sm->full_a[s], par, nullptr) || !mbar_wait(&sm->full_b[s], par, nullptr)) {
-                    ok = false;
                     gemm_fail(args.err);
                     break;
                 }
@@ -244,13 +306,22 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
         }
     }
+    if (warp == 4 && lane == 0) {
+        // drain: wait (bounded) for the copies of the last S issued stages
+        for (int i = issued > S ? issued - S : 0; i < issued; ++i) {
+            const int s = i % S;
+            if (!mbar_wait(&sm->full_raw[s], (i / S) & 1, nullptr) || !mbar_wait(&sm->full_b[s], (i / S) & 1, nullptr)) {
+                gemm_fail(args.err);
+                break;
+            }
+        }
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 5) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(BN) : "memory");
     }
-    (void)ok;
 }
 
 // f32 rows -> fp16 rows (the activations of the tensor-core path)
