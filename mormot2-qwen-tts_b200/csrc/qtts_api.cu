@@ -22,6 +22,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/qtts.h"
@@ -57,6 +58,28 @@ static int set_err(int code, const char *fmt, ...) {
     } while (0)
 
 extern "C" const char *qtts_last_error(void) { return g_err.c_str(); }
+
+// ------------------------------------------------------------------ launches
+
+// a kernel launch with programmatic stream serialisation: the kernel may
+// start while its predecessor on the stream runs (its pdl_wait() orders the
+// dependent work), which hides launch and prologue latency between the
+// short kernels of the batched path, in graphs too
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------ handles
 
@@ -380,22 +403,32 @@ static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 
     CUtensorMap map;
     int rc = tensor_map_f16(&map, x, a.K, rows_cap, BN);
     if (rc) return rc;
-    gemm_kernel<WDT, BN><<<grid, G_THREADS, smem, st>>>(a, map);
-    CK(cudaGetLastError());
+    CK(launch_pdl(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, a, map));
     return QTTS_OK;
 }
 
 // y[t][n] (+)= x[t][:] . w[n][:] for t < T (w tile-packed; x: fp16 [rows_cap][K] on the
 // device, rows_cap >= T).  With `add`, the products are added to y (residual);
 // otherwise y is overwritten (zeroed first when the K split needs atomics).
-static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
-                bool add, int *err, cudaStream_t st) {
-    if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
-    const int bn = T <= 64 ? 64 : (T <= 128 ? 128 : 256);
+static int gemm_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
+
+// the K split of a GEMM: CTAs up to about one per SM
+static int gemm_split(int n_rows, int k, int T) {
+    const int bn = gemm_bn(T);
     const int tiles = ((n_rows + G_BM - 1) / G_BM) * ((T + bn - 1) / bn);
     const int kb = k / G_BK;
     int split = 1;
     while (split * 2 <= kb && kb % (split * 2) == 0 && tiles * split * 2 <= 160) split *= 2;
+    return split;
+}
+
+// y[t][n] (+)= ... with `zeroed`: y already holds zeros where a split-K
+// GEMM needs them (cleared by the kernel before it)
+static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
+                bool add, int *err, cudaStream_t st, bool zeroed = false) {
+    if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
+    const int bn = gemm_bn(T);
+    const int split = gemm_split(n_rows, k, T);
     GemmArgs a;
     a.w = w;
     a.n_rows = n_rows;
@@ -406,7 +439,7 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.atomic = (add || split > 1) ? 1 : 0;
     a.ksplit = split;
     a.err = err;
-    if (!add && split > 1) {
+    if (!add && split > 1 && !zeroed) {
         if (ld == n_rows)
             CK(cudaMemsetAsync(y, 0, static_cast<size_t>(T) * ld * 4, st));
         else
@@ -1607,24 +1640,49 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
     const int cap = b->max_tokens;
     for (int l = 0; l < s->cfg.layers && rc == QTTS_OK; ++l) {
         const DLayer &Ly = s->tlayers[l];
-        rmsnorm_f16_kernel<<<(T + 7) / 8, 256, 0, st>>>(b->x, nullptr, T, Ly.in_norm, eps, b->h16, nullptr);
-        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st))) return;
-        qkv_post_kernel<KVT><<<dim3(T, 4), 256, 0, st>>>(b->qkv, tok_seq, tok_pos, Ly.q_norm, Ly.k_norm, eps,
-                                                         b->rope_cos, b->rope_sin, b->q32, pool, l);
-        if (npitems > 0) attn_kernel<KVT><<<npitems, ATHREADS, 0, st>>>(pitems, b->q32, pool, l, b->attn16);
-        if (nditems > 0)
-            attn_decode_kernel<KVT><<<nditems, DTHREADS, sizeof(DecodeSmem<KVT>), st>>>(ditems, b->q32, pool, l,
-                                                                                        b->attn16, b->part, b->err);
-        if (ncomb > 0)
-            attn_combine_kernel<<<(ncomb * HQ + 7) / 8, 256, 0, st>>>(cfirst, ccount, ctok, ncomb, b->part, b->attn16);
+        // the split-K outputs (qkv, gu) are cleared by the norm before them
+        const long long zq = gemm_split(QKV_ROWS, H, T) > 1 ? static_cast<long long>(T) * QKV_ROWS / 4 : 0;
+        const long long zg = gemm_split(GU_ROWS, H, T) > 1 ? static_cast<long long>(T) * GU_ROWS / 4 : 0;
+        cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3((T + 7) / 8), dim3(256), 0, st, b->x, nullptr, T,
+                                   Ly.in_norm, eps, b->h16, nullptr, b->qkv, zq);
+        if (e != cudaSuccess) {
+            rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
+            return;
+        }
+        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st, true))) return;
+        e = launch_pdl(qkv_post_kernel<KVT>, dim3(T, 4), dim3(256), 0, st, b->qkv, tok_seq, tok_pos, Ly.q_norm,
+                       Ly.k_norm, eps, b->rope_cos, b->rope_sin, b->q32, pool, l);
+        if (e == cudaSuccess && npitems > 0)
+            e = launch_pdl(attn_kernel<KVT>, dim3(npitems), dim3(ATHREADS), 0, st, pitems, b->q32, pool, l, b->attn16);
+        if (e == cudaSuccess && nditems > 0)
+            e = launch_pdl(attn_decode_kernel<KVT>, dim3(nditems), dim3(DTHREADS), sizeof(DecodeSmem<KVT>), st, ditems,
+                           b->q32, pool, l, b->attn16, b->part, b->err);
+        if (e == cudaSuccess && ncomb > 0)
+            e = launch_pdl(attn_combine_kernel, dim3((ncomb * HQ + 7) / 8), dim3(256), 0, st, cfirst, ccount, ctok,
+                           ncomb, static_cast<const float *>(b->part), b->attn16);
+        if (e != cudaSuccess) {
+            rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
+            return;
+        }
         if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
-        rmsnorm_f16_kernel<<<(T + 7) / 8, 256, 0, st>>>(b->x, nullptr, T, Ly.post_norm, eps, b->h16, nullptr);
-        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, b->gu, GU_ROWS, false, b->err, st))) return;
+        e = launch_pdl(rmsnorm_f16_kernel, dim3((T + 7) / 8), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm, eps,
+                       b->h16, nullptr, b->gu, zg);
+        if (e != cudaSuccess) {
+            rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
+            return;
+        }
+        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, b->gu, GU_ROWS, false, b->err, st, true))) return;
         const long long np = static_cast<long long>(T) * INTER;
-        swiglu_f16_kernel<<<static_cast<unsigned>((np + 255) / 256), 256, 0, st>>>(b->gu, np, b->act16);
+        e = launch_pdl(swiglu_f16_kernel, dim3(static_cast<unsigned>((np + 255) / 256)), dim3(256), 0, st,
+                       static_cast<const float *>(b->gu), np, b->act16);
+        if (e != cudaSuccess) {
+            rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
+            return;
+        }
         if ((rc = gemm(Ly.wd, wdt, H, INTER, b->act16, T, cap, b->x, H, true, b->err, st))) return;
-        if (cudaGetLastError() != cudaSuccess) rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: kernel launch failed");
     }
+    if (rc == QTTS_OK && cudaGetLastError() != cudaSuccess)
+        rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: kernel launch failed");
 }
 
 // The host half of one batched forward: validation, KV pages, the token
@@ -1796,12 +1854,15 @@ static int batch_enqueue(qtts_batch *b, const BatchPlan &P, const float *x, bool
         batch_layers<__nv_bfloat16>(b, P.T, P.np, d_pitems, P.nd, d_ditems, m, m + P.T, P.ncomb, m + P.o_cf,
                                     m + P.o_cc, m + P.o_ct, wdt, st, rc);
     if (rc) return rc;
-    rmsnorm_f16_kernel<<<(P.nseq + 7) / 8, 256, 0, st>>>(b->x, m + P.o_last, P.nseq, b->stack->d_final_norm,
-                                                         b->stack->cfg.rms_eps, b->hlast16, b->hidden);
-    CK(cudaGetLastError());
+    const int hr = head >= 0 ? b->heads->mats[head].rows : 0;
+    const long long zl = head >= 0 && gemm_split(hr, H, P.nseq) > 1 ? static_cast<long long>(P.nseq) * hr / 4 : 0;
+    CK(launch_pdl(rmsnorm_f16_kernel, dim3((P.nseq + 7) / 8), dim3(256), 0, st, static_cast<const float *>(b->x),
+                  m + P.o_last, P.nseq, static_cast<const float *>(b->stack->d_final_norm), b->stack->cfg.rms_eps,
+                  b->hlast16, b->hidden, b->logits, zl));
     if (head >= 0) {
         const HeadMat &hm = b->heads->mats[head];
-        if ((rc = gemm(hm.t, wdt, hm.rows, H, b->hlast16, P.nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st)))
+        if ((rc = gemm(hm.t, wdt, hm.rows, H, b->hlast16, P.nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st,
+                       true)))
             return rc;
     }
     return QTTS_OK;
@@ -2059,22 +2120,23 @@ static int frame_enqueue(qtts_talkers *t, int n, const BatchPlan *plans, cudaStr
     CK(cudaMemcpyAsync(t->d_seqs, io_seqs(t), n * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemsetAsync(t->tb->err, 0, 16, st));
     CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
-    frames_begin_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->seen, t->cfg.vocab, t->hid, t->codec_emb, t->px,
-                                           t->d_codes, G);
-    CK(cudaGetLastError());
+    CK(launch_pdl(frames_begin_kernel, dim3(n), dim3(256), 0, st, static_cast<const int *>(t->d_seqs), t->ss, t->seen,
+                  t->cfg.vocab, static_cast<const float *>(t->hid), static_cast<const float *>(t->codec_emb), t->px,
+                  t->d_codes, G));
     for (int g = 0; g < G - 1; ++g) {
         if ((rc = batch_enqueue(t->pb, plans[g], t->px, true, g, st))) return rc;
-        frames_pred_argmax_kernel<<<n, 256, 0, st>>>(t->pb->logits, pv, g, G, t->pred_emb, t->px, t->d_codes);
-        CK(cudaGetLastError());
+        CK(launch_pdl(frames_pred_argmax_kernel, dim3(n), dim3(256), 0, st, static_cast<const float *>(t->pb->logits),
+                      pv, g, G, static_cast<const float *>(t->pred_emb), t->px, t->d_codes));
     }
-    frames_talker_in_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->ss, t->d_codes, G, t->codec_emb, t->pred_emb, pv,
-                                               t->d_trail, t->tts_pad, t->xt);
-    CK(cudaGetLastError());
+    CK(launch_pdl(frames_talker_in_kernel, dim3(n), dim3(256), 0, st, static_cast<const int *>(t->d_seqs),
+                  static_cast<const SeqState *>(t->ss), static_cast<const int *>(t->d_codes), G,
+                  static_cast<const float *>(t->codec_emb), static_cast<const float *>(t->pred_emb), pv,
+                  static_cast<const float *const *>(t->d_trail), static_cast<const float *>(t->tts_pad), t->xt));
     if ((rc = batch_enqueue(t->tb, plans[G - 1], t->xt, true, 0, st))) return rc;
-    frames_choose0_kernel<<<n, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
-                                             t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
-                                             t->d_done, 0);
-    CK(cudaGetLastError());
+    CK(launch_pdl(frames_choose0_kernel, dim3(n), dim3(256), 0, st, static_cast<const int *>(t->d_seqs),
+                  static_cast<const float *>(t->tb->logits), static_cast<const float *>(t->tb->hidden), t->cfg.vocab,
+                  t->cfg.codec_eos, t->cfg.repetition_penalty, static_cast<const unsigned char *>(t->seen), t->ss,
+                  t->hid, t->d_done, 0));
     CK(cudaMemcpyAsync(io_codes(t), t->d_codes, static_cast<size_t>(n) * G * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(io_done(t), t->d_done, n * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(io_errs(t), t->tb->err, 4, cudaMemcpyDeviceToHost, st));

@@ -50,9 +50,15 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *s) {
 }
 
 // One warp per row: out16[o] = fp16(rmsnorm(x[idx[o]]) * w); optionally the
-// float32 normed row too (the normed state returned as `hidden`).
+// float32 normed row too (the normed state returned as `hidden`).  The grid
+// also zeroes zero[0..nzero4*4) (the output of the next split-K GEMM).
 __global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, const float *w, float eps, __half *out16,
-                                   float *out32) {
+                                   float *out32, float *zero, long long nzero4) {
+    pdl_trigger();
+    pdl_wait();
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < nzero4;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        reinterpret_cast<float4 *>(zero)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (o >= rows) return;
     const float *r = x + static_cast<size_t>(idx ? idx[o] : o) * H;
@@ -83,6 +89,8 @@ template <class KVT>
 __global__ void qkv_post_kernel(const float *qkv, const int *tok_seq, const int *tok_pos, const float *q_norm,
                                 const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
                                 float *q32, KVPool<KVT> pool, int layer) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x, v = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int seq = tok_seq[t], pos = tok_pos[t];
     const int off = v < 16 ? v * HD : (v < 24 ? QDIM + (v - 16) * HD : QDIM + KVDIM + (v - 24) * HD);
@@ -135,6 +143,8 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(const AttnItem *items, c
     __shared__ __align__(16) float ks[AKT][HD];
     __shared__ __align__(16) float vs[AKT][HD];
     __shared__ __align__(16) float ws[8][HD + 4];
+    pdl_trigger();
+    pdl_wait();
     const AttnItem it = items[blockIdx.x];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = it.qb - it.qa, nc = 2 * R;
@@ -288,6 +298,8 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
                                                               float *part, int *err) {
     extern __shared__ __align__(128) uint8_t dsm_raw[];
     DecodeSmem<KVT> *sm = reinterpret_cast<DecodeSmem<KVT> *>(dsm_raw);
+    pdl_trigger();
+    pdl_wait();
     const AttnItem it = items[blockIdx.x];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = tid >> 6, j = tid & 63;  // scores: (head, key); output: (head, dim pair j)
@@ -384,6 +396,8 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
 // first[call*8 + h] .. +count of kv head h hold its partials.
 __global__ void attn_combine_kernel(const int *first, const int *count, const int *tok, int ncalls, const float *part,
                                     __half *attn16) {
+    pdl_trigger();
+    pdl_wait();
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (w >= ncalls * HQ) return;
     const int call = w / HQ, qh = w - call * HQ, h = qh >> 1, q = qh & 1;
@@ -411,6 +425,8 @@ __global__ void attn_combine_kernel(const int *first, const int *count, const in
 
 // act16[t][j] = fp16(silu(gate) * up); gate j and up j are columns 2j, 2j+1
 __global__ void swiglu_f16_kernel(const float *gu, long long n_pairs, __half *act16) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n_pairs) return;
     const float2 gv = *reinterpret_cast<const float2 *>(gu + 2 * i);
@@ -438,6 +454,8 @@ struct SeqState {
 // Start: reset the state of seqs[i], clear its history marks.
 __global__ void frames_start_kernel(const int *seqs, const int *trailing_rows, SeqState *ss, unsigned char *seen,
                                     int vocab) {
+    pdl_trigger();
+    pdl_wait();
     const int s = seqs[blockIdx.x];
     unsigned char *m = seen + static_cast<size_t>(s) * vocab;
     for (int i = threadIdx.x; i < vocab; i += blockDim.x) m[i] = 0;
@@ -452,6 +470,8 @@ __global__ void frames_start_kernel(const int *seqs, const int *trailing_rows, S
 // input rows 2i, 2i+1 = [talker state, codec_emb[code 0]].
 __global__ void frames_begin_kernel(const int *seqs, SeqState *ss, unsigned char *seen, int vocab,
                                     const float *hid, const float *codec_emb, float *px, int *codes, int groups) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x, s = seqs[i];
     const int c0 = ss[s].next_code0;
     const float *h = hid + static_cast<size_t>(s) * H;
@@ -495,6 +515,8 @@ __device__ __forceinline__ unsigned long long block_argmax(unsigned long long b,
 // is pred_emb[g][code] (talker.pas:670-675).
 __global__ void frames_pred_argmax_kernel(const float *logits, int vocab, int g, int groups, const float *pred_emb,
                                           float *px, int *codes) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ unsigned long long red[32];
     const int i = blockIdx.x;
     const float *lg = logits + static_cast<size_t>(i) * vocab;
@@ -518,6 +540,8 @@ __global__ void frames_pred_argmax_kernel(const float *logits, int vocab, int g,
 __global__ void frames_talker_in_kernel(const int *seqs, const SeqState *ss, const int *codes, int groups,
                                         const float *codec_emb, const float *pred_emb, int pvocab,
                                         const float *const *trailing, const float *tts_pad, float *xt) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x, s = seqs[i];
     const int *cd = codes + i * groups;
     const int step = ss[s].step;
@@ -542,6 +566,8 @@ __global__ void frames_talker_in_kernel(const int *seqs, const SeqState *ss, con
 __global__ void frames_choose0_kernel(const int *seqs, const float *logits, const float *hidden, int vocab, int eos,
                                       float penalty, const unsigned char *seen, SeqState *ss, float *hid, int *done,
                                       int start) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ unsigned long long red[32];
     const int i = blockIdx.x, s = seqs[i];
     const float *lg = logits + static_cast<size_t>(i) * vocab;

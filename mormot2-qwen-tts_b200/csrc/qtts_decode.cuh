@@ -283,6 +283,13 @@ __device__ __forceinline__ int key_index(unsigned long long k) {
 // may hold an older copy)
 __device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
+// programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while its predecessor runs; pdl_wait() returns
+// once the predecessor grid has completed and its writes are visible (at
+// once without such a launch), pdl_trigger() lets the successor launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ shared memory
 
 struct __align__(128) Smem {

@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    pdl_trigger();
     const uint32_t tmem = sm->tmem_base;
     // every copy issued is waited for before the CTA exits (also on a
     // timeout), so no bulk copy lands in shared memory of a later CTA
@@ -245,17 +246,27 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         // ---- producer: the weight chunk (bulk copy) and the activations (TMA)
         if (lane == 0) {
             const uint8_t *wt = args.w + (static_cast<size_t>(blockIdx.x) * kb_total + kb0) * CHUNK;
+            // the weights of the first stages do not depend on the previous
+            // kernel: they are on their way before its completion is awaited
+            const int pre = kb_n < S ? kb_n : S;
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_tx(&sm->full_raw[i], CHUNK);
+                bulk_g2s(sm->raw[i], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[i]);
+            }
+            pdl_wait();
             for (int i = 0; i < kb_n; ++i) {
                 const int s = i % S;
-                if (i >= S && !mbar_wait(&sm->empty[s], ((i / S) - 1) & 1, nullptr)) {
-                    gemm_fail(args.err);
-                    break;
+                if (i >= S) {
+                    if (!mbar_wait(&sm->empty[s], ((i / S) - 1) & 1, nullptr)) {
+                        gemm_fail(args.err);
+                        break;
+                    }
+                    mbar_arrive_tx(&sm->full_raw[s], CHUNK);
+                    bulk_g2s(sm->raw[s], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[s]);
                 }
-                mbar_arrive_tx(&sm->full_raw[s], CHUNK);
-                bulk_g2s(sm->raw[s], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[s]);
                 mbar_arrive_tx(&sm->full_b[s], BN * 128);
                 tma_load_2d(sm->b[s], &xmap, (kb0 + i) * G_BK, tok0, &sm->full_b[s]);
-                issued = i + 1;
+                issued = i + 1;  // (a break happens at i >= S: every stage before it has both copies)
             }
         }
     } else if (warp == 5) {
@@ -281,6 +292,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
     // ---- epilogue: warps 4-7, TMEM lane quarter = warp % 4
     if (warp >= 4) {
+        pdl_wait();  // out may be written by the previous kernels
         const bool good = mbar_wait(&sm->accum, 0, nullptr);
         if (!good) gemm_fail(args.err);
         __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of warps 4/5 had other work
