@@ -233,10 +233,11 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     utterance (15 batched predictor steps + 1 batched talker step) through
     qtts_talkers_next_frame, codes read back to the host each frame."""
     B, K, W = args.batch, args.batch_steps, 3
+    lo, hi = args.batch_ctx
     rng = np.random.default_rng(SEED + 7 + rank)
-    ctx = rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, B)
+    ctx = rng.integers(lo, hi + 1, B)
     chunk = 16384
-    tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=chunk, max_pos=BATCH_CTX[1] + K + W + 8, kv_dtype="bf16")
+    tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=chunk, max_pos=hi + K + W + 8, kv_dtype="bf16")
     pb = qtts.QwenBatch(pstack, ph, max_seqs=B, max_tokens=2 * B, max_pos=16, kv_dtype="bf16")
     ts = qtts.QwenTalkers(tb, pb, m["ce"], m["pe"], synth.CODEC_EOS)
     stream = torch.cuda.ExternalStream(ts.stream, device=torch.device("cuda", local_rank))
@@ -276,14 +277,17 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     pb.free()
     # algorithmic bytes of one batched frame: the weights once, the talker KV
     # of every utterance (bf16), the predictor KV
-    wb = weight_bytes_per_frame("q8_0")
+    tl, pl = args.talker_layers, args.pred_layers
+    wb = weight_bytes_per_frame("q8_0", tl, pl)
     mean_ctx = float(ctx.mean()) + W + K / 2.0
-    kv = 28 * KV_POS_BF16 * B * (mean_ctx + 1)
-    kv += sum(5 * KV_POS_BF16 * B * ((0 if g == 0 else g + 1) + (2 if g == 0 else 1)) for g in range(15))
+    kv = tl * KV_POS_BF16 * B * (mean_ctx + 1)
+    kv += sum(pl * KV_POS_BF16 * B * ((0 if g == 0 else g + 1) + (2 if g == 0 else 1)) for g in range(15))
     peaks = measured_peaks()
     peak = peaks["hbm_gbs"] if peaks else 6650.0
     achieved = (wb + kv) / (ms / 1000.0 / K) / 1e9
-    return {"workload": f"configs[2]: {B} utterances per GPU, contexts U({BATCH_CTX[0]},{BATCH_CTX[1]}), Q8_0 weights, "
+    extra = {} if (tl, pl) == (28, 5) else {"layers_override": f"talker {tl}, predictor {pl} (profiling case)"}
+    return {**extra,
+            "workload": f"configs[2]: {B} utterances per GPU, contexts U({lo},{hi}), Q8_0 weights, "
                         "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs",
             "metric": "frames/s per GPU @B=%d" % B if world == 1 else "box frames/s @B=%d per GPU" % B,
             "value": world * frames / (ms / 1000.0), "unit": "frames/s", "steps": K, "warmup": W,
@@ -324,6 +328,19 @@ def gpu_arm(args, rank, world, local_rank):
     batched = None
     if args.batch > 0 and dtype == "q8_0":
         batched = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist)
+    if args.only_batched:
+        # the configs[2] measurement alone (profiling runs)
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "n_gpus": world, "batched": batched}), flush=True)
+        for o in (th, ph):
+            o.free()
+        for st in (tstack, pstack):
+            qtts.stack_destroy(st)
+        dev.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     tlm = qtts.QwenLm(tstack, th, max_pos)
     plm = qtts.QwenLm(pstack, ph, 32)
     tk = qtts.QwenTalker(tlm, plm, m["ce"], m["pe"], synth.CODEC_EOS)
@@ -449,6 +466,8 @@ def main():
     # configs[2] beside the bench line: B utterances decoded together (0: off)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=20)
+    ap.add_argument("--batch-ctx", type=int, nargs=2, default=list(BATCH_CTX), metavar=("LO", "HI"))
+    ap.add_argument("--only-batched", action="store_true", help="run the configs[2] measurement alone")
     # smaller stacks for profiler captures only (the benchmark is 28 + 5)
     ap.add_argument("--talker-layers", type=int, default=28)
     ap.add_argument("--pred-layers", type=int, default=5)

@@ -2105,10 +2105,11 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
     return QTTS_OK;
 }
 
-// context splits per sequence of the batched talker step: about 4 CTAs per
-// SM over all (utterance, kv head) pairs, 2 to DMAX_SPLITS
+// context splits per sequence of the batched talker step: about 4 waves of
+// the decode attention CTAs (6 resident per SM with a bf16 cache) over all
+// (utterance, kv head) pairs, 2 to DMAX_SPLITS
 static int talker_splits(const qtts_talkers *t, int n) {
-    const int want = (4 * t->tb->dev->sms + n * HKV - 1) / (n * HKV);
+    const int want = (24 * t->tb->dev->sms + n * HKV / 2) / (n * HKV);
     return want < 2 ? 2 : (want > DMAX_SPLITS ? DMAX_SPLITS : want);
 }
 

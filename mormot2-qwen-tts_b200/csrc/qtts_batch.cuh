@@ -253,9 +253,10 @@ __global__ void __launch_bounds__(ATHREADS) attn_kernel(const AttnItem *items, c
 // One new row per sequence (the decode steps of the talker and the
 // predictor): split-K over the context.  One CTA per (sequence, kv head,
 // split); the split's keys [ka, kb) (ka page-aligned) are visited in tiles of
-// DSPLIT keys (4 pages), double-buffered: the K and V pages of a tile come in
-// by bulk copies (16 positions x 128 of one head are contiguous in a page)
-// while the previous tile is used.  Per tile, 128 threads score the 2 query
+// DSPLIT keys (4 pages): the K and V pages of a tile come in by bulk copies
+// (16 positions x 128 of one head are contiguous in a page).  One buffer per
+// CTA keeps shared memory at 33 KB (bf16), so that 6 CTAs share an SM and
+// hide each other's copy latency.  Per tile, 128 threads score the 2 query
 // heads x 64 keys, a shuffle softmax per head updates the running (m, l), and
 // thread (head, dim pair) accumulates the output.  A single split writes the
 // normalised row, several write (m, l, o) partials for attn_combine_kernel.
@@ -265,12 +266,12 @@ constexpr int DMAX_SPLITS = 16;  // fixed split count per sequence at most
 
 template <class KVT>
 struct DecodeSmem {
-    KVT ks[2][DSPLIT][HD];
-    KVT vs[2][DSPLIT][HD];
+    KVT ks[DSPLIT][HD];
+    KVT vs[DSPLIT][HD];
     float qs[2][HD];
     float p[2][DSPLIT];
     float red[4][2];
-    uint64_t bar[2];
+    uint64_t bar;
     int ok;
 };
 
@@ -281,14 +282,14 @@ __device__ __forceinline__ float2 load2(const __nv_bfloat16 *s) {
 
 template <class KVT>
 __device__ __forceinline__ void decode_issue(DecodeSmem<KVT> *sm, const KVPool<KVT> &pool, int layer, int seq,
-                                             int head, int k0, int nk, int buf) {
+                                             int head, int k0, int nk) {
     constexpr uint32_t PAGE_BYTES = PAGE * HD * sizeof(KVT);
     const int npg = (nk + PAGE - 1) / PAGE;
-    mbar_arrive_tx(&sm->bar[buf], 2 * npg * PAGE_BYTES);
+    mbar_arrive_tx(&sm->bar, 2 * npg * PAGE_BYTES);
     for (int i = 0; i < npg; ++i) {
         const int pos = k0 + i * PAGE;
-        bulk_g2s(&sm->ks[buf][i * PAGE][0], kv_at(pool, layer, seq, pos, 0, head), PAGE_BYTES, &sm->bar[buf]);
-        bulk_g2s(&sm->vs[buf][i * PAGE][0], kv_at(pool, layer, seq, pos, 1, head), PAGE_BYTES, &sm->bar[buf]);
+        bulk_g2s(&sm->ks[i * PAGE][0], kv_at(pool, layer, seq, pos, 0, head), PAGE_BYTES, &sm->bar);
+        bulk_g2s(&sm->vs[i * PAGE][0], kv_at(pool, layer, seq, pos, 1, head), PAGE_BYTES, &sm->bar);
     }
 }
 
@@ -306,10 +307,9 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
     const int nkeys = it.kb > it.ka ? it.kb - it.ka : 0;
     const int ntiles = (nkeys + DSPLIT - 1) / DSPLIT;
     if (tid == 0) {
-        mbar_init(&sm->bar[0], 1);
-        mbar_init(&sm->bar[1], 1);
+        mbar_init(&sm->bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        if (ntiles > 0) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys), 0);
+        if (ntiles > 0) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys));
     }
     for (int i = tid; i < 2 * HD / 4; i += DTHREADS) {
         const int hq = i / (HD / 4), d4 = i - hq * (HD / 4);
@@ -320,12 +320,10 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
     float m_run = -INFINITY, l_run = 0.f, ox = 0.f, oy = 0.f;
     int waited = 0;  // tiles whose copies are known to have landed (thread 0)
     for (int t = 0; t < ntiles; ++t) {
-        const int buf = t & 1;
         const int k0 = it.ka + t * DSPLIT, nk = min(DSPLIT, it.kb - k0);
         if (tid == 0) {
-            if (t + 1 < ntiles)
-                decode_issue(sm, pool, layer, it.seq, it.h, k0 + DSPLIT, min(DSPLIT, it.kb - k0 - DSPLIT), buf ^ 1);
-            const bool got = mbar_wait(&sm->bar[buf], (t >> 1) & 1, nullptr);
+            // tile t was issued before the loop (t = 0) or at the end of t-1
+            const bool got = mbar_wait(&sm->bar, t & 1, nullptr);
             waited = got ? t + 1 : waited;
             sm->ok = got ? 1 : 0;
         }
@@ -338,7 +336,7 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
 #pragma unroll 8
             for (int e = 0; e < HD / 2; ++e) {
                 const int pr = (e + j) & (HD / 2 - 1);
-                const float2 kv2 = load2(&sm->ks[buf][j][2 * pr]);
+                const float2 kv2 = load2(&sm->ks[j][2 * pr]);
                 const float2 qv2 = *reinterpret_cast<const float2 *>(&sm->qs[q][2 * pr]);
                 a = fmaf(qv2.x, kv2.x, a);
                 a = fmaf(qv2.y, kv2.y, a);
@@ -364,19 +362,19 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
         oy *= corr;
         for (int k = 0; k < nk; ++k) {
             const float pk = sm->p[q][k];
-            const float2 v2 = load2(&sm->vs[buf][k][2 * j]);
+            const float2 v2 = load2(&sm->vs[k][2 * j]);
             ox = fmaf(pk, v2.x, ox);
             oy = fmaf(pk, v2.y, oy);
         }
         m_run = m_new;
-        __syncthreads();  // (D) buffer, p and red free for the next tiles
+        __syncthreads();  // (D) buffer, p and red free: the next tile comes in
+        if (tid == 0 && t + 1 < ntiles) decode_issue(sm, pool, layer, it.seq, it.h, k0 + DSPLIT, min(DSPLIT, it.kb - k0 - DSPLIT));
     }
     if (tid == 0 && waited < ntiles) {
-        // a wait gave up: report it, then wait (bounded) for every copy
-        // issued so that none lands after the CTA has exited
+        // a wait gave up: report it, then wait (bounded) for the copy in
+        // flight so that none lands after the CTA has exited
         atomicCAS(err, 0, ERR_TIMEOUT);
-        const int issued = min(ntiles, waited + 2);
-        for (int t = waited; t < issued; ++t) mbar_wait(&sm->bar[t & 1], (t >> 1) & 1, nullptr);
+        mbar_wait(&sm->bar, waited & 1, nullptr);
     }
     if (it.part < 0) {
         const float inv = 1.0f / l_run;

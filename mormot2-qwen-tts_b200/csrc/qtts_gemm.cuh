@@ -157,6 +157,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ __half2 u32_as_half2(uint32_t u) {
+    __half2 h;
+    *reinterpret_cast<uint32_t *>(&h) = u;
+    return h;
+}
 __device__ __forceinline__ void gemm_fail(int *err) {
     if (err) atomicCAS(err, 0, ERR_TIMEOUT);
 }
@@ -211,23 +216,26 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
             const uint8_t *raw = sm->raw[s];
             uint8_t *dst = sm->a[s] + (r >> 3) * 1024 + (r & 7) * 128;
-            float dsc[2] = {0.f, 0.f};
+            __half2 d2lo = __float2half2_rn(0.f), d2hi = d2lo;  // the two blocks' scales, broadcast
             if (WDT == WDT_Q8) {
-                const __half2 d2 = *reinterpret_cast<const __half2 *>(raw + G_BM * G_BK + r * 4);
-                dsc[0] = __low2float(d2);
-                dsc[1] = __high2float(d2);
+                const __half2 dd = *reinterpret_cast<const __half2 *>(raw + G_BM * G_BK + r * 4);
+                d2lo = __low2half2(dd);
+                d2hi = __high2half2(dd);
             }
 #pragma unroll
             for (int c = 0; c < 8; ++c) {  // 8 groups of 8 k
                 __half2 h[4];
                 if (WDT == WDT_Q8) {
+                    // q + 128 in the mantissa of fp16 1024 (exact), minus 1152,
+                    // times d in fp16: the exact product q * d rounded once
                     const uint2 q = *reinterpret_cast<const uint2 *>(raw + (c * G_BM + r) * 8);
-                    const float d = dsc[c >> 2];
-                    const float4 lo = dq4(q.x), hi = dq4(q.y);
-                    h[0] = __floats2half2_rn(lo.x * d, lo.y * d);
-                    h[1] = __floats2half2_rn(lo.z * d, lo.w * d);
-                    h[2] = __floats2half2_rn(hi.x * d, hi.y * d);
-                    h[3] = __floats2half2_rn(hi.z * d, hi.w * d);
+                    const uint32_t ux = q.x ^ 0x80808080u, uy = q.y ^ 0x80808080u;
+                    const __half2 bias = __float2half2_rn(1152.f);
+                    const __half2 d2 = c < 4 ? d2lo : d2hi;
+                    h[0] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x5140)), bias), d2);
+                    h[1] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x7362)), bias), d2);
+                    h[2] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias), d2);
+                    h[3] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias), d2);
                 } else {
                     const float4 *v = reinterpret_cast<const float4 *>(raw + (c * G_BM + r) * 32);
                     const float4 lo = v[0], hi = v[1];
