@@ -1626,6 +1626,14 @@ extern "C" int qtts_batch_length(qtts_batch *b, int seq, int *length) {
     return QTTS_OK;
 }
 
+// blocks of rmsnorm_f16_kernel: 8 rows each, and enough threads to clear
+// nzero4 float4s of the next GEMM's output in a few passes
+static unsigned norm_grid(int rows, long long nzero4) {
+    long long g = (rows + 7) / 8;
+    const long long gz = std::min<long long>((nzero4 + 1023) / 1024, 2 * 148);
+    return static_cast<unsigned>(std::max(g, gz));
+}
+
 template <class KVT>
 static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pitems, int nditems,
                          const AttnItem *ditems, const int *tok_seq, const int *tok_pos, int ncomb, const int *cfirst,
@@ -1643,7 +1651,7 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
         // the split-K outputs (qkv, gu) are cleared by the norm before them
         const long long zq = gemm_split(QKV_ROWS, H, T) > 1 ? static_cast<long long>(T) * QKV_ROWS / 4 : 0;
         const long long zg = gemm_split(GU_ROWS, H, T) > 1 ? static_cast<long long>(T) * GU_ROWS / 4 : 0;
-        cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3((T + 7) / 8), dim3(256), 0, st, b->x, nullptr, T,
+        cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, zq)), dim3(256), 0, st, b->x, nullptr, T,
                                    Ly.in_norm, eps, b->h16, nullptr, b->qkv, zq);
         if (e != cudaSuccess) {
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
@@ -1665,8 +1673,8 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
             return;
         }
         if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
-        e = launch_pdl(rmsnorm_f16_kernel, dim3((T + 7) / 8), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm, eps,
-                       b->h16, nullptr, b->gu, zg);
+        e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, zg)), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm,
+                       eps, b->h16, nullptr, b->gu, zg);
         if (e != cudaSuccess) {
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
             return;
@@ -1856,7 +1864,7 @@ static int batch_enqueue(qtts_batch *b, const BatchPlan &P, const float *x, bool
     if (rc) return rc;
     const int hr = head >= 0 ? b->heads->mats[head].rows : 0;
     const long long zl = head >= 0 && gemm_split(hr, H, P.nseq) > 1 ? static_cast<long long>(P.nseq) * hr / 4 : 0;
-    CK(launch_pdl(rmsnorm_f16_kernel, dim3((P.nseq + 7) / 8), dim3(256), 0, st, static_cast<const float *>(b->x),
+    CK(launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(P.nseq, zl)), dim3(256), 0, st, static_cast<const float *>(b->x),
                   m + P.o_last, P.nseq, static_cast<const float *>(b->stack->d_final_norm), b->stack->cfg.rms_eps,
                   b->hlast16, b->hidden, b->logits, zl));
     if (head >= 0) {
