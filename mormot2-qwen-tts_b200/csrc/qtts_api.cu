@@ -211,6 +211,43 @@ __global__ void pack_kernel(const void *src, int src_dtype, int rows, int k, uin
     reinterpret_cast<__half *>(row + k)[b] = dh;
 }
 
+// The batch-1 kernel's layouts by kv head (its per-head phases):
+// QKV rows [HKV][q(2h), q(2h+1), k(h), v(h)][H] from the [q | k | v] rows,
+// one thread per 16-byte piece of a row.
+__global__ void qkv_by_head_kernel(const uint8_t *src, int wdt, uint8_t *dst) {
+    const int rb = row_bytes(wdt, H), pieces = rb / 16;
+    const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<long long>(QKV_ROWS) * pieces) return;
+    const int row = static_cast<int>(t / pieces), pc = static_cast<int>(t % pieces);
+    const int h = row / QKV_HEAD, part = (row % QKV_HEAD) / HD, i = row % HD;
+    const int srow = part < 2 ? (2 * h + part) * HD + i : (part == 2 ? QDIM : QDIM + KVDIM) + h * HD + i;
+    reinterpret_cast<uint4 *>(dst + static_cast<size_t>(row) * rb)[pc] =
+        reinterpret_cast<const uint4 *>(src + static_cast<size_t>(srow) * rb)[pc];
+}
+
+// the O projection (row-packed [H][QDIM]) by kv head: row h*H + n = columns
+// [h*KO, (h+1)*KO) of row n, with the scales of those 8 blocks (Q8_0) after
+// them.  One thread per (row, block).
+__global__ void oproj_by_head_kernel(const uint8_t *src, int wdt, uint8_t *dst) {
+    constexpr int NB = KO / 32;  // blocks of a kv head's columns
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= HKV * H * NB) return;
+    const int b = t % NB, row = t / NB;  // row of the regrouped matrix
+    const int h = row / H, n = row % H;
+    const int sb = h * NB + b;           // block in the source row
+    if (wdt == WDT_Q8) {
+        const uint8_t *srow = src + static_cast<size_t>(n) * row_bytes(WDT_Q8, QDIM);
+        uint8_t *drow = dst + static_cast<size_t>(row) * row_bytes(WDT_Q8, KO);
+        for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<uint32_t *>(drow + b * 32 + i) = *reinterpret_cast<const uint32_t *>(srow + sb * 32 + i);
+        reinterpret_cast<uint16_t *>(drow + KO)[b] = reinterpret_cast<const uint16_t *>(srow + QDIM)[sb];
+    } else {
+        const float *srow = reinterpret_cast<const float *>(src + static_cast<size_t>(n) * QDIM * 4);
+        float *drow = reinterpret_cast<float *>(dst + static_cast<size_t>(row) * KO * 4);
+        for (int i = 0; i < 32; ++i) drow[b * 32 + i] = srow[sb * 32 + i];
+    }
+}
+
 // f32 -> ggml blocks (34 bytes), the same rule
 __global__ void quantize_ggml_kernel(const float *src, long long nb, uint8_t *dst) {
     long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -573,8 +610,10 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
         size_t bo = static_cast<size_t>(H) * row_bytes(wdt, QDIM);
         size_t bgu = static_cast<size_t>(GU_ROWS) * row_bytes(wdt, H);
         size_t bd = static_cast<size_t>(H) * row_bytes(wdt, INTER);
+        size_t boh = static_cast<size_t>(HKV) * H * row_bytes(wdt, KO);
         uint8_t *wqkv = alloc(bqkv), *wo = alloc(bo), *wgu = alloc(bgu), *wd = alloc(bd);
-        if (!wqkv || !wo || !wgu || !wd) {
+        uint8_t *wqkvh = alloc(bqkv), *woh = alloc(boh);
+        if (!wqkv || !wo || !wgu || !wd || !wqkvh || !woh) {
             rc = set_err(QTTS_E_OOM, "qtts_stack_create: out of device memory at layer %d", l);
             break;
         }
@@ -587,8 +626,19 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
         if ((rc = upload_matrix(dev, a.gate_proj, sd, INTER, H, wgu, dt, 2, 0))) break;
         if ((rc = upload_matrix(dev, a.up_proj, sd, INTER, H, wgu, dt, 2, 1))) break;
         if ((rc = upload_matrix(dev, a.down_proj, sd, H, INTER, wd, dt, 1, 0))) break;
+        {
+            const long long nq = static_cast<long long>(QKV_ROWS) * (row_bytes(wdt, H) / 16);
+            qkv_by_head_kernel<<<static_cast<unsigned>((nq + 255) / 256), 256, 0, dev->load>>>(wqkv, wdt, wqkvh);
+            oproj_by_head_kernel<<<(HKV * H * (KO / 32) + 255) / 256, 256, 0, dev->load>>>(wo, wdt, woh);
+            if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(dev->load) != cudaSuccess) {
+                rc = set_err(QTTS_E_CUDA, "qtts_stack_create: per-head layouts failed at layer %d", l);
+                break;
+            }
+        }
         d.wqkv = wqkv;
         d.wo = wo;
+        d.wqkvh = wqkvh;
+        d.woh = woh;
         d.wgu = wgu;
         d.wd = wd;
         float *p;
@@ -838,7 +888,7 @@ static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
     };
     size_t ox = take(RMAX * H * 4), oqkv = take(RMAX * QKV_ROWS * 4), oact = take(RMAX * INTER * 4),
            opart = take(static_cast<size_t>(HKV) * maxS * RMAX * 2 * PSTRIDE * 4),
-           oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(16), oerr = take(16),
+           oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(BAR_WORDS * 4), oerr = take(16),
            olog = take(static_cast<size_t>(max_head_rows) * 4), ohid = take(H * 4), oxt = take(H * 4);
     CK(cudaStreamCreateWithFlags(&r.stream, cudaStreamNonBlocking));
     CK(cudaMalloc(&r.block, off));
@@ -883,7 +933,7 @@ static int runner_check(Runner &r) {
     if (r.h_err[0] != 0) {
         int code = r.h_err[0], where = r.h_err[1];
         CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
-        CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+        CK(cudaMemsetAsync(r.s.bar, 0, BAR_WORDS * 4, r.stream));
         CK(cudaStreamSynchronize(r.stream));
         return set_err(code == ERR_CAPACITY ? QTTS_E_CAPACITY : QTTS_E_TIMEOUT,
                        "device wait gave up (code %d at %d): the kernel returned early", code, where);
@@ -1369,7 +1419,7 @@ constexpr size_t NA_PART = NA_ACT + al256(static_cast<size_t>(RMAX) * INTER * 4)
 constexpr size_t NA_ARG =
     NA_PART + al256(static_cast<size_t>(HKV) * (NOALLOC_MAX_SMS / HKV) * RMAX * 2 * PSTRIDE * 4);
 constexpr size_t NA_BAR = NA_ARG + al256(static_cast<size_t>(NOALLOC_MAX_SMS) * 8);
-constexpr size_t NA_ERR = NA_BAR + al256(16);
+constexpr size_t NA_ERR = NA_BAR + al256(BAR_WORDS * 4);
 constexpr size_t NA_LOGITS = NA_ERR + al256(16);
 constexpr size_t NA_HIDDEN = NA_LOGITS + al256(static_cast<size_t>(NOALLOC_MAX_HEAD_ROWS) * 4);
 constexpr size_t NA_XT = NA_HIDDEN + al256(H * 4);
@@ -1434,7 +1484,7 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
     r.s.xt = reinterpret_cast<float *>(sc + NA_XT);
     // the array keeps the last call's contents: the barrier counters and the
     // error word must start at zero
-    CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+    CK(cudaMemsetAsync(r.s.bar, 0, BAR_WORDS * 4, r.stream));
     CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
     const int wdt = m->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
     Job j = base_job(m);
@@ -1458,7 +1508,7 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
         CK(cudaMemcpyAsync(err, r.s.err, 8, cudaMemcpyDeviceToHost, r.stream));
         CK(cudaStreamSynchronize(r.stream));
         if (err[0] != 0) {
-            CK(cudaMemsetAsync(r.s.bar, 0, 16, r.stream));
+            CK(cudaMemsetAsync(r.s.bar, 0, BAR_WORDS * 4, r.stream));
             CK(cudaMemsetAsync(r.s.err, 0, 16, r.stream));
             CK(cudaStreamSynchronize(r.stream));
             return set_err(err[0] == ERR_CAPACITY ? QTTS_E_CAPACITY : QTTS_E_TIMEOUT,

@@ -64,7 +64,10 @@ constexpr int PRODUCER_WARP = NWARPS - 1;
 constexpr int STAGE_BYTES = 24576;
 constexpr int NSTAGES = 5;
 constexpr int ACT_FLOATS = RMAX * INTER;  // staged activations [R][K]
-constexpr int MAX_PARTS = 48;             // (row, 1024-segment) partial sums of a CTA slice (grid >= 128)
+constexpr int MAX_PARTS = 64;             // (row, K segment) partial sums of a CTA slice (grid >= 128)
+constexpr int KO = 2 * HD;                // O-projection columns of one kv head (its 2 query heads)
+constexpr int QKV_HEAD = 4 * HD;          // QKV rows of one kv head: q(2h), q(2h+1), k(h), v(h)
+constexpr int BAR_WORDS = 16;             // barrier counters: [0] grid, [1] exit, [2 + h] group of kv head h
 constexpr int PSTRIDE = 132;              // attention partial: o[128], m, l
 constexpr int ATT_TILE = 32;              // context positions per attention tile
 constexpr int XS_MAX = 16;                // residual rows owned by a CTA (grid >= 64)
@@ -81,6 +84,19 @@ constexpr long long WAIT_CYCLES = 4000000000ll;
 
 __host__ __device__ constexpr int row_bytes(int wdt, int k) { return wdt == WDT_F32 ? k * 4 : k + k / 16; }
 
+// the CTAs of a grid of g are split into HKV contiguous groups, one per kv
+// head: CTA b belongs to head (b * HKV) / g, index j of nj in its group
+__host__ __device__ inline void head_group(int b, int g, int &h, int &j, int &nj) {
+    h = (b * HKV) / g;
+    const int g0 = (h * g + HKV - 1) / HKV, g1 = ((h + 1) * g + HKV - 1) / HKV;
+    j = b - g0;
+    nj = g1 - g0;
+}
+
+// contexts of at most one attention tile take the per-head path (attention
+// of a kv head in every CTA of its group, fused with the O projection)
+__host__ __device__ inline bool per_head_path(int T) { return T <= ATT_TILE; }
+
 // attention splits of a context of T positions over a grid of g CTAs
 __host__ __device__ inline int att_splits(int T, int g) {
     int s = (T + ATT_TILE - 1) / ATT_TILE;
@@ -93,6 +109,9 @@ __host__ __device__ inline int att_splits(int T, int g) {
 
 struct DLayer {
     const uint8_t *wqkv, *wo, *wgu, *wd;
+    // batch-1 kernel layouts: QKV rows by kv head [HKV][q(2h) q(2h+1) k(h) v(h)][H],
+    // the O projection by kv head [HKV][H rows][KO columns]
+    const uint8_t *wqkvh, *woh;
     const float *in_norm, *post_norm, *q_norm, *k_norm;
 };
 
@@ -114,9 +133,10 @@ struct Scratch {
     float *x;       // [RMAX][H] residual stream
     float *qkv;     // [RMAX][QKV_ROWS]
     float *act;     // [RMAX][INTER]
-    float *part;    // [HKV*maxS][RMAX][2][PSTRIDE] attention partials
+    float *part;    // [HKV*maxS][RMAX][2][PSTRIDE] attention partials, or (per-head path)
+                    // [RMAX][HKV * H] O-projection partials, one H-vector per kv head
     unsigned long long *arg;  // [grid] argmax keys
-    unsigned *bar;  // [0] barrier counter, [1] exit counter
+    unsigned *bar;  // [BAR_WORDS]: [0] grid barrier, [1] exit, [2 + h] group barrier of kv head h
     int *err;       // [0] error code, [1] where
     float *logits;  // [max head rows]
     float *hidden;  // [H] normed state of the last row
@@ -318,12 +338,13 @@ struct __align__(128) Smem {
 
 // Matrix phases in program order.  The producer and the compute warps walk
 // the same order; it must not depend on data.
-enum Mat { M_QKV, M_O, M_GU, M_D, M_HEAD };
+enum Mat { M_QKV, M_O, M_OH, M_GU, M_D, M_HEAD };
 
 __device__ __forceinline__ int mat_rows(Mat m, int head_rows) {
     switch (m) {
         case M_QKV: return QKV_ROWS;
         case M_O: return H;
+        case M_OH: return HKV * H;  // by kv head
         case M_GU: return GU_ROWS;
         case M_D: return H;
         default: return head_rows;
@@ -332,13 +353,22 @@ __device__ __forceinline__ int mat_rows(Mat m, int head_rows) {
 __device__ __forceinline__ int mat_k(Mat m) {
     switch (m) {
         case M_O: return QDIM;
+        case M_OH: return KO;
         case M_D: return INTER;
         default: return H;
     }
 }
-// rows [r0, r1) of an N-row matrix owned by CTA b of G (pairs for gate/up)
+// rows [r0, r1) of an N-row matrix owned by CTA b of G (pairs for gate/up;
+// QKV and the O projection by kv head: rows of the head's block split over
+// the CTAs of its group)
 __device__ __forceinline__ void mat_slice(Mat m, int n, int b, int g, int &r0, int &r1) {
-    if (m == M_GU) {
+    if (m == M_QKV || m == M_OH) {
+        int h, j, nj;
+        head_group(b, g, h, j, nj);
+        const int per = n / HKV;
+        r0 = h * per + j * per / nj;
+        r1 = h * per + (j + 1) * per / nj;
+    } else if (m == M_GU) {
         int p = n / 2;
         r0 = 2 * static_cast<int>(static_cast<long long>(b) * p / g);
         r1 = 2 * static_cast<int>(static_cast<long long>(b + 1) * p / g);
@@ -472,6 +502,39 @@ struct Compute {
         mark(200 + where);  // departure
     }
 
+    // barrier among the CTAs of this CTA's kv-head group (the same counter
+    // scheme as grid_sync, on the group's own counter)
+    unsigned gtarget = 0;
+    __device__ void group_sync(int where) {
+        const bool bad = named_or(!ok);
+        mark(100 + where);
+        if (tid == 0) {
+            int h, j, nj;
+            head_group(blockIdx.x, gridDim.x, h, j, nj);
+            gtarget += nj;
+            int b = bad ? 1 : 0;
+            if (!bad) {
+                unsigned *bar = job->s.bar + 2 + h;
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+                const long long t0 = clock64();
+                while (true) {
+                    unsigned v;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+                    if (v >= gtarget) break;
+                    if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > WAIT_CYCLES) {
+                        fail(ERR_TIMEOUT, where);
+                        b = 1;
+                        break;
+                    }
+                }
+            }
+            sm->bcast = b;
+        }
+        named_sync();
+        ok = sm->bcast == 0;
+        mark(200 + where);
+    }
+
     // ---------------------------------------------------------------- staging
 
     // act[r][0..H) = x_r * w for the rows x_r = ((a + b) + c) (up to 3
@@ -479,12 +542,28 @@ struct Compute {
     // of squares of x_r per warp in red[]: the RMSNorm scale 1/rms(x_r) is
     // applied by the GEMV epilogue (norm_inv), so staging needs one barrier.
     // With init_resid, this CTA's residual rows [c0, c1) come from the sum.
+    //  opart != NULL (per-head path): the rows are a[r] (+ b[r] + c[r]) plus
+    //  the O projection, the sum of its HKV per-kv-head partials
+    //  opart[r][h][..] in head order.
     __device__ void stage_norm(const float *const *a, const float *const *b, const float *const *c, int R,
-                               const float *w, bool init_resid) {
+                               const float *w, bool init_resid, const float *opart = nullptr) {
         float ss[RMAX] = {0.f, 0.f, 0.f, 0.f};
         for (int idx = tid; idx < R * (H / 4); idx += NCT) {
             const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
             float4 v = ldcg4(a[r] + i);
+            float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (opart) {
+                // all HKV loads in flight together, summed in head order
+                const float *op = opart + static_cast<size_t>(r) * (HKV * H) + i;
+                float4 t[HKV];
+#pragma unroll
+                for (int hh = 0; hh < HKV; ++hh) t[hh] = ldcg4(op + hh * H);
+                y = t[0];
+#pragma unroll
+                for (int hh = 1; hh < HKV; ++hh) {
+                    y.x = y.x + t[hh].x; y.y = y.y + t[hh].y; y.z = y.z + t[hh].z; y.w = y.w + t[hh].w;
+                }
+            }
             if (b && b[r]) {
                 const float4 t = ldcg4(b[r] + i);
                 v.x = v.x + t.x; v.y = v.y + t.y; v.z = v.z + t.z; v.w = v.w + t.w;
@@ -492,6 +571,9 @@ struct Compute {
             if (c && c[r]) {
                 const float4 t = ldcg4(c[r] + i);
                 v.x = v.x + t.x; v.y = v.y + t.y; v.z = v.z + t.z; v.w = v.w + t.w;
+            }
+            if (opart) {
+                v.x = v.x + y.x; v.y = v.y + y.y; v.z = v.z + y.z; v.w = v.w + y.w;
             }
             const float4 g = *reinterpret_cast<const float4 *>(w + i);
             *reinterpret_cast<float4 *>(sm->act + r * H + i) = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
@@ -583,7 +665,8 @@ struct Compute {
     //  job->s.arg; E_HEAD0 applies ChooseCode0's processors first.
     template <int K>
     __device__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld, float eps) {
-        constexpr int SEG = K / 1024;
+        constexpr int SEGW = K < 1024 ? K : 1024;  // K segment of one item
+        constexpr int SEG = K / SEGW;
         const int rb = row_bytes(WDT, K);
         const int n = mat_rows(m, head_rows);
         int r0, r1;
@@ -620,11 +703,8 @@ struct Compute {
 #pragma unroll
                 for (int r = 0; r < RMAX; ++r) aa[r] = ab[r] = 0.f;
 #pragma unroll
-                for (int uu = 0; uu < 2; ++uu) {
-                    const int u = seg * 2 + uu;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const int e = u * 512 + 128 * g + 4 * lane;  // first of this lane's 4 elements
+                    for (int g = 0; g < SEGW / 128; ++g) {
+                        const int e = seg * SEGW + 128 * g + 4 * lane;  // first of this lane's 4 elements
                         float4 wa, wb;
                         float da = 1.f, db = 1.f;
                         if (WDT == WDT_Q8) {
@@ -657,7 +737,6 @@ struct Compute {
                             }
                         }
                     }
-                }
                 const int row = ch * sr + ra;  // row within the slice
 #pragma unroll
                 for (int r = 0; r < RMAX; ++r) {
@@ -782,11 +861,21 @@ struct Compute {
     // Issued at the end of P1, before the barrier: the cached K/V rows of the
     // first tile of this CTA's split (positions < L0, written in earlier
     // steps), bulk-copied into sm->kv.  Thread 0.
-    __device__ void prefetch_kv(const DCtx &kv, int layer, int R, int L0) {
+    __device__ void prefetch_kv(const DCtx &kv, int layer, int R, int L0, bool head_path) {
         if (tid == 0) {
             sm->kv_rows = 0;
             int S, h, s, p0, p1;
-            if (ok && att_item(L0 + R, S, h, s, p0, p1)) {
+            bool have = false;
+            if (head_path) {
+                int j, nj;
+                head_group(blockIdx.x, gridDim.x, h, j, nj);
+                p0 = 0;
+                p1 = L0 + R;
+                have = true;
+            } else {
+                have = att_item(L0 + R, S, h, s, p0, p1);
+            }
+            if (ok && have) {
                 const int n = min(min(p1, L0), p0 + ATT_TILE) - p0;
                 if (n > 0) {
                     const size_t off = ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + p0) * HD;
@@ -805,13 +894,29 @@ struct Compute {
     // normed and rotated, the new K/V appended to the cache (split 0), then
     // online-softmax attention over [p0, p1) with positions spread over the
     // warps; the partial (o, max, sum) of every (row, q head) to global.
-    __device__ void attention(const DLayer &Ly, const DCtx &kv, int layer, int R, int L0, float eps) {
+    //  head_path (a context of one tile): CTA b takes its group's kv head and
+    //  the whole context, CTA 0 of the group appends, and the normalised
+    //  output of row r goes to act[r][KO] for the O projection by head.
+    __device__ void attention(const DLayer &Ly, const DCtx &kv, int layer, int R, int L0, float eps,
+                              bool head_path) {
         const int T = L0 + R;
         int S, h, s, p0, p1;
-        if (!att_item(T, S, h, s, p0, p1)) return;
+        bool append;
+        if (head_path) {
+            int j, nj;
+            head_group(blockIdx.x, gridDim.x, h, j, nj);
+            S = 1;
+            s = 0;
+            p0 = 0;
+            p1 = T;
+            append = j == 0;
+        } else {
+            if (!att_item(T, S, h, s, p0, p1)) return;
+            append = s == 0;
+        }
         const bool prefetched = sm->kv_rows > 0;
-        // shared layout inside sm->act: q[R][2][HD] | kn[R][HD] | vn[R][HD] | warp states
-        float *qs = sm->act;
+        // shared layout inside sm->act: [head path: o[R][KO]] | q[R][2][HD] | kn[R][HD] | vn[R][HD] | warp states
+        float *qs = sm->act + (head_path ? RMAX * KO : 0);
         float *kn = qs + RMAX * 2 * HD;
         float *vn = kn + RMAX * HD;
         float *wst = vn + RMAX * HD;  // [NCW][PSTRIDE]
@@ -819,9 +924,9 @@ struct Compute {
         // 1. the new rows
         for (int vec = warp; vec < 4 * R; vec += NCW) {
             const int r = vec >> 2, t = vec & 3;  // t: 0,1 = q heads, 2 = k, 3 = v
-            const float *src = job->s.qkv + r * QKV_ROWS;
-            const int off = t < 2 ? (2 * h + t) * HD : (t == 2 ? QDIM + h * HD : QDIM + KVDIM + h * HD);
-            const float4 x = ldcg4(src + off + 4 * lane);
+            // QKV rows by kv head: q(2h), q(2h+1), k(h), v(h)
+            const float *src = job->s.qkv + r * QKV_ROWS + h * QKV_HEAD + t * HD;
+            const float4 x = ldcg4(src + 4 * lane);
             float y[4] = {x.x, x.y, x.z, x.w};
             if (t < 3) {
                 const float *nw = t < 2 ? Ly.q_norm : Ly.k_norm;
@@ -850,7 +955,7 @@ struct Compute {
             }
             float *dst = t < 2 ? qs + (r * 2 + t) * HD : (t == 2 ? kn + r * HD : vn + r * HD);
             *reinterpret_cast<float4 *>(dst + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
-            if (s == 0 && t >= 2) {
+            if (append && t >= 2) {
                 float *cache = (t == 2 ? kv.k : kv.v) +
                                ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + (L0 + r)) * HD;
                 *reinterpret_cast<float4 *>(cache + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
@@ -944,25 +1049,33 @@ struct Compute {
                     acc.w = fmaf(v.w, e, acc.w);
                 }
             }
-            float *pp = job->s.part + ((static_cast<size_t>(h * S + s) * RMAX + r) * 2 + qq) * PSTRIDE;
-            *reinterpret_cast<float4 *>(pp + 4 * lane) = acc;
-            if (lane == 0) {
-                pp[HD] = M;
-                pp[HD + 1] = L;
+            if (head_path) {
+                const float inv = 1.0f / L;
+                *reinterpret_cast<float4 *>(sm->act + r * KO + qq * HD + 4 * lane) =
+                    make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            } else {
+                float *pp = job->s.part + ((static_cast<size_t>(h * S + s) * RMAX + r) * 2 + qq) * PSTRIDE;
+                *reinterpret_cast<float4 *>(pp + 4 * lane) = acc;
+                if (lane == 0) {
+                    pp[HD] = M;
+                    pp[HD + 1] = L;
+                }
             }
         }
+        if (head_path) named_sync();
     }
 
     // ---------------------------------------------------------------- stack
 
     // one forward of a stack over R rows at positions L0..L0+R-1; layer 0's
     // input row r is in0[r] (+ in1[r]) (+ in2[r])
-    __device__ void stack(const DStack &st, const DCtx &kv, int R, int L0, const float *const *in0,
+    __device__ __forceinline__ void stack(const DStack &st, const DCtx &kv, int R, int L0, const float *const *in0,
                           const float *const *in1, const float *const *in2) {
         const Scratch &S = job->s;
         const float *xr[RMAX];
         for (int r = 0; r < RMAX; ++r) xr[r] = S.x + r * H;
         const int nsplit = att_splits(L0 + R, gridDim.x);
+        const bool hp = per_head_path(L0 + R);
         for (int l = 0; l < st.layers && ok; ++l) {
             const DLayer Ly = st.layer[l];
             // P1
@@ -973,23 +1086,40 @@ struct Compute {
             mark(10);
             gemv<H>(M_QKV, 0, R, E_STORE, S.qkv, QKV_ROWS, st.eps);
             mark(11);
-            prefetch_kv(kv, l, R, L0);
-            grid_sync(1);
+            prefetch_kv(kv, l, R, L0, hp);
+            if (hp)
+                group_sync(7);  // the QKV rows of this kv head come from its group
+            else
+                grid_sync(1);
             if (!ok) return;
             // P2
-            attention(Ly, kv, l, R, L0, st.eps);
+            attention(Ly, kv, l, R, L0, st.eps, hp);
             mark(21);
-            grid_sync(2);
-            if (!ok) return;
-            // P3
-            stage_attn(R, nsplit);
-            mark(30);
-            gemv<QDIM>(M_O, 0, R, E_RESID, S.x, H, -1.f);
-            mark(31);
-            grid_sync(3);
-            if (!ok) return;
-            // P4
-            stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, false);
+            if (hp) {
+                // the O projection restricted to this head's columns, by head
+                gemv<KO>(M_OH, 0, R, E_STORE, S.part, HKV * H, -1.f);
+                mark(31);
+                grid_sync(3);
+                if (!ok) return;
+                // P4: residual + the HKV partials (layer 0's residual is still
+                // its input rows: they reach S.x with the down projection)
+                if (l == 0)
+                    stage_norm(in0, in1, in2, R, Ly.post_norm, true, S.part);
+                else
+                    stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, true, S.part);
+            } else {
+                grid_sync(2);
+                if (!ok) return;
+                // P3
+                stage_attn(R, nsplit);
+                mark(30);
+                gemv<QDIM>(M_O, 0, R, E_RESID, S.x, H, -1.f);
+                mark(31);
+                grid_sync(3);
+                if (!ok) return;
+                // P4
+                stage_norm(xr, nullptr, nullptr, R, Ly.post_norm, false);
+            }
             mark(40);
             gemv<H>(M_GU, 0, R, E_SWIGLU, S.act, INTER, st.eps);
             mark(41);
@@ -1021,11 +1151,15 @@ struct Compute {
 
 // the program, walked by the producer
 template <int WDT, class V>
-__device__ void walk_stack(V &v, const DStack &st) {
+__device__ void walk_stack(V &v, const DStack &st, int T) {
+    const bool hp = per_head_path(T);
     for (int l = 0; l < st.layers; ++l) {
         const DLayer Ly = st.layer[l];
-        v.matrix(Ly.wqkv, M_QKV, 0, st.keep_l2);
-        v.matrix(Ly.wo, M_O, 0, st.keep_l2);
+        v.matrix(Ly.wqkvh, M_QKV, 0, st.keep_l2);
+        if (hp)
+            v.matrix(Ly.woh, M_OH, 0, st.keep_l2);
+        else
+            v.matrix(Ly.wo, M_O, 0, st.keep_l2);
         v.matrix(Ly.wgu, M_GU, 0, st.keep_l2);
         v.matrix(Ly.wd, M_D, 0, st.keep_l2);
     }
@@ -1036,14 +1170,16 @@ __device__ void produce(Smem *sm, const Job &job) {
     Producer<WDT> p;
     p.sm = sm;
     if (job.mode == 0) {
-        walk_stack<WDT>(p, job.st);
+        walk_stack<WDT>(p, job.st, job.L0 + job.rows);
         if (job.head_w) p.matrix(job.head_w, M_HEAD, job.head_rows, false);
     } else {
+        // the contexts of the frame's calls (as the compute warps see them)
+        const int tlen = job.fs->tlen;
         for (int g = 0; g < job.groups - 1; ++g) {
-            walk_stack<WDT>(p, job.pst);
+            walk_stack<WDT>(p, job.pst, g == 0 ? 2 : g + 2);
             p.matrix(job.pheads[g], M_HEAD, job.pvocab, false);
         }
-        walk_stack<WDT>(p, job.tst);
+        walk_stack<WDT>(p, job.tst, tlen + 1);
         p.matrix(job.theads, M_HEAD, job.tvocab, false);
     }
 }
@@ -1056,7 +1192,7 @@ __device__ void compute(Smem *sm, const Job &job) {
     c.tid = threadIdx.x;
     c.warp = threadIdx.x >> 5;
     c.lane = threadIdx.x & 31;
-    mat_slice(M_O, H, blockIdx.x, gridDim.x, c.c0, c.c1);
+    mat_slice(M_D, H, blockIdx.x, gridDim.x, c.c0, c.c1);  // the rows of its down-projection slice
     const Scratch &S = job.s;
     c.mark(1);
     if (job.mode == 0) {
@@ -1153,6 +1289,7 @@ __device__ void compute(Smem *sm, const Job &job) {
         __threadfence();
         if (atomicAdd(S.bar + 1, 1u) == gridDim.x - 1) {
             S.bar[0] = 0u;
+            for (int h = 0; h < HKV; ++h) S.bar[2 + h] = 0u;
             S.bar[1] = 0u;
             __threadfence();
         }
