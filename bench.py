@@ -300,6 +300,60 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
                         "the host inside the timed region; the prefill is outside it"}
 
 
+PREFILL_LEN = (256, 2048)  # configs[3]: prompt lengths drawn uniformly
+PREFILL_SEQS = 16
+
+
+def prefill_measure(args, qtts, torch, m, dev, rank):
+    """one batched prefill of 16 prompts of
+    U(256, 2048) N(0,1) rows through the 28-layer talker with float32
+    weights (tcgen05 projections with fp16 activations, causal attention in
+    f32) and its head on the last rows; each step resets the sequences and
+    runs qtts_batch_forward from host memory (the rows up, the logits and
+    normed states back)."""
+    rng = np.random.default_rng(SEED + 11 + rank)
+    lens = rng.integers(PREFILL_LEN[0], PREFILL_LEN[1] + 1, PREFILL_SEQS)
+    T = int(lens.sum())
+    th = qtts.QwenLmHeads(dev, "talker", synth.HIDDEN, "f32")
+    th.add(m["th"])
+    st = qtts.qwen_lm_stack(dev, synth.CONFIG, m["tl"], m["tf"], "f32")
+    b = qtts.QwenBatch(st, th, max_seqs=PREFILL_SEQS, max_tokens=T, max_pos=PREFILL_LEN[1], kv_dtype="f32")
+    x = np.concatenate([synth.prompt(SEED + 2000 + i, int(n)) for i, n in enumerate(lens)])
+    x = torch.from_numpy(x).pin_memory().numpy()
+    seqs = np.arange(PREFILL_SEQS)
+
+    def step():
+        for q in range(PREFILL_SEQS):
+            b.reset(q)
+        b.forward(seqs, lens, x)
+
+    step()  # warm-up
+    torch.cuda.synchronize()
+    K = max(1, args.prefill_steps)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = (time.perf_counter() - t0) / K
+    b.free()
+    qtts.stack_destroy(st)
+    th.free()
+    # FLOPs of one prefill: the projections of every row (2 per weight) and
+    # causal attention (QK and PV, 2 x 2 per query head, key and dim)
+    proj = 2.0 * LAYER_CELLS * 28 * T + 2.0 * 3072 * 1024 * PREFILL_SEQS
+    att = 28 * 16 * 128 * 4.0 * float(sum(int(n) * (int(n) + 1) // 2 for n in lens))
+    peaks = measured_peaks()
+    peak = peaks["bf16_tflops"] if peaks else 1590.0
+    achieved = (proj + att) / dt / 1e12
+    return {"workload": f"configs[3]: prefill of {PREFILL_SEQS} prompts U({PREFILL_LEN[0]},{PREFILL_LEN[1]}) rows "
+                        f"({T} rows), 28-layer talker, f32 weights, fp16 activations, f32 softmax, f32 KV",
+            "metric": "prefill tokens/s per GPU", "value": T / dt, "unit": "tokens/s", "ms_per_step": dt * 1000.0,
+            "steps": K, "rows": T,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops_per_step": proj + att, "attention_flops": att,
+                         "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)" if peaks else "fallback"},
+            "timing": "host wall clock around qtts_batch_forward (rows from pinned host memory, logits back)"}
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import qtts
@@ -341,6 +395,9 @@ def gpu_arm(args, rank, world, local_rank):
             dist.barrier()
             dist.destroy_process_group()
         return
+    prefill = None
+    if args.prefill_steps > 0 and rank == 0 and (args.talker_layers, args.pred_layers) == (28, 5):
+        prefill = prefill_measure(args, qtts, torch, m, dev, rank)
     tlm = qtts.QwenLm(tstack, th, max_pos)
     plm = qtts.QwenLm(pstack, ph, 32)
     tk = qtts.QwenTalker(tlm, plm, m["ce"], m["pe"], synth.CODEC_EOS)
@@ -441,6 +498,7 @@ def gpu_arm(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "restarts_at_eos": restarts,
             "batched": batched,
+            "prefill": prefill,
             "weights_generation_s": m["gen_s"],
         }
         print(json.dumps(line), flush=True)
@@ -468,6 +526,8 @@ def main():
     ap.add_argument("--batch-steps", type=int, default=20)
     ap.add_argument("--batch-ctx", type=int, nargs=2, default=list(BATCH_CTX), metavar=("LO", "HI"))
     ap.add_argument("--only-batched", action="store_true", help="run the configs[2] measurement alone")
+    # configs[3] beside the bench line: batched prefill steps (0: off)
+    ap.add_argument("--prefill-steps", type=int, default=2)
     # smaller stacks for profiler captures only (the benchmark is 28 + 5)
     ap.add_argument("--talker-layers", type=int, default=28)
     ap.add_argument("--pred-layers", type=int, default=5)

@@ -460,12 +460,14 @@ static int gemm_split(int n_rows, int k, int T) {
 }
 
 // y[t][n] (+)= ... with `zeroed`: y already holds zeros where a split-K
-// GEMM needs them (cleared by the kernel before it)
+// GEMM needs them (cleared by the kernel before it).  With swiglu16 (gate/up
+// pairs in consecutive rows), no K split and the epilogue writes
+// fp16(silu(gate) * up) to swiglu16[t][n / 2] (row stride ld) instead of y.
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
-                bool add, int *err, cudaStream_t st, bool zeroed = false) {
+                bool add, int *err, cudaStream_t st, bool zeroed = false, __half *swiglu16 = nullptr) {
     if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
     const int bn = gemm_bn(T);
-    const int split = gemm_split(n_rows, k, T);
+    const int split = swiglu16 ? 1 : gemm_split(n_rows, k, T);
     GemmArgs a;
     a.w = w;
     a.n_rows = n_rows;
@@ -476,6 +478,8 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.atomic = (add || split > 1) ? 1 : 0;
     a.ksplit = split;
     a.err = err;
+    a.swiglu16 = swiglu16;
+    a.ld16 = swiglu16 ? ld : 0;
     if (!add && split > 1 && !zeroed) {
         if (ld == n_rows)
             CK(cudaMemsetAsync(y, 0, static_cast<size_t>(T) * ld * 4, st));
@@ -1539,7 +1543,7 @@ struct qtts_batch {
     float *rope_cos, *rope_sin;
     cudaStream_t stream;
     // per-call buffers
-    float *x, *qkv, *q32, *gu, *part, *hidden, *logits;
+    float *x, *qkv, *q32, *part, *hidden, *logits;
     __half *h16, *attn16, *act16, *hlast16;
     int *meta;  // token metadata and attention items
     size_t meta_bytes;
@@ -1620,7 +1624,6 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         {reinterpret_cast<void **>(&b->x), T * H * 4},
         {reinterpret_cast<void **>(&b->qkv), T * QKV_ROWS * 4},
         {reinterpret_cast<void **>(&b->q32), T * QDIM * 4},
-        {reinterpret_cast<void **>(&b->gu), T * GU_ROWS * 4},
         {reinterpret_cast<void **>(&b->part), static_cast<size_t>(max_seqs) * HKV * max_splits * 2 * PSTRIDE * 4},
         {reinterpret_cast<void **>(&b->hidden), static_cast<size_t>(max_seqs) * H * 4},
         {reinterpret_cast<void **>(&b->logits), static_cast<size_t>(max_seqs) * (b->head_rows > 0 ? b->head_rows : 1) * 4},
@@ -1700,7 +1703,6 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
         const DLayer &Ly = s->tlayers[l];
         // the split-K outputs (qkv, gu) are cleared by the norm before them
         const long long zq = gemm_split(QKV_ROWS, H, T) > 1 ? static_cast<long long>(T) * QKV_ROWS / 4 : 0;
-        const long long zg = gemm_split(GU_ROWS, H, T) > 1 ? static_cast<long long>(T) * GU_ROWS / 4 : 0;
         cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, zq)), dim3(256), 0, st, b->x, nullptr, T,
                                    Ly.in_norm, eps, b->h16, nullptr, b->qkv, zq);
         if (e != cudaSuccess) {
@@ -1723,20 +1725,15 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
             return;
         }
         if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
-        e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, zg)), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm,
-                       eps, b->h16, nullptr, b->gu, zg);
+        e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, 0)), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm,
+                       eps, b->h16, nullptr, nullptr, 0ll);  // gate/up: no K split, SwiGLU in its epilogue
         if (e != cudaSuccess) {
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
             return;
         }
-        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, b->gu, GU_ROWS, false, b->err, st, true))) return;
-        const long long np = static_cast<long long>(T) * INTER;
-        e = launch_pdl(swiglu_f16_kernel, dim3(static_cast<unsigned>((np + 255) / 256)), dim3(256), 0, st,
-                       static_cast<const float *>(b->gu), np, b->act16);
-        if (e != cudaSuccess) {
-            rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
+        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, nullptr, INTER, false, b->err, st, true,
+                       b->act16)))
             return;
-        }
         if ((rc = gemm(Ly.wd, wdt, H, INTER, b->act16, T, cap, b->x, H, true, b->err, st))) return;
     }
     if (rc == QTTS_OK && cudaGetLastError() != cudaSuccess)

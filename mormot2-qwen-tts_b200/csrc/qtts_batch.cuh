@@ -1,7 +1,8 @@
 // qtts_batch.cuh -- the batched forward of libqtts (sm_100a): many sequences
 // (utterances) through one stack per call, the projections on the tcgen05
 // GEMM (qtts_gemm.cuh), the rest here: RMSNorm to fp16, q/k-norm + RoPE +
-// append into a paged KV cache, causal GQA attention over the pages, SwiGLU.
+// append into a paged KV cache, causal GQA attention over the pages (SwiGLU
+// is in the gate/up GEMM epilogue).
 //
 // Paged KV cache: pages of 16 positions; a page holds, for every layer, K and
 // V of the 8 KV heads: [page][layer][k|v][head][16][128], in float32 or bf16.
@@ -419,17 +420,6 @@ __global__ void attn_combine_kernel(const int *first, const int *count, const in
     __half *dst = attn16 + static_cast<size_t>(tok[call]) * QDIM + qh * HD + 4 * lane;
     *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
     *reinterpret_cast<__half2 *>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
-}
-
-// act16[t][j] = fp16(silu(gate) * up); gate j and up j are columns 2j, 2j+1
-__global__ void swiglu_f16_kernel(const float *gu, long long n_pairs, __half *act16) {
-    pdl_trigger();
-    pdl_wait();
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n_pairs) return;
-    const float2 gv = *reinterpret_cast<const float2 *>(gu + 2 * i);
-    const float s = gv.x / (1.0f + expf(-gv.x));
-    act16[i] = __float2half_rn(s * gv.y);
 }
 
 // ------------------------------------------------------------------ batched frames

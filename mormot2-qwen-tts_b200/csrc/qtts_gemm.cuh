@@ -12,14 +12,15 @@
 //    layout (gemm_tile_pack_kernel): the 128 rows x 64 k of one stage are one
 //    contiguous chunk (Q8_0: 8192 int8 + 256 fp16 scales = 8704 bytes), so
 //    one bulk copy (cp.async.bulk) brings a stage's weights into shared
-//    memory; warps 0-3 (one weight row per thread) dequantise it there to
-//    fp16 (w = q * d, rounded once) in the UMMA K-major 128B-swizzle layout,
-//    fence.proxy.async, then an mbarrier arrival.
+//    memory; warps 0-7 (two threads per weight row, 32 k each) dequantise it
+//    there to fp16 (w = q * d, rounded once) in the UMMA K-major 128B-swizzle
+//    layout, fence.proxy.async, then an mbarrier arrival.
 //  - B operand (activations, fp16 [T][K]): one TMA tiled load per stage
-//    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast).
+//    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast); warp 8 lane 0
+//    issues both copies of a stage.
 //  - MMA: one thread issues tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 ->
 //    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage) and tcgen05.commit frees the
-//    stage; the accumulator (BN TMEM columns) is read back by warps 4-7 with
+//    stage; the accumulator (BN TMEM columns) is read back by warps 8-11 with
 //    tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31 = its weight rows).
 //  - every mbarrier wait is bounded; a timeout sets the error word.
 #pragma once
@@ -33,7 +34,8 @@ namespace qtts {
 
 constexpr int G_BM = 128;           // weight rows per CTA tile
 constexpr int G_BK = 64;            // K per stage (128 bytes of fp16)
-constexpr int G_THREADS = 256;
+constexpr int G_THREADS = 384;   // warps 0-7 dequantise, 8 loads, 9 issues MMAs, 8-11 read TMEM back
+constexpr int G_DQ = 256;        // dequantising threads: 2 per weight row
 constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
 
 // one tile-packed chunk: 128 rows x 64 k.  The values are grouped by 8 k:
@@ -59,6 +61,9 @@ struct GemmArgs {
     int atomic;        // add into out (split-K and/or residual) instead of storing
     int ksplit;        // K blocks per split = (K / G_BK) / ksplit
     int *err;          // error word (QTTS_E_TIMEOUT on a wait that gave up)
+    __half *swiglu16;  // non-NULL (no K split): rows are gate/up pairs (2j, 2j+1) and the
+                       // epilogue writes fp16(silu(gate) * up) to swiglu16[t * ld16 + j]
+    int ld16;
 };
 
 template <int WDT, int BN>
@@ -183,14 +188,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&sm->full_raw[s], 1);
-            mbar_init(&sm->full_a[s], 128);
+            mbar_init(&sm->full_a[s], G_DQ);
             mbar_init(&sm->full_b[s], 1);
             mbar_init(&sm->empty[s], 1);
         }
         mbar_init(&sm->accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 5) {  // TMEM: BN f32 columns for the 128 x BN accumulator
+    if (warp == 9) {  // TMEM: BN f32 columns for the 128 x BN accumulator
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
                      "n"(BN)
                      : "memory");
@@ -205,9 +210,10 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // timeout), so no bulk copy lands in shared memory of a later CTA
     int issued = 0;
 
-    if (warp < 4) {
-        // ---- dequantisers: thread = weight row of the tile
-        const int r = tid;
+    if (warp < 8) {
+        // ---- dequantisers: two threads per weight row of the tile, 4 of
+        // the 8 groups of 8 k each
+        const int r = tid & (G_BM - 1), c0 = (tid >> 7) * 4;
         for (int i = 0; i < kb_n; ++i) {
             const int s = i % S;
             if (!mbar_wait(&sm->full_raw[s], (i / S) & 1, nullptr)) {
@@ -223,7 +229,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 d2hi = __high2half2(dd);
             }
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 8 groups of 8 k
+            for (int c = c0; c < c0 + 4; ++c) {  // 4 groups of 8 k
                 __half2 h[4];
                 if (WDT == WDT_Q8) {
                     // q + 128 in the mantissa of fp16 1024 (exact), minus 1152,
@@ -250,7 +256,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&sm->full_a[s]);
         }
-    } else if (warp == 4) {
+    } else if (warp == 8) {
         // ---- producer: the weight chunk (bulk copy) and the activations (TMA)
         if (lane == 0) {
             const uint8_t *wt = args.w + (static_cast<size_t>(blockIdx.x) * kb_total + kb0) * CHUNK;
@@ -277,7 +283,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 issued = i + 1;  // (a break happens at i >= S: every stage before it has both copies)
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ---- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(G_BM, BN);
@@ -298,12 +304,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             umma_commit(&sm->accum);
         }
     }
-    // ---- epilogue: warps 4-7, TMEM lane quarter = warp % 4
-    if (warp >= 4) {
+    // ---- epilogue: warps 8-11, TMEM lane quarter = warp % 4
+    if (warp >= 8) {
         pdl_wait();  // out may be written by the previous kernels
         const bool good = mbar_wait(&sm->accum, 0, nullptr);
         if (!good) gemm_fail(args.err);
-        __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of warps 4/5 had other work
+        __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of warps 8/9 had other work
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int q = warp & 3;
         const int n = row0 + 32 * q + lane;
@@ -311,6 +317,21 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         for (int c = 0; c < BN; c += 32) {
             float v[32];
             tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
+            if (args.swiglu16) {
+                // the up row of a pair is the next lane: SiLU(gate) * up, as
+                // the separate SwiGLU kernel computes it
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                    const int t = tok0 + c + j;
+                    if (good && n < args.n_rows && (lane & 1) == 0 && t < args.T) {
+                        const float g = v[j];
+                        const float sl = g / (1.0f + expf(-g));
+                        args.swiglu16[static_cast<size_t>(t) * args.ld16 + (n >> 1)] = __float2half_rn(sl * up);
+                    }
+                }
+                continue;
+            }
             if (good && n < args.n_rows) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -326,7 +347,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
         }
     }
-    if (warp == 4 && lane == 0) {
+    if (warp == 8 && lane == 0) {
         // drain: wait (bounded) for the copies of the last S issued stages
         for (int i = issued > S ? issued - S : 0; i < issued; ++i) {
             const int s = i % S;
@@ -338,7 +359,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(BN) : "memory");
     }
