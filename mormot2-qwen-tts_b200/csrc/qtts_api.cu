@@ -425,6 +425,10 @@ static int gemm_init(qtts_device *dev) {
     if ((rc = gemm_attr<WDT_Q8, 64>()) || (rc = gemm_attr<WDT_Q8, 128>()) || (rc = gemm_attr<WDT_Q8, 256>()) ||
         (rc = gemm_attr<WDT_F32, 64>()) || (rc = gemm_attr<WDT_F32, 128>()) || (rc = gemm_attr<WDT_F32, 256>()))
         return rc;
+    CK(cudaFuncSetAttribute(attn_prefill_tc_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(sizeof(TaSmem) + 1024)));
+    CK(cudaFuncSetAttribute(attn_prefill_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(sizeof(TaSmem) + 1024)));
     CK(cudaFuncSetAttribute(attn_decode_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             static_cast<int>(sizeof(DecodeSmem<float>))));
     CK(cudaFuncSetAttribute(attn_decode_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1689,8 +1693,9 @@ static unsigned norm_grid(int rows, long long nzero4) {
 
 template <class KVT>
 static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pitems, int nditems,
-                         const AttnItem *ditems, const int *tok_seq, const int *tok_pos, int ncomb, const int *cfirst,
-                         const int *ccount, const int *ctok, int wdt, cudaStream_t st, int &rc) {
+                         const AttnItem *ditems, int ntitems, const AttnItem *titems, const int *tok_seq,
+                         const int *tok_pos, int ncomb, const int *cfirst, const int *ccount, const int *ctok, int wdt,
+                         cudaStream_t st, int &rc) {
     const qtts_stack *s = b->stack;
     KVPool<KVT> pool;
     pool.base = static_cast<KVT *>(b->pool);
@@ -1714,6 +1719,9 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
                        Ly.k_norm, eps, b->rope_cos, b->rope_sin, b->q32, pool, l);
         if (e == cudaSuccess && npitems > 0)
             e = launch_pdl(attn_kernel<KVT>, dim3(npitems), dim3(ATHREADS), 0, st, pitems, b->q32, pool, l, b->attn16);
+        if (e == cudaSuccess && ntitems > 0)
+            e = launch_pdl(attn_prefill_tc_kernel<KVT>, dim3(ntitems), dim3(TA_THREADS), sizeof(TaSmem) + 1024, st,
+                           titems, static_cast<const float *>(b->q32), pool, l, b->attn16, b->err);
         if (e == cudaSuccess && nditems > 0)
             e = launch_pdl(attn_decode_kernel<KVT>, dim3(nditems), dim3(DTHREADS), sizeof(DecodeSmem<KVT>), st, ditems,
                            b->q32, pool, l, b->attn16, b->part, b->err);
@@ -1746,11 +1754,11 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
 // rows (one new row of a sequence) get `dsplits` page-aligned context splits
 // each (0: one split per DSPLIT keys).
 struct BatchPlan {
-    int nseq, T, np, nd, ncomb, ring;  // ring: slot of the ring, -1 = fixed slot
-    size_t meta_ints, o_ditems, o_cf, o_cc, o_ct, o_last;
+    int nseq, T, np, nd, ntc, ncomb, ring;  // ring: slot of the ring, -1 = fixed slot
+    size_t meta_ints, o_ditems, o_titems, o_cf, o_cc, o_ct, o_last;
     const int *hm;                     // pinned: meta | page table
     bool same_shape(const BatchPlan &o) const {
-        return nseq == o.nseq && T == o.T && np == o.np && nd == o.nd && ncomb == o.ncomb &&
+        return nseq == o.nseq && T == o.T && np == o.np && nd == o.nd && ntc == o.ntc && ncomb == o.ncomb &&
                meta_ints == o.meta_ints && hm == o.hm;
     }
 };
@@ -1788,7 +1796,7 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
     }
     // metadata: tokens, attention items, combine lists
     std::vector<int> tok_seq(T), tok_pos(T), last(nseq);
-    std::vector<AttnItem> pitems, ditems;
+    std::vector<AttnItem> pitems, ditems, titems;
     std::vector<int> cfirst, ccount, ctok;
     int t = 0, nparts = 0;
     for (int i = 0; i < nseq; ++i) {
@@ -1821,6 +1829,11 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
                 }
             }
             if (S > 1) ctok.push_back(t);
+        } else if (n > TC_MIN_ROWS) {
+            // long runs of new rows: tensor-core attention, per query head
+            for (int qa = 0; qa < n; qa += TA_ROWS)
+                for (int qh = 0; qh < HQ; ++qh)
+                    titems.push_back({t, L0, qa, qa + TA_ROWS < n ? qa + TA_ROWS : n, qh, 0, L0 + n, sq, -1});
         } else {
             for (int qa = 0; qa < n; qa += AQB)
                 for (int h = 0; h < HKV; ++h)
@@ -1839,6 +1852,9 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
     P->o_ditems = meta.size();
     ip = reinterpret_cast<const int *>(ditems.data());
     meta.insert(meta.end(), ip, ip + ditems.size() * (sizeof(AttnItem) / 4));
+    P->o_titems = meta.size();
+    ip = reinterpret_cast<const int *>(titems.data());
+    meta.insert(meta.end(), ip, ip + titems.size() * (sizeof(AttnItem) / 4));
     P->o_cf = meta.size();
     meta.insert(meta.end(), cfirst.begin(), cfirst.end());
     P->o_cc = meta.size();
@@ -1873,6 +1889,7 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
     P->T = T;
     P->np = static_cast<int>(pitems.size());
     P->nd = static_cast<int>(ditems.size());
+    P->ntc = static_cast<int>(titems.size());
     P->ncomb = static_cast<int>(ctok.size());
     P->meta_ints = meta.size();
     for (int i = 0; i < nseq; ++i) b->len[seqs[i]] += rows[i];
@@ -1902,12 +1919,13 @@ static int batch_enqueue(qtts_batch *b, const BatchPlan &P, const float *x, bool
     const int *m = b->meta;
     const AttnItem *d_pitems = reinterpret_cast<const AttnItem *>(m + 2 * P.T);
     const AttnItem *d_ditems = reinterpret_cast<const AttnItem *>(m + P.o_ditems);
+    const AttnItem *d_titems = reinterpret_cast<const AttnItem *>(m + P.o_titems);
     if (b->kv_dtype == QTTS_DTYPE_F32)
-        batch_layers<float>(b, P.T, P.np, d_pitems, P.nd, d_ditems, m, m + P.T, P.ncomb, m + P.o_cf, m + P.o_cc,
-                            m + P.o_ct, wdt, st, rc);
+        batch_layers<float>(b, P.T, P.np, d_pitems, P.nd, d_ditems, P.ntc, d_titems, m, m + P.T, P.ncomb, m + P.o_cf,
+                            m + P.o_cc, m + P.o_ct, wdt, st, rc);
     else
-        batch_layers<__nv_bfloat16>(b, P.T, P.np, d_pitems, P.nd, d_ditems, m, m + P.T, P.ncomb, m + P.o_cf,
-                                    m + P.o_cc, m + P.o_ct, wdt, st, rc);
+        batch_layers<__nv_bfloat16>(b, P.T, P.np, d_pitems, P.nd, d_ditems, P.ntc, d_titems, m, m + P.T, P.ncomb,
+                                    m + P.o_cf, m + P.o_cc, m + P.o_ct, wdt, st, rc);
     if (rc) return rc;
     const int hr = head >= 0 ? b->heads->mats[head].rows : 0;
     const long long zl = head >= 0 && gemm_split(hr, H, P.nseq) > 1 ? static_cast<long long>(P.nseq) * hr / 4 : 0;

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include "qtts_decode.cuh"
+#include "qtts_gemm.cuh"
 
 namespace qtts {
 
@@ -578,6 +579,249 @@ __global__ void frames_choose0_kernel(const int *seqs, const float *logits, cons
         ss[s].done = code == eos ? 1 : 0;
         if (!start) ss[s].step += 1;
         done[i] = code == eos ? 1 : 0;
+    }
+}
+
+// ------------------------------------------------------------------ prefill attention (tensor cores)
+//
+// Causal attention of long runs of new rows (prefill) on the 5th-generation
+// tensor cores, flash-attention style.  One CTA (128 threads) per (sequence,
+// query head, block of up to 128 new rows); thread r owns query row r.
+//  - Q (128 rows x 128 dims), the K tile (128 keys x 128 dims) and the V tile
+//    transposed (128 dims x 128 keys) are converted to fp16 by the threads
+//    and stored in the UMMA K-major 128B-swizzle layout (two 64-element
+//    atoms along K, as the GEMM's A tile).
+//  - S = Q K^T: 8 x tcgen05.mma (M 128, N 128, K 16) into 128 TMEM columns;
+//    thread r reads its row back (tcgen05.ld), masks causally, updates its
+//    running (max, sum) in f32, rescales its row of the O accumulator in
+//    TMEM (tcgen05.ld / st) and writes P = exp(S - max) as fp16 into the
+//    A-operand layout; then O += P V^T: 8 more MMAs into the other 128
+//    TMEM columns.  After the last tile, O / sum goes to attn16 as fp16.
+//  - every mbarrier wait is bounded; a timeout sets the error word.
+constexpr int TA_ROWS = 128;   // query rows per CTA (MMA M)
+constexpr int TA_KEYS = 128;   // keys per tile (MMA N of S, K of P V^T)
+constexpr int TA_THREADS = 128;
+constexpr int TC_MIN_ROWS = 32;  // sequences with more new rows than this use this kernel
+constexpr int TA_TILE = TA_ROWS * HD * 2;  // 32 KB: one fp16 operand tile
+
+struct __align__(1024) TaSmem {
+    uint8_t q[TA_TILE];
+    uint8_t k[TA_TILE];
+    uint8_t vt[TA_TILE];
+    uint8_t p[TA_TILE];
+    uint64_t s_done, o_done;
+    uint32_t tmem_base;
+};
+
+// byte offset of element (row, kk) of a 128 x 128 fp16 operand tile in the
+// K-major 128B-swizzle layout (atoms of 64 K elements, 16 KB each)
+__device__ __forceinline__ uint32_t ta_off(int row, int kk) {
+    const int a = kk >> 6, c = kk & 63, j = c >> 3;
+    return a * (TA_ROWS * 128) + (row >> 3) * 1024 + (row & 7) * 128 + ((j ^ (row & 7)) << 4) + (c & 7) * 2;
+}
+// store 8 consecutive K elements (one 16-byte chunk) of row `row` from kk
+__device__ __forceinline__ void ta_store8(uint8_t *tile, int row, int kk, const float *v) {
+    __half2 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(tile + ta_off(row, kk)) = *reinterpret_cast<uint4 *>(h);
+}
+__device__ __forceinline__ float kv_val(const float *p) { return __ldg(p); }
+__device__ __forceinline__ float kv_val(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+        "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+        "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+        "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
+// thread 0: the 8 MMAs (K = 128 in steps of 16) of one 128 x 128 x 128 product
+__device__ __forceinline__ void ta_mma(uint32_t tmem_d, const uint8_t *a, const uint8_t *b, bool accumulate) {
+    const uint32_t idesc = umma_idesc_f16(TA_ROWS, TA_KEYS);
+#pragma unroll
+    for (int k = 0; k < HD / 16; ++k) {
+        const uint64_t da = umma_desc_sw128(a + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
+        const uint64_t db = umma_desc_sw128(b + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
+        umma_f16(tmem_d, da, db, idesc, (accumulate || k > 0) ? 1u : 0u);
+    }
+}
+
+template <class KVT>
+__global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
+                                                                       KVPool<KVT> pool, int layer, __half *attn16,
+                                                                       int *err) {
+    extern __shared__ __align__(1024) uint8_t ta_raw[];
+    TaSmem *sm = reinterpret_cast<TaSmem *>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&sm->s_done, 1);
+        mbar_init(&sm->o_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // S: columns [0, 128), O: [128, 256)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&sm->tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    pdl_trigger();
+    pdl_wait();
+    const AttnItem it = items[blockIdx.x];
+    const int qh = it.h, h = qh >> 1;          // query head, its kv head
+    const int nq = it.qb - it.qa;              // 1..128 rows
+    const int kend = it.L0 + it.qb;            // keys [0, kend) (causal)
+    const int r = tid;                         // this thread's query row
+    const int qpos = it.L0 + it.qa + r;
+    // Q: row r, 128 dims
+    {
+        const float *src = q32 + static_cast<size_t>(it.t0 + it.qa + (r < nq ? r : 0)) * QDIM + qh * HD;
+        for (int kk = 0; kk < HD; kk += 8) {
+            float v[8];
+            if (r < nq) {
+                const float4 a = load4(src + kk), b = load4(src + kk + 4);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+            }
+            ta_store8(sm->q, r, kk, v);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tm = sm->tmem_base, tm_s = tm, tm_o = tm + TA_KEYS;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+    float m_run = -INFINITY, l_run = 0.f;
+    bool failed = false;  // uniform over the CTA
+    uint64_t *pending = nullptr;  // the barrier of a wait that gave up
+    int t = 0;
+    for (int kt = 0; kt < kend; kt += TA_KEYS, ++t) {
+        // K tile: thread = key row; V^T tile: thread = dim row
+        {
+            const int kp = kt + r;
+            for (int kk = 0; kk < HD; kk += 8) {
+                float v[8];
+                if (kp < kend) {
+                    const KVT *kr = kv_at(pool, layer, it.seq, kp, 0, h) + kk;
+                    const float4 a = load4(kr), b = load4(kr + 4);
+                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+                }
+                ta_store8(sm->k, r, kk, v);
+            }
+            for (int kc = 0; kc < TA_KEYS; kc += 8) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int p = kt + kc + i;
+                    v[i] = p < kend ? kv_val(kv_at(pool, layer, it.seq, p, 1, h) + r) : 0.f;
+                }
+                ta_store8(sm->vt, r, kc, v);
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            ta_mma(tm_s, sm->q, sm->k, false);
+            umma_commit(&sm->s_done);
+        }
+        bool good = mbar_wait(&sm->s_done, t & 1, nullptr);
+        if (!good) pending = &sm->s_done;
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // row maximum of the masked, scaled scores (first pass over TMEM)
+        float mt = -INFINITY;
+        for (int c = 0; c < TA_KEYS; c += 32) {
+            float sv[32];
+            tmem_ld32(tm_s + lane_base + c, sv);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (kt + c + j <= qpos) mt = fmaxf(mt, sv[j] * scale);
+        }
+        const float m_new = fmaxf(m_run, mt);
+        const float corr = expf(m_run - m_new);  // 0 on the first tile
+        // P = exp(S - m) to the A-operand tile (second pass), row sum
+        float lt = 0.f;
+        for (int c = 0; c < TA_KEYS; c += 32) {
+            float sv[32];
+            tmem_ld32(tm_s + lane_base + c, sv);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float e = kt + c + j <= qpos ? expf(sv[j] * scale - m_new) : 0.f;
+                sv[j] = e;
+                lt += e;
+            }
+#pragma unroll
+            for (int g = 0; g < 4; ++g) ta_store8(sm->p, r, c + 8 * g, sv + 8 * g);
+        }
+        l_run = fmaf(l_run, corr, lt);
+        m_run = m_new;
+        if (t > 0) {
+            // rescale this row of the O accumulator
+            for (int c = 0; c < HD; c += 32) {
+                float ov[32];
+                tmem_ld32(tm_o + lane_base + c, ov);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) ov[j] *= corr;
+                tmem_st32(tm_o + lane_base + c, ov);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            ta_mma(tm_o, sm->p, sm->vt, t > 0);
+            umma_commit(&sm->o_done);
+        }
+        if (good && !mbar_wait(&sm->o_done, t & 1, nullptr)) {
+            good = false;
+            pending = &sm->o_done;
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (__syncthreads_or(!good)) {
+            failed = true;
+            break;
+        }
+    }
+    // O / sum of row r to attn16 (the TMEM loads are warp-wide: every lane
+    // takes part, the rows beyond the block only skip the store)
+    {
+        const float inv = 1.0f / l_run;
+        __half *dst = attn16 + static_cast<size_t>(it.t0 + it.qa + (r < nq ? r : 0)) * QDIM + qh * HD;
+        for (int c = 0; c < HD; c += 32) {
+            float ov[32];
+            tmem_ld32(tm_o + lane_base + c, ov);
+            if (!failed && r < nq) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                    *reinterpret_cast<__half2 *>(dst + c + j) = __floats2half2_rn(ov[j] * inv, ov[j + 1] * inv);
+            }
+        }
+    }
+    if (failed && pending) {
+        // a wait gave up: report it and wait (bounded) once more, so that no
+        // MMA still runs on this CTA's TMEM when it is freed
+        atomicCAS(err, 0, ERR_TIMEOUT);
+        mbar_wait(pending, t & 1, nullptr);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tm) : "memory");
     }
 }
 
