@@ -590,7 +590,7 @@ __global__ void frames_choose0_kernel(const int *seqs, const float *logits, cons
 //  - Q (128 rows x 128 dims), the K tile (128 keys x 128 dims) and the V tile
 //    transposed (128 dims x 128 keys) are converted to fp16 by the threads
 //    and stored in the UMMA K-major 128B-swizzle layout (two 64-element
-//    atoms along K, as the GEMM's A tile).
+//    atoms along K, as the GEMM's A tile); P takes the K tile's place.
 //  - S = Q K^T: 8 x tcgen05.mma (M 128, N 128, K 16) into 128 TMEM columns;
 //    thread r reads its row back (tcgen05.ld), masks causally, updates its
 //    running (max, sum) in f32, rescales its row of the O accumulator in
@@ -604,11 +604,11 @@ constexpr int TA_THREADS = 128;
 constexpr int TC_MIN_ROWS = 32;  // sequences with more new rows than this use this kernel
 constexpr int TA_TILE = TA_ROWS * HD * 2;  // 32 KB: one fp16 operand tile
 
+// 97 KB: two CTAs share an SM (and its 512 TMEM columns)
 struct __align__(1024) TaSmem {
     uint8_t q[TA_TILE];
-    uint8_t k[TA_TILE];
+    uint8_t kp[TA_TILE];  // the K tile, then (once S is computed) P
     uint8_t vt[TA_TILE];
-    uint8_t p[TA_TILE];
     uint64_t s_done, o_done;
     uint32_t tmem_base;
 };
@@ -652,7 +652,7 @@ __device__ __forceinline__ void ta_mma(uint32_t tmem_d, const uint8_t *a, const 
 }
 
 template <class KVT>
-__global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
+__global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
                                                                        KVPool<KVT> pool, int layer, __half *attn16,
                                                                        int *err) {
     extern __shared__ __align__(1024) uint8_t ta_raw[];
@@ -715,7 +715,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
 #pragma unroll
                     for (int i = 0; i < 8; ++i) v[i] = 0.f;
                 }
-                ta_store8(sm->k, r, kk, v);
+                ta_store8(sm->kp, r, kk, v);
             }
             for (int kc = 0; kc < TA_KEYS; kc += 8) {
                 float v[8];
@@ -732,7 +732,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
         __syncthreads();
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm_s, sm->q, sm->k, false);
+            ta_mma(tm_s, sm->q, sm->kp, false);
             umma_commit(&sm->s_done);
         }
         bool good = mbar_wait(&sm->s_done, t & 1, nullptr);
@@ -750,7 +750,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
         }
         const float m_new = fmaxf(m_run, mt);
         const float corr = expf(m_run - m_new);  // 0 on the first tile
-        // P = exp(S - m) to the A-operand tile (second pass), row sum
+        // P = exp(S - m) into the A-operand tile over K (the S product has
+        // completed: s_done), second pass over TMEM; row sum
         float lt = 0.f;
         for (int c = 0; c < TA_KEYS; c += 32) {
             float sv[32];
@@ -762,7 +763,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
                 lt += e;
             }
 #pragma unroll
-            for (int g = 0; g < 4; ++g) ta_store8(sm->p, r, c + 8 * g, sv + 8 * g);
+            for (int g = 0; g < 4; ++g) ta_store8(sm->kp, r, c + 8 * g, sv + 8 * g);  // K is consumed
         }
         l_run = fmaf(l_run, corr, lt);
         m_run = m_new;
@@ -782,7 +783,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
         __syncthreads();
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm_o, sm->p, sm->vt, t > 0);
+            ta_mma(tm_o, sm->kp, sm->vt, t > 0);
             umma_commit(&sm->o_done);
         }
         if (good && !mbar_wait(&sm->o_done, t & 1, nullptr)) {

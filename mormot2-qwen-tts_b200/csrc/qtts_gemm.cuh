@@ -41,9 +41,10 @@ constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
 // one tile-packed chunk: 128 rows x 64 k.  The values are grouped by 8 k:
 // [8 groups][128 rows][8 values] (so that thread r reads group c of its row
 // at a conflict-free address), then for Q8_0 the scales [128 rows][2 fp16]
-// of the two 32-blocks.
+// of the two 32-blocks.  Float32 weights are kept as fp16 here (the value
+// the tensor core multiplies, rounded once when the copy is made).
 __host__ __device__ constexpr int g_chunk_bytes(int wdt) {
-    return wdt == WDT_Q8 ? G_BM * G_BK + G_BM * 4 : G_BM * G_BK * 4;
+    return wdt == WDT_Q8 ? G_BM * G_BK + G_BM * 4 : G_BM * G_BK * 2;
 }
 // pipeline depth from the shared-memory budget (at most 6 stages)
 __host__ __device__ constexpr int g_stages(int wdt, int bn) {
@@ -112,9 +113,9 @@ __global__ void gemm_tile_pack_kernel(const uint8_t *src, int wdt, int n_rows, i
             lo = *reinterpret_cast<const float4 *>(row + k);
             hi = *reinterpret_cast<const float4 *>(row + k + 4);
         }
-        float4 *o = reinterpret_cast<float4 *>(chunk + (c * G_BM + r) * 32);
-        o[0] = lo;
-        o[1] = hi;
+        __half2 h[4] = {__floats2half2_rn(lo.x, lo.y), __floats2half2_rn(lo.z, lo.w), __floats2half2_rn(hi.x, hi.y),
+                        __floats2half2_rn(hi.z, hi.w)};
+        *reinterpret_cast<uint4 *>(chunk + (c * G_BM + r) * 16) = *reinterpret_cast<uint4 *>(h);
     }
 }
 
@@ -243,12 +244,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     h[2] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias), d2);
                     h[3] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias), d2);
                 } else {
-                    const float4 *v = reinterpret_cast<const float4 *>(raw + (c * G_BM + r) * 32);
-                    const float4 lo = v[0], hi = v[1];
-                    h[0] = __floats2half2_rn(lo.x, lo.y);
-                    h[1] = __floats2half2_rn(lo.z, lo.w);
-                    h[2] = __floats2half2_rn(hi.x, hi.y);
-                    h[3] = __floats2half2_rn(hi.z, hi.w);
+                    // fp16 already: the swizzled copy only
+                    *reinterpret_cast<uint4 *>(h) = *reinterpret_cast<const uint4 *>(raw + (c * G_BM + r) * 16);
                 }
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(h);
             }
