@@ -339,13 +339,14 @@ def prefill_measure(args, qtts, torch, m, dev, rank):
     th.free()
     # FLOPs of one prefill: the projections of every row (2 per weight) and
     # causal attention (QK and PV, 2 x 2 per query head, key and dim)
-    proj = 2.0 * LAYER_CELLS * 28 * T + 2.0 * 3072 * 1024 * PREFILL_SEQS
-    att = 28 * 16 * 128 * 4.0 * float(sum(int(n) * (int(n) + 1) // 2 for n in lens))
+    L = len(m["tl"])
+    proj = 2.0 * LAYER_CELLS * L * T + 2.0 * 3072 * 1024 * PREFILL_SEQS
+    att = L * 16 * 128 * 4.0 * float(sum(int(n) * (int(n) + 1) // 2 for n in lens))
     peaks = measured_peaks()
     peak = peaks["bf16_tflops"] if peaks else 1590.0
     achieved = (proj + att) / dt / 1e12
     return {"workload": f"configs[3]: prefill of {PREFILL_SEQS} prompts U({PREFILL_LEN[0]},{PREFILL_LEN[1]}) rows "
-                        f"({T} rows), 28-layer talker, f32 weights, fp16 activations, f32 softmax, f32 KV",
+                        f"({T} rows), {L}-layer talker, f32 weights, fp16 activations, f32 softmax, f32 KV",
             "metric": "prefill tokens/s per GPU", "value": T / dt, "unit": "tokens/s", "ms_per_step": dt * 1000.0,
             "steps": K, "rows": T,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -396,8 +397,17 @@ def gpu_arm(args, rank, world, local_rank):
             dist.destroy_process_group()
         return
     prefill = None
-    if args.prefill_steps > 0 and rank == 0 and (args.talker_layers, args.pred_layers) == (28, 5):
+    if args.prefill_steps > 0 and rank == 0 and (args.talker_layers, args.pred_layers) == (28, 5) or args.only_prefill:
         prefill = prefill_measure(args, qtts, torch, m, dev, rank)
+    if args.only_prefill:
+        # the configs[3] measurement alone (profiling runs)
+        print(json.dumps({"impl": "ours", "prefill": prefill}), flush=True)
+        for o in (th, ph):
+            o.free()
+        for st in (tstack, pstack):
+            qtts.stack_destroy(st)
+        dev.close()
+        return
     tlm = qtts.QwenLm(tstack, th, max_pos)
     plm = qtts.QwenLm(pstack, ph, 32)
     tk = qtts.QwenTalker(tlm, plm, m["ce"], m["pe"], synth.CODEC_EOS)
@@ -528,6 +538,7 @@ def main():
     ap.add_argument("--only-batched", action="store_true", help="run the configs[2] measurement alone")
     # configs[3] beside the bench line: batched prefill steps (0: off)
     ap.add_argument("--prefill-steps", type=int, default=2)
+    ap.add_argument("--only-prefill", action="store_true", help="run the configs[3] measurement alone")
     # smaller stacks for profiler captures only (the benchmark is 28 + 5)
     ap.add_argument("--talker-layers", type=int, default=28)
     ap.add_argument("--pred-layers", type=int, default=5)
