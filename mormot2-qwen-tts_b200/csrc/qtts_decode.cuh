@@ -312,12 +312,19 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // ------------------------------------------------------------------ shared memory
 
+// Matrix phases in program order.  The producer and the compute warps walk
+// the same order; it must not depend on data.  The matrices before M_HEAD
+// have a fixed shape (their slices are computed once per launch).
+enum Mat { M_QKV, M_O, M_OH, M_GU, M_D, M_HEAD };
+constexpr int M_FIXED = M_HEAD;
+
 struct __align__(128) Smem {
     uint8_t ring[NSTAGES][STAGE_BYTES];
     float act[ACT_FLOATS];            // GEMV activations; attention scratch
     float kv[2][ATT_TILE][HD];        // attention K / V tile
     float xs[RMAX][XS_MAX];           // this CTA's rows of the residual stream
     float part[MAX_PARTS * RMAX];     // GEMV partial sums of the slice
+    int slice[M_FIXED][2];            // rows [r0, r1) of each fixed matrix owned by this CTA
     float red[NWARPS * RMAX];
     unsigned long long keys[NWARPS];
     uint64_t full[NSTAGES];
@@ -335,10 +342,6 @@ struct __align__(128) Smem {
 #define named_or(v) cta_or(v)
 
 // ------------------------------------------------------------------ program walk
-
-// Matrix phases in program order.  The producer and the compute warps walk
-// the same order; it must not depend on data.
-enum Mat { M_QKV, M_O, M_OH, M_GU, M_D, M_HEAD };
 
 __device__ __forceinline__ int mat_rows(Mat m, int head_rows) {
     switch (m) {
@@ -614,32 +617,45 @@ struct Compute {
     }
 
     // the attention output of all 16 query heads: combine the S partials of
-    // each (row, head): o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-    __device__ void stage_attn(int R, int S) {
+    // each (row, head): o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+    // A warp per (row, head): lane s brings (m_s, l_s) (S <= 32), lane d
+    // dims 4d..4d+3 of 4 splits per round trip.
+    __device__ __forceinline__ void stage_attn(int R, int S) {
         const size_t split_stride = static_cast<size_t>(RMAX) * 2 * PSTRIDE;
-        for (int idx = tid; idx < R * HQ * (HD / 4); idx += NCT) {
-            const int r = idx / (HQ * (HD / 4));
-            const int rem = idx - r * HQ * (HD / 4);
-            const int qh = rem / (HD / 4), d4 = rem - qh * (HD / 4);
+        for (int task = warp; task < R * HQ; task += NCW) {
+            const int r = task / HQ, qh = task - r * HQ;
             const int h = qh >> 1, q = qh & 1;
             const float *base = job->s.part + ((static_cast<size_t>(h) * S * RMAX + r) * 2 + q) * PSTRIDE;
-            float M = -INFINITY;
-            for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * split_stride + HD));
-            float L = 0.f;
+            float ms = -INFINITY, ls = 0.f;
+            if (lane < S) {
+                const float2 u = __ldcg(reinterpret_cast<const float2 *>(base + lane * split_stride + HD));
+                ms = u.x;
+                ls = u.y;
+            }
+            float M = ms;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float e = ms == -INFINITY ? 0.f : expf(ms - M);
+            const float L = warp_sum(ls * e);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s = 0; s < S; ++s) {
-                const float *ps = base + s * split_stride;
-                const float ms = __ldcg(ps + HD);
-                const float e = ms == -INFINITY ? 0.f : expf(ms - M);
-                L = fmaf(__ldcg(ps + HD + 1), e, L);
-                const float4 o = ldcg4(ps + 4 * d4);
-                acc.x = fmaf(o.x, e, acc.x);
-                acc.y = fmaf(o.y, e, acc.y);
-                acc.z = fmaf(o.z, e, acc.z);
-                acc.w = fmaf(o.w, e, acc.w);
+            for (int s0 = 0; s0 < S; s0 += 4) {
+                float4 o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (s0 + j < S) o[j] = ldcg4(base + (s0 + j) * split_stride + 4 * lane);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float es = __shfl_sync(0xffffffffu, e, (s0 + j) & 31);
+                    if (s0 + j < S) {
+                        acc.x = fmaf(o[j].x, es, acc.x);
+                        acc.y = fmaf(o[j].y, es, acc.y);
+                        acc.z = fmaf(o[j].z, es, acc.z);
+                        acc.w = fmaf(o[j].w, es, acc.w);
+                    }
+                }
             }
             const float inv = 1.0f / L;
-            *reinterpret_cast<float4 *>(sm->act + r * QDIM + qh * HD + 4 * d4) =
+            *reinterpret_cast<float4 *>(sm->act + r * QDIM + qh * HD + 4 * lane) =
                 make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         }
         named_sync();
@@ -649,6 +665,17 @@ struct Compute {
 
     // Epilogue kinds
     enum Epi { E_STORE, E_RESID, E_SWIGLU, E_HEAD, E_HEAD0 };
+
+    // rows [r0, r1) of matrix m owned by this CTA (the fixed matrices from
+    // the table filled at the start of the launch)
+    __device__ __forceinline__ void slice_of(Mat m, int head_rows, int &r0, int &r1) const {
+        if (m < M_FIXED) {
+            r0 = sm->slice[m][0];
+            r1 = sm->slice[m][1];
+        } else {
+            mat_slice(m, head_rows, blockIdx.x, gridDim.x, r0, r1);
+        }
+    }
 
     // GEMV over this CTA's slice of matrix m; activations staged in sm->act
     // as [R][K].  Work items are (row pair, 1024-wide K segment), the
@@ -663,14 +690,22 @@ struct Compute {
     //  E_SWIGLU: out[r*ld + row/2] = silu(y_gate) * y_up
     //  E_HEAD / E_HEAD0: out[row] = y (R == 1), the CTA's argmax key to
     //  job->s.arg; E_HEAD0 applies ChooseCode0's processors first.
+    //  RR: activation rows the dot-product loop is compiled for (1, or RMAX
+    //  with the rows past R skipped): gemv() dispatches on R.
     template <int K>
-    __device__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld, float eps) {
+    __device__ __forceinline__ void gemv(Mat m, int head_rows, int R, int kind, float *out, int ld, float eps) {
+        if (R == 1)
+            gemv_rr<K, 1>(m, head_rows, R, kind, out, ld, eps);
+        else
+            gemv_rr<K, RMAX>(m, head_rows, R, kind, out, ld, eps);
+    }
+    template <int K, int RR>
+    __device__ __forceinline__ void gemv_rr(Mat m, int head_rows, int R, int kind, float *out, int ld, float eps) {
         constexpr int SEGW = K < 1024 ? K : 1024;  // K segment of one item
         constexpr int SEG = K / SEGW;
         const int rb = row_bytes(WDT, K);
-        const int n = mat_rows(m, head_rows);
         int r0, r1;
-        mat_slice(m, n, blockIdx.x, gridDim.x, r0, r1);
+        slice_of(m, head_rows, r0, r1);
         const int nrows = r1 - r0;
         const int sr = stage_rows(WDT, K, m);
         const int nchunks = (nrows + sr - 1) / sr;
@@ -699,9 +734,9 @@ struct Compute {
                 const bool two = ra + 1 < nr;
                 const uint8_t *rowa = base + ra * rb;
                 const uint8_t *rowb = two ? rowa + rb : rowa;
-                float aa[RMAX], ab[RMAX];
+                float aa[RR], ab[RR];
 #pragma unroll
-                for (int r = 0; r < RMAX; ++r) aa[r] = ab[r] = 0.f;
+                for (int r = 0; r < RR; ++r) aa[r] = ab[r] = 0.f;
 #pragma unroll
                     for (int g = 0; g < SEGW / 128; ++g) {
                         const int e = seg * SEGW + 128 * g + 4 * lane;  // first of this lane's 4 elements
@@ -717,8 +752,8 @@ struct Compute {
                             wb = *reinterpret_cast<const float4 *>(rowb + 4 * e);
                         }
 #pragma unroll
-                        for (int r = 0; r < RMAX; ++r) {
-                            if (r < R) {
+                        for (int r = 0; r < RR; ++r) {
+                            if (RR == 1 || r < R) {
                                 const float4 xv = *reinterpret_cast<const float4 *>(sm->act + r * K + e);
                                 float pa = wa.x * xv.x, pb = wb.x * xv.x;
                                 pa = fmaf(wa.y, xv.y, pa);
@@ -739,8 +774,8 @@ struct Compute {
                     }
                 const int row = ch * sr + ra;  // row within the slice
 #pragma unroll
-                for (int r = 0; r < RMAX; ++r) {
-                    if (r < R) {
+                for (int r = 0; r < RR; ++r) {
+                    if (RR == 1 || r < R) {
                         const float s = warp_sum2(aa[r], ab[r], lane);
                         if (lane == 0) sm->part[(row * SEG + seg) * RMAX + r] = s;
                         if (lane == 16 && two) sm->part[((row + 1) * SEG + seg) * RMAX + r] = s;
@@ -1193,6 +1228,11 @@ __device__ void compute(Smem *sm, const Job &job) {
     c.warp = threadIdx.x >> 5;
     c.lane = threadIdx.x & 31;
     mat_slice(M_D, H, blockIdx.x, gridDim.x, c.c0, c.c1);  // the rows of its down-projection slice
+    if (c.tid < M_FIXED) {
+        const Mat m = static_cast<Mat>(c.tid);
+        mat_slice(m, mat_rows(m, 0), blockIdx.x, gridDim.x, sm->slice[c.tid][0], sm->slice[c.tid][1]);
+    }
+    c.cta_sync();
     const Scratch &S = job.s;
     c.mark(1);
     if (job.mode == 0) {

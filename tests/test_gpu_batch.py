@@ -106,3 +106,31 @@ def test_batch_mixed_rows_and_errors(device):
     b.free()
     qtts.stack_destroy(st)
     heads.free()
+
+
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_prefill_after_context_tensor_cores(device, kv):
+    # the tensor-core prefill attention with cached positions before the new
+    # rows (L0 > 0), blocks of 128 rows with a ragged last block, and a run
+    # of <= 32 rows (CUDA-core path) in the same call
+    head = synth.talker_head(97)
+    st, heads, ost, oh = build(device, 97, 2, "q8_0", head)
+    b = qtts.QwenBatch(st, heads, max_seqs=3, max_tokens=700, max_pos=800, kv_dtype=kv)
+    first = [40, 130, 7]
+    second = [300, 261, 20]
+    p1 = [synth.prompt(500 + i, n) for i, n in enumerate(first)]
+    p2 = [synth.prompt(600 + i, n) for i, n in enumerate(second)]
+    b.forward([0, 1, 2], first, np.concatenate(p1))
+    lg, hd = b.forward([2, 0, 1], [second[2], second[0], second[1]], np.concatenate([p2[2], p2[0], p2[1]]))
+    atol, cmin = (2e-2, 0.9999) if kv == "f32" else (5e-2, 0.999)
+    lo = np.zeros(3072, np.float32)
+    for i, s in enumerate([2, 0, 1]):
+        o = O.OraLm(ost, oh, 800)
+        o.forward(p1[s], 0, lo)
+        o.forward(p2[s], 0, lo)
+        assert np.abs(lg[i] - lo).max() <= atol and cosine(lg[i], lo) >= cmin, (s, np.abs(lg[i] - lo).max())
+        o.free()
+    assert [b.length(s) for s in range(3)] == [340, 391, 27]
+    b.free()
+    qtts.stack_destroy(st)
+    heads.free()
