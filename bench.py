@@ -226,14 +226,28 @@ BATCH_CTX = (50, 1000)  # configs[2]: per-utterance context drawn uniformly
 KV_POS_BF16 = 8 * 128 * 2 * 2  # K + V of one position in one layer (bf16)
 
 
-def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist):
+BOX_BATCH = 128       # configs[4]: concurrent utterances per GPU
+BOX_PROMPT = (20, 80)  # configs[4]: prompt rows
+BOX_FRAMES = 300       # configs[4]: frames per utterance
+
+
+def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist, box=False):
     """B utterances (default 64) decoded together,
     Q8_0 weights, contexts drawn uniformly in [50, 1000] (prefilled through
     the batched path), paged bf16 KV cache; one step = one frame of every
     utterance (15 batched predictor steps + 1 batched talker step) through
-    qtts_talkers_next_frame, codes read back to the host each frame."""
-    B, K, W = args.batch, args.batch_steps, 3
-    lo, hi = args.batch_ctx
+    qtts_talkers_next_frame, codes read back to the host each frame.
+
+    box=True: configs[4], 128 concurrent utterances per GPU whose prompts of
+    U(20, 80) rows have generated half of their 300 frames: contexts
+    U(170, 230), the mean context of the whole generation; value = frames/s
+    of the box (all ranks)."""
+    if box:
+        B, K, W = BOX_BATCH, args.batch_steps, 3
+        lo, hi = BOX_PROMPT[0] + BOX_FRAMES // 2, BOX_PROMPT[1] + BOX_FRAMES // 2
+    else:
+        B, K, W = args.batch, args.batch_steps, 3
+        lo, hi = args.batch_ctx
     rng = np.random.default_rng(SEED + 7 + rank)
     ctx = rng.integers(lo, hi + 1, B)
     chunk = 16384
@@ -286,9 +300,15 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     peak = peaks["hbm_gbs"] if peaks else 6650.0
     achieved = (wb + kv) / (ms / 1000.0 / K) / 1e9
     extra = {} if (tl, pl) == (28, 5) else {"layers_override": f"talker {tl}, predictor {pl} (profiling case)"}
+    if box:
+        workload = (f"configs[4]: {B} concurrent utterances per GPU, prompts U{BOX_PROMPT} rows at frame "
+                    f"{BOX_FRAMES // 2} of {BOX_FRAMES} (contexts U({lo},{hi}), the generation's mean), Q8_0 weights, "
+                    "paged bf16 KV, fp16 activations on the tcgen05 GEMMs; a sample of the 1024 x 300-frame run")
+    else:
+        workload = (f"configs[2]: {B} utterances per GPU, contexts U({lo},{hi}), Q8_0 weights, "
+                    "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs")
     return {**extra,
-            "workload": f"configs[2]: {B} utterances per GPU, contexts U({lo},{hi}), Q8_0 weights, "
-                        "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs",
+            "workload": workload,
             "metric": "frames/s per GPU @B=%d" % B if world == 1 else "box frames/s @B=%d per GPU" % B,
             "value": world * frames / (ms / 1000.0), "unit": "frames/s", "steps": K, "warmup": W,
             "ms_per_batched_frame": ms / K, "frames": frames, "prefill_s_rank0": prefill_s,
@@ -380,9 +400,11 @@ def gpu_arm(args, rank, world, local_rank):
     pstack = qtts.qwen_lm_stack(dev, synth.CONFIG, m["pl"], m["pf"], dtype)
     # the batched frames share the stacks; they run first and
     # are freed before the lms take ownership of the stacks
-    batched = None
+    batched = box = None
     if args.batch > 0 and dtype == "q8_0":
         batched = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist)
+        if not args.only_batched and (args.talker_layers, args.pred_layers) == (28, 5):
+            box = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist, box=True)
     if args.only_batched:
         # the configs[2] measurement alone (profiling runs)
         if rank == 0:
@@ -508,6 +530,7 @@ def gpu_arm(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "restarts_at_eos": restarts,
             "batched": batched,
+            "box": box,
             "prefill": prefill,
             "weights_generation_s": m["gen_s"],
         }

@@ -252,6 +252,39 @@ int qtts_talker_probe(qtts_talker *t, float *logits, float *hidden);
 int qtts_talker_step(qtts_talker *t, int *step);
 int qtts_talker_destroy(qtts_talker *t);
 
+/* How each code is chosen: TQwenSampling (talker.pas:60-73), as read by
+ * QwenSamplingFromConfig (talker.pas:203-230; qwen_tts defaults: sampling
+ * on, temperature 0.9, top_k 50, top_p 1 for both the talker's code 0 and
+ * the predictor's codes).  do_sample = 0: greedy (the first maximum).  The
+ * draw replaces TInferSampler (mormot2-ai, NewSampler talker.pas:455-469):
+ * z = logit / temperature, the values >= the top_k-th largest, the nucleus
+ * of mass top_p in (z desc, index asc) order, an inverse-CDF draw whose
+ * uniform is a function of (seed, frame, code group) alone (frame = the
+ * index of the frame the code belongs to, group = 0 for code 0, g for the
+ * predictor's code g).  Limits: temperature > 0, 1 <= top_k <= 64,
+ * 0 < top_p <= 1. */
+typedef struct qtts_sampling {
+    int32_t do_sample;
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    int32_t sub_do_sample;
+    float sub_temperature;
+    int32_t sub_top_k;
+    float sub_top_p;
+    uint64_t seed;
+} qtts_sampling;
+
+/* The sampling of TQwenTalker (its fSampler / fSubSampler, talker.pas:
+ * 583-586) for the frames that follow; the draw of the first code 0 is made
+ * by qtts_talker_start, so set it before.  A new talker is greedy. */
+int qtts_talker_set_sampling(qtts_talker *t, const qtts_sampling *s);
+/* TInferSampler.Next (the draw of talker.pas:626-629, 632-638) on the
+ * device: the index drawn from work[n] (host float32 logits after the
+ * processors, n <= 4096) with draw (step, group) of the stream `seed`. */
+int qtts_sample(qtts_device *dev, const float *work, int n, float temperature, int top_k, float top_p,
+                uint64_t seed, int step, int group, int32_t *code);
+
 /* ------------------------------------------------------------------ talkers (batched frames) */
 
 typedef struct qtts_talkers qtts_talkers;

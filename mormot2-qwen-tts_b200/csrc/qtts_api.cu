@@ -160,6 +160,8 @@ struct qtts_talker {
     int *d_hist;  // codes of qtts_talker_run
     size_t hist_cap;
     int started;
+    SampleParams samp0, samp;  // code 0 / the predictor's codes (on = 0: greedy)
+    uint64_t seed;
 };
 
 // ------------------------------------------------------------------ kernels
@@ -291,6 +293,32 @@ __global__ void choose0_kernel(const float *logits, int vocab, int eos, FrameSta
         fs->hist_len = 0;
         fs->step = 0;
     }
+}
+
+// ChooseCode0 after the prefill with a draw (sampling mode): the values of
+// choose0_kernel, then the draw (0, 0) of the stream; NCT threads
+__global__ void __launch_bounds__(NCT) choose0_sample_kernel(const float *logits, int vocab, int eos, FrameState *fs,
+                                                             SampleParams p, float u) {
+    __shared__ SampleScratch ss;
+    const int c = sample_draw<NCT>(
+        [&](int i) {
+            const float w = logits[i];
+            return (i >= vocab - 1024 && i != eos) || i == eos ? -INFINITY : w;  // eos: fewer than 2 frames
+        },
+        vocab, p, u, &ss, static_cast<int>(threadIdx.x));
+    if (threadIdx.x == 0) {
+        fs->next_code0 = c;
+        fs->done = c == eos ? 1 : 0;
+        fs->hist_len = 0;
+        fs->step = 0;
+    }
+}
+
+// TInferSampler.Next on values already in device memory: NCT threads
+__global__ void __launch_bounds__(NCT) sample_kernel(const float *work, int n, SampleParams p, float u, int *code) {
+    __shared__ SampleScratch ss;
+    const int c = sample_draw<NCT>([&](int i) { return work[i]; }, n, p, u, &ss, static_cast<int>(threadIdx.x));
+    if (threadIdx.x == 0) *code = c;
 }
 
 // ------------------------------------------------------------------ helpers
@@ -1184,8 +1212,13 @@ extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows,
     std::vector<float> tmp(logits ? 0 : t->cfg.vocab);
     int rc = qtts_lm_forward(tl, prefill, rows, 0, logits ? logits : tmp.data(), hidden);
     if (rc) return rc;
-    // the first ChooseCode0 (empty history), then the frame state
-    choose0_kernel<<<1, 1024, 0, st>>>(tl->run.s.logits, t->cfg.vocab, t->cfg.codec_eos, t->fs);
+    // the first ChooseCode0 (empty history): the argmax or the draw (0, 0);
+    // then the frame state
+    if (t->samp0.on)
+        choose0_sample_kernel<<<1, NCT, 0, st>>>(tl->run.s.logits, t->cfg.vocab, t->cfg.codec_eos, t->fs, t->samp0,
+                                                 sample_uniform(t->seed, 0, 0));
+    else
+        choose0_kernel<<<1, 1024, 0, st>>>(tl->run.s.logits, t->cfg.vocab, t->cfg.codec_eos, t->fs);
     CK(cudaGetLastError());
     FrameState h;
     CK(cudaMemcpyAsync(&h, t->fs, sizeof(h), cudaMemcpyDeviceToHost, st));
@@ -1223,6 +1256,9 @@ static Job frame_job(qtts_talker *t) {
     j.eos = t->cfg.codec_eos;
     j.penalty = t->cfg.repetition_penalty;
     j.seen = t->seen;
+    j.samp0 = t->samp0;
+    j.samp = t->samp;
+    j.seed = t->seed;
     j.fs = t->fs;
     j.codes_hist = nullptr;
     j.codes_cap = 0;
@@ -1371,6 +1407,61 @@ extern "C" int qtts_talker_destroy(qtts_talker *t) {
     if (!t) return QTTS_OK;
     cudaSetDevice(t->talker->dev->ordinal);
     talker_free(t);
+    return QTTS_OK;
+}
+
+static int sampling_params(const char *who, int on, float temperature, int top_k, float top_p, SampleParams *out) {
+    out->on = on ? 1 : 0;
+    out->temperature = temperature;
+    out->top_k = top_k;
+    out->top_p = top_p;
+    if (!on) return QTTS_OK;
+    if (!(temperature > 0.0f) || top_k < 1 || top_k > SAMPLE_MAX_K || !(top_p > 0.0f) || !(top_p <= 1.0f))
+        return set_err(QTTS_E_ARG, "%s: temperature %g, top_k %d, top_p %g (need > 0, 1..%d, (0, 1])", who,
+                       static_cast<double>(temperature), top_k, static_cast<double>(top_p), SAMPLE_MAX_K);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_set_sampling(qtts_talker *t, const qtts_sampling *s) {
+    if (!t || !s) return set_err(QTTS_E_ARG, "qtts_talker_set_sampling: NULL argument");
+    SampleParams a, b;
+    int rc = sampling_params("qtts_talker_set_sampling", s->do_sample, s->temperature, s->top_k, s->top_p, &a);
+    if (rc) return rc;
+    rc = sampling_params("qtts_talker_set_sampling (predictor)", s->sub_do_sample, s->sub_temperature,
+                         s->sub_top_k, s->sub_top_p, &b);
+    if (rc) return rc;
+    if (t->cfg.vocab > SAMPLE_MAX_V || t->cfg.pred_vocab > SAMPLE_MAX_V)
+        return set_err(QTTS_E_ARG, "qtts_talker_set_sampling: vocabularies of %d / %d, at most %d", t->cfg.vocab,
+                       t->cfg.pred_vocab, SAMPLE_MAX_V);
+    t->samp0 = a;
+    t->samp = b;
+    t->seed = s->seed;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_sample(qtts_device *dev, const float *work, int n, float temperature, int top_k, float top_p,
+                           uint64_t seed, int step, int group, int32_t *code) {
+    if (!dev || !work || !code) return set_err(QTTS_E_ARG, "qtts_sample: NULL argument");
+    if (n <= 0 || n > SAMPLE_MAX_V) return set_err(QTTS_E_ARG, "qtts_sample: %d values (1..%d)", n, SAMPLE_MAX_V);
+    SampleParams p;
+    int rc = sampling_params("qtts_sample", 1, temperature, top_k, top_p, &p);
+    if (rc) return rc;
+    CK(cudaSetDevice(dev->ordinal));
+    float *d = nullptr;
+    int *dc = nullptr;
+    cudaError_t e = cudaMalloc(&d, static_cast<size_t>(n) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&dc, 4);
+    if (e == cudaSuccess) e = cudaMemcpy(d, work, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        sample_kernel<<<1, NCT>>>(d, n, p, sample_uniform(seed, step, group), dc);
+        e = cudaGetLastError();
+    }
+    int c = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&c, dc, 4, cudaMemcpyDeviceToHost);
+    if (d) cudaFree(d);
+    if (dc) cudaFree(dc);
+    if (e != cudaSuccess) return set_err(QTTS_E_CUDA, "qtts_sample: %s", cudaGetErrorString(e));
+    *code = c;
     return QTTS_OK;
 }
 

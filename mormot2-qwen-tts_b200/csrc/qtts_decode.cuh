@@ -41,6 +41,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "qtts_sample.cuh"
+
 namespace qtts {
 
 constexpr int H = 1024;                     // hidden
@@ -178,6 +180,10 @@ struct Job {
     int eos;
     float penalty;
     unsigned char *seen;     // [tvocab] codes already returned
+    // TQwenSampling (talker.pas:59-73): code 0 and the predictor's codes;
+    // draw (frame, group) of the stream `seed`
+    SampleParams samp0, samp;
+    unsigned long long seed;
     FrameState *fs;
     int *codes_hist;         // [cap][groups] codes by frame index (may be NULL)
     int codes_cap;
@@ -862,6 +868,17 @@ struct Compute {
         return s;
     }
 
+    // after a grid barrier: the code drawn from the logits of the last head
+    // (every compute thread of the CTA calls it; sm->act is the scratch);
+    // code 0 (talker) from the values after ChooseCode0's processors
+    __device__ int sample_code(int V, const SampleParams &p, float u, bool talker) {
+        SampleScratch *ss = reinterpret_cast<SampleScratch *>(sm->act);
+        const float *lg = job->s.logits;
+        if (talker)
+            return sample_draw<NCT>([&](int i) { return choose0_value(i, __ldcg(lg + i)); }, V, p, u, ss, tid);
+        return sample_draw<NCT>([&](int i) { return __ldcg(lg + i); }, V, p, u, ss, tid);
+    }
+
     // after a grid barrier: the winning index over all CTAs' keys
     __device__ int reduce_argmax() {
         unsigned long long b = 0ull;
@@ -1283,7 +1300,9 @@ __device__ void compute(Smem *sm, const Job &job) {
             c.head(job.pst, R, job.pvocab, Compute<WDT>::E_HEAD, nullptr);
             c.grid_sync(6);
             if (!c.ok) break;
-            code = c.reduce_argmax();
+            // ChooseCode (talker.pas:632-638): the draw (frame, group g + 1) or the argmax
+            code = job.samp.on ? c.sample_code(job.pvocab, job.samp, sample_uniform(job.seed, step, g + 1), false)
+                               : c.reduce_argmax();
             if (blockIdx.x == 0 && c.tid == 0) {
                 fs->codes[g + 1] = code;
                 if (job.codes_hist && step < job.codes_cap) job.codes_hist[step * job.groups + g + 1] = code;
@@ -1304,10 +1323,13 @@ __device__ void compute(Smem *sm, const Job &job) {
             c.stack(job.tst, job.tctx, 1, tlen, in0, in1, in2);
             if (c.ok) c.head(job.tst, 1, job.tvocab, Compute<WDT>::E_HEAD0, S.hidden);
             if (c.ok) c.grid_sync(8);
-            if (c.ok && blockIdx.x == 0 && c.warp == 0) {
-                // ChooseCode0 of the next frame; the history holds this frame's code 0
-                const int next = c.reduce_argmax();
-                if (c.lane == 0) {
+            if (c.ok && blockIdx.x == 0 && (job.samp0.on || c.warp == 0)) {
+                // ChooseCode0 of the next frame (its draw is (step + 1, 0));
+                // the history holds this frame's code 0
+                const int next = job.samp0.on ? c.sample_code(job.tvocab, job.samp0,
+                                                              sample_uniform(job.seed, step + 1, 0), true)
+                                              : c.reduce_argmax();
+                if (c.tid == 0) {
                     fs->next_code0 = next;
                     fs->done = next == job.eos ? 1 : 0;
                     fs->step = step + 1;

@@ -58,6 +58,13 @@ class TalkerConfig(ctypes.Structure):
                 ("codec_eos", ctypes.c_int32), ("repetition_penalty", ctypes.c_float)]
 
 
+class Sampling(ctypes.Structure):
+    """TQwenSampling (talker.pas:60-73)."""
+    _fields_ = [("do_sample", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_k", ctypes.c_int32),
+                ("top_p", ctypes.c_float), ("sub_do_sample", ctypes.c_int32), ("sub_temperature", ctypes.c_float),
+                ("sub_top_k", ctypes.c_int32), ("sub_top_p", ctypes.c_float), ("seed", ctypes.c_uint64)]
+
+
 P = ctypes.c_void_p
 I = ctypes.c_int
 PI = ctypes.POINTER(ctypes.c_int)
@@ -99,6 +106,8 @@ EXPORTS = {
     "qtts_talker_probe": [P, P, P],
     "qtts_talker_step": [P, PI],
     "qtts_talker_destroy": [P],
+    "qtts_talker_set_sampling": [P, ctypes.POINTER(Sampling)],
+    "qtts_sample": [P, P, I, ctypes.c_float, I, ctypes.c_float, ctypes.c_uint64, I, I, PI],
     "qtts_talkers_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
     "qtts_talkers_start": [P, I, P, P, P, P, P, P],
     "qtts_talkers_next_frame": [P, I, P, P, P],
@@ -164,6 +173,15 @@ class QwenDevice:
         v = ctypes.c_int64()
         check(lib().qtts_device_bytes(self.handle, ctypes.byref(v)))
         return v.value
+
+    def sample(self, work, temperature=0.9, top_k=50, top_p=1.0, seed=0, step=0, group=0):
+        """TInferSampler.Next on the device: the index drawn from work
+        (logits after the processors) with draw (step, group) of `seed`."""
+        w = _f32(work)
+        c = ctypes.c_int()
+        check(lib().qtts_sample(self.handle, _ptr(w), w.size, temperature, top_k, top_p, seed, step, group,
+                                ctypes.byref(c)))
+        return c.value
 
     def quantize_q8_0(self, x):
         """InferQuantizeRowQ8_0Ref on the device: float32 -> ggml blocks."""
@@ -361,7 +379,8 @@ def stack_destroy(stack):
 
 
 class QwenTalker:
-    """The per-frame device loop of TQwenTalker (talker.pas:471-681), greedy."""
+    """The per-frame device loop of TQwenTalker (talker.pas:471-681), greedy
+    or sampling (set_sampling)."""
 
     def __init__(self, talker, predictor, codec_emb, pred_emb, eos, vocab=3072, pred_vocab=2048, groups=16,
                  repetition_penalty=1.05):
@@ -374,6 +393,15 @@ class QwenTalker:
         self.groups = groups
         self.vocab = vocab
         self.hidden = talker.hidden
+
+    def set_sampling(self, do_sample=True, temperature=0.9, top_k=50, top_p=1.0, sub_do_sample=True,
+                     sub_temperature=0.9, sub_top_k=50, sub_top_p=1.0, seed=0):
+        """TQwenSampling for the frames that follow (call before start for
+        the first code 0); defaults of QwenSamplingFromConfig (talker.pas:
+        203-230)."""
+        s = Sampling(int(do_sample), temperature, top_k, top_p, int(sub_do_sample), sub_temperature, sub_top_k,
+                     sub_top_p, seed)
+        check(lib().qtts_talker_set_sampling(self.handle, ctypes.byref(s)))
 
     def start(self, prefill, trailing, tts_pad, logits=None, hidden=None):
         """The device part of TQwenTalker.Start: prefill rows, trailing text

@@ -72,6 +72,12 @@ def _load():
         "ora_talker_next_frame": (ctypes.c_int, [P, P]),
         "ora_talker_check_frame": (ctypes.c_int, [P, P, P]),
         "ora_talker_logits": (P, [P]),
+        "ora_talker_set_sampling": (None, [P, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                           ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                           ctypes.c_uint64]),
+        "ora_sample": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                      ctypes.c_float]),
+        "ora_sample_uniform": (ctypes.c_float, [ctypes.c_uint64, ctypes.c_int, ctypes.c_int]),
         "ora_talker_hidden": (P, [P]),
         "ora_rope_table": (None, [ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P]),
     }
@@ -136,6 +142,18 @@ def choose_code0(logits, eos, history, penalty=1.05):
     h = np.ascontiguousarray(history, dtype=np.int32)
     work = np.empty_like(lg)
     return lib.ora_choose_code0(_p(lg), lg.size, eos, _p(h) if h.size else None, h.size, penalty, _p(work))
+
+
+def sample_uniform(seed, step, group):
+    """u in [0, 1) of draw (step, group) of a stream (seed)."""
+    return lib.ora_sample_uniform(seed, step, group)
+
+
+def sample(work, temperature, top_k, top_p, u):
+    """TInferSampler.Next restated (qtts_oracle.c): the index drawn from
+    work (logits after the processors) with the uniform u."""
+    w = _f32(work)
+    return lib.ora_sample(_p(w), w.size, temperature, top_k, top_p, u)
 
 
 def rope_table(max_pos, head_dim, theta):
@@ -226,7 +244,8 @@ class OraLm:
 
 
 class OraTalker:
-    """TQwenTalker's frame loop (greedy) on the CPU."""
+    """TQwenTalker's frame loop (greedy, or sampling after set_sampling) on
+    the CPU."""
 
     def __init__(self, talker, theads, pred, pheads, codec_emb, pred_emb, eos, penalty=1.05, groups=16):
         self.ce = _f32(codec_emb)
@@ -238,6 +257,12 @@ class OraTalker:
                                             vocab, _p(self.pe), pvocab, groups, eos, penalty)
         self.hidden = talker.hidden
         self.vocab = vocab
+
+    def set_sampling(self, do_sample=True, temperature=0.9, top_k=50, top_p=1.0, sub_do_sample=True,
+                     sub_temperature=0.9, sub_top_k=50, sub_top_p=1.0, seed=0):
+        """TQwenSampling (talker.pas:59-73); defaults of qwen_tts (203-229)."""
+        lib.ora_talker_set_sampling(self.handle, int(do_sample), temperature, top_k, top_p, int(sub_do_sample),
+                                    sub_temperature, sub_top_k, sub_top_p, seed)
 
     def start(self, prefill, trailing, tts_pad):
         p = _f32(prefill)

@@ -588,6 +588,112 @@ int ora_choose_code0(const float *logits, int vocab, int eos, const int *history
     return ora_argmax(work, vocab);
 }
 
+/* ---------------------------------------------------------------- sampling */
+
+/* TInferSampler.Next (mormot2-ai, used at talker.pas:626-629 and 632-638;
+ * its source is absent here) restated after the logits warpers of
+ * transformers' generate, which the reference's options mirror
+ * (generation_config: temperature, top_k, top_p; talker.pas:203-229):
+ *   z = logit / temperature; keep the values >= the top_k-th largest (ties
+ *   kept, -inf never); order them by (z desc, index asc); keep the nucleus
+ *   whose probability mass before each kept value is < top_p (at least one);
+ *   draw by inverse CDF with u in [0, 1): the first value whose running sum
+ *   of exp(z - z_max), in that order, exceeds u * (sum over the nucleus).
+ * u comes from a counter-based generator: splitmix64 (Vigna's published
+ * finaliser) of seed + (16 * step + group + 1) * golden ratio, top 24 bits.
+ * The running sums are sequential in candidate order so that another
+ * implementation can repeat them exactly. */
+#define ORA_SAMPLE_MAX_K 64
+#define ORA_SAMPLE_MAX_CAND 128
+
+static uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+float ora_sample_uniform(uint64_t seed, int step, int group) {
+    uint64_t c = (uint64_t)step * 16u + (uint64_t)group + 1u;
+    uint64_t z = mix64(seed + c * 0x9E3779B97F4A7C15ull);
+    return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+/* orderable key of a float: larger value, larger key */
+static uint32_t okey(float z) {
+    uint32_t b;
+    memcpy(&b, &z, 4);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+static int cmp_u32_desc(const void *a, const void *b) {
+    uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
+    return x < y ? 1 : (x > y ? -1 : 0);
+}
+
+/* the index drawn from work[0..n) (logits after the processors) */
+int ora_sample(const float *work, int n, float temperature, int top_k, float top_p, float u) {
+    if (n <= 0) return 0;
+    uint32_t *keys = (uint32_t *)malloc((size_t)n * 4), *sk = (uint32_t *)malloc((size_t)n * 4);
+    float *z = (float *)malloc((size_t)n * 4);
+    for (int i = 0; i < n; i++) {
+        z[i] = work[i] / temperature;
+        keys[i] = sk[i] = okey(z[i]);
+    }
+    int k = top_k < 1 ? 1 : (top_k < n ? top_k : n);
+    qsort(sk, n, 4, cmp_u32_desc);
+    uint32_t thr = sk[k - 1];
+    free(sk);
+    int ci[ORA_SAMPLE_MAX_CAND], nc = 0, ncand = 0;
+    for (int i = 0; i < n; i++)
+        if (keys[i] >= thr && z[i] != -INFINITY) {
+            if (nc < ORA_SAMPLE_MAX_CAND) ci[nc++] = i;
+            ncand++;
+        }
+    /* no candidate (all -inf) or more ties than kept: the first maximum of z */
+    int code = ora_argmax(z, n);
+    if (nc > 0 && ncand <= ORA_SAMPLE_MAX_CAND) {
+        /* rank of each candidate under (z desc, index asc) */
+        int sidx[ORA_SAMPLE_MAX_CAND];
+        float sz[ORA_SAMPLE_MAX_CAND], sw[ORA_SAMPLE_MAX_CAND];
+        for (int c = 0; c < nc; c++) {
+            int r = 0;
+            for (int m = 0; m < nc; m++)
+                if (keys[ci[m]] > keys[ci[c]] || (keys[ci[m]] == keys[ci[c]] && ci[m] < ci[c])) r++;
+            sidx[r] = ci[c];
+            sz[r] = z[ci[c]];
+        }
+        float mx = sz[0];
+        for (int c = 0; c < nc; c++) sw[c] = expf(sz[c] - mx);
+        float total = 0.0f;
+        for (int c = 0; c < nc; c++) total += sw[c];
+        int nk = nc;
+        if (top_p < 1.0f) {
+            float acc = 0.0f;
+            for (int c = 0; c < nc; c++) {
+                if (c > 0 && acc / total >= top_p) {
+                    nk = c;
+                    break;
+                }
+                acc += sw[c];
+            }
+        }
+        float wsum = 0.0f;
+        for (int c = 0; c < nk; c++) wsum += sw[c];
+        float target = u * wsum, acc = 0.0f;
+        code = sidx[nk - 1];
+        for (int c = 0; c < nk; c++) {
+            acc += sw[c];
+            if (acc > target) {
+                code = sidx[c];
+                break;
+            }
+        }
+    }
+    free(keys);
+    free(z);
+    return code;
+}
+
 /* ---------------------------------------------------------------- talker */
 
 /* the device-side part of TQwenTalker (talker.pas:78-158): both stacks, the
@@ -605,7 +711,25 @@ typedef struct {
     float *logits, *work, *past_hidden, *plogits, *x;
     int *history;
     int nhist, step, cap;
+    /* TQwenSampling (talker.pas:59-73): code 0 and the predictor's codes */
+    int do_sample, sub_do_sample, top_k, sub_top_k;
+    float temperature, top_p, sub_temperature, sub_top_p;
+    uint64_t seed;
 } ora_talker;
+
+void ora_talker_set_sampling(ora_talker *t, int do_sample, float temperature, int top_k, float top_p,
+                             int sub_do_sample, float sub_temperature, int sub_top_k, float sub_top_p,
+                             uint64_t seed) {
+    t->do_sample = do_sample;
+    t->temperature = temperature;
+    t->top_k = top_k;
+    t->top_p = top_p;
+    t->sub_do_sample = sub_do_sample;
+    t->sub_temperature = sub_temperature;
+    t->sub_top_k = sub_top_k;
+    t->sub_top_p = sub_top_p;
+    t->seed = seed;
+}
 
 ora_talker *ora_talker_create(ora_lm *talker, const ora_heads *th, ora_lm *pred, const ora_heads *ph,
                               const float *codec_emb, int vocab, const float *pred_emb, int pvocab, int groups,
@@ -670,6 +794,9 @@ static void add_row(float *y, const float *row, int H) {
 static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap) {
     int H = t->H;
     int code = ora_choose_code0(t->logits, t->vocab, t->eos, t->history, t->nhist, t->penalty, t->work);
+    if (t->do_sample && !force)
+        code = ora_sample(t->work, t->vocab, t->temperature, t->top_k, t->top_p,
+                          ora_sample_uniform(t->seed, t->step, 0));
     if (force) {
         gap[0] = t->work[code] - t->work[force[0]];
         if (t->work[force[0]] == -INFINITY) gap[0] = INFINITY;
@@ -692,6 +819,9 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap)
             if (ora_lm_forward(t->pred, t->x, 1, t->ph, g, t->plogits, NULL, NULL, NULL)) return -1;
         }
         int best = ora_argmax(t->plogits, t->pvocab);
+        if (t->sub_do_sample && !force)
+            best = ora_sample(t->plogits, t->pvocab, t->sub_temperature, t->sub_top_k, t->sub_top_p,
+                              ora_sample_uniform(t->seed, t->step, g + 1));
         if (force) {
             gap[g + 1] = t->plogits[best] - t->plogits[force[g + 1]];
             best = force[g + 1];
