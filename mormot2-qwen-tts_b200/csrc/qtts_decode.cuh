@@ -427,6 +427,24 @@ struct Producer {
 
 // ------------------------------------------------------------------ compute
 
+// the draw of a frame's code from the logits lg[V] of the last head (NCT
+// threads; talker: ChooseCode0's processors first, as choose0_value)
+__device__ __noinline__ int frame_draw(const float *lg, int V, SampleParams p, float u, SampleScratch *ss, int tid,
+                                       bool talker, int vocab, int eos, int hist_now, const unsigned char *seen,
+                                       float penalty) {
+    if (talker)
+        return sample_draw<NCT>(
+            [&](int i) {
+                const float s = __ldcg(lg + i);
+                if (i >= vocab - 1024 && i != eos) return -INFINITY;
+                if (i == eos && hist_now < 2) return -INFINITY;
+                if (penalty != 1.0f && seen[i]) return s > 0.f ? __fdiv_rn(s, penalty) : s * penalty;
+                return s;
+            },
+            V, p, u, ss, tid);
+    return sample_draw<NCT>([&](int i) { return __ldcg(lg + i); }, V, p, u, ss, tid);
+}
+
 template <int WDT>
 struct Compute {
     Smem *sm;
@@ -870,13 +888,11 @@ struct Compute {
 
     // after a grid barrier: the code drawn from the logits of the last head
     // (every compute thread of the CTA calls it; sm->act is the scratch);
-    // code 0 (talker) from the values after ChooseCode0's processors
-    __device__ int sample_code(int V, const SampleParams &p, float u, bool talker) {
-        SampleScratch *ss = reinterpret_cast<SampleScratch *>(sm->act);
-        const float *lg = job->s.logits;
-        if (talker)
-            return sample_draw<NCT>([&](int i) { return choose0_value(i, __ldcg(lg + i)); }, V, p, u, ss, tid);
-        return sample_draw<NCT>([&](int i) { return __ldcg(lg + i); }, V, p, u, ss, tid);
+    // code 0 (talker) from the values after ChooseCode0's processors.  The
+    // draw is a call (frame_draw), so that the layer code stays compact.
+    __device__ __forceinline__ int sample_code(int V, const SampleParams &p, float u, bool talker) {
+        return frame_draw(job->s.logits, V, p, u, reinterpret_cast<SampleScratch *>(sm->act), tid, talker,
+                          job->tvocab, job->eos, hist_now, job->seen, job->penalty);
     }
 
     // after a grid barrier: the winning index over all CTAs' keys
