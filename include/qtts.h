@@ -317,6 +317,12 @@ int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t *seqs, int3
  * them with events. */
 int qtts_talkers_stream(qtts_talkers *t, void **stream);
 int qtts_talkers_destroy(qtts_talkers *t);
+/* The sampling of every utterance of the batch (TQwenSampling as for
+ * qtts_talker_set_sampling): utterance s draws from the stream seed + s, so
+ * that it picks the codes a lone qtts_talker with seed + s would pick from
+ * the same logits.  The first code 0 is drawn by qtts_talkers_start: set it
+ * before. */
+int qtts_talkers_set_sampling(qtts_talkers *t, const qtts_sampling *s);
 
 /* ------------------------------------------------------------------ utilities */
 

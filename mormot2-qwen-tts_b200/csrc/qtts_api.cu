@@ -2102,6 +2102,8 @@ struct qtts_talkers {
     std::vector<int> graph_seqs;
     BatchPlan graph_plans[MAX_GROUPS];
     int frames_eager = 0, frames_graph = 0, captures = 0;
+    SampleParams samp0 = {}, samp = {};  // code 0 / the predictor's codes (on = 0: greedy)
+    uint64_t seed = 0;                   // utterance s draws from stream seed + s
 };
 
 static void talkers_free(qtts_talkers *t) {
@@ -2259,7 +2261,7 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
     if ((rc = batch_run(t->tb, nseq, seqs, rows, prefill, false, 0, st))) return rc;
     frames_choose0_kernel<<<nseq, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
                                                 t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
-                                                t->d_done, 1);
+                                                t->d_done, 1, t->samp0, static_cast<unsigned long long>(t->seed));
     CK(cudaGetLastError());
     if ((rc = talkers_finish(t, "qtts_talkers_start"))) return rc;
     for (int i = 0; i < nseq; ++i) {
@@ -2291,7 +2293,9 @@ static int frame_enqueue(qtts_talkers *t, int n, const BatchPlan *plans, cudaStr
     for (int g = 0; g < G - 1; ++g) {
         if ((rc = batch_enqueue(t->pb, plans[g], t->px, true, g, st))) return rc;
         CK(launch_pdl(frames_pred_argmax_kernel, dim3(n), dim3(256), 0, st, static_cast<const float *>(t->pb->logits),
-                      pv, g, G, static_cast<const float *>(t->pred_emb), t->px, t->d_codes));
+                      pv, g, G, static_cast<const float *>(t->pred_emb), t->px, t->d_codes,
+                      static_cast<const int *>(t->d_seqs), static_cast<const SeqState *>(t->ss), t->samp,
+                      static_cast<unsigned long long>(t->seed)));
     }
     CK(launch_pdl(frames_talker_in_kernel, dim3(n), dim3(256), 0, st, static_cast<const int *>(t->d_seqs),
                   static_cast<const SeqState *>(t->ss), static_cast<const int *>(t->d_codes), G,
@@ -2301,7 +2305,7 @@ static int frame_enqueue(qtts_talkers *t, int n, const BatchPlan *plans, cudaStr
     CK(launch_pdl(frames_choose0_kernel, dim3(n), dim3(256), 0, st, static_cast<const int *>(t->d_seqs),
                   static_cast<const float *>(t->tb->logits), static_cast<const float *>(t->tb->hidden), t->cfg.vocab,
                   t->cfg.codec_eos, t->cfg.repetition_penalty, static_cast<const unsigned char *>(t->seen), t->ss,
-                  t->hid, t->d_done, 0));
+                  t->hid, t->d_done, 0, t->samp0, static_cast<unsigned long long>(t->seed)));
     CK(cudaMemcpyAsync(io_codes(t), t->d_codes, static_cast<size_t>(n) * G * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(io_done(t), t->d_done, n * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(io_errs(t), t->tb->err, 4, cudaMemcpyDeviceToHost, st));
@@ -2394,5 +2398,30 @@ extern "C" int qtts_talkers_destroy(qtts_talkers *t) {
     cudaSetDevice(t->tb->dev->ordinal);
     cudaStreamSynchronize(t->stream);
     talkers_free(t);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_set_sampling(qtts_talkers *t, const qtts_sampling *s) {
+    if (!t || !s) return set_err(QTTS_E_ARG, "qtts_talkers_set_sampling: NULL argument");
+    SampleParams a, b;
+    int rc = sampling_params("qtts_talkers_set_sampling", s->do_sample, s->temperature, s->top_k, s->top_p, &a);
+    if (rc) return rc;
+    rc = sampling_params("qtts_talkers_set_sampling (predictor)", s->sub_do_sample, s->sub_temperature, s->sub_top_k,
+                         s->sub_top_p, &b);
+    if (rc) return rc;
+    if (t->cfg.vocab > SAMPLE_MAX_V || t->cfg.pred_vocab > SAMPLE_MAX_V)
+        return set_err(QTTS_E_ARG, "qtts_talkers_set_sampling: vocabularies of %d / %d, at most %d", t->cfg.vocab,
+                       t->cfg.pred_vocab, SAMPLE_MAX_V);
+    CK(cudaSetDevice(t->tb->dev->ordinal));
+    CK(cudaStreamSynchronize(t->stream));
+    t->samp0 = a;
+    t->samp = b;
+    t->seed = s->seed;
+    // the captured frame holds the old options
+    if (t->graph) {
+        cudaGraphExecDestroy(t->graph);
+        t->graph = nullptr;
+        t->graph_seqs.clear();
+    }
     return QTTS_OK;
 }

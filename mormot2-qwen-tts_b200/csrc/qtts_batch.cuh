@@ -502,19 +502,32 @@ __device__ __forceinline__ unsigned long long block_argmax(unsigned long long b,
 // ChooseCode (talker.pas:632-638), greedy, after predictor step g: code g+1
 // of row i = the first maximum of its logits; the next predictor input row
 // is pred_emb[g][code] (talker.pas:670-675).
-__global__ void frames_pred_argmax_kernel(const float *logits, int vocab, int g, int groups, const float *pred_emb,
-                                          float *px, int *codes) {
+//  samp.on: the code is drawn (draw (frame, g + 1) of the utterance's
+//  stream seed + s), else the first maximum; 256 threads.
+__global__ void __launch_bounds__(256) frames_pred_argmax_kernel(const float *logits, int vocab, int g, int groups,
+                                                                 const float *pred_emb, float *px, int *codes,
+                                                                 const int *seqs, const SeqState *ss,
+                                                                 SampleParams samp, unsigned long long seed) {
     pdl_trigger();
     pdl_wait();
     __shared__ unsigned long long red[32];
+    __shared__ SampleScratch scr;
     const int i = blockIdx.x;
     const float *lg = logits + static_cast<size_t>(i) * vocab;
-    unsigned long long b = 0ull;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
-        const unsigned long long k = argkey(lg[j], j);
-        b = k > b ? k : b;
+    int code;
+    if (samp.on) {
+        const int s = seqs[i];
+        code = sample_draw<256>([&](int j) { return lg[j]; }, vocab, samp,
+                                sample_uniform(seed + static_cast<unsigned long long>(s), ss[s].step, g + 1), &scr,
+                                static_cast<int>(threadIdx.x));
+    } else {
+        unsigned long long b = 0ull;
+        for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+            const unsigned long long k = argkey(lg[j], j);
+            b = k > b ? k : b;
+        }
+        code = key_index(block_argmax(b, red));
     }
-    const int code = key_index(block_argmax(b, red));
     if (threadIdx.x == 0) codes[i * groups + g + 1] = code;
     if (g + 1 < groups - 1) {
         const float *e = pred_emb + (static_cast<size_t>(g) * vocab + code) * H;
@@ -552,26 +565,43 @@ __global__ void frames_talker_in_kernel(const int *seqs, const SeqState *ss, con
 // repetition penalty once per distinct code of the history; the normed
 // state of the row becomes the utterance's talker state.  done[i] = eos
 // chosen (read by the host).  start != 0: after the prefill (empty history).
-__global__ void frames_choose0_kernel(const int *seqs, const float *logits, const float *hidden, int vocab, int eos,
-                                      float penalty, const unsigned char *seen, SeqState *ss, float *hid, int *done,
-                                      int start) {
+//  samp0.on: code 0 is drawn (draw (frame, 0) of the utterance's stream
+//  seed + s; frame = the index of the frame the code belongs to), else the
+//  first maximum; 256 threads.
+__global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, const float *logits, const float *hidden,
+                                                             int vocab, int eos, float penalty,
+                                                             const unsigned char *seen, SeqState *ss, float *hid,
+                                                             int *done, int start, SampleParams samp0,
+                                                             unsigned long long seed) {
     pdl_trigger();
     pdl_wait();
     __shared__ unsigned long long red[32];
+    __shared__ SampleScratch scr;
     const int i = blockIdx.x, s = seqs[i];
     const float *lg = logits + static_cast<size_t>(i) * vocab;
     const unsigned char *m = seen + static_cast<size_t>(s) * vocab;
     const int hist = ss[s].hist_len;
-    unsigned long long b = 0ull;
-    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    // ChooseCode0's processors (talker.pas:595-625)
+    auto value = [&](int j) {
         float w = lg[j];
         if (j >= vocab - 1024 && j != eos) w = -INFINITY;
         else if (j == eos && hist < 2) w = -INFINITY;
         else if (penalty != 1.0f && m[j]) w = w > 0.f ? __fdiv_rn(w, penalty) : w * penalty;
-        const unsigned long long k = argkey(w, j);
-        b = k > b ? k : b;
+        return w;
+    };
+    int code;
+    if (samp0.on) {
+        const int frame = start ? 0 : ss[s].step + 1;
+        code = sample_draw<256>(value, vocab, samp0, sample_uniform(seed + static_cast<unsigned long long>(s), frame, 0),
+                                &scr, static_cast<int>(threadIdx.x));
+    } else {
+        unsigned long long b = 0ull;
+        for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+            const unsigned long long k = argkey(value(j), j);
+            b = k > b ? k : b;
+        }
+        code = key_index(block_argmax(b, red));
     }
-    const int code = key_index(block_argmax(b, red));
     for (int c = threadIdx.x; c < H / 4; c += blockDim.x)
         store4(hid + static_cast<size_t>(s) * H + 4 * c, load4(hidden + static_cast<size_t>(i) * H + 4 * c));
     if (threadIdx.x == 0) {

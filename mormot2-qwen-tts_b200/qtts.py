@@ -107,6 +107,7 @@ EXPORTS = {
     "qtts_talker_step": [P, PI],
     "qtts_talker_destroy": [P],
     "qtts_talker_set_sampling": [P, ctypes.POINTER(Sampling)],
+    "qtts_talkers_set_sampling": [P, ctypes.POINTER(Sampling)],
     "qtts_sample": [P, P, I, ctypes.c_float, I, ctypes.c_float, ctypes.c_uint64, I, I, PI],
     "qtts_talkers_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
     "qtts_talkers_start": [P, I, P, P, P, P, P, P],
@@ -475,6 +476,14 @@ class QwenTalkers:
         self.handle = h
         self.groups = groups
         self.hidden = talker.hidden
+
+    def set_sampling(self, do_sample=True, temperature=0.9, top_k=50, top_p=1.0, sub_do_sample=True,
+                     sub_temperature=0.9, sub_top_k=50, sub_top_p=1.0, seed=0):
+        """TQwenSampling for every utterance (utterance s: stream seed + s);
+        call before start for the first code 0."""
+        s = Sampling(int(do_sample), temperature, top_k, top_p, int(sub_do_sample), sub_temperature, sub_top_k,
+                     sub_top_p, seed)
+        check(lib().qtts_talkers_set_sampling(self.handle, ctypes.byref(s)))
 
     def start(self, seqs, prefills, trailings, tts_pad):
         """TQwenTalker.Start for utterances seqs[i]: prefills[i] [rows][hidden],

@@ -71,6 +71,7 @@ def _load():
         "ora_talker_start": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P]),
         "ora_talker_next_frame": (ctypes.c_int, [P, P]),
         "ora_talker_check_frame": (ctypes.c_int, [P, P, P]),
+        "ora_talker_check_frame_ranks": (ctypes.c_int, [P, P, P, P]),
         "ora_talker_logits": (P, [P]),
         "ora_talker_set_sampling": (None, [P, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
                                            ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
@@ -288,6 +289,17 @@ class OraTalker:
         if rc < 0:
             raise RuntimeError("oracle: KV cache full")
         return rc == 1, gap
+
+    def check_frame_ranks(self, codes):
+        """check_frame with the rank of each choice among its values (after
+        the processors): returns (more, gaps, ranks)."""
+        c = np.ascontiguousarray(codes, dtype=np.int32)
+        gap = np.zeros(self.groups, np.float32)
+        rank = np.zeros(self.groups, np.int32)
+        rc = lib.ora_talker_check_frame_ranks(self.handle, _p(c), _p(gap), _p(rank))
+        if rc < 0:
+            raise RuntimeError("oracle: KV cache full")
+        return rc == 1, gap, rank
 
     def logits(self):
         ptr = lib.ora_talker_logits(self.handle)

@@ -791,7 +791,14 @@ static void add_row(float *y, const float *row, int H) {
  * under the same rule (0 for a first maximum or a tie; +inf for a forbidden
  * id).  Returns 1 after a frame, 0 when code 0 is eos, -1 when a cache is
  * full. */
-static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap) {
+/* rank of v among x[n]: the values strictly greater */
+static int rank_of(const float *x, int n, float v) {
+    int r = 0;
+    for (int i = 0; i < n; i++) r += x[i] > v;
+    return r;
+}
+
+static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap, int *rank) {
     int H = t->H;
     int code = ora_choose_code0(t->logits, t->vocab, t->eos, t->history, t->nhist, t->penalty, t->work);
     if (t->do_sample && !force)
@@ -800,6 +807,7 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap)
     if (force) {
         gap[0] = t->work[code] - t->work[force[0]];
         if (t->work[force[0]] == -INFINITY) gap[0] = INFINITY;
+        if (rank) rank[0] = rank_of(t->work, t->vocab, t->work[force[0]]);
         code = force[0];
     }
     if (code == t->eos) return 0;
@@ -824,6 +832,7 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap)
                               ora_sample_uniform(t->seed, t->step, g + 1));
         if (force) {
             gap[g + 1] = t->plogits[best] - t->plogits[force[g + 1]];
+            if (rank) rank[g + 1] = rank_of(t->plogits, t->pvocab, t->plogits[force[g + 1]]);
             best = force[g + 1];
         }
         codes[g + 1] = best;
@@ -841,13 +850,21 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap)
 }
 
 /* returns 1 and fills codes[groups], 0 at eos, -1 when a cache is full */
-int ora_talker_next_frame(ora_talker *t, int *codes) { return talker_frame(t, NULL, codes, NULL); }
+int ora_talker_next_frame(ora_talker *t, int *codes) { return talker_frame(t, NULL, codes, NULL, NULL); }
 
 /* the frame chosen elsewhere (codes[groups]), with the gaps of its choices */
 int ora_talker_check_frame(ora_talker *t, const int *codes, float *gap) {
     int own[64];
     if (t->groups > 64) return -1;
-    return talker_frame(t, codes, own, gap);
+    return talker_frame(t, codes, own, gap, NULL);
+}
+
+/* as ora_talker_check_frame, with rank[g]: how many of choice g's values
+ * (after the processors) are strictly above the value of codes[g] */
+int ora_talker_check_frame_ranks(ora_talker *t, const int *codes, float *gap, int *rank) {
+    int own[64];
+    if (t->groups > 64) return -1;
+    return talker_frame(t, codes, own, gap, rank);
 }
 
 const float *ora_talker_logits(const ora_talker *t) { return t->logits; }

@@ -164,3 +164,40 @@ def test_batched_eos_and_errors(device):
         rig.dev.next_frame([0])
     assert e.value.code == qtts.E_CAPACITY
     rig.free()
+
+
+def test_batched_sampled_frames(device):
+    # the batched loop in sampling mode (qwen_tts defaults: temperature 0.9,
+    # top_k 50): every drawn code is one of the top-k of the oracle's values
+    # for that choice (the oracle replays each frame driven by the device's
+    # codes; fp16 activations may move a value near the k-th by a few
+    # places), and another seed gives other codes.  Two runs with the same
+    # seed are not compared: the split-K projections add their partial sums
+    # with float atomics, whose order varies, and the fp16 activations carry
+    # that last-bit variation into the logits (about 1e-4), enough to move an
+    # inverse-CDF draw though not a greedy choice.
+    def run(seed, check):
+        rig = Rig(device, 91, 2, 2, "q8_0", "f32", 4)
+        rig.dev.set_sampling(seed=seed)
+        for s in range(4):
+            rig.ora[s].set_sampling(seed=seed + s)
+        start(rig, [0, 1, 2, 3], 91)
+        out, ranks = [], []
+        for _ in range(5):
+            codes, more = rig.dev.next_frame([0, 1, 2, 3])
+            out.append(codes.copy())
+            if check:
+                for i in range(4):
+                    if more[i]:
+                        m, _, rank = rig.ora[i].check_frame_ranks(codes[i])
+                        assert m
+                        ranks.append(rank)
+        rig.free()
+        return np.array(out), np.array(ranks)
+
+    a, ranks = run(21, True)
+    c, _ = run(22, False)
+    assert not np.array_equal(a[0], c[0])
+    assert ranks.size > 0 and ranks.max() < 50 + 8, ranks.max()
+    assert (ranks < 50).mean() >= 0.95
+    assert (ranks > 0).mean() >= 0.3  # not the argmax every time
