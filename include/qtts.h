@@ -55,6 +55,7 @@ typedef struct qtts_stack qtts_stack;
 typedef struct qtts_heads qtts_heads;
 typedef struct qtts_lm qtts_lm;
 typedef struct qtts_talker qtts_talker;
+typedef struct qtts_textproj qtts_textproj;
 
 /* The decoder configuration of one stack (TDecoderConfig: talker_config or
  * talker_config.code_predictor_config of config.json, talker.pas:252-273).
@@ -284,6 +285,23 @@ int qtts_talker_set_sampling(qtts_talker *t, const qtts_sampling *s);
  * processors, n <= 4096) with draw (step, group) of the stream `seed`. */
 int qtts_sample(qtts_device *dev, const float *work, int n, float temperature, int top_k, float top_p,
                 uint64_t seed, int step, int group, int32_t *code);
+
+/* ------------------------------------------------------------------ text projection */
+
+/* TQwenTalker.TextProject (talker.pas:390-421), Qwen3TTSTalkerResizeMLP:
+ * y = fc2(silu(fc1(text_embedding[id]))) in float32 with biases, for the
+ * text rows of the prompt and of the trailing text (talker.pas:532-574).
+ * emb [vocab][text_hidden] in emb_dtype (QTTS_DTYPE_BF16 as in the
+ * checkpoint, or F32; kept on the device as given), fc1_w
+ * [text_hidden][text_hidden], fc1_b [text_hidden], fc2_w
+ * [hidden][text_hidden], fc2_b [hidden]; copied at create. */
+int qtts_textproj_create(qtts_device *dev, int vocab, int text_hidden, int hidden, int emb_dtype, const void *emb,
+                         const float *fc1_w, const float *fc1_b, const float *fc2_w, const float *fc2_b,
+                         qtts_textproj **out);
+/* y[n][hidden] (host) = the projection of the text tokens ids[n] (host); an
+ * id outside [0, vocab) is QTTS_E_ARG, as TextProject raises. */
+int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, float *y);
+int qtts_textproj_destroy(qtts_textproj *t);
 
 /* ------------------------------------------------------------------ talkers (batched frames) */
 

@@ -1467,6 +1467,153 @@ extern "C" int qtts_sample(qtts_device *dev, const float *work, int n, float tem
 
 // ------------------------------------------------------------------ utilities
 
+// ------------------------------------------------------------------ text projection
+//
+// TQwenTalker.TextProject (talker.pas:390-421): Qwen3TTSTalkerResizeMLP,
+// y = fc2(silu(fc1(text_embedding[id]))), float32 with biases, the rows of
+// the prompt and of the trailing text (talker.pas:532-574).  The embedding
+// table stays on the device in its source format (BF16 as in the
+// checkpoint, or float32); fc1 / fc2 in float32.
+
+struct qtts_textproj {
+    qtts_device *dev;
+    int vocab, text_hidden, hidden, emb_dtype;
+    void *emb;
+    float *w1, *b1, *w2, *b2;
+    float *e, *h, *y;  // [cap][text_hidden] x2, [cap][hidden]
+    int *ids;
+    int cap;
+};
+
+// e[r][k] = emb[ids[r]][k] widened to float32; ids checked on the host
+__global__ void text_gather_kernel(const void *emb, int dtype, int kdim, const int *ids, int n, float *e) {
+    const int r = blockIdx.x;
+    if (r >= n) return;
+    const size_t row = static_cast<size_t>(ids[r]) * kdim;
+    for (int k = threadIdx.x; k < kdim; k += blockDim.x)
+        e[static_cast<size_t>(r) * kdim + k] = dtype == QTTS_DTYPE_BF16
+                                                   ? __bfloat162float(static_cast<const __nv_bfloat16 *>(emb)[row + k])
+                                                   : static_cast<const float *>(emb)[row + k];
+}
+
+// y[r][o] = sum_k x[r][k] w[o][k] + b[o] (then silu as TextProject: 0 below
+// -80, else v / (1 + exp(-v))): a warp per output o, its weight row in
+// registers (kdim <= 32 * TP_KPL), the rows of x streamed
+constexpr int TP_KPL = 64;
+__global__ void __launch_bounds__(256) text_linear_kernel(const float *x, int n, int kdim, const float *w,
+                                                         const float *b, int odim, int silu, float *y) {
+    const int o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (o >= odim) return;
+    float wr[TP_KPL];
+#pragma unroll
+    for (int j = 0; j < TP_KPL; ++j) {
+        const int k = lane + 32 * j;
+        wr[j] = k < kdim ? w[static_cast<size_t>(o) * kdim + k] : 0.f;
+    }
+    const float bo = b[o];
+    for (int r = 0; r < n; ++r) {
+        const float *xr = x + static_cast<size_t>(r) * kdim;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < TP_KPL; ++j) {
+            const int k = lane + 32 * j;
+            if (k < kdim) acc = fmaf(wr[j], xr[k], acc);
+        }
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+        if (lane == 0) {
+            float v = acc + bo;
+            if (silu) v = v < -80.f ? 0.f : v / (1.0f + expf(-v));
+            y[static_cast<size_t>(r) * odim + o] = v;
+        }
+    }
+}
+
+static void textproj_free(qtts_textproj *t) {
+    for (void *p : {t->emb, static_cast<void *>(t->w1), static_cast<void *>(t->b1), static_cast<void *>(t->w2),
+                    static_cast<void *>(t->b2), static_cast<void *>(t->e), static_cast<void *>(t->h),
+                    static_cast<void *>(t->y), static_cast<void *>(t->ids)})
+        if (p) cudaFree(p);
+    delete t;
+}
+
+extern "C" int qtts_textproj_create(qtts_device *dev, int vocab, int text_hidden, int hidden, int emb_dtype,
+                                    const void *emb, const float *fc1_w, const float *fc1_b, const float *fc2_w,
+                                    const float *fc2_b, qtts_textproj **out) {
+    if (!dev || !emb || !fc1_w || !fc1_b || !fc2_w || !fc2_b || !out)
+        return set_err(QTTS_E_ARG, "qtts_textproj_create: NULL argument");
+    *out = nullptr;
+    if (vocab <= 0 || text_hidden <= 0 || text_hidden > 32 * TP_KPL || hidden <= 0)
+        return set_err(QTTS_E_ARG, "qtts_textproj_create: vocab %d, text hidden %d (1..%d), hidden %d", vocab,
+                       text_hidden, 32 * TP_KPL, hidden);
+    if (emb_dtype != QTTS_DTYPE_F32 && emb_dtype != QTTS_DTYPE_BF16)
+        return set_err(QTTS_E_ARG, "qtts_textproj_create: embedding dtype %d (F32 or BF16)", emb_dtype);
+    CK(cudaSetDevice(dev->ordinal));
+    qtts_textproj *t = new qtts_textproj();
+    t->dev = dev;
+    t->vocab = vocab;
+    t->text_hidden = text_hidden;
+    t->hidden = hidden;
+    t->emb_dtype = emb_dtype;
+    const size_t eb = static_cast<size_t>(vocab) * text_hidden * (emb_dtype == QTTS_DTYPE_BF16 ? 2 : 4);
+    const size_t w1 = static_cast<size_t>(text_hidden) * text_hidden * 4, w2 = static_cast<size_t>(hidden) * text_hidden * 4;
+    cudaError_t e = cudaMalloc(&t->emb, eb);
+    if (e == cudaSuccess) e = cudaMalloc(&t->w1, w1);
+    if (e == cudaSuccess) e = cudaMalloc(&t->b1, static_cast<size_t>(text_hidden) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&t->w2, w2);
+    if (e == cudaSuccess) e = cudaMalloc(&t->b2, static_cast<size_t>(hidden) * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(t->emb, emb, eb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->w1, fc1_w, w1, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->b1, fc1_b, static_cast<size_t>(text_hidden) * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->w2, fc2_w, w2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->b2, fc2_b, static_cast<size_t>(hidden) * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        textproj_free(t);
+        return set_err(e == cudaErrorMemoryAllocation ? QTTS_E_OOM : QTTS_E_CUDA, "qtts_textproj_create: %s",
+                       cudaGetErrorString(e));
+    }
+    *out = t;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, float *y) {
+    if (!t || (n > 0 && (!ids || !y))) return set_err(QTTS_E_ARG, "qtts_text_project: NULL argument");
+    if (n <= 0) return QTTS_OK;
+    for (int r = 0; r < n; ++r)
+        if (ids[r] < 0 || ids[r] >= t->vocab)
+            return set_err(QTTS_E_ARG, "qtts_text_project: text token %d out of range", ids[r]);
+    CK(cudaSetDevice(t->dev->ordinal));
+    if (n > t->cap) {
+        for (void *p : {static_cast<void *>(t->e), static_cast<void *>(t->h), static_cast<void *>(t->y),
+                        static_cast<void *>(t->ids)})
+            if (p) cudaFree(p);
+        t->e = t->h = t->y = nullptr;
+        t->ids = nullptr;
+        t->cap = 0;
+        cudaError_t e = cudaMalloc(&t->e, static_cast<size_t>(n) * t->text_hidden * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&t->h, static_cast<size_t>(n) * t->text_hidden * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&t->y, static_cast<size_t>(n) * t->hidden * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&t->ids, static_cast<size_t>(n) * 4);
+        if (e != cudaSuccess) return set_err(QTTS_E_OOM, "qtts_text_project: %s", cudaGetErrorString(e));
+        t->cap = n;
+    }
+    CK(cudaMemcpy(t->ids, ids, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice));
+    text_gather_kernel<<<n, 256>>>(t->emb, t->emb_dtype, t->text_hidden, t->ids, n, t->e);
+    text_linear_kernel<<<(t->text_hidden + 7) / 8, 256>>>(t->e, n, t->text_hidden, t->w1, t->b1, t->text_hidden, 1,
+                                                          t->h);
+    text_linear_kernel<<<(t->hidden + 7) / 8, 256>>>(t->h, n, t->text_hidden, t->w2, t->b2, t->hidden, 0, t->y);
+    CK(cudaGetLastError());
+    CK(cudaMemcpy(y, t->y, static_cast<size_t>(n) * t->hidden * 4, cudaMemcpyDeviceToHost));
+    return QTTS_OK;
+}
+
+extern "C" int qtts_textproj_destroy(qtts_textproj *t) {
+    if (!t) return QTTS_OK;
+    cudaSetDevice(t->dev->ordinal);
+    textproj_free(t);
+    return QTTS_OK;
+}
+
 extern "C" int qtts_quantize_q8_0(qtts_device *dev, const float *src, int64_t n, uint8_t *dst) {
     if (!dev || !src || !dst || n < 0 || (n & 31) != 0) return set_err(QTTS_E_ARG, "qtts_quantize_q8_0: bad argument");
     if (n == 0) return QTTS_OK;

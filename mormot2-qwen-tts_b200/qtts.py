@@ -115,6 +115,9 @@ EXPORTS = {
     "qtts_talkers_stream": [P, ctypes.POINTER(P)],
     "qtts_talkers_destroy": [P],
     "qtts_quantize_q8_0": [P, P, ctypes.c_int64, P],
+    "qtts_textproj_create": [P, I, I, I, I, P, P, P, P, P, ctypes.POINTER(P)],
+    "qtts_text_project": [P, P, I, P],
+    "qtts_textproj_destroy": [P],
 }
 
 
@@ -459,6 +462,35 @@ class QwenTalker:
     def free(self):
         if self.handle:
             check(lib().qtts_talker_destroy(self.handle))
+            self.handle = None
+
+
+class QwenTextProject:
+    """TQwenTalker.TextProject (talker.pas:390-421) on the device: the text
+    embedding table (BF16 uint16 rows or float32) and the float32 fc1 / fc2
+    with biases."""
+
+    def __init__(self, device, emb, fc1_w, fc1_b, fc2_w, fc2_b):
+        if emb.dtype == np.uint16:
+            dt, e = DTYPES["bf16"], np.ascontiguousarray(emb)
+        else:
+            dt, e = DTYPES["f32"], _f32(emb)
+        self.w = [_f32(a) for a in (fc1_w, fc1_b, fc2_w, fc2_b)]
+        self.hidden = self.w[2].shape[0]
+        h = P()
+        check(lib().qtts_textproj_create(device.handle, e.shape[0], e.shape[1], self.hidden, dt, _ptr(e),
+                                         *(_ptr(a) for a in self.w), ctypes.byref(h)))
+        self.handle = h
+
+    def project(self, ids):
+        i = np.ascontiguousarray(ids, dtype=np.int32)
+        y = np.zeros((i.size, self.hidden), np.float32)
+        check(lib().qtts_text_project(self.handle, _ptr(i), i.size, _ptr(y)))
+        return y
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_textproj_destroy(self.handle))
             self.handle = None
 
 

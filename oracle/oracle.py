@@ -79,6 +79,7 @@ def _load():
         "ora_sample": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
                                       ctypes.c_float]),
         "ora_sample_uniform": (ctypes.c_float, [ctypes.c_uint64, ctypes.c_int, ctypes.c_int]),
+        "ora_text_project": (None, [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, P, P, P, P, P]),
         "ora_talker_hidden": (P, [P]),
         "ora_rope_table": (None, [ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P]),
     }
@@ -155,6 +156,17 @@ def sample(work, temperature, top_k, top_p, u):
     work (logits after the processors) with the uniform u."""
     w = _f32(work)
     return lib.ora_sample(_p(w), w.size, temperature, top_k, top_p, u)
+
+
+def text_project(emb, ids, w1, b1, w2, b2):
+    """TQwenTalker.TextProject restated: [n][hidden] float32."""
+    emb, w1, b1, w2, b2 = (_f32(a) for a in (emb, w1, b1, w2, b2))
+    i = np.ascontiguousarray(ids, dtype=np.int32)
+    vocab, th = emb.shape
+    hidden = w2.shape[0]
+    y = np.zeros((i.size, hidden), np.float32)
+    lib.ora_text_project(_p(emb), vocab, th, hidden, _p(i), i.size, _p(w1), _p(b1), _p(w2), _p(b2), _p(y))
+    return y
 
 
 def rope_table(max_pos, head_dim, theta):

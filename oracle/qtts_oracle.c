@@ -588,6 +588,28 @@ int ora_choose_code0(const float *logits, int vocab, int eos, const int *history
     return ora_argmax(work, vocab);
 }
 
+/* ---------------------------------------------------------------- text projection */
+
+/* TQwenTalker.TextProject (talker.pas:390-421): for each id, the text
+ * embedding row (float32 here; BF16 tables are widened by the caller), then
+ * h = fc1 . e + b1 (TInferBackend.Linear with bias), silu as the reference
+ * writes it (0 below -80, else v / (1 + exp(-v))), y = fc2 . h + b2. */
+void ora_text_project(const float *emb, int vocab, int th, int hidden, const int *ids, int n, const float *w1,
+                      const float *b1, const float *w2, const float *b2, float *y) {
+    float *e = (float *)malloc((size_t)th * sizeof(float)), *h = (float *)malloc((size_t)th * sizeof(float));
+    for (int r = 0; r < n; r++) {
+        int id = ids[r] < 0 ? 0 : (ids[r] >= vocab ? vocab - 1 : ids[r]);
+        memcpy(e, emb + (size_t)id * th, (size_t)th * sizeof(float));
+        for (int o = 0; o < th; o++) {
+            float v = dot_f32(w1 + (size_t)o * th, e, th) + b1[o];
+            h[o] = v < -80.0f ? 0.0f : v / (1.0f + expf(-v));
+        }
+        for (int o = 0; o < hidden; o++) y[(size_t)r * hidden + o] = dot_f32(w2 + (size_t)o * th, h, th) + b2[o];
+    }
+    free(e);
+    free(h);
+}
+
 /* ---------------------------------------------------------------- sampling */
 
 /* TInferSampler.Next (mormot2-ai, used at talker.pas:626-629 and 632-638;
