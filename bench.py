@@ -177,6 +177,24 @@ def cpu_frames(m, dtype, prompt, frames, threads=None):
     return dt, done, n
 
 
+def max_over_ranks(values, dist, device):
+    """Each of `values` (timings of this rank) replaced by its maximum over
+    the ranks of the job (the values themselves without a process group):
+    the job's time is that of its slowest rank."""
+    import torch
+    if not dist:
+        return [float(v) for v in values]
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def job_value(world, units, ms):
+    """Whole-job throughput: the units every rank processed over the
+    max-over-ranks time (weak scaling: each rank does `units`)."""
+    return world * units / (ms / 1000.0)
+
+
 def reference_arm(args, rank):
     if rank != 0:
         return
@@ -280,11 +298,7 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
         frames += int(more.sum())
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
+    ms = max_over_ranks([e0.elapsed_time(e1)], dist, "cuda")[0]
     world = dist.get_world_size() if dist else 1
     ts.free()
     tb.free()
@@ -310,7 +324,7 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     return {**extra,
             "workload": workload,
             "metric": "frames/s per GPU @B=%d" % B if world == 1 else "box frames/s @B=%d per GPU" % B,
-            "value": world * frames / (ms / 1000.0), "unit": "frames/s", "steps": K, "warmup": W,
+            "value": job_value(world, frames, ms), "unit": "frames/s", "steps": K, "warmup": W,
             "ms_per_batched_frame": ms / K, "frames": frames, "prefill_s_rank0": prefill_s,
             "mean_ctx": float(ctx.mean()),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -485,11 +499,7 @@ def gpu_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms_e2e = f0.elapsed_time(f1)
     wall_e2e = time.perf_counter() - w0
-    # max over ranks
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = float(t[0]), float(t[1])
+    ms, ms_e2e = max_over_ranks([ms, ms_e2e], dist, "cuda")
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         # bounded CPU sample: ~15 s of the oracle on the host cores
@@ -500,7 +510,7 @@ def gpu_arm(args, rank, world, local_rank):
                "sample": f"{done} frames of the same utterance after its prefill (C restatement of the reference "
                          "CPU path, AVX2+FMA, OpenMP over output rows)"}
     if rank == 0:
-        fps = world * K / (ms / 1000.0)
+        fps = job_value(world, K, ms)
         wb = weight_bytes_per_frame(dtype, args.talker_layers, args.pred_layers)
         kv = sum(kv_bytes_frame(talker_len0 + f, args.talker_layers, args.pred_layers) for f in range(K)) / K
         alg = wb + kv  # algorithmic bytes per launch (one frame)
@@ -521,7 +531,7 @@ def gpu_arm(args, rank, world, local_rank):
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                          "kernel": "qtts::decode_kernel (frame mode)",
                          "algorithmic_bytes_per_launch": alg},
-            "e2e": {"value": world * K / (ms_e2e / 1000.0), "unit": "frames/s",
+            "e2e": {"value": job_value(world, K, ms_e2e), "unit": "frames/s",
                     "h2d_bytes_per_step": prompt_bytes / K,
                     "d2h_bytes_per_step": 104 + (3072 * 4) / K,
                     "wall_s_rank0": wall_e2e, "includes": "qtts_talker_start (prompt upload + prefill) + K x qtts_talker_next_frame"},
