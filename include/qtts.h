@@ -282,7 +282,9 @@ typedef struct qtts_sampling {
 int qtts_talker_set_sampling(qtts_talker *t, const qtts_sampling *s);
 /* TInferSampler.Next (the draw of talker.pas:626-629, 632-638) on the
  * device: the index drawn from work[n] (host float32 logits after the
- * processors, n <= 4096) with draw (step, group) of the stream `seed`. */
+ * processors, n <= 4096) with draw (step, group) of the stream `seed`.
+ * Blocking; it uses a buffer of the device object, so calls on one device
+ * from several threads must not overlap. */
 int qtts_sample(qtts_device *dev, const float *work, int n, float temperature, int top_k, float top_p,
                 uint64_t seed, int step, int group, int32_t *code);
 

@@ -92,6 +92,7 @@ struct qtts_device {
     size_t staging_bytes;
     int64_t bytes;      // stack weights held (TQwenVulkan.DeviceBytes)
     char name[256];
+    float *draw_in;     // qtts_sample: SAMPLE_MAX_V values + the code (made on first use)
 };
 
 struct qtts_stack {
@@ -598,6 +599,7 @@ extern "C" int qtts_device_close(qtts_device *dev) {
     if (!dev) return QTTS_OK;
     cudaSetDevice(dev->ordinal);
     if (dev->staging) cudaFree(dev->staging);
+    if (dev->draw_in) cudaFree(dev->draw_in);
     cudaStreamDestroy(dev->load);
     delete dev;
     return QTTS_OK;
@@ -1447,19 +1449,21 @@ extern "C" int qtts_sample(qtts_device *dev, const float *work, int n, float tem
     int rc = sampling_params("qtts_sample", 1, temperature, top_k, top_p, &p);
     if (rc) return rc;
     CK(cudaSetDevice(dev->ordinal));
-    float *d = nullptr;
-    int *dc = nullptr;
-    cudaError_t e = cudaMalloc(&d, static_cast<size_t>(n) * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&dc, 4);
-    if (e == cudaSuccess) e = cudaMemcpy(d, work, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice);
+    // the values and the code in one buffer of the device object, made on
+    // the first draw (draws on one device are serialised by the caller)
+    if (!dev->draw_in && cudaMalloc(&dev->draw_in, (SAMPLE_MAX_V + 1) * 4) != cudaSuccess) {
+        dev->draw_in = nullptr;
+        return set_err(QTTS_E_OOM, "qtts_sample: out of device memory");
+    }
+    float *d = dev->draw_in;
+    int *dc = reinterpret_cast<int *>(d + SAMPLE_MAX_V);
+    cudaError_t e = cudaMemcpy(d, work, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
         sample_kernel<<<1, NCT>>>(d, n, p, sample_uniform(seed, step, group), dc);
         e = cudaGetLastError();
     }
     int c = 0;
     if (e == cudaSuccess) e = cudaMemcpy(&c, dc, 4, cudaMemcpyDeviceToHost);
-    if (d) cudaFree(d);
-    if (dc) cudaFree(dc);
     if (e != cudaSuccess) return set_err(QTTS_E_CUDA, "qtts_sample: %s", cudaGetErrorString(e));
     *code = c;
     return QTTS_OK;
