@@ -499,7 +499,21 @@ def gpu_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms_e2e = f0.elapsed_time(f1)
     wall_e2e = time.perf_counter() - w0
-    ms, ms_e2e = max_over_ranks([ms, ms_e2e], dist, "cuda")
+    # the same frames in sampling mode, the reference engine's default
+    # (QwenSamplingFromConfig, talker.pas:203-230: temperature 0.9, top_k 50,
+    # top_p 1 for both choosers); everything resident, device events
+    tk.set_sampling(seed=SEED + rank)
+    tk.start(prompt, None, m["pad"])
+    run_frames(W)
+    tk.start(prompt, None, m["pad"])
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    restarts_s = run_frames(K)
+    g1.record(stream)
+    torch.cuda.synchronize()
+    ms_s = g0.elapsed_time(g1)
+    ms, ms_e2e, ms_s = max_over_ranks([ms, ms_e2e, ms_s], dist, "cuda")
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         # bounded CPU sample: ~15 s of the oracle on the host cores
@@ -539,6 +553,9 @@ def gpu_arm(args, rank, world, local_rank):
             "clocks": clk,
             "cpu_baseline": cpu,
             "restarts_at_eos": restarts,
+            "sampled": {"value": job_value(world, K, ms_s), "unit": "frames/s", "ms_per_frame": ms_s / K,
+                        "mode": "sampling: temperature 0.9, top_k 50, top_p 1 for code 0 and the predictor "
+                                "(qwen_tts defaults), seeded draws on the device", "restarts_at_eos": restarts_s},
             "batched": batched,
             "box": box,
             "prefill": prefill,
