@@ -429,6 +429,8 @@ struct Producer {
 
 // the draw of a frame's code from the logits lg[V] of the last head (NCT
 // threads; talker: ChooseCode0's processors first, as choose0_value)
+static_assert(sizeof(SampleScratch) <= sizeof(float) * ACT_FLOATS, "the draw's scratch lives in the activation buffer");
+
 __device__ __noinline__ int frame_draw(const float *lg, int V, SampleParams p, float u, SampleScratch *ss, int tid,
                                        bool talker, int vocab, int eos, int hist_now, const unsigned char *seen,
                                        float penalty) {

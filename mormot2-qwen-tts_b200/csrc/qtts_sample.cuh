@@ -18,9 +18,11 @@
 // them exactly.
 //
 // One CTA (NT threads, named barrier 1) draws: a radix select (4 passes of
-// 8 bits over the orderable keys) finds the top_k-th largest value, the
-// candidates are ranked by counting, the weights exp(z - z_max) are
-// computed in parallel and summed by thread 0.
+// 8 bits over the orderable keys, two histograms used in turn so that one
+// is cleared while the other is scanned) finds the top_k-th largest value,
+// the candidates are gathered one atomic per warp (ballot) and ranked by
+// counting, the weights exp(z - z_max) are computed in parallel and summed
+// by thread 0.
 #pragma once
 #include <stdint.h>
 
@@ -51,7 +53,7 @@ __host__ __device__ inline float sample_uniform(uint64_t seed, int step, int gro
 }
 
 struct SampleScratch {
-    unsigned hist[256];
+    unsigned hist[2][256];  // the radix passes alternate between the two
     unsigned cnt, sel, rem;
     int code;
     alignas(8) unsigned ckey[SAMPLE_MAX_CAND];
@@ -59,6 +61,7 @@ struct SampleScratch {
     int sidx[SAMPLE_MAX_CAND];
     float sz[SAMPLE_MAX_CAND];
     float sw[SAMPLE_MAX_CAND];
+    unsigned long long pk[SAMPLE_MAX_CAND];  // (key, ~index) of the candidates, for the ranking
 };
 
 // orderable key of a float (larger value, larger key) and back
@@ -93,20 +96,23 @@ __device__ int sample_draw(Load load, int V, const SampleParams &p, float u, Sam
     // radix select of the top_k-th largest key, 8 bits a pass from the top
     unsigned prefix = 0u, mask = 0u;
     unsigned rem = static_cast<unsigned>(min(max(p.top_k, 1), V));
+    for (int b = tid; b < 512; b += NT) (&ss->hist[0][0])[b] = 0u;
+    sample_sync<NT>();
     for (int d = 3; d >= 0; --d) {
-        for (int b = tid; b < 256; b += NT) ss->hist[b] = 0u;
-        sample_sync<NT>();
+        unsigned *hist = ss->hist[d & 1];
 #pragma unroll
         for (int j = 0; j < KPT; ++j)
-            if (tid + j * NT < V && (key[j] & mask) == prefix) atomicAdd(&ss->hist[(key[j] >> (8 * d)) & 255u], 1u);
+            if (tid + j * NT < V && (key[j] & mask) == prefix) atomicAdd(&hist[(key[j] >> (8 * d)) & 255u], 1u);
         sample_sync<NT>();
+        // the other histogram is cleared for the next pass while warp 0 scans this one
+        for (int b = tid - 32; b >= 0 && b < 256; b += NT - 32) ss->hist[(d & 1) ^ 1][b] = 0u;
         if (tid < 32) {
             // lane: bins 255 - 8 lane - q, q = 0..7 (descending); counts of
             // the bins above as an exclusive prefix over the lanes
             unsigned c[8], tot = 0u;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                c[q] = ss->hist[255 - 8 * lane - q];
+                c[q] = hist[255 - 8 * lane - q];
                 tot += c[q];
             }
             unsigned incl = tot;
@@ -133,15 +139,21 @@ __device__ int sample_draw(Load load, int V, const SampleParams &p, float u, Sam
         mask |= 0xFFu << (8 * d);
         rem = ss->rem;
     }
-    // candidates: keys >= the threshold, -inf excluded
+    // candidates: keys >= the threshold, -inf excluded; one atomic per
+    // warp and pass (ballot), each lane at its prefix in the warp's run
     if (tid == 0) ss->cnt = 0u;
     sample_sync<NT>();
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
         const int i = tid + j * NT;
-        if (i < V && key[j] >= prefix && key[j] != key_ninf) {
-            const unsigned s = atomicAdd(&ss->cnt, 1u);
-            if (s < SAMPLE_MAX_CAND) {
+        const bool c = i < V && key[j] >= prefix && key[j] != key_ninf;
+        const unsigned b = __ballot_sync(0xffffffffu, c);
+        if (b) {
+            unsigned base = 0u;
+            if (lane == __ffs(b) - 1) base = atomicAdd(&ss->cnt, static_cast<unsigned>(__popc(b)));
+            base = __shfl_sync(0xffffffffu, base, __ffs(b) - 1);
+            const unsigned s = base + static_cast<unsigned>(__popc(b & ((1u << lane) - 1u)));
+            if (c && s < SAMPLE_MAX_CAND) {
                 ss->ckey[s] = key[j];
                 ss->cidx[s] = i;
             }
@@ -175,17 +187,19 @@ __device__ int sample_draw(Load load, int V, const SampleParams &p, float u, Sam
         sample_sync<NT>();
         return static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(b & 0xFFFFFFFFull));
     }
-    // rank under (z desc, index asc)
+    // rank under (z desc, index asc): (key, ~index) as one 64-bit value,
+    // larger first; the loops stay rolled (the draw runs between layers,
+    // where its code is fetched cold: a smaller body is the faster one)
+    unsigned long long *pk = ss->pk;
+    for (int c = tid; c < n; c += NT)
+        pk[c] = (static_cast<unsigned long long>(ss->ckey[c]) << 32) | (0xFFFFFFFFu - static_cast<unsigned>(ss->cidx[c]));
+    sample_sync<NT>();
     for (int c = tid; c < n; c += NT) {
-        const unsigned kc = ss->ckey[c];
-        const int ic = ss->cidx[c];
+        const unsigned long long kc = pk[c];
         int r = 0;
-        for (int m = 0; m < n; ++m) {
-            const unsigned km = ss->ckey[m];
-            r += (km > kc || (km == kc && ss->cidx[m] < ic)) ? 1 : 0;
-        }
-        ss->sidx[r] = ic;
-        ss->sz[r] = sample_unkey(kc);
+        for (int m = 0; m < n; ++m) r += pk[m] > kc ? 1 : 0;
+        ss->sidx[r] = static_cast<int>(0xFFFFFFFFu - static_cast<unsigned>(kc));
+        ss->sz[r] = sample_unkey(static_cast<unsigned>(kc >> 32));
     }
     sample_sync<NT>();
     const float mx = ss->sz[0];
@@ -205,8 +219,11 @@ __device__ int sample_draw(Load load, int V, const SampleParams &p, float u, Sam
                 acc += ss->sw[c];
             }
         }
-        float wsum = 0.0f;
-        for (int c = 0; c < nk; ++c) wsum += ss->sw[c];
+        float wsum = total;
+        if (nk < n) {
+            wsum = 0.0f;
+            for (int c = 0; c < nk; ++c) wsum += ss->sw[c];
+        }
         const float target = u * wsum;
         float acc = 0.0f;
         int code = ss->sidx[nk - 1];
