@@ -305,6 +305,41 @@ int qtts_textproj_create(qtts_device *dev, int vocab, int text_hidden, int hidde
 int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, float *y);
 int qtts_textproj_destroy(qtts_textproj *t);
 
+/* The token ids that TQwenTalker.Start places around the text (config.json,
+ * read at talker.pas:256-265): text tokens tts_bos/tts_eos/tts_pad
+ * (tts_*_token_id; their rows are projections, talker.pas:339-344) and codec
+ * ids codec_pad/codec_bos (talker_config.codec_*_id). */
+typedef struct qtts_prompt_tokens {
+    int32_t tts_bos;
+    int32_t tts_eos;
+    int32_t tts_pad;
+    int32_t codec_pad;
+    int32_t codec_bos;
+} qtts_prompt_tokens;
+
+/* TQwenTalker.Start (talker.pas:528-592) from token ids, its rows built on
+ * the device: ids[n_ids] = PromptIds(text), i.e. [im_start, assistant, \n]
+ * text [im_end, \n, im_start, assistant, \n] (n_ids >= 9, as Start's "empty
+ * text" check); codec[n_codec] = the think / language / voice ids then
+ * codec_pad, codec_bos (talker.pas:515-527; n_codec >= 2); non_streaming =
+ * aNonStreaming.  Every prefill and trailing row is the text projection of
+ * one token (role, text, tts_pad/bos/eos) plus, for the rows over the
+ * codec, the talker's codec embedding of one id (AddRow); then as
+ * qtts_talker_start.  A text token outside [0, vocab) or a codec id outside
+ * [0, talker vocab) is QTTS_E_ARG.  tp and t on the same device; tp's hidden
+ * is the talker's. */
+int qtts_talker_start_prompt(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok, const int32_t *ids,
+                             int n_ids, const int32_t *codec, int n_codec, int non_streaming, float *logits,
+                             float *hidden);
+/* The rows qtts_talker_start_prompt builds, copied to the host (the probes
+ * talker.prefill.embeds and talker.trailing of Start, talker.pas:575-576):
+ * *rows and *trailing_rows receive the counts; with prefill and trailing
+ * both NULL only the counts, else prefill [prefill_cap][hidden] and
+ * trailing [trailing_cap][hidden] must hold them. */
+int qtts_talker_prompt_rows(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok, const int32_t *ids,
+                            int n_ids, const int32_t *codec, int n_codec, int non_streaming, float *prefill,
+                            int prefill_cap, float *trailing, int trailing_cap, int *rows, int *trailing_rows);
+
 /* ------------------------------------------------------------------ talkers (batched frames) */
 
 typedef struct qtts_talkers qtts_talkers;

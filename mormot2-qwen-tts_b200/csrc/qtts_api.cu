@@ -1068,7 +1068,8 @@ static Job base_job(qtts_lm *m) {
     return j;
 }
 
-extern "C" int qtts_lm_forward(qtts_lm *m, const float *x, int rows, int head, float *logits, float *hidden) {
+// x: host rows, or device rows when x_dev (the prompt built on the device)
+static int lm_forward(qtts_lm *m, const float *x, bool x_dev, int rows, int head, float *logits, float *hidden) {
     if (!m) return set_err(QTTS_E_ARG, "qtts_lm_forward: NULL lm");
     if (rows <= 0) return QTTS_OK;
     if (!x) return set_err(QTTS_E_ARG, "qtts_lm_forward: x is NULL");
@@ -1090,8 +1091,13 @@ extern "C" int qtts_lm_forward(qtts_lm *m, const float *x, int rows, int head, f
     for (int r0 = 0; r0 < rows; r0 += RMAX) {
         int n = rows - r0 < RMAX ? rows - r0 : RMAX;
         bool last = r0 + n == rows;
-        memcpy(m->h_x, x + static_cast<size_t>(r0) * H, static_cast<size_t>(n) * H * 4);
-        CK(cudaMemcpyAsync(m->d_x, m->h_x, static_cast<size_t>(n) * H * 4, cudaMemcpyHostToDevice, m->run.stream));
+        if (x_dev) {
+            CK(cudaMemcpyAsync(m->d_x, x + static_cast<size_t>(r0) * H, static_cast<size_t>(n) * H * 4,
+                               cudaMemcpyDeviceToDevice, m->run.stream));
+        } else {
+            memcpy(m->h_x, x + static_cast<size_t>(r0) * H, static_cast<size_t>(n) * H * 4);
+            CK(cudaMemcpyAsync(m->d_x, m->h_x, static_cast<size_t>(n) * H * 4, cudaMemcpyHostToDevice, m->run.stream));
+        }
         j.rows = n;
         j.L0 = m->len;
         j.head_w = (last && logits) ? m->heads->mats[head].d : nullptr;
@@ -1110,6 +1116,10 @@ extern "C" int qtts_lm_forward(qtts_lm *m, const float *x, int rows, int head, f
     if (logits) memcpy(logits, m->h_out, hr * 4);
     if (hidden) memcpy(hidden, m->h_out + m->max_head_rows, H * 4);
     return QTTS_OK;
+}
+
+extern "C" int qtts_lm_forward(qtts_lm *m, const float *x, int rows, int head, float *logits, float *hidden) {
+    return lm_forward(m, x, false, rows, head, logits, hidden);
 }
 
 extern "C" int qtts_lm_destroy(qtts_lm *m) {
@@ -1189,10 +1199,11 @@ extern "C" int qtts_talker_create(qtts_lm *talker, qtts_lm *pred, const qtts_tal
     return QTTS_OK;
 }
 
-extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows, const float *trailing, int trailing_rows,
-                                 const float *tts_pad, float *logits, float *hidden) {
-    if (!t || !prefill || !tts_pad || rows <= 0 || trailing_rows < 0 || (trailing_rows > 0 && !trailing))
-        return set_err(QTTS_E_ARG, "qtts_talker_start: bad argument");
+// rows_dev: prefill, trailing and tts_pad are device rows (the prompt built
+// on the device, on the talker's stream), else host rows
+static int talker_start(qtts_talker *t, bool rows_dev, const float *prefill, int rows, const float *trailing,
+                        int trailing_rows, const float *tts_pad, float *logits, float *hidden) {
+    const cudaMemcpyKind kind = rows_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     qtts_lm *tl = t->talker;
     CK(cudaSetDevice(tl->dev->ordinal));
     cudaStream_t st = tl->run.stream;
@@ -1203,16 +1214,16 @@ extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows,
         t->trailing_cap = trailing_rows;
     }
     if (trailing_rows > 0)
-        CK(cudaMemcpyAsync(t->trailing, trailing, static_cast<size_t>(trailing_rows) * H * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(t->trailing, trailing, static_cast<size_t>(trailing_rows) * H * 4, kind, st));
     t->trailing_rows = trailing_rows;
-    CK(cudaMemcpyAsync(t->tts_pad, tts_pad, H * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(t->tts_pad, tts_pad, H * 4, kind, st));
     CK(cudaMemsetAsync(t->seen, 0, t->cfg.vocab, st));
     t->started = 0;
     // TQwenTalker.Start: fTalker.Reset; fTalker.Forward(prefill, rows, 0, ...)
     qtts_lm_reset(tl);
     // the head always runs: the first ChooseCode0 reads its logits
     std::vector<float> tmp(logits ? 0 : t->cfg.vocab);
-    int rc = qtts_lm_forward(tl, prefill, rows, 0, logits ? logits : tmp.data(), hidden);
+    int rc = lm_forward(tl, prefill, rows_dev, rows, 0, logits ? logits : tmp.data(), hidden);
     if (rc) return rc;
     // the first ChooseCode0 (empty history): the argmax or the draw (0, 0);
     // then the frame state
@@ -1231,6 +1242,13 @@ extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows,
     t->done = h.done;
     t->started = 1;
     return QTTS_OK;
+}
+
+extern "C" int qtts_talker_start(qtts_talker *t, const float *prefill, int rows, const float *trailing, int trailing_rows,
+                                 const float *tts_pad, float *logits, float *hidden) {
+    if (!t || !prefill || !tts_pad || rows <= 0 || trailing_rows < 0 || (trailing_rows > 0 && !trailing))
+        return set_err(QTTS_E_ARG, "qtts_talker_start: bad argument");
+    return talker_start(t, false, prefill, rows, trailing, trailing_rows, tts_pad, logits, hidden);
 }
 
 static Job frame_job(qtts_talker *t) {
@@ -1502,10 +1520,14 @@ __global__ void text_gather_kernel(const void *emb, int dtype, int kdim, const i
 
 // y[r][o] = sum_k x[r][k] w[o][k] + b[o] (then silu as TextProject: 0 below
 // -80, else v / (1 + exp(-v))): a warp per output o, its weight row in
-// registers (kdim <= 32 * TP_KPL), the rows of x streamed
+// registers (kdim <= 32 * TP_KPL), the rows of x streamed.  With codec, row
+// r then gets codec_emb[codec[r]][o] added when codec[r] >= 0 (AddRow of
+// Start, talker.pas:423-429, over the projected row).
 constexpr int TP_KPL = 64;
 __global__ void __launch_bounds__(256) text_linear_kernel(const float *x, int n, int kdim, const float *w,
-                                                         const float *b, int odim, int silu, float *y) {
+                                                         const float *b, int odim, int silu, float *y,
+                                                         const int *codec = nullptr,
+                                                         const float *codec_emb = nullptr) {
     const int o = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (o >= odim) return;
     float wr[TP_KPL];
@@ -1528,6 +1550,7 @@ __global__ void __launch_bounds__(256) text_linear_kernel(const float *x, int n,
         if (lane == 0) {
             float v = acc + bo;
             if (silu) v = v < -80.f ? 0.f : v / (1.0f + expf(-v));
+            if (codec && codec[r] >= 0) v += codec_emb[static_cast<size_t>(codec[r]) * odim + o];
             y[static_cast<size_t>(r) * odim + o] = v;
         }
     }
@@ -1580,14 +1603,14 @@ extern "C" int qtts_textproj_create(qtts_device *dev, int vocab, int text_hidden
     return QTTS_OK;
 }
 
-extern "C" int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, float *y) {
-    if (!t || (n > 0 && (!ids || !y))) return set_err(QTTS_E_ARG, "qtts_text_project: NULL argument");
-    if (n <= 0) return QTTS_OK;
-    for (int r = 0; r < n; ++r)
-        if (ids[r] < 0 || ids[r] >= t->vocab)
-            return set_err(QTTS_E_ARG, "qtts_text_project: text token %d out of range", ids[r]);
+// t->y[n][hidden] = the projections of the text tokens ids[n] (host, checked
+// by the caller), each plus codec_emb[codec[r]] where codec (host, or NULL)
+// gives one >= 0; ids and codec go up on `st`, which then holds the work
+static int textproj_run(qtts_textproj *t, const int32_t *ids, const int32_t *codec, const float *codec_emb, int n,
+                        cudaStream_t st) {
     CK(cudaSetDevice(t->dev->ordinal));
     if (n > t->cap) {
+        CK(cudaStreamSynchronize(st));
         for (void *p : {static_cast<void *>(t->e), static_cast<void *>(t->h), static_cast<void *>(t->y),
                         static_cast<void *>(t->ids)})
             if (p) cudaFree(p);
@@ -1597,17 +1620,128 @@ extern "C" int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, fl
         cudaError_t e = cudaMalloc(&t->e, static_cast<size_t>(n) * t->text_hidden * 4);
         if (e == cudaSuccess) e = cudaMalloc(&t->h, static_cast<size_t>(n) * t->text_hidden * 4);
         if (e == cudaSuccess) e = cudaMalloc(&t->y, static_cast<size_t>(n) * t->hidden * 4);
-        if (e == cudaSuccess) e = cudaMalloc(&t->ids, static_cast<size_t>(n) * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&t->ids, static_cast<size_t>(n) * 2 * 4);  // ids, then codec
         if (e != cudaSuccess) return set_err(QTTS_E_OOM, "qtts_text_project: %s", cudaGetErrorString(e));
         t->cap = n;
     }
-    CK(cudaMemcpy(t->ids, ids, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice));
-    text_gather_kernel<<<n, 256>>>(t->emb, t->emb_dtype, t->text_hidden, t->ids, n, t->e);
-    text_linear_kernel<<<(t->text_hidden + 7) / 8, 256>>>(t->e, n, t->text_hidden, t->w1, t->b1, t->text_hidden, 1,
-                                                          t->h);
-    text_linear_kernel<<<(t->hidden + 7) / 8, 256>>>(t->h, n, t->text_hidden, t->w2, t->b2, t->hidden, 0, t->y);
+    int *d_codec = t->ids + t->cap;
+    CK(cudaMemcpyAsync(t->ids, ids, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, st));
+    if (codec) CK(cudaMemcpyAsync(d_codec, codec, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, st));
+    text_gather_kernel<<<n, 256, 0, st>>>(t->emb, t->emb_dtype, t->text_hidden, t->ids, n, t->e);
+    text_linear_kernel<<<(t->text_hidden + 7) / 8, 256, 0, st>>>(t->e, n, t->text_hidden, t->w1, t->b1,
+                                                                 t->text_hidden, 1, t->h);
+    text_linear_kernel<<<(t->hidden + 7) / 8, 256, 0, st>>>(t->h, n, t->text_hidden, t->w2, t->b2, t->hidden, 0,
+                                                            t->y, codec ? d_codec : nullptr, codec_emb);
     CK(cudaGetLastError());
+    return QTTS_OK;
+}
+
+extern "C" int qtts_text_project(qtts_textproj *t, const int32_t *ids, int n, float *y) {
+    if (!t || (n > 0 && (!ids || !y))) return set_err(QTTS_E_ARG, "qtts_text_project: NULL argument");
+    if (n <= 0) return QTTS_OK;
+    for (int r = 0; r < n; ++r)
+        if (ids[r] < 0 || ids[r] >= t->vocab)
+            return set_err(QTTS_E_ARG, "qtts_text_project: text token %d out of range", ids[r]);
+    int rc = textproj_run(t, ids, nullptr, nullptr, n, 0);
+    if (rc) return rc;
     CK(cudaMemcpy(y, t->y, static_cast<size_t>(n) * t->hidden * 4, cudaMemcpyDeviceToHost));
+    return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ the prompt of Start
+
+// The rows of TQwenTalker.Start (talker.pas:528-574), each as (text token,
+// codec id or -1): every row is the projection of one text token (the role,
+// the text, or tts_pad / tts_bos / tts_eos, whose vectors are projections
+// too, talker.pas:339-344), plus one codec embedding for the rows over the
+// codec.  Listed in the order prefill rows, trailing rows, then tts_pad (the
+// row after the trailing text).
+struct PromptPlan {
+    std::vector<int32_t> text, codec;
+    int rows = 0, trailing = 0;
+};
+
+static int prompt_plan(const char *fn, const qtts_talker *t, const qtts_textproj *tp, const qtts_prompt_tokens *tok,
+                       const int32_t *ids, int n_ids, const int32_t *codec, int n_codec, int non_streaming,
+                       PromptPlan &p) {
+    if (!t || !tp || !tok || !ids || !codec) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
+    // [im_start, assistant, \n] text [im_end, \n, im_start, assistant, \n]
+    if (n_ids < 9) return set_err(QTTS_E_ARG, "%s: empty text (%d prompt ids, at least 9)", fn, n_ids);
+    if (n_codec < 2) return set_err(QTTS_E_ARG, "%s: %d codec ids (at least pad and bos)", fn, n_codec);
+    if (tp->dev != t->talker->dev || tp->hidden != H)
+        return set_err(QTTS_E_ARG, "%s: the text projection is on another device or %d wide", fn, tp->hidden);
+    auto row = [&p](int32_t text, int32_t c) {
+        p.text.push_back(text);
+        p.codec.push_back(c);
+    };
+    const int32_t *text = ids + 3;
+    const int n_text = n_ids - 8;
+    // the role (3 rows), then tts_pad x (codec - 2) + tts_bos over the codec
+    // ids but the last one
+    for (int i = 0; i < 3; ++i) row(ids[i], -1);
+    for (int i = 0; i < n_codec - 1; ++i) row(i < n_codec - 2 ? tok->tts_pad : tok->tts_bos, codec[i]);
+    if (non_streaming) {
+        // the text then tts_eos, each over codec_pad; tts_pad over codec_bos;
+        // what follows is tts_pad alone
+        for (int i = 0; i < n_text; ++i) row(text[i], tok->codec_pad);
+        row(tok->tts_eos, tok->codec_pad);
+        row(tok->tts_pad, tok->codec_bos);
+        p.rows = static_cast<int>(p.text.size());
+        row(tok->tts_pad, -1);
+    } else {
+        // the first text token over codec_bos; the next ones then tts_eos,
+        // one per frame
+        row(text[0], tok->codec_bos);
+        p.rows = static_cast<int>(p.text.size());
+        for (int i = 1; i < n_text; ++i) row(text[i], -1);
+        row(tok->tts_eos, -1);
+    }
+    p.trailing = static_cast<int>(p.text.size()) - p.rows;
+    row(tok->tts_pad, -1);
+    for (size_t r = 0; r < p.text.size(); ++r) {
+        if (p.text[r] < 0 || p.text[r] >= tp->vocab)
+            return set_err(QTTS_E_ARG, "%s: text token %d out of range", fn, p.text[r]);
+        if (p.codec[r] >= t->cfg.vocab) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
+        if (p.codec[r] < -1) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
+    }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talker_start_prompt(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok,
+                                        const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
+                                        int non_streaming, float *logits, float *hidden) {
+    PromptPlan p;
+    int rc = prompt_plan("qtts_talker_start_prompt", t, tp, tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    if (rc) return rc;
+    cudaStream_t st = t->talker->run.stream;
+    rc = textproj_run(tp, p.text.data(), p.codec.data(), t->codec_emb, static_cast<int>(p.text.size()), st);
+    if (rc) return rc;
+    const float *y = tp->y;
+    return talker_start(t, true, y, p.rows, y + static_cast<size_t>(p.rows) * H, p.trailing,
+                        y + static_cast<size_t>(p.rows + p.trailing) * H, logits, hidden);
+}
+
+extern "C" int qtts_talker_prompt_rows(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok,
+                                       const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
+                                       int non_streaming, float *prefill, int prefill_cap, float *trailing,
+                                       int trailing_cap, int *rows, int *trailing_rows) {
+    PromptPlan p;
+    int rc = prompt_plan("qtts_talker_prompt_rows", t, tp, tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    if (rc) return rc;
+    if (rows) *rows = p.rows;
+    if (trailing_rows) *trailing_rows = p.trailing;
+    if (!prefill && !trailing) return QTTS_OK;  // the counts alone
+    if (!prefill || !trailing || prefill_cap < p.rows || trailing_cap < p.trailing)
+        return set_err(QTTS_E_ARG, "qtts_talker_prompt_rows: buffers of %d and %d rows for %d and %d", prefill_cap,
+                       trailing_cap, p.rows, p.trailing);
+    cudaStream_t st = t->talker->run.stream;
+    rc = textproj_run(tp, p.text.data(), p.codec.data(), t->codec_emb, static_cast<int>(p.text.size()), st);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(prefill, tp->y, static_cast<size_t>(p.rows) * H * 4, cudaMemcpyDeviceToHost, st));
+    if (p.trailing > 0)
+        CK(cudaMemcpyAsync(trailing, tp->y + static_cast<size_t>(p.rows) * H, static_cast<size_t>(p.trailing) * H * 4,
+                           cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
     return QTTS_OK;
 }
 

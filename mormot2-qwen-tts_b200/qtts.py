@@ -65,6 +65,54 @@ class Sampling(ctypes.Structure):
                 ("sub_top_k", ctypes.c_int32), ("sub_top_p", ctypes.c_float), ("seed", ctypes.c_uint64)]
 
 
+class PromptTokens(ctypes.Structure):
+    """The token ids around the text in TQwenTalker.Start (talker.pas:256-265)."""
+    _fields_ = [("tts_bos", ctypes.c_int32), ("tts_eos", ctypes.c_int32), ("tts_pad", ctypes.c_int32),
+                ("codec_pad", ctypes.c_int32), ("codec_bos", ctypes.c_int32)]
+
+
+def prompt_tokens(config):
+    """PromptTokens from a config.json dict (TQwenTalker.Create, talker.pas:
+    256-261): tts_*_token_id at the top, codec_*_id in talker_config."""
+    tc = config["talker_config"]
+    return PromptTokens(config["tts_bos_token_id"], config["tts_eos_token_id"], config["tts_pad_token_id"],
+                        tc["codec_pad_id"], tc["codec_bos_id"])
+
+
+def start_codec_ids(talker_config, speaker="", language=""):
+    """The codec ids of TQwenTalker.Start (talker.pas:488-527): think,
+    think_bos, language, think_eos (nothink, think_bos, think_eos when the
+    language is auto), the voice, then codec_pad and codec_bos.  A dialect
+    voice (spk_is_dialect naming a codec language) speaking chinese or auto
+    takes that language.  Unknown voice or language: EQwenLm, as Start
+    raises."""
+    tc = talker_config
+    spk = (speaker or "").lower()
+    spk_id = -1
+    if spk:
+        if spk not in tc.get("spk_id", {}):
+            raise EQwenLm(E_ARG, "Start: unknown speaker %r" % speaker)
+        spk_id = int(tc["spk_id"][spk])
+    lang = (language or "").lower() or "auto"
+    lang_id = -1
+    if lang != "auto":
+        if lang not in tc.get("codec_language_id", {}):
+            raise EQwenLm(E_ARG, "Start: unknown language %r" % language)
+        lang_id = int(tc["codec_language_id"][lang])
+    if spk and lang in ("chinese", "auto"):
+        d = tc.get("spk_is_dialect", {}).get(spk)
+        d = "" if d is None else (str(d).lower() if isinstance(d, bool) else str(d))
+        if d not in ("", "false", "true") and d in tc.get("codec_language_id", {}):
+            lang_id = int(tc["codec_language_id"][d])
+    if lang_id < 0:
+        codec = [tc["codec_nothink_id"], tc["codec_think_bos_id"], tc["codec_think_eos_id"]]
+    else:
+        codec = [tc["codec_think_id"], tc["codec_think_bos_id"], lang_id, tc["codec_think_eos_id"]]
+    if spk_id >= 0:
+        codec.append(spk_id)
+    return codec + [tc["codec_pad_id"], tc["codec_bos_id"]]
+
+
 P = ctypes.c_void_p
 I = ctypes.c_int
 PI = ctypes.POINTER(ctypes.c_int)
@@ -118,6 +166,8 @@ EXPORTS = {
     "qtts_textproj_create": [P, I, I, I, I, P, P, P, P, P, ctypes.POINTER(P)],
     "qtts_text_project": [P, P, I, P],
     "qtts_textproj_destroy": [P],
+    "qtts_talker_start_prompt": [P, P, ctypes.POINTER(PromptTokens), P, I, P, I, I, P, P],
+    "qtts_talker_prompt_rows": [P, P, ctypes.POINTER(PromptTokens), P, I, P, I, I, P, I, P, I, PI, PI],
 }
 
 
@@ -415,6 +465,30 @@ class QwenTalker:
         check(lib().qtts_talker_start(self.handle, _ptr(p), p.size // self.hidden, _ptr(t),
                                       0 if t is None else t.size // self.hidden, _ptr(_f32(tts_pad)),
                                       _ptr(logits), _ptr(hidden)))
+
+    def start_prompt(self, textproj, tokens, ids, codec, non_streaming=False, logits=None, hidden=None):
+        """TQwenTalker.Start from token ids, the prompt rows built on the
+        device: ids = PromptIds(text), codec = start_codec_ids(...),
+        tokens = prompt_tokens(config)."""
+        i = np.ascontiguousarray(ids, dtype=np.int32)
+        c = np.ascontiguousarray(codec, dtype=np.int32)
+        check(lib().qtts_talker_start_prompt(self.handle, textproj.handle, ctypes.byref(tokens), _ptr(i), i.size,
+                                             _ptr(c), c.size, int(non_streaming), _ptr(logits), _ptr(hidden)))
+
+    def prompt_rows(self, textproj, tokens, ids, codec, non_streaming=False):
+        """(prefill, trailing) rows that start_prompt builds (the probes
+        talker.prefill.embeds / talker.trailing)."""
+        i = np.ascontiguousarray(ids, dtype=np.int32)
+        c = np.ascontiguousarray(codec, dtype=np.int32)
+        rows, tr = ctypes.c_int(), ctypes.c_int()
+        args = (self.handle, textproj.handle, ctypes.byref(tokens), _ptr(i), i.size, _ptr(c), c.size,
+                int(non_streaming))
+        check(lib().qtts_talker_prompt_rows(*args, None, 0, None, 0, ctypes.byref(rows), ctypes.byref(tr)))
+        pf = np.zeros((rows.value, self.hidden), np.float32)
+        tt = np.zeros((tr.value, self.hidden), np.float32)
+        check(lib().qtts_talker_prompt_rows(*args, _ptr(pf), rows.value, _ptr(tt), tr.value, ctypes.byref(rows),
+                                            ctypes.byref(tr)))
+        return pf, tt
 
     def next_frame(self, codes):
         """TQwenTalker.NextFrame: fills codes[groups] (int32); False at eos."""

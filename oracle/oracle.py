@@ -169,6 +169,49 @@ def text_project(emb, ids, w1, b1, w2, b2):
     return y
 
 
+def start_rows(emb, w1, b1, w2, b2, codec_emb, tokens, ids, codec, non_streaming=False):
+    """The rows of TQwenTalker.Start (talker.pas:528-574) restated step by
+    step: (prefill, trailing, tts_pad).  tokens: dict with tts_bos, tts_eos,
+    tts_pad, codec_pad, codec_bos.  The tts vectors are projections of their
+    token ids (talker.pas:339-344); AddRow adds a codec embedding row."""
+    ce = _f32(codec_emb)
+    proj = lambda t: text_project(emb, list(t), w1, b1, w2, b2)  # noqa: E731
+    tts_bos, tts_eos, tts_pad = (proj([tokens[k]])[0] for k in ("tts_bos", "tts_eos", "tts_pad"))
+    ids = list(ids)
+    n_codec = len(codec)
+    text = ids[3:3 + len(ids) - 8]
+    n_text = len(text)
+    hidden = ce.shape[1]
+    if non_streaming:
+        rows = 3 + (n_codec - 1) + (n_text + 1) + 1
+    else:
+        rows = 3 + (n_codec - 1) + 1
+    prefill = np.zeros((rows, hidden), np.float32)
+    prefill[0:3] = proj(ids[0:3])
+    r = 3
+    for i in range(n_codec - 1):
+        prefill[r] = tts_pad if i < n_codec - 2 else tts_bos
+        prefill[r] += ce[codec[i]]
+        r += 1
+    if non_streaming:
+        prefill[r:r + n_text] = proj(text)
+        prefill[r + n_text] = tts_eos
+        for i in range(n_text + 1):
+            prefill[r + i] += ce[tokens["codec_pad"]]
+        r += n_text + 1
+        prefill[r] = tts_pad
+        prefill[r] += ce[tokens["codec_bos"]]
+        trailing = tts_pad[None, :].copy()
+    else:
+        prefill[r] = proj(text[0:1])[0]
+        prefill[r] += ce[tokens["codec_bos"]]
+        trailing = np.zeros((n_text, hidden), np.float32)
+        if n_text > 1:
+            trailing[0:n_text - 1] = proj(text[1:])
+        trailing[n_text - 1] = tts_eos
+    return prefill, trailing, tts_pad
+
+
 def rope_table(max_pos, head_dim, theta):
     c = np.empty((max_pos, head_dim // 2), dtype=np.float32)
     s = np.empty_like(c)
