@@ -49,6 +49,9 @@ extern "C" {
 #define QTTS_DTYPE_F32 0
 #define QTTS_DTYPE_Q8_0 1 /* ggml block_q8_0: fp16 scale + 32 int8, 34 bytes */
 #define QTTS_DTYPE_BF16 2 /* source rows only: widened exactly to float32 */
+#define QTTS_DTYPE_F16 3  /* a safetensors F16 tensor (not a weight source) */
+#define QTTS_DTYPE_OTHER -1 /* a safetensors tensor of another dtype */
+#define QTTS_MAX_DIMS 8   /* dimensions of a safetensors tensor */
 
 typedef struct qtts_device qtts_device;
 typedef struct qtts_stack qtts_stack;
@@ -56,6 +59,7 @@ typedef struct qtts_heads qtts_heads;
 typedef struct qtts_lm qtts_lm;
 typedef struct qtts_talker qtts_talker;
 typedef struct qtts_textproj qtts_textproj;
+typedef struct qtts_safetensors qtts_safetensors;
 
 /* The decoder configuration of one stack (TDecoderConfig: talker_config or
  * talker_config.code_predictor_config of config.json, talker.pas:252-273).
@@ -339,6 +343,47 @@ int qtts_talker_start_prompt(qtts_talker *t, qtts_textproj *tp, const qtts_promp
 int qtts_talker_prompt_rows(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok, const int32_t *ids,
                             int n_ids, const int32_t *codec, int n_codec, int non_streaming, float *prefill,
                             int prefill_cap, float *trailing, int trailing_cap, int *rows, int *trailing_rows);
+
+/* ------------------------------------------------------------------ files */
+
+/* TSafeTensorsFile.Create (mormot2-ai; used at talker.pas:299): maps a
+ * .safetensors file read-only and reads its header.  A header that is not
+ * the format (size, JSON, unknown dtype, data_offsets outside the data or
+ * not shape x dtype bytes, a name twice) is QTTS_E_ARG. */
+int qtts_safetensors_open(const char *path, qtts_safetensors **out);
+/* The tensors of the file, in header order: count, then name i. */
+int qtts_safetensors_count(qtts_safetensors *f, int *n);
+int qtts_safetensors_name(qtts_safetensors *f, int i, char *buf, int len);
+/* TSafeTensorsFile.Tensor (talker.pas:300): dtype (QTTS_DTYPE_F32, _BF16,
+ * _F16 or _OTHER), ndim and shape[QTTS_MAX_DIMS], a pointer to its bytes in
+ * the mapping (valid until close) and their count; NULL outputs skipped.  An
+ * absent name is QTTS_E_ARG. */
+int qtts_safetensors_tensor(qtts_safetensors *f, const char *name, int *dtype, int *ndim, int64_t *shape,
+                            const void **data, int64_t *bytes);
+int qtts_safetensors_close(qtts_safetensors *f);
+
+/* QwenLmStack (lm.pas:174-179: TQwen3Model.CreateStack of the file, with
+ * aPrefix "talker.model." or "talker.code_predictor.model."): the stack
+ * from the tensors {prefix}layers.{i}.self_attn.{q,k,v,o}_proj.weight,
+ * .self_attn.{q,k}_norm.weight, .mlp.{gate,up,down}_proj.weight,
+ * .input_layernorm.weight, .post_attention_layernorm.weight and
+ * {prefix}norm.weight.  Matrices F32 or BF16 (read in place, converted on
+ * the device to config->dtype as qtts_stack_create); norms widened to
+ * float32 (QwenWiden, lm.pas:159-172).  A missing tensor or a shape other
+ * than the config's is QTTS_E_ARG. */
+int qtts_stack_create_safetensors(qtts_device *dev, const qtts_stack_config *config, qtts_safetensors *f,
+                                  const char *prefix, qtts_stack **out);
+/* TQwenLmHeads.Add (lm.pas:277-308) from the file's tensor `name`
+ * ([rows][hidden], F32 or BF16, e.g. talker.codec_head.weight,
+ * talker.code_predictor.lm_head.{g}.weight). */
+int qtts_heads_add_safetensors(qtts_heads *heads, qtts_safetensors *f, const char *name, int rows, int *index);
+/* The cached blob of a stack: its weights as held on the device (F32 rows
+ * or row-packed Q8_0), its config and norms, and a crc32c of the whole,
+ * written to `path` (through path.tmp, then renamed) ... */
+int qtts_stack_save(const qtts_stack *stack, const char *path);
+/* ... and read back without a conversion.  Not a blob of this build
+ * (magic, dimensions, size) or a checksum mismatch: QTTS_E_ARG. */
+int qtts_stack_load(qtts_device *dev, const char *path, qtts_stack **out);
 
 /* ------------------------------------------------------------------ talkers (batched frames) */
 

@@ -29,6 +29,7 @@
 #include "qtts_decode.cuh"
 #include "qtts_gemm.cuh"
 #include "qtts_batch.cuh"
+#include "qtts_safetensors.h"
 
 #include <cudaTypedefs.h>
 
@@ -612,15 +613,18 @@ static void stack_free(qtts_stack *s) {
     delete s;
 }
 
-extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, const qtts_layer_src *layers,
-                                 const float *final_norm, qtts_stack **out) {
-    if (!dev || !c || !layers || !final_norm || !out) return set_err(QTTS_E_ARG, "qtts_stack_create: NULL argument");
-    *out = nullptr;
-    if (!dims_ok(c))
-        return set_err(QTTS_E_ARG, "qtts_stack_create: unsupported dimensions (hidden %d, heads %d/%d, head_dim %d, intermediate %d, layers %d)",
-                       c->hidden, c->heads, c->kv_heads, c->head_dim, c->intermediate, c->layers);
-    if (c->dtype != QTTS_DTYPE_F32 && c->dtype != QTTS_DTYPE_Q8_0)
-        return set_err(QTTS_E_ARG, "qtts_stack_create: weights must be F32 or Q8_0");
+// The matrices of layer l into its device buffers (wqkv [QKV_ROWS], wo,
+// wgu [gate/up interleaved], wd, in the stack's format), and its four norms
+// (float32 host pointers: input, post, q, k).
+struct LayerFill {
+    virtual int matrices(int l, uint8_t *wqkv, uint8_t *wo, uint8_t *wgu, uint8_t *wd) = 0;
+    virtual void norms(int l, const float *n[4]) = 0;
+};
+
+// One Qwen3 stack on the device from `fill`: allocations, the batch-1
+// per-head layouts, the norms and the layer table
+static int stack_build(qtts_device *dev, const qtts_stack_config *c, LayerFill &fill, const float *final_norm,
+                       qtts_stack **out) {
     CK(cudaSetDevice(dev->ordinal));
     qtts_stack *s = new qtts_stack();
     s->dev = dev;
@@ -637,12 +641,6 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
     };
     int64_t mat_bytes = 0;
     for (int l = 0; l < c->layers && rc == QTTS_OK; ++l) {
-        const qtts_layer_src &a = layers[l];
-        int sd = a.dtype;
-        if (sd != QTTS_DTYPE_F32 && sd != QTTS_DTYPE_BF16 && sd != QTTS_DTYPE_Q8_0) {
-            rc = set_err(QTTS_E_ARG, "qtts_stack_create: layer %d has dtype %d", l, sd);
-            break;
-        }
         DLayer &d = hl[l];
         size_t bqkv = static_cast<size_t>(QKV_ROWS) * row_bytes(wdt, H);
         size_t bo = static_cast<size_t>(H) * row_bytes(wdt, QDIM);
@@ -656,14 +654,7 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
             break;
         }
         mat_bytes += bqkv + bo + bgu + bd;
-        int dt = c->dtype;
-        if ((rc = upload_matrix(dev, a.q_proj, sd, QDIM, H, wqkv, dt, 1, 0))) break;
-        if ((rc = upload_matrix(dev, a.k_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM))) break;
-        if ((rc = upload_matrix(dev, a.v_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM + KVDIM))) break;
-        if ((rc = upload_matrix(dev, a.o_proj, sd, H, QDIM, wo, dt, 1, 0))) break;
-        if ((rc = upload_matrix(dev, a.gate_proj, sd, INTER, H, wgu, dt, 2, 0))) break;
-        if ((rc = upload_matrix(dev, a.up_proj, sd, INTER, H, wgu, dt, 2, 1))) break;
-        if ((rc = upload_matrix(dev, a.down_proj, sd, H, INTER, wd, dt, 1, 0))) break;
+        if ((rc = fill.matrices(l, wqkv, wo, wgu, wd))) break;
         {
             const long long nq = static_cast<long long>(QKV_ROWS) * (row_bytes(wdt, H) / 16);
             qkv_by_head_kernel<<<static_cast<unsigned>((nq + 255) / 256), 256, 0, dev->load>>>(wqkv, wdt, wqkvh);
@@ -679,14 +670,16 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
         d.woh = woh;
         d.wgu = wgu;
         d.wd = wd;
+        const float *n[4];
+        fill.norms(l, n);
         float *p;
-        if ((rc = upload_floats(dev, a.input_norm, H, &p, s->allocs))) break;
+        if ((rc = upload_floats(dev, n[0], H, &p, s->allocs))) break;
         d.in_norm = p;
-        if ((rc = upload_floats(dev, a.post_norm, H, &p, s->allocs))) break;
+        if ((rc = upload_floats(dev, n[1], H, &p, s->allocs))) break;
         d.post_norm = p;
-        if ((rc = upload_floats(dev, a.q_norm, HD, &p, s->allocs))) break;
+        if ((rc = upload_floats(dev, n[2], HD, &p, s->allocs))) break;
         d.q_norm = p;
-        if ((rc = upload_floats(dev, a.k_norm, HD, &p, s->allocs))) break;
+        if ((rc = upload_floats(dev, n[3], HD, &p, s->allocs))) break;
         d.k_norm = p;
     }
     if (rc == QTTS_OK) rc = upload_floats(dev, final_norm, H, &s->d_final_norm, s->allocs);
@@ -711,6 +704,50 @@ extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, c
     dev->bytes += s->bytes;
     *out = s;
     return QTTS_OK;
+}
+
+extern "C" int qtts_stack_create(qtts_device *dev, const qtts_stack_config *c, const qtts_layer_src *layers,
+                                 const float *final_norm, qtts_stack **out) {
+    if (!dev || !c || !layers || !final_norm || !out) return set_err(QTTS_E_ARG, "qtts_stack_create: NULL argument");
+    *out = nullptr;
+    if (!dims_ok(c))
+        return set_err(QTTS_E_ARG, "qtts_stack_create: unsupported dimensions (hidden %d, heads %d/%d, head_dim %d, intermediate %d, layers %d)",
+                       c->hidden, c->heads, c->kv_heads, c->head_dim, c->intermediate, c->layers);
+    if (c->dtype != QTTS_DTYPE_F32 && c->dtype != QTTS_DTYPE_Q8_0)
+        return set_err(QTTS_E_ARG, "qtts_stack_create: weights must be F32 or Q8_0");
+    for (int l = 0; l < c->layers; ++l) {
+        const int sd = layers[l].dtype;
+        if (sd != QTTS_DTYPE_F32 && sd != QTTS_DTYPE_BF16 && sd != QTTS_DTYPE_Q8_0)
+            return set_err(QTTS_E_ARG, "qtts_stack_create: layer %d has dtype %d", l, sd);
+    }
+    // host rows (F32, BF16 or ggml Q8_0 blocks), converted on the device
+    struct HostFill : LayerFill {
+        qtts_device *dev;
+        const qtts_layer_src *layers;
+        int dt;
+        int matrices(int l, uint8_t *wqkv, uint8_t *wo, uint8_t *wgu, uint8_t *wd) override {
+            const qtts_layer_src &a = layers[l];
+            const int sd = a.dtype;
+            int rc;
+            if ((rc = upload_matrix(dev, a.q_proj, sd, QDIM, H, wqkv, dt, 1, 0))) return rc;
+            if ((rc = upload_matrix(dev, a.k_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM))) return rc;
+            if ((rc = upload_matrix(dev, a.v_proj, sd, KVDIM, H, wqkv, dt, 1, QDIM + KVDIM))) return rc;
+            if ((rc = upload_matrix(dev, a.o_proj, sd, H, QDIM, wo, dt, 1, 0))) return rc;
+            if ((rc = upload_matrix(dev, a.gate_proj, sd, INTER, H, wgu, dt, 2, 0))) return rc;
+            if ((rc = upload_matrix(dev, a.up_proj, sd, INTER, H, wgu, dt, 2, 1))) return rc;
+            return upload_matrix(dev, a.down_proj, sd, H, INTER, wd, dt, 1, 0);
+        }
+        void norms(int l, const float *n[4]) override {
+            n[0] = layers[l].input_norm;
+            n[1] = layers[l].post_norm;
+            n[2] = layers[l].q_norm;
+            n[3] = layers[l].k_norm;
+        }
+    } fill;
+    fill.dev = dev;
+    fill.layers = layers;
+    fill.dt = c->dtype;
+    return stack_build(dev, c, fill, final_norm, out);
 }
 
 extern "C" int qtts_stack_bytes(const qtts_stack *s, int64_t *bytes) {
@@ -1750,6 +1787,274 @@ extern "C" int qtts_textproj_destroy(qtts_textproj *t) {
     cudaSetDevice(t->dev->ordinal);
     textproj_free(t);
     return QTTS_OK;
+}
+
+// ------------------------------------------------------------------ files
+
+struct qtts_safetensors {
+    qtts_st::File f;
+    std::string path;
+};
+
+extern "C" int qtts_safetensors_open(const char *path, qtts_safetensors **out) {
+    if (!path || !out) return set_err(QTTS_E_ARG, "qtts_safetensors_open: NULL argument");
+    *out = nullptr;
+    qtts_safetensors *f = new qtts_safetensors();
+    f->path = path;
+    std::string err;
+    if (!f->f.open(path, err)) {
+        delete f;
+        return set_err(QTTS_E_ARG, "qtts_safetensors_open: %s: %s", path, err.c_str());
+    }
+    *out = f;
+    return QTTS_OK;
+}
+
+extern "C" int qtts_safetensors_count(qtts_safetensors *f, int *n) {
+    if (!f || !n) return set_err(QTTS_E_ARG, "qtts_safetensors_count: NULL argument");
+    *n = static_cast<int>(f->f.tensors.size());
+    return QTTS_OK;
+}
+
+extern "C" int qtts_safetensors_name(qtts_safetensors *f, int i, char *buf, int len) {
+    if (!f || !buf || len <= 0 || i < 0 || i >= static_cast<int>(f->f.tensors.size()))
+        return set_err(QTTS_E_ARG, "qtts_safetensors_name: bad argument");
+    const std::string &n = f->f.tensors[i].name;
+    if (static_cast<int>(n.size()) >= len) return set_err(QTTS_E_ARG, "qtts_safetensors_name: buffer of %d for %d", len,
+                                                          static_cast<int>(n.size()) + 1);
+    memcpy(buf, n.c_str(), n.size() + 1);
+    return QTTS_OK;
+}
+
+static int st_dtype(const std::string &d) {
+    if (d == "F32") return QTTS_DTYPE_F32;
+    if (d == "BF16") return QTTS_DTYPE_BF16;
+    if (d == "F16") return QTTS_DTYPE_F16;
+    return QTTS_DTYPE_OTHER;
+}
+
+extern "C" int qtts_safetensors_tensor(qtts_safetensors *f, const char *name, int *dtype, int *ndim, int64_t *shape,
+                                       const void **data, int64_t *bytes) {
+    if (!f || !name) return set_err(QTTS_E_ARG, "qtts_safetensors_tensor: NULL argument");
+    const qtts_st::Tensor *t = f->f.find(name);
+    if (!t) return set_err(QTTS_E_ARG, "qtts_safetensors_tensor: no tensor %s in %s", name, f->path.c_str());
+    if (t->shape.size() > QTTS_MAX_DIMS)
+        return set_err(QTTS_E_ARG, "qtts_safetensors_tensor: %s has %d dimensions", name,
+                       static_cast<int>(t->shape.size()));
+    if (dtype) *dtype = st_dtype(t->dtype);
+    if (ndim) *ndim = static_cast<int>(t->shape.size());
+    if (shape)
+        for (size_t i = 0; i < t->shape.size(); ++i) shape[i] = t->shape[i];
+    if (data) *data = f->f.data + t->begin;
+    if (bytes) *bytes = static_cast<int64_t>(t->end - t->begin);
+    return QTTS_OK;
+}
+
+extern "C" int qtts_safetensors_close(qtts_safetensors *f) {
+    delete f;
+    return QTTS_OK;
+}
+
+// the tensor `name` as [rows][cols] in F32 or BF16 (its bytes in the
+// mapping), else QTTS_E_ARG as QwenWiden raises (lm.pas:164-168)
+static int st_matrix(qtts_safetensors *f, const std::string &name, int64_t rows, int64_t cols, const void **data,
+                     int *dtype) {
+    const qtts_st::Tensor *t = f->f.find(name);
+    if (!t) return set_err(QTTS_E_ARG, "%s: no tensor %s", f->path.c_str(), name.c_str());
+    if (f->f.count(*t) != static_cast<uint64_t>(rows * cols))
+        return set_err(QTTS_E_ARG, "%s: %s has %llu values instead of [%lld,%lld]", f->path.c_str(), name.c_str(),
+                       static_cast<unsigned long long>(f->f.count(*t)), static_cast<long long>(rows),
+                       static_cast<long long>(cols));
+    const int dt = st_dtype(t->dtype);
+    if (dt != QTTS_DTYPE_F32 && dt != QTTS_DTYPE_BF16)
+        return set_err(QTTS_E_ARG, "%s: %s is %s (F32 or BF16 expected)", f->path.c_str(), name.c_str(),
+                       t->dtype.c_str());
+    *data = f->f.data + t->begin;
+    *dtype = dt;
+    return QTTS_OK;
+}
+
+// QwenWiden (lm.pas:159-172): the tensor widened to float32 on the host
+static int st_widen(qtts_safetensors *f, const std::string &name, int64_t n, std::vector<float> &out) {
+    const void *d;
+    int dt;
+    int rc = st_matrix(f, name, 1, n, &d, &dt);
+    if (rc) return rc;
+    out.resize(static_cast<size_t>(n));
+    if (dt == QTTS_DTYPE_F32) {
+        memcpy(out.data(), d, static_cast<size_t>(n) * 4);
+    } else {
+        const uint8_t *b = static_cast<const uint8_t *>(d);
+        for (int64_t i = 0; i < n; ++i) {
+            const uint32_t v = static_cast<uint32_t>(b[2 * i] | (b[2 * i + 1] << 8)) << 16;
+            memcpy(&out[i], &v, 4);
+        }
+    }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_stack_create_safetensors(qtts_device *dev, const qtts_stack_config *c, qtts_safetensors *f,
+                                             const char *prefix, qtts_stack **out) {
+    if (!dev || !c || !f || !prefix || !out) return set_err(QTTS_E_ARG, "qtts_stack_create_safetensors: NULL argument");
+    *out = nullptr;
+    if (c->layers <= 0 || c->layers > 1024) return set_err(QTTS_E_ARG, "qtts_stack_create_safetensors: %d layers", c->layers);
+    const int64_t hid = c->hidden, q = static_cast<int64_t>(c->heads) * c->head_dim,
+                  kv = static_cast<int64_t>(c->kv_heads) * c->head_dim, inter = c->intermediate;
+    std::vector<qtts_layer_src> src(c->layers);
+    std::vector<std::vector<float>> norms(static_cast<size_t>(c->layers) * 4);
+    for (int l = 0; l < c->layers; ++l) {
+        const std::string p = std::string(prefix) + "layers." + std::to_string(l) + ".";
+        qtts_layer_src &s = src[l];
+        struct M {
+            const char *name;
+            int64_t rows, cols;
+            const void **dst;
+        } mats[] = {{"self_attn.q_proj.weight", q, hid, &s.q_proj},   {"self_attn.k_proj.weight", kv, hid, &s.k_proj},
+                    {"self_attn.v_proj.weight", kv, hid, &s.v_proj},  {"self_attn.o_proj.weight", hid, q, &s.o_proj},
+                    {"mlp.gate_proj.weight", inter, hid, &s.gate_proj}, {"mlp.up_proj.weight", inter, hid, &s.up_proj},
+                    {"mlp.down_proj.weight", hid, inter, &s.down_proj}};
+        for (int m = 0; m < 7; ++m) {
+            int dt;
+            int rc = st_matrix(f, p + mats[m].name, mats[m].rows, mats[m].cols, mats[m].dst, &dt);
+            if (rc) return rc;
+            if (m == 0) s.dtype = dt;
+            if (dt != s.dtype)
+                return set_err(QTTS_E_ARG, "%s: the matrices of layer %d mix F32 and BF16", f->path.c_str(), l);
+        }
+        const char *nn[4] = {"input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
+                             "self_attn.k_norm.weight"};
+        const int64_t nl[4] = {hid, hid, c->head_dim, c->head_dim};
+        for (int k = 0; k < 4; ++k) {
+            int rc = st_widen(f, p + nn[k], nl[k], norms[static_cast<size_t>(l) * 4 + k]);
+            if (rc) return rc;
+        }
+        s.input_norm = norms[static_cast<size_t>(l) * 4].data();
+        s.post_norm = norms[static_cast<size_t>(l) * 4 + 1].data();
+        s.q_norm = norms[static_cast<size_t>(l) * 4 + 2].data();
+        s.k_norm = norms[static_cast<size_t>(l) * 4 + 3].data();
+    }
+    std::vector<float> fn;
+    int rc = st_widen(f, std::string(prefix) + "norm.weight", hid, fn);
+    if (rc) return rc;
+    return qtts_stack_create(dev, c, src.data(), fn.data(), out);
+}
+
+extern "C" int qtts_heads_add_safetensors(qtts_heads *h, qtts_safetensors *f, const char *name, int rows, int *index) {
+    if (!h || !f || !name) return set_err(QTTS_E_ARG, "qtts_heads_add_safetensors: NULL argument");
+    if (rows <= 0) return set_err(QTTS_E_ARG, "qtts_heads_add_safetensors: %d rows", rows);
+    const void *d;
+    int dt;
+    int rc = st_matrix(f, name, rows, h->hidden, &d, &dt);
+    if (rc) return rc;
+    return qtts_heads_add(h, d, dt, rows, index);
+}
+
+// The cached blob of a stack: its weights in the device format (F32 rows or
+// row-packed Q8_0, as held), written and read back without a conversion.
+//   "QTTSSTK1" | qtts_stack_config | per layer: wqkv wo wgu wd (device
+//   bytes), input / post / q / k norms (float32) | final norm | crc32c of
+//   all the bytes before it (u32, little-endian)
+static const char BLOB_MAGIC[8] = {'Q', 'T', 'T', 'S', 'S', 'T', 'K', '1'};
+
+struct LayerBytes {
+    size_t qkv, o, gu, d;
+};
+static LayerBytes layer_bytes(int wdt) {
+    return {static_cast<size_t>(QKV_ROWS) * row_bytes(wdt, H), static_cast<size_t>(H) * row_bytes(wdt, QDIM),
+            static_cast<size_t>(GU_ROWS) * row_bytes(wdt, H), static_cast<size_t>(H) * row_bytes(wdt, INTER)};
+}
+
+extern "C" int qtts_stack_save(const qtts_stack *s, const char *path) {
+    if (!s || !path) return set_err(QTTS_E_ARG, "qtts_stack_save: NULL argument");
+    CK(cudaSetDevice(s->dev->ordinal));
+    const int wdt = s->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    const LayerBytes lb = layer_bytes(wdt);
+    std::vector<uint8_t> blob(sizeof(BLOB_MAGIC) + sizeof(qtts_stack_config));
+    memcpy(blob.data(), BLOB_MAGIC, sizeof(BLOB_MAGIC));
+    memcpy(blob.data() + sizeof(BLOB_MAGIC), &s->cfg, sizeof(qtts_stack_config));
+    auto append = [&](const void *dptr, size_t n) -> int {
+        const size_t at = blob.size();
+        blob.resize(at + n);
+        CK(cudaMemcpy(blob.data() + at, dptr, n, cudaMemcpyDeviceToHost));
+        return QTTS_OK;
+    };
+    int rc = QTTS_OK;
+    for (const DLayer &d : s->hlayers) {
+        if ((rc = append(d.wqkv, lb.qkv)) || (rc = append(d.wo, lb.o)) || (rc = append(d.wgu, lb.gu)) ||
+            (rc = append(d.wd, lb.d)) || (rc = append(d.in_norm, H * 4)) || (rc = append(d.post_norm, H * 4)) ||
+            (rc = append(d.q_norm, HD * 4)) || (rc = append(d.k_norm, HD * 4)))
+            return rc;
+    }
+    if ((rc = append(s->d_final_norm, H * 4))) return rc;
+    const uint32_t crc = crc32c(0, blob.data(), blob.size());
+    for (int i = 0; i < 4; ++i) blob.push_back(static_cast<uint8_t>(crc >> (8 * i)));
+    const std::string tmp = std::string(path) + ".tmp";
+    FILE *fp = fopen(tmp.c_str(), "wb");
+    if (!fp) return set_err(QTTS_E_ARG, "qtts_stack_save: cannot write %s", tmp.c_str());
+    const bool ok = fwrite(blob.data(), 1, blob.size(), fp) == blob.size();
+    if (fclose(fp) != 0 || !ok || rename(tmp.c_str(), path) != 0) {
+        remove(tmp.c_str());
+        return set_err(QTTS_E_ARG, "qtts_stack_save: writing %s failed", path);
+    }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_stack_load(qtts_device *dev, const char *path, qtts_stack **out) {
+    if (!dev || !path || !out) return set_err(QTTS_E_ARG, "qtts_stack_load: NULL argument");
+    *out = nullptr;
+    qtts_st::File map;  // only its mapping is used
+    map.fd = ::open(path, O_RDONLY | O_CLOEXEC);
+    struct stat st;
+    if (map.fd < 0 || fstat(map.fd, &st) != 0) return set_err(QTTS_E_ARG, "qtts_stack_load: cannot open %s", path);
+    map.size = static_cast<size_t>(st.st_size);
+    const size_t head = sizeof(BLOB_MAGIC) + sizeof(qtts_stack_config);
+    if (map.size < head + 4) return set_err(QTTS_E_ARG, "qtts_stack_load: %s is no stack blob", path);
+    map.map = mmap(nullptr, map.size, PROT_READ, MAP_PRIVATE, map.fd, 0);
+    if (map.map == MAP_FAILED) {
+        map.map = nullptr;
+        return set_err(QTTS_E_ARG, "qtts_stack_load: mmap of %s failed", path);
+    }
+    const uint8_t *b = static_cast<const uint8_t *>(map.map);
+    qtts_stack_config c;
+    memcpy(&c, b + sizeof(BLOB_MAGIC), sizeof(c));
+    if (memcmp(b, BLOB_MAGIC, sizeof(BLOB_MAGIC)) != 0 || !dims_ok(&c) || c.layers > 1024 ||
+        (c.dtype != QTTS_DTYPE_F32 && c.dtype != QTTS_DTYPE_Q8_0))
+        return set_err(QTTS_E_ARG, "qtts_stack_load: %s is no stack blob of this build's dimensions", path);
+    const int wdt = c.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
+    const LayerBytes lb = layer_bytes(wdt);
+    const size_t per_layer = lb.qkv + lb.o + lb.gu + lb.d + (2 * H + 2 * HD) * 4;
+    if (map.size != head + per_layer * c.layers + H * 4 + 4)
+        return set_err(QTTS_E_ARG, "qtts_stack_load: %s has %zu bytes, %zu expected", path, map.size,
+                       head + per_layer * c.layers + H * 4 + 4);
+    uint32_t want = 0;
+    for (int i = 3; i >= 0; --i) want = (want << 8) | b[map.size - 4 + i];
+    if (crc32c(0, b, map.size - 4) != want) return set_err(QTTS_E_ARG, "qtts_stack_load: %s: checksum mismatch", path);
+    // the layers from their device bytes, uploaded as they are; then the
+    // create path's norms, per-head layouts and layer table
+    struct BlobFill : LayerFill {
+        const uint8_t *base;
+        LayerBytes lb;
+        size_t per_layer;
+        int matrices(int l, uint8_t *wqkv, uint8_t *wo, uint8_t *wgu, uint8_t *wd) override {
+            const uint8_t *p = base + per_layer * l;
+            CK(cudaMemcpy(wqkv, p, lb.qkv, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(wo, p + lb.qkv, lb.o, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(wgu, p + lb.qkv + lb.o, lb.gu, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(wd, p + lb.qkv + lb.o + lb.gu, lb.d, cudaMemcpyHostToDevice));
+            return QTTS_OK;
+        }
+        void norms(int l, const float *n[4]) override {
+            const uint8_t *p = base + per_layer * l + lb.qkv + lb.o + lb.gu + lb.d;
+            n[0] = reinterpret_cast<const float *>(p);
+            n[1] = reinterpret_cast<const float *>(p + H * 4);
+            n[2] = reinterpret_cast<const float *>(p + 2 * H * 4);
+            n[3] = reinterpret_cast<const float *>(p + 2 * H * 4 + HD * 4);
+        }
+    } fill;
+    fill.base = b + head;
+    fill.lb = lb;
+    fill.per_layer = per_layer;
+    return stack_build(dev, &c, fill, reinterpret_cast<const float *>(b + head + per_layer * c.layers), out);
 }
 
 extern "C" int qtts_quantize_q8_0(qtts_device *dev, const float *src, int64_t n, uint8_t *dst) {

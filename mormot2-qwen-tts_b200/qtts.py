@@ -124,6 +124,15 @@ EXPORTS = {
     "qtts_device_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
     "qtts_device_close": [P],
     "qtts_stack_create": [P, ctypes.POINTER(StackConfig), ctypes.POINTER(LayerSrc), P, ctypes.POINTER(P)],
+    "qtts_safetensors_open": [ctypes.c_char_p, ctypes.POINTER(P)],
+    "qtts_safetensors_count": [P, PI],
+    "qtts_safetensors_name": [P, I, ctypes.c_char_p, I],
+    "qtts_safetensors_tensor": [P, ctypes.c_char_p, PI, PI, P, ctypes.POINTER(P), ctypes.POINTER(ctypes.c_int64)],
+    "qtts_safetensors_close": [P],
+    "qtts_stack_create_safetensors": [P, ctypes.POINTER(StackConfig), P, ctypes.c_char_p, ctypes.POINTER(P)],
+    "qtts_heads_add_safetensors": [P, P, ctypes.c_char_p, I, PI],
+    "qtts_stack_save": [P, ctypes.c_char_p],
+    "qtts_stack_load": [P, ctypes.c_char_p, ctypes.POINTER(P)],
     "qtts_stack_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
     "qtts_stack_destroy": [P],
     "qtts_heads_create": [P, ctypes.c_char_p, I, I, ctypes.POINTER(P)],
@@ -265,6 +274,73 @@ class QwenStack:
         return v.value
 
 
+    def save(self, path):
+        """The cached blob of the stack (its device bytes, config, norms and
+        a crc32c)."""
+        check(lib().qtts_stack_save(self.handle, os.fsencode(path)))
+
+
+def _stack_config(config, layers, dtype):
+    return StackConfig(layers, config["hidden"], config["heads"], config["kv_heads"], config["head_dim"],
+                       config["intermediate"], config["rms_eps"], config["rope_theta"], DTYPES[dtype])
+
+
+def qwen_lm_stack_load(device, path):
+    """A stack from a blob written by QwenStack.save, without a conversion."""
+    h = P()
+    check(lib().qtts_stack_load(device.handle, os.fsencode(path), ctypes.byref(h)))
+    return QwenStack(h, None)
+
+
+class SafeTensorsFile:
+    """TSafeTensorsFile: a .safetensors file mapped read-only by the library."""
+
+    DTYPE_NAMES = {DTYPE_F32: "F32", DTYPE_BF16: "BF16", 3: "F16", -1: "other"}
+
+    def __init__(self, path):
+        h = P()
+        check(lib().qtts_safetensors_open(os.fsencode(path), ctypes.byref(h)))
+        self.handle = h
+        self.path = path
+
+    def names(self):
+        n = ctypes.c_int()
+        check(lib().qtts_safetensors_count(self.handle, ctypes.byref(n)))
+        out = []
+        buf = ctypes.create_string_buffer(4096)
+        for i in range(n.value):
+            check(lib().qtts_safetensors_name(self.handle, i, buf, len(buf)))
+            out.append(buf.value.decode())
+        return out
+
+    def tensor(self, name):
+        """(dtype name, shape, bytes) of the tensor `name`; the bytes are a
+        copy of the mapped data."""
+        dt, nd = ctypes.c_int(), ctypes.c_int()
+        shape = (ctypes.c_int64 * 8)()
+        data, nb = P(), ctypes.c_int64()
+        check(lib().qtts_safetensors_tensor(self.handle, name.encode(), ctypes.byref(dt), ctypes.byref(nd), shape,
+                                            ctypes.byref(data), ctypes.byref(nb)))
+        raw = ctypes.string_at(data.value, nb.value) if nb.value else b""
+        return self.DTYPE_NAMES[dt.value], tuple(shape[i] for i in range(nd.value)), raw
+
+    def close(self):
+        if self.handle:
+            check(lib().qtts_safetensors_close(self.handle))
+            self.handle = None
+
+
+def qwen_lm_stack_safetensors(device, config, layers, file, prefix, dtype="q8_0"):
+    """QwenLmStack (lm.pas:174-179) from a safetensors file: the tensors
+    {prefix}layers.{i}.* and {prefix}norm.weight (e.g. prefix
+    'talker.model.'), converted on the device to `dtype`."""
+    cfg = _stack_config(config, layers, dtype)
+    h = P()
+    check(lib().qtts_stack_create_safetensors(device.handle, ctypes.byref(cfg), file.handle, prefix.encode(),
+                                              ctypes.byref(h)))
+    return QwenStack(h, layers)
+
+
 def qwen_lm_stack(device, config, layers, final_norm, dtype="q8_0"):
     """QwenLmStack (lm.pas:174-179): config = dict of the decoder config
     (layers, hidden, heads, kv_heads, head_dim, intermediate, rms_eps,
@@ -310,6 +386,13 @@ class QwenLmHeads:
             raise EQwenLm(E_ARG, f"{self.name}: head of {t.size} values instead of [{rows},{self.hidden}]")
         idx = ctypes.c_int()
         check(lib().qtts_heads_add(self.handle, _ptr(t), DTYPE_F32, rows, ctypes.byref(idx)))
+        return idx.value
+
+    def add_file(self, file, name, rows):
+        """TQwenLmHeads.Add from a safetensors tensor [rows][hidden] (F32 or
+        BF16, read in place); returns its index."""
+        idx = ctypes.c_int()
+        check(lib().qtts_heads_add_safetensors(self.handle, file.handle, name.encode(), rows, ctypes.byref(idx)))
         return idx.value
 
     def digest(self):
