@@ -408,6 +408,14 @@ int qtts_talkers_create(qtts_batch *talker, qtts_batch *predictor, const qtts_ta
  * them, empty history, ChooseCode0 of frame 0. */
 int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows, const float *prefill,
                        const int32_t *trailing_rows, const float *trailing, const float *tts_pad);
+/* TQwenTalker.Start from token ids (as qtts_talker_start_prompt) for nseq
+ * utterances seqs[i] at once, every prompt row built on the device in one
+ * text projection: utterance i's ids (n_ids[i] of them) and codec ids
+ * (n_codec[i]) follow those of the utterances before it in ids / codec;
+ * non_streaming[i] (NULL: all streaming).  Then as qtts_talkers_start. */
+int qtts_talkers_start_prompt(qtts_talkers *t, qtts_textproj *tp, const qtts_prompt_tokens *tok, int nseq,
+                              const int32_t *seqs, const int32_t *ids, const int32_t *n_ids, const int32_t *codec,
+                              const int32_t *n_codec, const int32_t *non_streaming);
 /* TQwenTalker.NextFrame (talker.pas:640-681) for nseq started utterances
  * seqs[i] (distinct): codes [nseq][groups] receives row i's frame and
  * more[i] = 1, or more[i] = 0 when the utterance has chosen eos (its codes

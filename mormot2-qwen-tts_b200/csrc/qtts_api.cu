@@ -1698,14 +1698,14 @@ struct PromptPlan {
     int rows = 0, trailing = 0;
 };
 
-static int prompt_plan(const char *fn, const qtts_talker *t, const qtts_textproj *tp, const qtts_prompt_tokens *tok,
-                       const int32_t *ids, int n_ids, const int32_t *codec, int n_codec, int non_streaming,
-                       PromptPlan &p) {
-    if (!t || !tp || !tok || !ids || !codec) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
+static int prompt_plan(const char *fn, const qtts_device *dev, int codec_vocab, const qtts_textproj *tp,
+                       const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
+                       int non_streaming, PromptPlan &p) {
+    if (!tp || !tok || !ids || !codec) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
     // [im_start, assistant, \n] text [im_end, \n, im_start, assistant, \n]
     if (n_ids < 9) return set_err(QTTS_E_ARG, "%s: empty text (%d prompt ids, at least 9)", fn, n_ids);
     if (n_codec < 2) return set_err(QTTS_E_ARG, "%s: %d codec ids (at least pad and bos)", fn, n_codec);
-    if (tp->dev != t->talker->dev || tp->hidden != H)
+    if (tp->dev != dev || tp->hidden != H)
         return set_err(QTTS_E_ARG, "%s: the text projection is on another device or %d wide", fn, tp->hidden);
     auto row = [&p](int32_t text, int32_t c) {
         p.text.push_back(text);
@@ -1738,7 +1738,7 @@ static int prompt_plan(const char *fn, const qtts_talker *t, const qtts_textproj
     for (size_t r = 0; r < p.text.size(); ++r) {
         if (p.text[r] < 0 || p.text[r] >= tp->vocab)
             return set_err(QTTS_E_ARG, "%s: text token %d out of range", fn, p.text[r]);
-        if (p.codec[r] >= t->cfg.vocab) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
+        if (p.codec[r] >= codec_vocab) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
         if (p.codec[r] < -1) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
     }
     return QTTS_OK;
@@ -1747,8 +1747,10 @@ static int prompt_plan(const char *fn, const qtts_talker *t, const qtts_textproj
 extern "C" int qtts_talker_start_prompt(qtts_talker *t, qtts_textproj *tp, const qtts_prompt_tokens *tok,
                                         const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
                                         int non_streaming, float *logits, float *hidden) {
+    if (!t) return set_err(QTTS_E_ARG, "qtts_talker_start_prompt: NULL talker");
     PromptPlan p;
-    int rc = prompt_plan("qtts_talker_start_prompt", t, tp, tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    int rc = prompt_plan("qtts_talker_start_prompt", t->talker->dev, t->cfg.vocab, tp, tok, ids, n_ids, codec, n_codec,
+                         non_streaming, p);
     if (rc) return rc;
     cudaStream_t st = t->talker->run.stream;
     rc = textproj_run(tp, p.text.data(), p.codec.data(), t->codec_emb, static_cast<int>(p.text.size()), st);
@@ -1762,8 +1764,10 @@ extern "C" int qtts_talker_prompt_rows(qtts_talker *t, qtts_textproj *tp, const 
                                        const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
                                        int non_streaming, float *prefill, int prefill_cap, float *trailing,
                                        int trailing_cap, int *rows, int *trailing_rows) {
+    if (!t) return set_err(QTTS_E_ARG, "qtts_talker_prompt_rows: NULL talker");
     PromptPlan p;
-    int rc = prompt_plan("qtts_talker_prompt_rows", t, tp, tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    int rc = prompt_plan("qtts_talker_prompt_rows", t->talker->dev, t->cfg.vocab, tp, tok, ids, n_ids, codec, n_codec,
+                         non_streaming, p);
     if (rc) return rc;
     if (rows) *rows = p.rows;
     if (trailing_rows) *trailing_rows = p.trailing;
@@ -2805,10 +2809,12 @@ static int talkers_finish(qtts_talkers *t, const char *who) {
     return QTTS_OK;
 }
 
-extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows,
-                                  const float *prefill, const int32_t *trailing_rows, const float *trailing,
-                                  const float *tts_pad) {
+// rows_dev: prefill, trailing and tts_pad are device rows (the prompts built
+// on the device, queued on t->stream), else host rows
+static int talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows, const float *prefill,
+                         const int32_t *trailing_rows, const float *trailing, const float *tts_pad, bool rows_dev) {
     if (!t || !rows || !prefill || !tts_pad) return set_err(QTTS_E_ARG, "qtts_talkers_start: NULL argument");
+    const cudaMemcpyKind kind = rows_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     int rc = distinct_seqs(t, nseq, seqs, "qtts_talkers_start");
     if (rc) return rc;
     size_t ntrail = 0;
@@ -2833,11 +2839,11 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
         if (tr > 0) {
             if (cudaMalloc(&t->trail[s], static_cast<size_t>(tr) * H * 4) != cudaSuccess)
                 return set_err(QTTS_E_OOM, "qtts_talkers_start: out of device memory");
-            CK(cudaMemcpy(t->trail[s], src, static_cast<size_t>(tr) * H * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(t->trail[s], src, static_cast<size_t>(tr) * H * 4, kind));
             src += static_cast<size_t>(tr) * H;
         }
         CK(cudaMemcpy(t->d_trail + s, &t->trail[s], sizeof(float *), cudaMemcpyHostToDevice));
-        CK(cudaMemcpy(t->tts_pad + static_cast<size_t>(s) * H, tts_pad, H * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(t->tts_pad + static_cast<size_t>(s) * H, tts_pad, H * 4, kind));
         qtts_batch_reset(t->tb, s);
         io_seqs(t)[i] = s;
         io_aux(t)[i] = tr;
@@ -2848,7 +2854,7 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
     CK(cudaMemsetAsync(t->pb->err, 0, 16, st));
     frames_start_kernel<<<nseq, 256, 0, st>>>(t->d_seqs, t->d_aux, t->ss, t->seen, t->cfg.vocab);
     CK(cudaGetLastError());
-    if ((rc = batch_run(t->tb, nseq, seqs, rows, prefill, false, 0, st))) return rc;
+    if ((rc = batch_run(t->tb, nseq, seqs, rows, prefill, rows_dev, 0, st))) return rc;
     frames_choose0_kernel<<<nseq, 256, 0, st>>>(t->d_seqs, t->tb->logits, t->tb->hidden, t->cfg.vocab,
                                                 t->cfg.codec_eos, t->cfg.repetition_penalty, t->seen, t->ss, t->hid,
                                                 t->d_done, 1, t->samp0, static_cast<unsigned long long>(t->seed));
@@ -2859,6 +2865,48 @@ extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs
         t->done[seqs[i]] = 0;  // eos is forbidden before 2 frames
     }
     return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const int32_t *rows,
+                                  const float *prefill, const int32_t *trailing_rows, const float *trailing,
+                                  const float *tts_pad) {
+    return talkers_start(t, nseq, seqs, rows, prefill, trailing_rows, trailing, tts_pad, false);
+}
+
+extern "C" int qtts_talkers_start_prompt(qtts_talkers *t, qtts_textproj *tp, const qtts_prompt_tokens *tok, int nseq,
+                                         const int32_t *seqs, const int32_t *ids, const int32_t *n_ids,
+                                         const int32_t *codec, const int32_t *n_codec, const int32_t *non_streaming) {
+    const char *fn = "qtts_talkers_start_prompt";
+    if (!t || !tp || !seqs || !ids || !n_ids || !codec || !n_codec || nseq <= 0)
+        return set_err(QTTS_E_ARG, "%s: NULL argument or no utterance", fn);
+    // every utterance's rows as (text token, codec id): the prefill rows of
+    // all utterances in order, then their trailing rows, then tts_pad
+    std::vector<int32_t> rows(nseq), trs(nseq), pt, pc, tt, tc;
+    size_t io = 0, co = 0;
+    for (int i = 0; i < nseq; ++i) {
+        if (n_ids[i] < 0 || n_codec[i] < 0) return set_err(QTTS_E_ARG, "%s: entry %d: negative count", fn, i);
+        PromptPlan p;
+        int rc = prompt_plan(fn, t->tb->dev, t->cfg.vocab, tp, tok, ids + io, n_ids[i], codec + co, n_codec[i],
+                             non_streaming ? non_streaming[i] : 0, p);
+        if (rc) return rc;
+        rows[i] = p.rows;
+        trs[i] = p.trailing;
+        pt.insert(pt.end(), p.text.begin(), p.text.begin() + p.rows);
+        pc.insert(pc.end(), p.codec.begin(), p.codec.begin() + p.rows);
+        tt.insert(tt.end(), p.text.begin() + p.rows, p.text.begin() + p.rows + p.trailing);
+        tc.insert(tc.end(), p.codec.begin() + p.rows, p.codec.begin() + p.rows + p.trailing);
+        io += static_cast<size_t>(n_ids[i]);
+        co += static_cast<size_t>(n_codec[i]);
+    }
+    const size_t R = pt.size(), T = tt.size();
+    pt.insert(pt.end(), tt.begin(), tt.end());
+    pc.insert(pc.end(), tc.begin(), tc.end());
+    pt.push_back(tok->tts_pad);
+    pc.push_back(-1);
+    int rc = textproj_run(tp, pt.data(), pc.data(), t->codec_emb, static_cast<int>(pt.size()), t->stream);
+    if (rc) return rc;
+    const float *y = tp->y;
+    return talkers_start(t, nseq, seqs, rows.data(), y, trs.data(), y + R * H, y + (R + T) * H, true);
 }
 
 // context splits per sequence of the batched talker step: about 4 waves of

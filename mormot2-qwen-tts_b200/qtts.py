@@ -168,6 +168,7 @@ EXPORTS = {
     "qtts_sample": [P, P, I, ctypes.c_float, I, ctypes.c_float, ctypes.c_uint64, I, I, PI],
     "qtts_talkers_create": [P, P, ctypes.POINTER(TalkerConfig), P, P, ctypes.POINTER(P)],
     "qtts_talkers_start": [P, I, P, P, P, P, P, P],
+    "qtts_talkers_start_prompt": [P, P, ctypes.POINTER(PromptTokens), I, P, P, P, P, P, P],
     "qtts_talkers_next_frame": [P, I, P, P, P],
     "qtts_talkers_stream": [P, ctypes.POINTER(P)],
     "qtts_talkers_destroy": [P],
@@ -685,6 +686,19 @@ class QwenTalkers:
         tr = _f32(np.concatenate(tl)) if tl else None
         check(lib().qtts_talkers_start(self.handle, sq.size, _ptr(sq), _ptr(rows), _ptr(pf), _ptr(trs), _ptr(tr),
                                        _ptr(_f32(tts_pad))))
+
+    def start_prompt(self, textproj, tokens, seqs, prompts):
+        """TQwenTalker.Start from token ids for utterances seqs[i], their
+        rows built on the device: prompts[i] = (ids, codec, non_streaming)
+        as QwenTalker.start_prompt takes them."""
+        sq = np.ascontiguousarray(seqs, dtype=np.int32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p[0], np.int32) for p in prompts]), np.int32)
+        codec = np.ascontiguousarray(np.concatenate([np.asarray(p[1], np.int32) for p in prompts]), np.int32)
+        n_ids = np.array([len(p[0]) for p in prompts], np.int32)
+        n_codec = np.array([len(p[1]) for p in prompts], np.int32)
+        ns = np.array([int(p[2]) for p in prompts], np.int32)
+        check(lib().qtts_talkers_start_prompt(self.handle, textproj.handle, ctypes.byref(tokens), sq.size, _ptr(sq),
+                                              _ptr(ids), _ptr(n_ids), _ptr(codec), _ptr(n_codec), _ptr(ns)))
 
     def next_frame(self, seqs):
         """TQwenTalker.NextFrame for utterances seqs: returns (codes [n][groups],

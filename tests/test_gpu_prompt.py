@@ -122,3 +122,39 @@ def test_start_prompt_checks_its_ids(device):
     assert tk.t.dev.length == 3 + 6 + 1
     tp.free()
     tk.free()
+
+
+def test_batched_start_prompt_matches_oracle(device):
+    # qtts_talkers_start_prompt: three utterances (streaming and not, texts of
+    # 1, 4 and 9 tokens) started in one call; each oracle talker starts from
+    # the oracle's own rows, then the frames are checked as the batched
+    # frame loop's (every choice a maximum of the oracle's values)
+    from test_gpu_frames import GAP, Rig, frame
+    bits, emb, w1, b1, w2, b2 = textproj_weights(17)
+    rig = Rig(device, 94, 2, 2, "f32", "f32", nseq=3)
+    tp = qtts.QwenTextProject(device, bits, w1, b1, w2, b2)
+    prompts = [(prompt_ids(18, 4), CODEC, False), (prompt_ids(19, 1), CODEC[-2:], True),
+               (prompt_ids(20, 9), CODEC[:3] + CODEC[-2:], False)]
+    seqs = [2, 0, 1]
+    rig.dev.start_prompt(tp, tokens(), seqs, prompts)
+    ce = synth.codec_embedding(94)
+    rows = {}
+    for s, (ids, codec, ns) in zip(seqs, prompts):
+        pf, tr, pad = O.start_rows(emb, w1, b1, w2, b2, ce, TOK, ids, codec, ns)
+        rig.ora[s].start(pf, tr, pad)
+        rows[s] = pf.shape[0]
+    stats = [0, 0]
+    live = list(seqs)
+    frames = {s: 0 for s in seqs}
+    for _ in range(4):
+        _, more = frame(rig, live, GAP[("f32", "f32")], stats)
+        for s, m in zip(list(live), more):
+            if m:
+                frames[s] += 1
+            else:
+                live.remove(s)  # eos: the utterance is over
+    for s in seqs:
+        assert rig.tb.length(s) == rows[s] + frames[s]
+    assert stats[0] >= 0.9 * stats[1], stats
+    tp.free()
+    rig.free()
