@@ -389,6 +389,99 @@ def prefill_measure(args, qtts, torch, m, dev, rank):
             "timing": "host wall clock around qtts_batch_forward (rows from pinned host memory, logits back)"}
 
 
+def start_prompt_measure(qtts, tk, dev, cpu_leg):
+    """TQwenTalker.Start (talker.pas:471-592) from token ids on the device
+    (qtts_talker_start_prompt: 32 text tokens, streaming, a voice; the text
+    projection of every prompt row, the codec rows, the talker's prefill and
+    the first ChooseCode0), host wall clock around the synchronous call.
+    With cpu_leg, the same rows restated on the host cores (the reference
+    builds them with TextProject on the CPU) are timed beside it.  A
+    synthetic 4096-row BF16 text table stands for the 151,936-row one: Start
+    only gathers its prompt's rows."""
+    rng = np.random.default_rng(SEED + 7)
+    th, hid, vocab = 2048, synth.HIDDEN, 4096
+    emb = (rng.standard_normal((vocab, th)) * 0.05).astype(np.float32)
+    bits = (emb.view(np.uint32) >> 16).astype(np.uint16)
+    emb = (bits.astype(np.uint32) << 16).view(np.float32)
+    w1 = (rng.standard_normal((th, th)) * 0.02).astype(np.float32)
+    b1 = (rng.standard_normal(th) * 0.02).astype(np.float32)
+    w2 = (rng.standard_normal((hid, th)) * 0.02).astype(np.float32)
+    b2 = (rng.standard_normal(hid) * 0.02).astype(np.float32)
+    tp = qtts.QwenTextProject(dev, bits, w1, b1, w2, b2)
+    tok = qtts.PromptTokens(4093, 4094, 4095, 2148, 2149)
+    ids = [4000, 4001, 4002] + [int(v) for v in rng.integers(0, 3990, 32)] + [4003, 4002, 4000, 4001, 4002]
+    codec = [2155, 2156, 2157, 3065, 2148, 2149]
+    try:
+        for _ in range(3):
+            tk.start_prompt(tp, tok, ids, codec)
+        n = 20
+        t0 = time.perf_counter()
+        for _ in range(n):
+            tk.start_prompt(tp, tok, ids, codec)
+        ms = (time.perf_counter() - t0) * 1000.0 / n
+        rows, trailing = tk.prompt_rows(tp, tok, ids, codec)
+        out = {"ms_per_start": ms, "prefill_rows": int(rows.shape[0]), "trailing_rows": int(trailing.shape[0]),
+               "text_tokens": 32,
+               "includes": "qtts_talker_start_prompt: ids up, text projection (fc1 2048x2048 + SiLU + fc2) of "
+                           "every row with the codec rows added, 28-layer prefill, first ChooseCode0",
+               "timing": "host wall clock around the synchronous call, 20 calls after 3"}
+        if cpu_leg:
+            import oracle as O
+            toks = {"tts_bos": 4093, "tts_eos": 4094, "tts_pad": 4095, "codec_pad": 2148, "codec_bos": 2149}
+            ce = synth.codec_embedding(SEED)
+            t0 = time.perf_counter()
+            O.start_rows(emb, w1, b1, w2, b2, ce, toks, ids, codec)
+            out["cpu_baseline_rows_ms"] = (time.perf_counter() - t0) * 1000.0
+            out["cpu_baseline_kind"] = "port: the rows alone (no prefill), C restatement, one thread"
+        return out
+    finally:
+        tp.free()
+
+
+def heads_load_measure(qtts, dev, m, cpu_leg):
+    """TQwenLmHeads.Add of the 15 predictor heads from a BF16 safetensors
+    file, converted to Q8_0 (the conversion ParallelQ8MatchesSerial times,
+    tests/test.tts.qwen.talker.pas:256-304): qtts_heads_add_safetensors reads
+    the rows in place and quantises them on the device.  Host wall clock,
+    the file in the page cache (one untimed pass first)."""
+    import shutil
+    import tempfile
+
+    import torch
+    from safetensors.torch import save_file
+    d = tempfile.mkdtemp(prefix="qtts_heads_")
+    try:
+        path = os.path.join(d, "heads.safetensors")
+        names = [f"talker.code_predictor.lm_head.{g}.weight" for g in range(len(m["ph"]))]
+        save_file({n: torch.from_numpy(h).to(torch.bfloat16) for n, h in zip(names, m["ph"])}, path)
+        runs = []
+        for _ in range(4):
+            f = qtts.SafeTensorsFile(path)
+            t0 = time.perf_counter()
+            h = qtts.QwenLmHeads(dev, "predictor", synth.HIDDEN, "q8_0")
+            for n in names:
+                h.add_file(f, n, synth.PRED_VOCAB)
+            runs.append((time.perf_counter() - t0) * 1000.0)
+            crc = h.digest()  # after the timer, as the reference's test reads it
+            h.free()
+            f.close()
+        out = {"ms": min(runs[1:]), "heads": len(names), "rows": synth.PRED_VOCAB, "hidden": synth.HIDDEN,
+               "bf16_bytes": os.path.getsize(path), "crc32c": "%08x" % crc,
+               "timing": "host wall clock around heads create + 15 x qtts_heads_add_safetensors (each "
+                         "synchronous), the file opened before and the digest read after, as the reference's "
+                         "test times it; best of 3 after 1"}
+        if cpu_leg:
+            import oracle as O
+            t0 = time.perf_counter()
+            for hm in m["ph"]:
+                O.quantize_q8_0(torch.from_numpy(hm).to(torch.bfloat16).float().numpy())
+            out["cpu_baseline_ms"] = (time.perf_counter() - t0) * 1000.0
+            out["cpu_baseline_kind"] = "port: ggml quantize_row_q8_0_ref restated in C, one thread, rows widened first"
+        return out
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import qtts
@@ -523,6 +616,18 @@ def gpu_arm(args, rank, world, local_rank):
         cpu = {"value": done / dt, "unit": "frames/s", "cores": used, "kind": "port",
                "sample": f"{done} frames of the same utterance after its prefill (C restatement of the reference "
                          "CPU path, AVX2+FMA, OpenMP over output rows)"}
+    # the prompt of Start and the heads' load, on rank 0 (no timed collective
+    # follows); a failure is recorded in the line, never fatal to it
+    start_p = heads_l = None
+    if rank == 0 and (args.talker_layers, args.pred_layers) == (28, 5):
+        try:
+            start_p = start_prompt_measure(qtts, tk, dev, not args.no_cpu_baseline)
+        except Exception as e:  # noqa: BLE001
+            start_p = {"error": f"{type(e).__name__}: {e}"}
+        try:
+            heads_l = heads_load_measure(qtts, dev, m, not args.no_cpu_baseline)
+        except Exception as e:  # noqa: BLE001
+            heads_l = {"error": f"{type(e).__name__}: {e}"}
     if rank == 0:
         fps = job_value(world, K, ms)
         wb = weight_bytes_per_frame(dtype, args.talker_layers, args.pred_layers)
@@ -559,6 +664,8 @@ def gpu_arm(args, rank, world, local_rank):
             "batched": batched,
             "box": box,
             "prefill": prefill,
+            "start_prompt": start_p,
+            "heads_load": heads_l,
             "weights_generation_s": m["gen_s"],
         }
         print(json.dumps(line), flush=True)
