@@ -7,7 +7,8 @@ cpu_baseline / reference legs of bench.py, as the checker.  The product
 
 Objects follow the reference: OraStack (QwenLmStack, lm.pas:174-179),
 OraHeads (TQwenLmHeads, lm.pas:64-100), OraLm (TQwenLm, lm.pas:102-143),
-OraTalker (TQwenTalker.Start/NextFrame, talker.pas:471-681).
+OraTalker (TQwenTalker.Start/NextFrame, talker.pas:471-681), OraCodec (the
+12 Hz decoder TQwenCodec, codec.pas; qtts_codec_oracle.c).
 """
 import ctypes
 import os
@@ -68,6 +69,13 @@ def _load():
         "ora_talker_create": (P, [P, P, P, P, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_float]),
         "ora_talker_free": (None, [P]),
+        "ora_codec_create": (P, [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(P),
+                                 ctypes.POINTER(ctypes.c_int64)]),
+        "ora_codec_free": (None, [P]),
+        "ora_codec_reset": (None, [P]),
+        "ora_codec_frames": (ctypes.c_longlong, [P]),
+        "ora_codec_decode": (ctypes.c_int, [P, P, ctypes.c_int, P]),
+        "ora_codec_error": (ctypes.c_char_p, []),
         "ora_talker_start": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P]),
         "ora_talker_next_frame": (ctypes.c_int, [P, P]),
         "ora_talker_check_frame": (ctypes.c_int, [P, P, P]),
@@ -210,6 +218,45 @@ def start_rows(emb, w1, b1, w2, b2, codec_emb, tokens, ids, codec, non_streaming
             trailing[0:n_text - 1] = proj(text[1:])
         trailing[n_text - 1] = tts_eos
     return prefill, trailing, tts_pad
+
+
+class OraCodec:
+    """TQwenCodec (the 12 Hz decoder, codec.pas) on the CPU: weights = dict
+    of the checkpoint's tensor names -> float32 arrays (the speech_tokenizer
+    model.safetensors, PyTorch layouts).  decode(codes [frames][16]) ->
+    frames * 1920 samples; frames of successive calls follow each other."""
+
+    FRAME_SAMPLES = 1920
+
+    def __init__(self, weights):
+        self._keep = {k: _f32(v) for k, v in weights.items()}
+        names = list(self._keep)
+        n = len(names)
+        cn = (ctypes.c_char_p * n)(*[k.encode() for k in names])
+        cp = (P * n)(*[self._keep[k].ctypes.data for k in names])
+        cc = (ctypes.c_int64 * n)(*[self._keep[k].size for k in names])
+        self.handle = lib.ora_codec_create(n, cn, cp, cc)
+        if not self.handle:
+            raise ValueError("oracle codec: " + lib.ora_codec_error().decode())
+
+    def decode(self, codes):
+        c = np.ascontiguousarray(codes, dtype=np.int32).reshape(-1, 16)
+        pcm = np.zeros(c.shape[0] * self.FRAME_SAMPLES, np.float32)
+        if lib.ora_codec_decode(self.handle, _p(c), c.shape[0], _p(pcm)):
+            raise ValueError("oracle codec: " + lib.ora_codec_error().decode())
+        return pcm
+
+    def reset(self):
+        lib.ora_codec_reset(self.handle)
+
+    @property
+    def frames(self):
+        return lib.ora_codec_frames(self.handle)
+
+    def free(self):
+        if self.handle:
+            lib.ora_codec_free(self.handle)
+            self.handle = None
 
 
 def rope_table(max_pos, head_dim, theta):
