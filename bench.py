@@ -482,6 +482,56 @@ def heads_load_measure(qtts, dev, m, cpu_leg):
         shutil.rmtree(d, ignore_errors=True)
 
 
+def codec_measure(qtts, dev, cpu_leg):
+    """The 12 Hz decoder (TQwenCodec.Decode, codec.pas:1010-1032) on the
+    device, seeded weights read from a safetensors file: 50 frames decoded
+    one call per frame (the streaming use, each call synchronous) and the
+    same 50 frames in one call; host wall clock.  One frame is 80 ms of
+    audio, so real time is 12.5 frames/s.  With cpu_leg, the C restatement
+    decodes 4 frames in one call on the host cores beside it."""
+    import shutil
+    import tempfile
+
+    from safetensors.numpy import save_file
+    w = synth.codec_weights(SEED)
+    d = tempfile.mkdtemp(prefix="qtts_codec_")
+    try:
+        path = os.path.join(d, "codec.safetensors")
+        save_file(w, path)
+        f = qtts.SafeTensorsFile(path)
+        c = qtts.QwenCodec(dev, f)
+        try:
+            codes = np.random.default_rng(SEED + 11).integers(0, 2048, (50, 16)).astype(np.int32)
+            c.decode(codes[:8])  # work buffers grown, kernels loaded
+            c.reset()
+            t0 = time.perf_counter()
+            for i in range(50):
+                c.decode(codes[i:i + 1])
+            ms_stream = (time.perf_counter() - t0) * 1000.0 / 50
+            c.reset()
+            t0 = time.perf_counter()
+            c.decode(codes)
+            ms_call = (time.perf_counter() - t0) * 1000.0 / 50
+        finally:
+            c.free()
+            f.close()
+        out = {"ms_per_frame_streaming": ms_stream, "ms_per_frame_50_per_call": ms_call,
+               "frames_per_s_streaming": 1000.0 / ms_stream, "realtime_factor_streaming": 80.0 / ms_stream,
+               "timing": "host wall clock around qtts_codec_decode (codes up, samples back), 50 frames after 8",
+               "kernels": "float32 CUDA-core GEMM over im2col rows for every convolution and projection"}
+        if cpu_leg:
+            import oracle as O
+            oc = O.OraCodec(w)
+            t0 = time.perf_counter()
+            oc.decode(codes[:4])
+            out["cpu_baseline_ms_per_frame"] = (time.perf_counter() - t0) * 1000.0 / 4
+            out["cpu_baseline_kind"] = "port: C restatement of TQwenCodec, AVX2, OpenMP, 4 frames in one call"
+            oc.free()
+        return out
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import qtts
@@ -618,7 +668,7 @@ def gpu_arm(args, rank, world, local_rank):
                          "CPU path, AVX2+FMA, OpenMP over output rows)"}
     # the prompt of Start and the heads' load, on rank 0 (no timed collective
     # follows); a failure is recorded in the line, never fatal to it
-    start_p = heads_l = None
+    start_p = heads_l = codec = None
     if rank == 0 and (args.talker_layers, args.pred_layers) == (28, 5):
         try:
             start_p = start_prompt_measure(qtts, tk, dev, not args.no_cpu_baseline)
@@ -628,6 +678,10 @@ def gpu_arm(args, rank, world, local_rank):
             heads_l = heads_load_measure(qtts, dev, m, not args.no_cpu_baseline)
         except Exception as e:  # noqa: BLE001
             heads_l = {"error": f"{type(e).__name__}: {e}"}
+        try:
+            codec = codec_measure(qtts, dev, not args.no_cpu_baseline)
+        except Exception as e:  # noqa: BLE001
+            codec = {"error": f"{type(e).__name__}: {e}"}
     if rank == 0:
         fps = job_value(world, K, ms)
         wb = weight_bytes_per_frame(dtype, args.talker_layers, args.pred_layers)
@@ -666,6 +720,7 @@ def gpu_arm(args, rank, world, local_rank):
             "prefill": prefill,
             "start_prompt": start_p,
             "heads_load": heads_l,
+            "codec": codec,
             "weights_generation_s": m["gen_s"],
         }
         print(json.dumps(line), flush=True)

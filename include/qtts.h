@@ -60,6 +60,7 @@ typedef struct qtts_lm qtts_lm;
 typedef struct qtts_talker qtts_talker;
 typedef struct qtts_textproj qtts_textproj;
 typedef struct qtts_safetensors qtts_safetensors;
+typedef struct qtts_codec qtts_codec;
 
 /* The decoder configuration of one stack (TDecoderConfig: talker_config or
  * talker_config.code_predictor_config of config.json, talker.pas:252-273).
@@ -384,6 +385,26 @@ int qtts_stack_save(const qtts_stack *stack, const char *path);
 /* ... and read back without a conversion.  Not a blob of this build
  * (magic, dimensions, size) or a checksum mismatch: QTTS_E_ARG. */
 int qtts_stack_load(qtts_device *dev, const char *path, qtts_stack **out);
+
+/* ------------------------------------------------------------------ the 12 Hz codec */
+
+/* TQwenCodec.Create (src/tts/mormot.ai.tts.qwen.codec.pas:651-727): the
+ * decoder of the speech_tokenizer checkpoint (its model.safetensors, F32 or
+ * BF16 tensors under the reference's names: decoder.quantizer.*,
+ * decoder.pre_conv.*, decoder.pre_transformer.*, decoder.upsample.*,
+ * decoder.decoder.*) on the device.  A missing tensor or a shape other than
+ * the reference's is QTTS_E_ARG. */
+int qtts_codec_create_safetensors(qtts_device *dev, qtts_safetensors *f, qtts_codec **out);
+/* TQwenCodec.Reset (codec.pas:769-786): the next frame starts a sentence. */
+int qtts_codec_reset(qtts_codec *c);
+/* TQwenCodec.Decode (codec.pas:1010-1032): codes[frames][16] (host) ->
+ * pcm[frames * 1920] (host) in [-1, 1]; frames of successive calls follow
+ * each other.  A code >= 2048 is QTTS_E_ARG (negative codes read as 0);
+ * at most 2048 frames a call. */
+int qtts_codec_decode(qtts_codec *c, const int32_t *codes, int frames, float *pcm);
+/* TQwenCodec.Frames: the frames decoded since the last reset. */
+int qtts_codec_frames(qtts_codec *c, int64_t *frames);
+int qtts_codec_destroy(qtts_codec *c);
 
 /* ------------------------------------------------------------------ talkers (batched frames) */
 

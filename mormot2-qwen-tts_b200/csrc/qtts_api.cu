@@ -3063,3 +3063,7 @@ extern "C" int qtts_talkers_set_sampling(qtts_talkers *t, const qtts_sampling *s
     }
     return QTTS_OK;
 }
+
+// ------------------------------------------------------------------ the 12 Hz codec
+
+#include "qtts_codec.cuh"

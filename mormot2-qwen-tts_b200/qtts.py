@@ -131,6 +131,11 @@ EXPORTS = {
     "qtts_safetensors_close": [P],
     "qtts_stack_create_safetensors": [P, ctypes.POINTER(StackConfig), P, ctypes.c_char_p, ctypes.POINTER(P)],
     "qtts_heads_add_safetensors": [P, P, ctypes.c_char_p, I, PI],
+    "qtts_codec_create_safetensors": [P, P, ctypes.POINTER(P)],
+    "qtts_codec_reset": [P],
+    "qtts_codec_decode": [P, P, I, P],
+    "qtts_codec_frames": [P, ctypes.POINTER(ctypes.c_int64)],
+    "qtts_codec_destroy": [P],
     "qtts_stack_save": [P, ctypes.c_char_p],
     "qtts_stack_load": [P, ctypes.c_char_p, ctypes.POINTER(P)],
     "qtts_stack_bytes": [P, ctypes.POINTER(ctypes.c_int64)],
@@ -620,6 +625,39 @@ class QwenTalker:
     def free(self):
         if self.handle:
             check(lib().qtts_talker_destroy(self.handle))
+            self.handle = None
+
+
+class QwenCodec:
+    """TQwenCodec (the 12 Hz decoder, codec.pas) on the device, from the
+    speech_tokenizer checkpoint: decode(codes [frames][16]) -> frames * 1920
+    samples in [-1, 1]; frames of successive calls follow each other."""
+
+    FRAME_SAMPLES = 1920
+
+    def __init__(self, device, file):
+        h = P()
+        check(lib().qtts_codec_create_safetensors(device.handle, file.handle, ctypes.byref(h)))
+        self.handle = h
+
+    def decode(self, codes):
+        c = np.ascontiguousarray(codes, dtype=np.int32).reshape(-1, 16)
+        pcm = np.zeros(c.shape[0] * self.FRAME_SAMPLES, np.float32)
+        check(lib().qtts_codec_decode(self.handle, _ptr(c), c.shape[0], _ptr(pcm)))
+        return pcm
+
+    def reset(self):
+        check(lib().qtts_codec_reset(self.handle))
+
+    @property
+    def frames(self):
+        v = ctypes.c_int64()
+        check(lib().qtts_codec_frames(self.handle, ctypes.byref(v)))
+        return v.value
+
+    def free(self):
+        if self.handle:
+            check(lib().qtts_codec_destroy(self.handle))
             self.handle = None
 
 

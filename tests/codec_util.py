@@ -1,6 +1,6 @@
 """The 12 Hz decoder (TQwenCodec, codec.pas) for the tests: seeded weights
-under the checkpoint's tensor names and shapes (the speech_tokenizer
-model.safetensors as codec.pas:651-726 reads it), and an independent
+under the checkpoint's tensor names and shapes (synth.codec_weights: the
+speech_tokenizer model.safetensors as codec.pas:651-726 reads it), and an independent
 restatement of the whole decoder with PyTorch modules in float64, applied
 to the whole sequence at once (no streaming state): causal convolutions as
 left padding, transposed convolutions cut on the right by K - s, LayerNorm,
@@ -10,86 +10,10 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
+from synth import codec_weights  # noqa: F401  (the seeded weights, shared with bench.py)
+
 RATES = (8, 5, 4, 3)
 DILATIONS = (1, 3, 9)
-
-
-def codec_weights(seed):
-    rng = np.random.default_rng(seed)
-    W = {}
-
-    def lin(name, *shape, gain=1.0):
-        fan_in = int(np.prod(shape[1:]))
-        W[name] = (rng.standard_normal(shape) * gain / np.sqrt(fan_in)).astype(np.float32)
-
-    def vec(name, n, mean=0.0, std=0.1):
-        W[name] = (mean + rng.standard_normal(n) * std).astype(np.float32)
-
-    for g in range(16):
-        p = ("decoder.quantizer.rvq_first.vq.layers.0._codebook" if g == 0
-             else f"decoder.quantizer.rvq_rest.vq.layers.{g - 1}._codebook")
-        W[p + ".embedding_sum"] = rng.standard_normal((2048, 256)).astype(np.float32)
-        W[p + ".cluster_usage"] = rng.uniform(0.5, 4.0, 2048).astype(np.float32)
-    W["decoder.quantizer.rvq_rest.vq.layers.3._codebook.cluster_usage"][:5] = 0.0  # the 1e-5 floor
-    lin("decoder.quantizer.rvq_first.output_proj.weight", 512, 256, 1, gain=0.5)
-    lin("decoder.quantizer.rvq_rest.output_proj.weight", 512, 256, 1, gain=0.2)
-    lin("decoder.pre_conv.conv.weight", 1024, 512, 3)
-    vec("decoder.pre_conv.conv.bias", 1024)
-    p = "decoder.pre_transformer."
-    lin(p + "input_proj.weight", 512, 1024)
-    vec(p + "input_proj.bias", 512)
-    lin(p + "output_proj.weight", 1024, 512)
-    vec(p + "output_proj.bias", 1024)
-    vec(p + "norm.weight", 512, 1.0)
-    for l in range(8):
-        q = f"{p}layers.{l}."
-        vec(q + "input_layernorm.weight", 512, 1.0)
-        vec(q + "post_attention_layernorm.weight", 512, 1.0)
-        for n in ("q", "k", "v"):
-            lin(q + f"self_attn.{n}_proj.weight", 1024, 512)
-        lin(q + "self_attn.o_proj.weight", 512, 1024)
-        lin(q + "mlp.gate_proj.weight", 1024, 512)
-        lin(q + "mlp.up_proj.weight", 1024, 512)
-        lin(q + "mlp.down_proj.weight", 512, 1024)
-        vec(q + "self_attn_layer_scale.scale", 512, 0.3)
-        vec(q + "mlp_layer_scale.scale", 512, 0.3)
-    for i in range(2):
-        lin(f"decoder.upsample.{i}.0.conv.weight", 1024, 1024, 2)
-        vec(f"decoder.upsample.{i}.0.conv.bias", 1024)
-        q = f"decoder.upsample.{i}.1."
-        lin(q + "dwconv.conv.weight", 1024, 1, 7)
-        vec(q + "dwconv.conv.bias", 1024)
-        vec(q + "norm.weight", 1024, 1.0)
-        vec(q + "norm.bias", 1024)
-        lin(q + "pwconv1.weight", 4096, 1024)
-        vec(q + "pwconv1.bias", 4096)
-        lin(q + "pwconv2.weight", 1024, 4096)
-        vec(q + "pwconv2.bias", 1024)
-        vec(q + "gamma", 1024, 0.3)
-    lin("decoder.decoder.0.conv.weight", 1536, 1024, 7)
-    vec("decoder.decoder.0.conv.bias", 1536)
-    for b in range(4):
-        cin, cout, rate = 1536 >> b, 1536 >> (b + 1), RATES[b]
-        q = f"decoder.decoder.{b + 1}.block."
-        vec(q + "0.alpha", cin)
-        vec(q + "0.beta", cin)
-        lin(q + "1.conv.weight", cin, cout, 2 * rate, gain=0.7)
-        vec(q + "1.conv.bias", cout)
-        for r in range(3):
-            u = f"{q}{r + 2}."
-            vec(u + "act1.alpha", cout)
-            vec(u + "act1.beta", cout)
-            lin(u + "conv1.conv.weight", cout, cout, 7, gain=0.5)
-            vec(u + "conv1.conv.bias", cout)
-            vec(u + "act2.alpha", cout)
-            vec(u + "act2.beta", cout)
-            lin(u + "conv2.conv.weight", cout, cout, 1, gain=0.5)
-            vec(u + "conv2.conv.bias", cout)
-    vec("decoder.decoder.5.alpha", 96)
-    vec("decoder.decoder.5.beta", 96)
-    lin("decoder.decoder.6.conv.weight", 1, 96, 7, gain=0.3)
-    vec("decoder.decoder.6.conv.bias", 1, 0.0, 0.01)
-    return W
 
 
 def torch_decode(W, codes):
