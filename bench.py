@@ -483,7 +483,7 @@ def heads_load_measure(qtts, dev, m, cpu_leg):
 
 
 def codec_measure(qtts, dev, cpu_leg):
-    """The 12 Hz decoder (TQwenCodec.Decode, codec.pas:1010-1032) on the
+    """The 12 Hz decoder (TQwenCodec.Decode, codec.pas:1019-1038) on the
     device, seeded weights read from a safetensors file: 50 frames decoded
     one call per frame (the streaming use, each call synchronous) and the
     same 50 frames in one call; host wall clock.  One frame is 80 ms of

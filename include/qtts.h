@@ -388,16 +388,16 @@ int qtts_stack_load(qtts_device *dev, const char *path, qtts_stack **out);
 
 /* ------------------------------------------------------------------ the 12 Hz codec */
 
-/* TQwenCodec.Create (src/tts/mormot.ai.tts.qwen.codec.pas:651-727): the
+/* TQwenCodec.Create (src/tts/mormot.ai.tts.qwen.codec.pas:644-731): the
  * decoder of the speech_tokenizer checkpoint (its model.safetensors, F32 or
  * BF16 tensors under the reference's names: decoder.quantizer.*,
  * decoder.pre_conv.*, decoder.pre_transformer.*, decoder.upsample.*,
  * decoder.decoder.*) on the device.  A missing tensor or a shape other than
  * the reference's is QTTS_E_ARG. */
 int qtts_codec_create_safetensors(qtts_device *dev, qtts_safetensors *f, qtts_codec **out);
-/* TQwenCodec.Reset (codec.pas:769-786): the next frame starts a sentence. */
+/* TQwenCodec.Reset (codec.pas:776-792): the next frame starts a sentence. */
 int qtts_codec_reset(qtts_codec *c);
-/* TQwenCodec.Decode (codec.pas:1010-1032): codes[frames][16] (host) ->
+/* TQwenCodec.Decode (codec.pas:1019-1038): codes[frames][16] (host) ->
  * pcm[frames * 1920] (host) in [-1, 1]; frames of successive calls follow
  * each other.  A code >= 2048 is QTTS_E_ARG (negative codes read as 0);
  * at most 2048 frames a call. */

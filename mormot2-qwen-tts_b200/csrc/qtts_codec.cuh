@@ -8,7 +8,7 @@
 // reference).  Every convolution is a product of its im2col rows with the
 // weights [out][in * K] (transposed convolutions with weights re-laid
 // [stride * out][taps * in] at load, as TQwenTransConv.Create,
-// codec.pas:358-392), on one tiled float32 GEMM kernel; the rest are row and
+// codec.pas:366-396), on one tiled float32 GEMM kernel; the rest are row and
 // element kernels.  Included at the end of qtts_api.cu (it uses the file's
 // safetensors helpers and error reporting).
 #pragma once
@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(256) gemm_kernel(const float *a, int M, int K,
 }
 
 // col[r][c*K + k] = buf[r + k*dil][c]: the im2col rows of a causal
-// convolution over [history ; input] (TQwenConv.Im2Col, codec.pas:319-335)
+// convolution over [history ; input] (TQwenConv.Im2Col, codec.pas:317-334)
 __global__ void im2col_kernel(const float *buf, int rows, int in, int K, int dil, float *col) {
     const long long n = static_cast<long long>(rows) * in * K;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -68,7 +68,7 @@ __global__ void im2col_kernel(const float *buf, int rows, int in, int K, int dil
     }
 }
 
-// x2[t][i*in + c] = buf[past + t - i][c] (TQwenTransConv.Forward, codec.pas:403-418)
+// x2[t][i*in + c] = buf[past + t - i][c] (TQwenTransConv.Forward, codec.pas:404-428)
 __global__ void tgather_kernel(const float *buf, int rows, int in, int taps, float *x2) {
     const long long n = static_cast<long long>(rows) * taps * in;
     const int past = taps - 1;
@@ -81,7 +81,7 @@ __global__ void tgather_kernel(const float *buf, int rows, int in, int taps, flo
     }
 }
 
-// SnakeBeta in place (TQwenSnake.Apply, codec.pas:443-457)
+// SnakeBeta in place (TQwenSnake.Apply, codec.pas:454-470)
 __global__ void snake_kernel(float *x, long long n, int ch, const float *alpha, const float *inv_beta) {
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -91,7 +91,7 @@ __global__ void snake_kernel(float *x, long long n, int ch, const float *alpha, 
     }
 }
 
-// the causal depthwise convolution of ConvNeXt (7 taps, codec.pas:516-523)
+// the causal depthwise convolution of ConvNeXt (7 taps, codec.pas:514-523)
 __global__ void dwconv_kernel(const float *buf, int rows, int dim, const float *w, const float *b, float *out) {
     const long long n = static_cast<long long>(rows) * dim;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -177,7 +177,7 @@ __global__ void rope_kernel(float *x, int rows, const float *cs, const float *sn
     }
 }
 
-// sliding-window attention (codec.pas:950-962): row r at position frames + r
+// sliding-window attention (codec.pas:990-1000): row r at position frames + r
 // sees positions max(0, p - 71) .. p of the cache (rows from cache_base);
 // one block of 128 per (row, head)
 __global__ void __launch_bounds__(128) window_attn_kernel(const float *q, const float *keys, const float *values,
@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(128) window_attn_kernel(const float *q, const 
     }
 }
 
-// the quantizer's sums (TQwenCodec.Quantize, codec.pas:867-899): q1 = the
+// the quantizer's sums (TQwenCodec.Quantize, codec.pas:886-917): q1 = the
 // codebook 0 row, q2 = the rows of codebooks 1..15 added in order; codes
 // checked on the host (negative ones read as 0)
 __global__ void quant_kernel(const int *codes, const float *codebook, float *q1, float *q2) {
@@ -384,7 +384,7 @@ int cx_tconv(qtts_codec *c, qtts_safetensors *f, const std::string &p, int in, i
 }
 
 // alpha = exp(a), inv_beta = 1 / (exp(b) + 1e-9), in float32 on the host
-// (TQwenSnake.Create, codec.pas:427-441)
+// (TQwenSnake.Create, codec.pas:431-452)
 int cx_snake(qtts_codec *c, qtts_safetensors *f, const std::string &p, int n, CSnake &v) {
     v.n = n;
     std::vector<float> a, b;
@@ -535,7 +535,7 @@ int cx_cache_room(qtts_codec *c, int rows) {
     return QTTS_OK;
 }
 
-// TQwenCodec.Transformer (codec.pas:927-985): x [rows][LATENT] -> y
+// TQwenCodec.Transformer (codec.pas:948-1017): x [rows][LATENT] -> y
 int cx_transformer(qtts_codec *c, const float *x, int rows, float *y) {
     const size_t R = static_cast<size_t>(rows);
     float *h, *n, *q, *k, *v, *att, *o, *g, *u;
@@ -779,7 +779,7 @@ extern "C" int qtts_codec_decode(qtts_codec *c, const int32_t *codes, int frames
     add_kernel<<<blocks_for(static_cast<long long>(F) * QUANT_DIM), 256, 0, c->st>>>(a, b, static_cast<long long>(F) * QUANT_DIM);
     if ((rc = cx_conv_fwd(c, c->pre, a, frames, b))) return rc;
     if ((rc = cx_transformer(c, b, frames, a))) return rc;
-    // the back part (TQwenCodec.Back, codec.pas:1034-1085)
+    // the back part (TQwenCodec.Back, codec.pas:1040-1084)
     int rows = frames;
     for (int i = 0; i < 2; ++i) {
         if ((rc = cx_tconv_fwd(c, c->up[i], a, rows, b))) return rc;

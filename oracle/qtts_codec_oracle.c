@@ -4,17 +4,18 @@
  *
  * TEST INFRASTRUCTURE ONLY (the checker of a device codec); the product
  * library never links it.  Every step cites the reference:
- *   quantizer      codec.pas:664-684 (codebook = embedding_sum / max(usage,
- *                  1e-5)), 867-899 (Quantize)
- *   pre-conv       codec.pas:685, TQwenConv 296-354 (causal, history rows)
- *   transformer    codec.pas:687-711, 901-985 (RMSNorm 1e-5, RoPE base
- *                  10000 on the frame index, 72-frame sliding window,
- *                  layer scales)
- *   upsampling     codec.pas:712-718, TQwenTransConv 358-423, TQwenConvNeXt
- *                  465-542 (depthwise 7, LayerNorm 1e-6, GELU, gamma)
- *   decoder        codec.pas:719-725, TQwenBlock 600-647 (SnakeBeta,
+ *   quantizer      codec.pas:667-689 (codebook = embedding_sum / max(usage,
+ *                  1e-5)), 886-917 (Quantize)
+ *   pre-conv       codec.pas:691, TQwenConv 296-363 (causal, history rows)
+ *   transformer    codec.pas:692-716, CacheRoom 919-946, Transformer
+ *                  948-1017 (RMSNorm 1e-5, RoPE base 10000 on the frame
+ *                  index, 72-frame sliding window, layer scales)
+ *   upsampling     codec.pas:717-723, TQwenTransConv 366-428, TQwenConvNeXt
+ *                  481-535 (depthwise 7, LayerNorm 1e-6, GELU, gamma)
+ *   decoder        codec.pas:724-729, TQwenBlock 592-641 (SnakeBeta,
  *                  transposed conv, residual units with dilations 1, 3, 9),
- *                  TQwenSnake 427-462, output clamp 1034-1085
+ *                  TQwenResUnit 538-590, TQwenSnake 431-478, Back and the
+ *                  output clamp 1040-1084
  * Weights are looked up by their names in the checkpoint, with the element
  * counts the reference checks (F32(name, dims)).  Dot products are float32
  * with AVX2 FMAs in a fixed order, the same for a row whatever the number of
@@ -23,7 +24,9 @@
  * The reference's CPU backend (mormot2-ai) is absent: RMSNorm, RoPE
  * (rotate-half pairs i, i + 32), attention softmax, SwiGLU, GELU (erf form)
  * and LayerNorm follow the PyTorch modules the reference mirrors (qwen_tts
- * 0.1.1, Qwen3TTSTokenizerV2Decoder). */
+ * 0.1.1, Qwen3TTSTokenizerV2Decoder).  The RoPE is the backend's Rope
+ * (codec.pas:985-986), the call its Qwen3 stacks make too, whose rotate-half
+ * pairs the language-model oracle pins to transformers' Qwen3. */
 #include <immintrin.h>
 #include <math.h>
 #include <omp.h>
@@ -70,7 +73,7 @@ static float dot(const float *a, const float *b, int n) {
     return s;
 }
 
-/* y[r][o] = x[r] . w[o] (+ b[o]); w [out][in] (Gemm, codec.pas:829-865) */
+/* y[r][o] = x[r] . w[o] (+ b[o]); w [out][in] (Gemm, codec.pas:830-853) */
 static void gemm(const float *x, int rows, int in, const float *w, int out, const float *b, float *y) {
 #pragma omp parallel for collapse(2) schedule(static) if ((long long)rows * in * out > 65536)
     for (int r = 0; r < rows; r++)
@@ -106,7 +109,7 @@ static const float *w_get(Table *t, const char *name, int64_t count) {
 
 /* ------------------------------------------------------------- layers */
 
-/* causal convolution, weights [out][in][k] (TQwenConv, codec.pas:296-354):
+/* causal convolution, weights [out][in][k] (TQwenConv, codec.pas:296-363):
  * y[t] = b + sum_k W[:, :, k] . x[t - (K-1-k) dil], the rows before the
  * first input from the history (zeros after a reset) */
 typedef struct {
@@ -149,7 +152,7 @@ static void conv_fwd(Conv *c, const float *x, int rows, float *y) {
 }
 
 /* causal transposed convolution, stride s, kernel K = taps * s, cut on the
- * right by K - s (TQwenTransConv, codec.pas:358-423): row t*s + j gets
+ * right by K - s (TQwenTransConv, codec.pas:366-428): row t*s + j gets
  * b + sum_{i < taps} x[t - i] . W[:, :, j + i*s]; W [in][out][K] in the file,
  * re-laid as [s*out][taps*in] */
 typedef struct {
@@ -198,7 +201,7 @@ static void tconv_fwd(TConv *c, const float *x, int rows, float *y) {
     free(buf);
 }
 
-/* SnakeBeta (TQwenSnake, codec.pas:427-462): x + 1/(exp(beta) + 1e-9) *
+/* SnakeBeta (TQwenSnake, codec.pas:431-478): x + 1/(exp(beta) + 1e-9) *
  * sin(x * exp(alpha))^2, the exps taken once in float32 */
 typedef struct {
     int n;
@@ -231,7 +234,7 @@ static void snake_fwd(const Snake *s, float *x, int rows) {
         }
 }
 
-/* ConvNeXt block (TQwenConvNeXt, codec.pas:465-542): causal depthwise
+/* ConvNeXt block (TQwenConvNeXt, codec.pas:481-535): causal depthwise
  * convolution (7), LayerNorm (1e-6), pwconv1 (4x), GELU, pwconv2, gamma,
  * residual */
 typedef struct {
@@ -293,7 +296,7 @@ static void next_fwd(Next *x, const float *in, int rows, float *y) {
     free(buf);
 }
 
-/* residual unit (TQwenResUnit, codec.pas:546-598): x += conv2(snake2(
+/* residual unit (TQwenResUnit, codec.pas:538-590): x += conv2(snake2(
  * conv1_dil(snake1(x)))) */
 typedef struct {
     Snake a1, a2;
@@ -301,7 +304,7 @@ typedef struct {
     int dim;
 } Res;
 
-/* decoder block (TQwenBlock, codec.pas:600-647) */
+/* decoder block (TQwenBlock, codec.pas:592-641) */
 typedef struct {
     int in, out, rate;
     Snake act;
@@ -356,7 +359,7 @@ static void rope(float *x, int rows, const float *cs, const float *sn) {
         }
 }
 
-/* the cache keeps positions cache_base .. frames-1 (codec.pas:901-925) */
+/* the cache keeps positions cache_base .. frames-1 (CacheRoom, codec.pas:919-946) */
 static int cache_room(ora_codec *c, int rows) {
     if (c->frames - c->cache_base + rows <= c->cache_cap) return 0;
     long long keep = c->frames - c->cache_base;
@@ -553,7 +556,7 @@ void ora_codec_reset(ora_codec *c) {
 
 long long ora_codec_frames(const ora_codec *c) { return c->frames; }
 
-/* TQwenCodec.Decode (codec.pas:1010-1032): codes[frames][16] -> pcm
+/* TQwenCodec.Decode (codec.pas:1019-1038): codes[frames][16] -> pcm
  * [frames * 1920]; 0 on success, -1 on a code >= 2048 (negative codes
  * clamp to 0) or an allocation failure */
 int ora_codec_decode(ora_codec *c, const int32_t *codes, int frames, float *pcm) {
@@ -586,7 +589,7 @@ int ora_codec_decode(ora_codec *c, const int32_t *codes, int frames, float *pcm)
     for (size_t i = 0; i < F * QUANT_DIM; i++) a[i] += t[i];
     conv_fwd(&c->pre, a, frames, b);
     if (transformer(c, b, frames, a)) return -1;
-    /* the back part (codec.pas:1034-1085) */
+    /* the back part (TQwenCodec.Back, codec.pas:1040-1084) */
     int rows = frames;
     for (int i = 0; i < 2; i++) {
         tconv_fwd(&c->up[i], a, rows, b);

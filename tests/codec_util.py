@@ -1,6 +1,6 @@
 """The 12 Hz decoder (TQwenCodec, codec.pas) for the tests: seeded weights
 under the checkpoint's tensor names and shapes (synth.codec_weights: the
-speech_tokenizer model.safetensors as codec.pas:651-726 reads it), and an independent
+speech_tokenizer model.safetensors as codec.pas:644-731 reads it), and an independent
 restatement of the whole decoder with PyTorch modules in float64, applied
 to the whole sequence at once (no streaming state): causal convolutions as
 left padding, transposed convolutions cut on the right by K - s, LayerNorm,

@@ -8,7 +8,7 @@ against the properties the reference states: frames decoded one call after
 another give exactly the samples of one call (codec.pas:5-8, bit for bit),
 including past the 72-frame attention window; a code changes no sample
 before its frame (everything is causal); out-of-range codes are refused,
-negative ones read as 0 (codec.pas:876-881)."""
+negative ones read as 0 (codec.pas:895-900)."""
 import numpy as np
 import pytest
 
