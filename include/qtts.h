@@ -322,6 +322,16 @@ typedef struct qtts_prompt_tokens {
     int32_t codec_bos;
 } qtts_prompt_tokens;
 
+/* The rows of TQwenTalker.Start (talker.pas:528-574) as a plan, on the host
+ * (no device): row r of the prefill, then of the trailing text, is the text
+ * projection of text_out[r] plus, when codec_out[r] >= 0, the codec
+ * embedding of codec_out[r]; *rows / *trailing_rows receive the counts.
+ * With text_out and codec_out both NULL only the counts; else they hold cap
+ * >= rows + trailing_rows entries.  Arguments as qtts_talker_start_prompt;
+ * the ids are not range-checked here (the start does it). */
+int qtts_prompt_plan(const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
+                     int non_streaming, int32_t *text_out, int32_t *codec_out, int cap, int *rows,
+                     int *trailing_rows);
 /* TQwenTalker.Start (talker.pas:528-592) from token ids, its rows built on
  * the device: ids[n_ids] = PromptIds(text), i.e. [im_start, assistant, \n]
  * text [im_end, \n, im_start, assistant, \n] (n_ids >= 9, as Start's "empty

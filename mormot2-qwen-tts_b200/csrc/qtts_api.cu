@@ -1698,15 +1698,13 @@ struct PromptPlan {
     int rows = 0, trailing = 0;
 };
 
-static int prompt_plan(const char *fn, const qtts_device *dev, int codec_vocab, const qtts_textproj *tp,
-                       const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
-                       int non_streaming, PromptPlan &p) {
-    if (!tp || !tok || !ids || !codec) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
+// the rows alone (host logic, no device): ids and codec counts checked
+static int plan_rows(const char *fn, const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids,
+                     const int32_t *codec, int n_codec, int non_streaming, PromptPlan &p) {
+    if (!tok || !ids || !codec) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
     // [im_start, assistant, \n] text [im_end, \n, im_start, assistant, \n]
     if (n_ids < 9) return set_err(QTTS_E_ARG, "%s: empty text (%d prompt ids, at least 9)", fn, n_ids);
     if (n_codec < 2) return set_err(QTTS_E_ARG, "%s: %d codec ids (at least pad and bos)", fn, n_codec);
-    if (tp->dev != dev || tp->hidden != H)
-        return set_err(QTTS_E_ARG, "%s: the text projection is on another device or %d wide", fn, tp->hidden);
     auto row = [&p](int32_t text, int32_t c) {
         p.text.push_back(text);
         p.codec.push_back(c);
@@ -1735,12 +1733,41 @@ static int prompt_plan(const char *fn, const qtts_device *dev, int codec_vocab, 
     }
     p.trailing = static_cast<int>(p.text.size()) - p.rows;
     row(tok->tts_pad, -1);
+    return QTTS_OK;
+}
+
+// the rows, then the checks against the text projection and the talker
+static int prompt_plan(const char *fn, const qtts_device *dev, int codec_vocab, const qtts_textproj *tp,
+                       const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids, const int32_t *codec, int n_codec,
+                       int non_streaming, PromptPlan &p) {
+    if (!tp) return set_err(QTTS_E_ARG, "%s: NULL argument", fn);
+    int rc = plan_rows(fn, tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    if (rc) return rc;
+    if (tp->dev != dev || tp->hidden != H)
+        return set_err(QTTS_E_ARG, "%s: the text projection is on another device or %d wide", fn, tp->hidden);
     for (size_t r = 0; r < p.text.size(); ++r) {
         if (p.text[r] < 0 || p.text[r] >= tp->vocab)
             return set_err(QTTS_E_ARG, "%s: text token %d out of range", fn, p.text[r]);
         if (p.codec[r] >= codec_vocab) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
         if (p.codec[r] < -1) return set_err(QTTS_E_ARG, "%s: codec id %d out of range", fn, p.codec[r]);
     }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_prompt_plan(const qtts_prompt_tokens *tok, const int32_t *ids, int n_ids, const int32_t *codec,
+                                int n_codec, int non_streaming, int32_t *text_out, int32_t *codec_out, int cap,
+                                int *rows, int *trailing_rows) {
+    PromptPlan p;
+    int rc = plan_rows("qtts_prompt_plan", tok, ids, n_ids, codec, n_codec, non_streaming, p);
+    if (rc) return rc;
+    if (rows) *rows = p.rows;
+    if (trailing_rows) *trailing_rows = p.trailing;
+    if (!text_out && !codec_out) return QTTS_OK;  // the counts alone
+    const int n = p.rows + p.trailing;
+    if (!text_out || !codec_out || cap < n)
+        return set_err(QTTS_E_ARG, "qtts_prompt_plan: buffers of %d entries for %d rows", cap, n);
+    memcpy(text_out, p.text.data(), static_cast<size_t>(n) * 4);
+    memcpy(codec_out, p.codec.data(), static_cast<size_t>(n) * 4);
     return QTTS_OK;
 }
 

@@ -181,6 +181,7 @@ EXPORTS = {
     "qtts_textproj_create": [P, I, I, I, I, P, P, P, P, P, ctypes.POINTER(P)],
     "qtts_text_project": [P, P, I, P],
     "qtts_textproj_destroy": [P],
+    "qtts_prompt_plan": [ctypes.POINTER(PromptTokens), P, I, P, I, I, P, P, I, PI, PI],
     "qtts_talker_start_prompt": [P, P, ctypes.POINTER(PromptTokens), P, I, P, I, I, P, P],
     "qtts_talker_prompt_rows": [P, P, ctypes.POINTER(PromptTokens), P, I, P, I, I, P, I, P, I, PI, PI],
 }
@@ -221,6 +222,24 @@ def _ptr(a):
 
 def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def prompt_plan(tokens, ids, codec, non_streaming=False):
+    """The rows of TQwenTalker.Start as (text token, codec id or -1) pairs:
+    (prefill [rows][2], trailing [trailing_rows][2]), computed by the
+    library on the host (qtts_prompt_plan, no device)."""
+    i = np.ascontiguousarray(ids, dtype=np.int32)
+    c = np.ascontiguousarray(codec, dtype=np.int32)
+    rows, tr = ctypes.c_int(), ctypes.c_int()
+    check(lib().qtts_prompt_plan(ctypes.byref(tokens), _ptr(i), i.size, _ptr(c), c.size, int(non_streaming), None,
+                                 None, 0, ctypes.byref(rows), ctypes.byref(tr)))
+    n = rows.value + tr.value
+    t_out = np.zeros(n, np.int32)
+    c_out = np.zeros(n, np.int32)
+    check(lib().qtts_prompt_plan(ctypes.byref(tokens), _ptr(i), i.size, _ptr(c), c.size, int(non_streaming),
+                                 _ptr(t_out), _ptr(c_out), n, ctypes.byref(rows), ctypes.byref(tr)))
+    plan = np.stack([t_out, c_out], 1)
+    return plan[:rows.value], plan[rows.value:]
 
 
 class QwenDevice:

@@ -80,3 +80,36 @@ def test_oracle_start_rows(non_streaming, n_text):
     np.testing.assert_array_equal(pf, np.array(expect, np.float32))
     np.testing.assert_array_equal(tr, np.array(expect_tr, np.float32))
     np.testing.assert_array_equal(pad, proj(3))
+
+
+@pytest.mark.parametrize("non_streaming", [False, True])
+@pytest.mark.parametrize("n_text", [1, 2, 7])
+def test_library_plan_builds_the_oracle_rows(non_streaming, n_text):
+    # qtts_prompt_plan (the library's host logic, no device): the rows it
+    # plans, built with the oracle's projections, are the rows of the
+    # oracle's step-by-step Start, bit for bit
+    emb, w1, b1, w2, b2, ce = small_weights(6)
+    ids = [10, 11, 12] + list(range(20, 20 + n_text)) + [13, 14, 10, 11, 12]
+    codec = [7, 8, 9, 4, 5] if n_text != 2 else [4, 5]
+    tok = qtts.PromptTokens(TOK["tts_bos"], TOK["tts_eos"], TOK["tts_pad"], TOK["codec_pad"], TOK["codec_bos"])
+    pre, trail = qtts.prompt_plan(tok, ids, codec, non_streaming)
+    opf, otr, _ = O.start_rows(emb, w1, b1, w2, b2, ce, TOK, ids, codec, non_streaming)
+    assert pre.shape[0] == opf.shape[0] and trail.shape[0] == otr.shape[0]
+
+    def build(plan):
+        rows = O.text_project(emb, plan[:, 0], w1, b1, w2, b2) if len(plan) else np.zeros((0, ce.shape[1]))
+        for r, c in enumerate(plan[:, 1]):
+            if c >= 0:
+                rows[r] += ce[c]
+        return rows
+
+    np.testing.assert_array_equal(build(pre), opf)
+    np.testing.assert_array_equal(build(trail), otr)
+
+
+def test_library_plan_checks_counts():
+    tok = qtts.PromptTokens(1, 2, 3, 4, 5)
+    for ids, codec in (([0] * 8, [4, 5]), ([0] * 9, [5])):
+        with pytest.raises(qtts.EQwenLm) as e:
+            qtts.prompt_plan(tok, ids, codec)
+        assert e.value.code == qtts.E_ARG
