@@ -69,6 +69,18 @@ def kv_bytes_frame(talker_len, tl=28, pl=5, groups=16):
     return t + p
 
 
+def oracle_module():
+    """oracle/oracle.py (the CPU restatement's wrapper), imported by path:
+    only the cpu_baseline and reference legs use it, as the checker."""
+    import importlib.util
+    if "qtts_oracle_wrapper" not in sys.modules:
+        spec = importlib.util.spec_from_file_location("qtts_oracle_wrapper", os.path.join(ROOT, "oracle", "oracle.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["qtts_oracle_wrapper"] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules["qtts_oracle_wrapper"]
+
+
 def measured_peaks():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -76,17 +88,36 @@ def measured_peaks():
         return None
 
 
+def source_digest():
+    """sha256 (first 16 hex digits) of the kernel sources (csrc/*.cu, *.cuh,
+    *.h): names the build a profile was captured on."""
+    import glob
+    import hashlib
+    h = hashlib.sha256()
+    for f in sorted(glob.glob(os.path.join(PKG, "csrc", "*"))):
+        if f.endswith((".cu", ".cuh", ".h")):
+            h.update(os.path.basename(f).encode())
+            h.update(open(f, "rb").read())
+    return h.hexdigest()[:16]
+
+
 def ncu_traffic(config):
-    """DRAM bytes per launch of the frame kernel from the committed ncu
-    summary (profiles/decode_kernel_<config>_frame.md), or None."""
+    """DRAM bytes per launch of the frame kernel from an ncu capture of THIS
+    build (profiles/decode_kernel_<config>_frame.md records the source
+    digest it was captured on and the measured bytes), else None: a figure
+    measured on other code is not reported."""
     path = os.path.join(ROOT, "profiles", f"decode_kernel_{config}_frame.md")
+    got = {}
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
+            for key in ("traffic_bytes_per_launch:", "source_digest:"):
+                if line.startswith(key):
+                    got[key] = line.split(":", 1)[1].strip()
     except OSError:
-        pass
-    return None
+        return None
+    if got.get("source_digest:") != source_digest() or "traffic_bytes_per_launch:" not in got:
+        return None
+    return float(got["traffic_bytes_per_launch:"])
 
 
 class Clocks:
@@ -144,11 +175,11 @@ def build_host_model(dtype, seed=SEED, tlayers=28, players=5):
     return m
 
 
-def cpu_frames(m, dtype, prompt, frames, threads=None):
-    """The oracle on host cores: prefill (untimed), then `frames` frames;
-    returns (seconds, frames done, threads used)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
+def cpu_frames(m, dtype, prompt, frames, threads=None, seconds=None, warmup=0):
+    """The oracle on host cores: prefill and `warmup` frames (untimed), then
+    up to `frames` frames, stopping early once `seconds` have passed (after 2
+    frames); returns (seconds, frames done, threads used)."""
+    O = oracle_module()
     if threads:
         O.set_threads(threads)
     ts = O.OraStack(synth.CONFIG, m["tl"], m["tf"], dtype)
@@ -158,11 +189,15 @@ def cpu_frames(m, dtype, prompt, frames, threads=None):
     ph = O.OraHeads(synth.HIDDEN, dtype)
     for h in m["ph"]:
         ph.add(h)
-    tlm = O.OraLm(ts, th, prompt.shape[0] + frames + 8)
+    tlm = O.OraLm(ts, th, prompt.shape[0] + frames + warmup + 8)
     plm = O.OraLm(ps, ph, 32)
     tk = O.OraTalker(tlm, th, plm, ph, m["ce"], m["pe"], synth.CODEC_EOS)
     tk.start(prompt, None, m["pad"])
     codes = np.zeros(16, np.int32)
+    for _ in range(warmup):
+        if not tk.next_frame(codes):
+            tk.start(prompt, None, m["pad"])
+    tk.start(prompt, None, m["pad"])
     done = 0
     t0 = time.perf_counter()
     for _ in range(frames):
@@ -170,11 +205,42 @@ def cpu_frames(m, dtype, prompt, frames, threads=None):
             tk.start(prompt, None, m["pad"])
             continue
         done += 1
+        if seconds is not None and done >= 2 and time.perf_counter() - t0 >= seconds:
+            break
     dt = time.perf_counter() - t0
     n = O.threads()
     for o in (tk, tlm, plm, ts, ps, th, ph):
         o.free()
     return dt, done, n
+
+
+def cpu_sample(dtype, seconds=15.0, threads=None):
+    """The bounded CPU sample of cpu_baseline: the oracle (the C restatement
+    of the reference CPU path) on `threads` host threads (default: all),
+    about `seconds` of frames after the utterance's prefill.  Runs in a
+    process of its own (bench.py --cpu-sample), so that no GPU context, no
+    process group and no OMP_NUM_THREADS inherited from a launcher shares the
+    cores with it."""
+    env = dict(os.environ)
+    n = threads or os.cpu_count()
+    env["OMP_NUM_THREADS"] = str(n)
+    env.pop("OMP_PROC_BIND", None)
+    env.pop("OMP_PLACES", None)
+    r = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-sample", dtype, "--cpu-seconds",
+                        str(seconds)], env=env, capture_output=True, text=True, timeout=600)
+    if r.returncode != 0:
+        return {"error": (r.stderr or r.stdout).strip()[-300:]}
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def cpu_sample_main(dtype, seconds):
+    m = build_host_model(dtype)
+    prompt = synth.config1_prompt(SEED, PROMPT_ROWS[dtype])
+    dt, done, used = cpu_frames(m, dtype, prompt, 156, seconds=seconds)
+    print(json.dumps({"value": done / dt, "unit": "frames/s", "cores": used, "kind": "port",
+                      "sample": f"{done} frames of the configs[1] utterance after its prefill, {dt:.1f} s (C "
+                                "restatement of the reference CPU path, AVX2+FMA, OpenMP over output rows, "
+                                f"{used} threads, own process)"}), flush=True)
 
 
 def max_over_ranks(values, dist, device):
@@ -200,11 +266,10 @@ def reference_arm(args, rank):
         return
     dtype = args.config
     m = build_host_model(dtype)
-    prompt = synth.prompt(SEED + 100, PROMPT_ROWS[dtype])
+    prompt = synth.config1_prompt(SEED, PROMPT_ROWS[dtype])
     cores = os.cpu_count()
-    # warm-up frames, then K timed frames (each step = one frame on the CPU)
-    cpu_frames(m, dtype, prompt, max(1, args.warmup), cores) if args.warmup else None
-    dt, done, used = cpu_frames(m, dtype, prompt, args.steps, cores)
+    # W warm-up frames, then K timed frames (each step = one frame on the CPU)
+    dt, done, used = cpu_frames(m, dtype, prompt, args.steps, cores, warmup=args.warmup)
     fps = done / dt
     line = {
         "impl": "reference",
@@ -266,8 +331,7 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     else:
         B, K, W = args.batch, args.batch_steps, 3
         lo, hi = args.batch_ctx
-    rng = np.random.default_rng(SEED + 7 + rank)
-    ctx = rng.integers(lo, hi + 1, B)
+    ctx = synth.config2_contexts(SEED, B, lo, hi, rank)
     chunk = 16384
     tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=chunk, max_pos=hi + K + W + 8, kv_dtype="bf16")
     pb = qtts.QwenBatch(pstack, ph, max_seqs=B, max_tokens=2 * B, max_pos=16, kv_dtype="bf16")
@@ -280,7 +344,7 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
         while j < B and rows + ctx[j] <= chunk:
             rows += int(ctx[j])
             j += 1
-        ts.start(list(range(i, j)), [synth.prompt(SEED + 1000 + s, int(ctx[s])) for s in range(i, j)],
+        ts.start(list(range(i, j)), [synth.config2_prompt(s, int(ctx[s]), SEED) for s in range(i, j)],
                  [None] * (j - i), m["pad"])
         i = j
     prefill_s = time.perf_counter() - t0
@@ -298,7 +362,7 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
         frames += int(more.sum())
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = max_over_ranks([e0.elapsed_time(e1)], dist, "cuda")[0]
+    ms = max_over_ranks([e0.elapsed_time(e1)], dist, "cpu")[0]
     world = dist.get_world_size() if dist else 1
     ts.free()
     tb.free()
@@ -345,14 +409,13 @@ def prefill_measure(args, qtts, torch, m, dev, rank):
     f32) and its head on the last rows; each step resets the sequences and
     runs qtts_batch_forward from host memory (the rows up, the logits and
     normed states back)."""
-    rng = np.random.default_rng(SEED + 11 + rank)
-    lens = rng.integers(PREFILL_LEN[0], PREFILL_LEN[1] + 1, PREFILL_SEQS)
+    lens = synth.config3_lengths(SEED, PREFILL_SEQS, PREFILL_LEN[0], PREFILL_LEN[1], rank)
     T = int(lens.sum())
     th = qtts.QwenLmHeads(dev, "talker", synth.HIDDEN, "f32")
     th.add(m["th"])
     st = qtts.qwen_lm_stack(dev, synth.CONFIG, m["tl"], m["tf"], "f32")
     b = qtts.QwenBatch(st, th, max_seqs=PREFILL_SEQS, max_tokens=T, max_pos=PREFILL_LEN[1], kv_dtype="f32")
-    x = np.concatenate([synth.prompt(SEED + 2000 + i, int(n)) for i, n in enumerate(lens)])
+    x = np.concatenate([synth.config3_prompt(i, int(n), SEED) for i, n in enumerate(lens)])
     x = torch.from_numpy(x).pin_memory().numpy()
     seqs = np.arange(PREFILL_SEQS)
 
@@ -426,7 +489,7 @@ def start_prompt_measure(qtts, tk, dev, cpu_leg):
                            "every row with the codec rows added, 28-layer prefill, first ChooseCode0",
                "timing": "host wall clock around the synchronous call, 20 calls after 3"}
         if cpu_leg:
-            import oracle as O
+            O = oracle_module()
             toks = {"tts_bos": 4093, "tts_eos": 4094, "tts_pad": 4095, "codec_pad": 2148, "codec_bos": 2149}
             ce = synth.codec_embedding(SEED)
             t0 = time.perf_counter()
@@ -471,7 +534,7 @@ def heads_load_measure(qtts, dev, m, cpu_leg):
                          "synchronous), the file opened before and the digest read after, as the reference's "
                          "test times it; best of 3 after 1"}
         if cpu_leg:
-            import oracle as O
+            O = oracle_module()
             t0 = time.perf_counter()
             for hm in m["ph"]:
                 O.quantize_q8_0(torch.from_numpy(hm).to(torch.bfloat16).float().numpy())
@@ -520,7 +583,7 @@ def codec_measure(qtts, dev, cpu_leg):
                "timing": "host wall clock around qtts_codec_decode (codes up, samples back), 50 frames after 8",
                "kernels": "float32 CUDA-core GEMM over im2col rows for every convolution and projection"}
         if cpu_leg:
-            import oracle as O
+            O = oracle_module()
             oc = O.OraCodec(w)
             t0 = time.perf_counter()
             oc.decode(codes[:4])
@@ -532,19 +595,40 @@ def codec_measure(qtts, dev, cpu_leg):
         shutil.rmtree(d, ignore_errors=True)
 
 
+def summary(line):
+    """The headline figures of every measurement in the line, compact (the
+    configs[2]-[4] numbers sit in long nested objects)."""
+    def pick(d, *keys):
+        for k in keys:
+            if not isinstance(d, dict) or k not in d:
+                return None
+            d = d[k]
+        return round(d, 4) if isinstance(d, float) else d
+    return {"b1_frames_s": pick(line, "value"), "b1_ms_per_frame": pick(line, "ms_per_step"),
+            "b1_hbm_frac": pick(line, "roofline", "frac"), "b1_e2e_frames_s": pick(line, "e2e", "value"),
+            "cpu_frames_s": pick(line, "cpu_baseline", "value"),
+            "b64_frames_s": pick(line, "batched", "value"), "b64_hbm_frac": pick(line, "batched", "roofline", "frac"),
+            "box_frames_s": pick(line, "box", "value"), "box_hbm_frac": pick(line, "box", "roofline", "frac"),
+            "prefill_tokens_s": pick(line, "prefill", "value"),
+            "prefill_tensor_frac": pick(line, "prefill", "roofline", "frac"),
+            "codec_ms_per_frame_streaming": pick(line, "codec", "ms_per_frame_streaming")}
+
+
 def gpu_arm(args, rank, world, local_rank):
     import torch
     import qtts
     torch.cuda.set_device(local_rank)
     dist = None
     if world > 1:
+        # the harness only: a barrier around the timed regions and the max of
+        # the ranks' timings.  Nothing of the path crosses devices (each rank
+        # decodes its own utterances), so gloo on the host serves it.
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
     dtype = args.config
     m = build_host_model(dtype, tlayers=args.talker_layers, players=args.pred_layers)
-    prompt = synth.prompt(SEED + 100 + rank, PROMPT_ROWS[dtype])
+    prompt = synth.config1_prompt(SEED, PROMPT_ROWS[dtype], rank)
     K, W = args.steps, args.warmup
     dev = qtts.QwenDevice(local_rank)
     th = qtts.QwenLmHeads(dev, "talker", synth.HIDDEN, dtype)
@@ -656,16 +740,12 @@ def gpu_arm(args, rank, world, local_rank):
     g1.record(stream)
     torch.cuda.synchronize()
     ms_s = g0.elapsed_time(g1)
-    ms, ms_e2e, ms_s = max_over_ranks([ms, ms_e2e, ms_s], dist, "cuda")
+    ms, ms_e2e, ms_s = max_over_ranks([ms, ms_e2e, ms_s], dist, "cpu")
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        # bounded CPU sample: ~15 s of the oracle on the host cores
-        t1, d1, _ = cpu_frames(m, dtype, prompt, 1, os.cpu_count())
-        nf = int(min(max(2, 15.0 / max(t1, 1e-3)), K))
-        dt, done, used = cpu_frames(m, dtype, prompt, nf, os.cpu_count())
-        cpu = {"value": done / dt, "unit": "frames/s", "cores": used, "kind": "port",
-               "sample": f"{done} frames of the same utterance after its prefill (C restatement of the reference "
-                         "CPU path, AVX2+FMA, OpenMP over output rows)"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and (args.talker_layers, args.pred_layers) == (28, 5):
+        # bounded CPU sample (~15 s of the oracle on all host cores), at N=1
+        # only and in a process of its own
+        cpu = cpu_sample(dtype)
     # the prompt of Start and the heads' load, on rank 0 (no timed collective
     # follows); a failure is recorded in the line, never fatal to it
     start_p = heads_l = codec = None
@@ -723,6 +803,7 @@ def gpu_arm(args, rank, world, local_rank):
             "codec": codec,
             "weights_generation_s": m["gen_s"],
         }
+        line["summary"] = summary(line)  # last key: it stays in a tail of the output
         print(json.dumps(line), flush=True)
     tk.free()
     tlm.free()
@@ -743,6 +824,9 @@ def main():
     ap.add_argument("--config", choices=["q8_0", "f32"], default="q8_0")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # the bounded CPU sample of cpu_baseline, run by bench.py in a process of its own
+    ap.add_argument("--cpu-sample", choices=["q8_0", "f32"], default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help=argparse.SUPPRESS)
     # configs[2] beside the bench line: B utterances decoded together (0: off)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=20)
@@ -758,7 +842,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
+    if args.cpu_sample:
+        cpu_sample_main(args.cpu_sample, args.cpu_seconds)
+    elif args.impl == "reference":
         reference_arm(args, rank)
     else:
         gpu_arm(args, rank, world, local_rank)

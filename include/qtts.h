@@ -160,13 +160,16 @@ int qtts_lm_forward(qtts_lm *lm, const float *x, int rows, int head, float *logi
  * milliseconds) are off limits, or a host whose GPU memory is all handed out
  * by its own pool allocator.  No counterpart in the reference.  x
  * [rows][hidden], logits (head rows) and hidden [hidden] are DEVICE pointers
- * owned by the caller (logits/hidden may be NULL); x is read in place.  The
+ * owned by the caller (logits/hidden may be NULL), each 16-byte aligned
+ * (QTTS_E_ARG otherwise, before anything runs); x is read in place.  The
  * call allocates nothing: the kernel's scratch is one static device array of
  * 833,280 bytes (every GPU that loads the library holds it until exit),
  * sized for at most 160 SMs and heads of at most 4096 rows; larger requests
- * fail with QTTS_E_CAPACITY.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) with that device current:
- * make that first call before any stream capture.  All calls on one GPU
+ * fail with QTTS_E_CAPACITY.  qtts_lm_create looks up the array's device
+ * address (cudaGetSymbolAddress, which may load the library's module on that
+ * device) with its device current, so these calls load nothing; only if that
+ * lookup failed does the first call repeat it: then make that first call
+ * before any stream capture and outside the real-time thread.  All calls on one GPU
  * share its copy of the array, which keeps the last call's contents (each
  * call first clears the barrier and error words it needs at zero): calls
  * that overlap on the same GPU, from two threads or two lms, race and must
@@ -455,6 +458,12 @@ int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t *seqs, int3
 /* The CUDA stream (cudaStream_t) the frames run on, for callers that time
  * them with events. */
 int qtts_talkers_stream(qtts_talkers *t, void **stream);
+/* The talker probes of TQwenTalker.Emit (talker.pas:590, 678) for utterance
+ * seq: the logits (head 0, [vocab]) and the normed state ([hidden]) of its
+ * last talker forward.  seq must have taken part in the last talker call of
+ * this object (qtts_talkers_start or _next_frame), else QTTS_E_STATE.
+ * Either pointer may be NULL. */
+int qtts_talkers_probe(qtts_talkers *t, int seq, float *logits, float *hidden);
 int qtts_talkers_destroy(qtts_talkers *t);
 /* The sampling of every utterance of the batch (TQwenSampling as for
  * qtts_talker_set_sampling): utterance s draws from the stream seed + s, so

@@ -159,8 +159,9 @@ struct qtts_talker {
     unsigned char *seen;
     FrameState *fs, *h_fs;
     const uint8_t **d_pheads;
-    int *d_hist;  // codes of qtts_talker_run
+    int *d_hist;  // codes of qtts_talker_run: room for one frame per talker position
     size_t hist_cap;
+    int step;     // FrameState.step as of the last call (frames since start)
     int started;
     SampleParams samp0, samp;  // code 0 / the predictor's codes (on = 0: greedy)
     uint64_t seed;
@@ -1040,6 +1041,8 @@ static void lm_free(qtts_lm *m) {
     delete m;
 }
 
+static void *noalloc_lookup(int ordinal);
+
 extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out) {
     if (!stack || !heads || !out) return set_err(QTTS_E_ARG, "qtts_lm_create: NULL argument");
     *out = nullptr;
@@ -1079,6 +1082,10 @@ extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos,
         return rc;
     }
     m->stack = stack;  // owned from here on
+    // the device address of qtts_lm_forward_noalloc's static scratch, taken
+    // here (set-up, this device current) so that those calls load nothing;
+    // a failure is not this call's: the first such call retries and reports
+    (void)noalloc_lookup(dev->ordinal);
     *out = m;
     return QTTS_OK;
 }
@@ -1217,8 +1224,10 @@ extern "C" int qtts_talker_create(qtts_lm *talker, qtts_lm *pred, const qtts_tal
         cudaMalloc(&t->tts_pad, H * 4) != cudaSuccess || cudaMalloc(&t->seen, c->vocab) != cudaSuccess ||
         cudaMalloc(&t->fs, sizeof(FrameState)) != cudaSuccess ||
         cudaMallocHost(reinterpret_cast<void **>(&t->h_fs), sizeof(FrameState)) != cudaSuccess ||
-        cudaMalloc(&t->d_pheads, sizeof(uint8_t *) * (c->groups - 1)) != cudaSuccess)
+        cudaMalloc(&t->d_pheads, sizeof(uint8_t *) * (c->groups - 1)) != cudaSuccess ||
+        cudaMalloc(&t->d_hist, static_cast<size_t>(talker->max_pos) * c->groups * 4) != cudaSuccess)
         rc = set_err(QTTS_E_OOM, "qtts_talker_create: out of device memory");
+    t->hist_cap = static_cast<size_t>(talker->max_pos) * c->groups;
     if (rc == QTTS_OK) {
         std::vector<const uint8_t *> ph(c->groups - 1);
         for (int g = 0; g < c->groups - 1; ++g) ph[g] = pred->heads->mats[g].d;
@@ -1277,6 +1286,7 @@ static int talker_start(qtts_talker *t, bool rows_dev, const float *prefill, int
     CK(cudaMemcpyAsync(t->fs, &h, sizeof(h), cudaMemcpyHostToDevice, st));
     CK(cudaStreamSynchronize(st));
     t->done = h.done;
+    t->step = h.step;
     t->started = 1;
     return QTTS_OK;
 }
@@ -1382,6 +1392,7 @@ static int next_frame(qtts_talker *t, int32_t *codes, int *more, uint64_t *stamp
     }
     for (int g = 0; g < t->cfg.groups; ++g) codes[g] = f.codes[g];
     t->done = f.done;
+    t->step = f.step;
     tl->len = f.tlen;
     pl->len = t->cfg.groups;
     *more = 1;
@@ -1399,17 +1410,12 @@ extern "C" int qtts_talker_run(qtts_talker *t, int frames, int32_t *codes, int *
                        tl->max_pos);
     CK(cudaSetDevice(tl->dev->ordinal));
     const int wdt = tl->stack->cfg.dtype == QTTS_DTYPE_F32 ? WDT_F32 : WDT_Q8;
-    size_t need = static_cast<size_t>(frames) * t->cfg.groups;
-    if (need > t->hist_cap) {
-        if (t->d_hist) CK(cudaFree(t->d_hist));
-        t->d_hist = nullptr;
-        t->hist_cap = 0;
-        CK(cudaMalloc(&t->d_hist, need * 4));
-        t->hist_cap = need;
-    }
-    CK(cudaMemcpyAsync(t->h_fs, t->fs, sizeof(FrameState), cudaMemcpyDeviceToHost, tl->run.stream));
-    CK(cudaStreamSynchronize(tl->run.stream));
-    const int step0 = t->h_fs->step;
+    // each frame takes one talker position, so the history buffer made at
+    // create (max_pos frames) holds the run: nothing is allocated or read
+    // back before the launches
+    if (static_cast<size_t>(frames) * t->cfg.groups > t->hist_cap)
+        return set_err(QTTS_E_CAPACITY, "qtts_talker_run: %d frames, room for %zu", frames, t->hist_cap / t->cfg.groups);
+    const int step0 = t->step;
     Job j = frame_job(t);
     // frame f is written at row (step0 + f) - step0: shift the base pointer
     j.codes_hist = t->d_hist - static_cast<ptrdiff_t>(step0) * t->cfg.groups;
@@ -1426,6 +1432,7 @@ extern "C" int qtts_talker_run(qtts_talker *t, int frames, int32_t *codes, int *
     if (n > 0) CK(cudaMemcpy(codes, t->d_hist, static_cast<size_t>(n) * t->cfg.groups * 4, cudaMemcpyDeviceToHost));
     *produced = n;
     t->done = f.done;
+    t->step = f.step;
     tl->len = f.tlen;
     if (n > 0) pl->len = t->cfg.groups;
     return QTTS_OK;
@@ -2149,21 +2156,30 @@ constexpr size_t NA_BYTES = NA_XT + al256(H * 4);  // 833,280 bytes
 // Every GPU that loads the library holds this array until the process exits.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
 
-// its device address, per device (taken once, with that device current)
+// its device address, per device (taken once, with that device current:
+// by qtts_lm_create, or else by the first call on the device)
 static std::mutex g_noalloc_mu;
 static void *g_noalloc_ptr[256];
 
-static int noalloc_scratch(int ordinal, unsigned char **out) {
-    if (ordinal < 0 || ordinal >= 256) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: device %d", ordinal);
+static void *noalloc_lookup(int ordinal) {
+    if (ordinal < 0 || ordinal >= 256) return nullptr;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (!g_noalloc_ptr[ordinal]) {
         void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return set_err(QTTS_E_CUDA, "qtts_lm_forward_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        g_noalloc_ptr[ordinal] = p;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) == cudaSuccess && p) g_noalloc_ptr[ordinal] = p;
     }
-    *out = static_cast<unsigned char *>(g_noalloc_ptr[ordinal]);
+    return g_noalloc_ptr[ordinal];
+}
+
+static int noalloc_scratch(int ordinal, unsigned char **out) {
+    if (ordinal < 0 || ordinal >= 256) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: device %d", ordinal);
+    void *p = noalloc_lookup(ordinal);
+    if (!p) {
+        void *q = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
+        return set_err(QTTS_E_CUDA, "qtts_lm_forward_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    }
+    *out = static_cast<unsigned char *>(p);
     return QTTS_OK;
 }
 
@@ -2172,6 +2188,11 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
     if (!m) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: NULL lm");
     if (rows <= 0) return QTTS_OK;
     if (!x) return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: x is NULL");
+    // the kernel moves these rows with 16-byte loads and stores: an address
+    // off that boundary is refused here, before anything is launched
+    const auto off16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
+    if (off16(x) || (logits && off16(logits)) || (hidden && off16(hidden)))
+        return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: x, logits and hidden must be 16-byte aligned");
     if (logits && (head < 0 || head >= static_cast<int>(m->heads->mats.size())))
         return set_err(QTTS_E_ARG, "qtts_lm_forward_noalloc: no head %d in %s", head, m->heads->name.c_str());
     if (logits && m->heads->mats[head].rows > NOALLOC_MAX_HEAD_ROWS)
@@ -2716,6 +2737,7 @@ struct qtts_talkers {
     int *d_seqs, *d_aux, *d_codes, *d_done;
     int *h_io;  // pinned: seqs | aux | codes | done | errs
     std::vector<char> started, done;
+    std::vector<int> last_talker;  // the utterances of the last talker call, in its row order
     std::vector<void *> allocs;
     // the frame as one CUDA graph, for one list of active utterances; its
     // calls read their metadata from fixed pinned slots rewritten each frame
@@ -2887,6 +2909,7 @@ static int talkers_start(qtts_talkers *t, int nseq, const int32_t *seqs, const i
                                                 t->d_done, 1, t->samp0, static_cast<unsigned long long>(t->seed));
     CK(cudaGetLastError());
     if ((rc = talkers_finish(t, "qtts_talkers_start"))) return rc;
+    t->last_talker.assign(seqs, seqs + nseq);
     for (int i = 0; i < nseq; ++i) {
         t->started[seqs[i]] = 1;
         t->done[seqs[i]] = 0;  // eos is forbidden before 2 frames
@@ -3043,12 +3066,29 @@ extern "C" int qtts_talkers_next_frame(qtts_talkers *t, int nseq, const int32_t 
     CK(cudaGraphLaunch(t->graph, st));
     CK(cudaStreamSynchronize(st));
     ++t->frames_graph;
+    t->last_talker = act;
     if (io_errs(t)[0] || io_errs(t)[1]) return set_err(QTTS_E_TIMEOUT, "qtts_talkers_next_frame: a device wait gave up");
     for (int j = 0; j < n; ++j) {
         std::memcpy(codes + static_cast<size_t>(slot[j]) * G, io_codes(t) + static_cast<size_t>(j) * G, G * 4);
         more[slot[j]] = 1;
         t->done[act[j]] = io_done(t)[j] ? 1 : 0;
     }
+    return QTTS_OK;
+}
+
+extern "C" int qtts_talkers_probe(qtts_talkers *t, int seq, float *logits, float *hidden) {
+    if (!t) return set_err(QTTS_E_ARG, "qtts_talkers_probe: NULL talkers");
+    if (seq < 0 || seq >= t->tb->max_seqs) return set_err(QTTS_E_ARG, "qtts_talkers_probe: bad sequence %d", seq);
+    int row = -1;
+    for (size_t i = 0; i < t->last_talker.size(); ++i)
+        if (t->last_talker[i] == seq) row = static_cast<int>(i);
+    if (row < 0) return set_err(QTTS_E_STATE, "qtts_talkers_probe: sequence %d took no part in the last talker call", seq);
+    CK(cudaSetDevice(t->tb->dev->ordinal));
+    CK(cudaStreamSynchronize(t->stream));
+    if (logits)
+        CK(cudaMemcpy(logits, t->tb->logits + static_cast<size_t>(row) * t->cfg.vocab, static_cast<size_t>(t->cfg.vocab) * 4,
+                      cudaMemcpyDeviceToHost));
+    if (hidden) CK(cudaMemcpy(hidden, t->hid + static_cast<size_t>(seq) * H, H * 4, cudaMemcpyDeviceToHost));
     return QTTS_OK;
 }
 

@@ -176,6 +176,7 @@ EXPORTS = {
     "qtts_talkers_start_prompt": [P, P, ctypes.POINTER(PromptTokens), I, P, P, P, P, P, P],
     "qtts_talkers_next_frame": [P, I, P, P, P],
     "qtts_talkers_stream": [P, ctypes.POINTER(P)],
+    "qtts_talkers_probe": [P, I, P, P],
     "qtts_talkers_destroy": [P],
     "qtts_quantize_q8_0": [P, P, ctypes.c_int64, P],
     "qtts_textproj_create": [P, I, I, I, I, P, P, P, P, P, ctypes.POINTER(P)],
@@ -722,6 +723,7 @@ class QwenTalkers:
                                         ctypes.byref(h)))
         self.handle = h
         self.groups = groups
+        self.vocab = vocab
         self.hidden = talker.hidden
 
     def set_sampling(self, do_sample=True, temperature=0.9, top_k=50, top_p=1.0, sub_do_sample=True,
@@ -765,6 +767,13 @@ class QwenTalkers:
         more = np.zeros(sq.size, np.int32)
         check(lib().qtts_talkers_next_frame(self.handle, sq.size, _ptr(sq), _ptr(codes), _ptr(more)))
         return codes, more.astype(bool)
+
+    def probe(self, seq):
+        """(logits, hidden) of utterance seq's last talker forward."""
+        lg = np.empty(self.vocab, np.float32)
+        hd = np.empty(self.hidden, np.float32)
+        check(lib().qtts_talkers_probe(self.handle, int(seq), _ptr(lg), _ptr(hd)))
+        return lg, hd
 
     @property
     def stream(self):

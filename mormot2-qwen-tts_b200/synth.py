@@ -185,3 +185,31 @@ def codec_weights(seed):
     lin("decoder.decoder.6.conv.weight", 1, 96, 7, gain=0.3)
     vec("decoder.decoder.6.conv.bias", 1, 0.0, 0.01)
     return W
+
+
+# The inputs of the benchmark workloads (BASELINE.json configs[1]-[3]), shared
+# by bench.py and by the full-size parity fixtures, so that the parity tests
+# check exactly what is timed.  `rank` offsets the draws of a replica.
+def config1_prompt(seed=1, rows=40, rank=0):
+    """the N(0, 1) prompt of the streaming utterance."""
+    return prompt(seed + 100 + rank, rows)
+
+
+def config2_contexts(seed=1, n=64, lo=50, hi=1000, rank=0):
+    """per-utterance context lengths, uniform in [lo, hi]."""
+    return np.random.default_rng(seed + 7 + rank).integers(lo, hi + 1, n)
+
+
+def config2_prompt(s, rows, seed=1):
+    """the N(0, 1) rows that fill utterance s's context."""
+    return prompt(seed + 1000 + s, rows)
+
+
+def config3_lengths(seed=1, n=16, lo=256, hi=2048, rank=0):
+    """prefill prompt lengths, uniform in [lo, hi]."""
+    return np.random.default_rng(seed + 11 + rank).integers(lo, hi + 1, n)
+
+
+def config3_prompt(i, rows, seed=1):
+    """the N(0, 1) rows of prompt i."""
+    return prompt(seed + 2000 + i, rows)

@@ -78,6 +78,7 @@ def _load():
         "ora_codec_error": (ctypes.c_char_p, []),
         "ora_talker_start": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P]),
         "ora_talker_next_frame": (ctypes.c_int, [P, P]),
+        "ora_talker_next_frame_margins": (ctypes.c_int, [P, P, P]),
         "ora_talker_check_frame": (ctypes.c_int, [P, P, P]),
         "ora_talker_check_frame_ranks": (ctypes.c_int, [P, P, P, P]),
         "ora_talker_logits": (P, [P]),
@@ -380,6 +381,16 @@ class OraTalker:
         if rc < 0:
             raise RuntimeError("oracle: KV cache full")
         return rc == 1
+
+    def next_frame_margins(self, codes):
+        """next_frame (greedy) with the margin of each choice: returns
+        (more, margins), margins[g] = the chosen value minus the next
+        largest value of choice g (after the processors)."""
+        m = np.zeros(self.groups, np.float32)
+        rc = lib.ora_talker_next_frame_margins(self.handle, _p(codes), _p(m))
+        if rc < 0:
+            raise RuntimeError("oracle: KV cache full")
+        return rc == 1, m
 
     def check_frame(self, codes):
         """The frame whose codes were chosen elsewhere: returns (more, gaps),

@@ -820,9 +820,19 @@ static int rank_of(const float *x, int n, float v) {
     return r;
 }
 
-static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap, int *rank) {
+/* x[best] minus the largest of the other values: how far the choice is
+ * from a tie (0 for a tie, +inf when every other value is -inf) */
+static float margin_of(const float *x, int n, int best) {
+    float second = -INFINITY;
+    for (int i = 0; i < n; i++)
+        if (i != best && x[i] > second) second = x[i];
+    return x[best] - second;
+}
+
+static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap, int *rank, float *margin) {
     int H = t->H;
     int code = ora_choose_code0(t->logits, t->vocab, t->eos, t->history, t->nhist, t->penalty, t->work);
+    if (margin) margin[0] = margin_of(t->work, t->vocab, code);
     if (t->do_sample && !force)
         code = ora_sample(t->work, t->vocab, t->temperature, t->top_k, t->top_p,
                           ora_sample_uniform(t->seed, t->step, 0));
@@ -849,6 +859,7 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap,
             if (ora_lm_forward(t->pred, t->x, 1, t->ph, g, t->plogits, NULL, NULL, NULL)) return -1;
         }
         int best = ora_argmax(t->plogits, t->pvocab);
+        if (margin) margin[g + 1] = margin_of(t->plogits, t->pvocab, best);
         if (t->sub_do_sample && !force)
             best = ora_sample(t->plogits, t->pvocab, t->sub_temperature, t->sub_top_k, t->sub_top_p,
                               ora_sample_uniform(t->seed, t->step, g + 1));
@@ -872,13 +883,20 @@ static int talker_frame(ora_talker *t, const int *force, int *codes, float *gap,
 }
 
 /* returns 1 and fills codes[groups], 0 at eos, -1 when a cache is full */
-int ora_talker_next_frame(ora_talker *t, int *codes) { return talker_frame(t, NULL, codes, NULL, NULL); }
+int ora_talker_next_frame(ora_talker *t, int *codes) { return talker_frame(t, NULL, codes, NULL, NULL, NULL); }
+
+/* as ora_talker_next_frame (greedy), with margin[g]: how far choice g's best
+ * value lies above the next one (the room a second implementation has for
+ * rounding differences before its first maximum moves) */
+int ora_talker_next_frame_margins(ora_talker *t, int *codes, float *margin) {
+    return talker_frame(t, NULL, codes, NULL, NULL, margin);
+}
 
 /* the frame chosen elsewhere (codes[groups]), with the gaps of its choices */
 int ora_talker_check_frame(ora_talker *t, const int *codes, float *gap) {
     int own[64];
     if (t->groups > 64) return -1;
-    return talker_frame(t, codes, own, gap, NULL);
+    return talker_frame(t, codes, own, gap, NULL, NULL);
 }
 
 /* as ora_talker_check_frame, with rank[g]: how many of choice g's values
@@ -886,7 +904,7 @@ int ora_talker_check_frame(ora_talker *t, const int *codes, float *gap) {
 int ora_talker_check_frame_ranks(ora_talker *t, const int *codes, float *gap, int *rank) {
     int own[64];
     if (t->groups > 64) return -1;
-    return talker_frame(t, codes, own, gap, rank);
+    return talker_frame(t, codes, own, gap, rank, NULL);
 }
 
 const float *ora_talker_logits(const ora_talker *t) { return t->logits; }

@@ -1,0 +1,197 @@
+"""Parity at the full sizes of BASELINE.json's configs, on exactly the inputs
+bench.py times (synth.config*_*, seed 1), through the C-ABI.
+
+Greedy codes and near-ties.  On random weights many choices are close: the
+oracle's own 156-frame trajectory of configs[1] has choices whose best value
+lies only 6.2e-6, 2.4e-5 and 9.4e-5 above the next one
+(tests/golden/config1_q8_0.npz, `margins`).  Any implementation whose float32
+sums run in another order (the reference's AVX2 path against Python
+included) can pick the other code there.  So the contract checked here is:
+
+- every device choice is the oracle's first maximum, or lies within NEAR_TIE
+  of the oracle's best value on the same trajectory (the oracle replays each
+  frame driven by the device's codes: ora_talker_check_frame_ranks);
+- against the oracle's own free-running codes (the fixture), the device's
+  codes are identical up to the first choice where they differ, and that
+  choice is a certified near-tie (its fixture margin <= NEAR_TIE);
+- the talker logits are within the north-star tolerance every frame, on the
+  replayed trajectory.
+
+NEAR_TIE for the batch-1 kernels (f32 activations, f32 KV) is 1e-4, the
+north-star f32 logits tolerance.  The batched path (fp16 activations on the
+tensor cores, bf16 KV) is held to its own measured logit error: a divergence
+must lie within twice the largest logit error measured in the same run, and
+that error within the Q8_0 tolerance.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import qtts
+import synth
+from model_util import TalkerPair, cosine
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+SEED = 1
+NEAR_TIE = 1e-4
+Q8_ATOL = 2e-2
+Q8_COS = 0.9999
+PREFILL_ATOL = 2e-3
+
+
+def report(name, **kv):
+    """One JSON line of measured figures (visible with pytest -s)."""
+    print(json.dumps({"test": name, **kv}), flush=True)
+
+
+def test_config1_q8_0_156_frames(device):
+    # 28-layer talker + 5-layer predictor, Q8_0, a 40-row prompt,
+    # 156 frames of streaming generation (the bench line's workload)
+    fx = np.load(os.path.join(GOLD, "config1_q8_0.npz"))
+    n_frames = fx["codes"].shape[0]
+    tp = TalkerPair(device, SEED, 28, 5, "q8_0", max_pos=256)
+    try:
+        lg, _ = tp.start(synth.config1_prompt(SEED), None, synth.text_rows(SEED, 1, key=1)[0])
+        lo = tp.ora.logits()
+        # the oracle on this machine is the oracle that wrote the fixture
+        assert np.array_equal(lo, fx["logits0"])
+        assert np.abs(lg - lo).max() <= Q8_ATOL and cosine(lg, lo) >= Q8_COS
+        worst, worst_cos = float(np.abs(lg - lo).max()), cosine(lg, lo)
+        cd = np.zeros(16, np.int32)
+        free_run, first_div, exact, gaps = True, None, 0, []
+        for f in range(n_frames):
+            assert tp.dev.next_frame(cd), f"frame {f}: eos on the device only"
+            more, gap, rank = tp.ora.check_frame_ranks(cd)
+            assert more, f"frame {f}: eos in the oracle only"
+            assert np.all(gap <= NEAR_TIE), (f, cd, gap)
+            exact += int(np.sum(rank == 0))
+            gaps += [float(g) for g in gap[gap > 0]]
+            if free_run and not np.array_equal(cd, fx["codes"][f]):
+                g = int(np.nonzero(cd != fx["codes"][f])[0][0])
+                margin = float(fx["margins"][f][g])
+                first_div = {"frame": f, "group": g, "oracle_margin": margin}
+                assert margin <= NEAR_TIE, first_div
+                free_run = False
+            lg, _ = tp.dev.probe()
+            lo = tp.ora.logits()
+            d, c = float(np.abs(lg - lo).max()), cosine(lg, lo)
+            assert d <= Q8_ATOL and c >= Q8_COS, (f, d, c)
+            worst, worst_cos = max(worst, d), min(worst_cos, c)
+        report("config1_q8_0_156_frames", frames=n_frames, choices=16 * n_frames, first_maxima=exact,
+               near_tie_gaps=gaps, identical_to_fixture=free_run, first_divergence=first_div,
+               max_abs_logit_diff=worst, min_cosine=worst_cos)
+    finally:
+        tp.free()
+
+
+def test_config3_prefill_16_prompts(device):
+    # 16 prompts of U(256, 2048) rows through the 28-layer talker
+    # (f32 weights; tensor-core projections with fp16 activations, f32
+    # softmax, f32 KV) in one batched call; the last row's logits within 2e-3
+    fx = np.load(os.path.join(GOLD, "config3_f32_prefill.npz"))
+    lens = synth.config3_lengths(SEED)
+    assert np.array_equal(lens, fx["lens"])
+    ls, final = synth.stack(SEED, "talker", 28)
+    th = qtts.QwenLmHeads(device, "talker", synth.HIDDEN, "f32")
+    th.add(synth.talker_head(SEED))
+    st = qtts.qwen_lm_stack(device, synth.CONFIG, ls, final, "f32")
+    del ls
+    b = qtts.QwenBatch(st, th, max_seqs=lens.size, max_tokens=int(lens.sum()), max_pos=int(lens.max()),
+                       kv_dtype="f32")
+    try:
+        x = np.concatenate([synth.config3_prompt(i, int(n), SEED) for i, n in enumerate(lens)])
+        logits, hidden = b.forward(np.arange(lens.size), lens, x)
+        d = np.abs(logits - fx["logits"]).max(axis=1)
+        dh = np.abs(hidden - fx["hidden"]).max(axis=1)
+        report("config3_prefill_16_prompts", rows=int(lens.sum()), max_abs_logit_diff=[float(v) for v in d],
+               max_abs_hidden_diff=float(dh.max()))
+        assert d.max() <= PREFILL_ATOL, d
+        for i in range(lens.size):
+            assert int(np.argmax(logits[i])) == int(np.argmax(fx["logits"][i])) or \
+                np.sort(fx["logits"][i])[-1] - np.sort(fx["logits"][i])[-2] <= 2 * PREFILL_ATOL
+    finally:
+        b.free()
+        qtts.stack_destroy(st)
+        th.free()
+
+
+def test_config2_b64_three_frames(device):
+    # 64 utterances with contexts U(50, 1000) (prefilled through
+    # the batched path), Q8_0 weights, paged bf16 KV, 3 frames of the
+    # batched loop (15 predictor steps + 1 talker step each, one CUDA graph)
+    fx = np.load(os.path.join(GOLD, "config2_q8_0_b64.npz"))
+    ctx = synth.config2_contexts(SEED)
+    assert np.array_equal(ctx, fx["ctx"])
+    B = ctx.size
+    tls, tf = synth.stack(SEED, "talker", 28)
+    pls, pf = synth.stack(SEED, "predictor", 5)
+    tst = qtts.qwen_lm_stack(device, synth.CONFIG, tls, tf, "q8_0")
+    pst = qtts.qwen_lm_stack(device, synth.CONFIG, pls, pf, "q8_0")
+    del tls, pls
+    th = qtts.QwenLmHeads(device, "talker", synth.HIDDEN, "q8_0")
+    th.add(synth.talker_head(SEED))
+    ph = qtts.QwenLmHeads(device, "predictor", synth.HIDDEN, "q8_0")
+    for h in synth.predictor_heads(SEED):
+        ph.add(h)
+    chunk = 16384
+    tb = qtts.QwenBatch(tst, th, max_seqs=B, max_tokens=chunk, max_pos=int(ctx.max()) + 8, kv_dtype="bf16")
+    pb = qtts.QwenBatch(pst, ph, max_seqs=B, max_tokens=2 * B, max_pos=16, kv_dtype="bf16")
+    ts = qtts.QwenTalkers(tb, pb, synth.codec_embedding(SEED), synth.predictor_embeddings(SEED), synth.CODEC_EOS)
+    try:
+        pad = synth.text_rows(SEED, 1, key=1)[0]
+        d0 = np.zeros(B)
+        c0 = np.zeros(B)
+        i = 0
+        while i < B:
+            j, rows = i, 0
+            while j < B and rows + ctx[j] <= chunk:
+                rows += int(ctx[j])
+                j += 1
+            ts.start(list(range(i, j)), [synth.config2_prompt(s, int(ctx[s]), SEED) for s in range(i, j)],
+                     [None] * (j - i), pad)
+            # the prefill's logits (ChooseCode0 of frame 0 reads them)
+            for s in range(i, j):
+                lg, _ = ts.probe(s)
+                d0[s], c0[s] = np.abs(lg - fx["logits0"][s]).max(), cosine(lg, fx["logits0"][s])
+            i = j
+        err = float(d0.max())
+        assert err <= Q8_ATOL and c0.min() >= Q8_COS, (err, c0.min())
+        bound = 2.0 * err
+        seqs = list(range(B))
+        alive = np.ones(B, bool)  # still on the oracle's own trajectory
+        divergences = []
+        for f in range(fx["codes"].shape[1]):
+            codes, more = ts.next_frame(seqs)
+            assert more.all()
+            for s in range(B):
+                if not alive[s]:
+                    continue
+                diff = np.nonzero(codes[s] != fx["codes"][s, f])[0]
+                if diff.size:
+                    g = int(diff[0])
+                    m = float(fx["margins"][s, f, g])
+                    divergences.append({"utterance": s, "frame": f, "group": g, "oracle_margin": m})
+                    assert m <= bound, divergences[-1]
+                    alive[s] = False
+        d3 = []
+        for s in np.nonzero(alive)[0]:
+            lg, _ = ts.probe(int(s))
+            d = float(np.abs(lg - fx["logits3"][s]).max())
+            assert d <= Q8_ATOL and cosine(lg, fx["logits3"][s]) >= Q8_COS, (s, d)
+            d3.append(d)
+        report("config2_b64_three_frames", utterances=B, frames=int(fx["codes"].shape[1]),
+               prefill_max_abs_logit_diff=err, prefill_min_cosine=float(c0.min()), divergence_bound=bound,
+               divergences=divergences, identical_utterances=int(alive.sum()),
+               frame3_max_abs_logit_diff=max(d3) if d3 else None)
+    finally:
+        ts.free()
+        tb.free()
+        pb.free()
+        qtts.stack_destroy(tst)
+        qtts.stack_destroy(pst)
+        th.free()
+        ph.free()

@@ -138,7 +138,12 @@ def test_predictor_protocol_length(small):
     lm.free()
 
 
-REF_DATASET = "/root/reference/tests/data/infer-ref/qwen3-tts-lm"
+# the reference checkout: $QTTS_REFERENCE, else a `reference` folder beside
+# this repository
+REF_ROOT = os.environ.get("QTTS_REFERENCE",
+                          os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                                       "reference"))
+REF_DATASET = os.path.join(REF_ROOT, "tests", "data", "infer-ref", "qwen3-tts-lm")
 
 
 @pytest.mark.skipif(not os.path.isdir(REF_DATASET), reason="reference dataset not present on this machine")
@@ -187,7 +192,13 @@ def test_check_frame_replays_next_frame():
         t.start(synth.prompt(81, 6), synth.text_rows(81, 2), pad)
     codes = np.zeros(16, np.int32)
     for f in range(3):
-        assert a.next_frame(codes)
+        if f < 2:
+            assert a.next_frame(codes)
+        else:
+            # the margins variant chooses the same codes; every margin is the
+            # best value's lead over the next one, so never negative
+            more, margins = a.next_frame_margins(codes)
+            assert more and np.all(margins >= 0) and margins.shape == (16,)
         more, gap = b.check_frame(codes)
         assert more and np.all(gap == 0), gap
         assert np.array_equal(a.logits(), b.logits())
