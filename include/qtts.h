@@ -178,6 +178,16 @@ int qtts_lm_forward(qtts_lm *lm, const float *x, int rows, int head, float *logi
 int qtts_lm_forward_noalloc(qtts_lm *lm, const float *x, int rows, int head, float *logits, float *hidden);
 /* TQwenLm.Length (lm.pas:136-138). */
 int qtts_lm_length(qtts_lm *lm, int *length);
+/* The failure path of the bounded device waits, for tests (the reference
+ * bounds its waits and aborts cleanly, mormot.ai.tts.qwen.pas:541-548): the
+ * following launches of this lm (forwards, and frames when it is a talker's
+ * talker lm) run their grid barriers expecting extra_arrivals (0 or 1) more
+ * CTAs than the grid holds -- an arrival that never comes -- with every grid
+ * and group barrier spin bounded by wait_cycles SM clock cycles (0: the
+ * default bound, about 2 s).  Such a launch returns QTTS_E_TIMEOUT with the
+ * place it gave up; its positions are not appended and the next launch
+ * starts clean.  (0, 0) restores normal operation. */
+int qtts_lm_set_wait_test(qtts_lm *lm, int extra_arrivals, int64_t wait_cycles);
 /* TQwenLm.Destroy (lm.pas:362-372): frees the cache, then the stack. */
 int qtts_lm_destroy(qtts_lm *lm);
 

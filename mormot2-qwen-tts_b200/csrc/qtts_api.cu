@@ -148,6 +148,9 @@ struct qtts_lm {
     float *h_x;            // pinned [RMAX][H]
     float *h_out;          // pinned [max rows + H]
     int max_head_rows;
+    // failure-path test knobs (qtts_lm_set_wait_test): 0 = normal
+    long long test_wait_cycles;
+    int test_bar_extra;
 };
 
 struct qtts_talker {
@@ -1090,6 +1093,14 @@ extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos,
     return QTTS_OK;
 }
 
+extern "C" int qtts_lm_set_wait_test(qtts_lm *m, int extra_arrivals, int64_t wait_cycles) {
+    if (!m || extra_arrivals < 0 || extra_arrivals > 1 || wait_cycles < 0)
+        return set_err(QTTS_E_ARG, "qtts_lm_set_wait_test: bad argument");
+    m->test_bar_extra = extra_arrivals;
+    m->test_wait_cycles = wait_cycles;
+    return QTTS_OK;
+}
+
 extern "C" int qtts_lm_reset(qtts_lm *m) {
     if (!m) return set_err(QTTS_E_ARG, "qtts_lm_reset: NULL lm");
     m->len = 0;
@@ -1109,6 +1120,8 @@ static Job base_job(qtts_lm *m) {
     j.rope_cos = m->rope_cos;
     j.rope_sin = m->rope_sin;
     j.rope_pos = m->max_pos;
+    j.wait_cycles = m->test_wait_cycles > 0 ? m->test_wait_cycles : WAIT_CYCLES;
+    j.bar_extra = m->test_bar_extra;
     return j;
 }
 

@@ -195,6 +195,11 @@ struct Job {
     Scratch s;
     const float *rope_cos, *rope_sin;  // [rope_pos][HD/2]
     int rope_pos;
+    // the bound of the grid and group barrier spins (cycles; WAIT_CYCLES
+    // unless a failure-path test shortens it), and arrivals those barriers
+    // expect beyond the grid (0; a test sets 1: an arrival that never comes)
+    long long wait_cycles;
+    int bar_extra;
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -508,16 +513,17 @@ struct Compute {
                 unsigned *bar = job->s.bar;
                 asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
                 const long long t0 = clock64();
+                const unsigned want = target + static_cast<unsigned>(job->bar_extra);
                 while (true) {
                     unsigned v;
                     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-                    if (v >= target) break;
+                    if (v >= want) break;
                     if (*reinterpret_cast<volatile int *>(job->s.err) != 0) {
                         fail(ERR_TIMEOUT, where);
                         b = 1;
                         break;
                     }
-                    if (clock64() - t0 > WAIT_CYCLES) {
+                    if (clock64() - t0 > job->wait_cycles) {
                         fail(ERR_TIMEOUT, where);
                         b = 1;
                         break;
@@ -550,7 +556,7 @@ struct Compute {
                     unsigned v;
                     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
                     if (v >= gtarget) break;
-                    if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > WAIT_CYCLES) {
+                    if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > job->wait_cycles) {
                         fail(ERR_TIMEOUT, where);
                         b = 1;
                         break;

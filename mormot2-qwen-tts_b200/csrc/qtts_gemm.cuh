@@ -10,17 +10,21 @@
 //    (which also gives the residual add for free).
 //  - A operand (weights): the matrix is kept a second time in a tile-packed
 //    layout (gemm_tile_pack_kernel): the 128 rows x 64 k of one stage are one
-//    contiguous chunk (Q8_0: 8192 int8 + 256 fp16 scales = 8704 bytes), so
-//    one bulk copy (cp.async.bulk) brings a stage's weights into shared
-//    memory; warps 0-7 (two threads per weight row, 32 k each) dequantise it
+//    contiguous chunk, so one bulk copy (cp.async.bulk) brings a stage's
+//    weights into shared memory.  Q8_0 (8192 int8 + 256 fp16 scales = 8704
+//    bytes): warps 0-7 (two threads per weight row, 32 k each) dequantise it
 //    there to fp16 (w = q * d, rounded once) in the UMMA K-major 128B-swizzle
-//    layout, fence.proxy.async, then an mbarrier arrival.
+//    layout, fence.proxy.async, then an mbarrier arrival.  Float32 weights
+//    (32 KB): two fp16 tiles already in that layout, hi = fp16(w) and
+//    lo = fp16(w - hi), copied straight into the A buffers; both are
+//    multiplied with the same activations into one accumulator, so a weight
+//    enters the sum to about 2^-22 of its value instead of fp16's 2^-11.
 //  - B operand (activations, fp16 [T][K]): one TMA tiled load per stage
 //    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast); warp 8 lane 0
 //    issues both copies of a stage.
 //  - MMA: one thread issues tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 ->
-//    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage) and tcgen05.commit frees the
-//    stage; the accumulator (BN TMEM columns) is read back by warps 8-11 with
+//    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage, twice for hi/lo float32
+//    weights) and tcgen05.commit frees the stage; the accumulator (BN TMEM columns) is read back by warps 8-11 with
 //    tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31 = its weight rows).
 //  - every mbarrier wait is bounded; a timeout sets the error word.
 #pragma once
@@ -38,19 +42,26 @@ constexpr int G_THREADS = 384;   // warps 0-7 dequantise, 8 loads, 9 issues MMAs
 constexpr int G_DQ = 256;        // dequantising threads: 2 per weight row
 constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
 
-// one tile-packed chunk: 128 rows x 64 k.  The values are grouped by 8 k:
-// [8 groups][128 rows][8 values] (so that thread r reads group c of its row
-// at a conflict-free address), then for Q8_0 the scales [128 rows][2 fp16]
-// of the two 32-blocks.  Float32 weights are kept as fp16 here (the value
-// the tensor core multiplies, rounded once when the copy is made).
+// one tile-packed chunk: 128 rows x 64 k.  Q8_0: the values grouped by 8
+// k, [8 groups][128 rows][8 values] (so that thread r reads group c of its
+// row at a conflict-free address), then the scales [128 rows][2 fp16] of the
+// two 32-blocks.  Float32: the hi tile then the lo tile, each the 16 KB
+// image of the UMMA K-major 128B-swizzle layout (row r, group c of 8 k at
+// byte (r / 8) * 1024 + (r % 8) * 128 + ((c ^ (r % 8)) * 16)).
 __host__ __device__ constexpr int g_chunk_bytes(int wdt) {
-    return wdt == WDT_Q8 ? G_BM * G_BK + G_BM * 4 : G_BM * G_BK * 2;
+    return wdt == WDT_Q8 ? G_BM * G_BK + G_BM * 4 : 2 * G_A_BYTES;
 }
+// the staging area of a Q8_0 chunk before dequantisation (float32 chunks
+// land in the A tiles directly)
+__host__ __device__ constexpr int g_raw_bytes(int wdt) { return wdt == WDT_Q8 ? g_chunk_bytes(wdt) : 0; }
+// A tiles per stage: one (Q8_0) or hi + lo (float32)
+__host__ __device__ constexpr int g_a_tiles(int wdt) { return wdt == WDT_Q8 ? 1 : 2; }
 // pipeline depth from the shared-memory budget (at most 6 stages)
+__host__ __device__ constexpr int g_stage_bytes(int wdt, int bn) {
+    return g_raw_bytes(wdt) + g_a_tiles(wdt) * G_A_BYTES + bn * 128;
+}
 __host__ __device__ constexpr int g_stages(int wdt, int bn) {
-    return (220 * 1024) / (g_chunk_bytes(wdt) + G_A_BYTES + bn * 128) < 6
-               ? (220 * 1024) / (g_chunk_bytes(wdt) + G_A_BYTES + bn * 128)
-               : 6;
+    return (220 * 1024) / g_stage_bytes(wdt, bn) < 6 ? (220 * 1024) / g_stage_bytes(wdt, bn) : 6;
 }
 
 struct GemmArgs {
@@ -70,11 +81,11 @@ struct GemmArgs {
 template <int WDT, int BN>
 struct __align__(1024) GemmSmem {
     static constexpr int S = g_stages(WDT, BN);
-    uint8_t a[S][G_A_BYTES];          // 1024-aligned: swizzle atoms
+    uint8_t a[S][g_a_tiles(WDT)][G_A_BYTES];  // 1024-aligned: swizzle atoms
     uint8_t b[S][BN * 128];
-    uint8_t raw[S][g_chunk_bytes(WDT)];  // the packed weights of a stage
-    uint64_t full_raw[S];             // bulk copy tx bytes
-    uint64_t full_a[S];               // 128 dequantiser arrivals
+    uint8_t raw[S][g_raw_bytes(WDT) > 0 ? g_raw_bytes(WDT) : 16];  // a Q8_0 stage's packed weights
+    uint64_t full_raw[S];             // bulk copy tx bytes (float32: the A tiles themselves)
+    uint64_t full_a[S];               // 256 dequantiser arrivals (Q8_0)
     uint64_t full_b[S];               // TMA tx bytes
     uint64_t empty[S];                // tcgen05.commit
     uint64_t accum;                   // last MMA done
@@ -107,15 +118,22 @@ __global__ void gemm_tile_pack_kernel(const uint8_t *src, int wdt, int n_rows, i
             reinterpret_cast<uint16_t *>(chunk + G_BM * G_BK)[r * 2 + c] = d;
         }
     } else {
-        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        float w[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (n < n_rows) {
             const float *row = reinterpret_cast<const float *>(src + static_cast<size_t>(n) * K * 4);
-            lo = *reinterpret_cast<const float4 *>(row + k);
-            hi = *reinterpret_cast<const float4 *>(row + k + 4);
+            const float4 a = *reinterpret_cast<const float4 *>(row + k);
+            const float4 b = *reinterpret_cast<const float4 *>(row + k + 4);
+            w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w, w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
         }
-        __half2 h[4] = {__floats2half2_rn(lo.x, lo.y), __floats2half2_rn(lo.z, lo.w), __floats2half2_rn(hi.x, hi.y),
-                        __floats2half2_rn(hi.z, hi.w)};
-        *reinterpret_cast<uint4 *>(chunk + (c * G_BM + r) * 16) = *reinterpret_cast<uint4 *>(h);
+        __half hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            hi[j] = __float2half_rn(w[j]);
+            lo[j] = __float2half_rn(w[j] - __half2float(hi[j]));  // the difference is exact in float32
+        }
+        const int off = (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4 *>(chunk + off) = *reinterpret_cast<const uint4 *>(hi);
+        *reinterpret_cast<uint4 *>(chunk + G_A_BYTES + off) = *reinterpret_cast<const uint4 *>(lo);
     }
 }
 
@@ -211,9 +229,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     // timeout), so no bulk copy lands in shared memory of a later CTA
     int issued = 0;
 
-    if (warp < 8) {
-        // ---- dequantisers: two threads per weight row of the tile, 4 of
-        // the 8 groups of 8 k each
+    if (warp < 8 && WDT == WDT_Q8) {
+        // ---- dequantisers (Q8_0): two threads per weight row of the tile,
+        // 4 of the 8 groups of 8 k each
         const int r = tid & (G_BM - 1), c0 = (tid >> 7) * 4;
         for (int i = 0; i < kb_n; ++i) {
             const int s = i % S;
@@ -222,7 +240,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 break;
             }
             const uint8_t *raw = sm->raw[s];
-            uint8_t *dst = sm->a[s] + (r >> 3) * 1024 + (r & 7) * 128;
+            uint8_t *dst = sm->a[s][0] + (r >> 3) * 1024 + (r & 7) * 128;
             __half2 d2lo = __float2half2_rn(0.f), d2hi = d2lo;  // the two blocks' scales, broadcast
             if (WDT == WDT_Q8) {
                 const __half2 dd = *reinterpret_cast<const __half2 *>(raw + G_BM * G_BK + r * 4);
@@ -231,22 +249,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
 #pragma unroll
             for (int c = c0; c < c0 + 4; ++c) {  // 4 groups of 8 k
+                // q + 128 in the mantissa of fp16 1024 (exact), minus 1152,
+                // times d in fp16: the exact product q * d rounded once
                 __half2 h[4];
-                if (WDT == WDT_Q8) {
-                    // q + 128 in the mantissa of fp16 1024 (exact), minus 1152,
-                    // times d in fp16: the exact product q * d rounded once
-                    const uint2 q = *reinterpret_cast<const uint2 *>(raw + (c * G_BM + r) * 8);
-                    const uint32_t ux = q.x ^ 0x80808080u, uy = q.y ^ 0x80808080u;
-                    const __half2 bias = __float2half2_rn(1152.f);
-                    const __half2 d2 = c < 4 ? d2lo : d2hi;
-                    h[0] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x5140)), bias), d2);
-                    h[1] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x7362)), bias), d2);
-                    h[2] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias), d2);
-                    h[3] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias), d2);
-                } else {
-                    // fp16 already: the swizzled copy only
-                    *reinterpret_cast<uint4 *>(h) = *reinterpret_cast<const uint4 *>(raw + (c * G_BM + r) * 16);
-                }
+                const uint2 q = *reinterpret_cast<const uint2 *>(raw + (c * G_BM + r) * 8);
+                const uint32_t ux = q.x ^ 0x80808080u, uy = q.y ^ 0x80808080u;
+                const __half2 bias = __float2half2_rn(1152.f);
+                const __half2 d2 = c < 4 ? d2lo : d2hi;
+                h[0] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x5140)), bias), d2);
+                h[1] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x7362)), bias), d2);
+                h[2] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias), d2);
+                h[3] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias), d2);
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(h);
             }
             // the tensor core reads shared memory through the async proxy
@@ -262,7 +275,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             const int pre = kb_n < S ? kb_n : S;
             for (int i = 0; i < pre; ++i) {
                 mbar_arrive_tx(&sm->full_raw[i], CHUNK);
-                bulk_g2s(sm->raw[i], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[i]);
+                bulk_g2s(WDT == WDT_Q8 ? sm->raw[i] : sm->a[i][0], wt + static_cast<size_t>(i) * CHUNK, CHUNK,
+                         &sm->full_raw[i]);
             }
             pdl_wait();
             for (int i = 0; i < kb_n; ++i) {
@@ -273,7 +287,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                         break;
                     }
                     mbar_arrive_tx(&sm->full_raw[s], CHUNK);
-                    bulk_g2s(sm->raw[s], wt + static_cast<size_t>(i) * CHUNK, CHUNK, &sm->full_raw[s]);
+                    bulk_g2s(WDT == WDT_Q8 ? sm->raw[s] : sm->a[s][0], wt + static_cast<size_t>(i) * CHUNK, CHUNK,
+                             &sm->full_raw[s]);
                 }
                 mbar_arrive_tx(&sm->full_b[s], BN * 128);
                 tma_load_2d(sm->b[s], &xmap, (kb0 + i) * G_BK, tok0, &sm->full_b[s]);
@@ -287,15 +302,20 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             for (int i = 0; i < kb_n; ++i) {
                 const int s = i % S;
                 const uint32_t par = (i / S) & 1;
-                if (!mbar_wait(&sm->full_a[s], par, nullptr) || !mbar_wait(&sm->full_b[s], par, nullptr)) {
+                // Q8_0: the dequantisers' arrivals; float32: the copy itself
+                uint64_t *ready = WDT == WDT_Q8 ? &sm->full_a[s] : &sm->full_raw[s];
+                if (!mbar_wait(ready, par, nullptr) || !mbar_wait(&sm->full_b[s], par, nullptr)) {
                     gemm_fail(args.err);
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint64_t da = umma_desc_sw128(sm->a[s]), db = umma_desc_sw128(sm->b[s]);
+                const uint64_t da = umma_desc_sw128(sm->a[s][0]), db = umma_desc_sw128(sm->b[s]);
 #pragma unroll
-                for (int k = 0; k < G_BK / 16; ++k)  // +32 bytes (2 in 16-byte units) per K=16
+                for (int k = 0; k < G_BK / 16; ++k) {  // +32 bytes (2 in 16-byte units) per K=16
                     umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+                    if (WDT != WDT_Q8)  // the lo tile, 16 KB (1024 16-byte units) further
+                        umma_f16(tmem, da + 1024 + 2 * k, db + 2 * k, idesc, 1u);
+                }
                 umma_commit(&sm->empty[s]);
             }
             umma_commit(&sm->accum);

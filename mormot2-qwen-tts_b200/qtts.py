@@ -153,6 +153,7 @@ EXPORTS = {
     "qtts_lm_forward": [P, P, I, I, P, P],
     "qtts_lm_forward_noalloc": [P, P, I, I, P, P],
     "qtts_lm_length": [P, PI],
+    "qtts_lm_set_wait_test": [P, I, ctypes.c_int64],
     "qtts_lm_destroy": [P],
     "qtts_batch_create": [P, P, I, I, I, I, ctypes.POINTER(P)],
     "qtts_batch_reset": [P, I],
@@ -489,6 +490,12 @@ class QwenLm:
         v = ctypes.c_int()
         check(lib().qtts_lm_length(self.handle, ctypes.byref(v)))
         return v.value
+
+    def set_wait_test(self, extra_arrivals, wait_cycles):
+        """qtts_lm_set_wait_test: make the grid barriers of the next launches
+        wait for an arrival that never comes, bounded by wait_cycles
+        (failure-path tests); (0, 0) restores normal operation."""
+        check(lib().qtts_lm_set_wait_test(self.handle, extra_arrivals, wait_cycles))
 
     def free(self):
         if self.handle:

@@ -4,8 +4,9 @@ the reference's TInferBackend.Linear on a head (mormot.ai.tts.qwen.lm.pas:
 
 Expected values: numpy in float64 on the same fp16 operands the tensor cores
 see (x rounded to fp16; Q8_0 weights dequantised as q*d in float32 and
-rounded to fp16; f32 weights rounded to fp16).  Only the f32 accumulation
-order differs, hence the tight tolerance.
+rounded to fp16; f32 weights as the two fp16 tiles hi = fp16(w) and
+lo = fp16(w - hi), both multiplied with x).  Only the f32 accumulation order
+differs, hence the tight tolerance.
 """
 import numpy as np
 import pytest
@@ -19,7 +20,9 @@ pytestmark = pytest.mark.gpu
 
 def fp16_weights(w, dtype):
     if dtype == "f32":
-        return w.astype(np.float16).astype(np.float64)
+        hi = w.astype(np.float16)
+        lo = (w - hi.astype(np.float32)).astype(np.float16)
+        return hi.astype(np.float64) + lo.astype(np.float64)
     q = O.quantize_q8_0(w).reshape(-1, 34)
     d = q[:, :2].copy().view(np.float16).astype(np.float32)        # [blocks, 1]
     qs = q[:, 2:].view(np.int8).astype(np.float32)                  # [blocks, 32]
