@@ -452,6 +452,63 @@ def prefill_measure(args, qtts, torch, m, dev, rank):
             "timing": "host wall clock around qtts_batch_forward (rows from pinned host memory, logits back)"}
 
 
+# the phases of the frame kernel as its trace marks them (qtts_decode.cuh
+# Compute::mark): (from tag, to tag) -> phase; 100 + b / 200 + b = arrival at /
+# departure from barrier b
+TRACE_PHASES = {
+    (10, 11): "QKV GEMV (P1)", (201, 21): "attention, split context (P2)", (207, 21): "attention, whole context (P2)",
+    (202, 30): "combine of the splits (P3)", (30, 31): "O GEMV + residual (P3)", (21, 31): "O GEMV by kv head",
+    (203, 40): "RMSNorm staging (P4)", (40, 41): "gate/up GEMV + SwiGLU (P4)", (204, 50): "staging (P5)",
+    (50, 51): "down GEMV + residual (P5)", (205, 10): "RMSNorm staging (P1)", (60, 61): "head GEMV + argmax keys",
+    (206, 10): "argmax + next input (P1 staging)", (11, 101): "K/V prefetch", (11, 107): "K/V prefetch",
+}
+# Q8_0 bytes a GEMV phase streams (row-packed, 34 B per 32 weights)
+TRACE_BYTES = {"QKV GEMV (P1)": 4096 * 1088, "O GEMV + residual (P3)": 1024 * 2176, "O GEMV by kv head": 8192 * 272,
+               "gate/up GEMV + SwiGLU (P4)": 6144 * 1088, "down GEMV + residual (P5)": 1024 * 3264}
+
+
+def trace_measure(qtts, tk):
+    """The phase trace of one configs[1] frame (qtts_talker_trace_frame:
+    CTA 0's timestamps at each phase boundary), the fastest of 5 traced
+    frames after 20 untraced ones: mean time of each phase over the
+    predictor's 75 layer steps and the talker's 28 layers, barriers apart,
+    and each GEMV phase's weight bytes over its time (GB/s; the talker's
+    weights stream from HBM, the predictor's are L2 hits)."""
+    codes = np.zeros(16, np.int32)
+    for _ in range(20):
+        tk.next_frame(codes)
+    best = None
+    for _ in range(5):
+        _, st = tk.trace_frame(codes)
+        if best is None or st[-1][1] - st[0][1] < best[-1][1] - best[0][1]:
+            best = st
+    st = best
+    heads = [i for i, (t, _) in enumerate(st) if t == 61]
+    split = heads[14]  # the 15th predictor head ends the predictor part
+    out = {"frame_us": (st[-1][1] - st[0][1]) / 1000.0}
+    peaks = measured_peaks()
+    peak = peaks["hbm_gbs"] if peaks else 6650.0
+    for name, lo, hi in (("predictor", 0, split + 1), ("talker", split, len(st))):
+        agg, bars = {}, {}
+        for i in range(lo + 1, hi):
+            a, b = st[i - 1][0], st[i][0]
+            d = st[i][1] - st[i - 1][1]
+            if 100 < a < 200 and b == a + 100:
+                bars.setdefault(f"barrier {a - 100}", []).append(d)
+            elif (a, b) in TRACE_PHASES:
+                agg.setdefault(TRACE_PHASES[(a, b)], []).append(d)
+        part = {"us": (st[hi - 1][1] - st[lo][1]) / 1000.0, "phases_us": {}, "barriers_us": {}, "gemv_gbs": {}}
+        for k, v in agg.items():
+            part["phases_us"][k] = round(float(np.mean(v)) / 1000.0, 3)
+            if k in TRACE_BYTES:
+                gbs = TRACE_BYTES[k] / float(np.mean(v))
+                part["gemv_gbs"][k] = {"gb_s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4)}
+        for k, v in bars.items():
+            part["barriers_us"][k] = {"mean": round(float(np.mean(v)) / 1000.0, 3), "count": len(v)}
+        out[name] = part
+    return out
+
+
 def start_prompt_measure(qtts, tk, dev, cpu_leg):
     """TQwenTalker.Start (talker.pas:471-592) from token ids on the device
     (qtts_talker_start_prompt: 32 text tokens, streaming, a voice; the text
@@ -693,6 +750,14 @@ def gpu_arm(args, rank, world, local_rank):
                 restarts += 1
         return restarts
 
+    if args.trace_frame:
+        # the phase trace alone (profiling runs)
+        tk.start(prompt, None, m["pad"])
+        print(json.dumps({"impl": "ours", "trace": trace_measure(qtts, tk)}), flush=True)
+        for o in (tk, tlm, plm, th, ph):
+            o.free()
+        dev.close()
+        return
     # warm-up
     tk.start(prompt, None, m["pad"])
     run_frames(W)
@@ -835,6 +900,9 @@ def main():
     # configs[3] beside the bench line: batched prefill steps (0: off)
     ap.add_argument("--prefill-steps", type=int, default=2)
     ap.add_argument("--only-prefill", action="store_true", help="run the configs[3] measurement alone")
+    ap.add_argument("--trace-frame", action="store_true",
+                    help="print the phase trace of one configs[1] frame alone (no batched/prefill legs: --batch 0 "
+                         "--prefill-steps 0)")
     # smaller stacks for profiler captures only (the benchmark is 28 + 5)
     ap.add_argument("--talker-layers", type=int, default=28)
     ap.add_argument("--pred-layers", type=int, default=5)

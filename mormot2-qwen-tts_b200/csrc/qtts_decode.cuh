@@ -337,6 +337,7 @@ struct __align__(128) Smem {
     float part[MAX_PARTS * RMAX];     // GEMV partial sums of the slice
     int slice[M_FIXED][2];            // rows [r0, r1) of each fixed matrix owned by this CTA
     float red[NWARPS * RMAX];
+    float inv[RMAX];                  // 1/rms of the staged rows, for the GEMV epilogue
     unsigned long long keys[NWARPS];
     uint64_t full[NSTAGES];
     uint64_t empty[NSTAGES];
@@ -744,6 +745,9 @@ struct Compute {
         const int pairs_full = (sr + 1) >> 1;  // pairs of a full chunk
         int it = warp;                         // next item of this warp
         bool good = ok;
+        // the staged rows' 1/rms, once (the barrier before the epilogue
+        // publishes it): the last warp has the fewest items
+        if (eps >= 0.f && warp == NCW - 1 && lane < R) sm->inv[lane] = norm_inv(lane, eps);
         for (int ch = 0; ch < nchunks; ++ch) {
             const int slot = (seq + ch) % NSTAGES;
             const uint32_t par = ((seq + ch) / NSTAGES) & 1;
@@ -837,7 +841,7 @@ struct Compute {
                     v += sm->part[((2 * p + 1) * SEG + sg) * RMAX + r];
                 }
                 if (eps >= 0.f) {
-                    const float inv = norm_inv(r, eps);
+                    const float inv = sm->inv[r];
                     g *= inv;
                     v *= inv;
                 }
@@ -850,7 +854,7 @@ struct Compute {
                 float y = 0.f;
 #pragma unroll
                 for (int sg = 0; sg < SEG; ++sg) y += sm->part[(row * SEG + sg) * RMAX + r];
-                if (eps >= 0.f) y *= norm_inv(r, eps);
+                if (eps >= 0.f) y *= sm->inv[r];
                 const int orow = r0 + row;
                 if (kind == E_STORE) {
                     out[r * ld + orow] = y;
@@ -1002,23 +1006,26 @@ struct Compute {
             const int r = vec >> 2, t = vec & 3;  // t: 0,1 = q heads, 2 = k, 3 = v
             // QKV rows by kv head: q(2h), q(2h+1), k(h), v(h)
             const float *src = job->s.qkv + r * QKV_ROWS + h * QKV_HEAD + t * HD;
+            // the norm weights and the RoPE row do not depend on the rows:
+            // their loads go out together with the row's
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), cs = g, sn = g;
+            if (t < 3) {
+                const float *nw = t < 2 ? Ly.q_norm : Ly.k_norm;
+                const int e0 = (4 * lane) & (half - 1);
+                const size_t ro = static_cast<size_t>(L0 + r) * half + e0;
+                g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
+                cs = *reinterpret_cast<const float4 *>(job->rope_cos + ro);
+                sn = *reinterpret_cast<const float4 *>(job->rope_sin + ro);
+            }
             const float4 x = ldcg4(src + 4 * lane);
             float y[4] = {x.x, x.y, x.z, x.w};
             if (t < 3) {
-                const float *nw = t < 2 ? Ly.q_norm : Ly.k_norm;
                 const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
                 const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
-                const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
                 y[0] = g.x * (y[0] * inv);
                 y[1] = g.y * (y[1] * inv);
                 y[2] = g.z * (y[2] * inv);
                 y[3] = g.w * (y[3] * inv);
-                const int pos = L0 + r;
-                const int e0 = (4 * lane) & (half - 1);
-                const float4 cs =
-                    *reinterpret_cast<const float4 *>(job->rope_cos + static_cast<size_t>(pos) * half + e0);
-                const float4 sn =
-                    *reinterpret_cast<const float4 *>(job->rope_sin + static_cast<size_t>(pos) * half + e0);
                 const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
                 float o[4];
 #pragma unroll
@@ -1108,22 +1115,27 @@ struct Compute {
         if (warp < nc) {
             const int r = warp >> 1, qq = warp & 1;
             const float *w0 = wst + (warp * npw) * PSTRIDE;
-            float M = -INFINITY;
-            for (int j = 0; j < npw; ++j) M = fmaxf(M, w0[j * PSTRIDE + HD]);
-            float L = 0.f;
+            // lane j brings warp j's (max, sum); the weights e^(m_j - M) are
+            // computed in parallel and broadcast to the dims loop
+            float mj = -INFINITY, lj = 0.f;
+            if (lane < npw) {
+                mj = w0[lane * PSTRIDE + HD];
+                lj = w0[lane * PSTRIDE + HD + 1];
+            }
+            float M = mj;
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+            const float ej = (mj == -INFINITY || M == -INFINITY) ? 0.f : expf(mj - M);
+            const float L = warp_sum(lj * ej);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (M != -INFINITY) {
-                for (int j = 0; j < npw; ++j) {
-                    const float *wj = w0 + j * PSTRIDE;
-                    const float mj = wj[HD];
-                    const float e = mj == -INFINITY ? 0.f : expf(mj - M);
-                    L = fmaf(wj[HD + 1], e, L);
-                    const float4 v = *reinterpret_cast<const float4 *>(wj + 4 * lane);
-                    acc.x = fmaf(v.x, e, acc.x);
-                    acc.y = fmaf(v.y, e, acc.y);
-                    acc.z = fmaf(v.z, e, acc.z);
-                    acc.w = fmaf(v.w, e, acc.w);
-                }
+#pragma unroll 4
+            for (int j = 0; j < npw; ++j) {
+                const float e = __shfl_sync(0xffffffffu, ej, j);
+                const float4 v = *reinterpret_cast<const float4 *>(w0 + j * PSTRIDE + 4 * lane);
+                acc.x = fmaf(v.x, e, acc.x);
+                acc.y = fmaf(v.y, e, acc.y);
+                acc.z = fmaf(v.z, e, acc.z);
+                acc.w = fmaf(v.w, e, acc.w);
             }
             if (head_path) {
                 const float inv = 1.0f / L;
