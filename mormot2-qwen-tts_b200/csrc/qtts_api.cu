@@ -82,6 +82,27 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// the same with thread-block clusters of cluster_z CTAs along z (> 1)
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                      unsigned cluster_z, Args &&...args) {
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = cluster_z;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ------------------------------------------------------------------ handles
 
 struct qtts_device {
@@ -478,31 +499,37 @@ static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 
     CUtensorMap map;
     int rc = tensor_map_f16(&map, x, a.K, rows_cap, BN);
     if (rc) return rc;
-    CK(launch_pdl(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, a, map));
+    if (grid.z > 1)
+        CK(launch_pdl_cluster(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, grid.z, a, map));
+    else
+        CK(launch_pdl(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, a, map));
     return QTTS_OK;
 }
 
 // y[t][n] (+)= x[t][:] . w[n][:] for t < T (w tile-packed; x: fp16 [rows_cap][K] on the
 // device, rows_cap >= T).  With `add`, the products are added to y (residual);
-// otherwise y is overwritten (zeroed first when the K split needs atomics).
+// otherwise y is overwritten.
 static int gemm_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
 
-// the K split of a GEMM: CTAs up to about one per SM
+// the K split of a GEMM: CTAs up to about one per SM, at most 8 per tile
+// (a portable cluster; clusters of 16 measured slower: 9.38 vs 7.79 ms per
+// B=64 frame)
 static int gemm_split(int n_rows, int k, int T) {
+    const int cap = 8;
     const int bn = gemm_bn(T);
     const int tiles = ((n_rows + G_BM - 1) / G_BM) * ((T + bn - 1) / bn);
     const int kb = k / G_BK;
     int split = 1;
-    while (split * 2 <= kb && kb % (split * 2) == 0 && tiles * split * 2 <= 160) split *= 2;
+    while (split * 2 <= cap && split * 2 <= kb && kb % (split * 2) == 0 && tiles * split * 2 <= 160) split *= 2;
     return split;
 }
 
-// y[t][n] (+)= ... with `zeroed`: y already holds zeros where a split-K
-// GEMM needs them (cleared by the kernel before it).  With swiglu16 (gate/up
-// pairs in consecutive rows), no K split and the epilogue writes
+// y[t][n] (+)= ...  A K split sums its partials in a fixed order inside a
+// cluster (no atomics, no cleared output).  With swiglu16 (gate/up pairs in
+// consecutive rows), no K split and the epilogue writes
 // fp16(silu(gate) * up) to swiglu16[t][n / 2] (row stride ld) instead of y.
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
-                bool add, int *err, cudaStream_t st, bool zeroed = false, __half *swiglu16 = nullptr) {
+                bool add, int *err, cudaStream_t st, __half *swiglu16 = nullptr) {
     if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
     const int bn = gemm_bn(T);
     const int split = swiglu16 ? 1 : gemm_split(n_rows, k, T);
@@ -513,17 +540,11 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.T = T;
     a.out = y;
     a.ld = ld;
-    a.atomic = (add || split > 1) ? 1 : 0;
+    a.atomic = add ? 1 : 0;
     a.ksplit = split;
     a.err = err;
     a.swiglu16 = swiglu16;
     a.ld16 = swiglu16 ? ld : 0;
-    if (!add && split > 1 && !zeroed) {
-        if (ld == n_rows)
-            CK(cudaMemsetAsync(y, 0, static_cast<size_t>(T) * ld * 4, st));
-        else
-            for (int t = 0; t < T; ++t) CK(cudaMemsetAsync(y + static_cast<size_t>(t) * ld, 0, n_rows * 4, st));
-    }
     dim3 grid((n_rows + G_BM - 1) / G_BM, (T + bn - 1) / bn, split);
     if (wdt == WDT_Q8) {
         if (bn == 64) return gemm_launch_t<WDT_Q8, 64>(a, x, rows_cap, grid, st);
@@ -2429,13 +2450,8 @@ extern "C" int qtts_batch_length(qtts_batch *b, int seq, int *length) {
     return QTTS_OK;
 }
 
-// blocks of rmsnorm_f16_kernel: 8 rows each, and enough threads to clear
-// nzero4 float4s of the next GEMM's output in a few passes
-static unsigned norm_grid(int rows, long long nzero4) {
-    long long g = (rows + 7) / 8;
-    const long long gz = std::min<long long>((nzero4 + 1023) / 1024, 2 * 148);
-    return static_cast<unsigned>(std::max(g, gz));
-}
+// blocks of rmsnorm_f16_kernel: 8 rows (warps) each
+static unsigned norm_grid(int rows) { return static_cast<unsigned>((rows + 7) / 8); }
 
 template <class KVT>
 static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pitems, int nditems,
@@ -2452,15 +2468,13 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
     const int cap = b->max_tokens;
     for (int l = 0; l < s->cfg.layers && rc == QTTS_OK; ++l) {
         const DLayer &Ly = s->tlayers[l];
-        // the split-K outputs (qkv, gu) are cleared by the norm before them
-        const long long zq = gemm_split(QKV_ROWS, H, T) > 1 ? static_cast<long long>(T) * QKV_ROWS / 4 : 0;
-        cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, zq)), dim3(256), 0, st, b->x, nullptr, T,
-                                   Ly.in_norm, eps, b->h16, nullptr, b->qkv, zq);
+        cudaError_t e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T)), dim3(256), 0, st, b->x, nullptr, T,
+                                   Ly.in_norm, eps, b->h16, static_cast<float *>(nullptr));
         if (e != cudaSuccess) {
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
             return;
         }
-        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st, true))) return;
+        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st))) return;
         e = launch_pdl(qkv_post_kernel<KVT>, dim3(T, 4), dim3(256), 0, st, b->qkv, tok_seq, tok_pos, Ly.q_norm,
                        Ly.k_norm, eps, b->rope_cos, b->rope_sin, b->q32, pool, l);
         if (e == cudaSuccess && npitems > 0)
@@ -2479,14 +2493,13 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
             return;
         }
         if ((rc = gemm(Ly.wo, wdt, H, QDIM, b->attn16, T, cap, b->x, H, true, b->err, st))) return;
-        e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T, 0)), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm,
-                       eps, b->h16, nullptr, nullptr, 0ll);  // gate/up: no K split, SwiGLU in its epilogue
+        e = launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(T)), dim3(256), 0, st, b->x, nullptr, T, Ly.post_norm,
+                       eps, b->h16, static_cast<float *>(nullptr));
         if (e != cudaSuccess) {
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
             return;
         }
-        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, nullptr, INTER, false, b->err, st, true,
-                       b->act16)))
+        if ((rc = gemm(Ly.wgu, wdt, GU_ROWS, H, b->h16, T, cap, nullptr, INTER, false, b->err, st, b->act16)))
             return;
         if ((rc = gemm(Ly.wd, wdt, H, INTER, b->act16, T, cap, b->x, H, true, b->err, st))) return;
     }
@@ -2674,14 +2687,12 @@ static int batch_enqueue(qtts_batch *b, const BatchPlan &P, const float *x, bool
                                     m + P.o_cf, m + P.o_cc, m + P.o_ct, wdt, st, rc);
     if (rc) return rc;
     const int hr = head >= 0 ? b->heads->mats[head].rows : 0;
-    const long long zl = head >= 0 && gemm_split(hr, H, P.nseq) > 1 ? static_cast<long long>(P.nseq) * hr / 4 : 0;
-    CK(launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(P.nseq, zl)), dim3(256), 0, st, static_cast<const float *>(b->x),
+    CK(launch_pdl(rmsnorm_f16_kernel, dim3(norm_grid(P.nseq)), dim3(256), 0, st, static_cast<const float *>(b->x),
                   m + P.o_last, P.nseq, static_cast<const float *>(b->stack->d_final_norm), b->stack->cfg.rms_eps,
-                  b->hlast16, b->hidden, b->logits, zl));
+                  b->hlast16, b->hidden));
     if (head >= 0) {
         const HeadMat &hm = b->heads->mats[head];
-        if ((rc = gemm(hm.t, wdt, hm.rows, H, b->hlast16, P.nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st,
-                       true)))
+        if ((rc = gemm(hm.t, wdt, hm.rows, H, b->hlast16, P.nseq, b->max_seqs, b->logits, hm.rows, false, b->err, st)))
             return rc;
     }
     return QTTS_OK;

@@ -52,15 +52,11 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *s) {
 }
 
 // One warp per row: out16[o] = fp16(rmsnorm(x[idx[o]]) * w); optionally the
-// float32 normed row too (the normed state returned as `hidden`).  The grid
-// also zeroes zero[0..nzero4*4) (the output of the next split-K GEMM).
+// float32 normed row too (the normed state returned as `hidden`).
 __global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, const float *w, float eps, __half *out16,
-                                   float *out32, float *zero, long long nzero4) {
+                                   float *out32) {
     pdl_trigger();
     pdl_wait();
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < nzero4;
-         i += static_cast<long long>(gridDim.x) * blockDim.x)
-        reinterpret_cast<float4 *>(zero)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (o >= rows) return;
     const float *r = x + static_cast<size_t>(idx ? idx[o] : o) * H;

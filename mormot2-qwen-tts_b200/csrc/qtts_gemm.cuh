@@ -6,8 +6,12 @@
 //
 //  - CTA tile: 128 weight rows (MMA M) x BN tokens (MMA N = 64, 128 or 256),
 //    K in blocks of 64 (one 128-byte swizzle row of fp16), an optional K
-//    split over blockIdx.z whose partial sums are added with f32 atomics
-//    (which also gives the residual add for free).
+//    split over blockIdx.z (2 to 8 ways).  The CTAs of one tile's split form
+//    a thread-block cluster: each leaves its partial tile in its shared
+//    memory, and after a cluster barrier CTA z sums rows [z/ks, (z+1)/ks) of
+//    the tile over the cluster's partials in split order (distributed shared
+//    memory) and stores them, or adds them to the residual: the sums come in
+//    a fixed order, so the results do not vary from run to run.
 //  - A operand (weights): the matrix is kept a second time in a tile-packed
 //    layout (gemm_tile_pack_kernel): the 128 rows x 64 k of one stage are one
 //    contiguous chunk, so one bulk copy (cp.async.bulk) brings a stage's
@@ -28,6 +32,7 @@
 //    tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31 = its weight rows).
 //  - every mbarrier wait is bounded; a timeout sets the error word.
 #pragma once
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -70,8 +75,8 @@ struct GemmArgs {
     int T;             // tokens
     float *out;        // out[t * ld + n]
     int ld;
-    int atomic;        // add into out (split-K and/or residual) instead of storing
-    int ksplit;        // K blocks per split = (K / G_BK) / ksplit
+    int atomic;        // add into out (the residual) instead of storing
+    int ksplit;        // K splits (a cluster of ksplit CTAs per tile); K blocks per split = (K / G_BK) / ksplit
     int *err;          // error word (QTTS_E_TIMEOUT on a wait that gave up)
     __half *swiglu16;  // non-NULL (no K split): rows are gate/up pairs (2j, 2j+1) and the
                        // epilogue writes fp16(silu(gate) * up) to swiglu16[t * ld16 + j]
@@ -81,6 +86,7 @@ struct GemmArgs {
 template <int WDT, int BN>
 struct __align__(1024) GemmSmem {
     static constexpr int S = g_stages(WDT, BN);
+    // the split-K partial tile [BN][128] f32 reuses the stage buffers
     uint8_t a[S][g_a_tiles(WDT)][G_A_BYTES];  // 1024-aligned: swizzle atoms
     uint8_t b[S][BN * 128];
     uint8_t raw[S][g_raw_bytes(WDT) > 0 ? g_raw_bytes(WDT) : 16];  // a Q8_0 stage's packed weights
@@ -90,6 +96,8 @@ struct __align__(1024) GemmSmem {
     uint64_t empty[S];                // tcgen05.commit
     uint64_t accum;                   // last MMA done
     uint32_t tmem_base;
+    static_assert(S * (g_a_tiles(WDT) * G_A_BYTES + BN * 128) >= G_BM * BN * 4,
+                  "the split-K partial tile must fit in the stage buffers");
 };
 
 // row-packed matrix (Q8_0: [K int8][K/32 fp16] per row; f32 rows) -> the
@@ -349,6 +357,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 }
                 continue;
             }
+            if (args.ksplit > 1) {
+                // the partial tile, [BN tokens][128 rows], over the stage
+                // buffers (every copy has landed and every MMA read them)
+                float *part = reinterpret_cast<float *>(sm);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 32; ++j) part[(c + j) * G_BM + 32 * q + lane] = v[j];
+                continue;
+            }
             if (good && n < args.n_rows) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -363,6 +380,30 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 }
             }
         }
+    }
+    if (args.ksplit > 1) {
+        // fixed-order split-K: the cluster's partials meet, CTA z sums its
+        // rows of the tile over ranks 0..ks-1 in order; a second barrier
+        // keeps every CTA's shared memory alive until the others have read it
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        pdl_wait();  // out may be written by the previous kernels
+        const int ks = args.ksplit, z = static_cast<int>(cl.block_rank());
+        const int rows_z = G_BM / ks, rz0 = z * rows_z;
+        const float *part = reinterpret_cast<const float *>(sm);
+        for (int idx = tid; idx < rows_z * BN; idx += G_THREADS) {
+            const int rr = rz0 + idx % rows_z, col = idx / rows_z;
+            float sum = 0.f;
+            for (int r = 0; r < ks; ++r)
+                sum += *cl.map_shared_rank(part + col * G_BM + rr, static_cast<unsigned>(r));
+            const int n = row0 + rr, t = tok0 + col;
+            if (n < args.n_rows && t < args.T) {
+                float *o = args.out + static_cast<size_t>(t) * args.ld + n;
+                *o = args.atomic ? *o + sum : sum;
+            }
+        }
+        cl.sync();
     }
     if (warp == 8 && lane == 0) {
         // drain: wait (bounded) for the copies of the last S issued stages

@@ -41,7 +41,7 @@ def test_batched_decode_matches_oracle(device, kv):
     oras = [O.OraLm(ost, oh, 400) for _ in range(nseq)]
     prompts = [synth.prompt(200 + i, int(c)) for i, c in enumerate(ctx)]
     lg, hd = b.forward(np.arange(nseq), ctx, np.concatenate(prompts))
-    atol, cmin = (2e-2, 0.9999) if kv == "f32" else (5e-2, 0.999)
+    atol, cmin = 2e-2, 0.9999  # the north-star Q8_0 tolerance, bf16 pages included
     lo = np.zeros(3072, np.float32)
     ho = np.zeros(1024, np.float32)
     for i in range(nseq):
@@ -122,7 +122,7 @@ def test_prefill_after_context_tensor_cores(device, kv):
     p2 = [synth.prompt(600 + i, n) for i, n in enumerate(second)]
     b.forward([0, 1, 2], first, np.concatenate(p1))
     lg, hd = b.forward([2, 0, 1], [second[2], second[0], second[1]], np.concatenate([p2[2], p2[0], p2[1]]))
-    atol, cmin = (2e-2, 0.9999) if kv == "f32" else (5e-2, 0.999)
+    atol, cmin = 2e-2, 0.9999  # the north-star Q8_0 tolerance, bf16 pages included
     lo = np.zeros(3072, np.float32)
     for i, s in enumerate([2, 0, 1]):
         o = O.OraLm(ost, oh, 800)

@@ -7,8 +7,8 @@ GEMM, f32 accumulation), so a greedy choice may differ from the oracle's on a
 near-tie.  Each frame is therefore replayed in the oracle driven by the
 device's codes (ora_talker_check_frame), and every choice must be a maximum
 of the oracle's values to within twice the logit tolerance of the batched
-forward (2e-2 abs with Q8_0 weights and f32 KV, 5e-2 with bf16 KV, 2e-3 with
-f32 weights and f32 KV).  Shapes follow BASELINE.json configs[2] at reduced
+forward (2e-2 abs with Q8_0 weights, f32 or bf16 KV -- the north-star Q8_0
+tolerance; 2e-3 with f32 weights and f32 KV).  Shapes follow BASELINE.json configs[2] at reduced
 size: ragged prompts, utterances started at different times, subsets of
 utterances per frame.
 """
@@ -21,7 +21,7 @@ import synth
 
 pytestmark = pytest.mark.gpu
 
-GAP = {("q8_0", "f32"): 4e-2, ("q8_0", "bf16"): 1e-1, ("f32", "f32"): 4e-3}
+GAP = {("q8_0", "f32"): 4e-2, ("q8_0", "bf16"): 4e-2, ("f32", "f32"): 4e-3}
 
 
 class Rig:
@@ -127,8 +127,10 @@ def test_batched_frames_match_oracle(device, dtype, kv):
     frames = {0: 4, 1: 5, 2: 4, 3: 5, 4: 2, 5: 3}
     for s in range(6):
         assert rig.tb.length(s) == lens[s] + frames[s]
-    # nearly all choices are the oracle's own first maximum
-    assert stats[0] >= 0.9 * stats[1], stats
+    # nearly all choices are the oracle's own first maximum (measured: 367,
+    # 368 and 367 of 368 for the three cases)
+    print({"batched_frames": [dtype, kv], "first_maxima": stats[0], "choices": stats[1]})
+    assert stats[0] >= 0.98 * stats[1], stats
     rig.free()
 
 
@@ -171,11 +173,9 @@ def test_batched_sampled_frames(device):
     # top_k 50): every drawn code is one of the top-k of the oracle's values
     # for that choice (the oracle replays each frame driven by the device's
     # codes; fp16 activations may move a value near the k-th by a few
-    # places), and another seed gives other codes.  Two runs with the same
-    # seed are not compared: the split-K projections add their partial sums
-    # with float atomics, whose order varies, and the fp16 activations carry
-    # that last-bit variation into the logits (about 1e-4), enough to move an
-    # inverse-CDF draw though not a greedy choice.
+    # places), another seed gives other codes, and the same seed gives the
+    # same codes: the split-K projections sum their partials in a fixed
+    # order, so a batched run repeats itself bit for bit.
     def run(seed, check):
         rig = Rig(device, 91, 2, 2, "q8_0", "f32", 4)
         rig.dev.set_sampling(seed=seed)
@@ -196,7 +196,9 @@ def test_batched_sampled_frames(device):
         return np.array(out), np.array(ranks)
 
     a, ranks = run(21, True)
+    b, _ = run(21, False)
     c, _ = run(22, False)
+    assert np.array_equal(a, b), "two runs with one seed differ"
     assert not np.array_equal(a[0], c[0])
     assert ranks.size > 0 and ranks.max() < 50 + 8, ranks.max()
     assert (ranks < 50).mean() >= 0.95
