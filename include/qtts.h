@@ -49,7 +49,7 @@ extern "C" {
 #define QTTS_DTYPE_F32 0
 #define QTTS_DTYPE_Q8_0 1 /* ggml block_q8_0: fp16 scale + 32 int8, 34 bytes */
 #define QTTS_DTYPE_BF16 2 /* source rows only: widened exactly to float32 */
-#define QTTS_DTYPE_F16 3  /* a safetensors F16 tensor (not a weight source) */
+#define QTTS_DTYPE_F16 3  /* a safetensors F16 tensor, or a half-float KV cache (not a weight source) */
 #define QTTS_DTYPE_OTHER -1 /* a safetensors tensor of another dtype */
 #define QTTS_MAX_DIMS 8   /* dimensions of a safetensors tensor */
 
@@ -147,6 +147,12 @@ int qtts_heads_destroy(qtts_heads *heads);
  * owned.  max_pos: KV cache capacity in positions (float32 cache, the
  * reference's default, talker.pas:188-190). */
 int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out);
+/* TQwenLm.Create with its aKvF16 argument (lm.pas:122-123, applied to the
+ * device context at lm.pas:352; TQwenTalkerOptions.KvF16, talker.pas:56):
+ * kv_dtype QTTS_DTYPE_F32 (as qtts_lm_create) or QTTS_DTYPE_F16, the K/V
+ * cache in half floats (round to nearest even; the current position is read
+ * back rounded too), half the cache memory and traffic. */
+int qtts_lm_create_kv(qtts_stack *stack, qtts_heads *heads, int max_pos, int kv_dtype, qtts_lm **out);
 /* TQwenLm.Reset (lm.pas:374-378): the next row is at position 0. */
 int qtts_lm_reset(qtts_lm *lm);
 /* TQwenLm.Forward (lm.pas:391-408): appends rows x[rows][hidden] at

@@ -162,7 +162,8 @@ struct qtts_lm {
     qtts_heads *heads;
     int max_pos;
     int len;
-    float *k, *v;          // KV cache
+    void *k, *v;           // KV cache, float32 or (kv16) half floats
+    int kv16;
     float *rope_cos, *rope_sin;
     Runner run;
     float *d_x;            // [RMAX][H] input rows
@@ -587,10 +588,14 @@ extern "C" int qtts_device_open(int ordinal, qtts_device **out) {
     if (prop.multiProcessorCount * XS_MAX < H || prop.multiProcessorCount < 128)
         return set_err(QTTS_E_ARG, "qtts_device_open: %d SMs is too few", prop.multiProcessorCount);
     size_t smem = sizeof(Smem) + 128;
-    CK(cudaFuncSetAttribute(decode_kernel<WDT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    CK(cudaFuncSetAttribute(decode_kernel<WDT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    int occ = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<WDT_Q8>, NTHREADS, smem));
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_F32, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_Q8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_F32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    CK(cudaFuncSetAttribute(decode_kernel<WDT_Q8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    int occ = 0, occ16 = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<WDT_Q8, 0>, NTHREADS, smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ16, decode_kernel<WDT_Q8, 1>, NTHREADS, smem));
+    occ = occ < occ16 ? occ : occ16;
     if (occ < 1) return set_err(QTTS_E_CUDA, "qtts_device_open: the decode kernel does not fit on an SM");
     qtts_device *d = new qtts_device();
     d->ordinal = ordinal;
@@ -1019,8 +1024,13 @@ static void runner_free(Runner &r) {
 
 static int launch(qtts_device *dev, Runner &r, const Job &job, int wdt) {
     void *args[] = {const_cast<Job *>(&job)};
-    const void *fn = wdt == WDT_F32 ? reinterpret_cast<const void *>(decode_kernel<WDT_F32>)
-                                    : reinterpret_cast<const void *>(decode_kernel<WDT_Q8>);
+    // the cache format of the launch: the lm's, or the talker's (whose
+    // predictor holds the same, qtts_talker_create)
+    const int kv16 = job.mode == 0 ? job.ctx.kv16 : job.tctx.kv16;
+    const void *fn = wdt == WDT_F32 ? (kv16 ? reinterpret_cast<const void *>(decode_kernel<WDT_F32, 1>)
+                                            : reinterpret_cast<const void *>(decode_kernel<WDT_F32, 0>))
+                                    : (kv16 ? reinterpret_cast<const void *>(decode_kernel<WDT_Q8, 1>)
+                                            : reinterpret_cast<const void *>(decode_kernel<WDT_Q8, 0>));
     CK(cudaLaunchCooperativeKernel(fn, dim3(r.grid), dim3(NTHREADS), args, dev->smem, r.stream));
     return QTTS_OK;
 }
@@ -1067,8 +1077,10 @@ static void lm_free(qtts_lm *m) {
 
 static void *noalloc_lookup(int ordinal);
 
-extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out) {
+static int lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, int kv_dtype, qtts_lm **out) {
     if (!stack || !heads || !out) return set_err(QTTS_E_ARG, "qtts_lm_create: NULL argument");
+    if (kv_dtype != QTTS_DTYPE_F32 && kv_dtype != QTTS_DTYPE_F16)
+        return set_err(QTTS_E_ARG, "qtts_lm_create: KV cache in F32 or F16");
     *out = nullptr;
     if (heads->hidden != stack->cfg.hidden)
         return set_err(QTTS_E_ARG, "qtts_lm_create: %s has a width of %d, its heads %d", heads->name.c_str(),
@@ -1084,13 +1096,15 @@ extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos,
     m->heads = heads;
     m->max_pos = max_pos;
     m->len = 0;
+    m->kv16 = kv_dtype == QTTS_DTYPE_F16 ? 1 : 0;
     m->max_head_rows = 4096;
     for (const HeadMat &hm : heads->mats) m->max_head_rows = hm.rows > m->max_head_rows ? hm.rows : m->max_head_rows;
     int rc = QTTS_OK;
     size_t kvn = static_cast<size_t>(stack->cfg.layers) * HKV * max_pos * HD;
     std::vector<float> cs, sn;
     rope_tables(max_pos, stack->cfg.rope_theta, cs, sn);
-    if (cudaMalloc(&m->k, kvn * 4) != cudaSuccess || cudaMalloc(&m->v, kvn * 4) != cudaSuccess ||
+    const size_t kvb = m->kv16 ? 2 : 4;
+    if (cudaMalloc(&m->k, kvn * kvb) != cudaSuccess || cudaMalloc(&m->v, kvn * kvb) != cudaSuccess ||
         cudaMalloc(&m->rope_cos, cs.size() * 4) != cudaSuccess || cudaMalloc(&m->rope_sin, sn.size() * 4) != cudaSuccess ||
         cudaMalloc(&m->d_x, RMAX * H * 4) != cudaSuccess ||
         cudaMallocHost(reinterpret_cast<void **>(&m->h_x), RMAX * H * 4) != cudaSuccess ||
@@ -1112,6 +1126,14 @@ extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos,
     (void)noalloc_lookup(dev->ordinal);
     *out = m;
     return QTTS_OK;
+}
+
+extern "C" int qtts_lm_create(qtts_stack *stack, qtts_heads *heads, int max_pos, qtts_lm **out) {
+    return lm_create(stack, heads, max_pos, QTTS_DTYPE_F32, out);
+}
+
+extern "C" int qtts_lm_create_kv(qtts_stack *stack, qtts_heads *heads, int max_pos, int kv_dtype, qtts_lm **out) {
+    return lm_create(stack, heads, max_pos, kv_dtype, out);
 }
 
 extern "C" int qtts_lm_set_wait_test(qtts_lm *m, int extra_arrivals, int64_t wait_cycles) {
@@ -1163,6 +1185,7 @@ static int lm_forward(qtts_lm *m, const float *x, bool x_dev, int rows, int head
     j.st = dstack(m->stack);
     j.ctx.k = m->k;
     j.ctx.v = m->v;
+    j.ctx.kv16 = m->kv16;
     j.ctx.max_pos = m->max_pos;
     j.xin = m->d_x;
     // RMAX rows per launch; the head and the normed state come from the last
@@ -1234,6 +1257,8 @@ extern "C" int qtts_talker_create(qtts_lm *talker, qtts_lm *pred, const qtts_tal
         return set_err(QTTS_E_ARG, "qtts_talker_create: talker and predictor have different weight formats");
     if (talker->stack->cfg.rope_theta != pred->stack->cfg.rope_theta)
         return set_err(QTTS_E_ARG, "qtts_talker_create: talker and predictor have different RoPE bases");
+    if (talker->kv16 != pred->kv16)
+        return set_err(QTTS_E_ARG, "qtts_talker_create: talker and predictor caches of different formats");
     if (c->groups < 2 || c->groups > MAX_GROUPS) return set_err(QTTS_E_ARG, "qtts_talker_create: %d code groups", c->groups);
     if (c->vocab <= 1024 || c->pred_vocab <= 0 || c->codec_eos < 0 || c->codec_eos >= c->vocab)
         return set_err(QTTS_E_ARG, "qtts_talker_create: unexpected vocabularies (%d, %d, eos %d)", c->vocab, c->pred_vocab,
@@ -1340,9 +1365,11 @@ static Job frame_job(qtts_talker *t) {
     j.pst = dstack(pl->stack);
     j.tctx.k = tl->k;
     j.tctx.v = tl->v;
+    j.tctx.kv16 = tl->kv16;
     j.tctx.max_pos = tl->max_pos;
     j.pctx.k = pl->k;
     j.pctx.v = pl->v;
+    j.pctx.kv16 = pl->kv16;
     j.pctx.max_pos = pl->max_pos;
     j.theads = tl->heads->mats[0].d;
     j.tvocab = t->cfg.vocab;
@@ -2268,6 +2295,7 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
     j.st = dstack(m->stack);
     j.ctx.k = m->k;
     j.ctx.v = m->v;
+    j.ctx.kv16 = m->kv16;
     j.ctx.max_pos = m->max_pos;
     for (int r0 = 0; r0 < rows; r0 += RMAX) {
         const int n = rows - r0 < RMAX ? rows - r0 : RMAX;

@@ -125,10 +125,13 @@ struct DStack {
     int keep_l2;  // stream with L2 evict_last (weights that fit in L2)
 };
 
-struct DCtx {      // KV cache [layers][HKV][max_pos][HD], float32
-    float *k, *v;
+struct DCtx {      // KV cache [layers][HKV][max_pos][HD], float32 or (kv16) fp16
+    void *k, *v;
     int max_pos;
+    int kv16;      // the cache holds half floats (TQwenLm's aKvF16)
 };
+// bytes of one cached K or V element
+__host__ __device__ inline int kv_bytes(const DCtx &c) { return c.kv16 ? 2 : 4; }
 
 // scratch of one runner (one lm or one talker), all in global memory
 struct Scratch {
@@ -313,6 +316,13 @@ __device__ __forceinline__ int key_index(unsigned long long k) {
 // loads through L2 (data written by other CTAs in this launch: this SM's L1
 // may hold an older copy)
 __device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+// 4 halves (8-byte aligned, shared memory) -> float4
+__device__ __forceinline__ float4 h4_to_f4(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
 
 // programmatic dependent launch: a kernel launched with programmatic stream
 // serialisation may start while its predecessor runs; pdl_wait() returns
@@ -453,7 +463,9 @@ __device__ __noinline__ int frame_draw(const float *lg, int V, SampleParams p, f
     return sample_draw<NCT>([&](int i) { return __ldcg(lg + i); }, V, p, u, ss, tid);
 }
 
-template <int WDT>
+// KV16: the K/V cache holds half floats (a compile-time choice: a runtime
+// flag in the attention loop slowed the float32 frame by ~15 %)
+template <int WDT, int KV16>
 struct Compute {
     Smem *sm;
     const Job *job;
@@ -958,12 +970,15 @@ struct Compute {
             if (ok && have) {
                 const int n = min(min(p1, L0), p0 + ATT_TILE) - p0;
                 if (n > 0) {
-                    const size_t off = ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + p0) * HD;
+                    constexpr int es = KV16 ? 2 : 4;
+                    const size_t off = ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + p0) * HD * es;
                     // the rows were written through the generic proxy
                     asm volatile("fence.proxy.async.global;" ::: "memory");
-                    mbar_arrive_tx(&sm->kvbar, static_cast<uint32_t>(2 * n * HD * 4));
-                    bulk_g2s(&sm->kv[0][0][0], kv.k + off, static_cast<uint32_t>(n * HD * 4), &sm->kvbar);
-                    bulk_g2s(&sm->kv[1][0][0], kv.v + off, static_cast<uint32_t>(n * HD * 4), &sm->kvbar);
+                    mbar_arrive_tx(&sm->kvbar, static_cast<uint32_t>(2 * n * HD * es));
+                    bulk_g2s(&sm->kv[0][0][0], static_cast<const char *>(kv.k) + off, static_cast<uint32_t>(n * HD * es),
+                             &sm->kvbar);
+                    bulk_g2s(&sm->kv[1][0][0], static_cast<const char *>(kv.v) + off, static_cast<uint32_t>(n * HD * es),
+                             &sm->kvbar);
                     sm->kv_rows = n;
                 }
             }
@@ -1036,12 +1051,23 @@ struct Compute {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) y[j] = o[j];
             }
+            if (KV16 && t >= 2) {
+                // a half-float cache: this step reads the new K/V as later
+                // steps will, rounded to fp16
+#pragma unroll
+                for (int j = 0; j < 4; ++j) y[j] = __half2float(__float2half_rn(y[j]));
+            }
             float *dst = t < 2 ? qs + (r * 2 + t) * HD : (t == 2 ? kn + r * HD : vn + r * HD);
             *reinterpret_cast<float4 *>(dst + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
             if (append && t >= 2) {
-                float *cache = (t == 2 ? kv.k : kv.v) +
-                               ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + (L0 + r)) * HD;
-                *reinterpret_cast<float4 *>(cache + 4 * lane) = make_float4(y[0], y[1], y[2], y[3]);
+                const size_t e = ((static_cast<size_t>(layer) * HKV + h) * kv.max_pos + (L0 + r)) * HD + 4 * lane;
+                void *cache = t == 2 ? kv.k : kv.v;
+                if (KV16) {
+                    __half2 hh[2] = {__floats2half2_rn(y[0], y[1]), __floats2half2_rn(y[2], y[3])};
+                    *reinterpret_cast<uint2 *>(static_cast<__half *>(cache) + e) = *reinterpret_cast<uint2 *>(hh);
+                } else {
+                    *reinterpret_cast<float4 *>(static_cast<float *>(cache) + e) = make_float4(y[0], y[1], y[2], y[3]);
+                }
             }
         }
         if (prefetched) {
@@ -1058,8 +1084,10 @@ struct Compute {
         const bool active = combo < nc;
         const int cr = combo >> 1, cq = combo & 1;
         float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-        const float *kbase = kv.k + (static_cast<size_t>(layer) * HKV + h) * kv.max_pos * HD;
-        const float *vbase = kv.v + (static_cast<size_t>(layer) * HKV + h) * kv.max_pos * HD;
+        const size_t hoff = (static_cast<size_t>(layer) * HKV + h) * kv.max_pos * HD;
+        // a half-float cache keeps its tiles in shared memory as [ATT_TILE][HD] halves
+        const __half *ktile16 = reinterpret_cast<const __half *>(&sm->kv[0][0][0]);
+        const __half *vtile16 = reinterpret_cast<const __half *>(&sm->kv[1][0][0]);
         float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
         if (active) q = *reinterpret_cast<const float4 *>(qs + (cr * 2 + cq) * HD + 4 * lane);
         for (int tp = p0; tp < p1; tp += ATT_TILE) {
@@ -1068,12 +1096,23 @@ struct Compute {
             if (tp != p0 || !prefetched) {
                 // a tile that was not prefetched: plain loads of its cached rows
                 if (tp != p0) named_sync();
-                for (int i = tid; i < cached * (HD / 4); i += NCT) {
-                    const int pp = i / (HD / 4), d4 = i - pp * (HD / 4);
-                    reinterpret_cast<float4 *>(&sm->kv[0][pp][0])[d4] =
-                        ldcg4(kbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
-                    reinterpret_cast<float4 *>(&sm->kv[1][pp][0])[d4] =
-                        ldcg4(vbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
+                if (KV16) {
+                    const __half *kb = static_cast<const __half *>(kv.k) + hoff, *vb = static_cast<const __half *>(kv.v) + hoff;
+                    for (int i = tid; i < cached * (HD / 8); i += NCT) {
+                        const size_t g = static_cast<size_t>(tp) * HD + 8 * static_cast<size_t>(i);
+                        reinterpret_cast<uint4 *>(&sm->kv[0][0][0])[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + g));
+                        reinterpret_cast<uint4 *>(&sm->kv[1][0][0])[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + g));
+                    }
+                } else {
+                    const float *kbase = static_cast<const float *>(kv.k) + hoff;
+                    const float *vbase = static_cast<const float *>(kv.v) + hoff;
+                    for (int i = tid; i < cached * (HD / 4); i += NCT) {
+                        const int pp = i / (HD / 4), d4 = i - pp * (HD / 4);
+                        reinterpret_cast<float4 *>(&sm->kv[0][pp][0])[d4] =
+                            ldcg4(kbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
+                        reinterpret_cast<float4 *>(&sm->kv[1][pp][0])[d4] =
+                            ldcg4(vbase + static_cast<size_t>(tp + pp) * HD + 4 * d4);
+                    }
                 }
                 named_sync();
             }
@@ -1081,9 +1120,17 @@ struct Compute {
                 for (int pp = sub; pp < nt; pp += npw) {
                     const int p = tp + pp;
                     if (p > L0 + cr) break;  // causal
-                    const float *kp = p < L0 ? &sm->kv[0][pp][0] : kn + (p - L0) * HD;
-                    const float *vp = p < L0 ? &sm->kv[1][pp][0] : vn + (p - L0) * HD;
-                    const float4 k = *reinterpret_cast<const float4 *>(kp + 4 * lane);
+                    float4 k, v;
+                    if (p >= L0) {
+                        k = *reinterpret_cast<const float4 *>(kn + (p - L0) * HD + 4 * lane);
+                        v = *reinterpret_cast<const float4 *>(vn + (p - L0) * HD + 4 * lane);
+                    } else if (KV16) {
+                        k = h4_to_f4(ktile16 + pp * HD + 4 * lane);
+                        v = h4_to_f4(vtile16 + pp * HD + 4 * lane);
+                    } else {
+                        k = *reinterpret_cast<const float4 *>(&sm->kv[0][pp][0] + 4 * lane);
+                        v = *reinterpret_cast<const float4 *>(&sm->kv[1][pp][0] + 4 * lane);
+                    }
                     float d = q.x * k.x;
                     d = fmaf(q.y, k.y, d);
                     d = fmaf(q.z, k.z, d);
@@ -1093,7 +1140,6 @@ struct Compute {
                     const float corr = expf(m - mn);
                     const float e = expf(d - mn);
                     l = l * corr + e;
-                    const float4 v = *reinterpret_cast<const float4 *>(vp + 4 * lane);
                     o[0] = fmaf(e, v.x, o[0] * corr);
                     o[1] = fmaf(e, v.y, o[1] * corr);
                     o[2] = fmaf(e, v.z, o[2] * corr);
@@ -1272,9 +1318,9 @@ __device__ void produce(Smem *sm, const Job &job) {
     }
 }
 
-template <int WDT>
+template <int WDT, int KV16>
 __device__ void compute(Smem *sm, const Job &job) {
-    Compute<WDT> c;
+    Compute<WDT, KV16> c;
     c.sm = sm;
     c.job = &job;
     c.tid = threadIdx.x;
@@ -1293,7 +1339,7 @@ __device__ void compute(Smem *sm, const Job &job) {
         for (int r = 0; r < RMAX; ++r) in[r] = job.xin + r * H;
         c.stack(job.st, job.ctx, job.rows, job.L0, in, nullptr, nullptr);
         if (job.head_w && c.ok) {
-            c.head(job.st, job.rows, job.head_rows, Compute<WDT>::E_HEAD, S.hidden);
+            c.head(job.st, job.rows, job.head_rows, Compute<WDT, KV16>::E_HEAD, S.hidden);
         } else if (c.ok) {
             // no head: still return the normed last state
             const float *last[1] = {S.x + (job.rows - 1) * H};
@@ -1333,7 +1379,7 @@ __device__ void compute(Smem *sm, const Job &job) {
             const int L0 = g == 0 ? 0 : g + 1;
             c.stack(job.pst, job.pctx, R, L0, in, nullptr, nullptr);
             if (!c.ok) break;
-            c.head(job.pst, R, job.pvocab, Compute<WDT>::E_HEAD, nullptr);
+            c.head(job.pst, R, job.pvocab, Compute<WDT, KV16>::E_HEAD, nullptr);
             c.grid_sync(6);
             if (!c.ok) break;
             // ChooseCode (talker.pas:632-638): the draw (frame, group g + 1) or the argmax
@@ -1357,7 +1403,7 @@ __device__ void compute(Smem *sm, const Job &job) {
             const float *tr = step < job.trailing_rows ? job.trailing + static_cast<size_t>(step) * H : job.tts_pad;
             const float *in2[RMAX] = {tr, nullptr, nullptr, nullptr};
             c.stack(job.tst, job.tctx, 1, tlen, in0, in1, in2);
-            if (c.ok) c.head(job.tst, 1, job.tvocab, Compute<WDT>::E_HEAD0, S.hidden);
+            if (c.ok) c.head(job.tst, 1, job.tvocab, Compute<WDT, KV16>::E_HEAD0, S.hidden);
             if (c.ok) c.grid_sync(8);
             if (c.ok && blockIdx.x == 0 && (job.samp0.on || c.warp == 0)) {
                 // ChooseCode0 of the next frame (its draw is (step + 1, 0));
@@ -1394,7 +1440,7 @@ __device__ void compute(Smem *sm, const Job &job) {
     }
 }
 
-template <int WDT>
+template <int WDT, int KV16>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ Job job) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem *sm = reinterpret_cast<Smem *>(smem_raw);
@@ -1415,7 +1461,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     if (threadIdx.x / 32 == PRODUCER_WARP) {
         if (threadIdx.x % 32 == 0) produce<WDT>(sm, job);
     } else {
-        compute<WDT>(sm, job);
+        compute<WDT, KV16>(sm, job);
     }
     // no bulk copy may be in flight when the CTA exits: after everyone is
     // done, wait for the last chunk issued into each slot (earlier chunks of

@@ -28,7 +28,7 @@ LIB_PATH = os.path.join(HERE, "libqtts.so")
 DTYPE_F32 = 0
 DTYPE_Q8_0 = 1
 DTYPE_BF16 = 2
-DTYPES = {"f32": DTYPE_F32, "q8_0": DTYPE_Q8_0, "bf16": DTYPE_BF16}
+DTYPES = {"f32": DTYPE_F32, "q8_0": DTYPE_Q8_0, "bf16": DTYPE_BF16, "f16": 3}
 
 E_ARG, E_OOM, E_CUDA, E_CAPACITY, E_TIMEOUT, E_STATE = 1, 2, 3, 4, 5, 6
 
@@ -154,6 +154,7 @@ EXPORTS = {
     "qtts_lm_forward_noalloc": [P, P, I, I, P, P],
     "qtts_lm_length": [P, PI],
     "qtts_lm_set_wait_test": [P, I, ctypes.c_int64],
+    "qtts_lm_create_kv": [P, P, I, I, ctypes.POINTER(P)],
     "qtts_lm_destroy": [P],
     "qtts_batch_create": [P, P, I, I, I, I, ctypes.POINTER(P)],
     "qtts_batch_reset": [P, I],
@@ -461,9 +462,14 @@ class QwenLm:
     """TQwenLm (lm.pas:102-143): a stack (owned), its heads (not owned) and
     its KV cache."""
 
-    def __init__(self, stack, heads, max_pos=4096):
+    def __init__(self, stack, heads, max_pos=4096, kv_dtype="f32"):
+        """kv_dtype "f16": the K/V cache in half floats (TQwenLm.Create's
+        aKvF16, lm.pas:122-123)."""
         h = P()
-        check(lib().qtts_lm_create(stack.handle, heads.handle, max_pos, ctypes.byref(h)))
+        if kv_dtype == "f32":
+            check(lib().qtts_lm_create(stack.handle, heads.handle, max_pos, ctypes.byref(h)))
+        else:
+            check(lib().qtts_lm_create_kv(stack.handle, heads.handle, max_pos, DTYPES[kv_dtype], ctypes.byref(h)))
         stack.handle = None  # owned by the lm from now on
         self.handle = h
         self.heads = heads

@@ -63,6 +63,7 @@ def _load():
         "ora_lm_free": (None, [P]),
         "ora_lm_reset": (None, [P]),
         "ora_lm_length": (ctypes.c_int, [P]),
+        "ora_lm_set_kv_f16": (None, [P, ctypes.c_int]),
         "ora_lm_forward": (ctypes.c_int, [P, P, ctypes.c_int, P, ctypes.c_int, P, P, P, P]),
         "ora_argmax": (ctypes.c_int, [P, ctypes.c_int]),
         "ora_choose_code0": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, P]),
@@ -318,13 +319,16 @@ class OraHeads:
 
 
 class OraLm:
-    """TQwenLm on the CPU (the stack is owned by the caller here)."""
+    """TQwenLm on the CPU (the stack is owned by the caller here); kv_f16:
+    the cache in half floats (TQwenLm.Create's aKvF16)."""
 
-    def __init__(self, stack, heads, max_pos=4096):
+    def __init__(self, stack, heads, max_pos=4096, kv_f16=False):
         self.stack = stack
         self.heads = heads
         self.hidden = stack.hidden
         self.handle = lib.ora_lm_create(stack.handle, max_pos)
+        if kv_f16:
+            lib.ora_lm_set_kv_f16(self.handle, 1)
 
     def reset(self):
         lib.ora_lm_reset(self.handle)

@@ -375,6 +375,7 @@ typedef struct {
     int max_pos, len;
     float *k, *v;          /* [layers][max_pos][kv_heads][head_dim] */
     float *rope_cos, *rope_sin; /* [max_pos][head_dim/2] */
+    int kv_f16;            /* the cache holds half floats (TQwenLm aKvF16, lm.pas:122-123, 352) */
 } ora_lm;
 
 /* RoPE tables as transformers computes them in float32: inv_freq_i =
@@ -415,6 +416,10 @@ void ora_lm_free(ora_lm *m) {
 
 /* TQwenLm.Reset (lm.pas:374-378) */
 void ora_lm_reset(ora_lm *m) { m->len = 0; }
+/* TQwenLm.Create's aKvF16 (lm.pas:122-123, applied at 352): K and V are kept
+ * in half floats (round to nearest even), so every read of a cached position,
+ * the current one included, sees the rounded value */
+void ora_lm_set_kv_f16(ora_lm *m, int on) { m->kv_f16 = on; }
 int ora_lm_length(const ora_lm *m) { return m->len; }
 
 /* Qwen3RMSNorm: x * (1/sqrt(mean(x^2) + eps)), then * weight */
@@ -486,6 +491,11 @@ static int stack_forward(ora_lm *m, float *x, int rows, float *states) {
             float *vc = m->v + (((size_t)l * m->max_pos + p) * Hkv) * D;
             memcpy(kc, k + (size_t)r * KV, KV * sizeof(float));
             memcpy(vc, v + (size_t)r * KV, KV * sizeof(float));
+            if (m->kv_f16)
+                for (int i = 0; i < KV; i++) {
+                    kc[i] = f16_to_f32(f32_to_f16(kc[i]));
+                    vc[i] = f16_to_f32(f32_to_f16(vc[i]));
+                }
         }
         /* causal GQA attention: query head hh reads kv head hh / grp */
 #pragma omp parallel for collapse(2) schedule(static)
