@@ -527,13 +527,13 @@ static int gemm_split(int n_rows, int k, int T) {
 
 // y[t][n] (+)= ...  A K split sums its partials in a fixed order inside a
 // cluster (no atomics, no cleared output).  With swiglu16 (gate/up pairs in
-// consecutive rows), no K split and the epilogue writes
-// fp16(silu(gate) * up) to swiglu16[t][n / 2] (row stride ld) instead of y.
+// consecutive rows), fp16(silu(gate) * up) goes to swiglu16[t][n / 2] (row
+// stride ld) instead of y.
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
                 bool add, int *err, cudaStream_t st, __half *swiglu16 = nullptr) {
     if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
     const int bn = gemm_bn(T);
-    const int split = swiglu16 ? 1 : gemm_split(n_rows, k, T);
+    const int split = gemm_split(n_rows, k, T);
     GemmArgs a;
     a.w = w;
     a.n_rows = n_rows;

@@ -56,8 +56,13 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *s) {
 __global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, const float *w, float eps, __half *out16,
                                    float *out32) {
     pdl_trigger();
-    pdl_wait();
     const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    // the norm weights do not depend on the previous kernel: loaded before
+    // waiting for it
+    float4 gw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gw[i] = load4(w + 4 * (lane + 32 * i));
+    pdl_wait();
     if (o >= rows) return;
     const float *r = x + static_cast<size_t>(idx ? idx[o] : o) * H;
     float4 v[8];
@@ -72,7 +77,7 @@ __global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, con
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int e = 4 * (lane + 32 * i);
-        const float4 g = load4(w + e);
+        const float4 g = gw[i];
         const float4 y = make_float4(g.x * (v[i].x * inv), g.y * (v[i].y * inv), g.z * (v[i].z * inv), g.w * (v[i].w * inv));
         *reinterpret_cast<__half2 *>(out16 + static_cast<size_t>(o) * H + e) = __floats2half2_rn(y.x, y.y);
         *reinterpret_cast<__half2 *>(out16 + static_cast<size_t>(o) * H + e + 2) = __floats2half2_rn(y.z, y.w);
@@ -88,24 +93,28 @@ __global__ void qkv_post_kernel(const float *qkv, const int *tok_seq, const int 
                                 const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
                                 float *q32, KVPool<KVT> pool, int layer) {
     pdl_trigger();
-    pdl_wait();
     const int t = blockIdx.x, v = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    // the token's metadata (copied before the call's first kernel), the norm
+    // weights and the RoPE row: loaded before waiting for the QKV GEMM
     const int seq = tok_seq[t], pos = tok_pos[t];
+    const int half = HD / 2, e0 = (4 * lane) & (half - 1);
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f), cs = g, sn = g;
+    if (v < 24) {
+        g = load4((v < 16 ? q_norm : k_norm) + 4 * lane);
+        cs = load4(rope_cos + static_cast<size_t>(pos) * half + e0);
+        sn = load4(rope_sin + static_cast<size_t>(pos) * half + e0);
+    }
+    pdl_wait();
     const int off = v < 16 ? v * HD : (v < 24 ? QDIM + (v - 16) * HD : QDIM + KVDIM + (v - 24) * HD);
     const float4 x = load4(qkv + static_cast<size_t>(t) * QKV_ROWS + off + 4 * lane);
     float y[4] = {x.x, x.y, x.z, x.w};
     if (v < 24) {
-        const float *nw = v < 16 ? q_norm : k_norm;
         const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
-        const float4 g = load4(nw + 4 * lane);
         y[0] = g.x * (y[0] * inv);
         y[1] = g.y * (y[1] * inv);
         y[2] = g.z * (y[2] * inv);
         y[3] = g.w * (y[3] * inv);
-        const int half = HD / 2, e0 = (4 * lane) & (half - 1);
-        const float4 cs = load4(rope_cos + static_cast<size_t>(pos) * half + e0);
-        const float4 sn = load4(rope_sin + static_cast<size_t>(pos) * half + e0);
         const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
         float o[4];
 #pragma unroll
@@ -298,17 +307,24 @@ __global__ void __launch_bounds__(DTHREADS) attn_decode_kernel(const AttnItem *i
     extern __shared__ __align__(128) uint8_t dsm_raw[];
     DecodeSmem<KVT> *sm = reinterpret_cast<DecodeSmem<KVT> *>(dsm_raw);
     pdl_trigger();
-    pdl_wait();
+    // the item (metadata copied before the call's first kernel) and, when
+    // its first tile holds only cached positions (written by earlier calls,
+    // which completed before this call's first copy), that tile's pages are
+    // on their way before the previous kernel (the append of the new row)
+    // has finished
     const AttnItem it = items[blockIdx.x];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q = tid >> 6, j = tid & 63;  // scores: (head, key); output: (head, dim pair j)
     const int nkeys = it.kb > it.ka ? it.kb - it.ka : 0;
     const int ntiles = (nkeys + DSPLIT - 1) / DSPLIT;
+    const bool early = ntiles > 0 && it.ka + min(DSPLIT, nkeys) <= it.L0;
     if (tid == 0) {
         mbar_init(&sm->bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        if (ntiles > 0) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys));
+        if (early) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys));
     }
+    pdl_wait();
+    if (tid == 0 && ntiles > 0 && !early) decode_issue(sm, pool, layer, it.seq, it.h, it.ka, min(DSPLIT, nkeys));
     for (int i = tid; i < 2 * HD / 4; i += DTHREADS) {
         const int hq = i / (HD / 4), d4 = i - hq * (HD / 4);
         store4(&sm->qs[hq][4 * d4], load4(q32 + static_cast<size_t>(it.t0) * QDIM + (2 * it.h + hq) * HD + 4 * d4));

@@ -78,8 +78,9 @@ struct GemmArgs {
     int atomic;        // add into out (the residual) instead of storing
     int ksplit;        // K splits (a cluster of ksplit CTAs per tile); K blocks per split = (K / G_BK) / ksplit
     int *err;          // error word (QTTS_E_TIMEOUT on a wait that gave up)
-    __half *swiglu16;  // non-NULL (no K split): rows are gate/up pairs (2j, 2j+1) and the
-                       // epilogue writes fp16(silu(gate) * up) to swiglu16[t * ld16 + j]
+    __half *swiglu16;  // non-NULL: rows are gate/up pairs (2j, 2j+1) and the epilogue (or,
+                       // with a K split, the cluster's reduction) writes fp16(silu(gate) * up)
+                       // to swiglu16[t * ld16 + j]
     int ld16;
 };
 
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         for (int c = 0; c < BN; c += 32) {
             float v[32];
             tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
-            if (args.swiglu16) {
+            if (args.swiglu16 && args.ksplit == 1) {
                 // the up row of a pair is the next lane: SiLU(gate) * up, as
                 // the separate SwiGLU kernel computes it
 #pragma unroll
@@ -392,15 +393,35 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         const int ks = args.ksplit, z = static_cast<int>(cl.block_rank());
         const int rows_z = G_BM / ks, rz0 = z * rows_z;
         const float *part = reinterpret_cast<const float *>(sm);
-        for (int idx = tid; idx < rows_z * BN; idx += G_THREADS) {
-            const int rr = rz0 + idx % rows_z, col = idx / rows_z;
-            float sum = 0.f;
-            for (int r = 0; r < ks; ++r)
-                sum += *cl.map_shared_rank(part + col * G_BM + rr, static_cast<unsigned>(r));
-            const int n = row0 + rr, t = tok0 + col;
-            if (n < args.n_rows && t < args.T) {
-                float *o = args.out + static_cast<size_t>(t) * args.ld + n;
-                *o = args.atomic ? *o + sum : sum;
+        if (args.swiglu16) {
+            // gate/up pairs (rows 2j, 2j+1; a chunk of rows_z >= 16 rows
+            // holds whole pairs): fp16(silu(gate) * up) as the unsplit epilogue
+            const int pz = rows_z / 2;
+            for (int idx = tid; idx < pz * BN; idx += G_THREADS) {
+                const int rr = rz0 + 2 * (idx % pz), col = idx / pz;
+                float g = 0.f, u = 0.f;
+                for (int r = 0; r < ks; ++r) {
+                    const float *pr = cl.map_shared_rank(part + col * G_BM + rr, static_cast<unsigned>(r));
+                    g += pr[0];
+                    u += pr[1];
+                }
+                const int n = row0 + rr, t = tok0 + col;
+                if (n < args.n_rows && t < args.T) {
+                    const float sl = g / (1.0f + expf(-g));
+                    args.swiglu16[static_cast<size_t>(t) * args.ld16 + (n >> 1)] = __float2half_rn(sl * u);
+                }
+            }
+        } else {
+            for (int idx = tid; idx < rows_z * BN; idx += G_THREADS) {
+                const int rr = rz0 + idx % rows_z, col = idx / rows_z;
+                float sum = 0.f;
+                for (int r = 0; r < ks; ++r)
+                    sum += *cl.map_shared_rank(part + col * G_BM + rr, static_cast<unsigned>(r));
+                const int n = row0 + rr, t = tok0 + col;
+                if (n < args.n_rows && t < args.T) {
+                    float *o = args.out + static_cast<size_t>(t) * args.ld + n;
+                    *o = args.atomic ? *o + sum : sum;
+                }
             }
         }
         cl.sync();
