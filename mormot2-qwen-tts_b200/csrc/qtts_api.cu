@@ -529,8 +529,19 @@ static int gemm_split(int n_rows, int k, int T) {
 // cluster (no atomics, no cleared output).  With swiglu16 (gate/up pairs in
 // consecutive rows), fp16(silu(gate) * up) goes to swiglu16[t][n / 2] (row
 // stride ld) instead of y.
+// the QKV projection's fused epilogue (GemmArgs::q32 and what follows it)
+struct QkvEpi {
+    float *q32;
+    const float *q_norm, *k_norm, *rope_cos, *rope_sin;
+    float eps;
+    const int *tok_seq, *tok_pos;
+    void *kv_base;
+    const int *kv_pages;
+    int kv_mpps, kv_layers, kv_layer, kv_bf16;
+};
+
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
-                bool add, int *err, cudaStream_t st, __half *swiglu16 = nullptr) {
+                bool add, int *err, cudaStream_t st, __half *swiglu16 = nullptr, const QkvEpi *qe = nullptr) {
     if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
     const int bn = gemm_bn(T);
     const int split = gemm_split(n_rows, k, T);
@@ -546,6 +557,30 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.err = err;
     a.swiglu16 = swiglu16;
     a.ld16 = swiglu16 ? ld : 0;
+    a.q32 = nullptr;
+    a.q_norm = a.k_norm = a.rope_cos = a.rope_sin = nullptr;
+    a.eps = 0.f;
+    a.tok_seq = a.tok_pos = nullptr;
+    a.kv_base = nullptr;
+    a.kv_pages = nullptr;
+    a.kv_mpps = a.kv_layers = a.kv_layer = a.kv_bf16 = 0;
+    if (qe) {
+        if (n_rows != QKV_ROWS) return set_err(QTTS_E_ARG, "gemm: the QKV epilogue needs the %d QKV rows", QKV_ROWS);
+        a.q32 = qe->q32;
+        a.q_norm = qe->q_norm;
+        a.k_norm = qe->k_norm;
+        a.rope_cos = qe->rope_cos;
+        a.rope_sin = qe->rope_sin;
+        a.eps = qe->eps;
+        a.tok_seq = qe->tok_seq;
+        a.tok_pos = qe->tok_pos;
+        a.kv_base = qe->kv_base;
+        a.kv_pages = qe->kv_pages;
+        a.kv_mpps = qe->kv_mpps;
+        a.kv_layers = qe->kv_layers;
+        a.kv_layer = qe->kv_layer;
+        a.kv_bf16 = qe->kv_bf16;
+    }
     dim3 grid((n_rows + G_BM - 1) / G_BM, (T + bn - 1) / bn, split);
     if (wdt == WDT_Q8) {
         if (bn == 64) return gemm_launch_t<WDT_Q8, 64>(a, x, rows_cap, grid, st);
@@ -2342,7 +2377,7 @@ struct qtts_batch {
     float *rope_cos, *rope_sin;
     cudaStream_t stream;
     // per-call buffers
-    float *x, *qkv, *q32, *part, *hidden, *logits;
+    float *x, *q32, *part, *hidden, *logits;
     __half *h16, *attn16, *act16, *hlast16;
     int *meta;  // token metadata and attention items
     size_t meta_bytes;
@@ -2421,7 +2456,6 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         {reinterpret_cast<void **>(&b->rope_cos), static_cast<size_t>(max_pos) * (HD / 2) * 4},
         {reinterpret_cast<void **>(&b->rope_sin), static_cast<size_t>(max_pos) * (HD / 2) * 4},
         {reinterpret_cast<void **>(&b->x), T * H * 4},
-        {reinterpret_cast<void **>(&b->qkv), T * QKV_ROWS * 4},
         {reinterpret_cast<void **>(&b->q32), T * QDIM * 4},
         {reinterpret_cast<void **>(&b->part), static_cast<size_t>(max_seqs) * HKV * max_splits * 2 * PSTRIDE * 4},
         {reinterpret_cast<void **>(&b->hidden), static_cast<size_t>(max_seqs) * H * 4},
@@ -2502,10 +2536,25 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
             rc = set_err(QTTS_E_CUDA, "qtts_batch_forward: launch failed: %s", cudaGetErrorString(e));
             return;
         }
-        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, b->qkv, QKV_ROWS, false, b->err, st))) return;
-        e = launch_pdl(qkv_post_kernel<KVT>, dim3(T, 4), dim3(256), 0, st, b->qkv, tok_seq, tok_pos, Ly.q_norm,
-                       Ly.k_norm, eps, b->rope_cos, b->rope_sin, b->q32, pool, l);
-        if (e == cudaSuccess && npitems > 0)
+        // the QKV GEMM's epilogue does q/k-norm + RoPE + the append to the pages
+        QkvEpi qe;
+        qe.q32 = b->q32;
+        qe.q_norm = Ly.q_norm;
+        qe.k_norm = Ly.k_norm;
+        qe.rope_cos = b->rope_cos;
+        qe.rope_sin = b->rope_sin;
+        qe.eps = eps;
+        qe.tok_seq = tok_seq;
+        qe.tok_pos = tok_pos;
+        qe.kv_base = pool.base;
+        qe.kv_pages = pool.pages;
+        qe.kv_mpps = pool.mpps;
+        qe.kv_layers = pool.layers;
+        qe.kv_layer = l;
+        qe.kv_bf16 = sizeof(KVT) == 2 ? 1 : 0;
+        if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, nullptr, QKV_ROWS, false, b->err, st, nullptr, &qe)))
+            return;
+        if (npitems > 0)
             e = launch_pdl(attn_kernel<KVT>, dim3(npitems), dim3(ATHREADS), 0, st, pitems, b->q32, pool, l, b->attn16);
         if (e == cudaSuccess && ntitems > 0)
             e = launch_pdl(attn_prefill_tc_kernel<KVT>, dim3(ntitems), dim3(TA_THREADS), sizeof(TaSmem) + 1024, st,

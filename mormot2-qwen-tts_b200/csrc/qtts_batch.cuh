@@ -1,8 +1,8 @@
 // qtts_batch.cuh -- the batched forward of libqtts (sm_100a): many sequences
 // (utterances) through one stack per call, the projections on the tcgen05
-// GEMM (qtts_gemm.cuh), the rest here: RMSNorm to fp16, q/k-norm + RoPE +
-// append into a paged KV cache, causal GQA attention over the pages (SwiGLU
-// is in the gate/up GEMM epilogue).
+// GEMM (qtts_gemm.cuh, whose epilogues also do q/k-norm + RoPE + the append
+// into the paged KV cache after the QKV projection, and SwiGLU after gate/up),
+// the rest here: RMSNorm to fp16, causal GQA attention over the pages.
 //
 // Paged KV cache: pages of 16 positions; a page holds, for every layer, K and
 // V of the 8 KV heads: [page][layer][k|v][head][16][128], in float32 or bf16.
@@ -17,7 +17,7 @@
 
 namespace qtts {
 
-constexpr int PAGE = 16;   // positions per page
+constexpr int PAGE = G_PAGE;  // positions per page (the QKV GEMM's epilogue appends to the pages too)
 constexpr int AQB = 16;    // query rows per attention item (prefill)
 constexpr int AKT = 16;    // keys per attention tile
 constexpr int ATHREADS = 256;
@@ -83,53 +83,6 @@ __global__ void rmsnorm_f16_kernel(const float *x, const int *idx, int rows, con
         *reinterpret_cast<__half2 *>(out16 + static_cast<size_t>(o) * H + e + 2) = __floats2half2_rn(y.z, y.w);
         if (out32) store4(out32 + static_cast<size_t>(o) * H + e, y);
     }
-}
-
-// q/k-norm + RoPE of every token's 16 q and 8 k heads, raw v; q to q32
-// [T][16][128], k and v appended to the pages at the token's position.
-// grid (T, 4), 8 warps: warp v of 32 = q head v (< 16), k head v-16, v head v-24.
-template <class KVT>
-__global__ void qkv_post_kernel(const float *qkv, const int *tok_seq, const int *tok_pos, const float *q_norm,
-                                const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
-                                float *q32, KVPool<KVT> pool, int layer) {
-    pdl_trigger();
-    const int t = blockIdx.x, v = blockIdx.y * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    // the token's metadata (copied before the call's first kernel), the norm
-    // weights and the RoPE row: loaded before waiting for the QKV GEMM
-    const int seq = tok_seq[t], pos = tok_pos[t];
-    const int half = HD / 2, e0 = (4 * lane) & (half - 1);
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f), cs = g, sn = g;
-    if (v < 24) {
-        g = load4((v < 16 ? q_norm : k_norm) + 4 * lane);
-        cs = load4(rope_cos + static_cast<size_t>(pos) * half + e0);
-        sn = load4(rope_sin + static_cast<size_t>(pos) * half + e0);
-    }
-    pdl_wait();
-    const int off = v < 16 ? v * HD : (v < 24 ? QDIM + (v - 16) * HD : QDIM + KVDIM + (v - 24) * HD);
-    const float4 x = load4(qkv + static_cast<size_t>(t) * QKV_ROWS + off + 4 * lane);
-    float y[4] = {x.x, x.y, x.z, x.w};
-    if (v < 24) {
-        const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
-        y[0] = g.x * (y[0] * inv);
-        y[1] = g.y * (y[1] * inv);
-        y[2] = g.z * (y[2] * inv);
-        y[3] = g.w * (y[3] * inv);
-        const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
-        float o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float partner = __shfl_xor_sync(0xffffffffu, y[j], 16);
-            o[j] = lane < 16 ? y[j] * cv[j] - partner * sv[j] : y[j] * cv[j] + partner * sv[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) y[j] = o[j];
-    }
-    const float4 r = make_float4(y[0], y[1], y[2], y[3]);
-    if (v < 16)
-        store4(q32 + static_cast<size_t>(t) * QDIM + v * HD + 4 * lane, r);
-    else
-        store4(kv_at(pool, layer, seq, pos, v < 24 ? 0 : 1, v < 24 ? v - 16 : v - 24) + 4 * lane, r);
 }
 
 // One attention work item: the new rows [qa, qb) of one sequence (token t0

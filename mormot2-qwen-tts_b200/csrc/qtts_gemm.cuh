@@ -17,23 +17,25 @@
 //    contiguous chunk, so one bulk copy (cp.async.bulk) brings a stage's
 //    weights into shared memory.  Q8_0 (8192 int8 + 256 fp16 scales = 8704
 //    bytes): warps 0-7 (two threads per weight row, 32 k each) dequantise it
-//    there to fp16 (w = q * d, rounded once) in the UMMA K-major 128B-swizzle
-//    layout, fence.proxy.async, then an mbarrier arrival.  Float32 weights
-//    (32 KB): two fp16 tiles already in that layout, hi = fp16(w) and
-//    lo = fp16(w - hi), copied straight into the A buffers; both are
-//    multiplied with the same activations into one accumulator, so a weight
-//    enters the sum to about 2^-22 of its value instead of fp16's 2^-11.
+//    there to two fp16 tiles, hi = fp16(q * d) and lo = q * d - hi (one fused
+//    fp16 multiply-add), in the UMMA K-major 128B-swizzle layout,
+//    fence.proxy.async, then an mbarrier arrival.  Float32 weights (32 KB):
+//    the two tiles hi = fp16(w), lo = fp16(w - hi) already in that layout,
+//    copied straight into the A buffers.  Both tiles are multiplied with the
+//    same activations into one accumulator, so a weight enters the sum to
+//    about 2^-22 of its value instead of fp16's 2^-11.
 //  - B operand (activations, fp16 [T][K]): one TMA tiled load per stage
 //    (cp.async.bulk.tensor.2d, 128B swizzle, no multicast); warp 8 lane 0
 //    issues both copies of a stage.
 //  - MMA: one thread issues tcgen05.mma.cta_group::1.kind::f16 (f16 x f16 ->
-//    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage, twice for hi/lo float32
-//    weights) and tcgen05.commit frees the stage; the accumulator (BN TMEM columns) is read back by warps 8-11 with
+//    f32 in TMEM, M=128, N=BN, 4 x K=16 per stage, each for the hi and the lo
+//    tile) and tcgen05.commit frees the stage; the accumulator (BN TMEM columns) is read back by warps 8-11 with
 //    tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31 = its weight rows).
 //  - every mbarrier wait is bounded; a timeout sets the error word.
 #pragma once
 #include <cooperative_groups.h>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -59,8 +61,9 @@ __host__ __device__ constexpr int g_chunk_bytes(int wdt) {
 // the staging area of a Q8_0 chunk before dequantisation (float32 chunks
 // land in the A tiles directly)
 __host__ __device__ constexpr int g_raw_bytes(int wdt) { return wdt == WDT_Q8 ? g_chunk_bytes(wdt) : 0; }
-// A tiles per stage: one (Q8_0) or hi + lo (float32)
-__host__ __device__ constexpr int g_a_tiles(int wdt) { return wdt == WDT_Q8 ? 1 : 2; }
+// A tiles per stage: hi + lo (both formats: the weight enters the product to
+// ~2^-22 of its value, not fp16's 2^-11)
+__host__ __device__ constexpr int g_a_tiles(int) { return 2; }
 // pipeline depth from the shared-memory budget (at most 6 stages)
 __host__ __device__ constexpr int g_stage_bytes(int wdt, int bn) {
     return g_raw_bytes(wdt) + g_a_tiles(wdt) * G_A_BYTES + bn * 128;
@@ -82,7 +85,70 @@ struct GemmArgs {
                        // with a K split, the cluster's reduction) writes fp16(silu(gate) * up)
                        // to swiglu16[t * ld16 + j]
     int ld16;
+    // non-NULL q32: the QKV projection (rows [q 2048][k 1024][v 1024], so a
+    // 128-row tile is one head), and the epilogue does what follows it per
+    // token: q/k RMSNorm (q_norm / k_norm, eps) and RoPE at the token's
+    // position, q to q32[t][2048], k and v appended to the paged cache
+    // (pages of G_PAGE positions, [page][layer][k|v][head][G_PAGE][128], f32
+    // or bf16)
+    float *q32;
+    const float *q_norm, *k_norm, *rope_cos, *rope_sin;
+    float eps;
+    const int *tok_seq, *tok_pos;
+    void *kv_base;
+    const int *kv_pages;
+    int kv_mpps, kv_layers, kv_layer, kv_bf16;
 };
+
+constexpr int G_PAGE = 16;  // positions per page of the paged KV cache
+
+// the QKV epilogue of token t (one warp): x[4] = this lane's dims 4L..4L+3
+// of head `head` (0-15 q, 16-23 k, 24-31 v)
+__device__ __forceinline__ void qkv_token_epilogue(const GemmArgs &a, int head, int t, float x[4], int lane) {
+    const int seq = a.tok_seq[t], pos = a.tok_pos[t];
+    if (head < 24) {
+        const float *nw = head < 16 ? a.q_norm : a.k_norm;
+        float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
+        const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
+        x[0] = g.x * (x[0] * inv);
+        x[1] = g.y * (x[1] * inv);
+        x[2] = g.z * (x[2] * inv);
+        x[3] = g.w * (x[3] * inv);
+        const int half = HD / 2, e0 = (4 * lane) & (half - 1);
+        const float4 cs = *reinterpret_cast<const float4 *>(a.rope_cos + static_cast<size_t>(pos) * half + e0);
+        const float4 sn = *reinterpret_cast<const float4 *>(a.rope_sin + static_cast<size_t>(pos) * half + e0);
+        const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float partner = __shfl_xor_sync(0xffffffffu, x[j], 16);
+            o[j] = lane < 16 ? x[j] * cv[j] - partner * sv[j] : x[j] * cv[j] + partner * sv[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = o[j];
+    }
+    if (head < 16) {
+        *reinterpret_cast<float4 *>(a.q32 + static_cast<size_t>(t) * QDIM + head * HD + 4 * lane) =
+            make_float4(x[0], x[1], x[2], x[3]);
+        return;
+    }
+    const int which = head < 24 ? 0 : 1, kvh = head < 24 ? head - 16 : head - 24;
+    const int page = a.kv_pages[seq * a.kv_mpps + pos / G_PAGE];
+    const size_t e = ((((static_cast<size_t>(page) * a.kv_layers + a.kv_layer) * 2 + which) * HKV + kvh) * G_PAGE +
+                      pos % G_PAGE) * HD + 4 * lane;
+    if (a.kv_bf16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t *>(&lo);
+        u.y = *reinterpret_cast<uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(a.kv_base) + e) = u;
+    } else {
+        *reinterpret_cast<float4 *>(static_cast<float *>(a.kv_base) + e) = make_float4(x[0], x[1], x[2], x[3]);
+    }
+}
 
 template <int WDT, int BN>
 struct __align__(1024) GemmSmem {
@@ -250,6 +316,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
             const uint8_t *raw = sm->raw[s];
             uint8_t *dst = sm->a[s][0] + (r >> 3) * 1024 + (r & 7) * 128;
+            uint8_t *dst_lo = sm->a[s][1] + (r >> 3) * 1024 + (r & 7) * 128;
             __half2 d2lo = __float2half2_rn(0.f), d2hi = d2lo;  // the two blocks' scales, broadcast
             if (WDT == WDT_Q8) {
                 const __half2 dd = *reinterpret_cast<const __half2 *>(raw + G_BM * G_BK + r * 4);
@@ -258,18 +325,25 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
 #pragma unroll
             for (int c = c0; c < c0 + 4; ++c) {  // 4 groups of 8 k
-                // q + 128 in the mantissa of fp16 1024 (exact), minus 1152,
-                // times d in fp16: the exact product q * d rounded once
-                __half2 h[4];
+                // q + 128 in the mantissa of fp16 1024 (exact), minus 1152:
+                // q exactly; hi = fp16(q * d) (the exact product rounded
+                // once), lo = q * d - hi by one fused fp16 multiply-add
+                __half2 h[4], lo[4];
                 const uint2 q = *reinterpret_cast<const uint2 *>(raw + (c * G_BM + r) * 8);
                 const uint32_t ux = q.x ^ 0x80808080u, uy = q.y ^ 0x80808080u;
                 const __half2 bias = __float2half2_rn(1152.f);
                 const __half2 d2 = c < 4 ? d2lo : d2hi;
-                h[0] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x5140)), bias), d2);
-                h[1] = __hmul2(__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x7362)), bias), d2);
-                h[2] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias), d2);
-                h[3] = __hmul2(__hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias), d2);
+                const __half2 qv[4] = {__hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x5140)), bias),
+                                       __hsub2(u32_as_half2(__byte_perm(ux, 0x64646464u, 0x7362)), bias),
+                                       __hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x5140)), bias),
+                                       __hsub2(u32_as_half2(__byte_perm(uy, 0x64646464u, 0x7362)), bias)};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    h[e] = __hmul2(qv[e], d2);
+                    lo[e] = __hfma2(qv[e], d2, __hneg2(h[e]));
+                }
                 *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(h);
+                *reinterpret_cast<uint4 *>(dst_lo + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4 *>(lo);
             }
             // the tensor core reads shared memory through the async proxy
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -322,8 +396,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                 for (int k = 0; k < G_BK / 16; ++k) {  // +32 bytes (2 in 16-byte units) per K=16
                     umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-                    if (WDT != WDT_Q8)  // the lo tile, 16 KB (1024 16-byte units) further
-                        umma_f16(tmem, da + 1024 + 2 * k, db + 2 * k, idesc, 1u);
+                    // the lo tile, 16 KB (1024 16-byte units) further
+                    umma_f16(tmem, da + 1024 + 2 * k, db + 2 * k, idesc, 1u);
                 }
                 umma_commit(&sm->empty[s]);
             }
@@ -358,7 +432,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 }
                 continue;
             }
-            if (args.ksplit > 1) {
+            if (args.ksplit > 1 || args.q32) {
                 // the partial tile, [BN tokens][128 rows], over the stage
                 // buffers (every copy has landed and every MMA read them)
                 float *part = reinterpret_cast<float *>(sm);
@@ -382,7 +456,41 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             }
         }
     }
-    if (args.ksplit > 1) {
+    if (args.q32) {
+        // the QKV epilogue: the tile's (partial) sums [BN][128] are in shared
+        // memory (of every CTA of the cluster with a K split); CTA z takes
+        // tokens [z BN/ks, (z+1) BN/ks), a warp a token, sums its 128 rows
+        // over the ranks in order and finishes the head
+        namespace cg = cooperative_groups;
+        const int ks = args.ksplit;
+        int z = 0;
+        if (ks > 1) {
+            cg::cluster_group cl = cg::this_cluster();
+            cl.sync();
+            z = static_cast<int>(cl.block_rank());
+        } else {
+            __syncthreads();
+        }
+        pdl_wait();  // the pages and q32 may be read by the previous kernels
+        const float *part = reinterpret_cast<const float *>(sm);
+        const int per = BN / ks, head = row0 / G_BM;
+        for (int i = warp; i < per; i += G_THREADS / 32) {
+            const int col = z * per + i, t = tok0 + col;
+            if (t >= args.T) continue;
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int r = 0; r < ks; ++r) {
+                const float *src = part + col * G_BM + 4 * lane;
+                if (ks > 1) src = cg::this_cluster().map_shared_rank(src, static_cast<unsigned>(r));
+                const float4 v = *reinterpret_cast<const float4 *>(src);
+                x[0] += v.x;
+                x[1] += v.y;
+                x[2] += v.z;
+                x[3] += v.w;
+            }
+            qkv_token_epilogue(args, head, t, x, lane);
+        }
+        if (ks > 1) cg::this_cluster().sync();
+    } else if (args.ksplit > 1) {
         // fixed-order split-K: the cluster's partials meet, CTA z sums its
         // rows of the tile over ranks 0..ks-1 in order; a second barrier
         // keeps every CTA's shared memory alive until the others have read it

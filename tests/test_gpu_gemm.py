@@ -3,10 +3,10 @@ the reference's TInferBackend.Linear on a head (mormot.ai.tts.qwen.lm.pas:
 404-406) for many rows at once.
 
 Expected values: numpy in float64 on the same fp16 operands the tensor cores
-see (x rounded to fp16; Q8_0 weights dequantised as q*d in float32 and
-rounded to fp16; f32 weights as the two fp16 tiles hi = fp16(w) and
-lo = fp16(w - hi), both multiplied with x).  Only the f32 accumulation order
-differs, hence the tight tolerance.
+see (x rounded to fp16; the weights as two fp16 tiles, hi and lo, both
+multiplied with x: hi = fp16(w), lo = fp16(w - hi) for f32 weights, hi =
+fp16(q*d), lo = q*d - hi for Q8_0, which carry the weight to ~2^-22).  Only
+the f32 accumulation order differs, hence the tight tolerance.
 """
 import numpy as np
 import pytest
@@ -24,9 +24,9 @@ def fp16_weights(w, dtype):
         lo = (w - hi.astype(np.float32)).astype(np.float16)
         return hi.astype(np.float64) + lo.astype(np.float64)
     q = O.quantize_q8_0(w).reshape(-1, 34)
-    d = q[:, :2].copy().view(np.float16).astype(np.float32)        # [blocks, 1]
-    qs = q[:, 2:].view(np.int8).astype(np.float32)                  # [blocks, 32]
-    return (qs * d).astype(np.float16).astype(np.float64).reshape(w.shape)
+    d = q[:, :2].copy().view(np.float16).astype(np.float64)        # [blocks, 1]
+    qs = q[:, 2:].view(np.int8).astype(np.float64)                  # [blocks, 32]
+    return (qs * d).reshape(w.shape)  # hi + lo carry q * d to ~2^-22
 
 
 @pytest.mark.parametrize("dtype", ["q8_0", "f32"])
