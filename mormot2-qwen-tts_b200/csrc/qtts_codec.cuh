@@ -19,21 +19,49 @@ constexpr int CG = 16, CB = 2048, CODE_DIM = 256, QUANT_DIM = 512, LATENT = 1024
 constexpr int TF_DIM = 512, TF_HEADS = 16, TF_HD = 64, TF_QKV = TF_HEADS * TF_HD, TF_MLP = 1024, TF_LAYERS = 8;
 constexpr int TF_WINDOW = 72, DEC_DIM = 1536, FRAME_SAMPLES = 1920;
 
+// The K chunk of a split GEMM: a K longer than this is cut into chunks of
+// KC, each chunk's products summed by its own CTAs into a partial, and the
+// partials added in chunk order by splitk_reduce_kernel.  The cut depends on
+// K alone, never on the rows of a call, so frames decoded one call at a time
+// still give exactly the samples of one call.
+constexpr int KC = 256;
+
 // y[M][N] = a[M][K] . w[N][K]^T (+ bias): 64 x 64 tiles, K by 16, 256
-// threads of 4 x 4 outputs; every load and store bounds-checked
+// threads of 4 x 4 outputs; every load and store bounds-checked.  With
+// gridDim.z > 1, CTA z takes K chunk [z KC, (z+1) KC) and writes its partial
+// (no bias) to y + z M N.
 __global__ void __launch_bounds__(256) gemm_kernel(const float *a, int M, int K, const float *w, int N,
                                                    const float *bias, float *y) {
     __shared__ float as[16][68], ws[16][68];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    const bool split = gridDim.z > 1;
+    const int kb = split ? blockIdx.z * KC : 0, ke = split ? min(K, kb + KC) : K;
+    if (split) {
+        y += static_cast<size_t>(blockIdx.z) * M * N;
+        bias = nullptr;
+    }
     float acc[4][4] = {};
-    for (int k0 = 0; k0 < K; k0 += 16) {
-        for (int i = threadIdx.x; i < 1024; i += 256) {
-            const int r = i >> 4, k = i & 15, gk = k0 + k;
-            as[k][r] = (m0 + r < M && gk < K) ? a[static_cast<size_t>(m0 + r) * K + gk] : 0.f;
-            ws[k][r] = (n0 + r < N && gk < K) ? w[static_cast<size_t>(n0 + r) * K + gk] : 0.f;
+    // the next K step's loads are in flight while this one is multiplied
+    float pa[4], pw[4];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = threadIdx.x + 256 * u, r = i >> 4, gk = k0 + (i & 15);
+            pa[u] = (m0 + r < M && gk < ke) ? a[static_cast<size_t>(m0 + r) * K + gk] : 0.f;
+            pw[u] = (n0 + r < N && gk < ke) ? w[static_cast<size_t>(n0 + r) * K + gk] : 0.f;
+        }
+    };
+    if (kb < ke) fetch(kb);
+    for (int k0 = kb; k0 < ke; k0 += 16) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = threadIdx.x + 256 * u, r = i >> 4, k = i & 15;
+            as[k][r] = pa[u];
+            ws[k][r] = pw[u];
         }
         __syncthreads();
+        if (k0 + 16 < ke) fetch(k0 + 16);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             float av[4], wv[4];
@@ -53,6 +81,16 @@ __global__ void __launch_bounds__(256) gemm_kernel(const float *a, int M, int K,
             const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
             if (m < M && n < N) y[static_cast<size_t>(m) * N + n] = acc[i][j] + (bias ? bias[n] : 0.f);
         }
+}
+
+// y[i] = (sum over z in order of part[z][i]) + bias[i % N]
+__global__ void splitk_reduce_kernel(const float *part, int S, long long MN, int N, const float *bias, float *y) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < MN;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float v = 0.f;
+        for (int z = 0; z < S; ++z) v += part[static_cast<size_t>(z) * MN + i];
+        y[i] = v + (bias ? bias[i % N] : 0.f);
+    }
 }
 
 // col[r][c*K + k] = buf[r + k*dil][c]: the im2col rows of a causal
@@ -303,15 +341,16 @@ struct qtts_codec {
     CSnake act_out;
     CConv conv_out;
     // work buffers, grown on demand
-    float *buf[12] = {};
-    size_t cap[12] = {};
+    float *buf[13] = {};  // indexed by W_A .. W_PART
+    size_t cap[13] = {};
     int *d_codes = nullptr;
     size_t codes_cap = 0;
 };
 
 namespace {
 
-enum { W_A, W_B, W_BUF, W_COL, W_X1, W_X2, W_T1, W_T2, W_T3, W_T4, W_T5, W_T6 };
+enum { W_A, W_B, W_BUF, W_COL, W_X1, W_X2, W_T1, W_T2, W_T3, W_T4, W_T5, W_T6, W_PART };
+static_assert(W_PART < 13, "qtts_codec::buf holds every work buffer");
 
 int cx_scratch(qtts_codec *c, int i, size_t n, float **out) {
     if (c->cap[i] < n) {
@@ -415,8 +454,22 @@ void codec_free(qtts_codec *c) {
 
 int cx_gemm(qtts_codec *c, const float *a, int M, int K, const float *w, int N, const float *bias, float *y) {
     if (M <= 0) return QTTS_OK;
-    const dim3 grid((N + 63) / 64, (M + 63) / 64);
-    qcodec::gemm_kernel<<<grid, 256, 0, c->st>>>(a, M, K, w, N, bias, y);
+    const int S = (K + KC - 1) / KC;
+    if (S <= 1) {
+        const dim3 grid((N + 63) / 64, (M + 63) / 64);
+        qcodec::gemm_kernel<<<grid, 256, 0, c->st>>>(a, M, K, w, N, bias, y);
+        CK(cudaGetLastError());
+        return QTTS_OK;
+    }
+    // a long K: chunks of KC on their own CTAs, partials added in order
+    float *part;
+    const long long MN = static_cast<long long>(M) * N;
+    int rc = cx_scratch(c, W_PART, static_cast<size_t>(S) * MN, &part);
+    if (rc) return rc;
+    const dim3 grid((N + 63) / 64, (M + 63) / 64, S);
+    qcodec::gemm_kernel<<<grid, 256, 0, c->st>>>(a, M, K, w, N, nullptr, part);
+    CK(cudaGetLastError());
+    qcodec::splitk_reduce_kernel<<<blocks_for(MN), 256, 0, c->st>>>(part, S, MN, N, bias, y);
     CK(cudaGetLastError());
     return QTTS_OK;
 }
