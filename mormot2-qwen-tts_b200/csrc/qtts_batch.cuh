@@ -697,29 +697,34 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
     uint64_t *pending = nullptr;  // the barrier of a wait that gave up
     int t = 0;
     for (int kt = 0; kt < kend; kt += TA_KEYS, ++t) {
-        // K tile: thread = key row; V^T tile: thread = dim row
+        // K and V: thread = key row kp, read contiguously (one page lookup
+        // each); K goes to its K-major tile row by row, V to the transposed
+        // tile (dim rows, key columns) one half at a time
         {
             const int kp = kt + r;
+            const bool in = kp < kend;
+            const KVT *kr = in ? kv_at(pool, layer, it.seq, kp, 0, h) : nullptr;
+            const KVT *vr = in ? kv_at(pool, layer, it.seq, kp, 1, h) : nullptr;
+            // V^T element (dim d, key r): K-major tile of V^T, row d, column r
+            const int ra = r >> 6, rc = r & 63, rj = rc >> 3, rb = (rc & 7) * 2;
             for (int kk = 0; kk < HD; kk += 8) {
-                float v[8];
-                if (kp < kend) {
-                    const KVT *kr = kv_at(pool, layer, it.seq, kp, 0, h) + kk;
-                    const float4 a = load4(kr), b = load4(kr + 4);
+                float v[8], w[8];
+                if (in) {
+                    const float4 a = load4(kr + kk), b = load4(kr + kk + 4);
                     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                    const float4 c = load4(vr + kk), d = load4(vr + kk + 4);
+                    w[0] = c.x; w[1] = c.y; w[2] = c.z; w[3] = c.w; w[4] = d.x; w[5] = d.y; w[6] = d.z; w[7] = d.w;
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+                    for (int i = 0; i < 8; ++i) v[i] = w[i] = 0.f;
                 }
                 ta_store8(sm->kp, r, kk, v);
-            }
-            for (int kc = 0; kc < TA_KEYS; kc += 8) {
-                float v[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int p = kt + kc + i;
-                    v[i] = p < kend ? kv_val(kv_at(pool, layer, it.seq, p, 1, h) + r) : 0.f;
+                    const int d = kk + i;
+                    const uint32_t off = ra * (TA_ROWS * 128) + (d >> 3) * 1024 + (d & 7) * 128 + ((rj ^ (d & 7)) << 4) + rb;
+                    *reinterpret_cast<__half *>(sm->vt + off) = __float2half_rn(w[i]);
                 }
-                ta_store8(sm->vt, r, kc, v);
             }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
