@@ -2666,10 +2666,11 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
             }
             if (S > 1) ctok.push_back(t);
         } else if (n > TC_MIN_ROWS) {
-            // long runs of new rows: tensor-core attention, per query head
+            // long runs of new rows: tensor-core attention, per kv head (both
+            // of its query heads in one CTA)
             for (int qa = 0; qa < n; qa += TA_ROWS)
-                for (int qh = 0; qh < HQ; ++qh)
-                    titems.push_back({t, L0, qa, qa + TA_ROWS < n ? qa + TA_ROWS : n, qh, 0, L0 + n, sq, -1});
+                for (int h = 0; h < HKV; ++h)
+                    titems.push_back({t, L0, qa, qa + TA_ROWS < n ? qa + TA_ROWS : n, h, 0, L0 + n, sq, -1});
         } else {
             for (int qa = 0; qa < n; qa += AQB)
                 for (int h = 0; h < HKV; ++h)

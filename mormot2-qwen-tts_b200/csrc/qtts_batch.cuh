@@ -580,29 +580,35 @@ __global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, co
 // ------------------------------------------------------------------ prefill attention (tensor cores)
 //
 // Causal attention of long runs of new rows (prefill) on the 5th-generation
-// tensor cores, flash-attention style.  One CTA (128 threads) per (sequence,
-// query head, block of up to 128 new rows); thread r owns query row r.
-//  - Q (128 rows x 128 dims), the K tile (128 keys x 128 dims) and the V tile
+// tensor cores, flash-attention style.  One CTA (256 threads) per (sequence,
+// kv head, block of up to 128 new rows) takes both query heads of the kv
+// head, so each K/V tile is read and converted once for the two; thread
+// 128 g + r owns query row r of head 2h + g.
+//  - Q of both heads, the K tile (128 keys x 128 dims) and the V tile
 //    transposed (128 dims x 128 keys) are converted to fp16 by the threads
 //    and stored in the UMMA K-major 128B-swizzle layout (two 64-element
-//    atoms along K, as the GEMM's A tile); P takes the K tile's place.
-//  - S = Q K^T: 8 x tcgen05.mma (M 128, N 128, K 16) into 128 TMEM columns;
-//    thread r reads its row back (tcgen05.ld), masks causally, updates its
-//    running (max, sum) in f32, rescales its row of the O accumulator in
-//    TMEM (tcgen05.ld / st) and writes P = exp(S - max) as fp16 into the
-//    A-operand layout; then O += P V^T: 8 more MMAs into the other 128
-//    TMEM columns.  After the last tile, O / sum goes to attn16 as fp16.
+//    atoms along K, as the GEMM's A tile); thread (g, r) reads key row r of
+//    K and V contiguously, dims [64 g, 64 g + 64).
+//  - S_g = Q_g K^T: 8 x tcgen05.mma (M 128, N 128, K 16) per head into TMEM
+//    columns [128 g, 128 g + 128); row r of head g is read back by thread
+//    128 g + r (warps 4g..4g+3 reach TMEM lanes 0-127), masked causally, its
+//    running (max, sum) updated in f32, its row of O_g rescaled in TMEM
+//    (tcgen05.ld / st) and P_g = exp(S - max) written as fp16 in the
+//    A-operand layout (P_0 over the consumed K tile, P_1 in its own tile);
+//    then O_g += P_g V^T into columns [256 + 128 g, ...).  After the last
+//    tile, O_g / sum goes to attn16 as fp16.
+//  - 512 TMEM columns and 160 KB of shared memory: one CTA per SM.
 //  - every mbarrier wait is bounded; a timeout sets the error word.
-constexpr int TA_ROWS = 128;   // query rows per CTA (MMA M)
+constexpr int TA_ROWS = 128;   // query rows per CTA and head (MMA M)
 constexpr int TA_KEYS = 128;   // keys per tile (MMA N of S, K of P V^T)
-constexpr int TA_THREADS = 128;
+constexpr int TA_THREADS = 256;
 constexpr int TC_MIN_ROWS = 32;  // sequences with more new rows than this use this kernel
 constexpr int TA_TILE = TA_ROWS * HD * 2;  // 32 KB: one fp16 operand tile
 
-// 97 KB: two CTAs share an SM (and its 512 TMEM columns)
 struct __align__(1024) TaSmem {
-    uint8_t q[TA_TILE];
-    uint8_t kp[TA_TILE];  // the K tile, then (once S is computed) P
+    uint8_t q[2][TA_TILE];
+    uint8_t kp[TA_TILE];  // the K tile, then (once both S are computed) P of head 0
+    uint8_t p1[TA_TILE];  // P of head 1
     uint8_t vt[TA_TILE];
     uint64_t s_done, o_done;
     uint32_t tmem_base;
@@ -621,8 +627,6 @@ __device__ __forceinline__ void ta_store8(uint8_t *tile, int row, int kk, const 
     for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
     *reinterpret_cast<uint4 *>(tile + ta_off(row, kk)) = *reinterpret_cast<uint4 *>(h);
 }
-__device__ __forceinline__ float kv_val(const float *p) { return __ldg(p); }
-__device__ __forceinline__ float kv_val(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
     asm volatile(
@@ -647,31 +651,31 @@ __device__ __forceinline__ void ta_mma(uint32_t tmem_d, const uint8_t *a, const 
 }
 
 template <class KVT>
-__global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
+__global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
                                                                        KVPool<KVT> pool, int layer, __half *attn16,
                                                                        int *err) {
     extern __shared__ __align__(1024) uint8_t ta_raw[];
     TaSmem *sm = reinterpret_cast<TaSmem *>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int g = tid >> 7, r = tid & (TA_ROWS - 1);  // query head 2h + g, row r
     if (tid == 0) {
         mbar_init(&sm->s_done, 1);
         mbar_init(&sm->o_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {  // S: columns [0, 128), O: [128, 256)
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&sm->tmem_base))
+    if (warp == 0) {  // S_g: columns [128 g, 128 g + 128), O_g: [256 + 128 g, ...)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&sm->tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     pdl_trigger();
     pdl_wait();
     const AttnItem it = items[blockIdx.x];
-    const int qh = it.h, h = qh >> 1;          // query head, its kv head
-    const int nq = it.qb - it.qa;              // 1..128 rows
-    const int kend = it.L0 + it.qb;            // keys [0, kend) (causal)
-    const int r = tid;                         // this thread's query row
+    const int h = it.h, qh = 2 * h + g;  // kv head, this thread's query head
+    const int nq = it.qb - it.qa;        // 1..128 rows
+    const int kend = it.L0 + it.qb;      // keys [0, kend) (causal)
     const int qpos = it.L0 + it.qa + r;
-    // Q: row r, 128 dims
+    // Q: row r of head qh, 128 dims
     {
         const float *src = q32 + static_cast<size_t>(it.t0 + it.qa + (r < nq ? r : 0)) * QDIM + qh * HD;
         for (int kk = 0; kk < HD; kk += 8) {
@@ -683,23 +687,24 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[i] = 0.f;
             }
-            ta_store8(sm->q, r, kk, v);
+            ta_store8(sm->q[g], r, kk, v);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tm = sm->tmem_base, tm_s = tm, tm_o = tm + TA_KEYS;
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const uint32_t tm = sm->tmem_base, tm_s = tm + TA_KEYS * g, tm_o = tm + 2 * TA_KEYS + HD * g;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    uint8_t *ptile = g == 0 ? sm->kp : sm->p1;
     const float scale = 1.0f / sqrtf(static_cast<float>(HD));
     float m_run = -INFINITY, l_run = 0.f;
     bool failed = false;  // uniform over the CTA
     uint64_t *pending = nullptr;  // the barrier of a wait that gave up
     int t = 0;
     for (int kt = 0; kt < kend; kt += TA_KEYS, ++t) {
-        // K and V: thread = key row kp, read contiguously (one page lookup
-        // each); K goes to its K-major tile row by row, V to the transposed
-        // tile (dim rows, key columns) one half at a time
+        // K and V: thread (g, r) = key row kt + r, dims [64 g, 64 g + 64),
+        // read contiguously (one page lookup each); K goes to its K-major
+        // tile, V to the transposed tile (dim rows, key columns)
         {
             const int kp = kt + r;
             const bool in = kp < kend;
@@ -707,7 +712,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
             const KVT *vr = in ? kv_at(pool, layer, it.seq, kp, 1, h) : nullptr;
             // V^T element (dim d, key r): K-major tile of V^T, row d, column r
             const int ra = r >> 6, rc = r & 63, rj = rc >> 3, rb = (rc & 7) * 2;
-            for (int kk = 0; kk < HD; kk += 8) {
+            for (int kk = 64 * g; kk < 64 * g + 64; kk += 8) {
                 float v[8], w[8];
                 if (in) {
                     const float4 a = load4(kr + kk), b = load4(kr + kk + 4);
@@ -732,7 +737,8 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
         __syncthreads();
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm_s, sm->q, sm->kp, false);
+            ta_mma(tm, sm->q[0], sm->kp, false);
+            ta_mma(tm + TA_KEYS, sm->q[1], sm->kp, false);
             umma_commit(&sm->s_done);
         }
         bool good = mbar_wait(&sm->s_done, t & 1, nullptr);
@@ -750,8 +756,8 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
         }
         const float m_new = fmaxf(m_run, mt);
         const float corr = expf(m_run - m_new);  // 0 on the first tile
-        // P = exp(S - m) into the A-operand tile over K (the S product has
-        // completed: s_done), second pass over TMEM; row sum
+        // P = exp(S - m) (both S products have completed: s_done, so head 0
+        // may write over the K tile), second pass over TMEM; row sum
         float lt = 0.f;
         for (int c = 0; c < TA_KEYS; c += 32) {
             float sv[32];
@@ -763,7 +769,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
                 lt += e;
             }
 #pragma unroll
-            for (int g = 0; g < 4; ++g) ta_store8(sm->kp, r, c + 8 * g, sv + 8 * g);  // K is consumed
+            for (int q = 0; q < 4; ++q) ta_store8(ptile, r, c + 8 * q, sv + 8 * q);
         }
         l_run = fmaf(l_run, corr, lt);
         m_run = m_new;
@@ -783,7 +789,8 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
         __syncthreads();
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm_o, sm->kp, sm->vt, t > 0);
+            ta_mma(tm + 2 * TA_KEYS, sm->kp, sm->vt, t > 0);
+            ta_mma(tm + 2 * TA_KEYS + HD, sm->p1, sm->vt, t > 0);
             umma_commit(&sm->o_done);
         }
         if (good && !mbar_wait(&sm->o_done, t & 1, nullptr)) {
@@ -822,7 +829,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) attn_prefill_tc_kernel(const At
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tm) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tm) : "memory");
     }
 }
 
