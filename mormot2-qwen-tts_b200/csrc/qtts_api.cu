@@ -2678,6 +2678,10 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
         }
         t += n;
     }
+    // the longest tensor-core attention items first (their key count sets
+    // the work), so that the short ones fill the last wave
+    std::stable_sort(titems.begin(), titems.end(),
+                     [](const AttnItem &a, const AttnItem &c) { return a.L0 + a.qb > c.L0 + c.qb; });
     if (static_cast<size_t>(nparts) > b->max_parts)
         return set_err(QTTS_E_CAPACITY, "qtts_batch_forward: too many attention splits");
     // tok_seq | tok_pos | prefill items | decode items | cfirst | ccount | ctok | last

@@ -584,11 +584,13 @@ __global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, co
 // kv head, block of up to 128 new rows) takes both query heads of the kv
 // head, so each K/V tile is read and converted once for the two; thread
 // 128 g + r owns query row r of head 2h + g.
-//  - Q of both heads, the K tile (128 keys x 128 dims) and the V tile
-//    transposed (128 dims x 128 keys) are converted to fp16 by the threads
-//    and stored in the UMMA K-major 128B-swizzle layout (two 64-element
-//    atoms along K, as the GEMM's A tile); thread (g, r) reads key row r of
-//    K and V contiguously, dims [64 g, 64 g + 64).
+//  - Q of both heads, the K tile and the V tile (128 keys x 128 dims each)
+//    are converted to fp16 and stored in the UMMA 128B-swizzle layout (rows
+//    of 128 bytes, two 64-element atoms along the row, as the GEMM's A
+//    tile).  The loads are coalesced: a warp reads one 512-byte row per
+//    instruction, and the 16 key rows of one KV page per batch of loads.
+//    Q and K are K-major operands; V keeps its rows (keys) and serves as
+//    the MN-major B operand of P V, so nothing is transposed.
 //  - S_g = Q_g K^T: 8 x tcgen05.mma (M 128, N 128, K 16) per head into TMEM
 //    columns [128 g, 128 g + 128); row r of head g is read back by thread
 //    128 g + r (warps 4g..4g+3 reach TMEM lanes 0-127), masked causally, its
@@ -609,7 +611,7 @@ struct __align__(1024) TaSmem {
     uint8_t q[2][TA_TILE];
     uint8_t kp[TA_TILE];  // the K tile, then (once both S are computed) P of head 0
     uint8_t p1[TA_TILE];  // P of head 1
-    uint8_t vt[TA_TILE];
+    uint8_t vt[TA_TILE];  // the V tile (rows of keys)
     uint64_t s_done, o_done;
     uint32_t tmem_base;
 };
@@ -626,6 +628,15 @@ __device__ __forceinline__ void ta_store8(uint8_t *tile, int row, int kk, const 
 #pragma unroll
     for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
     *reinterpret_cast<uint4 *>(tile + ta_off(row, kk)) = *reinterpret_cast<uint4 *>(h);
+}
+
+// store 4 consecutive elements (half a 16-byte chunk) of row `row` from kk (kk % 4 == 0)
+__device__ __forceinline__ void ta_store4(uint8_t *tile, int row, int kk, float4 v) {
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t *>(&a);
+    u.y = *reinterpret_cast<const uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(tile + ta_off(row, kk)) = u;
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
@@ -649,6 +660,24 @@ __device__ __forceinline__ void ta_mma(uint32_t tmem_d, const uint8_t *a, const 
         umma_f16(tmem_d, da, db, idesc, (accumulate || k > 0) ? 1u : 0u);
     }
 }
+
+// thread 0: O += P V for one 128-key tile.  P (128 rows x 128 keys) is
+// K-major; V (128 keys x 128 dims, rows of dims) is the MN-major B operand:
+// 128B-swizzle atoms of 8 keys x 64 dims, the two dim atoms 16 KB apart
+// (leading byte offset), groups of 8 keys 1024 bytes apart (stride byte
+// offset); each K = 16 step moves two key groups (2048 bytes) on.
+__device__ __forceinline__ void ta_mma_pv(uint32_t tmem_d, const uint8_t *p, const uint8_t *v, bool accumulate) {
+    const uint32_t idesc = umma_idesc_f16(TA_ROWS, HD) | (1u << 16);  // B MN-major
+    const uint64_t lbo = (TA_ROWS * 128) >> 4, sbo = 1024 >> 4;
+#pragma unroll
+    for (int k = 0; k < TA_KEYS / 16; ++k) {
+        const uint64_t da = umma_desc_sw128(p + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
+        const uint64_t db = ((smem_u32(v + 2048 * k) >> 4) & 0x3FFFull) | (lbo << 16) | (sbo << 32) | (1ull << 46) |
+                            (2ull << 61);
+        umma_f16(tmem_d, da, db, idesc, (accumulate || k > 0) ? 1u : 0u);
+    }
+}
+static_assert(PAGE == 16 && TA_KEYS == 8 * PAGE, "one warp per KV page of a key tile");
 
 template <class KVT>
 __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
@@ -675,19 +704,21 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
     const int nq = it.qb - it.qa;        // 1..128 rows
     const int kend = it.L0 + it.qb;      // keys [0, kend) (causal)
     const int qpos = it.L0 + it.qa + r;
-    // Q: row r of head qh, 128 dims
+    // Q: warp w takes rows [32 (w % 4), +32) of head 2h + w / 4, one row
+    // per load (lane l: dims 4l..4l+3), 16 loads in flight
     {
-        const float *src = q32 + static_cast<size_t>(it.t0 + it.qa + (r < nq ? r : 0)) * QDIM + qh * HD;
-        for (int kk = 0; kk < HD; kk += 8) {
-            float v[8];
-            if (r < nq) {
-                const float4 a = load4(src + kk), b = load4(src + kk + 4);
-                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            } else {
+        const int wg = warp >> 2, wr = 32 * (warp & 3);
+        const float *src = q32 + static_cast<size_t>(it.t0 + it.qa) * QDIM + (2 * h + wg) * HD + 4 * (tid & 31);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        for (int half = 0; half < 2; ++half) {
+            float4 qb[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int row = wr + 16 * half + i;
+                qb[i] = row < nq ? load4(src + static_cast<size_t>(row) * QDIM) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            ta_store8(sm->q[g], r, kk, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ta_store4(sm->q[wg], wr + 16 * half + i, 4 * (tid & 31), qb[i]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -702,34 +733,28 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
     uint64_t *pending = nullptr;  // the barrier of a wait that gave up
     int t = 0;
     for (int kt = 0; kt < kend; kt += TA_KEYS, ++t) {
-        // K and V: thread (g, r) = key row kt + r, dims [64 g, 64 g + 64),
-        // read contiguously (one page lookup each); K goes to its K-major
-        // tile, V to the transposed tile (dim rows, key columns)
+        // K and V: warp w copies the KV page of keys [kt + 16 w, +16): one
+        // 512-byte row per load (lane l: dims 4l..4l+3), the page's 16 K rows
+        // and 16 V rows in flight together; rows past the causal end are 0
         {
-            const int kp = kt + r;
-            const bool in = kp < kend;
-            const KVT *kr = in ? kv_at(pool, layer, it.seq, kp, 0, h) : nullptr;
-            const KVT *vr = in ? kv_at(pool, layer, it.seq, kp, 1, h) : nullptr;
-            // V^T element (dim d, key r): K-major tile of V^T, row d, column r
-            const int ra = r >> 6, rc = r & 63, rj = rc >> 3, rb = (rc & 7) * 2;
-            for (int kk = 64 * g; kk < 64 * g + 64; kk += 8) {
-                float v[8], w[8];
-                if (in) {
-                    const float4 a = load4(kr + kk), b = load4(kr + kk + 4);
-                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-                    const float4 c = load4(vr + kk), d = load4(vr + kk + 4);
-                    w[0] = c.x; w[1] = c.y; w[2] = c.z; w[3] = c.w; w[4] = d.x; w[5] = d.y; w[6] = d.z; w[7] = d.w;
-                } else {
+            const int k0 = kt + PAGE * warp, nk = kend - k0;
+            const int lane = tid & 31;
+            float4 kb[PAGE], vb[PAGE];
+            if (nk > 0) {
+                const KVT *kr = kv_at(pool, layer, it.seq, k0, 0, h) + 4 * lane;
+                const KVT *vr = kv_at(pool, layer, it.seq, k0, 1, h) + 4 * lane;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = w[i] = 0.f;
-                }
-                ta_store8(sm->kp, r, kk, v);
+                for (int i = 0; i < PAGE; ++i) kb[i] = i < nk ? load4(kr + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int d = kk + i;
-                    const uint32_t off = ra * (TA_ROWS * 128) + (d >> 3) * 1024 + (d & 7) * 128 + ((rj ^ (d & 7)) << 4) + rb;
-                    *reinterpret_cast<__half *>(sm->vt + off) = __float2half_rn(w[i]);
-                }
+                for (int i = 0; i < PAGE; ++i) vb[i] = i < nk ? load4(vr + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+#pragma unroll
+                for (int i = 0; i < PAGE; ++i) kb[i] = vb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < PAGE; ++i) {
+                ta_store4(sm->kp, PAGE * warp + i, 4 * lane, kb[i]);
+                ta_store4(sm->vt, PAGE * warp + i, 4 * lane, vb[i]);
             }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -789,8 +814,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
         __syncthreads();
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm + 2 * TA_KEYS, sm->kp, sm->vt, t > 0);
-            ta_mma(tm + 2 * TA_KEYS + HD, sm->p1, sm->vt, t > 0);
+            ta_mma_pv(tm + 2 * TA_KEYS, sm->kp, sm->vt, t > 0);
+            ta_mma_pv(tm + 2 * TA_KEYS + HD, sm->p1, sm->vt, t > 0);
             umma_commit(&sm->o_done);
         }
         if (good && !mbar_wait(&sm->o_done, t & 1, nullptr)) {
