@@ -465,8 +465,13 @@ static int tensor_map_f16(CUtensorMap *map, const __half *base, int k, int rows_
 
 template <int WDT, int BN>
 static int gemm_attr() {
+    // the CTAs of one SM share its 228 KB (1 KB of it reserved per CTA)
+    static_assert(g_ctas_per_sm(WDT, BN) * (sizeof(GemmSmem<WDT, BN>) + 1024 + 1024) <= 228 * 1024,
+                  "GEMM CTAs per SM exceed the shared memory");
     CK(cudaFuncSetAttribute(gemm_kernel<WDT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             static_cast<int>(sizeof(GemmSmem<WDT, BN>) + 1024)));
+    CK(cudaFuncSetAttribute(gemm_kernel<WDT, BN>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                            cudaSharedmemCarveoutMaxShared));
     return QTTS_OK;
 }
 
@@ -501,23 +506,25 @@ static int gemm_launch_t(const GemmArgs &a, const __half *x, int rows_cap, dim3 
     int rc = tensor_map_f16(&map, x, a.K, rows_cap, BN);
     if (rc) return rc;
     if (grid.z > 1)
-        CK(launch_pdl_cluster(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, grid.z, a, map));
+        CK(launch_pdl_cluster(gemm_kernel<WDT, BN>, grid, dim3(g_threads(WDT)), smem, st, grid.z, a, map));
     else
-        CK(launch_pdl(gemm_kernel<WDT, BN>, grid, dim3(G_THREADS), smem, st, a, map));
+        CK(launch_pdl(gemm_kernel<WDT, BN>, grid, dim3(g_threads(WDT)), smem, st, a, map));
     return QTTS_OK;
 }
 
 // y[t][n] (+)= x[t][:] . w[n][:] for t < T (w tile-packed; x: fp16 [rows_cap][K] on the
 // device, rows_cap >= T).  With `add`, the products are added to y (residual);
 // otherwise y is overwritten.
-static int gemm_bn(int T) { return T <= 64 ? 64 : (T <= 128 ? 128 : 256); }
+// tokens per tile: float32 weights stop at 128 (two CTAs per SM, one's
+// epilogue under the other's main loop)
+static int gemm_bn(int T, int wdt) { return T <= 64 ? 64 : (T <= 128 || wdt == WDT_F32 ? 128 : 256); }
 
 // the K split of a GEMM: CTAs up to about one per SM, at most 8 per tile
 // (a portable cluster; clusters of 16 measured slower: 9.38 vs 7.79 ms per
 // B=64 frame)
-static int gemm_split(int n_rows, int k, int T) {
+static int gemm_split(int n_rows, int k, int T, int wdt) {
     const int cap = 8;
-    const int bn = gemm_bn(T);
+    const int bn = gemm_bn(T, wdt);
     const int tiles = ((n_rows + G_BM - 1) / G_BM) * ((T + bn - 1) / bn);
     const int kb = k / G_BK;
     int split = 1;
@@ -543,8 +550,8 @@ struct QkvEpi {
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
                 bool add, int *err, cudaStream_t st, __half *swiglu16 = nullptr, const QkvEpi *qe = nullptr) {
     if (k % G_BK != 0) return set_err(QTTS_E_ARG, "gemm: K %d is not a multiple of %d", k, G_BK);
-    const int bn = gemm_bn(T);
-    const int split = gemm_split(n_rows, k, T);
+    const int bn = gemm_bn(T, wdt);
+    const int split = gemm_split(n_rows, k, T, wdt);
     GemmArgs a;
     a.w = w;
     a.n_rows = n_rows;

@@ -45,7 +45,7 @@ namespace qtts {
 
 constexpr int G_BM = 128;           // weight rows per CTA tile
 constexpr int G_BK = 64;            // K per stage (128 bytes of fp16)
-constexpr int G_THREADS = 384;   // warps 0-7 dequantise, 8 loads, 9 issues MMAs, 8-11 read TMEM back
+constexpr int G_THREADS = 384;   // Q8_0: warps 0-7 dequantise, 8 loads, 9 issues MMAs, 8-11 read TMEM back
 constexpr int G_DQ = 256;        // dequantising threads: 2 per weight row
 constexpr int G_A_BYTES = G_BM * G_BK * 2;  // 16 KB
 
@@ -64,12 +64,24 @@ __host__ __device__ constexpr int g_raw_bytes(int wdt) { return wdt == WDT_Q8 ? 
 // A tiles per stage: hi + lo (both formats: the weight enters the product to
 // ~2^-22 of its value, not fp16's 2^-11)
 __host__ __device__ constexpr int g_a_tiles(int) { return 2; }
+// threads of a CTA: float32 tiles need no dequantisers, so their CTA is the
+// four warps that load (warp 0), issue the MMAs (warp 1) and read TMEM back
+// (warps 0-3); Q8_0 adds eight dequantising warps in front (loader warp 8)
+__host__ __device__ constexpr int g_threads(int wdt) { return wdt == WDT_Q8 ? G_THREADS : 128; }
+__host__ __device__ constexpr int g_warp0(int wdt) { return wdt == WDT_Q8 ? 8 : 0; }
+// float32 tiles of up to 128 tokens run two CTAs per SM (BN TMEM columns and
+// under 113 KB of shared memory each), so that one CTA's epilogue overlaps
+// the other's main loop; the others run one CTA per SM
+__host__ __device__ constexpr int g_ctas_per_sm(int wdt, int bn) { return wdt == WDT_F32 && bn <= 128 ? 2 : 1; }
 // pipeline depth from the shared-memory budget (at most 6 stages)
 __host__ __device__ constexpr int g_stage_bytes(int wdt, int bn) {
     return g_raw_bytes(wdt) + g_a_tiles(wdt) * G_A_BYTES + bn * 128;
 }
+__host__ __device__ constexpr int g_stage_budget(int wdt, int bn) {
+    return g_ctas_per_sm(wdt, bn) == 2 ? 100 * 1024 : 220 * 1024;
+}
 __host__ __device__ constexpr int g_stages(int wdt, int bn) {
-    return (220 * 1024) / g_stage_bytes(wdt, bn) < 6 ? (220 * 1024) / g_stage_bytes(wdt, bn) : 6;
+    return g_stage_budget(wdt, bn) / g_stage_bytes(wdt, bn) < 6 ? g_stage_budget(wdt, bn) / g_stage_bytes(wdt, bn) : 6;
 }
 
 struct GemmArgs {
@@ -165,6 +177,7 @@ struct __align__(1024) GemmSmem {
     uint32_t tmem_base;
     static_assert(S * (g_a_tiles(WDT) * G_A_BYTES + BN * 128) >= G_BM * BN * 4,
                   "the split-K partial tile must fit in the stage buffers");
+    static_assert(S >= 2, "at least two pipeline stages");
 };
 
 // row-packed matrix (Q8_0: [K int8][K/32 fp16] per row; f32 rows) -> the
@@ -268,10 +281,11 @@ __device__ __forceinline__ void gemm_fail(int *err) {
 // ------------------------------------------------------------------ kernel
 
 template <int WDT, int BN>
-__global__ void __launch_bounds__(G_THREADS, 1)
+__global__ void __launch_bounds__(g_threads(WDT), g_ctas_per_sm(WDT, BN))
     gemm_kernel(const GemmArgs args, const __grid_constant__ CUtensorMap xmap) {
     using Smem = GemmSmem<WDT, BN>;
     constexpr int S = Smem::S;
+    constexpr int NT = g_threads(WDT), W0 = g_warp0(WDT);  // W0: loader, W0 + 1: MMA, W0..W0+3: epilogue
     constexpr uint32_t CHUNK = g_chunk_bytes(WDT);
     extern __shared__ __align__(1024) uint8_t gsmem_raw[];
     // the dynamic window is aligned up to 1024 bytes (the swizzle atom)
@@ -289,7 +303,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         mbar_init(&sm->accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 9) {  // TMEM: BN f32 columns for the 128 x BN accumulator
+    if (warp == W0 + 1) {  // TMEM: BN f32 columns for the 128 x BN accumulator
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
                      "n"(BN)
                      : "memory");
@@ -349,7 +363,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&sm->full_a[s]);
         }
-    } else if (warp == 8) {
+    } else if (warp == W0) {
         // ---- producer: the weight chunk (bulk copy) and the activations (TMA)
         if (lane == 0) {
             const uint8_t *wt = args.w + (static_cast<size_t>(blockIdx.x) * kb_total + kb0) * CHUNK;
@@ -378,7 +392,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 issued = i + 1;  // (a break happens at i >= S: every stage before it has both copies)
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == W0 + 1) {
         // ---- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(G_BM, BN);
@@ -404,12 +418,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             umma_commit(&sm->accum);
         }
     }
-    // ---- epilogue: warps 8-11, TMEM lane quarter = warp % 4
-    if (warp >= 8) {
+    // ---- epilogue: warps W0..W0+3, TMEM lane quarter = warp % 4
+    if (warp >= W0) {
         pdl_wait();  // out may be written by the previous kernels
         const bool good = mbar_wait(&sm->accum, 0, nullptr);
         if (!good) gemm_fail(args.err);
-        __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of warps 8/9 had other work
+        __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of the loader and MMA warps had other work
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int q = warp & 3;
         const int n = row0 + 32 * q + lane;
@@ -474,7 +488,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         pdl_wait();  // the pages and q32 may be read by the previous kernels
         const float *part = reinterpret_cast<const float *>(sm);
         const int per = BN / ks, head = row0 / G_BM;
-        for (int i = warp; i < per; i += G_THREADS / 32) {
+        for (int i = warp; i < per; i += NT / 32) {
             const int col = z * per + i, t = tok0 + col;
             if (t >= args.T) continue;
             float x[4] = {0.f, 0.f, 0.f, 0.f};
@@ -505,7 +519,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             // gate/up pairs (rows 2j, 2j+1; a chunk of rows_z >= 16 rows
             // holds whole pairs): fp16(silu(gate) * up) as the unsplit epilogue
             const int pz = rows_z / 2;
-            for (int idx = tid; idx < pz * BN; idx += G_THREADS) {
+            for (int idx = tid; idx < pz * BN; idx += NT) {
                 const int rr = rz0 + 2 * (idx % pz), col = idx / pz;
                 float g = 0.f, u = 0.f;
                 for (int r = 0; r < ks; ++r) {
@@ -520,7 +534,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 }
             }
         } else {
-            for (int idx = tid; idx < rows_z * BN; idx += G_THREADS) {
+            for (int idx = tid; idx < rows_z * BN; idx += NT) {
                 const int rr = rz0 + idx % rows_z, col = idx / rows_z;
                 float sum = 0.f;
                 for (int r = 0; r < ks; ++r)
@@ -534,7 +548,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         cl.sync();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == W0 && lane == 0) {
         // drain: wait (bounded) for the copies of the last S issued stages
         for (int i = issued > S ? issued - S : 0; i < issued; ++i) {
             const int s = i % S;
@@ -546,7 +560,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 9) {
+    if (warp == W0 + 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(BN) : "memory");
     }
