@@ -114,24 +114,26 @@ struct GemmArgs {
 
 constexpr int G_PAGE = 16;  // positions per page of the paged KV cache
 
-// the QKV epilogue of token t (one warp): x[4] = this lane's dims 4L..4L+3
-// of head `head` (0-15 q, 16-23 k, 24-31 v)
-__device__ __forceinline__ void qkv_token_epilogue(const GemmArgs &a, int head, int t, float x[4], int lane) {
-    const int seq = a.tok_seq[t], pos = a.tok_pos[t];
+// the QKV epilogue of token t at position pos (one warp): x[4] = this
+// lane's dims 4L..4L+3 of head `head` (0-15 q, 16-23 k, 24-31 v); page: the
+// KV page that holds pos (k and v heads)
+__device__ __forceinline__ void qkv_token_epilogue(const GemmArgs &a, int head, int t, int pos, int page, float x[4],
+                                                   int lane) {
     if (head < 24) {
+        // the RoPE row first: its loads overlap the norm's reduction
+        const int half = HD / 2, e0 = (4 * lane) & (half - 1);
+        const float4 cs = *reinterpret_cast<const float4 *>(a.rope_cos + static_cast<size_t>(pos) * half + e0);
+        const float4 sn = *reinterpret_cast<const float4 *>(a.rope_sin + static_cast<size_t>(pos) * half + e0);
         const float *nw = head < 16 ? a.q_norm : a.k_norm;
+        const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
         float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(HD) + a.eps);
-        const float4 g = *reinterpret_cast<const float4 *>(nw + 4 * lane);
         x[0] = g.x * (x[0] * inv);
         x[1] = g.y * (x[1] * inv);
         x[2] = g.z * (x[2] * inv);
         x[3] = g.w * (x[3] * inv);
-        const int half = HD / 2, e0 = (4 * lane) & (half - 1);
-        const float4 cs = *reinterpret_cast<const float4 *>(a.rope_cos + static_cast<size_t>(pos) * half + e0);
-        const float4 sn = *reinterpret_cast<const float4 *>(a.rope_sin + static_cast<size_t>(pos) * half + e0);
         const float cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
         float o[4];
 #pragma unroll
@@ -148,7 +150,6 @@ __device__ __forceinline__ void qkv_token_epilogue(const GemmArgs &a, int head, 
         return;
     }
     const int which = head < 24 ? 0 : 1, kvh = head < 24 ? head - 16 : head - 24;
-    const int page = a.kv_pages[seq * a.kv_mpps + pos / G_PAGE];
     const size_t e = ((((static_cast<size_t>(page) * a.kv_layers + a.kv_layer) * 2 + which) * HKV + kvh) * G_PAGE +
                       pos % G_PAGE) * HD + 4 * lane;
     if (a.kv_bf16) {
@@ -433,13 +434,16 @@ __global__ void __launch_bounds__(g_threads(WDT), g_ctas_per_sm(WDT, BN))
             tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
             if (args.swiglu16 && args.ksplit == 1) {
                 // the up row of a pair is the next lane: SiLU(gate) * up, as
-                // the separate SwiGLU kernel computes it
+                // the separate SwiGLU kernel computes it.  Of two columns, the
+                // even lane finishes the first and the odd lane the second
+                // (each sends the partner the value it lacks)
+                const bool odd = lane & 1;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);
-                    const int t = tok0 + c + j;
-                    if (good && n < args.n_rows && (lane & 1) == 0 && t < args.T) {
-                        const float g = v[j];
+                for (int j = 0; j < 32; j += 2) {
+                    const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+                    const float g = odd ? recv : v[j], up = odd ? v[j + 1] : recv;
+                    const int t = tok0 + c + j + (odd ? 1 : 0);
+                    if (good && (n & ~1) < args.n_rows && t < args.T) {
                         const float sl = g / (1.0f + expf(-g));
                         args.swiglu16[static_cast<size_t>(t) * args.ld16 + (n >> 1)] = __float2half_rn(sl * up);
                     }
@@ -487,21 +491,37 @@ __global__ void __launch_bounds__(g_threads(WDT), g_ctas_per_sm(WDT, BN))
         }
         pdl_wait();  // the pages and q32 may be read by the previous kernels
         const float *part = reinterpret_cast<const float *>(sm);
-        const int per = BN / ks, head = row0 / G_BM;
-        for (int i = warp; i < per; i += NT / 32) {
-            const int col = z * per + i, t = tok0 + col;
-            if (t >= args.T) continue;
-            float x[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int r = 0; r < ks; ++r) {
-                const float *src = part + col * G_BM + 4 * lane;
-                if (ks > 1) src = cg::this_cluster().map_shared_rank(src, static_cast<unsigned>(r));
-                const float4 v = *reinterpret_cast<const float4 *>(src);
-                x[0] += v.x;
-                x[1] += v.y;
-                x[2] += v.z;
-                x[3] += v.w;
+        const int per = BN / ks, head = row0 / G_BM, nw = NT / 32;
+        // a warp takes tokens i = warp + nw m; their positions and pages are
+        // fetched 32 at a time (lane j: the round's j-th token), then passed
+        // around by shuffles
+        for (int i0 = warp; i0 < per; i0 += 32 * nw) {
+            int my_pos = 0, my_page = 0;
+            {
+                const int ij = i0 + nw * lane, tj = tok0 + z * per + ij;
+                if (ij < per && tj < args.T) {
+                    my_pos = args.tok_pos[tj];
+                    if (head >= 16) my_page = args.kv_pages[args.tok_seq[tj] * args.kv_mpps + my_pos / G_PAGE];
+                }
             }
-            qkv_token_epilogue(args, head, t, x, lane);
+            for (int m = 0; m < 32; ++m) {
+                const int i = i0 + nw * m;
+                if (i >= per) break;  // uniform over the warp
+                const int col = z * per + i, t = tok0 + col;
+                const int pos = __shfl_sync(0xffffffffu, my_pos, m), page = __shfl_sync(0xffffffffu, my_page, m);
+                if (t >= args.T) continue;
+                float x[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int r = 0; r < ks; ++r) {
+                    const float *src = part + col * G_BM + 4 * lane;
+                    if (ks > 1) src = cg::this_cluster().map_shared_rank(src, static_cast<unsigned>(r));
+                    const float4 v = *reinterpret_cast<const float4 *>(src);
+                    x[0] += v.x;
+                    x[1] += v.y;
+                    x[2] += v.z;
+                    x[3] += v.w;
+                }
+                qkv_token_epilogue(args, head, t, pos, page, x, lane);
+            }
         }
         if (ks > 1) cg::this_cluster().sync();
     } else if (args.ksplit > 1) {
