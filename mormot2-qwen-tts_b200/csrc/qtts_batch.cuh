@@ -727,8 +727,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
     const uint32_t tm = sm->tmem_base, tm_s = tm + TA_KEYS * g, tm_o = tm + 2 * TA_KEYS + HD * g;
     const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     uint8_t *ptile = g == 0 ? sm->kp : sm->p1;
-    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = (1.0f / sqrtf(static_cast<float>(HD))) * 1.44269504088896341f;  // scale log2(e)
+    float m_run = -INFINITY, l_run = 0.f;  // running maximum of the raw scores, sum of exponentials
     bool failed = false;  // uniform over the CTA
     uint64_t *pending = nullptr;  // the barrier of a wait that gave up
     int t = 0;
@@ -770,36 +770,49 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
         if (!good) pending = &sm->s_done;
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // row maximum of the masked, scaled scores (first pass over TMEM)
-        float mt = -INFINITY;
+        // row maximum of the raw scores (first pass over TMEM; scale > 0, so
+        // it gives the maximum of the scaled ones).  Only a tile with a key
+        // past the block's first row is masked; four partial maxima (and
+        // sums below) keep the dependency chains short
+        const bool diag = kt + TA_KEYS - 1 > it.L0 + it.qa;
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         for (int c = 0; c < TA_KEYS; c += 32) {
             float sv[32];
             tmem_ld32(tm_s + lane_base + c, sv);
+            if (diag) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (kt + c + j <= qpos) mt = fmaxf(mt, sv[j] * scale);
+                for (int j = 0; j < 32; ++j)
+                    if (kt + c + j <= qpos) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+            }
         }
-        const float m_new = fmaxf(m_run, mt);
-        const float corr = expf(m_run - m_new);  // 0 on the first tile
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+        // exp(scale (s - m)) = exp2(s sl2 - m sl2), sl2 = scale log2(e)
+        const float ms = m_new * sl2;
+        const float corr = exp2f(fmaf(m_run, sl2, -ms));  // 0 on the first tile (m_run = -inf)
         // P = exp(S - m) (both S products have completed: s_done, so head 0
         // may write over the K tile), second pass over TMEM; row sum
-        float lt = 0.f;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
         for (int c = 0; c < TA_KEYS; c += 32) {
             float sv[32];
             tmem_ld32(tm_s + lane_base + c, sv);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                const float e = kt + c + j <= qpos ? expf(sv[j] * scale - m_new) : 0.f;
+                float e = exp2f(fmaf(sv[j], sl2, -ms));
+                if (diag && kt + c + j > qpos) e = 0.f;
                 sv[j] = e;
-                lt += e;
+                ls[j & 3] += e;
             }
 #pragma unroll
             for (int q = 0; q < 4; ++q) ta_store8(ptile, r, c + 8 * q, sv + 8 * q);
         }
-        l_run = fmaf(l_run, corr, lt);
+        l_run = fmaf(l_run, corr, (ls[0] + ls[1]) + (ls[2] + ls[3]));
         m_run = m_new;
-        if (t > 0) {
-            // rescale this row of the O accumulator
+        // rescale this row of the O accumulator, unless no row of the warp
+        // has a new maximum (TMEM loads and stores are warp-wide)
+        if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
             for (int c = 0; c < HD; c += 32) {
                 float ov[32];
                 tmem_ld32(tm_o + lane_base + c, ov);
