@@ -580,41 +580,47 @@ __global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, co
 // ------------------------------------------------------------------ prefill attention (tensor cores)
 //
 // Causal attention of long runs of new rows (prefill) on the 5th-generation
-// tensor cores, flash-attention style.  One CTA (256 threads) per (sequence,
-// kv head, block of up to 128 new rows) takes both query heads of the kv
-// head, so each K/V tile is read and converted once for the two; thread
-// 128 g + r owns query row r of head 2h + g.
-//  - Q of both heads, the K tile and the V tile (128 keys x 128 dims each)
-//    are converted to fp16 and stored in the UMMA 128B-swizzle layout (rows
-//    of 128 bytes, two 64-element atoms along the row, as the GEMM's A
-//    tile).  The loads are coalesced: a warp reads one 512-byte row per
-//    instruction, and the 16 key rows of one KV page per batch of loads.
-//    Q and K are K-major operands; V keeps its rows (keys) and serves as
-//    the MN-major B operand of P V, so nothing is transposed.
-//  - S_g = Q_g K^T: 8 x tcgen05.mma (M 128, N 128, K 16) per head into TMEM
-//    columns [128 g, 128 g + 128); row r of head g is read back by thread
-//    128 g + r (warps 4g..4g+3 reach TMEM lanes 0-127), masked causally, its
-//    running (max, sum) updated in f32, its row of O_g rescaled in TMEM
-//    (tcgen05.ld / st) and P_g = exp(S - max) written as fp16 in the
-//    A-operand layout (P_0 over the consumed K tile, P_1 in its own tile);
-//    then O_g += P_g V^T into columns [256 + 128 g, ...).  After the last
-//    tile, O_g / sum goes to attn16 as fp16.
-//  - 512 TMEM columns and 160 KB of shared memory: one CTA per SM.
-//  - every mbarrier wait is bounded; a timeout sets the error word.
+// tensor cores, flash-attention style.  One CTA per (sequence, kv head,
+// block of up to 128 new rows) takes both query heads of the kv head, so
+// each K/V tile is read and converted once for the two.
+//  - warps 8-11 (loaders) copy the K and V tiles (128 keys x 128 dims) of
+//    the key tiles in turn into two buffers, converted to fp16 in the UMMA
+//    128B-swizzle layout (rows of 128 bytes, two 64-element atoms along the
+//    row): a warp takes two KV pages, one 512-byte row per load, so tile
+//    t + 1 is on its way while tile t is in the products and the softmax.
+//    Q and K are K-major operands; V keeps its rows (keys) and serves as the
+//    MN-major B operand of P V, so nothing is transposed.
+//  - warps 0-7: thread 128 g + r owns query row r of head 2h + g.  S_g =
+//    Q_g K^T (8 x tcgen05.mma, M 128, N 128, K 16) lands in TMEM columns
+//    [128 g, +128); row r is read back by its thread (warps 4g..4g+3 reach
+//    TMEM lanes 0-127), masked causally on the diagonal tile, its running
+//    (max, sum) updated in f32, its row of O_g rescaled in TMEM when the
+//    maximum moved, and P_g = exp(S - max) written as fp16 in the A-operand
+//    layout (P_0 over the consumed K tile, P_1 in its own tile); then O_g +=
+//    P_g V into columns [256 + 128 g, +128).  After the last tile, O_g / sum
+//    goes to attn16 as fp16.
+//  - 512 TMEM columns and 225 KB of shared memory: one CTA per SM.
+//  - every mbarrier wait is bounded; a timeout sets the error word, and the
+//    MMA thread waits (bounded) for its own products before TMEM is freed.
 constexpr int TA_ROWS = 128;   // query rows per CTA and head (MMA M)
-constexpr int TA_KEYS = 128;   // keys per tile (MMA N of S, K of P V^T)
-constexpr int TA_THREADS = 256;
+constexpr int TA_KEYS = 128;   // keys per tile (MMA N of S, K of P V)
+constexpr int TA_CONSUMERS = 256;  // warps 0-7
+constexpr int TA_LOADERS = 128;    // warps 8-11
+constexpr int TA_THREADS = TA_CONSUMERS + TA_LOADERS;
 constexpr int TC_MIN_ROWS = 32;  // sequences with more new rows than this use this kernel
 constexpr int TA_TILE = TA_ROWS * HD * 2;  // 32 KB: one fp16 operand tile
 
 struct __align__(1024) TaSmem {
     uint8_t q[2][TA_TILE];
-    uint8_t kp[TA_TILE];  // the K tile, then (once both S are computed) P of head 0
-    uint8_t p1[TA_TILE];  // P of head 1
-    uint8_t vt[TA_TILE];  // the V tile (rows of keys)
-    uint64_t s_done, o_done;
+    uint8_t kp[2][TA_TILE];  // buffer b: the K tile, then (once both S are computed) P of head 0
+    uint8_t v[2][TA_TILE];   // buffer b: the V tile (rows of keys)
+    uint8_t p1[TA_TILE];     // P of head 1
+    uint64_t kv_full[2];     // the loaders' arrivals (TA_LOADERS)
+    uint64_t kv_free[2];     // tcgen05.commit after the P V products that read buffer b
+    uint64_t s_done, o_done, fin;
     uint32_t tmem_base;
 };
+static_assert(sizeof(TaSmem) + 1024 <= 232448, "prefill attention: shared memory above 227 KB");
 
 // byte offset of element (row, kk) of a 128 x 128 fp16 operand tile in the
 // K-major 128B-swizzle layout (atoms of 64 K elements, 16 KB each)
@@ -679,17 +685,32 @@ __device__ __forceinline__ void ta_mma_pv(uint32_t tmem_d, const uint8_t *p, con
 }
 static_assert(PAGE == 16 && TA_KEYS == 8 * PAGE, "one warp per KV page of a key tile");
 
+// consumer warps only: bar.sync on barrier 1 that also ORs a flag over them
+__device__ __forceinline__ bool ta_consumers_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "n"(TA_CONSUMERS)
+        : "memory");
+    return r != 0;
+}
+
 template <class KVT>
 __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
                                                                        KVPool<KVT> pool, int layer, __half *attn16,
                                                                        int *err) {
     extern __shared__ __align__(1024) uint8_t ta_raw[];
     TaSmem *sm = reinterpret_cast<TaSmem *>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int g = tid >> 7, r = tid & (TA_ROWS - 1);  // query head 2h + g, row r
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm->kv_full[b], TA_LOADERS);
+            mbar_init(&sm->kv_free[b], 1);
+        }
         mbar_init(&sm->s_done, 1);
         mbar_init(&sm->o_done, 1);
+        mbar_init(&sm->fin, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {  // S_g: columns [128 g, 128 g + 128), O_g: [256 + 128 g, ...)
@@ -700,15 +721,15 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
     pdl_trigger();
     pdl_wait();
     const AttnItem it = items[blockIdx.x];
-    const int h = it.h, qh = 2 * h + g;  // kv head, this thread's query head
+    const int h = it.h;                  // kv head
     const int nq = it.qb - it.qa;        // 1..128 rows
     const int kend = it.L0 + it.qb;      // keys [0, kend) (causal)
-    const int qpos = it.L0 + it.qa + r;
-    // Q: warp w takes rows [32 (w % 4), +32) of head 2h + w / 4, one row
-    // per load (lane l: dims 4l..4l+3), 16 loads in flight
-    {
+    const int ntiles = (kend + TA_KEYS - 1) / TA_KEYS;
+    if (warp < 8) {
+        // Q: warp w takes rows [32 (w % 4), +32) of head 2h + w / 4, one row
+        // per load (lane l: dims 4l..4l+3), 16 loads in flight
         const int wg = warp >> 2, wr = 32 * (warp & 3);
-        const float *src = q32 + static_cast<size_t>(it.t0 + it.qa) * QDIM + (2 * h + wg) * HD + 4 * (tid & 31);
+        const float *src = q32 + static_cast<size_t>(it.t0 + it.qa) * QDIM + (2 * h + wg) * HD + 4 * lane;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             float4 qb[16];
@@ -718,133 +739,152 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
                 qb[i] = row < nq ? load4(src + static_cast<size_t>(row) * QDIM) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ta_store4(sm->q[wg], wr + 16 * half + i, 4 * (tid & 31), qb[i]);
+            for (int i = 0; i < 16; ++i) ta_store4(sm->q[wg], wr + 16 * half + i, 4 * lane, qb[i]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tm = sm->tmem_base, tm_s = tm + TA_KEYS * g, tm_o = tm + 2 * TA_KEYS + HD * g;
-    const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    uint8_t *ptile = g == 0 ? sm->kp : sm->p1;
-    const float sl2 = (1.0f / sqrtf(static_cast<float>(HD))) * 1.44269504088896341f;  // scale log2(e)
-    float m_run = -INFINITY, l_run = 0.f;  // running maximum of the raw scores, sum of exponentials
-    bool failed = false;  // uniform over the CTA
-    uint64_t *pending = nullptr;  // the barrier of a wait that gave up
-    int t = 0;
-    for (int kt = 0; kt < kend; kt += TA_KEYS, ++t) {
-        // K and V: warp w copies the KV page of keys [kt + 16 w, +16): one
-        // 512-byte row per load (lane l: dims 4l..4l+3), the page's 16 K rows
-        // and 16 V rows in flight together; rows past the causal end are 0
-        {
-            const int k0 = kt + PAGE * warp, nk = kend - k0;
-            const int lane = tid & 31;
-            float4 kb[PAGE], vb[PAGE];
-            if (nk > 0) {
-                const KVT *kr = kv_at(pool, layer, it.seq, k0, 0, h) + 4 * lane;
-                const KVT *vr = kv_at(pool, layer, it.seq, k0, 1, h) + 4 * lane;
-#pragma unroll
-                for (int i = 0; i < PAGE; ++i) kb[i] = i < nk ? load4(kr + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int i = 0; i < PAGE; ++i) vb[i] = i < nk ? load4(vr + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-            } else {
-#pragma unroll
-                for (int i = 0; i < PAGE; ++i) kb[i] = vb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t tm = sm->tmem_base;
+    if (warp >= 8) {
+        // ---- loaders: tile t into buffer t % 2 once the P V products of
+        // tile t - 2 (the last to read it) are complete; warp 8 + j copies
+        // KV pages 2j and 2j + 1 of the tile (16 keys each), K then V, a
+        // page's 16 rows in flight together; rows past the causal end are 0
+        const int lw = warp - 8;
+        for (int t = 0; t < ntiles; ++t) {
+            const int b = t & 1, kt = t * TA_KEYS;
+            if (t >= 2 && !mbar_wait(&sm->kv_free[b], ((t >> 1) - 1) & 1, nullptr)) {
+                atomicCAS(err, 0, ERR_TIMEOUT);
+                break;
             }
+#pragma unroll 1
+            for (int pg = 2 * lw; pg < 2 * lw + 2; ++pg) {
+                const int k0 = kt + PAGE * pg, nk = kend - k0;
+#pragma unroll 1
+                for (int which = 0; which < 2; ++which) {
+                    float4 rb[PAGE];
+                    if (nk > 0) {
+                        const KVT *src = kv_at(pool, layer, it.seq, k0, which, h) + 4 * lane;
 #pragma unroll
-            for (int i = 0; i < PAGE; ++i) {
-                ta_store4(sm->kp, PAGE * warp + i, 4 * lane, kb[i]);
-                ta_store4(sm->vt, PAGE * warp + i, 4 * lane, vb[i]);
+                        for (int i = 0; i < PAGE; ++i)
+                            rb[i] = i < nk ? load4(src + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < PAGE; ++i) rb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    uint8_t *dst = which == 0 ? sm->kp[b] : sm->v[b];
+#pragma unroll
+                    for (int i = 0; i < PAGE; ++i) ta_store4(dst, PAGE * pg + i, 4 * lane, rb[i]);
+                }
             }
+            // the tensor core reads the tiles through the async proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&sm->kv_full[b]);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
+    } else {
+        // ---- consumers
+        const int g = tid >> 7, r = tid & (TA_ROWS - 1);  // query head 2h + g, row r
+        const int qh = 2 * h + g;
+        const int qpos = it.L0 + it.qa + r;
+        const uint32_t tm_s = tm + TA_KEYS * g, tm_o = tm + 2 * TA_KEYS + HD * g;
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const float sl2 = (1.0f / sqrtf(static_cast<float>(HD))) * 1.44269504088896341f;  // scale log2(e)
+        float m_run = -INFINITY, l_run = 0.f;  // running maximum of the raw scores, sum of exponentials
+        bool failed = false;
+        for (int t = 0; t < ntiles; ++t) {
+            const int b = t & 1, kt = t * TA_KEYS;
+            bool good = true;
+            if (tid == 0) {
+                // S_0, S_1 of tile t once it has landed (S's TMEM columns were
+                // read by every consumer before the last consumer barrier)
+                good = mbar_wait(&sm->kv_full[b], (t >> 1) & 1, nullptr);
+                if (good) {
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    ta_mma(tm, sm->q[0], sm->kp[b], false);
+                    ta_mma(tm + TA_KEYS, sm->q[1], sm->kp[b], false);
+                    umma_commit(&sm->s_done);
+                }
+            }
+            good = mbar_wait(&sm->s_done, t & 1, nullptr) && good;
+            __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma(tm, sm->q[0], sm->kp, false);
-            ta_mma(tm + TA_KEYS, sm->q[1], sm->kp, false);
-            umma_commit(&sm->s_done);
+            // row maximum of the raw scores (first pass over TMEM; scale > 0,
+            // so it gives the maximum of the scaled ones).  Only a tile with a
+            // key past the block's first row is masked; four partial maxima
+            // (and sums below) keep the dependency chains short
+            const bool diag = kt + TA_KEYS - 1 > it.L0 + it.qa;
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            for (int c = 0; c < TA_KEYS; c += 32) {
+                float sv[32];
+                tmem_ld32(tm_s + lane_base + c, sv);
+                if (diag) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (kt + c + j <= qpos) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+                }
+            }
+            const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+            // exp(scale (s - m)) = exp2(s sl2 - m sl2), sl2 = scale log2(e)
+            const float ms = m_new * sl2;
+            const float corr = exp2f(fmaf(m_run, sl2, -ms));  // 0 on the first tile (m_run = -inf)
+            // P_1's tile and the O accumulator: tile t - 1's P V products are
+            // complete (P_0 goes over this tile's K: both S products are done)
+            if (t > 0) good = mbar_wait(&sm->o_done, (t - 1) & 1, nullptr) && good;
+            __syncwarp();
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            uint8_t *ptile = g == 0 ? sm->kp[b] : sm->p1;
+            // P = exp(S - m), second pass over TMEM; row sum
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c = 0; c < TA_KEYS; c += 32) {
+                float sv[32];
+                tmem_ld32(tm_s + lane_base + c, sv);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float e = exp2f(fmaf(sv[j], sl2, -ms));
+                    if (diag && kt + c + j > qpos) e = 0.f;
+                    sv[j] = e;
+                    ls[j & 3] += e;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) ta_store8(ptile, r, c + 8 * q, sv + 8 * q);
+            }
+            l_run = fmaf(l_run, corr, (ls[0] + ls[1]) + (ls[2] + ls[3]));
+            m_run = m_new;
+            // rescale this row of the O accumulator, unless no row of the
+            // warp has a new maximum (TMEM loads and stores are warp-wide)
+            if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                for (int c = 0; c < HD; c += 32) {
+                    float ov[32];
+                    tmem_ld32(tm_o + lane_base + c, ov);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ov[j] *= corr;
+                    tmem_st32(tm_o + lane_base + c, ov);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            if (ta_consumers_or(!good)) {
+                failed = true;
+                break;
+            }
+            if (tid == 0) {
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                ta_mma_pv(tm + 2 * TA_KEYS, sm->kp[b], sm->v[b], t > 0);
+                ta_mma_pv(tm + 2 * TA_KEYS + HD, sm->p1, sm->v[b], t > 0);
+                umma_commit(&sm->o_done);
+                umma_commit(&sm->kv_free[b]);  // the loaders may refill buffer b
+            }
         }
-        bool good = mbar_wait(&sm->s_done, t & 1, nullptr);
-        if (!good) pending = &sm->s_done;
+        if (!failed && !mbar_wait(&sm->o_done, (ntiles - 1) & 1, nullptr)) failed = true;
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // row maximum of the raw scores (first pass over TMEM; scale > 0, so
-        // it gives the maximum of the scaled ones).  Only a tile with a key
-        // past the block's first row is masked; four partial maxima (and
-        // sums below) keep the dependency chains short
-        const bool diag = kt + TA_KEYS - 1 > it.L0 + it.qa;
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        for (int c = 0; c < TA_KEYS; c += 32) {
-            float sv[32];
-            tmem_ld32(tm_s + lane_base + c, sv);
-            if (diag) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (kt + c + j <= qpos) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
-            }
-        }
-        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
-        // exp(scale (s - m)) = exp2(s sl2 - m sl2), sl2 = scale log2(e)
-        const float ms = m_new * sl2;
-        const float corr = exp2f(fmaf(m_run, sl2, -ms));  // 0 on the first tile (m_run = -inf)
-        // P = exp(S - m) (both S products have completed: s_done, so head 0
-        // may write over the K tile), second pass over TMEM; row sum
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < TA_KEYS; c += 32) {
-            float sv[32];
-            tmem_ld32(tm_s + lane_base + c, sv);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                float e = exp2f(fmaf(sv[j], sl2, -ms));
-                if (diag && kt + c + j > qpos) e = 0.f;
-                sv[j] = e;
-                ls[j & 3] += e;
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) ta_store8(ptile, r, c + 8 * q, sv + 8 * q);
-        }
-        l_run = fmaf(l_run, corr, (ls[0] + ls[1]) + (ls[2] + ls[3]));
-        m_run = m_new;
-        // rescale this row of the O accumulator, unless no row of the warp
-        // has a new maximum (TMEM loads and stores are warp-wide)
-        if (t > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-            for (int c = 0; c < HD; c += 32) {
-                float ov[32];
-                tmem_ld32(tm_o + lane_base + c, ov);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) ov[j] *= corr;
-                tmem_st32(tm_o + lane_base + c, ov);
-            }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            ta_mma_pv(tm + 2 * TA_KEYS, sm->kp, sm->vt, t > 0);
-            ta_mma_pv(tm + 2 * TA_KEYS + HD, sm->p1, sm->vt, t > 0);
-            umma_commit(&sm->o_done);
-        }
-        if (good && !mbar_wait(&sm->o_done, t & 1, nullptr)) {
-            good = false;
-            pending = &sm->o_done;
-        }
-        __syncwarp();
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (__syncthreads_or(!good)) {
-            failed = true;
-            break;
-        }
-    }
-    // O / sum of row r to attn16 (the TMEM loads are warp-wide: every lane
-    // takes part, the rows beyond the block only skip the store)
-    {
+        // O / sum of row r to attn16 (the TMEM loads are warp-wide: every lane
+        // takes part, the rows beyond the block only skip the store)
         const float inv = 1.0f / l_run;
         __half *dst = attn16 + static_cast<size_t>(it.t0 + it.qa + (r < nq ? r : 0)) * QDIM + qh * HD;
         for (int c = 0; c < HD; c += 32) {
@@ -856,12 +896,13 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
                     *reinterpret_cast<__half2 *>(dst + c + j) = __floats2half2_rn(ov[j] * inv, ov[j + 1] * inv);
             }
         }
+        if (failed) atomicCAS(err, 0, ERR_TIMEOUT);
     }
-    if (failed && pending) {
-        // a wait gave up: report it and wait (bounded) once more, so that no
-        // MMA still runs on this CTA's TMEM when it is freed
-        atomicCAS(err, 0, ERR_TIMEOUT);
-        mbar_wait(pending, t & 1, nullptr);
+    // the MMA thread waits (bounded) for every product it issued, then TMEM
+    // is freed
+    if (tid == 0) {
+        umma_commit(&sm->fin);
+        if (!mbar_wait(&sm->fin, 0, nullptr)) atomicCAS(err, 0, ERR_TIMEOUT);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
