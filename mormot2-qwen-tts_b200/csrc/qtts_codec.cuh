@@ -8,7 +8,8 @@
 // reference).  Every convolution is a product of its im2col rows with the
 // weights [out][in * K] (transposed convolutions with weights re-laid
 // [stride * out][taps * in] at load, as TQwenTransConv.Create,
-// codec.pas:366-396), on one tiled float32 GEMM kernel; the rest are row and
+// codec.pas:366-396), and so are the linear layers: all on one tcgen05
+// product kernel with float32 accuracy (3xTF32); the rest are row and
 // element kernels.  Included at the end of qtts_api.cu (it uses the file's
 // safetensors helpers and error reporting).
 #pragma once
@@ -26,61 +27,220 @@ constexpr int TF_WINDOW = 72, DEC_DIM = 1536, FRAME_SAMPLES = 1920;
 // still give exactly the samples of one call.
 constexpr int KC = 256;
 
-// y[M][N] = a[M][K] . w[N][K]^T (+ bias): 64 x 64 tiles, K by 16, 256
-// threads of 4 x 4 outputs; every load and store bounds-checked.  With
-// gridDim.z > 1, CTA z takes K chunk [z KC, (z+1) KC) and writes its partial
-// (no bias) to y + z M N.
-__global__ void __launch_bounds__(256) gemm_kernel(const float *a, int M, int K, const float *w, int N,
-                                                   const float *bias, float *y) {
-    __shared__ float as[16][68], ws[16][68];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+// y[M][N] = a[M][K] . w[N][K]^T (+ bias) on the 5th-generation tensor cores
+// with float32 accuracy ("3xTF32"): every operand is split into its tf32
+// part (10-bit mantissa, rounded to nearest) and the float32 rest, x = hi +
+// lo, and the product is hi_a hi_w + hi_a lo_w + lo_a hi_w (tcgen05.mma
+// kind::tf32, f32 accumulation in TMEM); the dropped lo_a lo_w is below
+// 2^-20 of |a w|, and each lo enters with its own 10-bit mantissa.
+//  - the weights are split and packed once (tf32_pack_kernel): chunk (tile
+//    of 128 weight rows nt, K step of 32 ks) = the hi tile, then the lo
+//    tile, each 16 KB in the UMMA K-major 128B-swizzle layout (row r, the 4
+//    floats of group c at byte (r / 8) 1024 + (r % 8) 128 + ((c ^ (r % 8))
+//    16)), zero past N and K;
+//  - a CTA (256 threads) takes 128 rows of a by 128 weight rows over its K
+//    range: the whole K, or with gridDim.z > 1 chunk z of KC, whose partial
+//    (no bias) goes to y + z M N.  Per K step of 32 the weight chunk arrives
+//    by one bulk copy, the threads load, split and store the a tile, and
+//    thread 0 issues 4 x 3 MMAs (M 128, N 128, K 8); three stages: the
+//    weight chunk of step j + 1 is requested at step j, and a step's loads
+//    overlap the products of the steps before;
+//  - the accumulator (TMEM lanes = rows of a, columns = weight rows) goes to
+//    y by warps 0-7 (lane quarter warp % 4, column half warp / 4).
+// An output element's sum runs over the same MMAs in the same order whatever
+// M is, so frames decoded one call at a time still give the samples of one
+// call.
+constexpr int T3_ROWS = 128, T3_KS = 32;
+constexpr int T3_TILE = T3_ROWS * T3_KS * 4;  // 16 KB
+constexpr int T3_THREADS = 256;
+constexpr int T3_STAGES = 3;
+struct __align__(1024) T3Smem {
+    uint8_t a[T3_STAGES][2][T3_TILE];  // [stage][hi, lo]
+    uint8_t w[T3_STAGES][2][T3_TILE];  // [stage][hi, lo]: one packed chunk
+    uint64_t wfull[T3_STAGES], mdone[T3_STAGES];
+    uint32_t tmem_base;
+};
+static_assert(sizeof(T3Smem) + 1024 <= 232448, "codec products: shared memory above 227 KB");
+static_assert(KC % T3_KS == 0, "a K chunk is whole K steps");
+// c f32 (bit 4), a and b tf32 (2 at bits 7 and 10), K-major both, N 128, M 128
+constexpr uint32_t T3_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+
+__host__ __device__ inline uint32_t t3_off(int r, int c) {
+    return (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+}
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t u;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+    return __uint_as_float(u);
+}
+__device__ __forceinline__ void t3_split_store(uint8_t *hi_tile, uint8_t *lo_tile, uint32_t off, const float *v) {
+    float4 h, l;
+    h.x = tf32_rna(v[0]);
+    h.y = tf32_rna(v[1]);
+    h.z = tf32_rna(v[2]);
+    h.w = tf32_rna(v[3]);
+    l.x = v[0] - h.x;
+    l.y = v[1] - h.y;
+    l.z = v[2] - h.z;
+    l.w = v[3] - h.w;
+    *reinterpret_cast<float4 *>(hi_tile + off) = h;
+    *reinterpret_cast<float4 *>(lo_tile + off) = l;
+}
+__device__ __forceinline__ void umma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(T3_IDESC), "r"(acc)
+        : "memory");
+}
+
+// w [N][K] -> the packed chunks; one thread per (row of the padded tile
+// grid, K step, group of 4)
+__global__ void tf32_pack_kernel(const float *w, int N, int K, uint8_t *dst) {
+    const int KS = (K + T3_KS - 1) / T3_KS, NT = (N + T3_ROWS - 1) / T3_ROWS;
+    const long long total = static_cast<long long>(NT) * T3_ROWS * KS * (T3_KS / 4);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % (T3_KS / 4));
+        const long long rest = i / (T3_KS / 4);
+        const int ks = static_cast<int>(rest % KS);
+        const int row = static_cast<int>(rest / KS), nt = row / T3_ROWS, r = row % T3_ROWS;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int k = ks * T3_KS + 4 * c + j;
+            v[j] = row < N && k < K ? w[static_cast<size_t>(row) * K + k] : 0.f;
+        }
+        uint8_t *chunk = dst + (static_cast<size_t>(nt) * KS + ks) * (2 * T3_TILE);
+        t3_split_store(chunk, chunk + T3_TILE, t3_off(r, c), v);
+    }
+}
+
+__global__ void __launch_bounds__(T3_THREADS, 1) tc3_gemm_kernel(const float *a, int M, int K, const uint8_t *wp,
+                                                                int N, const float *bias, float *y, int *err) {
+    extern __shared__ __align__(1024) uint8_t t3_raw[];
+    T3Smem *sm = reinterpret_cast<T3Smem *>((reinterpret_cast<uintptr_t>(t3_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nt = blockIdx.x, m0 = blockIdx.y * T3_ROWS;
+    const int KS = (K + T3_KS - 1) / T3_KS;
     const bool split = gridDim.z > 1;
     const int kb = split ? blockIdx.z * KC : 0, ke = split ? min(K, kb + KC) : K;
+    const int s0 = kb / T3_KS, ns = (ke - kb + T3_KS - 1) / T3_KS;
     if (split) {
         y += static_cast<size_t>(blockIdx.z) * M * N;
         bias = nullptr;
     }
-    float acc[4][4] = {};
-    // the next K step's loads are in flight while this one is multiplied
-    float pa[4], pw[4];
-    auto fetch = [&](int k0) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = threadIdx.x + 256 * u, r = i >> 4, gk = k0 + (i & 15);
-            pa[u] = (m0 + r < M && gk < ke) ? a[static_cast<size_t>(m0 + r) * K + gk] : 0.f;
-            pw[u] = (n0 + r < N && gk < ke) ? w[static_cast<size_t>(n0 + r) * K + gk] : 0.f;
+    if (tid == 0) {
+        for (int b = 0; b < T3_STAGES; ++b) {
+            qtts::mbar_init(&sm->wfull[b], 1);
+            qtts::mbar_init(&sm->mdone[b], 1);
         }
-    };
-    if (kb < ke) fetch(kb);
-    for (int k0 = kb; k0 < ke; k0 += 16) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = threadIdx.x + 256 * u, r = i >> 4, k = i & 15;
-            as[k][r] = pa[u];
-            ws[k][r] = pw[u];
-        }
-        __syncthreads();
-        if (k0 + 16 < ke) fetch(k0 + 16);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            float av[4], wv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) av[i] = as[k][ty * 4 + i], wv[i] = ws[k][tx * 4 + i];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
-        }
-        __syncthreads();
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
-            if (m < M && n < N) y[static_cast<size_t>(m) * N + n] = acc[i][j] + (bias ? bias[n] : 0.f);
+    if (warp == 0) {  // 128 f32 columns: the 128 x 128 accumulator
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(
+                         qtts::smem_u32(&sm->tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tm = sm->tmem_base;
+    // float4 loads where every row of a starts on 16 bytes
+    const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
+    bool good = true;
+    int w_unwaited = -1;  // a step whose weight copy thread 0 gave up waiting for
+    // step j's weight chunk goes to stage j % 3: the first three now, step
+    // j + 1's at step j once the products of step j - 2 have freed its stage
+    auto copy_w = [&](int j) {
+        const int b = j % T3_STAGES;
+        qtts::mbar_arrive_tx(&sm->wfull[b], 2 * T3_TILE);
+        qtts::bulk_g2s(sm->w[b][0], wp + (static_cast<size_t>(nt) * KS + s0 + j) * (2 * T3_TILE), 2 * T3_TILE,
+                       &sm->wfull[b]);
+    };
+    if (tid == 0)
+        for (int j = 0; j < T3_STAGES && j < ns; ++j) copy_w(j);
+    for (int i = 0; i < ns; ++i) {
+        const int b = i % T3_STAGES, k0 = kb + T3_KS * i;
+        const uint32_t par = (i / T3_STAGES) & 1;
+        if (i >= 2) {
+            // the products of step i - 2 are done: stage (i + 1) % 3 is free
+            // for the a tile of step i + 1 and the weight chunk of step i + 1
+            good = qtts::mbar_wait(&sm->mdone[(i - 2) % T3_STAGES], ((i - 2) / T3_STAGES) & 1, nullptr) && good;
+            if (tid == 0 && i + 1 >= T3_STAGES && i + 1 < ns) copy_w(i + 1);
         }
+        // a rows [m0, m0 + 128) x k [k0, k0 + 32): 1024 groups of 4, 4 per thread
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int g = tid + T3_THREADS * u, r = g >> 3, c = g & 7, m = m0 + r, k = k0 + 4 * c;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (m < M) {
+                const float *src = a + static_cast<size_t>(m) * K + k;
+                if (vec) {
+                    if (k < ke) {  // K % 4 == 0 and k0 % 4 == 0: the group is whole
+                        const float4 q = *reinterpret_cast<const float4 *>(src);
+                        v[0] = q.x;
+                        v[1] = q.y;
+                        v[2] = q.z;
+                        v[3] = q.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[j] = k + j < ke ? src[j] : 0.f;
+                }
+            }
+            t3_split_store(sm->a[b][0], sm->a[b][1], t3_off(r, c), v);
+        }
+        // the tensor core reads shared memory through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            if (qtts::mbar_wait(&sm->wfull[b], par, nullptr)) {
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t ah = qtts::umma_desc_sw128(sm->a[b][0]), al = qtts::umma_desc_sw128(sm->a[b][1]);
+                const uint64_t wh = qtts::umma_desc_sw128(sm->w[b][0]), wl = qtts::umma_desc_sw128(sm->w[b][1]);
+#pragma unroll
+                for (int kk = 0; kk < T3_KS / 8; ++kk) {  // K 8 = 32 bytes = 2 units of 16 bytes
+                    umma_tf32(tm, ah + 2 * kk, wh + 2 * kk, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_tf32(tm, ah + 2 * kk, wl + 2 * kk, 1u);
+                    umma_tf32(tm, al + 2 * kk, wh + 2 * kk, 1u);
+                }
+            } else {
+                good = false;
+                w_unwaited = i;
+            }
+            qtts::umma_commit(&sm->mdone[b]);  // also without products, so that the waits end
+        }
+    }
+    // the last step's products, and with them every earlier one
+    good = qtts::mbar_wait(&sm->mdone[(ns - 1) % T3_STAGES], ((ns - 1) / T3_STAGES) & 1, nullptr) && good;
+    if (tid == 0 && w_unwaited >= 0)  // no copy may land after the CTA has gone
+        qtts::mbar_wait(&sm->wfull[w_unwaited % T3_STAGES], (w_unwaited / T3_STAGES) & 1, nullptr);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    {
+        const int q = warp & 3, half = warp >> 2, m = m0 + 32 * q + lane;
+        for (int c = 64 * half; c < 64 * half + 64; c += 32) {
+            float v[32];
+            qtts::tmem_ld32(tm + (static_cast<uint32_t>(32 * q) << 16) + c, v);
+            if (good && m < M) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int n = nt * T3_ROWS + c + j;
+                    if (n < N) y[static_cast<size_t>(m) * N + n] = v[j] + (bias ? bias[n] : 0.f);
+                }
+            }
+        }
+    }
+    if (!good && err) atomicCAS(err, 0, QTTS_E_TIMEOUT);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tm) : "memory");
+    }
 }
 
 // y[i] = (sum over z in order of part[z][i]) + bias[i % N]
@@ -345,6 +505,10 @@ struct qtts_codec {
     size_t cap[13] = {};
     int *d_codes = nullptr;
     size_t codes_cap = 0;
+    // the weights of the products, split and packed for tc3_gemm_kernel at
+    // their first use (keyed by the float32 weights)
+    std::unordered_map<const float *, const uint8_t *> packed;
+    int *d_err = nullptr;  // error word of the bounded device waits
 };
 
 namespace {
@@ -448,26 +612,49 @@ void codec_free(qtts_codec *c) {
     for (float *p : c->buf)
         if (p) cudaFree(p);
     if (c->d_codes) cudaFree(c->d_codes);
+    if (c->d_err) cudaFree(c->d_err);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
 }
 
+// the split, tile-packed copy of w [N][K] (made on the stream at its first use)
+int cx_packed(qtts_codec *c, const float *w, int N, int K, const uint8_t **out) {
+    const auto it = c->packed.find(w);
+    if (it != c->packed.end()) {
+        *out = it->second;
+        return QTTS_OK;
+    }
+    const size_t bytes = static_cast<size_t>((N + T3_ROWS - 1) / T3_ROWS) * ((K + T3_KS - 1) / T3_KS) * 2 * T3_TILE;
+    uint8_t *p;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return set_err(QTTS_E_OOM, "qtts_codec: out of device memory");
+    c->allocs.push_back(p);
+    tf32_pack_kernel<<<blocks_for(static_cast<long long>(bytes / 32)), 256, 0, c->st>>>(w, N, K, p);
+    CK(cudaGetLastError());
+    c->packed[w] = p;
+    *out = p;
+    return QTTS_OK;
+}
+
 int cx_gemm(qtts_codec *c, const float *a, int M, int K, const float *w, int N, const float *bias, float *y) {
     if (M <= 0) return QTTS_OK;
+    const uint8_t *wp;
+    int rc = cx_packed(c, w, N, K, &wp);
+    if (rc) return rc;
     const int S = (K + KC - 1) / KC;
+    const size_t smem = sizeof(T3Smem) + 1024;
     if (S <= 1) {
-        const dim3 grid((N + 63) / 64, (M + 63) / 64);
-        qcodec::gemm_kernel<<<grid, 256, 0, c->st>>>(a, M, K, w, N, bias, y);
+        const dim3 grid((N + T3_ROWS - 1) / T3_ROWS, (M + T3_ROWS - 1) / T3_ROWS);
+        qcodec::tc3_gemm_kernel<<<grid, T3_THREADS, smem, c->st>>>(a, M, K, wp, N, bias, y, c->d_err);
         CK(cudaGetLastError());
         return QTTS_OK;
     }
     // a long K: chunks of KC on their own CTAs, partials added in order
     float *part;
     const long long MN = static_cast<long long>(M) * N;
-    int rc = cx_scratch(c, W_PART, static_cast<size_t>(S) * MN, &part);
+    rc = cx_scratch(c, W_PART, static_cast<size_t>(S) * MN, &part);
     if (rc) return rc;
-    const dim3 grid((N + 63) / 64, (M + 63) / 64, S);
-    qcodec::gemm_kernel<<<grid, 256, 0, c->st>>>(a, M, K, w, N, nullptr, part);
+    const dim3 grid((N + T3_ROWS - 1) / T3_ROWS, (M + T3_ROWS - 1) / T3_ROWS, S);
+    qcodec::tc3_gemm_kernel<<<grid, T3_THREADS, smem, c->st>>>(a, M, K, wp, N, nullptr, part, c->d_err);
     CK(cudaGetLastError());
     qcodec::splitk_reduce_kernel<<<blocks_for(MN), 256, 0, c->st>>>(part, S, MN, N, bias, y);
     CK(cudaGetLastError());
@@ -667,6 +854,12 @@ extern "C" int qtts_codec_create_safetensors(qtts_device *dev, qtts_safetensors 
         codec_free(c);
         return set_err(QTTS_E_CUDA, "qtts_codec_create_safetensors: no stream");
     }
+    if (cudaMalloc(&c->d_err, 4) != cudaSuccess || cudaMemsetAsync(c->d_err, 0, 4, c->st) != cudaSuccess ||
+        cudaFuncSetAttribute(tc3_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(T3Smem) + 1024)) != cudaSuccess) {
+        codec_free(c);
+        return set_err(QTTS_E_CUDA, "qtts_codec_create_safetensors: device setup failed");
+    }
     int rc = QTTS_OK;
     // the quantizer: codebook = embedding_sum / max(cluster_usage, 1e-5)
     {
@@ -862,7 +1055,14 @@ extern "C" int qtts_codec_decode(qtts_codec *c, const int32_t *codes, int frames
     clamp_kernel<<<blocks_for(rows), 256, 0, c->st>>>(a, rows, a);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(pcm, a, static_cast<size_t>(rows) * 4, cudaMemcpyDeviceToHost, c->st));
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, c->d_err, 4, cudaMemcpyDeviceToHost, c->st));
     CK(cudaStreamSynchronize(c->st));
+    if (h_err) {
+        CK(cudaMemsetAsync(c->d_err, 0, 4, c->st));
+        CK(cudaStreamSynchronize(c->st));
+        return set_err(QTTS_E_TIMEOUT, "qtts_codec_decode: a device wait gave up");
+    }
     c->frames += frames;
     return QTTS_OK;
 }
