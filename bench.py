@@ -121,47 +121,97 @@ def ncu_traffic(config):
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clocks and clock-event reasons sampled DURING the timed region: an
+    NVML thread (read-only queries) every 2 ms, so that a region of tens of
+    milliseconds still holds samples; nvidia-smi -lms 200 where NVML cannot
+    be loaded.  start() returns once the first sample is in."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index):
-        self.index = index
-        self.p = None
+        import threading
+        self.index, self.p, self.nvml, self.samples = index, None, None, []
+        self.done = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.p = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = self._handle(pynvml, index)
+            self.mx = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception:
+            self.nvml = None
+            try:
+                self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}",
+                                           "--format=csv,noheader,nounits", "-lms", "200"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                self.p = None
+
+    @staticmethod
+    def _handle(pynvml, index):
+        # the CUDA device's own board (CUDA and NVML may number GPUs apart)
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(index)
+
+    def _sample(self):
+        pn = self.nvml
+        sm = pn.nvmlDeviceGetClockInfo(self.h, pn.NVML_CLOCK_SM)
+        r = pn.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        self.samples.append((float(sm), float(self.mx), {n for n, b in zip(self.NAMES, self.bits) if r & b}))
+
+    def _run(self):
+        while not self.done.wait(0.002):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def stop(self):
-        if not self.p:
-            return None
-        self.p.terminate()
-        try:
-            out, _ = self.p.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.p.kill()
-            out, _ = self.p.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 8:
-                continue
+        if self.nvml:
+            self.done.set()
+            self.t.join(timeout=5)
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+                self._sample()  # the end of the region
+            except Exception:
+                pass
+            rows = self.samples
+        elif self.p:
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            rows = []
+            for line in out.splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 8:
+                    continue
+                try:
+                    rows.append((float(f[1]), float(f[2]),
+                                 {n for n, v in zip(self.NAMES, f[4:8]) if v.lower().startswith("active")}))
+                except ValueError:
+                    continue
+        else:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not rows:
+            return None
+        reasons = set().union(*(r[2] for r in rows))
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "source": "NVML, every 2 ms during the timed region" if self.nvml else "nvidia-smi -lms 200"}
 
 
 def build_host_model(dtype, seed=SEED, tlayers=28, players=5):
@@ -314,23 +364,16 @@ BOX_PROMPT = (20, 80)  # configs[4]: prompt rows
 BOX_FRAMES = 300       # configs[4]: frames per utterance
 
 
-def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist, box=False):
+def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist):
     """B utterances (default 64) decoded together,
     Q8_0 weights, contexts drawn uniformly in [50, 1000] (prefilled through
     the batched path), paged bf16 KV cache; one step = one frame of every
     utterance (15 batched predictor steps + 1 batched talker step) through
     qtts_talkers_next_frame, codes read back to the host each frame.
 
-    box=True: configs[4], 128 concurrent utterances per GPU whose prompts of
-    U(20, 80) rows have generated half of their 300 frames: contexts
-    U(170, 230), the mean context of the whole generation; value = frames/s
-    of the box (all ranks)."""
-    if box:
-        B, K, W = BOX_BATCH, args.batch_steps, 3
-        lo, hi = BOX_PROMPT[0] + BOX_FRAMES // 2, BOX_PROMPT[1] + BOX_FRAMES // 2
-    else:
-        B, K, W = args.batch, args.batch_steps, 3
-        lo, hi = args.batch_ctx
+    """
+    B, K, W = args.batch, args.batch_steps, 3
+    lo, hi = args.batch_ctx
     ctx = synth.config2_contexts(SEED, B, lo, hi, rank)
     chunk = 16384
     tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=chunk, max_pos=hi + K + W + 8, kv_dtype="bf16")
@@ -378,16 +421,11 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
     peak = peaks["hbm_gbs"] if peaks else 6650.0
     achieved = (wb + kv) / (ms / 1000.0 / K) / 1e9
     extra = {} if (tl, pl) == (28, 5) else {"layers_override": f"talker {tl}, predictor {pl} (profiling case)"}
-    if box:
-        workload = (f"configs[4]: {B} concurrent utterances per GPU, prompts U{BOX_PROMPT} rows at frame "
-                    f"{BOX_FRAMES // 2} of {BOX_FRAMES} (contexts U({lo},{hi}), the generation's mean), Q8_0 weights, "
-                    "paged bf16 KV, fp16 activations on the tcgen05 GEMMs; a sample of the 1024 x 300-frame run")
-    else:
-        workload = (f"configs[2]: {B} utterances per GPU, contexts U({lo},{hi}), Q8_0 weights, "
-                    "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs")
+    workload = (f"configs[2]: {B} utterances per GPU, contexts U({lo},{hi}), Q8_0 weights, "
+                "paged bf16 KV (16-position pages), fp16 activations on the tcgen05 GEMMs")
     return {**extra,
             "workload": workload,
-            "metric": "frames/s per GPU @B=%d" % B if world == 1 else "box frames/s @B=%d per GPU" % B,
+            "metric": "frames/s per GPU @B=%d" % B if world == 1 else "frames/s of all GPUs @B=%d per GPU" % B,
             "value": job_value(world, frames, ms), "unit": "frames/s", "steps": K, "warmup": W,
             "ms_per_batched_frame": ms / K, "frames": frames, "prefill_s_rank0": prefill_s,
             "mean_ctx": float(ctx.mean()),
@@ -396,6 +434,118 @@ def batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, ran
                          "what": "whole batched frame (weights once + talker/predictor KV), CUDA events on the stream"},
             "e2e_note": "timed through qtts_talkers_next_frame (the public call), codes of every frame read back to "
                         "the host inside the timed region; the prefill is outside it"}
+
+
+def sum_over_ranks(values, dist):
+    """Each of `values` summed over the ranks of the job (gloo, CPU)."""
+    import torch
+    if not dist:
+        return [float(v) for v in values]
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(v) for v in t]
+
+
+def box_run(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist):
+    """BASELINE.json configs[4], the whole run: 1024 independent utterances
+    of up to 300 frames, prompts of U(20, 80) N(0,1) rows, Q8_0 weights,
+    paged bf16 KV, at most 128 concurrent utterances per GPU.  Rank r of N
+    takes utterances r, r + N, ...; its 128 slots start with its first 128,
+    and a slot whose utterance ends (codec EOS, or its 300th frame) takes the
+    next one (TQwenTalker.Start on the freed slot; a frame's admissions in
+    one call).  Timed: from the first admission to the last frame, CUDA
+    events on the talkers' stream, max over ranks; value = the frames of
+    every utterance of the box over that time.  The prompt rows are made on
+    the host before the timed region; their upload (inside Start) and every
+    frame's codes (read back) are in it."""
+    import collections
+    world = dist.get_world_size() if dist else 1
+    U, F = args.box_utterances, args.box_frames
+    mine = list(range(rank, U, world))
+    B = min(BOX_BATCH, len(mine))
+    lens = synth.config4_lengths(SEED, U, BOX_PROMPT[0], BOX_PROMPT[1])
+    prompts = {u: synth.config4_prompt(u, int(lens[u]), SEED) for u in mine}
+    tb = qtts.QwenBatch(tstack, th, max_seqs=B, max_tokens=B * BOX_PROMPT[1], max_pos=BOX_PROMPT[1] + F + 16,
+                        kv_dtype="bf16")
+    pb = qtts.QwenBatch(pstack, ph, max_seqs=B, max_tokens=2 * B, max_pos=16, kv_dtype="bf16")
+    ts = qtts.QwenTalkers(tb, pb, m["ce"], m["pe"], synth.CODEC_EOS)
+    stream = torch.cuda.ExternalStream(ts.stream, device=torch.device("cuda", local_rank))
+    # warm-up: 3 frames of the first utterances (the timed run starts them again)
+    ts.start(list(range(B)), [prompts[u] for u in mine[:B]], [None] * B, m["pad"])
+    for _ in range(3):
+        ts.next_frame(list(range(B)))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    tl, pl = args.talker_layers, args.pred_layers
+    pred_kv = sum(pl * KV_POS_BF16 * ((0 if g == 0 else g + 1) + (2 if g == 0 else 1)) for g in range(15))
+    queue = collections.deque(mine)
+    slot_utt, slot_frames, slot_ctx = [-1] * B, [0] * B, [0] * B
+    calls = {"start": 0, "next_frame": 0}
+
+    def admit(slots):
+        take = []
+        for s in slots:
+            if not queue:
+                break
+            u = queue.popleft()
+            slot_utt[s], slot_frames[s], slot_ctx[s] = u, 0, int(lens[u])
+            take.append(s)
+        if take:
+            ts.start(take, [prompts[slot_utt[s]] for s in take], [None] * len(take), m["pad"])
+            calls["start"] += 1
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    admit(range(B))
+    frames, eos, kv_bytes = 0, 0, 0.0
+    while True:
+        active = [s for s in range(B) if slot_utt[s] >= 0]
+        if not active:
+            break
+        _, more = ts.next_frame(active)
+        calls["next_frame"] += 1
+        freed = []
+        for s, mo in zip(active, more):
+            kv_bytes += tl * KV_POS_BF16 * (slot_ctx[s] + 1) + pred_kv
+            slot_ctx[s] += 1
+            if mo:
+                slot_frames[s] += 1
+                frames += 1
+            else:
+                eos += 1
+            if not mo or slot_frames[s] >= F:
+                slot_utt[s] = -1
+                freed.append(s)
+        if freed:
+            admit(freed)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks([e0.elapsed_time(e1)], dist, "cpu")[0]
+    tot_frames, tot_eos, tot_batched, tot_kv = sum_over_ranks([frames, eos, calls["next_frame"], kv_bytes], dist)
+    ts.free()
+    tb.free()
+    pb.free()
+    wb = weight_bytes_per_frame("q8_0", tl, pl)
+    # algorithmic bytes of the whole box: the weights once per batched frame
+    # of every rank, the KV of every utterance frame
+    algo = wb * tot_batched + tot_kv
+    peaks = measured_peaks()
+    peak = peaks["hbm_gbs"] if peaks else 6650.0
+    achieved = algo / (ms / 1000.0) / 1e9 / world  # per GPU, against one GPU's peak
+    return {"workload": f"configs[4]: {U} utterances of up to {F} frames, prompts U{BOX_PROMPT} N(0,1) rows, "
+                        f"at most {BOX_BATCH} concurrent per GPU (slots refilled as utterances end), Q8_0 "
+                        "weights, paged bf16 KV, fp16 activations on the tcgen05 GEMMs; the whole run",
+            "metric": "box frames/s (all GPUs)", "value": tot_frames / (ms / 1000.0), "unit": "frames/s",
+            "ms_total": ms, "frames": int(tot_frames), "eos_endings": int(tot_eos),
+            "batched_frames_rank0": calls["next_frame"], "start_calls_rank0": calls["start"],
+            "utterances": U, "utterances_rank0": len(mine),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "algorithmic_bytes": algo, "traffic": None,
+                         "what": "the whole run per GPU (weights once per batched frame + KV of every utterance "
+                                 "frame), CUDA events on the stream, max over ranks"},
+            "timing": "CUDA events on the talkers' stream around the whole run (admissions with their prompt "
+                      "uploads, every batched frame with its codes read back), max over ranks"}
 
 
 PREFILL_LEN = (256, 2048)  # configs[3]: prompt lengths drawn uniformly
@@ -706,7 +856,7 @@ def gpu_arm(args, rank, world, local_rank):
     if args.batch > 0 and dtype == "q8_0":
         batched = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist)
         if not args.only_batched and (args.talker_layers, args.pred_layers) == (28, 5):
-            box = batched_frames(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist, box=True)
+            box = box_run(args, qtts, torch, tstack, th, pstack, ph, m, local_rank, rank, dist)
     if args.only_batched:
         # the configs[2] measurement alone (profiling runs)
         if rank == 0:
@@ -899,6 +1049,8 @@ def main():
     # configs[2] beside the bench line: B utterances decoded together (0: off)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=20)
+    ap.add_argument("--box-utterances", type=int, default=1024, help="configs[4]: utterances of the box")
+    ap.add_argument("--box-frames", type=int, default=BOX_FRAMES, help="configs[4]: frames per utterance")
     ap.add_argument("--batch-ctx", type=int, nargs=2, default=list(BATCH_CTX), metavar=("LO", "HI"))
     ap.add_argument("--only-batched", action="store_true", help="run the configs[2] measurement alone")
     # configs[3] beside the bench line: batched prefill steps (0: off)

@@ -205,6 +205,17 @@ def config2_prompt(s, rows, seed=1):
     return prompt(seed + 1000 + s, rows)
 
 
+def config4_lengths(seed=1, n=1024, lo=20, hi=80):
+    """the prompt rows of every utterance of the box (utterance
+    u: entry u), uniform in [lo, hi]."""
+    return np.random.default_rng(seed + 13).integers(lo, hi + 1, n)
+
+
+def config4_prompt(u, rows, seed=1):
+    """the N(0, 1) prompt rows of utterance u."""
+    return prompt(seed + 3000 + u, rows)
+
+
 def config3_lengths(seed=1, n=16, lo=256, hi=2048, rank=0):
     """prefill prompt lengths, uniform in [lo, hi]."""
     return np.random.default_rng(seed + 11 + rank).integers(lo, hi + 1, n)
