@@ -1,7 +1,7 @@
 """The N > 1 logic of bench.py on CPU: two gloo ranks on 127.0.0.1 (the
 replicas of the scaling run; no data-path collective exists, only the
-max-over-ranks timing and the whole-job value), and the reference arm's
-rank handling (rank 0 alone runs it)."""
+max-over-ranks timing, the whole-job value and the box run's sums of
+frames), and the reference arm's rank handling (rank 0 alone runs it)."""
 import os
 import socket
 import sys
@@ -29,9 +29,11 @@ def _rank(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     # rank r took 10 + r ms for the frames and 20 - r ms end to end
     ms, e2e = bench.max_over_ranks([10.0 + rank, 20.0 - rank], dist, "cpu")
+    # the box run: rank r's frames and endings summed over the ranks
+    frames, eos = bench.sum_over_ranks([1000 + rank, rank], dist)
     dist.barrier()
     dist.destroy_process_group()
-    out.put((rank, ms, e2e, bench.job_value(world, 156, ms)))
+    out.put((rank, ms, e2e, bench.job_value(world, 156, ms), frames, eos))
 
 
 def test_max_over_ranks_and_job_value_gloo():
@@ -45,15 +47,17 @@ def test_max_over_ranks_and_job_value_gloo():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for _, ms, e2e, v in res:
+    for _, ms, e2e, v, frames, eos in res:
         assert ms == 11.0 and e2e == 20.0  # the slowest rank's times
         assert abs(v - 2 * 156 / 0.011) < 1e-6  # frames of both ranks over that time
+        assert frames == 2001.0 and eos == 1.0
 
 
 def test_single_rank_keeps_its_values():
     import bench
     assert bench.max_over_ranks([3.5, 4.0], None, "cpu") == [3.5, 4.0]
     assert bench.job_value(1, 100, 250.0) == 400.0
+    assert bench.sum_over_ranks([7, 2.5], None) == [7.0, 2.5]
 
 
 def test_reference_arm_runs_on_rank_0_only():
