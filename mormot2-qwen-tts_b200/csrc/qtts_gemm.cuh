@@ -64,10 +64,12 @@ __host__ __device__ constexpr int g_raw_bytes(int wdt) { return wdt == WDT_Q8 ? 
 // A tiles per stage: hi + lo (both formats: the weight enters the product to
 // ~2^-22 of its value, not fp16's 2^-11)
 __host__ __device__ constexpr int g_a_tiles(int) { return 2; }
-// threads of a CTA: float32 tiles need no dequantisers, so their CTA is the
-// four warps that load (warp 0), issue the MMAs (warp 1) and read TMEM back
-// (warps 0-3); Q8_0 adds eight dequantising warps in front (loader warp 8)
-__host__ __device__ constexpr int g_threads(int wdt) { return wdt == WDT_Q8 ? G_THREADS : 128; }
+// threads of a CTA: float32 tiles need no dequantisers, so their CTA is
+// eight warps: warp 0 loads, warp 1 issues the MMAs, and all eight read TMEM
+// back (two per lane quarter, each half of the columns) and run the
+// epilogue; Q8_0 has eight dequantising warps in front, warp 8 loads, 9
+// issues, 8-11 read TMEM back
+__host__ __device__ constexpr int g_threads(int wdt) { return wdt == WDT_Q8 ? G_THREADS : 256; }
 __host__ __device__ constexpr int g_warp0(int wdt) { return wdt == WDT_Q8 ? 8 : 0; }
 // float32 tiles of up to 128 tokens run two CTAs per SM (BN TMEM columns and
 // under 113 KB of shared memory each), so that one CTA's epilogue overlaps
@@ -286,7 +288,10 @@ __global__ void __launch_bounds__(g_threads(WDT), g_ctas_per_sm(WDT, BN))
     gemm_kernel(const GemmArgs args, const __grid_constant__ CUtensorMap xmap) {
     using Smem = GemmSmem<WDT, BN>;
     constexpr int S = Smem::S;
-    constexpr int NT = g_threads(WDT), W0 = g_warp0(WDT);  // W0: loader, W0 + 1: MMA, W0..W0+3: epilogue
+    constexpr int NT = g_threads(WDT), W0 = g_warp0(WDT);  // W0: loader, W0 + 1: MMA, W0..: epilogue
+    constexpr int EW = NT / 32 - W0;                      // epilogue warps: 4 or 8
+    constexpr int ECOLS = BN / (EW / 4);                  // TMEM columns per epilogue warp
+    static_assert(EW % 4 == 0 && ECOLS % 32 == 0, "whole lane quarters and 32-column loads");
     constexpr uint32_t CHUNK = g_chunk_bytes(WDT);
     extern __shared__ __align__(1024) uint8_t gsmem_raw[];
     // the dynamic window is aligned up to 1024 bytes (the swizzle atom)
@@ -419,17 +424,18 @@ __global__ void __launch_bounds__(g_threads(WDT), g_ctas_per_sm(WDT, BN))
             umma_commit(&sm->accum);
         }
     }
-    // ---- epilogue: warps W0..W0+3, TMEM lane quarter = warp % 4
+    // ---- epilogue: warps W0.., TMEM lane quarter = warp % 4, columns
+    // [ECOLS ch, ECOLS (ch + 1)) with ch = (warp - W0) / 4
     if (warp >= W0) {
         pdl_wait();  // out may be written by the previous kernels
         const bool good = mbar_wait(&sm->accum, 0, nullptr);
         if (!good) gemm_fail(args.err);
         __syncwarp();  // tcgen05.ld is warp-wide: lane 0 of the loader and MMA warps had other work
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int q = warp & 3;
+        const int q = warp & 3, ch = (warp - W0) >> 2;
         const int n = row0 + 32 * q + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = ECOLS * ch; c < ECOLS * (ch + 1); c += 32) {
             float v[32];
             tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c, v);
             if (args.swiglu16 && args.ksplit == 1) {
