@@ -546,6 +546,7 @@ struct QkvEpi {
     void *kv_base;
     const int *kv_pages;
     int kv_mpps, kv_layers, kv_layer, kv_bf16;
+    __half *kv16;  // the fp16 mirror of the pages, or NULL
 };
 
 static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, int T, int rows_cap, float *y, int ld,
@@ -572,6 +573,7 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
     a.kv_base = nullptr;
     a.kv_pages = nullptr;
     a.kv_mpps = a.kv_layers = a.kv_layer = a.kv_bf16 = 0;
+    a.kv16 = nullptr;
     if (qe) {
         if (n_rows != QKV_ROWS) return set_err(QTTS_E_ARG, "gemm: the QKV epilogue needs the %d QKV rows", QKV_ROWS);
         a.q32 = qe->q32;
@@ -588,6 +590,7 @@ static int gemm(const uint8_t *w, int wdt, int n_rows, int k, const __half *x, i
         a.kv_layers = qe->kv_layers;
         a.kv_layer = qe->kv_layer;
         a.kv_bf16 = qe->kv_bf16;
+        a.kv16 = qe->kv16;
     }
     dim3 grid((n_rows + G_BM - 1) / G_BM, (T + bn - 1) / bn, split);
     if (wdt == WDT_Q8) {
@@ -2378,6 +2381,7 @@ struct qtts_batch {
     qtts_heads *heads;
     int max_seqs, max_tokens, max_pos, kv_dtype, mpps, npages, head_rows;
     void *pool;
+    __half *kv16;  // the fp16 mirror of the pages (tensor-core prefill attention), or NULL
     int *d_pages;
     std::vector<int> h_pages;  // [max_seqs][mpps], -1 = none
     std::vector<int> free_pages;
@@ -2491,6 +2495,23 @@ extern "C" int qtts_batch_create(qtts_stack *stack, qtts_heads *heads, int max_s
         batch_free(b);
         return set_err(QTTS_E_CUDA, "qtts_batch_create: set-up failed");
     }
+    // a batch that can take long runs of new rows keeps the fp16 mirror of
+    // its pages for the tensor-core attention (cleared: a page's unwritten
+    // rows enter the P V product with weight 0 and must hold no NaN)
+    if (max_tokens > TC_MIN_ROWS) {
+        const size_t bytes = static_cast<size_t>(b->npages) * L * 2 * HKV * KV16_PAGE;
+        if (cudaMalloc(&b->kv16, bytes) != cudaSuccess) {
+            b->kv16 = nullptr;
+            batch_free(b);
+            return set_err(QTTS_E_OOM, "qtts_batch_create: out of device memory (%zu bytes)", bytes);
+        }
+        b->allocs.push_back(b->kv16);
+        if (cudaMemsetAsync(b->kv16, 0, bytes, b->stream) != cudaSuccess ||
+            cudaStreamSynchronize(b->stream) != cudaSuccess) {
+            batch_free(b);
+            return set_err(QTTS_E_CUDA, "qtts_batch_create: set-up failed");
+        }
+    }
     for (int k = 0; k < qtts_batch::NSLOT; ++k) {
         if (cudaHostAlloc(reinterpret_cast<void **>(&b->hmeta[k]), b->meta_bytes + b->h_pages.size() * 4,
                           cudaHostAllocDefault) != cudaSuccess ||
@@ -2560,13 +2581,15 @@ static void batch_layers(qtts_batch *b, int T, int npitems, const AttnItem *pite
         qe.kv_layers = pool.layers;
         qe.kv_layer = l;
         qe.kv_bf16 = sizeof(KVT) == 2 ? 1 : 0;
+        qe.kv16 = b->kv16;
         if ((rc = gemm(Ly.wqkv, wdt, QKV_ROWS, H, b->h16, T, cap, nullptr, QKV_ROWS, false, b->err, st, nullptr, &qe)))
             return;
         if (npitems > 0)
             e = launch_pdl(attn_kernel<KVT>, dim3(npitems), dim3(ATHREADS), 0, st, pitems, b->q32, pool, l, b->attn16);
         if (e == cudaSuccess && ntitems > 0)
             e = launch_pdl(attn_prefill_tc_kernel<KVT>, dim3(ntitems), dim3(TA_THREADS), sizeof(TaSmem) + 1024, st,
-                           titems, static_cast<const float *>(b->q32), pool, l, b->attn16, b->err);
+                           titems, static_cast<const float *>(b->q32), pool, static_cast<const __half *>(b->kv16), l,
+                           b->attn16, b->err);
         if (e == cudaSuccess && nditems > 0)
             e = launch_pdl(attn_decode_kernel<KVT>, dim3(nditems), dim3(DTHREADS), sizeof(DecodeSmem<KVT>), st, ditems,
                            b->q32, pool, l, b->attn16, b->part, b->err);
@@ -2673,7 +2696,7 @@ static int batch_plan(qtts_batch *b, int nseq, const int32_t *seqs, const int32_
                 }
             }
             if (S > 1) ctok.push_back(t);
-        } else if (n > TC_MIN_ROWS) {
+        } else if (n > TC_MIN_ROWS && b->kv16) {
             // long runs of new rows: tensor-core attention, per kv head (both
             // of its query heads in one CTA)
             for (int qa = 0; qa < n; qa += TA_ROWS)

@@ -582,14 +582,19 @@ __global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, co
 // Causal attention of long runs of new rows (prefill) on the 5th-generation
 // tensor cores, flash-attention style.  One CTA per (sequence, kv head,
 // block of up to 128 new rows) takes both query heads of the kv head, so
-// each K/V tile is read and converted once for the two.
-//  - warps 8-11 (loaders) copy the K and V tiles (128 keys x 128 dims) of
-//    the key tiles in turn into two buffers, converted to fp16 in the UMMA
-//    128B-swizzle layout (rows of 128 bytes, two 64-element atoms along the
-//    row): a warp takes two KV pages, one 512-byte row per load, so tile
-//    t + 1 is on its way while tile t is in the products and the softmax.
-//    Q and K are K-major operands; V keeps its rows (keys) and serves as the
-//    MN-major B operand of P V, so nothing is transposed.
+// each K/V tile is read once for the two.
+//  - K and V come from the fp16 mirror of the pages (written by the QKV
+//    epilogue beside the cache, each page already in the tensor cores'
+//    layout): warp 8 brings the 8 pages of a 128-key tile into one of two
+//    buffers with one bulk copy per page and K/V (tile t + 1 lands while
+//    tile t is in the products and the softmax), and clears the V rows of
+//    the pages past the causal end.  A tile is [8-key group][64-dim
+//    atom][8 rows x 128 bytes]: K is a K-major operand with 8-row groups
+//    2048 bytes apart and the second dim atom 1024 bytes on; V is the
+//    MN-major B operand of P V (dim atoms 1024 bytes apart, key groups 2048),
+//    so nothing is transposed or converted.
+//  - Q of both heads is converted to fp16 by warps 0-7 into the A-operand
+//    layout (rows of 128 bytes, the two 64-dim atoms 16 KB apart).
 //  - warps 0-7: thread 128 g + r owns query row r of head 2h + g.  S_g =
 //    Q_g K^T (8 x tcgen05.mma, M 128, N 128, K 16) lands in TMEM columns
 //    [128 g, +128); row r is read back by its thread (warps 4g..4g+3 reach
@@ -605,17 +610,16 @@ __global__ void __launch_bounds__(256) frames_choose0_kernel(const int *seqs, co
 constexpr int TA_ROWS = 128;   // query rows per CTA and head (MMA M)
 constexpr int TA_KEYS = 128;   // keys per tile (MMA N of S, K of P V)
 constexpr int TA_CONSUMERS = 256;  // warps 0-7
-constexpr int TA_LOADERS = 128;    // warps 8-11
-constexpr int TA_THREADS = TA_CONSUMERS + TA_LOADERS;
+constexpr int TA_THREADS = TA_CONSUMERS + 32;  // + warp 8: the copies
 constexpr int TC_MIN_ROWS = 32;  // sequences with more new rows than this use this kernel
 constexpr int TA_TILE = TA_ROWS * HD * 2;  // 32 KB: one fp16 operand tile
 
 struct __align__(1024) TaSmem {
     uint8_t q[2][TA_TILE];
-    uint8_t kp[2][TA_TILE];  // buffer b: the K tile, then (once both S are computed) P of head 0
-    uint8_t v[2][TA_TILE];   // buffer b: the V tile (rows of keys)
+    uint8_t kp[2][TA_TILE];  // buffer b: the K tile (8 mirror pages), then (once both S are computed) P of head 0
+    uint8_t v[2][TA_TILE];   // buffer b: the V tile (8 mirror pages)
     uint8_t p1[TA_TILE];     // P of head 1
-    uint64_t kv_full[2];     // the loaders' arrivals (TA_LOADERS)
+    uint64_t kv_full[2];     // the copies' bytes (one arrival: warp 8)
     uint64_t kv_free[2];     // tcgen05.commit after the P V products that read buffer b
     uint64_t s_done, o_done, fin;
     uint32_t tmem_base;
@@ -656,34 +660,44 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
         : "memory");
 }
 
-// thread 0: the 8 MMAs (K = 128 in steps of 16) of one 128 x 128 x 128 product
-__device__ __forceinline__ void ta_mma(uint32_t tmem_d, const uint8_t *a, const uint8_t *b, bool accumulate) {
+// a 128B-swizzle shared-memory descriptor with explicit leading and stride
+// byte offsets
+__device__ __forceinline__ uint64_t umma_desc_sw128_at(const void *smem, uint32_t lbo, uint32_t sbo) {
+    return ((smem_u32(smem) >> 4) & 0x3FFFull) | (static_cast<uint64_t>(lbo >> 4) << 16) |
+           (static_cast<uint64_t>(sbo >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// thread 0: S = Q K^T for one 128-key tile (8 MMAs, K = 16 each).  Q (128
+// rows x 128 dims) is the K-major A operand, its two 64-dim atoms 16 KB
+// apart; K (8 mirror pages) is the K-major B operand, 8-key groups 2048
+// bytes apart and the second dim atom 1024 bytes on; a K = 16 step moves 32
+// bytes inside an atom.
+__device__ __forceinline__ void ta_mma_s(uint32_t tmem_d, const uint8_t *q, const uint8_t *k) {
     const uint32_t idesc = umma_idesc_f16(TA_ROWS, TA_KEYS);
 #pragma unroll
-    for (int k = 0; k < HD / 16; ++k) {
-        const uint64_t da = umma_desc_sw128(a + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
-        const uint64_t db = umma_desc_sw128(b + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
-        umma_f16(tmem_d, da, db, idesc, (accumulate || k > 0) ? 1u : 0u);
+    for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint64_t da = umma_desc_sw128(q + (kk >> 2) * (TA_ROWS * 128)) + 2 * (kk & 3);
+        const uint64_t db = umma_desc_sw128_at(k + (kk >> 2) * 1024, 16, 2048) + 2 * (kk & 3);
+        umma_f16(tmem_d, da, db, idesc, kk > 0 ? 1u : 0u);
     }
 }
 
-// thread 0: O += P V for one 128-key tile.  P (128 rows x 128 keys) is
-// K-major; V (128 keys x 128 dims, rows of dims) is the MN-major B operand:
-// 128B-swizzle atoms of 8 keys x 64 dims, the two dim atoms 16 KB apart
-// (leading byte offset), groups of 8 keys 1024 bytes apart (stride byte
-// offset); each K = 16 step moves two key groups (2048 bytes) on.
+// thread 0: O += P V for one 128-key tile.  P (128 rows x 128 keys) is the
+// K-major A operand (atoms 16 KB apart); V (8 mirror pages: 128 keys x 128
+// dims) is the MN-major B operand, its dim atoms 1024 bytes apart (leading
+// byte offset) and 8-key groups 2048 apart (stride byte offset); a K = 16
+// step moves two key groups, 4096 bytes.
 __device__ __forceinline__ void ta_mma_pv(uint32_t tmem_d, const uint8_t *p, const uint8_t *v, bool accumulate) {
     const uint32_t idesc = umma_idesc_f16(TA_ROWS, HD) | (1u << 16);  // B MN-major
-    const uint64_t lbo = (TA_ROWS * 128) >> 4, sbo = 1024 >> 4;
 #pragma unroll
-    for (int k = 0; k < TA_KEYS / 16; ++k) {
-        const uint64_t da = umma_desc_sw128(p + (k >> 2) * (TA_ROWS * 128)) + 2 * (k & 3);
-        const uint64_t db = ((smem_u32(v + 2048 * k) >> 4) & 0x3FFFull) | (lbo << 16) | (sbo << 32) | (1ull << 46) |
-                            (2ull << 61);
-        umma_f16(tmem_d, da, db, idesc, (accumulate || k > 0) ? 1u : 0u);
+    for (int kk = 0; kk < TA_KEYS / 16; ++kk) {
+        const uint64_t da = umma_desc_sw128(p + (kk >> 2) * (TA_ROWS * 128)) + 2 * (kk & 3);
+        const uint64_t db = umma_desc_sw128_at(v + 4096 * kk, 1024, 2048);
+        umma_f16(tmem_d, da, db, idesc, (accumulate || kk > 0) ? 1u : 0u);
     }
 }
-static_assert(PAGE == 16 && TA_KEYS == 8 * PAGE, "one warp per KV page of a key tile");
+static_assert(PAGE == 16 && TA_KEYS == 8 * PAGE && TA_TILE == 8 * KV16_PAGE,
+              "a key tile is 8 mirror pages of K (and 8 of V)");
 
 // consumer warps only: bar.sync on barrier 1 that also ORs a flag over them
 __device__ __forceinline__ bool ta_consumers_or(bool v) {
@@ -698,14 +712,14 @@ __device__ __forceinline__ bool ta_consumers_or(bool v) {
 
 template <class KVT>
 __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const AttnItem *items, const float *q32,
-                                                                       KVPool<KVT> pool, int layer, __half *attn16,
-                                                                       int *err) {
+                                                                       KVPool<KVT> pool, const __half *kv16, int layer,
+                                                                       __half *attn16, int *err) {
     extern __shared__ __align__(1024) uint8_t ta_raw[];
     TaSmem *sm = reinterpret_cast<TaSmem *>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&sm->kv_full[b], TA_LOADERS);
+            mbar_init(&sm->kv_full[b], 1);
             mbar_init(&sm->kv_free[b], 1);
         }
         mbar_init(&sm->s_done, 1);
@@ -746,42 +760,43 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tm = sm->tmem_base;
-    if (warp >= 8) {
-        // ---- loaders: tile t into buffer t % 2 once the P V products of
-        // tile t - 2 (the last to read it) are complete; warp 8 + j copies
-        // KV pages 2j and 2j + 1 of the tile (16 keys each), K then V, a
-        // page's 16 rows in flight together; rows past the causal end are 0
-        const int lw = warp - 8;
+    if (warp == 8) {
+        // ---- copies: tile t into buffer t % 2 once the P V products of
+        // tile t - 2 (the last to read it) are complete: one bulk copy of 4 KB
+        // per mirror page and K/V; the V rows of pages past the causal end
+        // are cleared (P is 0 there, and 0 times a stale NaN is NaN)
+        int issued = 0;
         for (int t = 0; t < ntiles; ++t) {
             const int b = t & 1, kt = t * TA_KEYS;
             if (t >= 2 && !mbar_wait(&sm->kv_free[b], ((t >> 1) - 1) & 1, nullptr)) {
-                atomicCAS(err, 0, ERR_TIMEOUT);
+                if (lane == 0) atomicCAS(err, 0, ERR_TIMEOUT);
                 break;
             }
-#pragma unroll 1
-            for (int pg = 2 * lw; pg < 2 * lw + 2; ++pg) {
-                const int k0 = kt + PAGE * pg, nk = kend - k0;
-#pragma unroll 1
-                for (int which = 0; which < 2; ++which) {
-                    float4 rb[PAGE];
-                    if (nk > 0) {
-                        const KVT *src = kv_at(pool, layer, it.seq, k0, which, h) + 4 * lane;
-#pragma unroll
-                        for (int i = 0; i < PAGE; ++i)
-                            rb[i] = i < nk ? load4(src + i * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < PAGE; ++i) rb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                    uint8_t *dst = which == 0 ? sm->kp[b] : sm->v[b];
-#pragma unroll
-                    for (int i = 0; i < PAGE; ++i) ta_store4(dst, PAGE * pg + i, 4 * lane, rb[i]);
+            issued = t + 1;
+            const int npg = min(TA_KEYS / PAGE, (kend - kt + PAGE - 1) / PAGE);  // pages holding keys < kend
+            for (int i = npg * KV16_PAGE / 16 + lane; i < TA_TILE / 16; i += 32)
+                reinterpret_cast<uint4 *>(sm->v[b])[i] = make_uint4(0u, 0u, 0u, 0u);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_tx(&sm->kv_full[b], static_cast<uint32_t>(npg * 2 * KV16_PAGE));
+                for (int pg = 0; pg < npg; ++pg) {
+                    const int page = pool.pages[it.seq * pool.mpps + (kt >> 4) + pg];
+                    const uint8_t *k = reinterpret_cast<const uint8_t *>(kv16) +
+                                       kv16_page_index(page, pool.layers, layer, 0, h) * KV16_PAGE;
+                    const uint8_t *v = reinterpret_cast<const uint8_t *>(kv16) +
+                                       kv16_page_index(page, pool.layers, layer, 1, h) * KV16_PAGE;
+                    bulk_g2s(sm->kp[b] + pg * KV16_PAGE, k, KV16_PAGE, &sm->kv_full[b]);
+                    bulk_g2s(sm->v[b] + pg * KV16_PAGE, v, KV16_PAGE, &sm->kv_full[b]);
                 }
             }
-            // the tensor core reads the tiles through the async proxy
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&sm->kv_full[b]);
         }
+        // no copy may land after the CTA is gone (the consumers may have
+        // stopped early): wait (bounded) for the last one issued into each
+        // buffer; the earlier ones were consumed before their buffer refilled
+        if (lane == 0)
+            for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t)
+                mbar_wait(&sm->kv_full[t & 1], (t >> 1) & 1, nullptr);
     } else {
         // ---- consumers
         const int g = tid >> 7, r = tid & (TA_ROWS - 1);  // query head 2h + g, row r
@@ -801,8 +816,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1) attn_prefill_tc_kernel(const At
                 good = mbar_wait(&sm->kv_full[b], (t >> 1) & 1, nullptr);
                 if (good) {
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    ta_mma(tm, sm->q[0], sm->kp[b], false);
-                    ta_mma(tm + TA_KEYS, sm->q[1], sm->kp[b], false);
+                    ta_mma_s(tm, sm->q[0], sm->kp[b]);
+                    ta_mma_s(tm + TA_KEYS, sm->q[1], sm->kp[b]);
                     umma_commit(&sm->s_done);
                 }
             }

@@ -112,9 +112,25 @@ struct GemmArgs {
     void *kv_base;
     const int *kv_pages;
     int kv_mpps, kv_layers, kv_layer, kv_bf16;
+    // non-NULL: the fp16 mirror of the pages (same page numbers), written
+    // beside the cache for the tensor-core prefill attention
+    __half *kv16;
 };
 
 constexpr int G_PAGE = 16;  // positions per page of the paged KV cache
+
+// The fp16 mirror of one KV page (one layer, k or v, one kv head): its 16
+// positions x 128 dims, 4 KB, laid out as the tensor cores read a tile of
+// keys: [8-position group][64-dim atom][8 rows of 128 bytes, the 16-byte
+// chunks of row r at chunk ^ (r % 8)] (the UMMA 128B swizzle), so that a
+// page lands in shared memory by one bulk copy.
+constexpr int KV16_PAGE = G_PAGE * 128 * 2;  // bytes
+__host__ __device__ constexpr uint32_t kv16_off(int r, int d) {
+    return ((r >> 3) * 2 + (d >> 6)) * 1024 + (r & 7) * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + (d & 7) * 2;
+}
+__host__ __device__ constexpr size_t kv16_page_index(int page, int layers, int layer, int which, int kvh) {
+    return ((static_cast<size_t>(page) * layers + layer) * 2 + which) * 8 + kvh;  // 8 kv heads
+}
 
 // the QKV epilogue of token t at position pos (one warp): x[4] = this
 // lane's dims 4L..4L+3 of head `head` (0-15 q, 16-23 k, 24-31 v); page: the
@@ -162,6 +178,15 @@ __device__ __forceinline__ void qkv_token_epilogue(const GemmArgs &a, int head, 
         *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(a.kv_base) + e) = u;
     } else {
         *reinterpret_cast<float4 *>(static_cast<float *>(a.kv_base) + e) = make_float4(x[0], x[1], x[2], x[3]);
+    }
+    if (a.kv16) {
+        const __half2 lo = __floats2half2_rn(x[0], x[1]), hi = __floats2half2_rn(x[2], x[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t *>(&lo);
+        u.y = *reinterpret_cast<const uint32_t *>(&hi);
+        uint8_t *pg = reinterpret_cast<uint8_t *>(a.kv16) +
+                      kv16_page_index(page, a.kv_layers, a.kv_layer, which, kvh) * KV16_PAGE;
+        *reinterpret_cast<uint2 *>(pg + kv16_off(pos % G_PAGE, 4 * lane)) = u;
     }
 }
 
