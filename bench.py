@@ -88,16 +88,19 @@ def measured_peaks():
         return None
 
 
-def source_digest():
-    """sha256 (first 16 hex digits) of the kernel sources (csrc/*.cu, *.cuh,
-    *.h): names the build a profile was captured on."""
-    import glob
+# the sources of the batch-1 frame kernel (qtts::decode_kernel and the
+# sampler it inlines): a profile of that kernel names the build by them
+DECODE_SOURCES = ("qtts_decode.cuh", "qtts_sample.cuh")
+
+
+def source_digest(files=DECODE_SOURCES):
+    """sha256 (first 16 hex digits) of the named kernel sources under csrc/:
+    names the build of a kernel a profile was captured on."""
     import hashlib
     h = hashlib.sha256()
-    for f in sorted(glob.glob(os.path.join(PKG, "csrc", "*"))):
-        if f.endswith((".cu", ".cuh", ".h")):
-            h.update(os.path.basename(f).encode())
-            h.update(open(f, "rb").read())
+    for name in sorted(files):
+        h.update(name.encode())
+        h.update(open(os.path.join(PKG, "csrc", name), "rb").read())
     return h.hexdigest()[:16]
 
 
