@@ -160,7 +160,6 @@ def test_config2_b64_three_frames(device):
             i = j
         err = float(d0.max())
         assert err <= Q8_ATOL and c0.min() >= Q8_COS, (err, c0.min())
-        bound = 2.0 * err
         seqs = list(range(B))
         alive = np.ones(B, bool)  # still on the oracle's own trajectory
         divergences = []
@@ -175,14 +174,21 @@ def test_config2_b64_three_frames(device):
                     g = int(diff[0])
                     m = float(fx["margins"][s, f, g])
                     divergences.append({"utterance": s, "frame": f, "group": g, "oracle_margin": m})
-                    assert m <= bound, divergences[-1]
                     alive[s] = False
+        # the talker logits after three frames, on the utterances that kept
+        # the oracle's trajectory
         d3 = []
         for s in np.nonzero(alive)[0]:
             lg, _ = ts.probe(int(s))
             d = float(np.abs(lg - fx["logits3"][s]).max())
             assert d <= Q8_ATOL and cosine(lg, fx["logits3"][s]) >= Q8_COS, (s, d)
             d3.append(d)
+        # every divergence lies within twice the largest logit error measured
+        # in this run (the prefill's and frame 3's), itself within the Q8_0
+        # tolerance
+        bound = 2.0 * max([err] + d3)
+        for dv in divergences:
+            assert dv["oracle_margin"] <= bound, (dv, bound)
         report("config2_b64_three_frames", utterances=B, frames=int(fx["codes"].shape[1]),
                prefill_max_abs_logit_diff=err, prefill_min_cosine=float(c0.min()), divergence_bound=bound,
                divergences=divergences, identical_utterances=int(alive.sum()),
