@@ -609,11 +609,11 @@ def prefill_measure(args, qtts, torch, m, dev, rank):
 # Compute::mark): (from tag, to tag) -> phase; 100 + b / 200 + b = arrival at /
 # departure from barrier b
 TRACE_PHASES = {
-    (10, 11): "QKV GEMV (P1)", (201, 21): "attention, split context (P2)", (207, 21): "attention, whole context (P2)",
+    (10, 11): "QKV GEMV (P1)", (11, 21): "attention, polling its rows (P2)",
     (202, 30): "combine of the splits (P3)", (30, 31): "O GEMV + residual (P3)", (21, 31): "O GEMV by kv head",
     (203, 40): "RMSNorm staging (P4)", (40, 41): "gate/up GEMV + SwiGLU (P4)", (204, 50): "staging (P5)",
     (50, 51): "down GEMV + residual (P5)", (205, 10): "RMSNorm staging (P1)", (60, 61): "head GEMV + argmax keys",
-    (206, 10): "argmax + next input (P1 staging)", (11, 101): "K/V prefetch", (11, 107): "K/V prefetch",
+    (206, 10): "argmax + next input (P1 staging)", (51, 10): "RMSNorm staging, polling the residual (P1)",
 }
 # Q8_0 bytes a GEMV phase streams (row-packed, 34 B per 32 weights)
 TRACE_BYTES = {"QKV GEMV (P1)": 4096 * 1088, "O GEMV + residual (P3)": 1024 * 2176, "O GEMV by kv head": 8192 * 272,

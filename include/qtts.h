@@ -169,7 +169,7 @@ int qtts_lm_forward(qtts_lm *lm, const float *x, int rows, int head, float *logi
  * owned by the caller (logits/hidden may be NULL), each 16-byte aligned
  * (QTTS_E_ARG otherwise, before anything runs); x is read in place.  The
  * call allocates nothing: the kernel's scratch is one static device array of
- * 833,280 bytes (every GPU that loads the library holds it until exit),
+ * 931,584 bytes (every GPU that loads the library holds it until exit),
  * sized for at most 160 SMs and heads of at most 4096 rows; larger requests
  * fail with QTTS_E_CAPACITY.  qtts_lm_create looks up the array's device
  * address (cudaGetSymbolAddress, which may load the library's module on that

@@ -155,6 +155,8 @@ struct Runner {  // scratch + stream of one lm (and of a talker built on it)
     void *block;  // one allocation for all of the scratch
     int grid;
     int *h_err;   // pinned [2]
+    unsigned *epoch;  // the launch epoch of this scratch's tagged words (Job::epoch)
+    unsigned own_epoch = 0;
 };
 
 struct qtts_lm {
@@ -1037,7 +1039,8 @@ static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
         off += (bytes + 255) & ~static_cast<size_t>(255);
         return o;
     };
-    size_t ox = take(RMAX * H * 4), oqkv = take(RMAX * QKV_ROWS * 4), oact = take(RMAX * INTER * 4),
+    size_t ox = take(RMAX * H * 4), ox8 = take(RMAX * H * 8), oqkv = take(RMAX * QKV_ROWS * 8),
+           oact = take(RMAX * INTER * 4),
            opart = take(static_cast<size_t>(HKV) * maxS * RMAX * 2 * PSTRIDE * 4),
            oarg = take(static_cast<size_t>(r.grid) * 8), obar = take(BAR_WORDS * 4), oerr = take(16),
            olog = take(static_cast<size_t>(max_head_rows) * 4), ohid = take(H * 4), oxt = take(H * 4);
@@ -1046,8 +1049,11 @@ static int runner_init(Runner &r, qtts_device *dev, int max_head_rows) {
     CK(cudaMemset(r.block, 0, off));
     uint8_t *b = static_cast<uint8_t *>(r.block);
     r.s.x = reinterpret_cast<float *>(b + ox);
-    r.s.qkv = reinterpret_cast<float *>(b + oqkv);
+    r.s.x8 = reinterpret_cast<unsigned long long *>(b + ox8);
+    r.s.qkv = reinterpret_cast<unsigned long long *>(b + oqkv);
     r.s.act = reinterpret_cast<float *>(b + oact);
+    r.epoch = &r.own_epoch;
+    r.own_epoch = 0;
     r.s.part = reinterpret_cast<float *>(b + opart);
     r.s.arg = reinterpret_cast<unsigned long long *>(b + oarg);
     r.s.bar = reinterpret_cast<unsigned *>(b + obar);
@@ -1068,8 +1074,17 @@ static void runner_free(Runner &r) {
     r.stream = nullptr;
 }
 
-static int launch(qtts_device *dev, Runner &r, const Job &job, int wdt) {
-    void *args[] = {const_cast<Job *>(&job)};
+static int launch(qtts_device *dev, Runner &r, const Job &job_in, int wdt) {
+    // a new epoch for the tags of this launch's handoffs; before an epoch
+    // comes round again, the tagged words are cleared (tag 0 is never used)
+    Job job = job_in;
+    if (++*r.epoch >= EPOCH_LIMIT) {
+        CK(cudaMemsetAsync(r.s.x8, 0, static_cast<size_t>(RMAX) * H * 8, r.stream));
+        CK(cudaMemsetAsync(r.s.qkv, 0, static_cast<size_t>(RMAX) * QKV_ROWS * 8, r.stream));
+        *r.epoch = 1;
+    }
+    job.epoch = *r.epoch;
+    void *args[] = {&job};
     // the cache format of the launch: the lm's, or the talker's (whose
     // predictor holds the same, qtts_talker_create)
     const int kv16 = job.mode == 0 ? job.ctx.kv16 : job.tctx.kv16;
@@ -2247,8 +2262,9 @@ constexpr int NOALLOC_MAX_HEAD_ROWS = 4096;
 namespace {
 constexpr size_t al256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 constexpr size_t NA_X = 0;
-constexpr size_t NA_QKV = NA_X + al256(static_cast<size_t>(RMAX) * H * 4);
-constexpr size_t NA_ACT = NA_QKV + al256(static_cast<size_t>(RMAX) * QKV_ROWS * 4);
+constexpr size_t NA_X8 = NA_X + al256(static_cast<size_t>(RMAX) * H * 4);
+constexpr size_t NA_QKV = NA_X8 + al256(static_cast<size_t>(RMAX) * H * 8);
+constexpr size_t NA_ACT = NA_QKV + al256(static_cast<size_t>(RMAX) * QKV_ROWS * 8);
 constexpr size_t NA_PART = NA_ACT + al256(static_cast<size_t>(RMAX) * INTER * 4);
 constexpr size_t NA_ARG =
     NA_PART + al256(static_cast<size_t>(HKV) * (NOALLOC_MAX_SMS / HKV) * RMAX * 2 * PSTRIDE * 4);
@@ -2257,7 +2273,7 @@ constexpr size_t NA_ERR = NA_BAR + al256(BAR_WORDS * 4);
 constexpr size_t NA_LOGITS = NA_ERR + al256(16);
 constexpr size_t NA_HIDDEN = NA_LOGITS + al256(static_cast<size_t>(NOALLOC_MAX_HEAD_ROWS) * 4);
 constexpr size_t NA_XT = NA_HIDDEN + al256(H * 4);
-constexpr size_t NA_BYTES = NA_XT + al256(H * 4);  // 833,280 bytes
+constexpr size_t NA_BYTES = NA_XT + al256(H * 4);  // 931,584 bytes
 }  // namespace
 
 // Every GPU that loads the library holds this array until the process exits.
@@ -2267,6 +2283,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
 // by qtts_lm_create, or else by the first call on the device)
 static std::mutex g_noalloc_mu;
 static void *g_noalloc_ptr[256];
+static unsigned g_noalloc_epoch[256];  // launch epoch of the array's tagged words, per device
 
 static void *noalloc_lookup(int ordinal) {
     if (ordinal < 0 || ordinal >= 256) return nullptr;
@@ -2321,7 +2338,10 @@ extern "C" int qtts_lm_forward_noalloc(qtts_lm *m, const float *x, int rows, int
     r.block = nullptr;
     r.h_err = nullptr;
     r.s.x = reinterpret_cast<float *>(sc + NA_X);
-    r.s.qkv = reinterpret_cast<float *>(sc + NA_QKV);
+    r.s.x8 = reinterpret_cast<unsigned long long *>(sc + NA_X8);
+    r.s.qkv = reinterpret_cast<unsigned long long *>(sc + NA_QKV);
+    // the array's tagged words and their epoch live as long as the array
+    r.epoch = &g_noalloc_epoch[m->dev->ordinal];
     r.s.act = reinterpret_cast<float *>(sc + NA_ACT);
     r.s.part = reinterpret_cast<float *>(sc + NA_PART);
     r.s.arg = reinterpret_cast<unsigned long long *>(sc + NA_ARG);

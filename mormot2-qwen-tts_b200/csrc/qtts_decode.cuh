@@ -69,7 +69,7 @@ constexpr int ACT_FLOATS = RMAX * INTER;  // staged activations [R][K]
 constexpr int MAX_PARTS = 64;             // (row, K segment) partial sums of a CTA slice (grid >= 128)
 constexpr int KO = 2 * HD;                // O-projection columns of one kv head (its 2 query heads)
 constexpr int QKV_HEAD = 4 * HD;          // QKV rows of one kv head: q(2h), q(2h+1), k(h), v(h)
-constexpr int BAR_WORDS = 16;             // barrier counters: [0] grid, [1] exit, [2 + h] group of kv head h
+constexpr int BAR_WORDS = 16;             // barrier counters: [0] grid, [1] exit (the rest reserved)
 constexpr int PSTRIDE = 132;              // attention partial: o[128], m, l
 constexpr int ATT_TILE = 32;              // context positions per attention tile
 constexpr int XS_MAX = 16;                // residual rows owned by a CTA (grid >= 64)
@@ -136,12 +136,15 @@ __host__ __device__ inline int kv_bytes(const DCtx &c) { return c.kv16 ? 2 : 4; 
 // scratch of one runner (one lm or one talker), all in global memory
 struct Scratch {
     float *x;       // [RMAX][H] residual stream
-    float *qkv;     // [RMAX][QKV_ROWS]
+    // tagged handoffs: 64-bit words (tag << 32 | float bits), read by
+    // polling until the word carries the tag of the handoff (no barrier)
+    unsigned long long *x8;   // [RMAX][H] residual stream after the down projection
+    unsigned long long *qkv;  // [RMAX][QKV_ROWS] QKV rows
     float *act;     // [RMAX][INTER]
     float *part;    // [HKV*maxS][RMAX][2][PSTRIDE] attention partials, or (per-head path)
                     // [RMAX][HKV * H] O-projection partials, one H-vector per kv head
     unsigned long long *arg;  // [grid] argmax keys
-    unsigned *bar;  // [BAR_WORDS]: [0] grid barrier, [1] exit, [2 + h] group barrier of kv head h
+    unsigned *bar;  // [BAR_WORDS]: [0] grid barrier, [1] exit
     int *err;       // [0] error code, [1] where
     float *logits;  // [max head rows]
     float *hidden;  // [H] normed state of the last row
@@ -198,12 +201,18 @@ struct Job {
     Scratch s;
     const float *rope_cos, *rope_sin;  // [rope_pos][HD/2]
     int rope_pos;
-    // the bound of the grid and group barrier spins (cycles; WAIT_CYCLES
-    // unless a failure-path test shortens it), and arrivals those barriers
-    // expect beyond the grid (0; a test sets 1: an arrival that never comes)
+    // the bound of the grid barrier and tagged-word spins (cycles;
+    // WAIT_CYCLES unless a failure-path test shortens it), and arrivals the
+    // grid barrier expects beyond the grid (0; a test sets 1: an arrival
+    // that never comes)
     long long wait_cycles;
     int bar_extra;
+    // launch epoch (1 .. 2^22 - 1): the high bits of every handoff tag, so
+    // that no word left by an earlier launch carries a tag this one expects
+    unsigned epoch;
 };
+constexpr unsigned EPOCH_LIMIT = 1u << 22;  // the host clears the tagged words before reusing epoch 1
+constexpr int TAG_SEQ_BITS = 10;            // handoffs per launch < 1024 (a frame of 28 + 15 x 5 layers: 206)
 
 // ------------------------------------------------------------------ PTX helpers
 
@@ -316,6 +325,18 @@ __device__ __forceinline__ int key_index(unsigned long long k) {
 // loads through L2 (data written by other CTAs in this launch: this SM's L1
 // may hold an older copy)
 __device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+
+// tagged words of a handoff: one 8-byte access carries the value and its tag
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, unsigned tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ld_tagged2(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, unsigned tag) {
+    return static_cast<unsigned>(w >> 32) == tag;
+}
 // 4 halves (8-byte aligned, shared memory) -> float4
 __device__ __forceinline__ float4 h4_to_f4(const __half *p) {
     const uint2 u = *reinterpret_cast<const uint2 *>(p);
@@ -513,6 +534,41 @@ struct Compute {
         }
     }
 
+    // ---------------------------------------------------------------- tagged handoffs
+
+    // The QKV rows (to the attention) and the residual stream after the down
+    // projection (to the next layer's staging) pass between CTAs as tagged
+    // words instead of through a grid barrier: the producer stores value and
+    // tag in one 8-byte word, the consumer re-reads until the word carries
+    // the tag of this handoff.  Every CTA draws the tags in the same order.
+    unsigned hseq = 0;                     // handoffs so far in this launch
+    unsigned cur_tag = 0;                  // the tag the next tagged epilogue stores
+    unsigned long long *x8out = nullptr;   // E_RESID: also store the rows tagged here
+    __device__ __forceinline__ unsigned next_tag() {
+        ++hseq;
+        return (job->epoch << TAG_SEQ_BITS) | (hseq & ((1u << TAG_SEQ_BITS) - 1u));
+    }
+    // 4 consecutive tagged words (16-byte aligned) once all carry `tag`;
+    // bounded like the barriers (false: timeout or another CTA's failure)
+    __device__ __forceinline__ bool poll4(const unsigned long long *p, unsigned tag, float4 &out) {
+        unsigned long long a, b, c, d;
+        ld_tagged2(p, a, b);
+        ld_tagged2(p + 2, c, d);
+        if (!(tag_is(a, tag) && tag_is(b, tag) && tag_is(c, tag) && tag_is(d, tag))) {
+            const long long t0 = clock64();
+            while (true) {
+                if (!(tag_is(a, tag) && tag_is(b, tag))) ld_tagged2(p, a, b);
+                if (!(tag_is(c, tag) && tag_is(d, tag))) ld_tagged2(p + 2, c, d);
+                if (tag_is(a, tag) && tag_is(b, tag) && tag_is(c, tag) && tag_is(d, tag)) break;
+                if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > job->wait_cycles)
+                    return false;
+            }
+        }
+        out = make_float4(__uint_as_float(static_cast<unsigned>(a)), __uint_as_float(static_cast<unsigned>(b)),
+                          __uint_as_float(static_cast<unsigned>(c)), __uint_as_float(static_cast<unsigned>(d)));
+        return true;
+    }
+
     // grid-wide barrier among the compute warps of all CTAs: release-add on
     // a monotonic counter, acquire-poll until every CTA has arrived.  It also
     // makes `ok` uniform over the CTA (any thread's failure fails all).
@@ -550,39 +606,6 @@ struct Compute {
         mark(200 + where);  // departure
     }
 
-    // barrier among the CTAs of this CTA's kv-head group (the same counter
-    // scheme as grid_sync, on the group's own counter)
-    unsigned gtarget = 0;
-    __device__ void group_sync(int where) {
-        const bool bad = named_or(!ok);
-        mark(100 + where);
-        if (tid == 0) {
-            int h, j, nj;
-            head_group(blockIdx.x, gridDim.x, h, j, nj);
-            gtarget += nj;
-            int b = bad ? 1 : 0;
-            if (!bad) {
-                unsigned *bar = job->s.bar + 2 + h;
-                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
-                const long long t0 = clock64();
-                while (true) {
-                    unsigned v;
-                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-                    if (v >= gtarget) break;
-                    if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > job->wait_cycles) {
-                        fail(ERR_TIMEOUT, where);
-                        b = 1;
-                        break;
-                    }
-                }
-            }
-            sm->bcast = b;
-        }
-        named_sync();
-        ok = sm->bcast == 0;
-        mark(200 + where);
-    }
-
     // ---------------------------------------------------------------- staging
 
     // act[r][0..H) = x_r * w for the rows x_r = ((a + b) + c) (up to 3
@@ -593,12 +616,21 @@ struct Compute {
     //  opart != NULL (per-head path): the rows are a[r] (+ b[r] + c[r]) plus
     //  the O projection, the sum of its HKV per-kv-head partials
     //  opart[r][h][..] in head order.
+    //  a8 != NULL: the rows a[r] are the tagged words a8[r][..] of handoff
+    //  a8tag instead (the residual stream as the down projection left it).
     __device__ void stage_norm(const float *const *a, const float *const *b, const float *const *c, int R,
-                               const float *w, bool init_resid, const float *opart = nullptr) {
+                               const float *w, bool init_resid, const float *opart = nullptr,
+                               const unsigned long long *a8 = nullptr, unsigned a8tag = 0) {
         float ss[RMAX] = {0.f, 0.f, 0.f, 0.f};
         for (int idx = tid; idx < R * (H / 4); idx += NCT) {
             const int r = idx / (H / 4), i = 4 * (idx - r * (H / 4));
-            float4 v = ldcg4(a[r] + i);
+            float4 v;
+            if (a8) {
+                // warp-uniform verdict (every lane of a warp runs the same iterations)
+                if (!__all_sync(0xffffffffu, poll4(a8 + r * H + i, a8tag, v))) fail(ERR_TIMEOUT, 60);
+            } else {
+                v = ldcg4(a[r] + i);
+            }
             float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
             if (opart) {
                 // all HKV loads in flight together, summed in head order
@@ -709,7 +741,7 @@ struct Compute {
     // ---------------------------------------------------------------- GEMV
 
     // Epilogue kinds
-    enum Epi { E_STORE, E_RESID, E_SWIGLU, E_HEAD, E_HEAD0 };
+    enum Epi { E_STORE, E_RESID, E_SWIGLU, E_HEAD, E_HEAD0, E_TAGGED };
 
     // rows [r0, r1) of matrix m owned by this CTA (the fixed matrices from
     // the table filled at the start of the launch)
@@ -731,7 +763,10 @@ struct Compute {
     // CTA barrier, before the epilogue.  eps >= 0: the rows were staged by
     // stage_norm and y is scaled by their 1/rms.
     //  E_STORE: out[r*ld + row] = y
-    //  E_RESID: residual row: xs[r][row-c0] += y, out[r*H + row] = xs
+    //  E_TAGGED: the same as a tagged word (out is the 64-bit word array),
+    //  tag cur_tag
+    //  E_RESID: residual row: xs[r][row-c0] += y, out[r*H + row] = xs (and,
+    //  with x8out, the same as a tagged word of x8out, tag cur_tag)
     //  E_SWIGLU: out[r*ld + row/2] = silu(y_gate) * y_up
     //  E_HEAD / E_HEAD0: out[row] = y (R == 1), the CTA's argmax key to
     //  job->s.arg; E_HEAD0 applies ChooseCode0's processors first.
@@ -756,7 +791,7 @@ struct Compute {
         const int nchunks = (nrows + sr - 1) / sr;
         const int pairs_full = (sr + 1) >> 1;  // pairs of a full chunk
         int it = warp;                         // next item of this warp
-        bool good = ok;
+        bool good = __all_sync(0xffffffffu, ok);  // warp-uniform (the stage waits use warp votes)
         // the staged rows' 1/rms, once (the barrier before the epilogue
         // publishes it): the last warp has the fewest items
         if (eps >= 0.f && warp == NCW - 1 && lane < R) sm->inv[lane] = norm_inv(lane, eps);
@@ -870,10 +905,13 @@ struct Compute {
                 const int orow = r0 + row;
                 if (kind == E_STORE) {
                     out[r * ld + orow] = y;
+                } else if (kind == E_TAGGED) {
+                    st_tagged(reinterpret_cast<unsigned long long *>(out) + r * ld + orow, y, cur_tag);
                 } else if (kind == E_RESID) {
                     const float v = sm->xs[r][orow - c0] + y;
                     sm->xs[r][orow - c0] = v;
                     out[r * H + orow] = v;
+                    if (x8out) st_tagged(x8out + r * H + orow, v, cur_tag);
                 } else {
                     out[orow] = y;
                     const float w = kind == E_HEAD0 ? choose0_value(orow, y) : y;
@@ -992,8 +1030,10 @@ struct Compute {
     //  head_path (a context of one tile): CTA b takes its group's kv head and
     //  the whole context, CTA 0 of the group appends, and the normalised
     //  output of row r goes to act[r][KO] for the O projection by head.
+    //  The new rows arrive as the tagged words of handoff qtag (the QKV
+    //  GEMV's epilogue): each lane polls its 4 values.
     __device__ void attention(const DLayer &Ly, const DCtx &kv, int layer, int R, int L0, float eps,
-                              bool head_path) {
+                              bool head_path, unsigned qtag) {
         const int T = L0 + R;
         int S, h, s, p0, p1;
         bool append;
@@ -1020,7 +1060,7 @@ struct Compute {
         for (int vec = warp; vec < 4 * R; vec += NCW) {
             const int r = vec >> 2, t = vec & 3;  // t: 0,1 = q heads, 2 = k, 3 = v
             // QKV rows by kv head: q(2h), q(2h+1), k(h), v(h)
-            const float *src = job->s.qkv + r * QKV_ROWS + h * QKV_HEAD + t * HD;
+            const unsigned long long *src = job->s.qkv + r * QKV_ROWS + h * QKV_HEAD + t * HD;
             // the norm weights and the RoPE row do not depend on the rows:
             // their loads go out together with the row's
             float4 g = make_float4(0.f, 0.f, 0.f, 0.f), cs = g, sn = g;
@@ -1032,7 +1072,8 @@ struct Compute {
                 cs = *reinterpret_cast<const float4 *>(job->rope_cos + ro);
                 sn = *reinterpret_cast<const float4 *>(job->rope_sin + ro);
             }
-            const float4 x = ldcg4(src + 4 * lane);
+            float4 x;
+            if (!__all_sync(0xffffffffu, poll4(src + 4 * lane, qtag, x))) fail(ERR_TIMEOUT, 41);
             float y[4] = {x.x, x.y, x.z, x.w};
             if (t < 3) {
                 const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
@@ -1070,13 +1111,19 @@ struct Compute {
                 }
             }
         }
+        bool landed = true;
         if (prefetched) {
-            // every thread waits for the tile (bounded)
-            if (!mbar_wait(&sm->kvbar, kv_phase, &sm->abort_flag)) fail(ERR_TIMEOUT, 40);
-            kv_phase ^= 1u;
+            // every thread waits for the tile (bounded); a wait that gave up
+            // leaves sm->kv_rows set and the phase unchanged, so that the
+            // exit drains the copy
+            landed = mbar_wait(&sm->kvbar, kv_phase, &sm->abort_flag);
+            if (landed)
+                kv_phase ^= 1u;
+            else
+                fail(ERR_TIMEOUT, 40);
         }
         named_sync();
-        if (tid == 0) sm->kv_rows = 0;
+        if (tid == 0 && landed) sm->kv_rows = 0;
         // 2. online softmax: warps grouped by (row, q head), positions strided
         const float scale = 1.0f / sqrtf(static_cast<float>(HD));
         const int nc = 2 * R, npw = NCW / nc;
@@ -1202,7 +1249,11 @@ struct Compute {
     // ---------------------------------------------------------------- stack
 
     // one forward of a stack over R rows at positions L0..L0+R-1; layer 0's
-    // input row r is in0[r] (+ in1[r]) (+ in2[r])
+    // input row r is in0[r] (+ in1[r]) (+ in2[r]).  The QKV rows reach the
+    // attention, and the residual stream after a down projection reaches the
+    // next layer's staging, as tagged words (no barrier); the O partials and
+    // the SwiGLU rows, which every CTA reads whole, after a grid barrier, as
+    // does the last layer's residual (read by the head).
     __device__ __forceinline__ void stack(const DStack &st, const DCtx &kv, int R, int L0, const float *const *in0,
                           const float *const *in1, const float *const *in2) {
         const Scratch &S = job->s;
@@ -1210,24 +1261,26 @@ struct Compute {
         for (int r = 0; r < RMAX; ++r) xr[r] = S.x + r * H;
         const int nsplit = att_splits(L0 + R, gridDim.x);
         const bool hp = per_head_path(L0 + R);
+        unsigned xtag = 0;  // the residual handoff of the previous layer's down projection
+        // ok is uniform over the CTA at the top of each layer: a failure sets
+        // the CTA's abort flag, which the GEMV reads after its CTA barrier
         for (int l = 0; l < st.layers && ok; ++l) {
             const DLayer Ly = st.layer[l];
             // P1
             if (l == 0)
                 stage_norm(in0, in1, in2, R, Ly.in_norm, true);
             else
-                stage_norm(xr, nullptr, nullptr, R, Ly.in_norm, false);
+                stage_norm(nullptr, nullptr, nullptr, R, Ly.in_norm, false, nullptr, S.x8, xtag);
             mark(10);
-            gemv<H>(M_QKV, 0, R, E_STORE, S.qkv, QKV_ROWS, st.eps);
+            const unsigned qtag = next_tag();
+            cur_tag = qtag;
+            gemv<H>(M_QKV, 0, R, E_TAGGED, reinterpret_cast<float *>(S.qkv), QKV_ROWS, st.eps);
+            if (!ok) return;
             mark(11);
             prefetch_kv(kv, l, R, L0, hp);
-            if (hp)
-                group_sync(7);  // the QKV rows of this kv head come from its group
-            else
-                grid_sync(1);
-            if (!ok) return;
-            // P2
-            attention(Ly, kv, l, R, L0, st.eps, hp);
+            named_sync();  // thread 0's sm->kv_rows (the prefetched tile) for every thread
+            // P2: the rows of this CTA's kv head, polled as they land
+            attention(Ly, kv, l, R, L0, st.eps, hp, qtag);
             mark(21);
             if (hp) {
                 // the O projection restricted to this head's columns, by head
@@ -1262,9 +1315,16 @@ struct Compute {
             // P5
             stage_copy(S.act, R, INTER);
             mark(50);
+            const bool last = l + 1 == st.layers;
+            if (!last) {
+                xtag = next_tag();
+                cur_tag = xtag;
+                x8out = S.x8;
+            }
             gemv<INTER>(M_D, 0, R, E_RESID, S.x, H, -1.f);
+            x8out = nullptr;
             mark(51);
-            grid_sync(5);
+            if (last) grid_sync(5);
         }
     }
 
@@ -1433,7 +1493,6 @@ __device__ void compute(Smem *sm, const Job &job) {
         __threadfence();
         if (atomicAdd(S.bar + 1, 1u) == gridDim.x - 1) {
             S.bar[0] = 0u;
-            for (int h = 0; h < HKV; ++h) S.bar[2 + h] = 0u;
             S.bar[1] = 0u;
             __threadfence();
         }
