@@ -544,6 +544,8 @@ struct Compute {
     unsigned hseq = 0;                     // handoffs so far in this launch
     unsigned cur_tag = 0;                  // the tag the next tagged epilogue stores
     unsigned long long *x8out = nullptr;   // E_RESID: also store the rows tagged here
+    unsigned key_tag = 0;                  // E_HEAD*: store the CTA's argmax key tagged (0: plain)
+    const float *next_rows = nullptr;      // E_HEAD*: the table whose row the winning index selects next
     __device__ __forceinline__ unsigned next_tag() {
         ++hseq;
         return (job->epoch << TAG_SEQ_BITS) | (hseq & ((1u << TAG_SEQ_BITS) - 1u));
@@ -709,13 +711,29 @@ struct Compute {
                 ms = u.x;
                 ls = u.y;
             }
+            // the first splits' partial outputs travel with the (max, sum) loads
+            constexpr int PRE = WDT == WDT_Q8 ? 4 : 1;  // float32 weights leave fewer registers
+            float4 op[PRE];
+#pragma unroll
+            for (int j = 0; j < PRE; ++j)
+                if (j < S) op[j] = ldcg4(base + j * split_stride + 4 * lane);
             float M = ms;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
             const float e = ms == -INFINITY ? 0.f : expf(ms - M);
             const float L = warp_sum(ls * e);
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s0 = 0; s0 < S; s0 += 4) {
+#pragma unroll
+            for (int j = 0; j < PRE; ++j) {
+                const float es = __shfl_sync(0xffffffffu, e, j);
+                if (j < S) {
+                    acc.x = fmaf(op[j].x, es, acc.x);
+                    acc.y = fmaf(op[j].y, es, acc.y);
+                    acc.z = fmaf(op[j].z, es, acc.z);
+                    acc.w = fmaf(op[j].w, es, acc.w);
+                }
+            }
+            for (int s0 = PRE; s0 < S; s0 += 4) {
                 float4 o[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
@@ -929,10 +947,31 @@ struct Compute {
             }
             if (lane == 0) sm->keys[warp] = best;
             named_sync();
-            if (tid == 0) {
-                unsigned long long b = 0ull;
-                for (int w2 = 0; w2 < NCW; ++w2) b = sm->keys[w2] > b ? sm->keys[w2] : b;
-                job->s.arg[blockIdx.x] = b;
+            if (warp == 0) {
+                unsigned long long b = lane < NCW ? sm->keys[lane] : 0ull;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+                    b = t > b ? t : b;
+                }
+                if (key_tag) {
+                    // tagged key: the float bits, the tag, the index (< 4096)
+                    const unsigned idx = static_cast<unsigned>(key_index(b)) & 0xFFFu;
+                    const unsigned long long kt = (b & 0xFFFFFFFF00000000ull) |
+                                                  (static_cast<unsigned long long>(key_tag & 0xFFFFFu) << 12) |
+                                                  (0xFFFu - idx);
+                    if (lane == 0)
+                        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(job->s.arg + blockIdx.x), "l"(kt)
+                                     : "memory");
+                } else if (lane == 0) {
+                    job->s.arg[blockIdx.x] = b;
+                }
+                // the row the next step gathers if this CTA's candidate wins,
+                // brought into L2 while the keys meet
+                if (next_rows && b != 0ull) {
+                    const char *row = reinterpret_cast<const char *>(next_rows + static_cast<size_t>(key_index(b)) * H);
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 128 * lane));
+                }
             }
         }
     }
@@ -955,6 +994,44 @@ struct Compute {
     __device__ __forceinline__ int sample_code(int V, const SampleParams &p, float u, bool talker) {
         return frame_draw(job->s.logits, V, p, u, reinterpret_cast<SampleScratch *>(sm->act), tid, talker,
                           job->tvocab, job->eos, hist_now, job->seen, job->penalty);
+    }
+
+    // the winning index over all CTAs' tagged keys of handoff tag (no
+    // barrier): warp 0 polls the keys and reduces, the CTA reads its verdict;
+    // ok is uniform over the CTA afterwards
+    __device__ int reduce_argmax_tagged(unsigned tag) {
+        if (warp == 0) {
+            unsigned long long b = 0ull;
+            bool got = true;
+            for (int i = lane; i < static_cast<int>(gridDim.x); i += 32) {
+                const unsigned long long *p = job->s.arg + i;
+                unsigned long long k;
+                const long long t0 = clock64();
+                while (true) {
+                    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(k) : "l"(p) : "memory");
+                    if (static_cast<unsigned>((k >> 12) & 0xFFFFFu) == (tag & 0xFFFFFu)) break;
+                    if (*reinterpret_cast<volatile int *>(job->s.err) != 0 || clock64() - t0 > job->wait_cycles) {
+                        got = false;
+                        break;
+                    }
+                }
+                if (!got) break;
+                b = k > b ? k : b;
+            }
+            got = __all_sync(0xffffffffu, got);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+                b = t > b ? t : b;
+            }
+            if (!got) fail(ERR_TIMEOUT, 62);
+            if (lane == 0) sm->bcast = static_cast<int>(0xFFFu - static_cast<unsigned>(b & 0xFFFu));
+        }
+        named_sync();
+        if (*reinterpret_cast<volatile int *>(&sm->abort_flag)) ok = false;
+        const int code = sm->bcast;
+        named_sync();  // sm->bcast is the grid barrier's word too
+        return code;
     }
 
     // after a grid barrier: the winning index over all CTAs' keys
@@ -1439,12 +1516,26 @@ __device__ void compute(Smem *sm, const Job &job) {
             const int L0 = g == 0 ? 0 : g + 1;
             c.stack(job.pst, job.pctx, R, L0, in, nullptr, nullptr);
             if (!c.ok) break;
+            // greedy: the CTAs' argmax keys meet as tagged words (no barrier);
+            // the row of pred_emb[g] the winner selects is prefetched into L2
+            const bool tagged_keys = !job.samp.on && job.pvocab <= 4096;
+            c.key_tag = tagged_keys ? c.next_tag() : 0u;
+            c.next_rows = job.pred_emb + static_cast<size_t>(g) * job.pvocab * H;
             c.head(job.pst, R, job.pvocab, Compute<WDT, KV16>::E_HEAD, nullptr);
-            c.grid_sync(6);
+            const unsigned ktag = c.key_tag;
+            c.key_tag = 0u;
+            c.next_rows = nullptr;
             if (!c.ok) break;
             // ChooseCode (talker.pas:632-638): the draw (frame, group g + 1) or the argmax
-            code = job.samp.on ? c.sample_code(job.pvocab, job.samp, sample_uniform(job.seed, step, g + 1), false)
-                               : c.reduce_argmax();
+            if (tagged_keys) {
+                code = c.reduce_argmax_tagged(ktag);
+            } else {
+                c.grid_sync(6);
+                if (!c.ok) break;
+                code = job.samp.on ? c.sample_code(job.pvocab, job.samp, sample_uniform(job.seed, step, g + 1), false)
+                                   : c.reduce_argmax();
+            }
+            if (!c.ok) break;
             if (blockIdx.x == 0 && c.tid == 0) {
                 fs->codes[g + 1] = code;
                 if (job.codes_hist && step < job.codes_cap) job.codes_hist[step * job.groups + g + 1] = code;
@@ -1463,7 +1554,9 @@ __device__ void compute(Smem *sm, const Job &job) {
             const float *tr = step < job.trailing_rows ? job.trailing + static_cast<size_t>(step) * H : job.tts_pad;
             const float *in2[RMAX] = {tr, nullptr, nullptr, nullptr};
             c.stack(job.tst, job.tctx, 1, tlen, in0, in1, in2);
+            c.next_rows = job.codec_emb;  // the next frame starts from codec_emb[code 0]
             if (c.ok) c.head(job.tst, 1, job.tvocab, Compute<WDT, KV16>::E_HEAD0, S.hidden);
+            c.next_rows = nullptr;
             if (c.ok) c.grid_sync(8);
             if (c.ok && blockIdx.x == 0 && (job.samp0.on || c.warp == 0)) {
                 // ChooseCode0 of the next frame (its draw is (step + 1, 0));
