@@ -614,6 +614,7 @@ TRACE_PHASES = {
     (203, 40): "RMSNorm staging (P4)", (40, 41): "gate/up GEMV + SwiGLU (P4)", (204, 50): "staging (P5)",
     (50, 51): "down GEMV + residual (P5)", (205, 10): "RMSNorm staging (P1)", (60, 61): "head GEMV + argmax keys",
     (206, 10): "argmax + next input (P1 staging)", (51, 10): "RMSNorm staging, polling the residual (P1)",
+    (61, 10): "argmax keys polled + next input (P1 staging)",
 }
 # Q8_0 bytes a GEMV phase streams (row-packed, 34 B per 32 weights)
 TRACE_BYTES = {"QKV GEMV (P1)": 4096 * 1088, "O GEMV + residual (P3)": 1024 * 2176, "O GEMV by kv head": 8192 * 272,
