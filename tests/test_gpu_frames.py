@@ -203,3 +203,58 @@ def test_batched_sampled_frames(device):
     assert ranks.size > 0 and ranks.max() < 50 + 8, ranks.max()
     assert (ranks < 50).mean() >= 0.95
     assert (ranks > 0).mean() >= 0.3  # not the argmax every time
+
+
+def test_box_slots_take_the_next_utterance(device):
+    # BASELINE.json configs[4] as bench.py's box run drives it, at reduced
+    # size (2 + 2 layers, 4 slots, 10 utterances of at most 5 frames): the
+    # slots start with the first utterances, a slot whose utterance ends (eos
+    # or its frame limit) takes the next one, a frame's admissions in one
+    # Start call, prompts of U(20, 80) N(0,1) rows made as the box run makes
+    # them.  Every frame of every utterance is replayed in an oracle talker of
+    # its slot (started afresh with each admission).
+    slots, utts, limit, seed = 4, 10, 5, 81
+    rig = Rig(device, seed, 2, 2, "q8_0", "bf16", nseq=slots, max_pos=100)
+    lens = synth.config4_lengths(seed, utts, 20, 80)
+    pad = synth.text_rows(seed, 1, key=1)[0]
+    queue = list(range(utts))
+    slot_utt, slot_frames, ended = [-1] * slots, [0] * slots, {}
+
+    def admit(free):
+        take, rows = [], []
+        for s in free:
+            if not queue:
+                break
+            u = queue.pop(0)
+            slot_utt[s], slot_frames[s] = u, 0
+            take.append(s)
+            rows.append(synth.config4_prompt(u, int(lens[u]), seed))
+        if take:
+            rig.dev.start(take, rows, [None] * len(take), pad)
+            for s, p in zip(take, rows):
+                rig.ora[s].start(p, None, pad)
+        return len(take)
+
+    starts = [admit(range(slots))]
+    stats = [0, 0]
+    while True:
+        active = [s for s in range(slots) if slot_utt[s] >= 0]
+        if not active:
+            break
+        _, more = frame(rig, active, GAP[("q8_0", "bf16")], stats)
+        freed = []
+        for s, mo in zip(active, more):
+            if mo:
+                slot_frames[s] += 1
+            if not mo or slot_frames[s] >= limit:
+                ended[slot_utt[s]] = slot_frames[s]
+                slot_utt[s] = -1
+                freed.append(s)
+        if freed:
+            starts.append(admit(freed))
+    assert sorted(ended) == list(range(utts))
+    assert all(0 <= f <= limit for f in ended.values())
+    assert sum(starts) == utts and len(starts) > 1  # the slots were refilled
+    print({"box_frames": sum(ended.values()), "first_maxima": stats[0], "choices": stats[1]})
+    assert stats[0] >= 0.98 * stats[1], stats
+    rig.free()
