@@ -841,6 +841,15 @@ def gpu_arm(args, rank, world, local_rank):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    if args.only_codec:
+        # the codec leg alone (profiling runs): no language-model weights
+        dev = qtts.QwenDevice(local_rank)
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "codec": codec_measure(qtts, dev, False)}), flush=True)
+        dev.close()
+        if dist:
+            dist.destroy_process_group()
+        return
     dtype = args.config
     m = build_host_model(dtype, tlayers=args.talker_layers, players=args.pred_layers)
     prompt = synth.config1_prompt(SEED, PROMPT_ROWS[dtype], rank)
@@ -1060,6 +1069,7 @@ def main():
     # configs[3] beside the bench line: batched prefill steps (0: off)
     ap.add_argument("--prefill-steps", type=int, default=2)
     ap.add_argument("--only-prefill", action="store_true", help="run the configs[3] measurement alone")
+    ap.add_argument("--only-codec", action="store_true", help="run the codec measurement alone")
     ap.add_argument("--trace-frame", action="store_true",
                     help="print the phase trace of one configs[1] frame alone (no batched/prefill legs: --batch 0 "
                          "--prefill-steps 0)")
