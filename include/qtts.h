@@ -189,11 +189,20 @@ int qtts_lm_length(qtts_lm *lm, int *length);
  * following launches of this lm (forwards, and frames when it is a talker's
  * talker lm) run their grid barriers expecting extra_arrivals (0 or 1) more
  * CTAs than the grid holds -- an arrival that never comes -- with every grid
- * and group barrier spin bounded by wait_cycles SM clock cycles (0: the
+ * barrier and tagged-word spin bounded by wait_cycles SM clock cycles (0: the
  * default bound, about 2 s).  Such a launch returns QTTS_E_TIMEOUT with the
  * place it gave up; its positions are not appended and the next launch
  * starts clean.  (0, 0) restores normal operation. */
 int qtts_lm_set_wait_test(qtts_lm *lm, int extra_arrivals, int64_t wait_cycles);
+/* Test knob of the batch-1 kernel's tagged handoffs (no counterpart in the
+ * reference).  Values
+ * pass between the kernel's CTAs as words tagged with the launch's epoch, a
+ * counter of this lm's scratch that wraps after 2^22 - 1 launches, the host
+ * clearing the tagged words before epoch 1 comes round again.  This sets
+ * the counter (0 .. 2^22 - 1; the next launch of this lm, or of frames when
+ * it is a talker's talker lm, uses epoch + 1, or wraps), so that a test can
+ * cross the wrap in a few launches. */
+int qtts_lm_set_launch_epoch(qtts_lm *lm, uint32_t epoch);
 /* TQwenLm.Destroy (lm.pas:362-372): frees the cache, then the stack. */
 int qtts_lm_destroy(qtts_lm *lm);
 

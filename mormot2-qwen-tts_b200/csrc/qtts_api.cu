@@ -1197,6 +1197,13 @@ extern "C" int qtts_lm_create_kv(qtts_stack *stack, qtts_heads *heads, int max_p
     return lm_create(stack, heads, max_pos, kv_dtype, out);
 }
 
+extern "C" int qtts_lm_set_launch_epoch(qtts_lm *m, uint32_t epoch) {
+    if (!m || !m->run.epoch || epoch >= EPOCH_LIMIT)
+        return set_err(QTTS_E_ARG, "qtts_lm_set_launch_epoch: bad argument (epoch below %u)", EPOCH_LIMIT);
+    *m->run.epoch = epoch;
+    return QTTS_OK;
+}
+
 extern "C" int qtts_lm_set_wait_test(qtts_lm *m, int extra_arrivals, int64_t wait_cycles) {
     if (!m || extra_arrivals < 0 || extra_arrivals > 1 || wait_cycles < 0)
         return set_err(QTTS_E_ARG, "qtts_lm_set_wait_test: bad argument");

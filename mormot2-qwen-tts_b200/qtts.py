@@ -154,6 +154,7 @@ EXPORTS = {
     "qtts_lm_forward_noalloc": [P, P, I, I, P, P],
     "qtts_lm_length": [P, PI],
     "qtts_lm_set_wait_test": [P, I, ctypes.c_int64],
+    "qtts_lm_set_launch_epoch": [P, ctypes.c_uint32],
     "qtts_lm_create_kv": [P, P, I, I, ctypes.POINTER(P)],
     "qtts_lm_destroy": [P],
     "qtts_batch_create": [P, P, I, I, I, I, ctypes.POINTER(P)],
@@ -496,6 +497,12 @@ class QwenLm:
         v = ctypes.c_int()
         check(lib().qtts_lm_length(self.handle, ctypes.byref(v)))
         return v.value
+
+    def set_launch_epoch(self, epoch):
+        """qtts_lm_set_launch_epoch: set the epoch counter of this lm's
+        tagged handoffs (the next launch uses epoch + 1; at 2^22 - 1 it wraps
+        to 1 after the tagged words are cleared)."""
+        check(lib().qtts_lm_set_launch_epoch(self.handle, epoch))
 
     def set_wait_test(self, extra_arrivals, wait_cycles):
         """qtts_lm_set_wait_test: make the grid barriers of the next launches

@@ -158,6 +158,35 @@ def test_talker_frames_match_oracle(device, dtype):
     tp.free()
 
 
+def test_tagged_handoffs_across_the_epoch_wrap(device):
+    # The batch-1 kernel passes the QKV rows, the residual stream and, in
+    # greedy frames, the argmax keys between its CTAs as words tagged with
+    # the launch's epoch, a counter that wraps after 2^22 - 1 launches (the
+    # host clears the tagged words before epoch 1 comes round again).
+    # Launches on either side of the wrap must equal the oracle's.
+    pr = Pair(device, 97, "talker", 2, [synth.talker_head(97)], "q8_0", max_pos=32)
+    try:
+        with pytest.raises(qtts.EQwenLm):
+            pr.dev.set_launch_epoch(1 << 22)
+        x = synth.prompt(97, 9)
+        ld, lo = np.zeros(3072, np.float32), np.zeros(3072, np.float32)
+        pr.dev.set_launch_epoch((1 << 22) - 3)
+        for r0, r1 in ((0, 3), (3, 4), (4, 5), (5, 7), (7, 8), (8, 9)):  # epochs 2^22 - 2, 2^22 - 1, 1, 2, 3, 4
+            pr.dev.forward(x[r0:r1], output=0, logits=ld)
+            pr.ora.forward(x[r0:r1], 0, lo)
+            assert np.abs(ld - lo).max() <= Q8_LOGITS_ATOL and cosine(ld, lo) >= Q8_COSINE, (r0, r1)
+    finally:
+        pr.free()
+    # frames: the talker's launches use the talker lm's counter
+    tp = TalkerPair(device, 51, 2, 2, "q8_0")
+    try:
+        tp.start(synth.prompt(51, 12), synth.text_rows(51, 3), synth.text_rows(51, 1, key=1)[0])
+        tp.t.dev.set_launch_epoch((1 << 22) - 2)
+        assert run_frames(tp, 4, Q8_LOGITS_ATOL, Q8_COSINE) == 4
+    finally:
+        tp.free()
+
+
 def test_eos_ends_the_sentence(device):
     # a talker head whose eos row dominates: eos is forbidden for the first
     # 2 frames (talker.pas:610-611), then chosen; NextFrame returns false
